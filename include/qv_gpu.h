@@ -1,0 +1,218 @@
+/* quiver-b200 C ABI: the drop-in boundary between Quiver's host-side API and the sm_100a kernels.
+ *
+ * Every entry point is extern "C", takes plain pointers and sizes, never throws, and returns a
+ * qv_status. On failure qv_last_error() returns a thread-local message whose text matches what the
+ * reference's quiver::Error would carry for the same mistake (e.g. "vectors must not contain NaN
+ * or infinity"), so the C++ wrapper can rethrow quiver::Error and the Python layer ValueError.
+ *
+ * Citations name the reference interface each entry point replaces, as file:line of the reference
+ * Quiver project. The reference reaches that interface from Python through its nanobind module
+ * (python/quiver_ext.cc); these functions are what that binding's lambdas would call instead.
+ *
+ * Host-buffer entry points (no "_device" suffix) take caller-owned host memory that is valid only
+ * for the call; they copy inputs to the index's GPU, run there, and copy results back before
+ * returning. "_device" entry points take device pointers on the index's GPU plus a cudaStream_t
+ * passed as void* (NULL = the calling thread's stream for that device) and return once the work is
+ * enqueued. Index state is read-only during searches, so concurrent searches on one index are safe;
+ * add() must not run concurrently with other calls on the same index (the C++ wrapper serializes
+ * it with a shared mutex, as the reference does).
+ *
+ * Distances follow quiver::Metric (include/quiver/common.h:25-29): squared L2, 1 - <q,x> for inner
+ * product, 1 - cos for cosine; smaller is closer. Unfilled result slots get label
+ * QV_INVALID_LABEL (2^64-1) and distance +inf.
+ */
+#ifndef QV_GPU_H_
+#define QV_GPU_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum qv_status {
+  QV_OK = 0,
+  QV_ERR_INVALID = 1,     /* bad argument: quiver::Error in the reference */
+  QV_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  QV_ERR_OOM = 3,         /* device or host allocation failed */
+  QV_ERR_IO = 4,          /* file could not be read or written, or is corrupt */
+  QV_ERR_STATE = 5,       /* e.g. add() before the index holds trained centroids */
+  QV_ERR_UNSUPPORTED = 6, /* outside the GPU path (IVF training) */
+  QV_ERR_DEVICE = 7       /* a kernel reported an error through its status word */
+} qv_status;
+
+#define QV_INVALID_LABEL UINT64_MAX
+
+enum { QV_METRIC_L2 = 0, QV_METRIC_IP = 1, QV_METRIC_COSINE = 2 };
+
+/* Thread-local text of the last failure on this thread ("" if none). */
+const char* qv_last_error(void);
+/* Library version string. */
+const char* qv_version(void);
+/* Number of CUDA devices this process can use. */
+qv_status qv_device_count(int* count);
+
+/* ---- filters ----------------------------------------------------------------------------------
+ * Replaces quiver::Filter (include/quiver/filter.h:24-102) at the boundary. The binding's
+ * make_filter (python/quiver_ext.cc:40-51) builds a BitsetFilter or LabelSetFilter from the allowed
+ * labels; here the same information crosses as one of:
+ *   QV_FILTER_LABEL_SET:       data = allowed labels (size entries, any order, duplicates allowed)
+ *   QV_FILTER_LABEL_BITMAP:    data = BitsetFilter words: label L is admitted iff L < size and
+ *                              bit (L & 63) of data[L >> 6] is set
+ *   QV_FILTER_POSITION_BITMAP: data = one bit per stored row, in the order qv_flat_rows /
+ *                              qv_ivfpq_labels report (how an arbitrary PredicateFilter is passed:
+ *                              the caller evaluates contains(label) per stored label)
+ * A NULL qv_filter* means no filter. */
+enum { QV_FILTER_LABEL_SET = 1, QV_FILTER_LABEL_BITMAP = 2, QV_FILTER_POSITION_BITMAP = 3 };
+typedef struct qv_filter {
+  uint32_t kind;
+  const uint64_t* data;
+  uint64_t size;
+} qv_filter;
+
+/* ---- FlatIndex --------------------------------------------------------------------------------- */
+typedef struct qv_flat qv_flat;
+
+/* FlatIndex(dim, metric): include/quiver/flat_index.h:21 (src/flat_index.cc:41-47). */
+qv_status qv_flat_create(int device, size_t dim, uint32_t metric, qv_flat** out);
+qv_status qv_flat_destroy(qv_flat* index);
+/* add(vectors, n, labels): include/quiver/flat_index.h:25 (src/flat_index.cc:49-67). labels may be
+ * NULL (row i gets label size()+i). Cosine rows are normalized on the GPU exactly as
+ * simd::normalize does it. */
+qv_status qv_flat_add(qv_flat* index, const float* vectors, size_t n, const uint64_t* labels);
+/* search_batch(queries, nq, k, labels, distances, filter, pool): include/quiver/flat_index.h:34-36
+ * (src/flat_index.cc:126-140). Writes nq*k results, closest first. */
+qv_status qv_flat_search(const qv_flat* index, const float* queries, size_t nq, size_t k,
+                         const qv_filter* filter, uint64_t* labels, float* distances);
+/* size(), dim(), metric(): include/quiver/flat_index.h:38-40. */
+qv_status qv_flat_info(const qv_flat* index, size_t* size, size_t* dim, uint32_t* metric);
+/* vector(i) / label(i) host views: include/quiver/flat_index.h:43-44. Copies rows [first,
+ * first+count) as stored (normalized for cosine) and/or their labels; either output may be NULL. */
+qv_status qv_flat_rows(const qv_flat* index, size_t first, size_t count, float* vectors,
+                       uint64_t* labels);
+/* save/load: include/quiver/flat_index.h:46-47 (src/flat_index.cc:147-176), same .qvr format. */
+qv_status qv_flat_save(const qv_flat* index, const char* path);
+qv_status qv_flat_load(int device, const char* path, int verify_checksums, qv_flat** out);
+
+/* Device-resident search for composing kernels and for multi-GPU sharding. Queries, outputs and
+ * the optional position bitmap are device pointers on the index's GPU. keys (may be NULL) receive
+ * row_offset + local row of each result, the canonical tie-break key used to merge shards. */
+qv_status qv_flat_search_device(const qv_flat* index, const float* queries, size_t nq, size_t k,
+                                const uint64_t* position_bitmap, uint64_t* labels, float* distances,
+                                uint64_t* keys, void* stream);
+/* Global id of this index's row 0 when it is one id-range shard of a larger collection. */
+qv_status qv_flat_set_row_offset(qv_flat* index, uint64_t row_offset);
+
+/* ---- IvfPqIndex -------------------------------------------------------------------------------- */
+typedef struct qv_ivfpq qv_ivfpq;
+
+/* IvfPqParams: include/quiver/ivfpq_index.h:26-35. */
+typedef struct qv_ivfpq_params {
+  size_t dim;
+  uint32_t metric;
+  size_t nlist;
+  size_t m;
+  size_t train_iterations;
+  int store_vectors;
+  uint64_t seed;
+} qv_ivfpq_params;
+
+/* IvfPqIndex(params): include/quiver/ivfpq_index.h:46 (src/ivfpq_index.cc:95-103). */
+qv_status qv_ivfpq_create(int device, const qv_ivfpq_params* params, qv_ivfpq** out);
+qv_status qv_ivfpq_destroy(qv_ivfpq* index);
+/* train(): include/quiver/ivfpq_index.h:53. Training is not part of the GPU path; this returns
+ * QV_ERR_UNSUPPORTED. Trained state comes from qv_ivfpq_load or qv_ivfpq_set_trained. */
+qv_status qv_ivfpq_train(qv_ivfpq* index, const float* vectors, size_t n);
+/* Installs trained state (nlist x dim centroids, m x 256 x dsub codebooks), as load() does
+ * (src/ivfpq_index.cc:531-543), including the L2 precomputed term table. */
+qv_status qv_ivfpq_set_trained(qv_ivfpq* index, const float* centroids, const float* codebooks);
+qv_status qv_ivfpq_is_trained(const qv_ivfpq* index, int* trained);
+/* add(vectors, n, labels, pool): include/quiver/ivfpq_index.h:57-58 (src/ivfpq_index.cc:208-271):
+ * coarse assignment and PQ encode on the GPU, appended per list in input order. */
+qv_status qv_ivfpq_add(qv_ivfpq* index, const float* vectors, size_t n, const uint64_t* labels);
+/* The assign + encode half of add() without appending: cell ids and m-byte codes per vector,
+ * bit-identical to src/ivfpq_index.cc:235-246. */
+qv_status qv_ivfpq_encode(const qv_ivfpq* index, const float* vectors, size_t n, uint32_t* assign,
+                          uint8_t* codes);
+/* search_batch(queries, nq, k, labels, distances, {nprobe, refine_factor, filter}, pool):
+ * include/quiver/ivfpq_index.h:62-64 (src/ivfpq_index.cc:421-437, :275-381). */
+qv_status qv_ivfpq_search(const qv_ivfpq* index, const float* queries, size_t nq, size_t k,
+                          size_t nprobe, size_t refine_factor, const qv_filter* filter,
+                          uint64_t* labels, float* distances);
+/* size(), memory_bytes(), list_sizes(): include/quiver/ivfpq_index.h:69-75. */
+qv_status qv_ivfpq_info(const qv_ivfpq* index, qv_ivfpq_params* params, size_t* size,
+                        size_t* memory_bytes);
+qv_status qv_ivfpq_list_sizes(const qv_ivfpq* index, uint64_t* sizes /* nlist */);
+/* Stored labels in storage (list-major) order; `labels` holds size() entries. */
+qv_status qv_ivfpq_labels(const qv_ivfpq* index, uint64_t* labels);
+/* save/load: include/quiver/ivfpq_index.h:66-67 (src/ivfpq_index.cc:465-576), same .qvr format.
+ * load recomputes the precomputed table as the reference does (:542). */
+qv_status qv_ivfpq_save(const qv_ivfpq* index, const char* path);
+qv_status qv_ivfpq_load(int device, const char* path, int verify_checksums, qv_ivfpq** out);
+/* One id-range shard of a .qvr: keeps the entries whose label lies in [label_begin, label_end)
+ * (list order preserved) and remembers each list's global offset so that candidate keys
+ * (list << 32 | offset-in-full-list) match the unsharded index. */
+qv_status qv_ivfpq_load_shard(int device, const char* path, int verify_checksums,
+                              uint64_t label_begin, uint64_t label_end, qv_ivfpq** out);
+
+/* Device-resident stages for composing and for multi-GPU sharding (all pointers on the index's
+ * GPU). qv_ivfpq_search_device runs the whole search. qv_ivfpq_candidates_device stops after the
+ * ADC scan and returns each query's best `keep` (distance, key, label), sorted, padded with
+ * (+inf, UINT64_MAX, QV_INVALID_LABEL); keys are list << 32 | offset-in-full-list.
+ * qv_ivfpq_refine_device writes the exact distance of every candidate this index stores and +inf
+ * for the others (keys not held here), so shards' outputs can be min-reduced. */
+qv_status qv_ivfpq_search_device(const qv_ivfpq* index, const float* queries, size_t nq, size_t k,
+                                 size_t nprobe, size_t refine_factor,
+                                 const uint64_t* position_bitmap, uint64_t* labels,
+                                 float* distances, void* stream);
+qv_status qv_ivfpq_candidates_device(const qv_ivfpq* index, const float* queries, size_t nq,
+                                     size_t keep, size_t nprobe, const uint64_t* position_bitmap,
+                                     float* distances, uint64_t* keys, uint64_t* labels,
+                                     void* stream);
+qv_status qv_ivfpq_refine_device(const qv_ivfpq* index, const float* queries, size_t nq,
+                                 size_t keep, const uint64_t* keys, float* exact, void* stream);
+/* Builds the per-position bitmap a _device search takes from a host filter (uploaded once). The
+ * bitmap is allocated on the index's GPU; release it with qv_device_free. */
+qv_status qv_flat_filter_bitmap(const qv_flat* index, const qv_filter* filter,
+                                uint64_t** device_bitmap);
+qv_status qv_ivfpq_filter_bitmap(const qv_ivfpq* index, const qv_filter* filter,
+                                 uint64_t** device_bitmap);
+qv_status qv_device_free(int device, void* ptr);
+
+/* ---- shard merge ---------------------------------------------------------------------------------
+ * k-way merge of per-shard results: parts x nq x k (distance, key, label) triples, each row sorted
+ * by (distance, key), into nq x k sorted by (distance, key). Device pointers on `device`. Replaces
+ * nothing in the reference (which has no sharding); it is the final step of a sharded search. */
+qv_status qv_merge_topk_device(int device, size_t parts, size_t nq, size_t k,
+                               const float* distances, const uint64_t* keys,
+                               const uint64_t* labels, float* out_distances, uint64_t* out_keys,
+                               uint64_t* out_labels, void* stream);
+/* Per-row top-k of candidate lists: nq x n (distance, key, label) -> nq x k sorted by
+ * (distance, key). Used after min-reducing shard refine outputs. */
+qv_status qv_select_topk_device(int device, size_t nq, size_t n, size_t k, const float* distances,
+                                const uint64_t* keys, const uint64_t* labels,
+                                float* out_distances, uint64_t* out_keys, uint64_t* out_labels,
+                                void* stream);
+
+/* Counters of the last search on the calling thread (for the bench and tests): kernel launches
+ * issued, queries whose screen could not be certified and were rescanned exactly, and, when timing
+ * is enabled, the device time of the search's dominant kernel (measured with CUDA events on the
+ * stream it runs on), its name and its algorithmic work (FLOPs for the distance screen, bytes for
+ * scans) so callers can compute a roofline fraction. */
+typedef struct qv_search_stats {
+  uint64_t kernel_launches;
+  uint64_t rescanned_queries;
+  double dominant_kernel_ms;
+  double dominant_kernel_work;
+  uint32_t dominant_work_is_bytes;
+  char dominant_kernel[64];
+} qv_search_stats;
+qv_status qv_last_search_stats(qv_search_stats* stats);
+/* Enables (1) or disables (0) the per-search kernel timing above for the calling thread. */
+qv_status qv_set_timing(int enable);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QV_GPU_H_ */

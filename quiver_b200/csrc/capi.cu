@@ -1,0 +1,877 @@
+// The extern "C" boundary (include/qv_gpu.h): index handles, argument validation with the
+// reference's error wording, host<->device staging, and the .qvr load/save of both index types.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <shared_mutex>
+#include <string>
+#include <vector>
+
+#include "qv_gpu.h"
+#include "qv_state.h"
+#include "qvr.h"
+
+struct qv_flat {
+  qv::FlatState s;
+  mutable std::shared_mutex mu;  // searches shared, add exclusive
+};
+
+struct qv_ivfpq {
+  qv::IvfState s;
+  mutable std::shared_mutex mu;
+};
+
+namespace qv {
+
+namespace {
+thread_local std::string t_error;
+thread_local SearchStats t_stats;
+constexpr size_t kMaxDimension = 65536;    // include/quiver/common.h:20
+constexpr size_t kMaxLists = size_t{1} << 24;  // src/ivfpq_index.cc:71
+constexpr uint32_t kMeta = fourcc("META"), kVect = fourcc("VECT"), kLabl = fourcc("LABL"),
+                   kCent = fourcc("CENT"), kPqcb = fourcc("PQCB"), kLoff = fourcc("LOFF"),
+                   kCode = fourcc("CODE");
+
+struct FlatMeta {  // src/flat_index.cc:24-29
+  uint64_t dim, count;
+  uint32_t metric, reserved;
+};
+struct IvfPqMeta {  // src/ivfpq_index.cc:32-43
+  uint64_t dim, nlist, m, count, train_iterations, seed;
+  uint32_t metric, store_vectors, trained, reserved;
+};
+}  // namespace
+
+void set_error(const std::string& msg) { t_error = msg; }
+const std::string& last_error() { return t_error; }
+SearchStats& thread_stats() { return t_stats; }
+bool& thread_timing() {
+  thread_local bool on = false;
+  return on;
+}
+
+cudaStream_t thread_stream(int device) {
+  thread_local std::map<int, cudaStream_t> streams;
+  auto it = streams.find(device);
+  if (it != streams.end()) return it->second;
+  cudaStream_t s = nullptr;
+  QV_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  streams[device] = s;
+  return s;
+}
+
+int sm_count(int device) {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = cache.find(device);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  QV_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device));
+  cache[device] = n;
+  return n;
+}
+
+void check_finite(const float* v, size_t count) {
+  bool ok = true;
+  for (size_t i = 0; i < count; ++i) ok &= std::isfinite(v[i]);
+  QV_REQUIRE(ok, "vectors must not contain NaN or infinity");
+}
+
+namespace {
+
+void check_metric(uint32_t metric) {
+  QV_REQUIRE(metric == QV_METRIC_L2 || metric == QV_METRIC_IP || metric == QV_METRIC_COSINE,
+             "unknown metric");
+}
+
+void check_labels(const uint64_t* labels, size_t n) {
+  if (labels == nullptr) return;
+  QV_REQUIRE(std::find(labels, labels + n, kInvalidLabel) == labels + n,
+             "label 2^64-1 is reserved (it marks empty result slots)");
+}
+
+template <class T>
+void h2d(DeviceBuffer& dst, const T* src, size_t n, cudaStream_t st) {
+  dst.allocate(std::max<size_t>(1, n) * sizeof(T), st);
+  if (n > 0) QV_CUDA(cudaMemcpyAsync(dst.get(), src, n * sizeof(T), cudaMemcpyHostToDevice, st));
+}
+
+// Device position bitmap for a host filter (nullptr when there is no filter).
+DeviceBuffer device_filter(const uint64_t* d_labels, size_t count, const qv_filter* f,
+                           cudaStream_t st) {
+  DeviceBuffer bm;
+  if (f == nullptr) return bm;
+  bm.allocate(std::max<size_t>(1, (count + 63) / 64) * sizeof(uint64_t), st);
+  build_position_bitmap(d_labels, count, *f, bm.get<uint64_t>(), st);
+  return bm;
+}
+
+void fill_unfilled(uint64_t* labels, float* dists, size_t n) {
+  std::fill(labels, labels + n, kInvalidLabel);
+  std::fill(dists, dists + n, std::numeric_limits<float>::infinity());
+}
+
+size_t result_size(size_t nq, size_t k) {
+  size_t total = 0;
+  QV_REQUIRE(!__builtin_mul_overflow(nq, k, &total) && total <= (size_t{1} << 40),
+             "nq * k is too large");
+  return total;
+}
+
+// ---- IVF list bookkeeping ----------------------------------------------------------------------
+
+// Gathers rows of `src_old` (old storage order) and `src_new` (new rows) into `dst` following
+// `from`: value < n_old picks an old row, otherwise row (value - n_old) of the new batch.
+__global__ void gather_rows_kernel(const float* src_old, size_t n_old, const float* src_new,
+                                   const uint64_t* from, size_t n_total, int dim, float* dst) {
+  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  if (i >= n_total * dim) return;
+  const size_t r = i / dim;
+  const int c = static_cast<int>(i - r * dim);
+  const uint64_t f = from[r];
+  dst[i] = f < n_old ? src_old[f * dim + c] : src_new[(f - n_old) * dim + c];
+}
+
+void ivf_append(IvfState& s, const std::vector<uint32_t>& assign, const std::vector<uint8_t>& codes,
+                const std::vector<uint64_t>& labels, const float* d_new_vectors, cudaStream_t st) {
+  const size_t n = assign.size(), m = s.m, nlist = s.nlist;
+  std::vector<uint64_t> extra(nlist, 0);
+  for (uint32_t l : assign) ++extra[l];
+  for (size_t l = 0; l < nlist; ++l) {
+    const uint64_t len = s.host_offsets[l + 1] - s.host_offsets[l];
+    QV_REQUIRE(len + extra[l] <= std::numeric_limits<uint32_t>::max(),
+               "too many vectors in one IVF cell (2^32 limit); use a larger nlist");
+  }
+  std::vector<uint64_t> off(nlist + 1, 0);
+  for (size_t l = 0; l < nlist; ++l)
+    off[l + 1] = off[l] + (s.host_offsets[l + 1] - s.host_offsets[l]) + extra[l];
+  const size_t total = s.count + n;
+  std::vector<uint8_t> new_codes(total * m);
+  std::vector<uint64_t> new_labels(total);
+  std::vector<uint64_t> from(total);
+  std::vector<uint64_t> cursor(nlist);
+  for (size_t l = 0; l < nlist; ++l) {  // old entries first, in their order
+    const uint64_t b = s.host_offsets[l], e = s.host_offsets[l + 1];
+    std::memcpy(new_codes.data() + off[l] * m, s.host_codes.data() + b * m, (e - b) * m);
+    for (uint64_t i = b; i < e; ++i) {
+      new_labels[off[l] + (i - b)] = s.host_labels[i];
+      from[off[l] + (i - b)] = i;
+    }
+    cursor[l] = off[l] + (e - b);
+  }
+  for (size_t i = 0; i < n; ++i) {  // then the new ones in input order (src/ivfpq_index.cc:263-269)
+    const uint64_t pos = cursor[assign[i]]++;
+    std::memcpy(new_codes.data() + pos * m, codes.data() + i * m, m);
+    new_labels[pos] = labels[i];
+    from[pos] = s.count + i;
+  }
+  if (s.store_vectors) {
+    DeviceBuffer dfrom, nv(std::max<size_t>(1, total * s.dim) * sizeof(float));
+    h2d(dfrom, from.data(), total, st);
+    gather_rows_kernel<<<ceil_div(total * s.dim, 256), 256, 0, st>>>(
+        s.vectors.get<float>(), s.count, d_new_vectors, dfrom.get<uint64_t>(), total,
+        static_cast<int>(s.dim), nv.get<float>());
+    check_launch("gather_rows_kernel");
+    QV_CUDA(cudaStreamSynchronize(st));
+    s.vectors = std::move(nv);
+  }
+  s.host_offsets = std::move(off);
+  s.host_codes = std::move(new_codes);
+  s.host_labels = std::move(new_labels);
+  s.count = total;
+  ivf_upload_lists(s, st);
+}
+
+void ivf_validate_params(const qv_ivfpq_params& p) {
+  QV_REQUIRE(p.dim >= 1 && p.dim <= kMaxDimension,
+             "dimension must be in [1, " + std::to_string(kMaxDimension) + "]");
+  QV_REQUIRE(p.m > 0 && p.dim % p.m == 0, "PQ: dimension " + std::to_string(p.dim) +
+                                              " must be divisible by m=" + std::to_string(p.m));
+  QV_REQUIRE(p.nlist >= 1 && p.nlist <= kMaxLists, "nlist must be in [1, 2^24]");
+  check_metric(p.metric);
+}
+
+std::unique_ptr<qv_ivfpq> ivf_new(int device, const qv_ivfpq_params& p) {
+  ivf_validate_params(p);
+  auto h = std::make_unique<qv_ivfpq>();
+  IvfState& s = h->s;
+  s.device = device;
+  s.dim = p.dim;
+  s.nlist = p.nlist;
+  s.m = p.m;
+  s.dsub = p.dim / p.m;
+  s.metric = p.metric;
+  s.train_iterations = p.train_iterations;
+  s.store_vectors = p.store_vectors != 0;
+  s.seed = p.seed;
+  s.host_offsets.assign(p.nlist + 1, 0);
+  s.host_global_base.assign(p.nlist, 0);
+  DeviceScope scope(device);
+  ivf_upload_lists(s, thread_stream(device));
+  return h;
+}
+
+void ivf_load_into(qv_ivfpq** out, int device, const char* path, bool verify, bool shard,
+                   uint64_t label_begin, uint64_t label_end) {
+  QV_REQUIRE(path != nullptr && out != nullptr, "null argument");
+  QvrFile f(path, QvrKind::kIvfPq, verify);
+  const std::string corrupt = std::string("corrupt index file '") + path + "': ";
+  IvfPqMeta meta;
+  std::memcpy(&meta, f.array(kMeta, 1, sizeof(IvfPqMeta)), sizeof(meta));
+  auto chk = [&](bool c, const char* what) {
+    if (!c) fail(QV_ERR_IO, corrupt + what);
+  };
+  chk(meta.dim >= 1 && meta.dim <= 65536, "bad dimension");
+  chk(meta.m >= 1 && meta.m <= meta.dim && meta.dim % meta.m == 0, "bad m");
+  chk(meta.nlist >= 1 && meta.nlist <= kMaxLists, "bad nlist");
+  chk((meta.nlist + 1) * sizeof(uint64_t) <= f.size(), "bad nlist");
+  chk(meta.metric <= QV_METRIC_COSINE, "bad metric");
+  chk(meta.count <= f.size(), "bad count");
+  qv_ivfpq_params p{meta.dim, meta.metric, meta.nlist, meta.m, meta.train_iterations,
+                    meta.store_vectors != 0, meta.seed};
+  auto h = ivf_new(device, p);
+  IvfState& s = h->s;
+  DeviceScope scope(device);
+  cudaStream_t st = thread_stream(device);
+  const size_t count = meta.count, d = s.dim;
+  if (meta.trained != 0) {
+    const float* cent = reinterpret_cast<const float*>(f.array(kCent, s.nlist * d, 4));
+    const float* cb =
+        reinterpret_cast<const float*>(f.array(kPqcb, s.m * kSubCentroids * s.dsub, 4));
+    bool finite = true;
+    for (size_t i = 0; i < s.nlist * d; ++i) finite &= std::isfinite(cent[i]);
+    for (size_t i = 0; i < s.m * kSubCentroids * s.dsub; ++i) finite &= std::isfinite(cb[i]);
+    chk(finite, "non-finite centroids");
+    ivf_set_trained(s, cent, cb, st);
+  } else {
+    chk(count == 0, "untrained index with vectors");
+  }
+  const uint64_t* offsets = reinterpret_cast<const uint64_t*>(f.array(kLoff, s.nlist + 1, 8));
+  chk(offsets[0] == 0 && offsets[s.nlist] == count, "bad list offsets");
+  for (size_t l = 0; l < s.nlist; ++l) chk(offsets[l] <= offsets[l + 1], "bad list offsets");
+  const uint8_t* codes = f.array(kCode, count * s.m, 1);
+  const uint64_t* labels = reinterpret_cast<const uint64_t*>(f.array(kLabl, count, 8));
+  const float* vectors = nullptr;
+  if (s.store_vectors) {
+    vectors = reinterpret_cast<const float*>(f.array(kVect, count * d, 4));
+    bool finite = true;
+    for (size_t i = 0; i < count * d; ++i) finite &= std::isfinite(vectors[i]);
+    chk(finite, "non-finite stored vectors");
+  }
+  // Keep every entry, or (shard) the entries whose label is in [label_begin, label_end).
+  std::vector<uint64_t> keep_pos;
+  keep_pos.reserve(shard ? count / 2 : count);
+  std::vector<uint64_t> off(s.nlist + 1, 0);
+  std::vector<uint32_t> gbase(s.nlist, 0);
+  for (size_t l = 0; l < s.nlist; ++l) {
+    bool first = true;
+    for (uint64_t i = offsets[l]; i < offsets[l + 1]; ++i) {
+      if (shard && (labels[i] < label_begin || labels[i] >= label_end)) continue;
+      if (first) {
+        gbase[l] = static_cast<uint32_t>(i - offsets[l]);
+        first = false;
+      }
+      keep_pos.push_back(i);
+    }
+    off[l + 1] = keep_pos.size();
+  }
+  s.count = keep_pos.size();
+  s.host_offsets = std::move(off);
+  s.host_global_base = std::move(gbase);
+  s.host_codes.resize(s.count * s.m);
+  s.host_labels.resize(s.count);
+  for (size_t i = 0; i < s.count; ++i) {
+    std::memcpy(s.host_codes.data() + i * s.m, codes + keep_pos[i] * s.m, s.m);
+    s.host_labels[i] = labels[keep_pos[i]];
+  }
+  if (shard) {  // entries of a list kept by one shard must be contiguous in the full list
+    for (size_t l = 0; l < s.nlist; ++l) {
+      const uint64_t b = s.host_offsets[l], e = s.host_offsets[l + 1];
+      if (e > b)
+        chk(keep_pos[e - 1] - keep_pos[b] == e - b - 1,
+            "label range of a shard is not contiguous within an inverted list");
+    }
+  }
+  ivf_upload_lists(s, st);
+  if (s.store_vectors) {
+    s.vectors.allocate(std::max<size_t>(1, s.count * d) * sizeof(float));
+    std::vector<float> v(s.count * d);
+    for (size_t i = 0; i < s.count; ++i)
+      std::memcpy(v.data() + i * d, vectors + keep_pos[i] * d, d * sizeof(float));
+    if (!v.empty())
+      QV_CUDA(cudaMemcpyAsync(s.vectors.get(), v.data(), v.size() * sizeof(float),
+                              cudaMemcpyHostToDevice, st));
+    QV_CUDA(cudaStreamSynchronize(st));
+  }
+  *out = h.release();
+}
+
+}  // namespace
+}  // namespace qv
+
+using namespace qv;
+
+extern "C" {
+
+const char* qv_last_error(void) { return qv::last_error().c_str(); }
+const char* qv_version(void) { return "quiver-b200 0.1.0 (sm_100a)"; }
+
+qv_status qv_device_count(int* count) {
+  return guarded([&] {
+    QV_REQUIRE(count != nullptr, "null argument");
+    QV_CUDA(cudaGetDeviceCount(count));
+  });
+}
+
+qv_status qv_last_search_stats(qv_search_stats* stats) {
+  return guarded([&] {
+    QV_REQUIRE(stats != nullptr, "null argument");
+    std::memset(stats, 0, sizeof(*stats));
+    stats->kernel_launches = t_stats.kernel_launches;
+    stats->rescanned_queries = t_stats.rescanned_queries;
+    stats->dominant_kernel_ms = t_stats.dominant_ms;
+    stats->dominant_kernel_work = t_stats.dominant_work;
+    stats->dominant_work_is_bytes = t_stats.work_is_bytes ? 1u : 0u;
+    std::strncpy(stats->dominant_kernel, t_stats.dominant_name.c_str(),
+                 sizeof(stats->dominant_kernel) - 1);
+  });
+}
+
+qv_status qv_set_timing(int enable) {
+  return guarded([&] { thread_timing() = enable != 0; });
+}
+
+qv_status qv_device_free(int device, void* ptr) {
+  return guarded([&] {
+    DeviceScope scope(device);
+    if (ptr != nullptr) QV_CUDA(cudaFree(ptr));
+  });
+}
+
+// ---- Flat --------------------------------------------------------------------------------------
+
+qv_status qv_flat_create(int device, size_t dim, uint32_t metric, qv_flat** out) {
+  return guarded([&] {
+    QV_REQUIRE(out != nullptr, "null argument");
+    QV_REQUIRE(dim >= 1 && dim <= kMaxDimension,
+               "dimension must be in [1, " + std::to_string(kMaxDimension) + "]");
+    check_metric(metric);
+    int ndev = 0;
+    QV_CUDA(cudaGetDeviceCount(&ndev));
+    QV_REQUIRE(device >= 0 && device < ndev, "no CUDA device " + std::to_string(device));
+    auto h = std::make_unique<qv_flat>();
+    h->s.device = device;
+    h->s.dim = dim;
+    h->s.metric = metric;
+    *out = h.release();
+  });
+}
+
+qv_status qv_flat_destroy(qv_flat* index) {
+  return guarded([&] {
+    if (index == nullptr) return;
+    DeviceScope scope(index->s.device);
+    delete index;
+  });
+}
+
+qv_status qv_flat_add(qv_flat* index, const float* vectors, size_t n, const uint64_t* labels) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr, "null index");
+    if (n == 0) return;  // src/flat_index.cc:50
+    QV_REQUIRE(vectors != nullptr, "vectors must not be null");
+    FlatState& s = index->s;
+    check_finite(vectors, n * s.dim);
+    check_labels(labels, n);
+    std::unique_lock lock(index->mu);
+    QV_REQUIRE(s.n + n <= std::numeric_limits<uint32_t>::max(),
+               "FlatIndex holds at most 2^32 vectors");
+    DeviceScope scope(s.device);
+    cudaStream_t st = thread_stream(s.device);
+    std::vector<uint64_t> lab(n);
+    for (size_t i = 0; i < n; ++i) lab[i] = labels ? labels[i] : s.n + i;
+    flat_reserve(s, s.n + n, st);
+    QV_CUDA(cudaMemcpyAsync(s.x.get<float>() + s.n * s.dim, vectors, n * s.dim * sizeof(float),
+                            cudaMemcpyHostToDevice, st));
+    DeviceBuffer dl;
+    h2d(dl, lab.data(), n, st);
+    flat_append(s, s.x.get<float>() + s.n * s.dim, dl.get<uint64_t>(), n, st);
+    s.host_labels.insert(s.host_labels.end(), lab.begin(), lab.end());
+  });
+}
+
+qv_status qv_flat_search(const qv_flat* index, const float* queries, size_t nq, size_t k,
+                         const qv_filter* filter, uint64_t* labels, float* distances) {
+  return guarded([&] {
+    t_stats = SearchStats{};
+    QV_REQUIRE(index != nullptr, "null index");
+    if (nq == 0 || k == 0) return;  // src/flat_index.cc:128
+    QV_REQUIRE(queries != nullptr && labels != nullptr && distances != nullptr,
+               "search_batch: null buffer");
+    const FlatState& s = index->s;
+    const size_t total = result_size(nq, k);
+    check_finite(queries, nq * s.dim);
+    std::shared_lock lock(index->mu);
+    DeviceScope scope(s.device);
+    cudaStream_t st = thread_stream(s.device);
+    DeviceBuffer dq, dl(total * sizeof(uint64_t), st), dd(total * sizeof(float), st);
+    h2d(dq, queries, nq * s.dim, st);
+    DeviceBuffer bm = device_filter(s.labels.get<uint64_t>(), s.n, filter, st);
+    flat_search(s, dq.get<float>(), nq, k, bm.get<uint64_t>(), dl.get<uint64_t>(),
+                dd.get<float>(), nullptr, st);
+    QV_CUDA(cudaMemcpyAsync(labels, dl.get(), total * sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaMemcpyAsync(distances, dd.get(), total * sizeof(float), cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaStreamSynchronize(st));
+  });
+}
+
+qv_status qv_flat_search_device(const qv_flat* index, const float* queries, size_t nq, size_t k,
+                                const uint64_t* position_bitmap, uint64_t* labels,
+                                float* distances, uint64_t* keys, void* stream) {
+  return guarded([&] {
+    t_stats = SearchStats{};
+    QV_REQUIRE(index != nullptr, "null index");
+    if (nq == 0 || k == 0) return;
+    QV_REQUIRE(queries != nullptr && labels != nullptr && distances != nullptr,
+               "search_batch: null buffer");
+    result_size(nq, k);
+    const FlatState& s = index->s;
+    std::shared_lock lock(index->mu);
+    DeviceScope scope(s.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(s.device);
+    flat_search(s, queries, nq, k, position_bitmap, labels, distances, keys, st);
+  });
+}
+
+qv_status qv_flat_set_row_offset(qv_flat* index, uint64_t row_offset) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr, "null index");
+    std::unique_lock lock(index->mu);
+    index->s.row_offset = row_offset;
+  });
+}
+
+qv_status qv_flat_info(const qv_flat* index, size_t* size, size_t* dim, uint32_t* metric) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr, "null index");
+    std::shared_lock lock(index->mu);
+    if (size) *size = index->s.n;
+    if (dim) *dim = index->s.dim;
+    if (metric) *metric = index->s.metric;
+  });
+}
+
+qv_status qv_flat_rows(const qv_flat* index, size_t first, size_t count, float* vectors,
+                       uint64_t* labels) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr, "null index");
+    std::shared_lock lock(index->mu);
+    const FlatState& s = index->s;
+    QV_REQUIRE(first <= s.n && count <= s.n - first, "row range out of bounds");
+    if (count == 0) return;
+    DeviceScope scope(s.device);
+    cudaStream_t st = thread_stream(s.device);
+    if (vectors)
+      QV_CUDA(cudaMemcpyAsync(vectors, s.x.get<float>() + first * s.dim,
+                              count * s.dim * sizeof(float), cudaMemcpyDeviceToHost, st));
+    if (labels) std::memcpy(labels, s.host_labels.data() + first, count * sizeof(uint64_t));
+    QV_CUDA(cudaStreamSynchronize(st));
+  });
+}
+
+qv_status qv_flat_filter_bitmap(const qv_flat* index, const qv_filter* filter,
+                                uint64_t** device_bitmap) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr && filter != nullptr && device_bitmap != nullptr, "null argument");
+    std::shared_lock lock(index->mu);
+    const FlatState& s = index->s;
+    DeviceScope scope(s.device);
+    cudaStream_t st = thread_stream(s.device);
+    const size_t words = std::max<size_t>(1, (s.n + 63) / 64);
+    void* p = nullptr;
+    QV_CUDA(cudaMalloc(&p, words * sizeof(uint64_t)));
+    build_position_bitmap(s.labels.get<uint64_t>(), s.n, *filter, static_cast<uint64_t*>(p), st);
+    QV_CUDA(cudaStreamSynchronize(st));
+    *device_bitmap = static_cast<uint64_t*>(p);
+  });
+}
+
+qv_status qv_flat_save(const qv_flat* index, const char* path) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr && path != nullptr, "null argument");
+    std::shared_lock lock(index->mu);
+    const FlatState& s = index->s;
+    std::vector<float> v(s.n * s.dim);
+    if (!v.empty()) {
+      DeviceScope scope(s.device);
+      cudaStream_t st = thread_stream(s.device);
+      QV_CUDA(cudaMemcpyAsync(v.data(), s.x.get(), v.size() * sizeof(float), cudaMemcpyDeviceToHost, st));
+      QV_CUDA(cudaStreamSynchronize(st));
+    }
+    FlatMeta meta{s.dim, s.n, s.metric, 0};
+    QvrWriter w(QvrKind::kFlat);
+    w.add(kMeta, &meta, sizeof(meta));
+    w.add(kVect, v.data(), v.size() * sizeof(float));
+    w.add(kLabl, s.host_labels.data(), s.host_labels.size() * sizeof(uint64_t));
+    w.commit(path);
+  });
+}
+
+qv_status qv_flat_load(int device, const char* path, int verify_checksums, qv_flat** out) {
+  return guarded([&] {
+    QV_REQUIRE(path != nullptr && out != nullptr, "null argument");
+    QvrFile f(path, QvrKind::kFlat, verify_checksums != 0);
+    FlatMeta meta;
+    std::memcpy(&meta, f.array(kMeta, 1, sizeof(FlatMeta)), sizeof(meta));
+    const std::string corrupt = "corrupt index file: ";
+    if (!(meta.dim > 0 && meta.dim <= kMaxDimension)) fail(QV_ERR_IO, corrupt + "bad dimension");
+    if (meta.metric > QV_METRIC_COSINE) fail(QV_ERR_IO, corrupt + "unknown metric");
+    if (meta.count > f.size() / sizeof(uint64_t)) fail(QV_ERR_IO, corrupt + "bad vector count");
+    if (meta.count > f.size() / (meta.dim * sizeof(float) + 1))
+      fail(QV_ERR_IO, corrupt + "bad vector count");
+    const float* v = reinterpret_cast<const float*>(f.array(kVect, meta.count * meta.dim, 4));
+    const uint64_t* l = reinterpret_cast<const uint64_t*>(f.array(kLabl, meta.count, 8));
+    for (size_t i = 0; i < meta.count * meta.dim; ++i)
+      if (!std::isfinite(v[i])) fail(QV_ERR_IO, corrupt + "non-finite vector values");
+    qv_flat* h = nullptr;
+    qv_status st = qv_flat_create(device, meta.dim, meta.metric, &h);
+    if (st != QV_OK) fail(st, last_error());
+    std::unique_ptr<qv_flat> owner(h);
+    // Stored rows are already normalized: append them without re-normalizing.
+    FlatState& s = h->s;
+    if (meta.count > 0) {
+      DeviceScope scope(device);
+      cudaStream_t cs = thread_stream(device);
+      flat_reserve(s, meta.count, cs);
+      QV_CUDA(cudaMemcpyAsync(s.x.get(), v, meta.count * meta.dim * sizeof(float),
+                              cudaMemcpyHostToDevice, cs));
+      DeviceBuffer dl;
+      h2d(dl, l, meta.count, cs);
+      const uint32_t metric = s.metric;
+      s.metric = QV_METRIC_L2;  // skip the normalization pass of flat_append
+      flat_append(s, s.x.get<float>(), dl.get<uint64_t>(), meta.count, cs);
+      s.metric = metric;
+      s.host_labels.assign(l, l + meta.count);
+    }
+    *out = owner.release();
+  });
+}
+
+// ---- IVF-PQ ------------------------------------------------------------------------------------
+
+qv_status qv_ivfpq_create(int device, const qv_ivfpq_params* params, qv_ivfpq** out) {
+  return guarded([&] {
+    QV_REQUIRE(params != nullptr && out != nullptr, "null argument");
+    int ndev = 0;
+    QV_CUDA(cudaGetDeviceCount(&ndev));
+    QV_REQUIRE(device >= 0 && device < ndev, "no CUDA device " + std::to_string(device));
+    *out = ivf_new(device, *params).release();
+  });
+}
+
+qv_status qv_ivfpq_destroy(qv_ivfpq* index) {
+  return guarded([&] {
+    if (index == nullptr) return;
+    DeviceScope scope(index->s.device);
+    delete index;
+  });
+}
+
+qv_status qv_ivfpq_train(qv_ivfpq* index, const float* vectors, size_t n) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr, "null index");
+    (void)vectors;
+    (void)n;
+    fail(QV_ERR_UNSUPPORTED,
+         "IVF-PQ training is not part of the GPU search path: load a trained index (.qvr) or "
+         "install centroids and codebooks with set_trained");
+  });
+}
+
+qv_status qv_ivfpq_set_trained(qv_ivfpq* index, const float* centroids, const float* codebooks) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr && centroids != nullptr && codebooks != nullptr, "null argument");
+    std::unique_lock lock(index->mu);
+    IvfState& s = index->s;
+    QV_REQUIRE(!s.trained, "index is already trained");
+    check_finite(centroids, s.nlist * s.dim);
+    check_finite(codebooks, s.m * kSubCentroids * s.dsub);
+    DeviceScope scope(s.device);
+    ivf_set_trained(s, centroids, codebooks, thread_stream(s.device));
+  });
+}
+
+qv_status qv_ivfpq_is_trained(const qv_ivfpq* index, int* trained) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr && trained != nullptr, "null argument");
+    std::shared_lock lock(index->mu);
+    *trained = index->s.trained ? 1 : 0;
+  });
+}
+
+static void ivf_encode_host(const IvfState& s, const float* vectors, size_t n, cudaStream_t st,
+                            DeviceBuffer& dx, std::vector<uint32_t>& assign,
+                            std::vector<uint8_t>& codes) {
+  h2d(dx, vectors, n * s.dim, st);
+  if (s.metric == QV_METRIC_COSINE) normalize_rows_device(dx.get<float>(), n, s.dim, st);
+  DeviceBuffer da(n * sizeof(uint32_t), st), dc(n * s.m, st);
+  ivf_encode_device(s, dx.get<float>(), n, da.get<uint32_t>(), dc.get<uint8_t>(), st);
+  assign.resize(n);
+  codes.resize(n * s.m);
+  QV_CUDA(cudaMemcpyAsync(assign.data(), da.get(), n * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+  QV_CUDA(cudaMemcpyAsync(codes.data(), dc.get(), n * s.m, cudaMemcpyDeviceToHost, st));
+  QV_CUDA(cudaStreamSynchronize(st));
+}
+
+qv_status qv_ivfpq_add(qv_ivfpq* index, const float* vectors, size_t n, const uint64_t* labels) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr, "null index");
+    QV_REQUIRE(vectors != nullptr || n == 0, "vectors must not be null");
+    if (n == 0) return;
+    IvfState& s = index->s;
+    check_finite(vectors, n * s.dim);
+    check_labels(labels, n);
+    {
+      std::shared_lock lock(index->mu);
+      QV_REQUIRE(s.trained, "IVF-PQ index must be trained before add()");
+    }
+    DeviceScope scope(s.device);
+    cudaStream_t st = thread_stream(s.device);
+    DeviceBuffer dx;
+    std::vector<uint32_t> assign;
+    std::vector<uint8_t> codes;
+    ivf_encode_host(s, vectors, n, st, dx, assign, codes);  // trained state is immutable
+    std::unique_lock lock(index->mu);
+    std::vector<uint64_t> lab(n);
+    for (size_t i = 0; i < n; ++i) lab[i] = labels ? labels[i] : s.count + i;
+    ivf_append(s, assign, codes, lab, dx.get<float>(), st);
+  });
+}
+
+qv_status qv_ivfpq_encode(const qv_ivfpq* index, const float* vectors, size_t n, uint32_t* assign,
+                          uint8_t* codes) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr && (n == 0 || (vectors && assign && codes)), "null argument");
+    if (n == 0) return;
+    const IvfState& s = index->s;
+    check_finite(vectors, n * s.dim);
+    std::shared_lock lock(index->mu);
+    QV_REQUIRE(s.trained, "IVF-PQ index must be trained before add()");
+    DeviceScope scope(s.device);
+    cudaStream_t st = thread_stream(s.device);
+    DeviceBuffer dx;
+    std::vector<uint32_t> a;
+    std::vector<uint8_t> c;
+    ivf_encode_host(s, vectors, n, st, dx, a, c);
+    std::memcpy(assign, a.data(), n * sizeof(uint32_t));
+    std::memcpy(codes, c.data(), n * s.m);
+  });
+}
+
+qv_status qv_ivfpq_search(const qv_ivfpq* index, const float* queries, size_t nq, size_t k,
+                          size_t nprobe, size_t refine_factor, const qv_filter* filter,
+                          uint64_t* labels, float* distances) {
+  return guarded([&] {
+    t_stats = SearchStats{};
+    QV_REQUIRE(index != nullptr, "null index");
+    if (nq == 0 || k == 0) return;  // src/ivfpq_index.cc:424
+    QV_REQUIRE(queries != nullptr && labels != nullptr && distances != nullptr,
+               "search_batch: null buffer");
+    const IvfState& s = index->s;
+    const size_t total = result_size(nq, k);
+    check_finite(queries, nq * s.dim);
+    std::shared_lock lock(index->mu);
+    if (!s.trained || s.count == 0) {
+      fill_unfilled(labels, distances, total);
+      return;
+    }
+    DeviceScope scope(s.device);
+    cudaStream_t st = thread_stream(s.device);
+    DeviceBuffer dq, dl(total * sizeof(uint64_t), st), dd(total * sizeof(float), st);
+    h2d(dq, queries, nq * s.dim, st);
+    DeviceBuffer bm = device_filter(s.labels.get<uint64_t>(), s.count, filter, st);
+    ivf_search(s, dq.get<float>(), nq, k, nprobe, refine_factor, bm.get<uint64_t>(),
+               dl.get<uint64_t>(), dd.get<float>(), st);
+    QV_CUDA(cudaMemcpyAsync(labels, dl.get(), total * sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaMemcpyAsync(distances, dd.get(), total * sizeof(float), cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaStreamSynchronize(st));
+  });
+}
+
+qv_status qv_ivfpq_search_device(const qv_ivfpq* index, const float* queries, size_t nq, size_t k,
+                                 size_t nprobe, size_t refine_factor,
+                                 const uint64_t* position_bitmap, uint64_t* labels,
+                                 float* distances, void* stream) {
+  return guarded([&] {
+    t_stats = SearchStats{};
+    QV_REQUIRE(index != nullptr, "null index");
+    if (nq == 0 || k == 0) return;
+    result_size(nq, k);
+    const IvfState& s = index->s;
+    std::shared_lock lock(index->mu);
+    DeviceScope scope(s.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(s.device);
+    ivf_search(s, queries, nq, k, nprobe, refine_factor, position_bitmap, labels, distances, st);
+  });
+}
+
+qv_status qv_ivfpq_candidates_device(const qv_ivfpq* index, const float* queries, size_t nq,
+                                     size_t keep, size_t nprobe, const uint64_t* position_bitmap,
+                                     float* distances, uint64_t* keys, uint64_t* labels,
+                                     void* stream) {
+  return guarded([&] {
+    t_stats = SearchStats{};
+    QV_REQUIRE(index != nullptr && distances && keys && labels, "null argument");
+    const IvfState& s = index->s;
+    std::shared_lock lock(index->mu);
+    DeviceScope scope(s.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(s.device);
+    ivf_candidates(s, queries, nq, keep, nprobe, position_bitmap, distances, keys, labels, st);
+  });
+}
+
+qv_status qv_ivfpq_refine_device(const qv_ivfpq* index, const float* queries, size_t nq,
+                                 size_t keep, const uint64_t* keys, float* exact, void* stream) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr && keys && exact, "null argument");
+    const IvfState& s = index->s;
+    std::shared_lock lock(index->mu);
+    DeviceScope scope(s.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(s.device);
+    ivf_refine(s, queries, nq, keep, keys, exact, st);
+  });
+}
+
+qv_status qv_ivfpq_filter_bitmap(const qv_ivfpq* index, const qv_filter* filter,
+                                 uint64_t** device_bitmap) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr && filter != nullptr && device_bitmap != nullptr, "null argument");
+    std::shared_lock lock(index->mu);
+    const IvfState& s = index->s;
+    DeviceScope scope(s.device);
+    cudaStream_t st = thread_stream(s.device);
+    const size_t words = std::max<size_t>(1, (s.count + 63) / 64);
+    void* p = nullptr;
+    QV_CUDA(cudaMalloc(&p, words * sizeof(uint64_t)));
+    build_position_bitmap(s.labels.get<uint64_t>(), s.count, *filter, static_cast<uint64_t*>(p), st);
+    QV_CUDA(cudaStreamSynchronize(st));
+    *device_bitmap = static_cast<uint64_t*>(p);
+  });
+}
+
+qv_status qv_ivfpq_info(const qv_ivfpq* index, qv_ivfpq_params* params, size_t* size,
+                        size_t* memory_bytes) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr, "null index");
+    std::shared_lock lock(index->mu);
+    const IvfState& s = index->s;
+    if (params) {
+      params->dim = s.dim;
+      params->metric = s.metric;
+      params->nlist = s.nlist;
+      params->m = s.m;
+      params->train_iterations = s.train_iterations;
+      params->store_vectors = s.store_vectors ? 1 : 0;
+      params->seed = s.seed;
+    }
+    if (size) *size = s.count;
+    if (memory_bytes) {  // src/ivfpq_index.cc:446-455
+      size_t b = (s.trained ? s.nlist * s.dim + s.m * kSubCentroids * s.dsub : 0) * sizeof(float);
+      b += s.precomputed.bytes();
+      b += s.count * s.m + s.count * sizeof(uint64_t);
+      if (s.store_vectors) b += s.count * s.dim * sizeof(float);
+      *memory_bytes = b;
+    }
+  });
+}
+
+qv_status qv_ivfpq_list_sizes(const qv_ivfpq* index, uint64_t* sizes) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr && sizes != nullptr, "null argument");
+    std::shared_lock lock(index->mu);
+    const IvfState& s = index->s;
+    for (size_t l = 0; l < s.nlist; ++l) sizes[l] = s.host_offsets[l + 1] - s.host_offsets[l];
+  });
+}
+
+qv_status qv_ivfpq_labels(const qv_ivfpq* index, uint64_t* labels) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr && labels != nullptr, "null argument");
+    std::shared_lock lock(index->mu);
+    std::memcpy(labels, index->s.host_labels.data(), index->s.count * sizeof(uint64_t));
+  });
+}
+
+qv_status qv_ivfpq_save(const qv_ivfpq* index, const char* path) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr && path != nullptr, "null argument");
+    std::shared_lock lock(index->mu);
+    const IvfState& s = index->s;
+    IvfPqMeta meta{s.dim, s.nlist, s.m, s.count, s.train_iterations, s.seed, s.metric,
+                   s.store_vectors ? 1u : 0u, s.trained ? 1u : 0u, 0};
+    std::vector<float> vec;
+    if (s.store_vectors && s.count > 0) {
+      vec.resize(s.count * s.dim);
+      DeviceScope scope(s.device);
+      cudaStream_t st = thread_stream(s.device);
+      QV_CUDA(cudaMemcpyAsync(vec.data(), s.vectors.get(), vec.size() * sizeof(float),
+                              cudaMemcpyDeviceToHost, st));
+      QV_CUDA(cudaStreamSynchronize(st));
+    }
+    QvrWriter w(QvrKind::kIvfPq);
+    w.add(kMeta, &meta, sizeof(meta));
+    w.add(kCent, s.host_centroids.data(), s.host_centroids.size() * sizeof(float));
+    w.add(kPqcb, s.host_codebooks.data(), s.host_codebooks.size() * sizeof(float));
+    w.add(kLoff, s.host_offsets.data(), s.host_offsets.size() * sizeof(uint64_t));
+    w.add(kCode, s.host_codes.data(), s.host_codes.size());
+    w.add(kLabl, s.host_labels.data(), s.host_labels.size() * sizeof(uint64_t));
+    if (s.store_vectors) w.add(kVect, vec.data(), vec.size() * sizeof(float));
+    w.commit(path);
+  });
+}
+
+qv_status qv_ivfpq_load(int device, const char* path, int verify_checksums, qv_ivfpq** out) {
+  return guarded(
+      [&] { ivf_load_into(out, device, path, verify_checksums != 0, false, 0, UINT64_MAX); });
+}
+
+qv_status qv_ivfpq_load_shard(int device, const char* path, int verify_checksums,
+                              uint64_t label_begin, uint64_t label_end, qv_ivfpq** out) {
+  return guarded([&] {
+    ivf_load_into(out, device, path, verify_checksums != 0, true, label_begin, label_end);
+  });
+}
+
+// ---- merge -------------------------------------------------------------------------------------
+
+qv_status qv_merge_topk_device(int device, size_t parts, size_t nq, size_t k,
+                               const float* distances, const uint64_t* keys,
+                               const uint64_t* labels, float* out_distances, uint64_t* out_keys,
+                               uint64_t* out_labels, void* stream) {
+  return guarded([&] {
+    QV_REQUIRE(distances && keys && out_distances, "null argument");
+    DeviceScope scope(device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(device);
+    merge_topk(parts, nq, k, distances, keys, labels, out_distances, out_keys, out_labels, st);
+  });
+}
+
+qv_status qv_select_topk_device(int device, size_t nq, size_t n, size_t k, const float* distances,
+                                const uint64_t* keys, const uint64_t* labels,
+                                float* out_distances, uint64_t* out_keys, uint64_t* out_labels,
+                                void* stream) {
+  return guarded([&] {
+    QV_REQUIRE(distances && keys && out_distances, "null argument");
+    QV_REQUIRE(k <= n || n == 0, "select_topk: k > n");
+    DeviceScope scope(device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(device);
+    select_topk(nq, n, k, distances, keys, labels, out_distances, out_keys, out_labels, st);
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,633 @@
+// Exact FlatIndex search on the GPU (src/flat_index.cc:69-140 of the reference).
+//
+// Pipeline per batch:
+//   1. prep:     copy queries into a zero-padded row-major buffer, normalizing cosine queries with
+//                simd::normalize's exact arithmetic; per-query squared norm and norm for the screen.
+//   2. screen:   a fast approximate pass over all rows. Each work unit is (query tile, row chunk);
+//                one thread owns one query and keeps its KK best approximate candidates in a
+//                private max-heap in shared memory. Units publish their KK-th value as a per-query
+//                threshold that later units start from.
+//   3. finalize: per query, merge the units' candidates, keep the KK best, recompute those
+//                exactly in the reference's AVX2 summation order, sort by (distance, row) and emit
+//                the top k. A certificate proves no other row can enter the top k: every row left
+//                out has screen distance >= T (the KK-th candidate's), and |screen - exact| <= eps
+//                (a rigorous float error bound), so T - eps >= D_k (the k-th exact distance)
+//                suffices. Queries that fail it are listed for step 4.
+//   4. rescan:   failed queries are answered by an exact scan of every row (reference arithmetic),
+//                so results never depend on the screen's precision.
+// Distances returned are bit-identical to the reference's; ties are broken by row id.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "qv_state.h"
+
+namespace qv {
+namespace {
+
+using dev::kFull;
+
+constexpr int kScreenRows = 32;   // rows per shared-memory tile of the SIMT screen
+constexpr int kScreenDChunk = 256;  // columns per shared-memory tile
+constexpr int kFinalizeThreads = 256;
+constexpr int kMaxCandidatesPerQuery = 1024;  // n_chunks * KK, merged in one block
+constexpr float kInf = __builtin_huge_valf();
+
+// ---- normalization and per-row statistics ---------------------------------------------------------
+
+// simd::normalize (src/simd/dispatch.cc:119-135) of a row held in memory, by one warp.
+__device__ void warp_normalize(float* v, int dim, int lane) {
+  const float ns = dev::warp_dot_avx2(v, v, dim, lane);
+  __syncwarp();
+  if (!isfinite(ns)) {
+    double acc = 0.0;
+    if (lane == 0) {
+      for (int i = 0; i < dim; ++i) {
+        const double x = static_cast<double>(v[i]);
+        acc = __dadd_rn(acc, __dmul_rn(x, x));
+      }
+    }
+    acc = __shfl_sync(kFull, acc, 0);
+    const double inv = (acc > 0.0 && isfinite(acc)) ? __ddiv_rn(1.0, __dsqrt_rn(acc)) : 0.0;
+    if (inv == 0.0) return;
+    for (int i = lane; i < dim; i += 32) v[i] = __double2float_rn(__dmul_rn(static_cast<double>(v[i]), inv));
+    __syncwarp();
+    return;
+  }
+  if (ns <= 0.0f) return;
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ns));
+  for (int i = lane; i < dim; i += 32) v[i] = __fmul_rn(v[i], inv);
+  __syncwarp();
+}
+
+__global__ void normalize_rows_kernel(float* x, size_t n, int dim) {
+  const int lane = threadIdx.x & 31;
+  const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= n) return;
+  warp_normalize(x + row * dim, dim, lane);
+}
+
+// Squared norm of each row (screen only; any summation order) and the max row norm.
+__global__ void row_stats_kernel(const float* x, size_t n, int dim, float* norm2,
+                                 unsigned* max_norm_bits) {
+  const int lane = threadIdx.x & 31;
+  const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= n) return;
+  const float* v = x + row * dim;
+  float s = 0.0f;
+  for (int i = lane; i < dim; i += 32) s = fmaf(v[i], v[i], s);
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+  if (lane == 0) {
+    norm2[row] = s;
+    atomicMax(max_norm_bits, __float_as_uint(sqrtf(s) * 1.0001f));
+  }
+}
+
+__global__ void to_bf16_kernel(const float* x, size_t n, int dim, int kpad, __nv_bfloat16* out) {
+  const size_t total = n * static_cast<size_t>(kpad);
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t r = i / kpad;
+    const int c = static_cast<int>(i - r * kpad);
+    out[i] = __float2bfloat16_rn(c < dim ? x[r * dim + c] : 0.0f);
+  }
+}
+
+// Queries -> zero-padded rows (dpad columns), normalized for cosine; squared norm and norm.
+__global__ void prep_queries_kernel(const float* q, size_t nq, int dim, int dpad, bool cosine,
+                                    float* qp, float* qnorm2, float* qnorm) {
+  const int lane = threadIdx.x & 31;
+  const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= nq) return;
+  float* out = qp + row * dpad;
+  for (int i = lane; i < dpad; i += 32) out[i] = i < dim ? q[row * dim + i] : 0.0f;
+  __syncwarp();
+  if (cosine) warp_normalize(out, dim, lane);
+  float s = 0.0f;
+  for (int i = lane; i < dim; i += 32) s = fmaf(out[i], out[i], s);
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
+  if (lane == 0) {
+    qnorm2[row] = s;
+    qnorm[row] = sqrtf(s) * 1.0001f;
+  }
+}
+
+// ---- per-thread bounded max-heap in shared memory (interleaved: element i of thread t at i*stride+t)
+
+struct ThreadHeap {
+  float* d;
+  uint32_t* r;
+  int stride;
+  int n;
+  int cap;
+  __device__ float top_d() const { return d[0]; }
+  __device__ uint32_t top_r() const { return r[0]; }
+  __device__ void push(float dist, uint32_t row) {
+    if (n < cap) {  // sift up
+      int i = n++;
+      while (i > 0) {
+        const int p = (i - 1) >> 1;
+        const float pd = d[p * stride];
+        const uint32_t pr = r[p * stride];
+        if (!dev::key_less(pd, pr, dist, row)) break;
+        d[i * stride] = pd;
+        r[i * stride] = pr;
+        i = p;
+      }
+      d[i * stride] = dist;
+      r[i * stride] = row;
+      return;
+    }
+    if (!dev::key_less(dist, row, d[0], r[0])) return;
+    int i = 0;  // replace the root and sift down
+    for (;;) {
+      const int l = 2 * i + 1;
+      if (l >= n) break;
+      int w = l;
+      float wd = d[l * stride];
+      uint32_t wr = r[l * stride];
+      if (l + 1 < n) {
+        const float rd = d[(l + 1) * stride];
+        const uint32_t rr = r[(l + 1) * stride];
+        if (dev::key_less(wd, wr, rd, rr)) {
+          w = l + 1;
+          wd = rd;
+          wr = rr;
+        }
+      }
+      if (!dev::key_less(dist, row, wd, wr)) break;
+      d[i * stride] = wd;
+      r[i * stride] = wr;
+      i = w;
+    }
+    d[i * stride] = dist;
+    r[i * stride] = row;
+  }
+};
+
+// ---- SIMT screen ---------------------------------------------------------------------------------
+// Unit u: chunk = u / n_qtiles, query tile = u % n_qtiles (chunk-major, so concurrently running
+// units share row chunks in L2). Thread t owns query qtile*qpb + t. Screen distance:
+//   L2: ||q||^2 + ||x||^2 - 2<q,x>,  IP/cosine: 1 - <q,x>,  float32 with FMA.
+template <bool kL2>
+__global__ void __launch_bounds__(128) flat_screen_simt_kernel(
+    const float* __restrict__ qp, int dpad, const float* __restrict__ qnorm2, int nq, int qpb,
+    const float* __restrict__ x, int dim, const float* __restrict__ xnorm2, int64_t nrows,
+    const uint64_t* __restrict__ bitmap, int64_t chunk_rows, int n_qtiles, int n_chunks, int kk,
+    float* __restrict__ cand_d, uint32_t* __restrict__ cand_r, int* __restrict__ cand_n,
+    unsigned* __restrict__ thr_bits) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* xs = reinterpret_cast<float*>(smem_raw);  // kScreenRows x kScreenDChunk
+  float* hd = xs + kScreenRows * kScreenDChunk;     // kk x qpb
+  uint32_t* hr = reinterpret_cast<uint32_t*>(hd + static_cast<size_t>(kk) * qpb);
+
+  const int chunk = blockIdx.x / n_qtiles;
+  const int qtile = blockIdx.x - chunk * n_qtiles;
+  const int t = threadIdx.x;
+  const int q = qtile * qpb + t;
+  const bool active = t < qpb && q < nq;
+  const int64_t r0 = static_cast<int64_t>(chunk) * chunk_rows;
+  const int64_t r1 = min(nrows, r0 + chunk_rows);
+
+  ThreadHeap heap{hd + (active ? t : 0), hr + (active ? t : 0), qpb, 0, kk};
+  float thr = active ? dev::from_ordered_bits(thr_bits[q]) : -kInf;
+  const float qn = (active && kL2) ? qnorm2[q] : 0.0f;
+  const float* qrow = qp + static_cast<size_t>(active ? q : 0) * dpad;
+  const int warp = t >> 5, lane = t & 31, nwarps = blockDim.x >> 5;
+
+  for (int64_t rb = r0; rb < r1; rb += kScreenRows) {
+    const int nr = static_cast<int>((r1 - rb < kScreenRows ? r1 - rb : kScreenRows));
+    float acc[kScreenRows];
+#pragma unroll
+    for (int r = 0; r < kScreenRows; ++r) acc[r] = 0.0f;
+    for (int c0 = 0; c0 < dim; c0 += kScreenDChunk) {
+      const int dc = min(kScreenDChunk, dpad - c0);
+      __syncthreads();
+      for (int rr = warp; rr < kScreenRows; rr += nwarps) {
+        const float* src = x + (rb + rr) * static_cast<int64_t>(dim);
+        for (int c = lane; c < dc; c += 32) {
+          const int col = c0 + c;
+          xs[rr * kScreenDChunk + c] = (rr < nr && col < dim) ? src[col] : 0.0f;
+        }
+      }
+      __syncthreads();
+      if (active) {
+        for (int cc = 0; cc < dc; cc += 32) {
+          float qv[32];
+#pragma unroll
+          for (int j = 0; j < 32; j += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(qrow + c0 + cc + j);
+            qv[j] = v.x;
+            qv[j + 1] = v.y;
+            qv[j + 2] = v.z;
+            qv[j + 3] = v.w;
+          }
+#pragma unroll
+          for (int r = 0; r < kScreenRows; ++r) {
+            const float4* xr = reinterpret_cast<const float4*>(xs + r * kScreenDChunk + cc);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float4 v = xr[j];
+              acc[r] = fmaf(qv[4 * j], v.x, acc[r]);
+              acc[r] = fmaf(qv[4 * j + 1], v.y, acc[r]);
+              acc[r] = fmaf(qv[4 * j + 2], v.z, acc[r]);
+              acc[r] = fmaf(qv[4 * j + 3], v.w, acc[r]);
+            }
+          }
+        }
+      }
+    }
+    if (!active) continue;
+#pragma unroll
+    for (int r = 0; r < kScreenRows; ++r) {
+      if (r < nr) {
+        const int64_t row = rb + r;
+        float dist = kL2 ? fmaf(-2.0f, acc[r], qn + xnorm2[row]) : 1.0f - acc[r];
+        dist = dev::nan_to_inf(dist);
+        if (dist <= thr && dev::bitmap_test(bitmap, static_cast<uint64_t>(row))) {
+          heap.push(dist, static_cast<uint32_t>(row));
+          if (heap.n == kk) thr = fminf(thr, heap.top_d());
+        }
+      }
+    }
+  }
+  if (!active) return;
+  const size_t base = (static_cast<size_t>(q) * n_chunks + chunk) * kk;
+  for (int i = 0; i < heap.n; ++i) {
+    cand_d[base + i] = hd[i * qpb + t];
+    cand_r[base + i] = hr[i * qpb + t];
+  }
+  cand_n[static_cast<size_t>(q) * n_chunks + chunk] = heap.n;
+  if (heap.n == kk) atomicMin(thr_bits + q, dev::ordered_bits(heap.top_d()));
+}
+
+// ---- finalize: merge, exact rerank, certificate ------------------------------------------------------
+
+struct EpsModel {
+  float c_l2;   // multiplies (||q|| + max||x||)^2
+  float c_ip;   // multiplies ||q|| * max||x||
+  float c_abs;  // constant term (1 - dot rounding)
+};
+
+__device__ __forceinline__ float screen_eps(const EpsModel& e, bool l2, float qnorm, float xmax) {
+  if (l2) {
+    const float s = qnorm + xmax;
+    return e.c_l2 * s * s;
+  }
+  return e.c_ip * qnorm * xmax + e.c_abs * (1.0f + qnorm * xmax);
+}
+
+__global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
+    const float* __restrict__ qp, int dpad, const float* __restrict__ qnorm, int nq,
+    const float* __restrict__ x, int dim, const uint64_t* __restrict__ labels, uint64_t row_offset,
+    bool l2, EpsModel eps_model, float xmax, const float* __restrict__ cand_d,
+    const uint32_t* __restrict__ cand_r, const int* __restrict__ cand_n, int n_chunks, int kk,
+    int pool, int k, uint64_t* __restrict__ out_labels, float* __restrict__ out_d,
+    uint64_t* __restrict__ out_keys, int* __restrict__ fail_count, int* __restrict__ fail_q,
+    float* __restrict__ fail_dk) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* sd = reinterpret_cast<float*>(smem_raw);               // pool
+  uint64_t* sk = reinterpret_cast<uint64_t*>(sd + pool);        // pool (8-byte aligned: pool%2==0)
+  __shared__ int s_total;
+  const int q = blockIdx.x;
+  if (q >= nq) return;
+  if (threadIdx.x == 0) {
+    int tot = 0;
+    for (int c = 0; c < n_chunks; ++c) tot += cand_n[static_cast<size_t>(q) * n_chunks + c];
+    s_total = tot;
+  }
+  for (int i = threadIdx.x; i < pool; i += blockDim.x) {
+    sd[i] = kInf;
+    sk[i] = ~0ull;
+  }
+  __syncthreads();
+  // Gather: chunk c's candidates land at [c*kk, c*kk + n_c).
+  for (int i = threadIdx.x; i < n_chunks * kk; i += blockDim.x) {
+    const int c = i / kk, j = i - c * kk;
+    const size_t slot = static_cast<size_t>(q) * n_chunks + c;
+    if (j < cand_n[slot]) {
+      sd[i] = cand_d[slot * kk + j];
+      sk[i] = cand_r[slot * kk + j];
+    }
+  }
+  dev::block_bitonic_sort<false>(sd, sk, nullptr, pool);
+  const int total = s_total;
+  const int m = min(total, kk);
+  const float T = total >= kk ? sd[kk - 1] : kInf;
+  __syncthreads();
+  // Exact rerank of the m best (reference AVX2 order), one warp per candidate.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const float* qrow = qp + static_cast<size_t>(q) * dpad;
+  for (int i = warp; i < m; i += nwarps) {
+    const uint64_t row = sk[i];
+    const float e = dev::nan_to_inf(dev::warp_exact_distance(qrow, x + row * dim, dim, l2, lane));
+    if (lane == 0) sd[i] = e;
+  }
+  __syncthreads();
+  // Re-sort the first m' = next_pow2(m) entries (the tail beyond m holds screen values; mask them).
+  int mp = 1;
+  while (mp < m) mp <<= 1;
+  for (int i = m + threadIdx.x; i < mp; i += blockDim.x) {
+    sd[i] = kInf;
+    sk[i] = ~0ull;
+  }
+  dev::block_bitonic_sort<false>(sd, sk, nullptr, mp);
+  if (threadIdx.x == 0) {
+    const float dk = m >= k ? sd[k - 1] : kInf;
+    bool ok = true;
+    if (total >= kk && m >= k) {
+      const float eps = screen_eps(eps_model, l2, qnorm[q], xmax);
+      ok = (T - eps) >= dk;
+    }
+    if (!ok) {
+      const int slot = atomicAdd(fail_count, 1);
+      fail_q[slot] = q;
+      fail_dk[slot] = dk;
+    }
+  }
+  for (int j = threadIdx.x; j < k; j += blockDim.x) {
+    const size_t o = static_cast<size_t>(q) * k + j;
+    if (j < m) {
+      out_d[o] = sd[j];
+      out_labels[o] = labels[sk[j]];
+      if (out_keys) out_keys[o] = row_offset + sk[j];
+    } else {
+      out_d[o] = kInf;
+      out_labels[o] = kInvalidLabel;
+      if (out_keys) out_keys[o] = ~0ull;
+    }
+  }
+}
+
+// ---- exact rescan of uncertified queries -------------------------------------------------------------
+// Block-wide threshold buffer: rows whose exact distance is <= the running threshold are appended;
+// when the buffer might overflow it is sorted and cut to k, which tightens the threshold.
+__global__ void __launch_bounds__(256) flat_rescan_kernel(
+    const float* __restrict__ qp, int dpad, const float* __restrict__ x, int dim, int64_t nrows,
+    const uint64_t* __restrict__ labels, const uint64_t* __restrict__ bitmap, uint64_t row_offset,
+    bool l2, int k, int cap, const int* __restrict__ fail_count, const int* __restrict__ fail_q,
+    const float* __restrict__ fail_dk, uint64_t* __restrict__ out_labels,
+    float* __restrict__ out_d, uint64_t* __restrict__ out_keys) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* bd = reinterpret_cast<float*>(smem_raw);
+  uint64_t* bk = reinterpret_cast<uint64_t*>(bd + cap);
+  __shared__ int s_cnt;
+  __shared__ float s_thr;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int nfail = *fail_count;
+  for (int f = blockIdx.x; f < nfail; f += gridDim.x) {
+    const int q = fail_q[f];
+    const float* qrow = qp + static_cast<size_t>(q) * dpad;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      s_cnt = 0;
+      s_thr = fail_dk[f];
+    }
+    __syncthreads();
+    const int64_t per_round = static_cast<int64_t>(nwarps) * 32;
+    for (int64_t rb = 0; rb < nrows; rb += per_round) {
+      const float thr = s_thr;
+      const int64_t w0 = rb + static_cast<int64_t>(warp) * 32;
+      for (int i = 0; i < 32; ++i) {
+        const int64_t row = w0 + i;
+        if (row >= nrows) break;
+        if (!dev::bitmap_test(bitmap, static_cast<uint64_t>(row))) continue;
+        const float e =
+            dev::nan_to_inf(dev::warp_exact_distance(qrow, x + row * dim, dim, l2, lane));
+        if (lane == 0 && e <= thr) {
+          const int slot = atomicAdd(&s_cnt, 1);
+          bd[slot] = e;
+          bk[slot] = static_cast<uint64_t>(row);
+        }
+      }
+      __syncthreads();
+      if (s_cnt > cap - per_round) {  // compact to the k best
+        for (int i = s_cnt + threadIdx.x; i < cap; i += blockDim.x) {
+          bd[i] = kInf;
+          bk[i] = ~0ull;
+        }
+        dev::block_bitonic_sort<false>(bd, bk, nullptr, cap);
+        if (threadIdx.x == 0) {
+          s_cnt = min(s_cnt, k);
+          if (s_cnt == k) s_thr = fminf(s_thr, bd[k - 1]);
+        }
+      }
+      __syncthreads();
+    }
+    for (int i = s_cnt + threadIdx.x; i < cap; i += blockDim.x) {
+      bd[i] = kInf;
+      bk[i] = ~0ull;
+    }
+    dev::block_bitonic_sort<false>(bd, bk, nullptr, cap);
+    const int m = min(s_cnt, k);
+    for (int j = threadIdx.x; j < k; j += blockDim.x) {
+      const size_t o = static_cast<size_t>(q) * k + j;
+      if (j < m) {
+        out_d[o] = bd[j];
+        out_labels[o] = labels[bk[j]];
+        if (out_keys) out_keys[o] = row_offset + bk[j];
+      } else {
+        out_d[o] = kInf;
+        out_labels[o] = kInvalidLabel;
+        if (out_keys) out_keys[o] = ~0ull;
+      }
+    }
+  }
+}
+
+__global__ void fill_u32_kernel(unsigned* p, size_t n, unsigned v) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    p[i] = v;
+}
+
+int env_int(const char* name, int dflt) {
+  const char* v = std::getenv(name);
+  return (v != nullptr && *v != '\0') ? std::atoi(v) : dflt;
+}
+
+}  // namespace
+
+// ---- host launchers ----------------------------------------------------------------------------------
+
+void normalize_rows_device(float* d_x, size_t n, size_t dim, cudaStream_t st) {
+  if (n == 0) return;
+  const int rows_per_block = 8;
+  normalize_rows_kernel<<<ceil_div(n, rows_per_block), 32 * rows_per_block, 0, st>>>(
+      d_x, n, static_cast<int>(dim));
+  check_launch("normalize_rows_kernel");
+}
+
+void flat_reserve(FlatState& s, size_t rows, cudaStream_t st) {
+  if (rows <= s.cap) return;
+  size_t cap = std::max<size_t>(rows, s.cap + s.cap / 2);
+  DeviceBuffer x(cap * s.dim * sizeof(float)), n2(cap * sizeof(float)),
+      lab(cap * sizeof(uint64_t));
+  if (s.n > 0) {
+    QV_CUDA(cudaMemcpyAsync(x.get(), s.x.get(), s.n * s.dim * sizeof(float),
+                            cudaMemcpyDeviceToDevice, st));
+    QV_CUDA(cudaMemcpyAsync(n2.get(), s.xnorm2.get(), s.n * sizeof(float),
+                            cudaMemcpyDeviceToDevice, st));
+    QV_CUDA(cudaMemcpyAsync(lab.get(), s.labels.get(), s.n * sizeof(uint64_t),
+                            cudaMemcpyDeviceToDevice, st));
+  }
+  QV_CUDA(cudaStreamSynchronize(st));
+  s.x = std::move(x);
+  s.xnorm2 = std::move(n2);
+  s.labels = std::move(lab);
+  s.cap = cap;
+}
+
+void flat_append(FlatState& s, const float* d_rows, const uint64_t* d_labels, size_t n,
+                 cudaStream_t st) {
+  if (n == 0) return;
+  flat_reserve(s, s.n + n, st);
+  float* dst = s.x.get<float>() + s.n * s.dim;
+  if (d_rows != dst)
+    QV_CUDA(cudaMemcpyAsync(dst, d_rows, n * s.dim * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  QV_CUDA(cudaMemcpyAsync(s.labels.get<uint64_t>() + s.n, d_labels, n * sizeof(uint64_t),
+                          cudaMemcpyDeviceToDevice, st));
+  if (s.metric == QV_METRIC_COSINE) normalize_rows_device(dst, n, s.dim, st);
+  DeviceBuffer maxbits(sizeof(unsigned), st);
+  QV_CUDA(cudaMemsetAsync(maxbits.get(), 0, sizeof(unsigned), st));
+  row_stats_kernel<<<ceil_div(n, 8), 256, 0, st>>>(dst, n, static_cast<int>(s.dim),
+                                                   s.xnorm2.get<float>() + s.n,
+                                                   maxbits.get<unsigned>());
+  check_launch("row_stats_kernel");
+  unsigned bits = 0;
+  QV_CUDA(cudaMemcpyAsync(&bits, maxbits.get(), sizeof(bits), cudaMemcpyDeviceToHost, st));
+  QV_CUDA(cudaStreamSynchronize(st));
+  float mx;
+  memcpy(&mx, &bits, sizeof(mx));
+  s.max_norm = std::max(s.max_norm, mx);
+  s.n += n;
+  s.xbf16.release();  // rebuilt lazily by the tensor screen
+}
+
+void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k,
+                 const uint64_t* d_bitmap, uint64_t* d_labels, float* d_dists, uint64_t* d_keys,
+                 cudaStream_t st) {
+  if (nq == 0 || k == 0) return;
+  QV_REQUIRE(k <= 1024, "k > 1024 is not supported by the GPU FlatIndex");
+  const int dim = static_cast<int>(s.dim);
+  const int dpad = static_cast<int>(ceil_div(s.dim, 32) * 32);
+  const bool l2 = s.metric == QV_METRIC_L2;
+  const int nsm = sm_count(s.device);
+
+  DeviceBuffer qp(nq * dpad * sizeof(float), st), qn2(nq * sizeof(float), st),
+      qn(nq * sizeof(float), st);
+  prep_queries_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(d_queries, nq, dim, dpad,
+                                                       s.metric == QV_METRIC_COSINE,
+                                                       qp.get<float>(), qn2.get<float>(),
+                                                       qn.get<float>());
+  check_launch("prep_queries_kernel");
+
+  if (s.n == 0) {  // nothing stored: every slot unfilled
+    std::vector<float> inf(nq * k, INFINITY);
+    std::vector<uint64_t> inv(nq * k, kInvalidLabel);
+    QV_CUDA(cudaMemcpyAsync(d_dists, inf.data(), nq * k * sizeof(float), cudaMemcpyHostToDevice, st));
+    QV_CUDA(cudaMemcpyAsync(d_labels, inv.data(), nq * k * sizeof(uint64_t), cudaMemcpyHostToDevice, st));
+    if (d_keys)
+      QV_CUDA(cudaMemcpyAsync(d_keys, inv.data(), nq * k * sizeof(uint64_t), cudaMemcpyHostToDevice, st));
+    QV_CUDA(cudaStreamSynchronize(st));
+    return;
+  }
+
+  // Candidate budget: KK >= k plus a margin, power of two.
+  // QV_FLAT_KK overrides the budget (any value >= k); small budgets exercise the exact rescan.
+  int kk = static_cast<int>(next_pow2(k + std::max<size_t>(8, k / 4)));
+  const int forced_kk = env_int("QV_FLAT_KK", 0);
+  if (forced_kk > 0) kk = std::max<int>(static_cast<int>(k), forced_kk);
+  const int heap_budget = 64 * 1024;
+  int qpb = std::min<int>(128, heap_budget / (kk * 8));
+  if (qpb >= 32) qpb = qpb / 32 * 32;
+  qpb = std::max(1, qpb);
+  const int n_qtiles = static_cast<int>(ceil_div(nq, qpb));
+  int max_chunks = std::max(1, kMaxCandidatesPerQuery / kk);
+  const int target_units = 8 * nsm;
+  int n_chunks = static_cast<int>(std::min<size_t>(
+      std::min<size_t>(max_chunks, ceil_div(target_units, n_qtiles)), ceil_div(s.n, kScreenRows)));
+  n_chunks = std::max(1, n_chunks);
+  int64_t chunk_rows = static_cast<int64_t>(ceil_div(ceil_div(s.n, n_chunks), kScreenRows)) * kScreenRows;
+  n_chunks = static_cast<int>(ceil_div(s.n, static_cast<size_t>(chunk_rows)));
+
+  const size_t slots = nq * static_cast<size_t>(n_chunks);
+  DeviceBuffer cand_d(slots * kk * sizeof(float), st), cand_r(slots * kk * sizeof(uint32_t), st),
+      cand_n(slots * sizeof(int), st), thr(nq * sizeof(unsigned), st);
+  QV_CUDA(cudaMemsetAsync(cand_n.get(), 0, slots * sizeof(int), st));
+  fill_u32_kernel<<<std::min<size_t>(ceil_div(nq, 256), 1024), 256, 0, st>>>(
+      thr.get<unsigned>(), nq, 0xff800000u /* ordered bits of +inf */);
+  check_launch("fill_u32_kernel");
+
+  const size_t smem = kScreenRows * kScreenDChunk * sizeof(float) +
+                      static_cast<size_t>(kk) * qpb * (sizeof(float) + sizeof(uint32_t));
+  const dim3 grid(static_cast<unsigned>(n_qtiles * n_chunks));
+  KernelTimer timer(st, "flat_screen_simt_kernel", 2.0 * nq * static_cast<double>(s.n) * dim,
+                    false);
+  if (l2) {
+    QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    flat_screen_simt_kernel<true><<<grid, 128, smem, st>>>(
+        qp.get<float>(), dpad, qn2.get<float>(), static_cast<int>(nq), qpb, s.x.get<float>(), dim,
+        s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, chunk_rows, n_qtiles,
+        n_chunks, kk, cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(),
+        thr.get<unsigned>());
+  } else {
+    QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    flat_screen_simt_kernel<false><<<grid, 128, smem, st>>>(
+        qp.get<float>(), dpad, qn2.get<float>(), static_cast<int>(nq), qpb, s.x.get<float>(), dim,
+        s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, chunk_rows, n_qtiles,
+        n_chunks, kk, cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(),
+        thr.get<unsigned>());
+  }
+  timer.stop();
+  check_launch("flat_screen_simt_kernel");
+
+  // Error model of the float32 screen against the reference's float32 result: both sums carry
+  // at most gamma_d = d*u/(1-d*u) relative error of sum|q_i x_i| (u = 2^-24), plus the rounding
+  // of the final 1 - dot or norm combination; doubled for margin.
+  const double u = std::ldexp(1.0, -24);
+  const double gamma = (dim + 2) * u / (1.0 - (dim + 2) * u);
+  EpsModel em;
+  em.c_l2 = static_cast<float>(2.0 * (2.0 * gamma + 4.0 * u));
+  em.c_ip = static_cast<float>(2.0 * (2.0 * gamma));
+  em.c_abs = static_cast<float>(2.0 * (2.0 * u));
+
+  const int pool = static_cast<int>(next_pow2(static_cast<size_t>(n_chunks) * kk));
+  DeviceBuffer fail(sizeof(int) + nq * (sizeof(int) + sizeof(float)), st);
+  int* fail_count = fail.get<int>();
+  int* fail_q = fail_count + 1;
+  float* fail_dk = reinterpret_cast<float*>(fail_q + nq);
+  QV_CUDA(cudaMemsetAsync(fail_count, 0, sizeof(int), st));
+  const size_t fsmem = pool * (sizeof(float) + sizeof(uint64_t));
+  QV_CUDA(cudaFuncSetAttribute(flat_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)fsmem));
+  flat_finalize_kernel<<<static_cast<unsigned>(nq), kFinalizeThreads, fsmem, st>>>(
+      qp.get<float>(), dpad, qn.get<float>(), static_cast<int>(nq), s.x.get<float>(), dim,
+      s.labels.get<uint64_t>(), s.row_offset, l2, em, s.max_norm, cand_d.get<float>(),
+      cand_r.get<uint32_t>(), cand_n.get<int>(), n_chunks, kk, pool, static_cast<int>(k),
+      d_labels, d_dists, d_keys, fail_count, fail_q, fail_dk);
+  check_launch("flat_finalize_kernel");
+
+  const int cap = static_cast<int>(next_pow2(k + 256));
+  const size_t rsmem = cap * (sizeof(float) + sizeof(uint64_t));
+  QV_CUDA(cudaFuncSetAttribute(flat_rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)rsmem));
+  flat_rescan_kernel<<<static_cast<unsigned>(std::min<size_t>(nq, 2 * nsm)), 256, rsmem, st>>>(
+      qp.get<float>(), dpad, s.x.get<float>(), dim, static_cast<int64_t>(s.n),
+      s.labels.get<uint64_t>(), d_bitmap, s.row_offset, l2, static_cast<int>(k), cap, fail_count,
+      fail_q, fail_dk, d_labels, d_dists, d_keys);
+  check_launch("flat_rescan_kernel");
+  int nfail = 0;
+  QV_CUDA(cudaMemcpyAsync(&nfail, fail_count, sizeof(int), cudaMemcpyDeviceToHost, st));
+  QV_CUDA(cudaStreamSynchronize(st));
+  timer.finish();
+  thread_stats().rescanned_queries += static_cast<uint64_t>(nfail);
+}
+
+}  // namespace qv

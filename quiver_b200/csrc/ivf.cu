@@ -1,0 +1,710 @@
+// IVF-PQ on the GPU: trained-state preparation, the assign + PQ encode of add(), and search
+// (coarse probe, lookup tables, ADC scan of the probed inverted lists with a bitmap filter, and
+// the optional exact re-rank). Reference: src/ivfpq_index.cc, src/product_quantizer.cc,
+// src/internal/centroid_table.h.
+//
+// Bit-exactness: every value the reference computes in float32 (centroid norms, coarse distances,
+// assignments, residuals, codes, lookup tables, ADC sums, precomputed terms, exact re-rank
+// distances) is computed here with the same operations in the same order and the same rounding
+// (__fmul_rn/__fadd_rn/__fsub_rn for separately rounded steps). Ties between equal distances are
+// broken by the candidate key (list << 32 | offset in the full list) and probes by list id; the
+// reference leaves both unspecified.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "qv_state.h"
+
+namespace qv {
+namespace {
+
+constexpr float kInf = __builtin_huge_valf();
+constexpr size_t kMaxPrecomputedBytes = size_t{256} << 20;  // src/ivfpq_index.cc:74
+constexpr int kScanThreads = 256;
+constexpr int kTileP = 32;  // points (or queries) per coarse tile
+constexpr int kTileC = 64;  // centroids per coarse tile
+constexpr int kTileD = 64;  // dims per coarse tile
+
+// ---- trained state -------------------------------------------------------------------------------
+
+// CentroidTable::reset norms (src/internal/centroid_table.h:43-59): sequential, separately rounded.
+__global__ void centroid_norms_kernel(const float* c, size_t k, int dim, float* out) {
+  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  if (i >= k) return;
+  const float* v = c + i * dim;
+  float s = 0.0f;
+  for (int j = 0; j < dim; ++j) s = __fadd_rn(s, __fmul_rn(v[j], v[j]));
+  out[i] = s;
+}
+
+// Impl::precompute (src/ivfpq_index.cc:112-129): v += r*r + 2*c*r over t, each step rounded.
+__global__ void precompute_kernel(const float* cents, size_t nlist, const float* cb, int m,
+                                  int dsub, float* pre) {
+  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  const size_t total = nlist * m * kSubCentroids;
+  if (i >= total) return;
+  const int c = static_cast<int>(i % kSubCentroids);
+  const int j = static_cast<int>((i / kSubCentroids) % m);
+  const size_t l = i / (static_cast<size_t>(kSubCentroids) * m);
+  const float* cl = cents + l * (static_cast<size_t>(m) * dsub) + static_cast<size_t>(j) * dsub;
+  const float* r = cb + (static_cast<size_t>(j) * kSubCentroids + c) * dsub;
+  float v = 0.0f;
+  for (int t = 0; t < dsub; ++t) {
+    const float rr = __fmul_rn(r[t], r[t]);
+    const float cr = __fmul_rn(__fmul_rn(2.0f, cl[t]), r[t]);
+    v = __fadd_rn(v, __fadd_rn(rr, cr));
+  }
+  pre[i] = v;
+}
+
+// ---- coarse: shared tile machinery -----------------------------------------------------------------
+// A block covers kTileP points x all centroids; 256 threads = 32 points x 8 centroid lanes. Each
+// thread accumulates 8 centroids (c = cbase + lane8 + 8*i) over dims in ascending order, so each
+// (point, centroid) sum is sequential in j exactly like CentroidTable.
+enum CoarseMode { kDot = 0, kL2Diff = 1 };
+
+template <int kMode>
+__device__ __forceinline__ void coarse_tile(const float* __restrict__ xs_t /*kTileD x kTileP*/,
+                                            const float* __restrict__ cs /*kTileC x kTileD*/,
+                                            int nd, int p, int cl, float acc[8]) {
+  for (int j = 0; j < nd; ++j) {
+    const float xv = xs_t[j * kTileP + p];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float cv = cs[(cl + 8 * i) * (kTileD + 1) + j];
+      if (kMode == kDot) {
+        acc[i] = __fadd_rn(acc[i], __fmul_rn(xv, cv));
+      } else {
+        const float d = __fsub_rn(xv, cv);
+        acc[i] = __fadd_rn(acc[i], __fmul_rn(d, d));
+      }
+    }
+  }
+}
+
+// Loads points [p0, p0+kTileP) x dims [d0, d0+nd) transposed, and centroids [c0, c0+kTileC).
+__device__ __forceinline__ void load_coarse_tiles(const float* __restrict__ x, size_t n,
+                                                  const float* __restrict__ cents, size_t nlist,
+                                                  int dim, size_t p0, size_t c0, int d0, int nd,
+                                                  float* xs_t, float* cs) {
+  for (int idx = threadIdx.x; idx < kTileP * kTileD; idx += blockDim.x) {
+    const int p = idx / kTileD, j = idx - p * kTileD;
+    const size_t gp = p0 + p;
+    xs_t[j * kTileP + p] = (gp < n && j < nd) ? x[gp * dim + d0 + j] : 0.0f;
+  }
+  for (int idx = threadIdx.x; idx < kTileC * kTileD; idx += blockDim.x) {
+    const int c = idx / kTileD, j = idx - c * kTileD;
+    const size_t gc = c0 + c;
+    cs[c * (kTileD + 1) + j] = (gc < nlist && j < nd) ? cents[gc * dim + d0 + j] : 0.0f;
+  }
+}
+
+// CentroidTable::nearest_batch (src/internal/centroid_table.h:94-144): d = ||c||^2 - 2<x,c> (or
+// -<x,c> for max inner product), first strict minimum over ascending c.
+__global__ void __launch_bounds__(256) coarse_assign_kernel(const float* __restrict__ x, size_t n,
+                                                            const float* __restrict__ cents,
+                                                            const float* __restrict__ cnorm2,
+                                                            size_t nlist, int dim, bool by_ip,
+                                                            uint32_t* __restrict__ out) {
+  __shared__ float xs_t[kTileD * kTileP];
+  __shared__ float cs[kTileC * (kTileD + 1)];
+  __shared__ float bd[8][kTileP];
+  __shared__ uint32_t bc[8][kTileP];
+  const int p = threadIdx.x & 31, cl = threadIdx.x >> 5;
+  const size_t p0 = static_cast<size_t>(blockIdx.x) * kTileP;
+  // (best distance, centroid) starts at (+inf, 0) like the reference's zero-initialized output.
+  float best_d = kInf;
+  uint32_t best_c = 0;
+  for (size_t c0 = 0; c0 < nlist; c0 += kTileC) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    for (int d0 = 0; d0 < dim; d0 += kTileD) {
+      const int nd = min(kTileD, dim - d0);
+      __syncthreads();
+      load_coarse_tiles(x, n, cents, nlist, dim, p0, c0, d0, nd, xs_t, cs);
+      __syncthreads();
+      coarse_tile<kDot>(xs_t, cs, nd, p, cl, acc);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const size_t c = c0 + cl + 8 * i;
+      if (c < nlist) {
+        const float d = by_ip ? -acc[i] : __fsub_rn(cnorm2[c], __fmul_rn(2.0f, acc[i]));
+        if (d < best_d) {  // ascending c within this thread: strict < keeps the first minimum
+          best_d = d;
+          best_c = static_cast<uint32_t>(c);
+        }
+      }
+    }
+  }
+  bd[cl][p] = best_d;
+  bc[cl][p] = best_c;
+  __syncthreads();
+  if (cl == 0) {
+    float d = bd[0][p];
+    uint32_t c = bc[0][p];
+    for (int i = 1; i < 8; ++i) {
+      const float di = bd[i][p];
+      const uint32_t ci = bc[i][p];
+      if (di < d || (di == d && ci < c)) {
+        d = di;
+        c = ci;
+      }
+    }
+    const size_t gp = p0 + p;
+    if (gp < n) out[gp] = c;
+  }
+}
+
+// Search-time coarse distances (src/ivfpq_index.cc:285-297 with CentroidTable::l2 / ::dot):
+// L2: sum_j (q_j - c_j)^2; IP/cosine: -(sum_j q_j c_j), j ascending, separately rounded.
+__global__ void __launch_bounds__(256) coarse_dist_kernel(const float* __restrict__ q, size_t nq,
+                                                          const float* __restrict__ cents,
+                                                          size_t nlist, int dim, bool ip,
+                                                          float* __restrict__ out) {
+  __shared__ float xs_t[kTileD * kTileP];
+  __shared__ float cs[kTileC * (kTileD + 1)];
+  const int p = threadIdx.x & 31, cl = threadIdx.x >> 5;
+  const size_t p0 = static_cast<size_t>(blockIdx.x) * kTileP;
+  const size_t c0 = static_cast<size_t>(blockIdx.y) * kTileC;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+  for (int d0 = 0; d0 < dim; d0 += kTileD) {
+    const int nd = min(kTileD, dim - d0);
+    __syncthreads();
+    load_coarse_tiles(q, nq, cents, nlist, dim, p0, c0, d0, nd, xs_t, cs);
+    __syncthreads();
+    if (ip) {
+      coarse_tile<kDot>(xs_t, cs, nd, p, cl, acc);
+    } else {
+      coarse_tile<kL2Diff>(xs_t, cs, nd, p, cl, acc);
+    }
+  }
+  const size_t gp = p0 + p;
+  if (gp >= nq) return;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const size_t c = c0 + cl + 8 * i;
+    if (c < nlist) out[gp * nlist + c] = ip ? -acc[i] : acc[i];
+  }
+}
+
+// partial_sort of the nlist probe candidates (src/ivfpq_index.cc:298-300), ties by list id.
+__global__ void select_probes_kernel(const float* __restrict__ coarse, size_t nlist, int pool,
+                                     int nprobe, uint32_t* __restrict__ probes,
+                                     float* __restrict__ probe_d) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* sd = reinterpret_cast<float*>(smem_raw);
+  uint64_t* sk = reinterpret_cast<uint64_t*>(sd + pool);
+  const size_t q = blockIdx.x;
+  for (int i = threadIdx.x; i < pool; i += blockDim.x) {
+    if (static_cast<size_t>(i) < nlist) {
+      sd[i] = coarse[q * nlist + i];
+      sk[i] = static_cast<uint64_t>(i);
+    } else {
+      sd[i] = kInf;
+      sk[i] = ~0ull;
+    }
+  }
+  dev::block_bitonic_sort<false>(sd, sk, nullptr, pool);
+  for (int i = threadIdx.x; i < nprobe; i += blockDim.x) {
+    probes[q * nprobe + i] = static_cast<uint32_t>(sk[i]);
+    probe_d[q * nprobe + i] = sd[i];
+  }
+}
+
+// ---- encode ------------------------------------------------------------------------------------------
+
+// residual = v - c_l (src/ivfpq_index.cc:243)
+__global__ void residual_kernel(const float* __restrict__ x, size_t n, int dim,
+                                const float* __restrict__ cents, const uint32_t* __restrict__ assign,
+                                float* __restrict__ out) {
+  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  if (i >= n * dim) return;
+  const size_t row = i / dim;
+  const int j = static_cast<int>(i - row * dim);
+  out[i] = __fsub_rn(x[i], cents[static_cast<size_t>(assign[row]) * dim + j]);
+}
+
+// ProductQuantizer::encode (src/product_quantizer.cc:165-171): per sub-space the first index of
+// the minimum of sum_t (r_t - cb_t)^2 (CentroidTable::l2 + argmin_n). grid.y = sub-space.
+__global__ void pq_encode_kernel(const float* __restrict__ resid, size_t n, int dim, int m,
+                                 int dsub, const float* __restrict__ cb,
+                                 uint8_t* __restrict__ codes) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* sc = reinterpret_cast<float*>(smem_raw);  // 256 x dsub
+  const int j = blockIdx.y;
+  for (int i = threadIdx.x; i < kSubCentroids * dsub; i += blockDim.x)
+    sc[i] = cb[static_cast<size_t>(j) * kSubCentroids * dsub + i];
+  __syncthreads();
+  const size_t row = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  if (row >= n) return;
+  const float* r = resid + row * dim + static_cast<size_t>(j) * dsub;
+  // argmin_n: the minimum m (NaN never wins), then the first index holding m. A strict-< scan
+  // finds that index whenever m is finite; only when m = +inf is a second pass needed.
+  float best = kInf;
+  int code = 0;
+  for (int c = 0; c < kSubCentroids; ++c) {
+    float s = 0.0f;
+    for (int t = 0; t < dsub; ++t) {
+      const float d = __fsub_rn(r[t], sc[c * dsub + t]);
+      s = __fadd_rn(s, __fmul_rn(d, d));
+    }
+    if (s < best) {
+      best = s;
+      code = c;
+    }
+  }
+  if (best == kInf) {
+    for (int c = 0; c < kSubCentroids; ++c) {
+      float s = 0.0f;
+      for (int t = 0; t < dsub; ++t) {
+        const float d = __fsub_rn(r[t], sc[c * dsub + t]);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+      }
+      if (s == kInf) {
+        code = c;
+        break;
+      }
+    }
+  }
+  codes[row * m + j] = static_cast<uint8_t>(code);
+}
+
+// ---- scan ------------------------------------------------------------------------------------------
+
+struct ScanArgs {
+  const float* q;           // nq x dim (normalized for cosine)
+  int dim, m, dsub;
+  bool ip, use_pre;
+  const float* cents;
+  const float* cb;
+  const float* pre;
+  const uint64_t* offsets;
+  const uint32_t* global_base;
+  const uint8_t* codes;
+  const uint64_t* labels;
+  const float* vectors;
+  const uint64_t* bitmap;   // positions
+  const uint32_t* probes;   // nq x nprobe
+  const float* probe_d;
+  int nprobe;
+  int keep, k, cap;
+  bool refine;
+  // outputs (final mode): labels/dists nq x k. candidate mode: dists/keys/labels nq x keep
+  bool candidate_mode;
+  uint64_t* out_labels;
+  float* out_d;
+  uint64_t* out_keys;
+};
+
+// Compacts the block buffer to its best `keep` (distance, key) entries; updates the threshold.
+__device__ void scan_compact(float* bd, uint64_t* bk, uint64_t* bp, int cap, int keep, int* cnt,
+                             float* thr) {
+  for (int i = *cnt + threadIdx.x; i < cap; i += blockDim.x) {
+    bd[i] = kInf;
+    bk[i] = ~0ull;
+    bp[i] = ~0ull;
+  }
+  dev::block_bitonic_sort<true>(bd, bk, bp, cap);
+  if (threadIdx.x == 0) {
+    if (*cnt >= keep) {
+      *cnt = keep;
+      *thr = fminf(*thr, bd[keep - 1]);
+    }
+  }
+  __syncthreads();
+}
+
+// One block per query: lookup tables in shared memory, then every probed list in probe order.
+// Codes of a list are staged through shared memory with coalesced 16-byte loads; each thread sums
+// one code's m table entries in ascending j from 0.0f (ProductQuantizer::adc, src/
+// product_quantizer.cc:188-217) and forms dist = ip ? 1-(base+s) : base+s
+// (src/ivfpq_index.cc:346). Survivors of the running threshold and the position bitmap go to a
+// block buffer that is compacted to the best `keep`.
+__global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int ts = a.m * kSubCentroids;
+  float* table = reinterpret_cast<float*>(smem_raw);
+  float* qtab = table + ts;                                // L2 precomputed only
+  float* qv = qtab + (a.use_pre ? ts : 0);                 // dim (residual scratch for L2)
+  uint8_t* cstage = reinterpret_cast<uint8_t*>(qv + ((a.dim + 3) & ~3));  // kScanThreads x m
+  float* bd = reinterpret_cast<float*>(cstage + ((kScanThreads * a.m + 15) & ~15));
+  uint64_t* bk = reinterpret_cast<uint64_t*>(bd + a.cap);
+  uint64_t* bp = bk + a.cap;
+  __shared__ int s_cnt;
+  __shared__ float s_thr;
+
+  const size_t q = blockIdx.x;
+  const float* qrow = a.q + q * a.dim;
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    s_cnt = 0;
+    s_thr = kInf;
+  }
+  for (int i = tid; i < a.dim; i += blockDim.x) qv[i] = qrow[i];
+  __syncthreads();
+  // Query-side tables: ip_table (CentroidTable::dot over each sub-space, sequential in t).
+  if (a.ip || a.use_pre) {
+    float* dst = a.ip ? table : qtab;
+    for (int e = tid; e < ts; e += blockDim.x) {
+      const int j = e / kSubCentroids, c = e - j * kSubCentroids;
+      const float* cbv = a.cb + static_cast<size_t>(e) * a.dsub;
+      const float* qs = qv + j * a.dsub;
+      float s = 0.0f;
+      for (int t = 0; t < a.dsub; ++t) s = __fadd_rn(s, __fmul_rn(qs[t], cbv[t]));
+      dst[e] = a.ip ? s : __fmul_rn(s, -2.0f);  // query_table = -2 * ip_table (:316-317)
+      (void)c;
+    }
+  }
+  __syncthreads();
+
+  for (int pi = 0; pi < a.nprobe; ++pi) {
+    const uint32_t l = a.probes[q * a.nprobe + pi];
+    const uint64_t off = a.offsets[l];
+    const int64_t len = static_cast<int64_t>(a.offsets[l + 1] - off);
+    if (len == 0) continue;
+    float base;
+    if (a.ip) {
+      base = -a.probe_d[q * a.nprobe + pi];
+    } else if (a.use_pre) {
+      base = a.probe_d[q * a.nprobe + pi];
+      const float* pre = a.pre + static_cast<size_t>(l) * ts;
+      __syncthreads();
+      for (int e = tid; e < ts; e += blockDim.x) table[e] = __fadd_rn(pre[e], qtab[e]);
+      __syncthreads();
+    } else {
+      // Residual L2 table (src/ivfpq_index.cc:339-341 with compute_l2_table).
+      base = 0.0f;
+      const float* c = a.cents + static_cast<size_t>(l) * a.dim;
+      __syncthreads();
+      for (int e = tid; e < ts; e += blockDim.x) {
+        const int j = e / kSubCentroids;
+        const float* cbv = a.cb + static_cast<size_t>(e) * a.dsub;
+        float s = 0.0f;
+        for (int t = 0; t < a.dsub; ++t) {
+          const int col = j * a.dsub + t;
+          const float r = __fsub_rn(qv[col], c[col]);
+          const float d = __fsub_rn(r, cbv[t]);
+          s = __fadd_rn(s, __fmul_rn(d, d));
+        }
+        table[e] = s;
+      }
+      __syncthreads();
+    }
+    const uint64_t gbase = static_cast<uint64_t>(a.global_base[l]);
+    for (int64_t r0 = 0; r0 < len; r0 += kScanThreads) {
+      const int nr = static_cast<int>(len - r0 < kScanThreads ? len - r0 : kScanThreads);
+      // stage nr codes (nr*m bytes) with 16-byte loads where the source allows it
+      const uint8_t* src = a.codes + (off + r0) * a.m;
+      const int bytes = nr * a.m;
+      __syncthreads();
+      if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        const int v16 = bytes >> 4;
+        for (int i = tid; i < v16; i += blockDim.x)
+          reinterpret_cast<uint4*>(cstage)[i] = reinterpret_cast<const uint4*>(src)[i];
+        for (int i = (v16 << 4) + tid; i < bytes; i += blockDim.x) cstage[i] = src[i];
+      } else {
+        for (int i = tid; i < bytes; i += blockDim.x) cstage[i] = src[i];
+      }
+      __syncthreads();
+      if (tid < nr) {
+        const uint8_t* code = cstage + tid * a.m;
+        float s = 0.0f;
+        for (int j = 0; j < a.m; ++j) s = __fadd_rn(s, table[j * kSubCentroids + code[j]]);
+        float dist = a.ip ? __fsub_rn(1.0f, __fadd_rn(base, s)) : __fadd_rn(base, s);
+        dist = dev::nan_to_inf(dist);
+        const uint64_t pos = off + r0 + tid;
+        if (dist <= s_thr && dev::bitmap_test(a.bitmap, pos)) {
+          const int slot = atomicAdd(&s_cnt, 1);
+          bd[slot] = dist;
+          bk[slot] = (static_cast<uint64_t>(l) << 32) | (gbase + static_cast<uint64_t>(r0 + tid));
+          bp[slot] = pos;
+        }
+      }
+      __syncthreads();
+      if (s_cnt > a.cap - kScanThreads) scan_compact(bd, bk, bp, a.cap, a.keep, &s_cnt, &s_thr);
+    }
+  }
+  __syncthreads();
+  scan_compact(bd, bk, bp, a.cap, a.keep, &s_cnt, &s_thr);
+  const int n = min(s_cnt, a.keep);
+  if (a.candidate_mode) {
+    for (int j = tid; j < a.keep; j += blockDim.x) {
+      const size_t o = q * a.keep + j;
+      a.out_d[o] = j < n ? bd[j] : kInf;
+      a.out_keys[o] = j < n ? bk[j] : ~0ull;
+      a.out_labels[o] = j < n ? a.labels[bp[j]] : kInvalidLabel;
+    }
+    return;
+  }
+  int nres = n;
+  if (a.refine && n > 0) {
+    // Exact re-rank (src/ivfpq_index.cc:362-373), one warp per candidate.
+    const int warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
+    for (int i = warp; i < n; i += nwarps) {
+      const float e = dev::nan_to_inf(
+          dev::warp_exact_distance(qv, a.vectors + bp[i] * a.dim, a.dim, !a.ip, lane));
+      if (lane == 0) bd[i] = e;
+    }
+    __syncthreads();
+    int np2 = 1;
+    while (np2 < n) np2 <<= 1;
+    for (int i = n + tid; i < np2; i += blockDim.x) {
+      bd[i] = kInf;
+      bk[i] = ~0ull;
+      bp[i] = ~0ull;
+    }
+    dev::block_bitonic_sort<true>(bd, bk, bp, np2);
+  }
+  nres = min(nres, a.k);
+  for (int j = tid; j < a.k; j += blockDim.x) {
+    const size_t o = q * a.k + j;
+    a.out_d[o] = j < nres ? bd[j] : kInf;
+    a.out_labels[o] = j < nres ? a.labels[bp[j]] : kInvalidLabel;
+  }
+}
+
+// Exact distance of each candidate this shard stores, +inf for the others.
+__global__ void ivf_refine_kernel(const float* __restrict__ qn, size_t nq, int dim, int keep,
+                                  const uint64_t* __restrict__ keys, const uint64_t* offsets,
+                                  const uint32_t* global_base, size_t nlist, const float* vectors,
+                                  bool l2, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const size_t w = blockIdx.x * static_cast<size_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= nq * keep) return;
+  const size_t q = w / keep;
+  const uint64_t key = keys[w];
+  float e = kInf;
+  if (key != ~0ull) {
+    const uint64_t l = key >> 32;
+    const uint64_t g = key & 0xffffffffull;
+    if (l < nlist) {
+      const uint64_t b = global_base[l];
+      const uint64_t len = offsets[l + 1] - offsets[l];
+      if (g >= b && g - b < len) {
+        const uint64_t pos = offsets[l] + (g - b);
+        e = dev::nan_to_inf(dev::warp_exact_distance(qn + q * dim, vectors + pos * dim, dim, l2, lane));
+      }
+    }
+  }
+  if (lane == 0) out[w] = e;
+}
+
+__global__ void copy_queries_kernel(const float* q, size_t total, float* out) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    out[i] = q[i];
+}
+
+struct Prepared {
+  DeviceBuffer qn, coarse, probes, probe_d;
+  int nprobe = 1;
+};
+
+Prepared prepare_search(const IvfState& s, const float* d_queries, size_t nq, size_t nprobe,
+                        cudaStream_t st) {
+  Prepared p;
+  p.nprobe = static_cast<int>(std::min(std::max<size_t>(nprobe, 1), s.nlist));  // :286
+  p.qn.allocate(nq * s.dim * sizeof(float), st);
+  copy_queries_kernel<<<std::min<size_t>(ceil_div(nq * s.dim, 256), 4096), 256, 0, st>>>(
+      d_queries, nq * s.dim, p.qn.get<float>());
+  check_launch("copy_queries_kernel");
+  if (s.metric == QV_METRIC_COSINE) normalize_rows_device(p.qn.get<float>(), nq, s.dim, st);
+  p.coarse.allocate(nq * s.nlist * sizeof(float), st);
+  dim3 grid(static_cast<unsigned>(ceil_div(nq, kTileP)), static_cast<unsigned>(ceil_div(s.nlist, kTileC)));
+  coarse_dist_kernel<<<grid, 256, 0, st>>>(p.qn.get<float>(), nq, s.centroids.get<float>(),
+                                           s.nlist, static_cast<int>(s.dim), s.ip(),
+                                           p.coarse.get<float>());
+  check_launch("coarse_dist_kernel");
+  const int pool = static_cast<int>(next_pow2(s.nlist));
+  p.probes.allocate(nq * p.nprobe * sizeof(uint32_t), st);
+  p.probe_d.allocate(nq * p.nprobe * sizeof(float), st);
+  const size_t smem = pool * (sizeof(float) + sizeof(uint64_t));
+  QV_CUDA(cudaFuncSetAttribute(select_probes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem));
+  select_probes_kernel<<<static_cast<unsigned>(nq), 512, smem, st>>>(
+      p.coarse.get<float>(), s.nlist, pool, p.nprobe, p.probes.get<uint32_t>(),
+      p.probe_d.get<float>());
+  check_launch("select_probes_kernel");
+  return p;
+}
+
+void run_scan(const IvfState& s, const Prepared& p, size_t nq, size_t keep, size_t k, bool refine,
+              const uint64_t* d_bitmap, bool candidate_mode, uint64_t* out_labels, float* out_d,
+              uint64_t* out_keys, cudaStream_t st) {
+  ScanArgs a{};
+  a.q = p.qn.get<float>();
+  a.dim = static_cast<int>(s.dim);
+  a.m = static_cast<int>(s.m);
+  a.dsub = static_cast<int>(s.dsub);
+  a.ip = s.ip();
+  a.use_pre = !s.ip() && s.use_precomputed();
+  a.cents = s.centroids.get<float>();
+  a.cb = s.codebooks.get<float>();
+  a.pre = s.precomputed.get<float>();
+  a.offsets = s.offsets.get<uint64_t>();
+  a.global_base = s.global_base.get<uint32_t>();
+  a.codes = s.codes.get<uint8_t>();
+  a.labels = s.labels.get<uint64_t>();
+  a.vectors = s.vectors.get<float>();
+  a.bitmap = d_bitmap;
+  a.probes = p.probes.get<uint32_t>();
+  a.probe_d = p.probe_d.get<float>();
+  a.nprobe = p.nprobe;
+  a.keep = static_cast<int>(keep);
+  a.k = static_cast<int>(k);
+  a.cap = static_cast<int>(std::max<size_t>(512, next_pow2(keep + kScanThreads)));
+  a.refine = refine;
+  a.candidate_mode = candidate_mode;
+  a.out_labels = out_labels;
+  a.out_d = out_d;
+  a.out_keys = out_keys;
+  const size_t ts = s.m * kSubCentroids * sizeof(float);
+  const size_t smem = ts * (a.use_pre ? 2 : 1) + ((s.dim + 3) & ~size_t{3}) * sizeof(float) +
+                      ((kScanThreads * s.m + 15) & ~size_t{15}) +
+                      a.cap * (sizeof(float) + 2 * sizeof(uint64_t));
+  if (smem > 227 * 1024) {
+    fail(QV_ERR_UNSUPPORTED,
+         "IVF-PQ search: m=" + std::to_string(s.m) + " with keep=" + std::to_string(keep) +
+             " needs " + std::to_string(smem) + " bytes of shared memory per query (max 232448)");
+  }
+  QV_CUDA(cudaFuncSetAttribute(ivf_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem));
+  ivf_scan_kernel<<<static_cast<unsigned>(nq), kScanThreads, smem, st>>>(a);
+  check_launch("ivf_scan_kernel");
+}
+
+}  // namespace
+
+// ---- host entry points ---------------------------------------------------------------------------------
+
+void ivf_set_trained(IvfState& s, const float* h_centroids, const float* h_codebooks,
+                     cudaStream_t st) {
+  const size_t cn = s.nlist * s.dim, bn = s.m * kSubCentroids * s.dsub;
+  s.host_centroids.assign(h_centroids, h_centroids + cn);
+  s.host_codebooks.assign(h_codebooks, h_codebooks + bn);
+  s.centroids.allocate(cn * sizeof(float));
+  s.codebooks.allocate(bn * sizeof(float));
+  s.cnorm2.allocate(s.nlist * sizeof(float));
+  QV_CUDA(cudaMemcpyAsync(s.centroids.get(), h_centroids, cn * sizeof(float),
+                          cudaMemcpyHostToDevice, st));
+  QV_CUDA(cudaMemcpyAsync(s.codebooks.get(), h_codebooks, bn * sizeof(float),
+                          cudaMemcpyHostToDevice, st));
+  centroid_norms_kernel<<<ceil_div(s.nlist, 256), 256, 0, st>>>(
+      s.centroids.get<float>(), s.nlist, static_cast<int>(s.dim), s.cnorm2.get<float>());
+  check_launch("centroid_norms_kernel");
+  s.precomputed.release();
+  const size_t pre_bytes = s.nlist * s.m * kSubCentroids * sizeof(float);
+  if (!s.ip() && pre_bytes <= kMaxPrecomputedBytes) {  // src/ivfpq_index.cc:114
+    s.precomputed.allocate(pre_bytes);
+    const size_t total = s.nlist * s.m * kSubCentroids;
+    precompute_kernel<<<ceil_div(total, 256), 256, 0, st>>>(
+        s.centroids.get<float>(), s.nlist, s.codebooks.get<float>(), static_cast<int>(s.m),
+        static_cast<int>(s.dsub), s.precomputed.get<float>());
+    check_launch("precompute_kernel");
+  }
+  QV_CUDA(cudaStreamSynchronize(st));
+  s.trained = true;
+}
+
+void ivf_encode_device(const IvfState& s, const float* d_x, size_t n, uint32_t* d_assign,
+                       uint8_t* d_codes, cudaStream_t st) {
+  if (n == 0) return;
+  coarse_assign_kernel<<<ceil_div(n, kTileP), 256, 0, st>>>(
+      d_x, n, s.centroids.get<float>(), s.cnorm2.get<float>(), s.nlist, static_cast<int>(s.dim),
+      s.metric == QV_METRIC_IP, d_assign);  // assign_by_ip (src/ivfpq_index.cc:107)
+  check_launch("coarse_assign_kernel");
+  DeviceBuffer resid(n * s.dim * sizeof(float), st);
+  residual_kernel<<<ceil_div(n * s.dim, 256), 256, 0, st>>>(
+      d_x, n, static_cast<int>(s.dim), s.centroids.get<float>(), d_assign, resid.get<float>());
+  check_launch("residual_kernel");
+  const size_t smem = kSubCentroids * s.dsub * sizeof(float);
+  QV_REQUIRE(smem <= 227 * 1024, "PQ sub-space too wide for the GPU encoder");
+  QV_CUDA(cudaFuncSetAttribute(pq_encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)smem));
+  dim3 grid(static_cast<unsigned>(ceil_div(n, 256)), static_cast<unsigned>(s.m));
+  pq_encode_kernel<<<grid, 256, smem, st>>>(resid.get<float>(), n, static_cast<int>(s.dim),
+                                            static_cast<int>(s.m), static_cast<int>(s.dsub),
+                                            s.codebooks.get<float>(), d_codes);
+  check_launch("pq_encode_kernel");
+}
+
+void ivf_upload_lists(IvfState& s, cudaStream_t st) {
+  s.offsets.allocate((s.nlist + 1) * sizeof(uint64_t));
+  s.global_base.allocate(s.nlist * sizeof(uint32_t));
+  QV_CUDA(cudaMemcpyAsync(s.offsets.get(), s.host_offsets.data(), (s.nlist + 1) * sizeof(uint64_t),
+                          cudaMemcpyHostToDevice, st));
+  QV_CUDA(cudaMemcpyAsync(s.global_base.get(), s.host_global_base.data(),
+                          s.nlist * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+  s.codes.allocate(std::max<size_t>(1, s.count * s.m));
+  s.labels.allocate(std::max<size_t>(1, s.count) * sizeof(uint64_t));
+  if (s.count > 0) {
+    QV_CUDA(cudaMemcpyAsync(s.codes.get(), s.host_codes.data(), s.count * s.m,
+                            cudaMemcpyHostToDevice, st));
+    QV_CUDA(cudaMemcpyAsync(s.labels.get(), s.host_labels.data(), s.count * sizeof(uint64_t),
+                            cudaMemcpyHostToDevice, st));
+  }
+  QV_CUDA(cudaStreamSynchronize(st));
+}
+
+static size_t keep_for(size_t count, size_t k, size_t refine_factor, bool store_vectors,
+                       bool* refine) {
+  // src/ivfpq_index.cc:303-307, saturating.
+  *refine = refine_factor > 0 && store_vectors;
+  const size_t factor = *refine ? refine_factor : 1;
+  const size_t kk = std::max<size_t>(k, 1);
+  return std::min(count, factor > count / kk ? count : k * factor);
+}
+
+void ivf_search(const IvfState& s, const float* d_queries, size_t nq, size_t k, size_t nprobe,
+                size_t refine_factor, const uint64_t* d_bitmap, uint64_t* d_labels,
+                float* d_dists, cudaStream_t st) {
+  if (nq == 0 || k == 0) return;
+  bool refine = false;
+  const size_t keep = keep_for(s.count, k, refine_factor, s.store_vectors, &refine);
+  if (keep == 0 || !s.trained) {  // src/ivfpq_index.cc:277-279, :308
+    std::vector<float> inf(nq * k, INFINITY);
+    std::vector<uint64_t> inv(nq * k, kInvalidLabel);
+    QV_CUDA(cudaMemcpyAsync(d_dists, inf.data(), nq * k * sizeof(float), cudaMemcpyHostToDevice, st));
+    QV_CUDA(cudaMemcpyAsync(d_labels, inv.data(), nq * k * sizeof(uint64_t), cudaMemcpyHostToDevice, st));
+    QV_CUDA(cudaStreamSynchronize(st));
+    return;
+  }
+  QV_REQUIRE(keep <= 3840, "IVF-PQ search: k * refine_factor above 3840 candidates per query is "
+                           "not supported on the GPU");
+  Prepared p = prepare_search(s, d_queries, nq, nprobe, st);
+  run_scan(s, p, nq, keep, k, refine, d_bitmap, false, d_labels, d_dists, nullptr, st);
+}
+
+void ivf_candidates(const IvfState& s, const float* d_queries, size_t nq, size_t keep,
+                    size_t nprobe, const uint64_t* d_bitmap, float* d_dists, uint64_t* d_keys,
+                    uint64_t* d_labels, cudaStream_t st) {
+  if (nq == 0 || keep == 0) return;
+  QV_REQUIRE(s.trained, "IVF-PQ index must be trained before search");
+  QV_REQUIRE(keep <= 3840, "IVF-PQ candidates: keep above 3840 is not supported on the GPU");
+  Prepared p = prepare_search(s, d_queries, nq, nprobe, st);
+  run_scan(s, p, nq, keep, keep, false, d_bitmap, true, d_labels, d_dists, d_keys, st);
+}
+
+void ivf_refine(const IvfState& s, const float* d_queries, size_t nq, size_t keep,
+                const uint64_t* d_keys, float* d_exact, cudaStream_t st) {
+  if (nq == 0 || keep == 0) return;
+  QV_REQUIRE(s.store_vectors, "refine needs store_vectors");
+  DeviceBuffer qn(nq * s.dim * sizeof(float), st);
+  copy_queries_kernel<<<std::min<size_t>(ceil_div(nq * s.dim, 256), 4096), 256, 0, st>>>(
+      d_queries, nq * s.dim, qn.get<float>());
+  check_launch("copy_queries_kernel");
+  if (s.metric == QV_METRIC_COSINE) normalize_rows_device(qn.get<float>(), nq, s.dim, st);
+  const size_t warps = nq * keep;
+  ivf_refine_kernel<<<ceil_div(warps, 8), 256, 0, st>>>(
+      qn.get<float>(), nq, static_cast<int>(s.dim), static_cast<int>(keep), d_keys,
+      s.offsets.get<uint64_t>(), s.global_base.get<uint32_t>(), s.nlist, s.vectors.get<float>(),
+      s.metric == QV_METRIC_L2, d_exact);
+  check_launch("ivf_refine_kernel");
+}
+
+}  // namespace qv

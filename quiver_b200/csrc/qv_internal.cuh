@@ -1,0 +1,364 @@
+// Internal helpers shared by the quiver-b200 CUDA translation units: error state behind the C ABI,
+// device memory ownership, per-thread streams, and the device restatements of the reference's
+// float reductions that make distances, assignments and codes bit-identical to the CPU library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdio>
+#include <string>
+#include <utility>
+
+#include "qv_gpu.h"
+
+namespace qv {
+
+// ---- error state ------------------------------------------------------------------------------
+
+void set_error(const std::string& msg);
+const std::string& last_error();
+
+// Thrown inside the library only; every extern "C" entry point catches it and returns its status.
+struct Failure {
+  qv_status status;
+  std::string msg;
+};
+
+[[noreturn]] inline void fail(qv_status s, const std::string& msg) { throw Failure{s, msg}; }
+
+#define QV_REQUIRE(cond, msg)                          \
+  do {                                                 \
+    if (!(cond)) ::qv::fail(QV_ERR_INVALID, (msg));    \
+  } while (0)
+
+#define QV_CUDA(call)                                                                         \
+  do {                                                                                        \
+    cudaError_t e_ = (call);                                                                  \
+    if (e_ != cudaSuccess) {                                                                  \
+      ::qv::fail(e_ == cudaErrorMemoryAllocation ? QV_ERR_OOM : QV_ERR_CUDA,                  \
+                 std::string(#call) + ": " + cudaGetErrorString(e_));                         \
+    }                                                                                         \
+  } while (0)
+
+// Runs `f` and converts any Failure (or std::bad_alloc) into a status + thread-local message.
+template <class F>
+qv_status guarded(F&& f) {
+  try {
+    f();
+    return QV_OK;
+  } catch (const Failure& e) {
+    set_error(e.msg);
+    return e.status;
+  } catch (const std::bad_alloc&) {
+    set_error("out of host memory");
+    return QV_ERR_OOM;
+  } catch (const std::exception& e) {
+    set_error(e.what());
+    return QV_ERR_INVALID;
+  }
+}
+
+// ---- devices, streams, memory -------------------------------------------------------------------
+
+// Makes `device` current for the scope and restores the previous device.
+class DeviceScope {
+ public:
+  explicit DeviceScope(int device) {
+    QV_CUDA(cudaGetDevice(&prev_));
+    if (prev_ != device) QV_CUDA(cudaSetDevice(device));
+  }
+  ~DeviceScope() {
+    int cur = -1;
+    if (cudaGetDevice(&cur) == cudaSuccess && cur != prev_) cudaSetDevice(prev_);
+  }
+  DeviceScope(const DeviceScope&) = delete;
+  DeviceScope& operator=(const DeviceScope&) = delete;
+
+ private:
+  int prev_ = 0;
+};
+
+// The calling thread's non-blocking stream on `device` (created on first use, kept for the
+// thread's lifetime), so concurrent host threads never serialize on one stream.
+cudaStream_t thread_stream(int device);
+
+// Owning device allocation. Allocated with cudaMallocAsync on a stream when given one.
+class DeviceBuffer {
+ public:
+  DeviceBuffer() = default;
+  DeviceBuffer(size_t bytes, cudaStream_t stream = nullptr) { allocate(bytes, stream); }
+  ~DeviceBuffer() { release(); }
+  DeviceBuffer(DeviceBuffer&& o) noexcept { swap(o); }
+  DeviceBuffer& operator=(DeviceBuffer&& o) noexcept {
+    if (this != &o) {
+      release();
+      swap(o);
+    }
+    return *this;
+  }
+  DeviceBuffer(const DeviceBuffer&) = delete;
+  DeviceBuffer& operator=(const DeviceBuffer&) = delete;
+
+  void allocate(size_t bytes, cudaStream_t stream = nullptr) {
+    release();
+    if (bytes == 0) return;
+    if (stream != nullptr) {
+      QV_CUDA(cudaMallocAsync(&ptr_, bytes, stream));
+      stream_ = stream;
+    } else {
+      QV_CUDA(cudaMalloc(&ptr_, bytes));
+    }
+    bytes_ = bytes;
+  }
+  void release() noexcept {
+    if (ptr_ != nullptr) {
+      if (stream_ != nullptr) {
+        cudaFreeAsync(ptr_, stream_);
+      } else {
+        cudaFree(ptr_);
+      }
+    }
+    ptr_ = nullptr;
+    bytes_ = 0;
+    stream_ = nullptr;
+  }
+  template <class T = void>
+  T* get() const noexcept {
+    return static_cast<T*>(ptr_);
+  }
+  size_t bytes() const noexcept { return bytes_; }
+
+ private:
+  void swap(DeviceBuffer& o) noexcept {
+    std::swap(ptr_, o.ptr_);
+    std::swap(bytes_, o.bytes_);
+    std::swap(stream_, o.stream_);
+  }
+  void* ptr_ = nullptr;
+  size_t bytes_ = 0;
+  cudaStream_t stream_ = nullptr;
+};
+
+// Per-thread launch accounting behind qv_last_search_stats().
+struct SearchStats {
+  uint64_t kernel_launches = 0;
+  uint64_t rescanned_queries = 0;
+  double dominant_ms = 0.0;
+  double dominant_work = 0.0;
+  bool work_is_bytes = false;
+  std::string dominant_name;
+};
+SearchStats& thread_stats();
+bool& thread_timing();  // qv_set_timing
+
+// Brackets one launch with CUDA events when timing is on; finish() (after the stream has been
+// synchronized) adds the elapsed time and work to the thread's stats.
+class KernelTimer {
+ public:
+  KernelTimer(cudaStream_t st, const char* name, double work, bool is_bytes)
+      : st_(st), name_(name), work_(work), bytes_(is_bytes), on_(thread_timing()) {
+    if (on_) {
+      cudaEventCreate(&e0_);
+      cudaEventCreate(&e1_);
+      cudaEventRecord(e0_, st_);
+    }
+  }
+  void stop() {
+    if (on_) cudaEventRecord(e1_, st_);
+  }
+  void finish() {
+    if (!on_) return;
+    float ms = 0.0f;
+    if (cudaEventElapsedTime(&ms, e0_, e1_) == cudaSuccess) {
+      SearchStats& s = thread_stats();
+      s.dominant_ms += ms;
+      s.dominant_work += work_;
+      s.work_is_bytes = bytes_;
+      s.dominant_name = name_;
+    }
+    cudaEventDestroy(e0_);
+    cudaEventDestroy(e1_);
+    on_ = false;
+  }
+  ~KernelTimer() {
+    if (on_) {
+      cudaEventDestroy(e0_);
+      cudaEventDestroy(e1_);
+    }
+  }
+
+ private:
+  cudaStream_t st_;
+  const char* name_;
+  double work_;
+  bool bytes_;
+  bool on_;
+  cudaEvent_t e0_ = nullptr, e1_ = nullptr;
+};
+inline void count_launch(uint64_t n = 1) { thread_stats().kernel_launches += n; }
+
+inline void check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) fail(QV_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  count_launch();
+}
+
+// Host-side input validation, as the reference's check_finite (src/flat_index.cc:34-38).
+void check_finite(const float* v, size_t count);
+
+// Number of SMs of `device` (cached).
+int sm_count(int device);
+
+constexpr int kSubCentroids = 256;
+constexpr uint64_t kInvalidLabel = UINT64_MAX;
+
+inline size_t ceil_div(size_t a, size_t b) { return (a + b - 1) / b; }
+inline size_t next_pow2(size_t x) {
+  size_t p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+}  // namespace qv
+
+// ---- device restatements of the reference's float reductions ------------------------------------
+//
+// Every operation names its rounding: __fmaf_rn where the reference executes an FMA,
+// __fmul_rn/__fadd_rn/__fsub_rn where it rounds a product and a sum separately. nvcc would otherwise
+// contract a*b+c into an FMA and change the last bit.
+
+namespace qv::dev {
+
+constexpr unsigned kFull = 0xffffffffu;
+
+// simd::avx2::dot (src/simd/kernels_avx2.cc:63-83), evaluated by one warp. Lane l owns the AVX2
+// accumulator element s[l >> 3][l & 7], so the 32-element blocks are read coalesced; the combine
+// is (s0+s1)+(s2+s3) per lane, then hsum (:17-23): (t[l]+t[l+4]) pairs, then (lo0+lo1)+(lo2+lo3).
+// The dim % 8 tail follows what GCC emits for the reference's scalar loop under its build flags:
+// with 4 or more elements left, the first 4 products are rounded and added in order, the rest
+// are FMAs. All lanes return the same value.
+template <bool kDiff>
+__device__ __forceinline__ float warp_reduce_avx2(const float* __restrict__ a,
+                                                  const float* __restrict__ b, int dim, int lane) {
+  float s = 0.0f;
+  int i = 0;
+  for (; i + 32 <= dim; i += 32) {
+    float u = a[i + lane], v = b[i + lane];
+    if (kDiff) {
+      u = __fsub_rn(u, v);
+      v = u;
+    }
+    s = __fmaf_rn(u, v, s);
+  }
+  for (; i + 8 <= dim; i += 8) {
+    if (lane < 8) {
+      float u = a[i + lane], v = b[i + lane];
+      if (kDiff) {
+        u = __fsub_rn(u, v);
+        v = u;
+      }
+      s = __fmaf_rn(u, v, s);
+    }
+  }
+  const float s1 = __shfl_down_sync(kFull, s, 8);
+  const float s2 = __shfl_down_sync(kFull, s, 16);
+  const float s3 = __shfl_down_sync(kFull, s, 24);
+  const float t = __fadd_rn(__fadd_rn(s, s1), __fadd_rn(s2, s3));
+  const float lo = __fadd_rn(t, __shfl_down_sync(kFull, t, 4));
+  const float lo1 = __shfl_down_sync(kFull, lo, 1);
+  const float lo2 = __shfl_down_sync(kFull, lo, 2);
+  const float lo3 = __shfl_down_sync(kFull, lo, 3);
+  float sum = __fadd_rn(__fadd_rn(lo, lo1), __fadd_rn(lo2, lo3));
+  sum = __shfl_sync(kFull, sum, 0);
+  int j = i;
+  if (dim - i >= 4) {
+    for (; j < i + 4; ++j) {
+      float u = a[j], v = b[j];
+      if (kDiff) {
+        u = __fsub_rn(u, v);
+        v = u;
+      }
+      sum = __fadd_rn(sum, __fmul_rn(u, v));
+    }
+  }
+  for (; j < dim; ++j) {
+    float u = a[j], v = b[j];
+    if (kDiff) {
+      u = __fsub_rn(u, v);
+      v = u;
+    }
+    sum = __fmaf_rn(u, v, sum);
+  }
+  return sum;
+}
+
+__device__ __forceinline__ float warp_dot_avx2(const float* a, const float* b, int dim, int lane) {
+  return warp_reduce_avx2<false>(a, b, dim, lane);
+}
+__device__ __forceinline__ float warp_l2sqr_avx2(const float* a, const float* b, int dim,
+                                                 int lane) {
+  return warp_reduce_avx2<true>(a, b, dim, lane);
+}
+
+// The reference's exact distance (src/flat_index.cc:87, src/ivfpq_index.cc:138-142).
+__device__ __forceinline__ float warp_exact_distance(const float* q, const float* x, int dim,
+                                                     bool l2, int lane) {
+  if (l2) return warp_l2sqr_avx2(q, x, dim, lane);
+  return __fsub_rn(1.0f, warp_dot_avx2(q, x, dim, lane));
+}
+
+// Distances order NaN after everything (src/flat_index.cc:88).
+__device__ __forceinline__ float nan_to_inf(float d) { return d == d ? d : __int_as_float(0x7f800000); }
+
+// Strict weak order on (distance, key): the canonical tie-break used by every selection.
+__device__ __forceinline__ bool key_less(float da, uint64_t ka, float db, uint64_t kb) {
+  return da < db || (da == db && ka < kb);
+}
+
+// float -> uint32 whose unsigned order matches the float order (for atomicMin on thresholds).
+__device__ __forceinline__ uint32_t ordered_bits(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float from_ordered_bits(uint32_t u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+
+__device__ __forceinline__ bool bitmap_test(const uint64_t* bm, uint64_t pos) {
+  return bm == nullptr || ((bm[pos >> 6] >> (pos & 63)) & 1ull) != 0;
+}
+
+// Block-wide bitonic sort of n (power of two) (distance, key) pairs in shared memory, ascending.
+// Optionally carries a 64-bit payload. All threads of the block must call it.
+template <bool kPayload>
+__device__ void block_bitonic_sort(float* d, uint64_t* k, uint64_t* p, int n) {
+  for (int size = 2; size <= n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < n / 2; i += blockDim.x) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool up = ((lo & size) == 0);
+        const bool swap = up ? key_less(d[hi], k[hi], d[lo], k[lo])
+                             : key_less(d[lo], k[lo], d[hi], k[hi]);
+        if (swap) {
+          float td = d[lo];
+          d[lo] = d[hi];
+          d[hi] = td;
+          uint64_t tk = k[lo];
+          k[lo] = k[hi];
+          k[hi] = tk;
+          if (kPayload) {
+            uint64_t tp = p[lo];
+            p[lo] = p[hi];
+            p[hi] = tp;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
+}  // namespace qv::dev

@@ -1,0 +1,102 @@
+// Host-side state of the GPU indexes behind the C ABI handles, and the launcher entry points the
+// kernels' translation units export to capi.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <vector>
+
+#include "qv_internal.cuh"
+
+namespace qv {
+
+// ---- Flat --------------------------------------------------------------------------------------
+// Rows live in HBM row-major as float32 exactly as the reference stores them (normalized for
+// cosine), with their labels, a squared norm per row for the L2 screen, and a bfloat16 copy padded
+// to a multiple of 64 columns for the tensor-core screen.
+struct FlatState {
+  int device = 0;
+  size_t dim = 0;
+  uint32_t metric = 0;
+  uint64_t row_offset = 0;
+  size_t n = 0, cap = 0;
+  DeviceBuffer x;         // cap x dim f32
+  DeviceBuffer xnorm2;    // cap f32, sum of squares (screen only)
+  DeviceBuffer labels;    // cap u64
+  DeviceBuffer xbf16;     // cap x kpad bf16 (tensor screen), kpad = dim rounded up to 64
+  size_t kpad = 0;
+  float max_norm = 0.0f;  // max ||x|| over stored rows (screen error bound)
+  std::vector<uint64_t> host_labels;
+};
+
+void flat_reserve(FlatState& s, size_t rows, cudaStream_t st);
+// Appends n rows (device pointer, row-major) with labels (device pointer).
+void flat_append(FlatState& s, const float* d_rows, const uint64_t* d_labels, size_t n,
+                 cudaStream_t st);
+void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k,
+                 const uint64_t* d_bitmap, uint64_t* d_labels, float* d_dists, uint64_t* d_keys,
+                 cudaStream_t st);
+
+// ---- IVF-PQ ------------------------------------------------------------------------------------
+// Inverted lists are stored list-major and contiguous in HBM (codes count x m bytes, labels,
+// optional float32 vectors) with offsets[nlist+1]; global_base[l] is the offset of this index's
+// first entry of list l inside the full (unsharded) list, which makes candidate keys comparable
+// across shards.
+struct IvfState {
+  int device = 0;
+  size_t dim = 0, nlist = 0, m = 0, dsub = 0;
+  uint32_t metric = 0;
+  size_t train_iterations = 20;
+  bool store_vectors = false;
+  uint64_t seed = 1234;
+  bool trained = false;
+  size_t count = 0;
+  DeviceBuffer centroids;    // nlist x dim f32
+  DeviceBuffer cnorm2;       // nlist f32, ||c||^2 sequential (CentroidTable::reset)
+  DeviceBuffer codebooks;    // m x 256 x dsub f32
+  DeviceBuffer precomputed;  // nlist x m x 256 f32 (L2 and within budget) or empty
+  DeviceBuffer offsets;      // nlist + 1 u64
+  DeviceBuffer global_base;  // nlist u32
+  DeviceBuffer codes;        // count x m u8
+  DeviceBuffer labels;       // count u64
+  DeviceBuffer vectors;      // count x dim f32 (store_vectors)
+  std::vector<float> host_centroids, host_codebooks;
+  std::vector<uint64_t> host_offsets;
+  std::vector<uint32_t> host_global_base;
+  std::vector<uint8_t> host_codes;
+  std::vector<uint64_t> host_labels;
+  bool ip() const { return metric != 0; }
+  bool use_precomputed() const { return precomputed.bytes() != 0; }
+};
+
+void ivf_set_trained(IvfState& s, const float* h_centroids, const float* h_codebooks,
+                     cudaStream_t st);
+// Coarse assignment + PQ encode of n device rows (already normalized for cosine when needed).
+void ivf_encode_device(const IvfState& s, const float* d_x, size_t n, uint32_t* d_assign,
+                       uint8_t* d_codes, cudaStream_t st);
+// Normalizes n rows in place with simd::normalize semantics (cosine).
+void normalize_rows_device(float* d_x, size_t n, size_t dim, cudaStream_t st);
+// Rebuilds device list arrays from the host mirrors (+ optional device vectors in storage order).
+void ivf_upload_lists(IvfState& s, cudaStream_t st);
+void ivf_search(const IvfState& s, const float* d_queries, size_t nq, size_t k, size_t nprobe,
+                size_t refine_factor, const uint64_t* d_bitmap, uint64_t* d_labels,
+                float* d_dists, cudaStream_t st);
+void ivf_candidates(const IvfState& s, const float* d_queries, size_t nq, size_t keep,
+                    size_t nprobe, const uint64_t* d_bitmap, float* d_dists, uint64_t* d_keys,
+                    uint64_t* d_labels, cudaStream_t st);
+void ivf_refine(const IvfState& s, const float* d_queries, size_t nq, size_t keep,
+                const uint64_t* d_keys, float* d_exact, cudaStream_t st);
+
+// ---- selection / merge -------------------------------------------------------------------------
+void merge_topk(size_t parts, size_t nq, size_t k, const float* d, const uint64_t* keys,
+                const uint64_t* labels, float* od, uint64_t* ok, uint64_t* ol, cudaStream_t st);
+void select_topk(size_t nq, size_t n, size_t k, const float* d, const uint64_t* keys,
+                 const uint64_t* labels, float* od, uint64_t* ok, uint64_t* ol, cudaStream_t st);
+
+// Position bitmap on device from a label bitmap/set, for `count` stored labels (device pointer).
+void build_position_bitmap(const uint64_t* d_labels, size_t count, const qv_filter& f,
+                           uint64_t* d_bitmap, cudaStream_t st);
+
+}  // namespace qv

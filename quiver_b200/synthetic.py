@@ -1,0 +1,75 @@
+"""Seeded synthetic workloads for the benchmark configurations and the tests.
+
+The reference measured on ann-benchmarks SIFT1M / GloVe-1.2M, which are not available here; these
+generators stand in for them with the shapes, sizes and value distributions the benchmark
+configurations specify:
+
+* ``skewed_ints``: every component min(G - 1, 255) with G ~ Geometric(p=0.03), i.e. P(v) is
+  proportional to 0.97^v clipped to 0..255, cast to float32 (SIFT-like integer descriptors).
+* ``mixture``: a C-component Gaussian mixture (centres N(0, s_c^2), per-component sigma, equal
+  weights), L2-normalized in float32 (GloVe-like angular data).
+* ``gaussian`` / ``clustered``: small test distributions (standard normal; blobs around 2*N(0,1)
+  centres with unit noise).
+
+All use numpy's PCG64 (``np.random.default_rng``), so a seed fixes the data on every machine.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def skewed_ints(n: int, dim: int, seed: int) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    return np.minimum(rng.geometric(0.03, (n, dim)) - 1, 255).astype(np.float32)
+
+
+def mixture(n: int, dim: int, components: int, sigma: float, centre_scale: float, centre_seed: int,
+            seed: int, sigma_from_centre_norm: bool = False, chunk: int = 1 << 20) -> np.ndarray:
+    """L2-normalized mixture samples. ``sigma_from_centre_norm``: per-component sigma is
+    ``sigma * ||centre||`` instead of ``sigma``."""
+    rc = np.random.default_rng(centre_seed)
+    centres = (rc.standard_normal((components, dim)) * centre_scale).astype(np.float32)
+    sig = (sigma * np.linalg.norm(centres, axis=1) if sigma_from_centre_norm
+           else np.full(components, sigma)).astype(np.float32)
+    rng = np.random.default_rng(seed)
+    out = np.empty((n, dim), np.float32)
+    for s in range(0, n, chunk):
+        e = min(n, s + chunk)
+        a = rng.integers(0, components, e - s)
+        x = centres[a] + sig[a, None] * rng.standard_normal((e - s, dim), dtype=np.float32)
+        x /= np.linalg.norm(x, axis=1, keepdims=True).astype(np.float32)
+        out[s:e] = x
+    return out
+
+
+def gaussian(n: int, dim: int, seed: int) -> np.ndarray:
+    return np.random.default_rng(seed).standard_normal((n, dim), dtype=np.float32)
+
+
+def clustered(n: int, dim: int, clusters: int, seed: int) -> np.ndarray:
+    centres = 2.0 * np.random.default_rng(clusters * 1000003 + dim).standard_normal(
+        (clusters, dim), dtype=np.float32)
+    rng = np.random.default_rng(seed)
+    a = rng.integers(0, clusters, n)
+    return (centres[a] + rng.standard_normal((n, dim), dtype=np.float32)).astype(np.float32)
+
+
+# ---- benchmark configurations (BASELINE configs[0..4]) ----------------------------------------------
+
+def config0(seed_db: int = 0, seed_q: int = 1):
+    """FlatIndex L2, k=10: 100,000 x 128 skewed ints, 1,000 queries."""
+    return skewed_ints(100_000, 128, seed_db), skewed_ints(1_000, 128, seed_q)
+
+
+def config1(n: int = 1_183_514, nq: int = 10_000):
+    """FlatIndex cosine, k=10: 1,183,514 x 100 from a 1,000-component mixture (sigma 0.35)."""
+    db = mixture(n, 100, 1000, 0.35, 1.0, centre_seed=42, seed=0)
+    q = mixture(nq, 100, 1000, 0.35, 1.0, centre_seed=42, seed=1)
+    return db, q
+
+
+def config4_chunk(rows: int, chunk_index: int, dim: int = 768):
+    """One chunk of config 4 (40M x 768 inner product, 4,096-component mixture, sigma 0.5*||c||)."""
+    seed = np.random.SeedSequence(4).spawn(64)[chunk_index]
+    return mixture(rows, dim, 4096, 0.5, 1.0 / np.sqrt(dim), centre_seed=44,
+                   seed=int(seed.generate_state(1)[0]), sigma_from_centre_norm=True)

@@ -1,0 +1,147 @@
+"""FlatIndex on the GPU through the C ABI, against the reference's golden outputs and the oracle.
+
+Distances must be bit-identical to the reference's (the GPU re-ranks in the reference's own float
+summation order) and labels identical except among tied distances."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, golden_flat_inputs
+from parity import assert_sorted, assert_topk_parity
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("idx", range(6))
+def test_flat_matches_reference_golden(gpu, manifest, idx):
+    case = manifest["flat"][idx]
+    base, q, labels = golden_flat_inputs(case)
+    g = np.load(os.path.join(GOLDEN, case["name"] + ".npz"))
+    ix = gpu.FlatIndex(case["dim"], case["metric"])
+    ix.add(base, labels)
+    l, d = ix.search(q, case["k"])
+    assert_sorted(d)
+    assert_topk_parity(l, d, g["labels"], g["dists"], exact=True, what=case["name"])
+    l, d = ix.search(q, case["k"], filter=g["filt_allowed"])
+    assert_topk_parity(l, d, g["filt_labels"], g["filt_dists"], exact=True, what="filtered")
+    l, d = ix.search(q[:3], case["n"] + 5) if case["n"] + 5 <= 1024 else (None, None)
+    if l is not None:
+        assert_topk_parity(l, d, g["all_labels"], g["all_dists"], exact=True, what="k>n")
+
+
+@pytest.mark.parametrize("metric", ["l2", "ip", "cosine"])
+@pytest.mark.parametrize("dim", [1, 13, 100, 128, 129, 768])
+def test_flat_matches_oracle_shapes(gpu, oracle, metric, dim):
+    rng = np.random.default_rng(dim * 7 + len(metric))
+    n = 777 if dim < 700 else 300
+    base = rng.standard_normal((n, dim)).astype(np.float32)
+    q = rng.standard_normal((19, dim)).astype(np.float32)
+    labels = rng.permutation(n).astype(np.uint64) * 5
+    ix = gpu.FlatIndex(dim, metric)
+    ix.add(base[: n // 2], labels[: n // 2])
+    ix.add(base[n // 2:], labels[n // 2:])  # two adds: appends keep row order
+    stored = oracle.normalize_rows(base) if metric == "cosine" else base
+    v, la = ix.rows()
+    assert np.array_equal(v, stored) and np.array_equal(la, labels)
+    for k in (1, 10, 64):
+        l, d = ix.search(q, k)
+        wl, wd = oracle.flat_search(stored, labels, metric, q, k)
+        assert_topk_parity(l, d, wl, wd, exact=True, what=f"{metric} d={dim} k={k}")
+
+
+def test_known_answer(gpu):
+    # tests/test_flat.cc:37-52 of the reference.
+    base = np.array([[1, 0, 0, 0], [0, 2, 0, 0], [1, 1, 0, 0]], np.float32)
+    q = np.array([3, 0.1, 0, 0], np.float32)
+    cos = gpu.FlatIndex(4, "cosine")
+    cos.add(base)
+    l, d = cos.search(q, 3)
+    assert l[0, 0] == 0 and abs(d[0, 0] - (1 - 3 / np.sqrt(9.01))) < 1e-5
+    ip = gpu.FlatIndex(4, "ip")
+    ip.add(base)
+    l, d = ip.search(q, 3)
+    assert l[0, 0] == 2 and abs(d[0, 0] - (1 - 3.1)) < 1e-5
+
+
+def test_fewer_than_k_and_filters(gpu):
+    # tests/test_flat.cc:54-72 of the reference.
+    x = np.random.default_rng(3).standard_normal((10, 8)).astype(np.float32)
+    ix = gpu.FlatIndex(8)
+    ix.add(x, labels=np.arange(100, 110))
+    l, d = ix.search(x[:1], 50)
+    assert (l[0] >= 0).sum() == 10 and np.isinf(d[0, 10:]).all()
+    l, d = ix.search(x[:1], 5, filter={103, 107})
+    assert set(l[0, :2].tolist()) <= {103, 107} and l[0, 2] == -1 and np.isinf(d[0, 4])
+    l, _ = ix.search(x[:2], 3, filter=[])
+    assert (l == -1).all()
+    l, _ = ix.search(x[:1], 3, filter=[2**62])  # sparse labels take the label-set path
+    assert (l == -1).all()
+
+
+def test_empty_index_and_errors(gpu):
+    ix = gpu.FlatIndex(4)
+    l, d = ix.search(np.ones((2, 4)), 3)
+    assert (l == -1).all() and np.isinf(d).all()
+    with pytest.raises(ValueError, match="NaN"):
+        ix.add(np.array([[1, np.nan, 0, 0]], np.float32))
+    with pytest.raises(ValueError, match="NaN"):
+        ix.search(np.array([[1, np.inf, 0, 0]], np.float32), 1)
+    with pytest.raises(ValueError, match="2\\*\\*63"):
+        ix.add(np.zeros((1, 4)), labels=[2**63])
+    with pytest.raises(ValueError, match="dimension"):
+        ix.add(np.zeros((1, 5)))
+    with pytest.raises(ValueError):
+        gpu.FlatIndex(0)
+    with pytest.raises(ValueError):
+        gpu.FlatIndex(4, metric="hamming")
+
+
+def test_uncertified_queries_take_the_exact_rescan(gpu, oracle, monkeypatch):
+    """Integer data has exact distance ties; with a candidate budget of k the certificate cannot
+    separate the boundary, so those queries must be answered by the exact rescan."""
+    from quiver_b200.synthetic import skewed_ints
+    base = skewed_ints(4000, 16, 3)
+    base[:, 8:] = 0  # many equal distances
+    q = skewed_ints(25, 16, 4)
+    q[:, 8:] = 0
+    labels = np.arange(4000, dtype=np.uint64)
+    ix = gpu.FlatIndex(16)
+    ix.add(base)
+    monkeypatch.setenv("QV_FLAT_KK", "10")
+    l, d = ix.search(q, 10)
+    stats = gpu.last_search_stats()
+    assert stats["rescanned_queries"] > 0
+    wl, wd = oracle.flat_search(base, labels, "l2", q, 10)
+    assert_topk_parity(l, d, wl, wd, exact=True, what="rescan")
+
+
+def test_save_load_roundtrip_and_reference_format(gpu, tmp_path, reference):
+    x = np.random.default_rng(4).standard_normal((100, 16)).astype(np.float32)
+    ix = gpu.FlatIndex(16, "cosine")
+    ix.add(x)
+    ix.save(tmp_path / "flat.qvr")
+    back = gpu.FlatIndex.load(tmp_path / "flat.qvr")
+    assert len(back) == 100 and back.metric == "cosine"
+    assert np.array_equal(back.search(x, 5)[0], ix.search(x, 5)[0])
+    # a file written by the reference library loads and searches identically
+    rf = reference.flat(16, "cosine")
+    rf.add(x)
+    rf.save(tmp_path / "ref.qvr")
+    from_ref = gpu.FlatIndex.load(tmp_path / "ref.qvr")
+    rl, rd = rf.search(x, 5)
+    l, d = from_ref.search(x, 5)
+    assert_topk_parity(l, d, rl, rd, exact=True, what="reference .qvr")
+
+
+def test_config0_full_size_against_reference(gpu, reference):
+    """BASELINE config 0 at its full size (100k x 128 skewed ints, 1,000 queries, k=10)."""
+    from quiver_b200.synthetic import config0
+    base, q = config0()
+    ix = gpu.FlatIndex(128, "l2")
+    ix.add(base)
+    l, d = ix.search(q, 10)
+    rf = reference.flat(128, "l2")
+    rf.add(base)
+    rl, rd = rf.search(q, 10)
+    assert_topk_parity(l, d, rl, rd, exact=True, what="config0")

@@ -1,0 +1,133 @@
+"""IvfPqIndex on the GPU through the C ABI: bit-exact assignments and PQ codes against the
+reference-trained .qvr fixtures, and search parity (nprobe sweep, refine, filter) against the
+reference's golden outputs and the oracle."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, golden_ivf_inputs
+from parity import assert_sorted, assert_topk_parity
+
+pytestmark = pytest.mark.gpu
+
+
+def _qvr(case):
+    return os.path.join(GOLDEN, case["name"] + ".qvr")
+
+
+@pytest.mark.parametrize("idx", range(3))
+def test_encode_bit_exact_against_reference_qvr(gpu, manifest, idx):
+    from oracle.oracle import QvrIvf
+    case = manifest["ivf"][idx]
+    base, _ = golden_ivf_inputs(case)
+    qv = QvrIvf(_qvr(case))
+    ix = gpu.IvfPqIndex.load(_qvr(case))
+    assign, codes = ix.encode(base)
+    order = np.argsort(qv.labels)
+    assert np.array_equal(qv.assignments()[order], assign)
+    assert np.array_equal(qv.codes[order], codes)
+    # add() through the GPU reproduces the reference's lists exactly (order, codes, labels)
+    fresh = gpu.IvfPqIndex(case["dim"], case["metric"], case["nlist"], case["m"],
+                           store_vectors=True)
+    fresh.set_trained(qv.centroids, qv.codebooks)
+    fresh.add(base[:700])
+    fresh.add(base[700:])
+    assert fresh.list_sizes() == [int(x) for x in np.diff(qv.offsets)]
+    assert np.array_equal(fresh.stored_labels(), qv.labels)
+
+
+@pytest.mark.parametrize("idx", range(3))
+def test_search_matches_reference_golden(gpu, manifest, idx):
+    case = manifest["ivf"][idx]
+    _, q = golden_ivf_inputs(case)
+    g = np.load(os.path.join(GOLDEN, case["name"] + "_search.npz"))
+    ix = gpu.IvfPqIndex.load(_qvr(case))
+    for nprobe, rf in case["searches"]:
+        l, d = ix.search(q, 10, nprobe=nprobe, refine_factor=rf)
+        assert_sorted(d)
+        assert_topk_parity(l, d, g[f"labels_{nprobe}_{rf}"], g[f"dists_{nprobe}_{rf}"],
+                           exact=True, what=f"{case['name']} nprobe={nprobe} rf={rf}")
+    l, d = ix.search(q, 10, nprobe=case["filter_nprobe"], filter=g["filt_allowed"])
+    assert_topk_parity(l, d, g["filt_labels"], g["filt_dists"], exact=True, what="filtered")
+    assert np.isin(l[l >= 0], g["filt_allowed"].astype(np.int64)).all()
+    l, d = ix.search(q[:5], 10, nprobe=case["nlist"], refine_factor=1 << 62)
+    assert_topk_parity(l, d, g["sat_labels"], g["sat_dists"], exact=True, what="saturated keep")
+
+
+@pytest.mark.parametrize("metric", ["l2", "ip", "cosine"])
+def test_search_matches_oracle_larger(gpu, oracle, reference, tmp_path, metric):
+    from oracle.oracle import QvrIvf
+    from quiver_b200.synthetic import clustered
+    base = clustered(20000, 64, 30, 5)
+    q = clustered(200, 64, 30, 6)
+    r = reference.ivf(64, metric, 128, 16, store_vectors=True, train_iterations=6)
+    r.train(base[:8000])
+    r.add(base)
+    path = tmp_path / "ix.qvr"
+    r.save(path)
+    qv = QvrIvf(path)
+    ix = gpu.IvfPqIndex.load(path)
+    for nprobe, rf in [(1, 0), (8, 0), (32, 4), (128, 1)]:
+        l, d = ix.search(q, 10, nprobe=nprobe, refine_factor=rf)
+        wl, wd = oracle.ivf_search(qv, q, 10, nprobe, rf)
+        assert_topk_parity(l, d, wl, wd, exact=True, what=f"{metric} {nprobe} {rf}")
+        rl, rd = r.search(q, 10, nprobe, rf)
+        assert_topk_parity(l, d, rl, rd, exact=True, what=f"ref {metric} {nprobe} {rf}")
+
+
+def test_errors_and_roundtrip(gpu, tmp_path, manifest):
+    case = manifest["ivf"][0]
+    base, q = golden_ivf_inputs(case)
+    ix = gpu.IvfPqIndex(case["dim"], "l2", nlist=case["nlist"], m=case["m"], store_vectors=True)
+    assert not ix.is_trained
+    with pytest.raises(ValueError, match="trained"):
+        ix.add(base[:3])
+    with pytest.raises(NotImplementedError):
+        ix.train(base)
+    with pytest.raises(ValueError):
+        gpu.IvfPqIndex(10, m=3)
+    l, d = ix.search(q[:2], 4)
+    assert (l == -1).all() and np.isinf(d).all()
+    loaded = gpu.IvfPqIndex.load(_qvr(case))
+    loaded.save(tmp_path / "again.qvr")
+    again = gpu.IvfPqIndex.load(tmp_path / "again.qvr")
+    assert again.list_sizes() == loaded.list_sizes() and len(again) == len(loaded)
+    a = again.search(q, 5, nprobe=8, refine_factor=2)
+    b = loaded.search(q, 5, nprobe=8, refine_factor=2)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+    l, _ = loaded.search(base[5], 1, nprobe=case["nlist"], refine_factor=2)
+    assert l[0, 0] == 5  # self-match (tests/test_quantizer.cc:258)
+    assert loaded.memory_bytes > 0
+
+
+def test_sharded_load_merges_to_unsharded(gpu, manifest):
+    """Two id-range shards of one .qvr, candidates merged, equal the unsharded search."""
+    import ctypes as C
+    import torch
+    case = manifest["ivf"][2]
+    _, q = golden_ivf_inputs(case)
+    whole = gpu.IvfPqIndex.load(_qvr(case))
+    n = len(whole)
+    shards = [gpu.IvfPqIndex.load(_qvr(case), label_range=(0, n // 2)),
+              gpu.IvfPqIndex.load(_qvr(case), label_range=(n // 2, n))]
+    assert len(shards[0]) + len(shards[1]) == n
+    lib = gpu.lib()
+    keep, nq = 10, q.shape[0]
+    dq = torch.from_numpy(q).cuda()
+    parts_d = torch.empty((2, nq, keep), dtype=torch.float32, device="cuda")
+    parts_k = torch.empty((2, nq, keep), dtype=torch.int64, device="cuda")
+    parts_l = torch.empty((2, nq, keep), dtype=torch.int64, device="cuda")
+    for i, s in enumerate(shards):
+        gpu._native.check(lib.qv_ivfpq_candidates_device(
+            s.handle, dq.data_ptr(), nq, keep, 8, None, parts_d[i].data_ptr(),
+            parts_k[i].data_ptr(), parts_l[i].data_ptr(), None))
+    od = torch.empty((nq, keep), dtype=torch.float32, device="cuda")
+    ol = torch.empty((nq, keep), dtype=torch.int64, device="cuda")
+    ok = torch.empty((nq, keep), dtype=torch.int64, device="cuda")
+    gpu._native.check(lib.qv_merge_topk_device(0, 2, nq, keep, parts_d.data_ptr(),
+                                               parts_k.data_ptr(), parts_l.data_ptr(),
+                                               od.data_ptr(), ok.data_ptr(), ol.data_ptr(), None))
+    torch.cuda.synchronize()
+    wl, wd = whole.search(q, keep, nprobe=8)
+    assert_topk_parity(ol.cpu().numpy(), od.cpu().numpy(), wl, wd, exact=True, what="sharded")
