@@ -87,19 +87,20 @@ __global__ void row_stats_kernel(const float* x, size_t n, int dim, float* norm2
   }
 }
 
-__global__ void to_bf16_kernel(const float* x, size_t n, int dim, int kpad, __nv_bfloat16* out) {
-  const size_t total = n * static_cast<size_t>(kpad);
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const size_t r = i / kpad;
-    const int c = static_cast<int>(i - r * kpad);
-    out[i] = __float2bfloat16_rn(c < dim ? x[r * dim + c] : 0.0f);
-  }
-}
+// Error model of the float32 SIMT screen against the reference's float32 result: both sums carry
+// at most gamma_d = d*u/(1-d*u) relative error of sum|q_i x_i| <= ||q|| ||x|| (u = 2^-24), plus the
+// rounding of the final 1 - dot or norm combination; doubled for margin.
+struct EpsModel {
+  float c_l2;   // multiplies (||q|| + max||x||)^2
+  float c_ip;   // multiplies ||q|| * max||x||
+  float c_abs;  // multiplies (1 + ||q|| * max||x||)
+};
 
-// Queries -> zero-padded rows (dpad columns), normalized for cosine; squared norm and norm.
+// Queries -> zero-padded rows (dpad columns), normalized for cosine; squared norm, and the SIMT
+// screen's error bound eps[q] (the tensor-core screen overwrites eps with its own bound).
 __global__ void prep_queries_kernel(const float* q, size_t nq, int dim, int dpad, bool cosine,
-                                    float* qp, float* qnorm2, float* qnorm) {
+                                    bool l2, EpsModel em, float xmax, float* qp, float* qnorm2,
+                                    float* eps) {
   const int lane = threadIdx.x & 31;
   const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= nq) return;
@@ -112,7 +113,13 @@ __global__ void prep_queries_kernel(const float* q, size_t nq, int dim, int dpad
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
   if (lane == 0) {
     qnorm2[row] = s;
-    qnorm[row] = sqrtf(s) * 1.0001f;
+    const float qn = sqrtf(s) * 1.0001f;
+    if (l2) {
+      const float t = qn + xmax;
+      eps[row] = em.c_l2 * t * t;
+    } else {
+      eps[row] = em.c_ip * qn * xmax + em.c_abs * (1.0f + qn * xmax);
+    }
   }
 }
 
@@ -267,24 +274,10 @@ __global__ void __launch_bounds__(128) flat_screen_simt_kernel(
 
 // ---- finalize: merge, exact rerank, certificate ------------------------------------------------------
 
-struct EpsModel {
-  float c_l2;   // multiplies (||q|| + max||x||)^2
-  float c_ip;   // multiplies ||q|| * max||x||
-  float c_abs;  // constant term (1 - dot rounding)
-};
-
-__device__ __forceinline__ float screen_eps(const EpsModel& e, bool l2, float qnorm, float xmax) {
-  if (l2) {
-    const float s = qnorm + xmax;
-    return e.c_l2 * s * s;
-  }
-  return e.c_ip * qnorm * xmax + e.c_abs * (1.0f + qnorm * xmax);
-}
-
 __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
-    const float* __restrict__ qp, int dpad, const float* __restrict__ qnorm, int nq,
+    const float* __restrict__ qp, int dpad, const float* __restrict__ eps_q, int nq,
     const float* __restrict__ x, int dim, const uint64_t* __restrict__ labels, uint64_t row_offset,
-    bool l2, EpsModel eps_model, float xmax, const float* __restrict__ cand_d,
+    bool l2, const float* __restrict__ cand_d,
     const uint32_t* __restrict__ cand_r, const int* __restrict__ cand_n, int n_chunks, int kk,
     int pool, int k, uint64_t* __restrict__ out_labels, float* __restrict__ out_d,
     uint64_t* __restrict__ out_keys, int* __restrict__ fail_count, int* __restrict__ fail_q,
@@ -339,10 +332,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
   if (threadIdx.x == 0) {
     const float dk = m >= k ? sd[k - 1] : kInf;
     bool ok = true;
-    if (total >= kk && m >= k) {
-      const float eps = screen_eps(eps_model, l2, qnorm[q], xmax);
-      ok = (T - eps) >= dk;
-    }
+    if (total >= kk && m >= k) ok = (T - eps_q[q]) >= dk;
     if (!ok) {
       const int slot = atomicAdd(fail_count, 1);
       fail_q[slot] = q;
@@ -505,7 +495,28 @@ void flat_append(FlatState& s, const float* d_rows, const uint64_t* d_labels, si
   memcpy(&mx, &bits, sizeof(mx));
   s.max_norm = std::max(s.max_norm, mx);
   s.n += n;
-  s.xbf16.release();  // rebuilt lazily by the tensor screen
+  s.x16_rows = 0;  // the fp16 copy is rebuilt by the next tensor-core search
+}
+
+// Chooses how many row chunks to split the database into: enough units (query tiles x chunks) to
+// fill the GPU, at most `max_chunks` (the finalize merges n_chunks * KK candidates per query in
+// one block), preferring counts that leave the last wave of a persistent grid nearly full.
+static int choose_chunks(size_t nrows, int n_qtiles, int max_chunks, int grid, int64_t align,
+                         int64_t* chunk_rows) {
+  const int limit = static_cast<int>(std::min<size_t>(max_chunks, ceil_div(nrows, align)));
+  int best = 1;
+  double best_eff = -1.0;
+  for (int c = std::max(1, limit / 2); c <= limit; ++c) {
+    const double units = static_cast<double>(c) * n_qtiles;
+    const double waves = std::ceil(units / grid);
+    const double eff = units / (waves * grid);
+    if (eff > best_eff + 1e-9 || (std::fabs(eff - best_eff) <= 1e-9 && c > best)) {
+      best_eff = eff;
+      best = c;
+    }
+  }
+  *chunk_rows = static_cast<int64_t>(ceil_div(ceil_div(nrows, best), align)) * align;
+  return static_cast<int>(ceil_div(nrows, static_cast<size_t>(*chunk_rows)));
 }
 
 void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k,
@@ -518,14 +529,6 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
   const bool l2 = s.metric == QV_METRIC_L2;
   const int nsm = sm_count(s.device);
 
-  DeviceBuffer qp(nq * dpad * sizeof(float), st), qn2(nq * sizeof(float), st),
-      qn(nq * sizeof(float), st);
-  prep_queries_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(d_queries, nq, dim, dpad,
-                                                       s.metric == QV_METRIC_COSINE,
-                                                       qp.get<float>(), qn2.get<float>(),
-                                                       qn.get<float>());
-  check_launch("prep_queries_kernel");
-
   if (s.n == 0) {  // nothing stored: every slot unfilled
     std::vector<float> inf(nq * k, INFINITY);
     std::vector<uint64_t> inv(nq * k, kInvalidLabel);
@@ -537,66 +540,89 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
     return;
   }
 
-  // Candidate budget: KK >= k plus a margin, power of two.
-  // QV_FLAT_KK overrides the budget (any value >= k); small budgets exercise the exact rescan.
-  int kk = static_cast<int>(next_pow2(k + std::max<size_t>(8, k / 4)));
-  const int forced_kk = env_int("QV_FLAT_KK", 0);
-  if (forced_kk > 0) kk = std::max<int>(static_cast<int>(k), forced_kk);
-  const int heap_budget = 64 * 1024;
-  int qpb = std::min<int>(128, heap_budget / (kk * 8));
-  if (qpb >= 32) qpb = qpb / 32 * 32;
-  qpb = std::max(1, qpb);
-  const int n_qtiles = static_cast<int>(ceil_div(nq, qpb));
-  int max_chunks = std::max(1, kMaxCandidatesPerQuery / kk);
-  const int target_units = 8 * nsm;
-  int n_chunks = static_cast<int>(std::min<size_t>(
-      std::min<size_t>(max_chunks, ceil_div(target_units, n_qtiles)), ceil_div(s.n, kScreenRows)));
-  n_chunks = std::max(1, n_chunks);
-  int64_t chunk_rows = static_cast<int64_t>(ceil_div(ceil_div(s.n, n_chunks), kScreenRows)) * kScreenRows;
-  n_chunks = static_cast<int>(ceil_div(s.n, static_cast<size_t>(chunk_rows)));
-
-  const size_t slots = nq * static_cast<size_t>(n_chunks);
-  DeviceBuffer cand_d(slots * kk * sizeof(float), st), cand_r(slots * kk * sizeof(uint32_t), st),
-      cand_n(slots * sizeof(int), st), thr(nq * sizeof(unsigned), st);
-  QV_CUDA(cudaMemsetAsync(cand_n.get(), 0, slots * sizeof(int), st));
-  fill_u32_kernel<<<std::min<size_t>(ceil_div(nq, 256), 1024), 256, 0, st>>>(
-      thr.get<unsigned>(), nq, 0xff800000u /* ordered bits of +inf */);
-  check_launch("fill_u32_kernel");
-
-  const size_t smem = kScreenRows * kScreenDChunk * sizeof(float) +
-                      static_cast<size_t>(kk) * qpb * (sizeof(float) + sizeof(uint32_t));
-  const dim3 grid(static_cast<unsigned>(n_qtiles * n_chunks));
-  KernelTimer timer(st, "flat_screen_simt_kernel", 2.0 * nq * static_cast<double>(s.n) * dim,
-                    false);
-  if (l2) {
-    QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<true>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    flat_screen_simt_kernel<true><<<grid, 128, smem, st>>>(
-        qp.get<float>(), dpad, qn2.get<float>(), static_cast<int>(nq), qpb, s.x.get<float>(), dim,
-        s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, chunk_rows, n_qtiles,
-        n_chunks, kk, cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(),
-        thr.get<unsigned>());
-  } else {
-    QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<false>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    flat_screen_simt_kernel<false><<<grid, 128, smem, st>>>(
-        qp.get<float>(), dpad, qn2.get<float>(), static_cast<int>(nq), qpb, s.x.get<float>(), dim,
-        s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, chunk_rows, n_qtiles,
-        n_chunks, kk, cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(),
-        thr.get<unsigned>());
-  }
-  timer.stop();
-  check_launch("flat_screen_simt_kernel");
-
-  // Error model of the float32 screen against the reference's float32 result: both sums carry
-  // at most gamma_d = d*u/(1-d*u) relative error of sum|q_i x_i| (u = 2^-24), plus the rounding
-  // of the final 1 - dot or norm combination; doubled for margin.
   const double u = std::ldexp(1.0, -24);
   const double gamma = (dim + 2) * u / (1.0 - (dim + 2) * u);
   EpsModel em;
   em.c_l2 = static_cast<float>(2.0 * (2.0 * gamma + 4.0 * u));
   em.c_ip = static_cast<float>(2.0 * (2.0 * gamma));
   em.c_abs = static_cast<float>(2.0 * (2.0 * u));
+  DeviceBuffer qp(nq * dpad * sizeof(float), st), qn2(nq * sizeof(float), st),
+      eps(nq * sizeof(float), st);
+  prep_queries_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(d_queries, nq, dim, dpad,
+                                                       s.metric == QV_METRIC_COSINE, l2, em,
+                                                       s.max_norm, qp.get<float>(),
+                                                       qn2.get<float>(), eps.get<float>());
+  check_launch("prep_queries_kernel");
+
+  // QV_FLAT_KK overrides the candidate budget of the SIMT screen (any value >= k); small budgets
+  // exercise the exact rescan. QV_FLAT_SCREEN=simt selects the SIMT screen.
+  const int forced_kk = env_int("QV_FLAT_KK", 0);
+  const bool tensor = forced_kk == 0 && flat_tc_eligible(s, k);
+  int kk, n_qtiles, n_chunks, qpb = 0;
+  int64_t chunk_rows = 0;
+  if (tensor) {
+    kk = flat_tc_kk();
+    n_qtiles = static_cast<int>(ceil_div(nq, 128));
+    n_chunks = choose_chunks(s.n, n_qtiles, std::max(1, kMaxCandidatesPerQuery / kk), nsm, 128,
+                             &chunk_rows);
+  } else {
+    kk = static_cast<int>(next_pow2(k + std::max<size_t>(8, k / 4)));
+    if (forced_kk > 0) kk = std::max<int>(static_cast<int>(k), forced_kk);
+    const int heap_budget = 64 * 1024;
+    qpb = std::min<int>(128, heap_budget / (kk * 8));
+    if (qpb >= 32) qpb = qpb / 32 * 32;
+    qpb = std::max(1, qpb);
+    n_qtiles = static_cast<int>(ceil_div(nq, qpb));
+    n_chunks = choose_chunks(s.n, n_qtiles, std::max(1, kMaxCandidatesPerQuery / kk), 3 * nsm,
+                             kScreenRows, &chunk_rows);
+  }
+
+  const size_t slots = nq * static_cast<size_t>(n_chunks);
+  DeviceBuffer cand_d(slots * kk * sizeof(float), st), cand_r(slots * kk * sizeof(uint32_t), st),
+      cand_n(slots * sizeof(int), st), thr(nq * sizeof(unsigned), st), err(sizeof(int), st);
+  QV_CUDA(cudaMemsetAsync(cand_n.get(), 0, slots * sizeof(int), st));
+  QV_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+  fill_u32_kernel<<<std::min<size_t>(ceil_div(nq, 256), 1024), 256, 0, st>>>(
+      thr.get<unsigned>(), nq, 0xff800000u /* ordered bits of +inf */);
+  check_launch("fill_u32_kernel");
+
+  if (tensor) {
+    {
+      FlatState& ms = const_cast<FlatState&>(s);  // the fp16 copy is a cache of the rows
+      std::lock_guard<std::mutex> lock(ms.x16_mu);
+      flat_tc_prepare(ms, st);
+    }
+    flat_screen_tc(s, qp.get<float>(), dpad, nq, d_bitmap, n_chunks, chunk_rows,
+                   cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(),
+                   thr.get<unsigned>(), eps.get<float>(), err.get<int>(), st);
+  } else {
+    const size_t smem = kScreenRows * kScreenDChunk * sizeof(float) +
+                        static_cast<size_t>(kk) * qpb * (sizeof(float) + sizeof(uint32_t));
+    const dim3 grid(static_cast<unsigned>(n_qtiles * n_chunks));
+    KernelTimer timer(st, "flat_screen_simt_kernel", 2.0 * nq * static_cast<double>(s.n) * dim,
+                      false);
+    if (l2) {
+      QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<true>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      flat_screen_simt_kernel<true><<<grid, 128, smem, st>>>(
+          qp.get<float>(), dpad, qn2.get<float>(), static_cast<int>(nq), qpb, s.x.get<float>(),
+          dim, s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, chunk_rows, n_qtiles,
+          n_chunks, kk, cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(),
+          thr.get<unsigned>());
+    } else {
+      QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<false>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      flat_screen_simt_kernel<false><<<grid, 128, smem, st>>>(
+          qp.get<float>(), dpad, qn2.get<float>(), static_cast<int>(nq), qpb, s.x.get<float>(),
+          dim, s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, chunk_rows, n_qtiles,
+          n_chunks, kk, cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(),
+          thr.get<unsigned>());
+    }
+    timer.stop();
+    check_launch("flat_screen_simt_kernel");
+    QV_CUDA(cudaStreamSynchronize(st));
+    timer.finish();
+  }
 
   const int pool = static_cast<int>(next_pow2(static_cast<size_t>(n_chunks) * kk));
   DeviceBuffer fail(sizeof(int) + nq * (sizeof(int) + sizeof(float)), st);
@@ -608,10 +634,10 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
   QV_CUDA(cudaFuncSetAttribute(flat_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)fsmem));
   flat_finalize_kernel<<<static_cast<unsigned>(nq), kFinalizeThreads, fsmem, st>>>(
-      qp.get<float>(), dpad, qn.get<float>(), static_cast<int>(nq), s.x.get<float>(), dim,
-      s.labels.get<uint64_t>(), s.row_offset, l2, em, s.max_norm, cand_d.get<float>(),
-      cand_r.get<uint32_t>(), cand_n.get<int>(), n_chunks, kk, pool, static_cast<int>(k),
-      d_labels, d_dists, d_keys, fail_count, fail_q, fail_dk);
+      qp.get<float>(), dpad, eps.get<float>(), static_cast<int>(nq), s.x.get<float>(), dim,
+      s.labels.get<uint64_t>(), s.row_offset, l2, cand_d.get<float>(), cand_r.get<uint32_t>(),
+      cand_n.get<int>(), n_chunks, kk, pool, static_cast<int>(k), d_labels, d_dists, d_keys,
+      fail_count, fail_q, fail_dk);
   check_launch("flat_finalize_kernel");
 
   const int cap = static_cast<int>(next_pow2(k + 256));
@@ -626,7 +652,6 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
   int nfail = 0;
   QV_CUDA(cudaMemcpyAsync(&nfail, fail_count, sizeof(int), cudaMemcpyDeviceToHost, st));
   QV_CUDA(cudaStreamSynchronize(st));
-  timer.finish();
   thread_stats().rescanned_queries += static_cast<uint64_t>(nfail);
 }
 

@@ -1,0 +1,678 @@
+// Tensor-core (tcgen05) screen for exact Flat search on sm_100a.
+//
+// The screen computes every query-row inner product with one fp16 MMA pass: queries and rows are
+// converted to float16 (times a power-of-two scale, which is exact, only when their magnitudes
+// need it), multiplied on the 5th-generation tensor cores with float32 accumulation in TMEM, and
+// each query keeps its KK best screen candidates. The exact re-rank and the certificate in
+// flat.cu then make the final result identical to the reference's: the float16 rounding errors
+// enter a rigorous per-query bound (measured ||q - q16|| and max ||x - x16||, plus accumulation
+// and reference rounding), and any query whose candidate set cannot be proven complete is
+// rescanned exactly.
+//
+// Kernel structure (one CTA per SM, persistent over work units = (query tile of 128, row chunk)):
+//   warp 0      TMA producer: the unit's query tile (A, resident) and a 4-stage ring of 128-row
+//               tiles of the database (B), 128-byte swizzled, no multicast.
+//   warp 1      MMA issuer: allocates TMEM, issues tcgen05.mma kind::f16 (M=128, N=128, K=16 steps)
+//               into one of two TMEM accumulators, commits to mbarriers.
+//   warps 2..5  epilogue: thread i of the 128 owns query i (= TMEM lane i), reads its 128 inner
+//               products with tcgen05.ld, and pushes survivors of its running threshold into a
+//               private bounded max-heap in shared memory.
+// Every mbarrier wait is bounded (2 s of GPU time); on timeout the CTA raises an error flag,
+// drains its outstanding copies (again bounded), frees TMEM and exits.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "qv_state.h"
+
+namespace qv {
+namespace tc {
+
+constexpr int kM = 128;          // queries per unit = TMEM lanes
+constexpr int kN = 128;          // database rows per MMA tile
+constexpr int kAtomK = 64;       // fp16 elements per 128-byte swizzled row
+constexpr int kAtomBytes = 128 * 128;  // one 128-row x 128-byte swizzle atom column
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr int kKK = 64;          // candidates per query per unit
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr uint32_t kIdesc = (1u << 4)            // D format f32
+                            | (0u << 7)          // A f16
+                            | (0u << 10)         // B f16
+                            | ((kN >> 3) << 17)  // N
+                            | ((kM >> 4) << 24); // M
+
+struct Args {
+  int nq, n_qtiles, n_chunks, total_units, ksteps;
+  int64_t nrows, chunk_rows;
+  bool l2;
+  const float* qscale_inv;  // per query: 1 / (s_q * s_x)
+  const float* qnorm2;      // per query ||q||^2 (L2)
+  const float* xnorm2;      // per row ||x||^2 (L2)
+  const uint64_t* bitmap;
+  float* cand_d;
+  uint32_t* cand_r;
+  int* cand_n;
+  unsigned* thr_bits;
+  int* err;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of `parity` to complete. False on timeout or abort.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err) {
+  if (mbar_test(bar, parity)) return true;
+  const uint64_t t0 = gtimer();
+  for (;;) {
+    if (mbar_test(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (gtimer() - t0 > kTimeoutNs) {
+      *abort_flag = 1;
+      atomicExch(err, 1);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+// K-major, 128-byte swizzle (8-row groups 1024 bytes apart), sm_100 descriptor version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return (static_cast<uint64_t>(addr >> 4) & 0x3FFFull) | (1ull << 16) | (64ull << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Bounded max-heap of (distance, row) in shared memory, element i at i*stride (stride 128).
+__device__ __forceinline__ void heap_push(float* d, uint32_t* r, int& n, float dist, uint32_t row) {
+  constexpr int s = kM;
+  if (n < kKK) {
+    int i = n++;
+    while (i > 0) {
+      const int p = (i - 1) >> 1;
+      const float pd = d[p * s];
+      const uint32_t pr = r[p * s];
+      if (!dev::key_less(pd, pr, dist, row)) break;
+      d[i * s] = pd;
+      r[i * s] = pr;
+      i = p;
+    }
+    d[i * s] = dist;
+    r[i * s] = row;
+    return;
+  }
+  if (!dev::key_less(dist, row, d[0], r[0])) return;
+  int i = 0;
+  for (;;) {
+    const int l = 2 * i + 1;
+    if (l >= n) break;
+    int w = l;
+    float wd = d[l * s];
+    uint32_t wr = r[l * s];
+    if (l + 1 < n) {
+      const float rd = d[(l + 1) * s];
+      const uint32_t rr = r[(l + 1) * s];
+      if (dev::key_less(wd, wr, rd, rr)) {
+        w = l + 1;
+        wd = rd;
+        wr = rr;
+      }
+    }
+    if (!dev::key_less(dist, row, wd, wr)) break;
+    d[i * s] = wd;
+    r[i * s] = wr;
+    i = w;
+  }
+  d[i * s] = dist;
+  r[i * s] = row;
+}
+
+template <int kAtoms>
+__global__ void __launch_bounds__(kThreads, 1)
+    flat_screen_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                          const __grid_constant__ CUtensorMap tmap_x, const Args a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  // 1024-byte alignment for the swizzle atoms.
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  unsigned char* smem_a = base;                                  // kAtoms x 16 KB
+  unsigned char* smem_b = smem_a + kAtoms * kAtomBytes;          // kStages x kAtoms x 16 KB
+  float* heap_d = reinterpret_cast<float*>(smem_b + kStages * kAtoms * kAtomBytes);
+  uint32_t* heap_r = reinterpret_cast<uint32_t*>(heap_d + kKK * kM);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(heap_r + kKK * kM);
+  // bars: full[kStages], empty[kStages], acc_full[2], acc_empty[2], a_full, a_empty
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  __shared__ int s_consumed;  // B fills the MMA warp has waited for (for the abort drain)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+  const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, ACC_EMPTY = 2 * kStages + 2,
+            A_FULL = 2 * kStages + 4, A_EMPTY = 2 * kStages + 5;
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    s_consumed = 0;
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(FULL + s), 1);
+      mbar_init(bar(EMPTY + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(ACC_FULL + b), 1);
+      mbar_init(bar(ACC_EMPTY + b), 4);  // one arrival per epilogue warp
+    }
+    mbar_init(bar(A_FULL), 1);
+    mbar_init(bar(A_EMPTY), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s_tmem)),
+                 "r"(2 * kN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s_tmem;
+  volatile int* abort_flag = &s_abort;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0, a_phase = 0;
+      int issued = 0;
+      bool first = true;
+      for (int u = blockIdx.x; u < a.total_units && !*abort_flag; u += gridDim.x) {
+        const int qtile = u % a.n_qtiles, chunk = u / a.n_qtiles;
+        const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
+        const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
+        const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
+        if (!first) {
+          if (!mbar_wait(bar(A_EMPTY), a_phase, abort_flag, a.err)) break;
+          a_phase ^= 1;
+        }
+        first = false;
+        mbar_expect_tx(bar(A_FULL), kAtoms * kAtomBytes);
+        for (int at = 0; at < kAtoms; ++at)
+          tma_load_2d(smem_u32(smem_a + at * kAtomBytes), &tmap_q, at * kAtomK, qtile * kM,
+                      bar(A_FULL));
+        for (int t = 0; t < ntiles; ++t) {
+          if (!mbar_wait(bar(EMPTY + stage), phase ^ 1, abort_flag, a.err)) break;
+          mbar_expect_tx(bar(FULL + stage), kAtoms * kAtomBytes);
+          unsigned char* dst = smem_b + stage * kAtoms * kAtomBytes;
+          for (int at = 0; at < kAtoms; ++at)
+            tma_load_2d(smem_u32(dst + at * kAtomBytes), &tmap_x, at * kAtomK,
+                        static_cast<int>(r0 + static_cast<int64_t>(t) * kN), bar(FULL + stage));
+          ++issued;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // Drain: wait (bounded) for every B fill the MMA warp did not consume.
+        const uint64_t t0 = gtimer();
+        for (int f = s_consumed; f < issued; ++f) {
+          const int s = f % kStages;
+          const uint32_t par = (f / kStages) & 1;
+          while (!mbar_test(bar(FULL + s), par) && gtimer() - t0 < kTimeoutNs) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0, accb = 0;
+      uint32_t phase = 0, acc_phase = 0, a_phase = 0;
+      int consumed = 0;
+      for (int u = blockIdx.x; u < a.total_units && !*abort_flag; u += gridDim.x) {
+        const int chunk = u / a.n_qtiles;
+        const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
+        const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
+        const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
+        if (!mbar_wait(bar(A_FULL), a_phase, abort_flag, a.err)) break;
+        a_phase ^= 1;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem_a);
+        bool ok = true;
+        for (int t = 0; t < ntiles && ok; ++t) {
+          ok = mbar_wait(bar(ACC_EMPTY + accb), acc_phase ^ 1, abort_flag, a.err);
+          if (!ok) break;
+          tc_fence_after();
+          ok = mbar_wait(bar(FULL + stage), phase, abort_flag, a.err);
+          if (!ok) break;
+          s_consumed = ++consumed;
+          tc_fence_after();
+          const uint32_t b_addr = smem_u32(smem_b + stage * kAtoms * kAtomBytes);
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(accb * kN);
+          for (int ks = 0; ks < a.ksteps; ++ks) {
+            const int at = ks >> 2, kin = ks & 3;
+            const uint32_t off = static_cast<uint32_t>(at * kAtomBytes + kin * 32);
+            umma_f16(d_tmem, smem_desc(a_addr + off), smem_desc(b_addr + off), ks > 0 ? 1u : 0u);
+          }
+          umma_commit(bar(EMPTY + stage));
+          umma_commit(bar(ACC_FULL + accb));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1;
+          }
+          if (++accb == 2) {
+            accb = 0;
+            acc_phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(bar(A_EMPTY));
+      }
+    }
+  } else {
+    // ---------------- epilogue: thread = query ----------------
+    const int quarter = warp & 3;
+    const int qi = quarter * 32 + lane;
+    float* hd = heap_d + qi;
+    uint32_t* hr = heap_r + qi;
+    int accb = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < a.total_units; u += gridDim.x) {
+      const int qtile = u % a.n_qtiles, chunk = u / a.n_qtiles;
+      const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
+      const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
+      const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
+      const int q = qtile * kM + qi;
+      const bool active = q < a.nq;
+      float thr = active ? dev::from_ordered_bits(a.thr_bits[q]) : -__int_as_float(0x7f800000);
+      const float inv = active ? a.qscale_inv[q] : 0.0f;
+      const float qn = (active && a.l2) ? a.qnorm2[q] : 0.0f;
+      int hn = 0;
+      bool ok = true;
+      for (int t = 0; t < ntiles; ++t) {
+        ok = mbar_wait(bar(ACC_FULL + accb), acc_phase, abort_flag, a.err);
+        if (!ok) break;
+        tc_fence_after();
+        const int64_t row0 = r0 + static_cast<int64_t>(t) * kN;
+        for (int c = 0; c < kN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                        static_cast<uint32_t>(accb * kN + c * 32),
+                    v);
+          if (!active) continue;
+          const int64_t cb = row0 + c * 32;
+          if (!a.l2) {
+            float mx = v[0];
+#pragma unroll
+            for (int j = 1; j < 32; ++j) mx = fmaxf(mx, v[j]);
+            if (1.0f - mx * inv > thr) continue;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float dist = 1.0f - v[j] * inv;
+              const int64_t row = cb + j;
+              if (dist <= thr && row < r1 && dev::bitmap_test(a.bitmap, static_cast<uint64_t>(row))) {
+                heap_push(hd, hr, hn, dist, static_cast<uint32_t>(row));
+                if (hn == kKK) thr = fminf(thr, hd[0]);
+              }
+            }
+          } else {
+            float w[32];
+            float mn = __int_as_float(0x7f800000);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int64_t row = cb + j;
+              const float xn = row < r1 ? a.xnorm2[row] : 0.0f;
+              w[j] = fmaf(-2.0f * inv, v[j], qn + xn);
+              mn = fminf(mn, w[j]);
+            }
+            if (mn > thr) continue;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int64_t row = cb + j;
+              if (w[j] <= thr && row < r1 && dev::bitmap_test(a.bitmap, static_cast<uint64_t>(row))) {
+                heap_push(hd, hr, hn, w[j], static_cast<uint32_t>(row));
+                if (hn == kKK) thr = fminf(thr, hd[0]);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(ACC_EMPTY + accb));
+        if (++accb == 2) {
+          accb = 0;
+          acc_phase ^= 1;
+        }
+      }
+      if (!ok) break;
+      if (active) {
+        const size_t slot = static_cast<size_t>(q) * a.n_chunks + chunk;
+        for (int i = 0; i < hn; ++i) {
+          a.cand_d[slot * kKK + i] = hd[i * kM];
+          a.cand_r[slot * kKK + i] = hr[i * kM];
+        }
+        a.cand_n[slot] = hn;
+        if (hn == kKK) atomicMin(a.thr_bits + q, dev::ordered_bits(hd[0]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(2 * kN));
+  }
+}
+
+// ---- fp16 operands ---------------------------------------------------------------------------------
+
+__device__ __forceinline__ float pow2_scale_for(float maxabs) {
+  // Keep data in fp16's comfortable range: scale by 2^E only when the largest magnitude is
+  // outside [2^-8, 2^14]; the scale is a power of two, so scaling itself is exact.
+  if (!(maxabs > 0.0f)) return 1.0f;
+  int e;
+  frexpf(maxabs, &e);  // maxabs in [2^(e-1), 2^e)
+  if (e >= -7 && e <= 14) return 1.0f;
+  return ldexpf(1.0f, 13 - e);
+}
+
+// Rows -> fp16 (kpad columns, zero padded) with one scale for the whole index; max row error.
+__global__ void rows_to_f16_kernel(const float* __restrict__ x, size_t n, int dim, int kpad,
+                                   float scale, __half* __restrict__ out,
+                                   unsigned* __restrict__ max_err_bits) {
+  const int lane = threadIdx.x & 31;
+  const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= n) return;
+  const float inv = 1.0f / scale;
+  double e2 = 0.0;
+  for (int c = lane; c < kpad; c += 32) {
+    const float v = c < dim ? x[row * dim + c] : 0.0f;
+    const __half h = __float2half_rn(v * scale);
+    out[row * kpad + c] = h;
+    const double diff = static_cast<double>(v) - static_cast<double>(__half2float(h)) * inv;
+    e2 += diff * diff;
+  }
+  for (int o = 16; o > 0; o >>= 1) e2 += __shfl_xor_sync(0xffffffffu, e2, o);
+  if (lane == 0) atomicMax(max_err_bits, __float_as_uint(static_cast<float>(sqrt(e2)) * 1.001f + 1e-30f));
+}
+
+__global__ void max_abs_kernel(const float* __restrict__ x, size_t total, unsigned* out_bits) {
+  float m = 0.0f;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    m = fmaxf(m, fabsf(x[i]));
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(out_bits, __float_as_uint(m));
+}
+
+// Queries (already normalized rows of qp, stride dpad) -> fp16 with a per-query power-of-two
+// scale; 1/(s_q s_x); and the screen's error bound eps[q] against the reference's distance.
+__global__ void queries_to_f16_kernel(const float* __restrict__ qp, int nq, int dim, int dpad,
+                                      int kpad, float x_scale, float x_err, float x_max_norm,
+                                      bool l2, float gamma, __half* __restrict__ q16,
+                                      float* __restrict__ qscale_inv, float* __restrict__ qnorm2,
+                                      float* __restrict__ eps) {
+  const int lane = threadIdx.x & 31;
+  const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (q >= nq) return;
+  const float* v = qp + static_cast<size_t>(q) * dpad;
+  float mx = 0.0f;
+  for (int c = lane; c < dim; c += 32) mx = fmaxf(mx, fabsf(v[c]));
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  const float s = pow2_scale_for(mx);
+  const float inv_s = 1.0f / s;
+  double e2 = 0.0, n2 = 0.0;
+  for (int c = lane; c < kpad; c += 32) {
+    const float x = c < dim ? v[c] : 0.0f;
+    const __half h = __float2half_rn(x * s);
+    q16[static_cast<size_t>(q) * kpad + c] = h;
+    const double diff = static_cast<double>(x) - static_cast<double>(__half2float(h)) * inv_s;
+    e2 += diff * diff;
+    n2 += static_cast<double>(x) * x;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    e2 += __shfl_xor_sync(0xffffffffu, e2, o);
+    n2 += __shfl_xor_sync(0xffffffffu, n2, o);
+  }
+  if (lane == 0) {
+    const double eq = sqrt(e2) * 1.001, qn = sqrt(n2) * 1.001;
+    const double xm = static_cast<double>(x_max_norm), ex = static_cast<double>(x_err);
+    const double u = 5.9604644775390625e-08;  // 2^-24
+    // |<q,x> - <q16,x16>| <= eq*||x|| + ||q16||*ex, plus float32 accumulation in the tensor core
+    // and the reference's own float32 summation (gamma each, relative to sum |q_i x_i|).
+    const double dot_err = eq * xm + (qn + eq) * ex + 2.0 * gamma * (qn + eq) * (xm + ex);
+    double e;
+    if (l2) {
+      const double s2 = (qn + xm) * (qn + xm);
+      e = 2.0 * dot_err + 3.0 * gamma * s2 + 4.0 * u * s2;
+    } else {
+      e = dot_err + 4.0 * u * (1.0 + qn * xm);
+    }
+    eps[q] = static_cast<float>(e * 1.01 + 1e-30);
+    qscale_inv[q] = 1.0f / (s * x_scale);
+    qnorm2[q] = static_cast<float>(n2);
+  }
+}
+
+// ---- tensor maps ---------------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (fn == nullptr) fail(QV_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  return fn;
+}
+
+// 2-D fp16 tensor [rows][kpad], boxes of 64 columns x 128 rows, 128-byte swizzle, zero fill.
+CUtensorMap make_map(const void* base, uint64_t rows, uint64_t kpad) {
+  CUtensorMap m;
+  std::memset(&m, 0, sizeof(m));
+  const cuuint64_t dims[2] = {kpad, rows};
+  const cuuint64_t strides[1] = {kpad * sizeof(__half)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kAtomK), static_cast<cuuint32_t>(kM)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
+                                 dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                 CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(QV_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string(r));
+  return m;
+}
+
+}  // namespace tc
+
+// ---- host side ------------------------------------------------------------------------------------
+
+bool flat_tc_eligible(const FlatState& s, size_t k) {
+  const char* e = std::getenv("QV_FLAT_SCREEN");
+  if (e != nullptr && std::strcmp(e, "simt") == 0) return false;
+  return s.dim <= 128 && k + 16 <= static_cast<size_t>(tc::kKK) && s.n >= static_cast<size_t>(tc::kN);
+}
+
+int flat_tc_kk() { return tc::kKK; }
+
+// Builds (once per set of rows) the fp16 copy of the index and its error statistics.
+void flat_tc_prepare(FlatState& s, cudaStream_t st) {
+  if (s.x16.bytes() != 0 && s.x16_rows == s.n) return;
+  // At least one full 64-column swizzle atom, so a TMA box never extends past a row.
+  const int kpad = static_cast<int>(std::max<size_t>(64, ceil_div(s.dim, 16) * 16));
+  DeviceBuffer bits(2 * sizeof(unsigned), st);
+  QV_CUDA(cudaMemsetAsync(bits.get(), 0, 2 * sizeof(unsigned), st));
+  tc::max_abs_kernel<<<std::min<size_t>(ceil_div(s.n * s.dim, 256), 4096), 256, 0, st>>>(
+      s.x.get<float>(), s.n * s.dim, bits.get<unsigned>());
+  check_launch("max_abs_kernel");
+  unsigned mb = 0;
+  QV_CUDA(cudaMemcpyAsync(&mb, bits.get(), sizeof(mb), cudaMemcpyDeviceToHost, st));
+  QV_CUDA(cudaStreamSynchronize(st));
+  float maxabs;
+  std::memcpy(&maxabs, &mb, sizeof(maxabs));
+  float scale = 1.0f;
+  if (maxabs > 0.0f) {
+    int e;
+    std::frexp(maxabs, &e);
+    if (e < -7 || e > 14) scale = std::ldexp(1.0f, 13 - e);
+  }
+  s.x16.allocate(s.n * kpad * sizeof(__half));
+  tc::rows_to_f16_kernel<<<ceil_div(s.n, 8), 256, 0, st>>>(s.x.get<float>(), s.n,
+                                                          static_cast<int>(s.dim), kpad, scale,
+                                                          s.x16.get<__half>(),
+                                                          bits.get<unsigned>() + 1);
+  check_launch("rows_to_f16_kernel");
+  unsigned eb = 0;
+  QV_CUDA(cudaMemcpyAsync(&eb, bits.get<unsigned>() + 1, sizeof(eb), cudaMemcpyDeviceToHost, st));
+  QV_CUDA(cudaStreamSynchronize(st));
+  std::memcpy(&s.x16_err, &eb, sizeof(float));
+  s.x16_scale = scale;
+  s.kpad = static_cast<size_t>(kpad);
+  s.x16_rows = s.n;
+}
+
+// Runs the tensor-core screen for the queries in qp (normalized, dpad stride). Writes the per-query
+// candidates in the layout flat_finalize_kernel reads, and eps[q].
+void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
+                    const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, float* cand_d,
+                    uint32_t* cand_r, int* cand_n, unsigned* thr_bits, float* eps, int* err,
+                    cudaStream_t st) {
+  const int kpad = static_cast<int>(s.kpad);
+  const bool l2 = s.metric == QV_METRIC_L2;
+  // Whole 128-row query tiles (zero rows past nq), so no TMA box extends past the tensor.
+  const size_t nq_pad = ceil_div(nq, tc::kM) * tc::kM;
+  DeviceBuffer q16(nq_pad * kpad * sizeof(__half), st), qinv(nq * sizeof(float), st),
+      qn2(nq * sizeof(float), st);
+  QV_CUDA(cudaMemsetAsync(q16.get(), 0, nq_pad * kpad * sizeof(__half), st));
+  const double gamma = (kpad + 2) * std::ldexp(1.0, -23);
+  tc::queries_to_f16_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(
+      qp, static_cast<int>(nq), static_cast<int>(s.dim), dpad, kpad, s.x16_scale, s.x16_err,
+      s.max_norm, l2, static_cast<float>(gamma), q16.get<__half>(), qinv.get<float>(),
+      qn2.get<float>(), eps);
+  check_launch("queries_to_f16_kernel");
+  const CUtensorMap mq = tc::make_map(q16.get(), nq_pad, kpad);
+  const CUtensorMap mx = tc::make_map(s.x16.get(), s.n, kpad);
+  tc::Args a{};
+  a.nq = static_cast<int>(nq);
+  a.n_qtiles = static_cast<int>(ceil_div(nq, tc::kM));
+  a.n_chunks = n_chunks;
+  a.total_units = a.n_qtiles * n_chunks;
+  a.ksteps = kpad / 16;
+  a.nrows = static_cast<int64_t>(s.n);
+  a.chunk_rows = chunk_rows;
+  a.l2 = l2;
+  a.qscale_inv = qinv.get<float>();
+  a.qnorm2 = qn2.get<float>();
+  a.xnorm2 = s.xnorm2.get<float>();
+  a.bitmap = d_bitmap;
+  a.cand_d = cand_d;
+  a.cand_r = cand_r;
+  a.cand_n = cand_n;
+  a.thr_bits = thr_bits;
+  a.err = err;
+  const int atoms = kpad > tc::kAtomK ? 2 : 1;
+  const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (1 + tc::kStages) +
+                      static_cast<size_t>(tc::kKK) * tc::kM * 8 + (2 * tc::kStages + 6) * 8;
+  const int grid = std::min(a.total_units, sm_count(s.device));
+  KernelTimer timer(st, "flat_screen_tc_kernel", 2.0 * nq * static_cast<double>(s.n) * s.dim,
+                    false);
+  if (atoms == 2) {
+    QV_CUDA(cudaFuncSetAttribute(tc::flat_screen_tc_kernel<2>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    tc::flat_screen_tc_kernel<2><<<grid, tc::kThreads, smem, st>>>(mq, mx, a);
+  } else {
+    QV_CUDA(cudaFuncSetAttribute(tc::flat_screen_tc_kernel<1>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    tc::flat_screen_tc_kernel<1><<<grid, tc::kThreads, smem, st>>>(mq, mx, a);
+  }
+  timer.stop();
+  check_launch("flat_screen_tc_kernel");
+  int e = 0;
+  QV_CUDA(cudaMemcpyAsync(&e, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  QV_CUDA(cudaStreamSynchronize(st));
+  timer.finish();
+  if (e != 0) fail(QV_ERR_DEVICE, "tensor-core screen timed out waiting on a pipeline barrier");
+}
+
+}  // namespace qv

@@ -25,11 +25,23 @@ struct FlatState {
   DeviceBuffer x;         // cap x dim f32
   DeviceBuffer xnorm2;    // cap f32, sum of squares (screen only)
   DeviceBuffer labels;    // cap u64
-  DeviceBuffer xbf16;     // cap x kpad bf16 (tensor screen), kpad = dim rounded up to 64
-  size_t kpad = 0;
   float max_norm = 0.0f;  // max ||x|| over stored rows (screen error bound)
   std::vector<uint64_t> host_labels;
+  // fp16 copy for the tensor-core screen (n x kpad, kpad = dim rounded up to 16), built on the
+  // first search after rows change; x16_err = max ||x - x16/scale|| over rows.
+  DeviceBuffer x16;
+  size_t kpad = 0, x16_rows = 0;
+  float x16_scale = 1.0f, x16_err = 0.0f;
+  std::mutex x16_mu;
 };
+
+bool flat_tc_eligible(const FlatState& s, size_t k);
+int flat_tc_kk();
+void flat_tc_prepare(FlatState& s, cudaStream_t st);
+void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
+                    const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, float* cand_d,
+                    uint32_t* cand_r, int* cand_n, unsigned* thr_bits, float* eps, int* err,
+                    cudaStream_t st);
 
 void flat_reserve(FlatState& s, size_t rows, cudaStream_t st);
 // Appends n rows (device pointer, row-major) with labels (device pointer).

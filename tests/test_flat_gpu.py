@@ -145,3 +145,27 @@ def test_config0_full_size_against_reference(gpu, reference):
     rf.add(base)
     rl, rd = rf.search(q, 10)
     assert_topk_parity(l, d, rl, rd, exact=True, what="config0")
+
+
+@pytest.mark.parametrize("metric", ["l2", "ip", "cosine"])
+def test_tensor_core_screen_equals_simt_screen(gpu, oracle, monkeypatch, metric):
+    """The tcgen05 fp16 screen and the float32 SIMT screen must produce identical final results
+    (both are re-ranked exactly and certified)."""
+    from quiver_b200.synthetic import mixture
+    base = mixture(20000, 100, 50, 0.35, 1.0, centre_seed=3, seed=4)
+    if metric != "cosine":
+        base = base * np.float32(3.0)
+    q = mixture(300, 100, 50, 0.35, 1.0, centre_seed=3, seed=5)
+    ix = gpu.FlatIndex(100, metric)
+    ix.add(base)
+    gpu._native.set_timing(True)
+    l1, d1 = ix.search(q, 10)
+    st = gpu.last_search_stats()
+    gpu._native.set_timing(False)
+    assert st["dominant_kernel"] == "flat_screen_tc_kernel"
+    monkeypatch.setenv("QV_FLAT_SCREEN", "simt")
+    l2_, d2 = ix.search(q, 10)
+    assert np.array_equal(d1, d2) and np.array_equal(l1, l2_)
+    stored = oracle.normalize_rows(base) if metric == "cosine" else base
+    wl, wd = oracle.flat_search(stored, np.arange(20000, dtype=np.uint64), metric, q, 10)
+    assert_topk_parity(l1, d1, wl, wd, exact=True, what=f"tc {metric}")
