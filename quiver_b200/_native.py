@@ -12,7 +12,8 @@ import threading
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libquiver_b200.so")
+# QUIVER_B200_LIB selects another build of the library (e.g. an instrumented one).
+LIB_PATH = os.environ.get("QUIVER_B200_LIB") or os.path.join(HERE, "libquiver_b200.so")
 
 QV_OK, QV_ERR_INVALID, QV_ERR_CUDA, QV_ERR_OOM, QV_ERR_IO, QV_ERR_STATE, QV_ERR_UNSUPPORTED, \
     QV_ERR_DEVICE = range(8)

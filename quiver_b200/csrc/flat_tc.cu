@@ -15,8 +15,8 @@
 //   warp 1      MMA issuer: allocates TMEM, issues tcgen05.mma kind::f16 (M=128, N=128, K=16 steps)
 //               into one of two TMEM accumulators, commits to mbarriers.
 //   warps 2..5  epilogue: thread i of the 128 owns query i (= TMEM lane i), reads its 128 inner
-//               products with tcgen05.ld, and pushes survivors of its running threshold into a
-//               private bounded max-heap in shared memory.
+//               products with tcgen05.ld, and appends survivors of its running threshold to a
+//               private candidate buffer in shared memory (compacted warp-wide when it fills).
 // Every mbarrier wait is bounded (2 s of GPU time); on timeout the CTA raises an error flag,
 // drains its outstanding copies (again bounded), frees TMEM and exits.
 #include <cuda.h>
@@ -38,8 +38,10 @@ constexpr int kAtomK = 64;       // fp16 elements per 128-byte swizzled row
 constexpr int kAtomBytes = 128 * 128;  // one 128-row x 128-byte swizzle atom column
 constexpr int kStages = 4;
 constexpr int kThreads = 192;
-constexpr int kKK = 64;          // candidates per query per unit
-constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr int kKK = 32;          // candidates per query per unit
+constexpr int kCap = 64;         // candidate buffer entries per query
+constexpr uint64_t kTimeoutNs = 2000000000ull;       // drain bound (global timer)
+constexpr long long kTimeoutCycles = 4000000000ll;     // ~2 s at 2 GHz (SM clock)
 constexpr uint32_t kIdesc = (1u << 4)            // D format f32
                             | (0u << 7)          // A f16
                             | (0u << 10)         // B f16
@@ -90,18 +92,22 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase of `parity` to complete. False on timeout or abort.
+// Bounded wait for the phase of `parity` to complete. False on timeout or abort. The bound is
+// counted in SM clock cycles (clock64 is a cheap per-SM counter; the global timer is a slow read)
+// and checked every 64 polls, so a healthy pipeline hand-off costs one or two polls.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int* err) {
   if (mbar_test(bar, parity)) return true;
-  const uint64_t t0 = gtimer();
-  for (;;) {
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_test(bar, parity)) return true;
-    if (*abort_flag) return false;
-    if (gtimer() - t0 > kTimeoutNs) {
-      *abort_flag = 1;
-      atomicExch(err, 1);
-      return false;
+    if ((i & 63) == 0) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > kTimeoutCycles) {
+        *abort_flag = 1;
+        atomicExch(err, 1);
+        return false;
+      }
     }
   }
 }
@@ -154,51 +160,76 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// Bounded max-heap of (distance, row) in shared memory, element i at i*stride (stride 128).
-__device__ __forceinline__ void heap_push(float* d, uint32_t* r, int& n, float dist, uint32_t row) {
-  constexpr int s = kM;
-  if (n < kKK) {
-    int i = n++;
-    while (i > 0) {
-      const int p = (i - 1) >> 1;
-      const float pd = d[p * s];
-      const uint32_t pr = r[p * s];
-      if (!dev::key_less(pd, pr, dist, row)) break;
-      d[i * s] = pd;
-      r[i * s] = pr;
-      i = p;
-    }
-    d[i * s] = dist;
-    r[i * s] = row;
-    return;
-  }
-  if (!dev::key_less(dist, row, d[0], r[0])) return;
-  int i = 0;
-  for (;;) {
-    const int l = 2 * i + 1;
-    if (l >= n) break;
-    int w = l;
-    float wd = d[l * s];
-    uint32_t wr = r[l * s];
-    if (l + 1 < n) {
-      const float rd = d[(l + 1) * s];
-      const uint32_t rr = r[(l + 1) * s];
-      if (dev::key_less(wd, wr, rd, rr)) {
-        w = l + 1;
-        wd = rd;
-        wr = rr;
-      }
-    }
-    if (!dev::key_less(dist, row, wd, wr)) break;
-    d[i * s] = wd;
-    r[i * s] = wr;
-    i = w;
-  }
-  d[i * s] = dist;
-  r[i * s] = row;
+// Minimum of 32 values as a 5-level tree (short dependency chains).
+__device__ __forceinline__ float tree_min32(const float (&v)[32]) {
+  float m[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m[i] = fminf(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+  for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) m[i] = fminf(m[i], m[i + w]);
+  return m[0];
 }
 
-template <int kAtoms>
+// Bit j set when v[j] <= thr and row cb + j is admitted by the position bitmap (OR tree).
+__device__ __forceinline__ uint32_t survivors32(const float (&v)[32], float thr,
+                                                const uint64_t* bitmap, int64_t cb) {
+  uint32_t b[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    b[i] = (v[2 * i] <= thr ? (1u << (2 * i)) : 0u) | (v[2 * i + 1] <= thr ? (2u << (2 * i)) : 0u);
+#pragma unroll
+  for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) b[i] |= b[i + w];
+  uint32_t m = b[0];
+  if (bitmap != nullptr && m != 0) {
+    // The 32 rows span at most two 64-bit words of the bitmap.
+    const uint64_t w0 = bitmap[static_cast<uint64_t>(cb) >> 6];
+    const uint64_t last = static_cast<uint64_t>(cb + 31) >> 6;
+    const uint64_t w1 = last != (static_cast<uint64_t>(cb) >> 6) ? bitmap[last] : 0ull;
+    const int sh = static_cast<int>(cb & 63);
+    const uint64_t bits = (w0 >> sh) | (sh ? (w1 << (64 - sh)) : 0ull);
+    m &= static_cast<uint32_t>(bits);
+  }
+  return m;
+}
+
+// Sorts one query's buffer (its first `cnt` entries; the rest padded with +inf) by
+// (distance, row), keeps the best kKK and tightens the threshold to the kKK-th distance when the
+// buffer holds that many. Entry i lives at i*kM. Called by all 32 lanes of a warp together (each
+// lane sorts its own column), so the network below runs without divergence.
+__device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, float& thr) {
+  for (int i = cnt; i < kCap; ++i) {
+    d[i * kM] = __int_as_float(0x7f800000);
+    r[i * kM] = 0xffffffffu;
+  }
+  for (int size = 2; size <= kCap; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = 0; i < kCap / 2; ++i) {
+        const int lo = 2 * i - (i & (stride - 1));
+        const int hi = lo + stride;
+        const bool up = (lo & size) == 0;
+        const float dl = d[lo * kM], dh = d[hi * kM];
+        const uint32_t rl = r[lo * kM], rh = r[hi * kM];
+        const bool swap = up ? dev::key_less(dh, rh, dl, rl) : dev::key_less(dl, rl, dh, rh);
+        if (swap) {
+          d[lo * kM] = dh;
+          d[hi * kM] = dl;
+          r[lo * kM] = rh;
+          r[hi * kM] = rl;
+        }
+      }
+    }
+  }
+  if (cnt >= kKK) {
+    cnt = kKK;
+    thr = fminf(thr, d[(kKK - 1) * kM]);
+  }
+}
+
+template <int kAtoms, bool kL2>
 __global__ void __launch_bounds__(kThreads, 1)
     flat_screen_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                           const __grid_constant__ CUtensorMap tmap_x, const Args a) {
@@ -208,9 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   unsigned char* smem_a = base;                                  // kAtoms x 16 KB
   unsigned char* smem_b = smem_a + kAtoms * kAtomBytes;          // kStages x kAtoms x 16 KB
-  float* heap_d = reinterpret_cast<float*>(smem_b + kStages * kAtoms * kAtomBytes);
-  uint32_t* heap_r = reinterpret_cast<uint32_t*>(heap_d + kKK * kM);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(heap_r + kKK * kM);
+  float* buf_d = reinterpret_cast<float*>(smem_b + kStages * kAtoms * kAtomBytes);
+  uint32_t* buf_r = reinterpret_cast<uint32_t*>(buf_d + kCap * kM);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(buf_r + kCap * kM);
   // bars: full[kStages], empty[kStages], acc_full[2], acc_empty[2], a_full, a_empty
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
@@ -342,10 +373,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue: thread = query ----------------
+    // Each query keeps an unsorted candidate buffer of kCap (distance, row) entries in shared
+    // memory. Per 32-column chunk: screen distances in registers; a warp-uniform skip when no lane
+    // can improve on its threshold; else survivors are appended with predicated stores (no
+    // divergent branches). When any lane's buffer could overflow on the next chunk, the warp
+    // compacts together: every lane sorts its buffer and keeps the best kKK, which also tightens
+    // its threshold to the kKK-th distance.
     const int quarter = warp & 3;
     const int qi = quarter * 32 + lane;
-    float* hd = heap_d + qi;
-    uint32_t* hr = heap_r + qi;
+    float* bd = buf_d + qi;
+    uint32_t* br = buf_r + qi;
+    const float kInfF = __int_as_float(0x7f800000);
     int accb = 0;
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < a.total_units; u += gridDim.x) {
@@ -355,10 +393,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
       const int q = qtile * kM + qi;
       const bool active = q < a.nq;
-      float thr = active ? dev::from_ordered_bits(a.thr_bits[q]) : -__int_as_float(0x7f800000);
+      float thr = active ? dev::from_ordered_bits(a.thr_bits[q]) : -kInfF;
       const float inv = active ? a.qscale_inv[q] : 0.0f;
-      const float qn = (active && a.l2) ? a.qnorm2[q] : 0.0f;
-      int hn = 0;
+      const float qn = (active && kL2) ? a.qnorm2[q] : 0.0f;
+      int cnt = 0;
       bool ok = true;
       for (int t = 0; t < ntiles; ++t) {
         ok = mbar_wait(bar(ACC_FULL + accb), acc_phase, abort_flag, a.err);
@@ -370,41 +408,43 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                         static_cast<uint32_t>(accb * kN + c * 32),
                     v);
-          if (!active) continue;
           const int64_t cb = row0 + c * 32;
-          if (!a.l2) {
-            float mx = v[0];
-#pragma unroll
-            for (int j = 1; j < 32; ++j) mx = fmaxf(mx, v[j]);
-            if (1.0f - mx * inv > thr) continue;
+          const int valid = static_cast<int>(r1 - cb < 32 ? r1 - cb : 32);  // rows of this chunk
+          // v[j] := screen distance; columns past the chunk end become +inf.
+          if (kL2) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const float dist = 1.0f - v[j] * inv;
-              const int64_t row = cb + j;
-              if (dist <= thr && row < r1 && dev::bitmap_test(a.bitmap, static_cast<uint64_t>(row))) {
-                heap_push(hd, hr, hn, dist, static_cast<uint32_t>(row));
-                if (hn == kKK) thr = fminf(thr, hd[0]);
-              }
+              const float xn = j < valid ? a.xnorm2[cb + j] : 0.0f;
+              v[j] = fmaf(-2.0f * inv, v[j], qn + xn);
             }
           } else {
-            float w[32];
-            float mn = __int_as_float(0x7f800000);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 1.0f - v[j] * inv;
+          }
+          if (valid < 32) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j >= valid) v[j] = kInfF;
+          }
+          const float mn = tree_min32(v);
+          if (!__any_sync(0xffffffffu, active && mn <= thr)) continue;
+          uint32_t mask = 0;
+          if (active && mn <= thr) mask = survivors32(v, thr, a.bitmap, cb);
+          // Compact only when some lane's survivors would not fit.
+          if (__any_sync(0xffffffffu, cnt + __popc(mask) > kCap)) {
+            compact_buffer(bd, br, cnt, thr);
+            mask &= survivors32(v, thr, nullptr, cb);
+          }
+          if (mask != 0) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const int64_t row = cb + j;
-              const float xn = row < r1 ? a.xnorm2[row] : 0.0f;
-              w[j] = fmaf(-2.0f * inv, v[j], qn + xn);
-              mn = fminf(mn, w[j]);
-            }
-            if (mn > thr) continue;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int64_t row = cb + j;
-              if (w[j] <= thr && row < r1 && dev::bitmap_test(a.bitmap, static_cast<uint64_t>(row))) {
-                heap_push(hd, hr, hn, w[j], static_cast<uint32_t>(row));
-                if (hn == kKK) thr = fminf(thr, hd[0]);
+              if ((mask >> j) & 1u) {
+                const int pos = cnt + __popc(mask & ((1u << j) - 1u));
+                bd[pos * kM] = v[j];
+                br[pos * kM] = static_cast<uint32_t>(cb + j);
               }
             }
+            cnt += __popc(mask);
           }
         }
         tc_fence_before();
@@ -414,16 +454,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           accb = 0;
           acc_phase ^= 1;
         }
+        // Pick up tighter thresholds published by units that finished meanwhile.
+        if ((t & 15) == 15 && active)
+          thr = fminf(thr, dev::from_ordered_bits(
+                               *reinterpret_cast<volatile unsigned*>(a.thr_bits + q)));
       }
       if (!ok) break;
+      compact_buffer(bd, br, cnt, thr);
       if (active) {
         const size_t slot = static_cast<size_t>(q) * a.n_chunks + chunk;
-        for (int i = 0; i < hn; ++i) {
-          a.cand_d[slot * kKK + i] = hd[i * kM];
-          a.cand_r[slot * kKK + i] = hr[i * kM];
+        for (int i = 0; i < cnt; ++i) {
+          a.cand_d[slot * kKK + i] = bd[i * kM];
+          a.cand_r[slot * kKK + i] = br[i * kM];
         }
-        a.cand_n[slot] = hn;
-        if (hn == kKK) atomicMin(a.thr_bits + q, dev::ordered_bits(hd[0]));
+        a.cand_n[slot] = cnt;
+        if (cnt == kKK) atomicMin(a.thr_bits + q, dev::ordered_bits(bd[(kKK - 1) * kM]));
       }
     }
   }
@@ -571,7 +616,7 @@ CUtensorMap make_map(const void* base, uint64_t rows, uint64_t kpad) {
 bool flat_tc_eligible(const FlatState& s, size_t k) {
   const char* e = std::getenv("QV_FLAT_SCREEN");
   if (e != nullptr && std::strcmp(e, "simt") == 0) return false;
-  return s.dim <= 128 && k + 16 <= static_cast<size_t>(tc::kKK) && s.n >= static_cast<size_t>(tc::kN);
+  return s.dim <= 128 && k + 8 <= static_cast<size_t>(tc::kKK) && s.n >= static_cast<size_t>(tc::kN);
 }
 
 int flat_tc_kk() { return tc::kKK; }
@@ -653,18 +698,18 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   a.err = err;
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
   const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (1 + tc::kStages) +
-                      static_cast<size_t>(tc::kKK) * tc::kM * 8 + (2 * tc::kStages + 6) * 8;
+                      static_cast<size_t>(tc::kCap) * tc::kM * 8 + (2 * tc::kStages + 6) * 8;
   const int grid = std::min(a.total_units, sm_count(s.device));
   KernelTimer timer(st, "flat_screen_tc_kernel", 2.0 * nq * static_cast<double>(s.n) * s.dim,
                     false);
+  auto launch = [&](auto kernel) {
+    QV_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kernel<<<grid, tc::kThreads, smem, st>>>(mq, mx, a);
+  };
   if (atoms == 2) {
-    QV_CUDA(cudaFuncSetAttribute(tc::flat_screen_tc_kernel<2>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    tc::flat_screen_tc_kernel<2><<<grid, tc::kThreads, smem, st>>>(mq, mx, a);
+    if (l2) launch(tc::flat_screen_tc_kernel<2, true>); else launch(tc::flat_screen_tc_kernel<2, false>);
   } else {
-    QV_CUDA(cudaFuncSetAttribute(tc::flat_screen_tc_kernel<1>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    tc::flat_screen_tc_kernel<1><<<grid, tc::kThreads, smem, st>>>(mq, mx, a);
+    if (l2) launch(tc::flat_screen_tc_kernel<1, true>); else launch(tc::flat_screen_tc_kernel<1, false>);
   }
   timer.stop();
   check_launch("flat_screen_tc_kernel");
