@@ -38,10 +38,12 @@ constexpr int kAtomK = 64;       // fp16 elements per 128-byte swizzled row
 constexpr int kAtomBytes = 128 * 128;  // one 128-row x 128-byte swizzle atom column
 constexpr int kStages = 4;
 constexpr int kThreads = 192;
+constexpr int kAcc = 4;          // TMEM accumulators of kN columns (4 x 128 = all 512 columns)
 constexpr int kKK = 32;          // candidates per query per unit
 constexpr int kCap = 64;         // candidate buffer entries per query
 constexpr uint64_t kTimeoutNs = 2000000000ull;       // drain bound (global timer)
 constexpr long long kTimeoutCycles = 4000000000ll;     // ~2 s at 2 GHz (SM clock)
+constexpr uint32_t kSuspendHintNs = 100000;           // one sleeping try_wait: at most 0.1 ms
 constexpr uint32_t kIdesc = (1u << 4)            // D format f32
                             | (0u << 7)          // A f16
                             | (0u << 10)         // B f16
@@ -60,8 +62,20 @@ struct Args {
   uint32_t* cand_r;
   int* cand_n;
   unsigned* thr_bits;
+  unsigned* slots;  // nq x n_chunks: each unit's published rank-r distance (ordered bits)
   int* err;
+  bool qmajor;      // unit order: query-tile-major (true) or row-chunk-major (false)
 };
+
+__device__ __forceinline__ void unit_coords(const Args& a, int u, int& qtile, int& chunk) {
+  if (a.qmajor) {
+    qtile = u / a.n_chunks;
+    chunk = u - qtile * a.n_chunks;
+  } else {
+    chunk = u / a.n_qtiles;
+    qtile = u - chunk * a.n_qtiles;
+  }
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -92,22 +106,34 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase of `parity` to complete. False on timeout or abort. The bound is
-// counted in SM clock cycles (clock64 is a cheap per-SM counter; the global timer is a slow read)
-// and checked every 64 polls, so a healthy pipeline hand-off costs one or two polls.
+// try_wait with a suspend-time hint: a waiting thread sleeps in hardware until the phase
+// completes (or the hint elapses) instead of spinning, so waiting warps leave the scheduler's
+// issue slots to the warps that share it.
+__device__ __forceinline__ bool mbar_sleep_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of `parity` to complete. False on timeout or abort. Each try sleeps
+// at most kSuspendHintNs; the 2 s bound is counted in SM clock cycles (clock64 is a cheap per-SM
+// counter; the global timer is a slow read).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int* err) {
   if (mbar_test(bar, parity)) return true;
   const long long t0 = clock64();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_test(bar, parity)) return true;
-    if ((i & 63) == 0) {
-      if (*abort_flag) return false;
-      if (clock64() - t0 > kTimeoutCycles) {
-        *abort_flag = 1;
-        atomicExch(err, 1);
-        return false;
-      }
+  for (;;) {
+    if (mbar_sleep_test(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kTimeoutCycles) {
+      *abort_flag = 1;
+      atomicExch(err, 1);
+      return false;
     }
   }
 }
@@ -158,6 +184,57 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  float (&lo)[32] = *reinterpret_cast<float(*)[32]>(v);
+  float (&hi)[32] = *reinterpret_cast<float(*)[32]>(v + 32);
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
+      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]),
+        "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]),
+        "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]),
+        "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]),
+        "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    lo[i] = __uint_as_float(r[i]);
+    hi[i] = __uint_as_float(r[32 + i]);
+  }
+}
+
+__device__ __forceinline__ float tree_min64(const float (&v)[64]) {
+  float m[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) m[i] = fminf(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+  for (int w = 16; w > 0; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) m[i] = fminf(m[i], m[i + w]);
+  return m[0];
+}
+
+__device__ __forceinline__ float tree_max64(const float (&v)[64]) {
+  float m[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) m[i] = fmaxf(v[2 * i], v[2 * i + 1]);
+#pragma unroll
+  for (int w = 16; w > 0; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) m[i] = fmaxf(m[i], m[i + w]);
+  return m[0];
 }
 
 // Minimum of 32 values as a 5-level tree (short dependency chains).
@@ -242,15 +319,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* buf_d = reinterpret_cast<float*>(smem_b + kStages * kAtoms * kAtomBytes);
   uint32_t* buf_r = reinterpret_cast<uint32_t*>(buf_d + kCap * kM);
   uint64_t* bars = reinterpret_cast<uint64_t*>(buf_r + kCap * kM);
-  // bars: full[kStages], empty[kStages], acc_full[2], acc_empty[2], a_full, a_empty
+  // bars: full[kStages], empty[kStages], acc_full[kAcc], acc_empty[kAcc], a_full, a_empty
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ int s_consumed;  // B fills the MMA warp has waited for (for the abort drain)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   auto bar = [&](int i) { return smem_u32(bars + i); };
-  const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, ACC_EMPTY = 2 * kStages + 2,
-            A_FULL = 2 * kStages + 4, A_EMPTY = 2 * kStages + 5;
+  const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, ACC_EMPTY = 2 * kStages + kAcc,
+            A_FULL = 2 * kStages + 2 * kAcc, A_EMPTY = 2 * kStages + 2 * kAcc + 1;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -259,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(FULL + s), 1);
       mbar_init(bar(EMPTY + s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kAcc; ++b) {
       mbar_init(bar(ACC_FULL + b), 1);
       mbar_init(bar(ACC_EMPTY + b), 4);  // one arrival per epilogue warp
     }
@@ -270,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&s_tmem)),
-                 "r"(2 * kN));
+                 "r"(kAcc * kN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -287,7 +364,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       bool first = true;
       for (int u = blockIdx.x; u < a.total_units && !*abort_flag; u += gridDim.x) {
-        const int qtile = u % a.n_qtiles, chunk = u / a.n_qtiles;
+        int qtile, chunk;
+        unit_coords(a, u, qtile, chunk);
         const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
         const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
         const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
@@ -332,7 +410,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0, acc_phase = 0, a_phase = 0;
       int consumed = 0;
       for (int u = blockIdx.x; u < a.total_units && !*abort_flag; u += gridDim.x) {
-        const int chunk = u / a.n_qtiles;
+        int qtile, chunk;
+        unit_coords(a, u, qtile, chunk);
         const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
         const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
         const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
@@ -362,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             stage = 0;
             phase ^= 1;
           }
-          if (++accb == 2) {
+          if (++accb == kAcc) {
             accb = 0;
             acc_phase ^= 1;
           }
@@ -386,8 +465,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float kInfF = __int_as_float(0x7f800000);
     int accb = 0;
     uint32_t acc_phase = 0;
+    // Units of one query tile run concurrently (query-tile-major order). Each publishes, after
+    // every compaction, its r_pub-th best distance into slots[q][chunk]; once every unit of the
+    // query has published, the union of their outputs holds >= n_chunks * r_pub >= kKK
+    // candidates no farther than the largest slot, so that value bounds every unit's threshold.
+    const int r_pub = (kKK + a.n_chunks - 1) / a.n_chunks;
     for (int u = blockIdx.x; u < a.total_units; u += gridDim.x) {
-      const int qtile = u % a.n_qtiles, chunk = u / a.n_qtiles;
+      int qtile, chunk;
+      unit_coords(a, u, qtile, chunk);
       const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
       const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
       const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
@@ -396,6 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float thr = active ? dev::from_ordered_bits(a.thr_bits[q]) : -kInfF;
       const float inv = active ? a.qscale_inv[q] : 0.0f;
       const float qn = (active && kL2) ? a.qnorm2[q] : 0.0f;
+      unsigned* qslots = a.slots + static_cast<size_t>(active ? q : 0) * a.n_chunks;
       int cnt = 0;
       bool ok = true;
       for (int t = 0; t < ntiles; ++t) {
@@ -403,61 +489,77 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         tc_fence_after();
         const int64_t row0 = r0 + static_cast<int64_t>(t) * kN;
-        for (int c = 0; c < kN / 32; ++c) {
-          float v[32];
-          tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                        static_cast<uint32_t>(accb * kN + c * 32),
+        for (int h = 0; h < kN / 64; ++h) {
+          float v[64];
+          tmem_ld64(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                        static_cast<uint32_t>(accb * kN + h * 64),
                     v);
-          const int64_t cb = row0 + c * 32;
-          const int valid = static_cast<int>(r1 - cb < 32 ? r1 - cb : 32);  // rows of this chunk
-          // v[j] := screen distance; columns past the chunk end become +inf.
+          const int64_t cb = row0 + h * 64;
+          const int valid = static_cast<int>(r1 - cb < 64 ? r1 - cb : 64);  // rows of this chunk
+          bool may;
           if (kL2) {
+            // v[j] := ||q||^2 + ||x||^2 - 2<q,x>; columns past the chunk end become +inf.
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
+            for (int j = 0; j < 64; ++j) {
               const float xn = j < valid ? a.xnorm2[cb + j] : 0.0f;
-              v[j] = fmaf(-2.0f * inv, v[j], qn + xn);
+              v[j] = j < valid ? fmaf(-2.0f * inv, v[j], qn + xn) : kInfF;
             }
+            may = active && tree_min64(v) <= thr;
           } else {
+            // Skip test on the raw inner products: the best screen distance is 1 - max * inv.
+            if (valid < 64) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = 1.0f - v[j] * inv;
-          }
-          if (valid < 32) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j >= valid) v[j] = kInfF;
-          }
-          const float mn = tree_min32(v);
-          if (!__any_sync(0xffffffffu, active && mn <= thr)) continue;
-          uint32_t mask = 0;
-          if (active && mn <= thr) mask = survivors32(v, thr, a.bitmap, cb);
-          // Compact only when some lane's survivors would not fit.
-          if (__any_sync(0xffffffffu, cnt + __popc(mask) > kCap)) {
-            compact_buffer(bd, br, cnt, thr);
-            mask &= survivors32(v, thr, nullptr, cb);
-          }
-          if (mask != 0) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if ((mask >> j) & 1u) {
-                const int pos = cnt + __popc(mask & ((1u << j) - 1u));
-                bd[pos * kM] = v[j];
-                br[pos * kM] = static_cast<uint32_t>(cb + j);
-              }
+              for (int j = 0; j < 64; ++j)
+                if (j >= valid) v[j] = -kInfF;
             }
-            cnt += __popc(mask);
+            may = active && 1.0f - tree_max64(v) * inv <= thr;
+          }
+          if (!__any_sync(0xffffffffu, may)) continue;
+          if (!kL2) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] = 1.0f - v[j] * inv;  // screen distances (-inf -> +inf)
+          }
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            float (&w)[32] = *reinterpret_cast<float(*)[32]>(v + 32 * half);
+            const int64_t cbh = cb + 32 * half;
+            uint32_t mask = may ? survivors32(w, thr, a.bitmap, cbh) : 0u;
+            // Compact only when some lane's survivors would not fit.
+            if (__any_sync(0xffffffffu, cnt + __popc(mask) > kCap)) {
+              compact_buffer(bd, br, cnt, thr);
+              mask &= survivors32(w, thr, nullptr, cbh);
+              if (active && cnt >= r_pub)
+                atomicMin(qslots + chunk, dev::ordered_bits(bd[(r_pub - 1) * kM]));
+            }
+            if (mask != 0) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if ((mask >> j) & 1u) {
+                  const int pos = cnt + __popc(mask & ((1u << j) - 1u));
+                  bd[pos * kM] = w[j];
+                  br[pos * kM] = static_cast<uint32_t>(cbh + j);
+                }
+              }
+              cnt += __popc(mask);
+            }
           }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(ACC_EMPTY + accb));
-        if (++accb == 2) {
+        if (++accb == kAcc) {
           accb = 0;
           acc_phase ^= 1;
         }
-        // Pick up tighter thresholds published by units that finished meanwhile.
-        if ((t & 15) == 15 && active)
+        // Tighten with the bound from all units of this query and with finished units' values.
+        if ((t & 7) == 7 && active) {
+          unsigned worst = 0u;
+          for (int c2 = 0; c2 < a.n_chunks; ++c2)
+            worst = max(worst, *reinterpret_cast<volatile unsigned*>(qslots + c2));
+          thr = fminf(thr, dev::from_ordered_bits(worst));
           thr = fminf(thr, dev::from_ordered_bits(
                                *reinterpret_cast<volatile unsigned*>(a.thr_bits + q)));
+        }
       }
       if (!ok) break;
       compact_buffer(bd, br, cnt, thr);
@@ -468,6 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           a.cand_r[slot * kKK + i] = br[i * kM];
         }
         a.cand_n[slot] = cnt;
+        if (cnt >= r_pub) atomicMin(qslots + chunk, dev::ordered_bits(bd[(r_pub - 1) * kM]));
         if (cnt == kKK) atomicMin(a.thr_bits + q, dev::ordered_bits(bd[(kKK - 1) * kM]));
       }
     }
@@ -477,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(2 * kN));
+                 "r"(kAcc * kN));
   }
 }
 
@@ -695,10 +798,17 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   a.cand_r = cand_r;
   a.cand_n = cand_n;
   a.thr_bits = thr_bits;
+  // Unit order: QV_FLAT_TC_ORDER=q selects query-tile-major (all row chunks of a query tile run
+  // together, sharing thresholds); the default row-chunk-major order shares row chunks in L2.
+  const char* order = std::getenv("QV_FLAT_TC_ORDER");
+  a.qmajor = order != nullptr && order[0] == 'q';
+  DeviceBuffer slots(nq * static_cast<size_t>(n_chunks) * sizeof(unsigned), st);
+  QV_CUDA(cudaMemsetAsync(slots.get(), 0xff, slots.bytes(), st));  // ~0u: larger than any bound
+  a.slots = slots.get<unsigned>();
   a.err = err;
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
   const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (1 + tc::kStages) +
-                      static_cast<size_t>(tc::kCap) * tc::kM * 8 + (2 * tc::kStages + 6) * 8;
+                      static_cast<size_t>(tc::kCap) * tc::kM * 8 + (2 * tc::kStages + 2 * tc::kAcc + 2) * 8;
   const int grid = std::min(a.total_units, sm_count(s.device));
   KernelTimer timer(st, "flat_screen_tc_kernel", 2.0 * nq * static_cast<double>(s.n) * s.dim,
                     false);
