@@ -104,6 +104,25 @@ qv_status qv_flat_search_device(const qv_flat* index, const float* queries, size
 /* Global id of this index's row 0 when it is one id-range shard of a larger collection. */
 qv_status qv_flat_set_row_offset(qv_flat* index, uint64_t row_offset);
 
+/* Allocation-free variant of qv_flat_search_device. It has no counterpart in the reference; it
+ * exists for callers that must not allocate device memory while they search (a serving loop with
+ * a fixed device-memory budget, or code running where cudaMalloc/cudaFree are not allowed, e.g.
+ * from a driver callback or while another thread holds the allocator). Same arguments and the same
+ * results as qv_flat_search_device (it screens on the CUDA cores and re-ranks and certifies
+ * exactly the same way), and it calls no cudaMalloc, cudaFree or other allocating routine: every
+ * temporary lives in one fixed scratch array of qv_flat_noalloc_max_bytes() bytes (64 MiB) that
+ * each GPU loading the library holds until the process exits. A call whose temporaries would not
+ * fit (roughly nq * (dim + n_chunks * KK * 8) bytes) fails with QV_ERR_INVALID; split the queries.
+ * The first call on a device looks up the scratch's device address (cudaGetSymbolAddress), so make
+ * that first call before any stream capture. All calls share the scratch and it keeps the last
+ * call's contents: calls whose work overlaps on the GPU (different streams, or another index on
+ * the same device) race; serialize them, e.g. on one stream. */
+qv_status qv_flat_search_device_noalloc(const qv_flat* index, const float* queries, size_t nq,
+                                        size_t k, const uint64_t* position_bitmap,
+                                        uint64_t* labels, float* distances, uint64_t* keys,
+                                        void* stream);
+size_t qv_flat_noalloc_max_bytes(void);
+
 /* ---- IvfPqIndex -------------------------------------------------------------------------------- */
 typedef struct qv_ivfpq qv_ivfpq;
 

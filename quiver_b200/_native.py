@@ -55,6 +55,8 @@ _SIGNATURES = {
     "qv_flat_search": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _vp]),
     "qv_flat_search_device": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp, _vp]),
     "qv_flat_set_row_offset": (_int, [_vp, _u64]),
+    "qv_flat_search_device_noalloc": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp, _vp]),
+    "qv_flat_noalloc_max_bytes": (_sz, []),
     "qv_flat_info": (_int, [_vp, C.POINTER(_sz), C.POINTER(_sz), C.POINTER(_u32)]),
     "qv_flat_rows": (_int, [_vp, _sz, _sz, _vp, _vp]),
     "qv_flat_save": (_int, [_vp, C.c_char_p]),

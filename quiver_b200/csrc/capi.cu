@@ -448,6 +448,27 @@ qv_status qv_flat_search_device(const qv_flat* index, const float* queries, size
   });
 }
 
+qv_status qv_flat_search_device_noalloc(const qv_flat* index, const float* queries, size_t nq,
+                                        size_t k, const uint64_t* position_bitmap,
+                                        uint64_t* labels, float* distances, uint64_t* keys,
+                                        void* stream) {
+  return guarded([&] {
+    t_stats = SearchStats{};
+    QV_REQUIRE(index != nullptr, "null index");
+    if (nq == 0 || k == 0) return;
+    QV_REQUIRE(queries != nullptr && labels != nullptr && distances != nullptr,
+               "search_batch: null buffer");
+    result_size(nq, k);
+    const FlatState& s = index->s;
+    std::shared_lock lock(index->mu);
+    DeviceScope scope(s.device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(s.device);
+    flat_search_noalloc(s, queries, nq, k, position_bitmap, labels, distances, keys, st);
+  });
+}
+
+size_t qv_flat_noalloc_max_bytes(void) { return flat_noalloc_max_bytes(); }
+
 qv_status qv_flat_set_row_offset(qv_flat* index, uint64_t row_offset) {
   return guarded([&] {
     QV_REQUIRE(index != nullptr, "null index");

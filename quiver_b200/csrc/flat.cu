@@ -22,6 +22,8 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
+#include <string>
 #include <vector>
 
 #include "qv_state.h"
@@ -653,6 +655,179 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
   QV_CUDA(cudaMemcpyAsync(&nfail, fail_count, sizeof(int), cudaMemcpyDeviceToHost, st));
   QV_CUDA(cudaStreamSynchronize(st));
   thread_stats().rescanned_queries += static_cast<uint64_t>(nfail);
+}
+
+// ---- allocation-free search ------------------------------------------------------------------------
+//
+// For callers that must not allocate device memory while they search (a serving loop with a fixed
+// memory budget, code running in a driver callback or under an allocator lock, ...): the same
+// Flat search, screened on the float32 CUDA cores and then certified and re-ranked exactly like
+// flat_search, with every temporary carved from one file-scope device array. Results are
+// identical to flat_search's.
+
+constexpr size_t kNoAllocScratchBytes = size_t{64} << 20;  // per device, held until exit
+constexpr int kNoAllocMaxDevices = 64;
+
+struct NoAllocLayout {
+  size_t qp, qn2, eps, cand_d, cand_r, cand_n, thr, fail, total;
+  int dpad, kk, qpb, n_qtiles, n_chunks;
+  int64_t chunk_rows;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
+
+static NoAllocLayout noalloc_layout(const FlatState& s, size_t nq, size_t k) {
+  NoAllocLayout L{};
+  L.dpad = static_cast<int>(ceil_div(s.dim, 32) * 32);
+  L.kk = static_cast<int>(next_pow2(k + std::max<size_t>(8, k / 4)));
+  L.qpb = std::min<int>(128, (64 * 1024) / (L.kk * 8));
+  if (L.qpb >= 32) L.qpb = L.qpb / 32 * 32;
+  L.qpb = std::max(1, L.qpb);
+  L.n_qtiles = static_cast<int>(ceil_div(nq, L.qpb));
+  L.n_chunks = choose_chunks(std::max<size_t>(s.n, 1), L.n_qtiles,
+                             std::max(1, kMaxCandidatesPerQuery / L.kk), 3 * sm_count(s.device),
+                             kScreenRows, &L.chunk_rows);
+  const size_t slots = nq * static_cast<size_t>(L.n_chunks);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align256(off + bytes);
+    return at;
+  };
+  L.qp = take(nq * L.dpad * sizeof(float));
+  L.qn2 = take(nq * sizeof(float));
+  L.eps = take(nq * sizeof(float));
+  L.cand_d = take(slots * L.kk * sizeof(float));
+  L.cand_r = take(slots * L.kk * sizeof(uint32_t));
+  L.cand_n = take(slots * sizeof(int));
+  L.thr = take(nq * sizeof(unsigned));
+  L.fail = take(sizeof(int) + nq * (sizeof(int) + sizeof(float)));
+  L.total = off;
+  return L;
+}
+
+__global__ void fill_unfilled_kernel(uint64_t* labels, float* dists, uint64_t* keys, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    labels[i] = kInvalidLabel;
+    dists[i] = __int_as_float(0x7f800000);
+    if (keys) keys[i] = ~0ull;
+  }
+}
+
+}  // namespace qv
+
+// The scratch itself. In host code this name is only a handle for cudaGetSymbolAddress.
+static __device__ __align__(256) unsigned char g_flat_noalloc_scratch[qv::kNoAllocScratchBytes];
+
+namespace qv {
+
+// Device address of the scratch on `device` (which must be current), resolved once per device.
+static unsigned char* noalloc_scratch(int device) {
+  static std::mutex mu;
+  static void* addr[kNoAllocMaxDevices] = {};
+  QV_REQUIRE(device >= 0 && device < kNoAllocMaxDevices, "device index out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[device] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_flat_noalloc_scratch);
+    if (e != cudaSuccess)
+      fail(QV_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+    addr[device] = p;
+  }
+  return static_cast<unsigned char*>(addr[device]);
+}
+
+size_t flat_noalloc_max_bytes() { return kNoAllocScratchBytes; }
+
+void flat_search_noalloc(const FlatState& s, const float* d_queries, size_t nq, size_t k,
+                         const uint64_t* d_bitmap, uint64_t* d_labels, float* d_dists,
+                         uint64_t* d_keys, cudaStream_t st) {
+  if (nq == 0 || k == 0) return;
+  QV_REQUIRE(k <= 1024, "k > 1024 is not supported by the GPU FlatIndex");
+  const NoAllocLayout L = noalloc_layout(s, nq, k);
+  if (L.total > kNoAllocScratchBytes)
+    fail(QV_ERR_INVALID, "allocation-free search needs " + std::to_string(L.total) +
+                             " bytes of scratch for nq=" + std::to_string(nq) +
+                             ", k=" + std::to_string(k) + "; its fixed scratch holds " +
+                             std::to_string(kNoAllocScratchBytes) + " bytes (search fewer queries "
+                             "per call)");
+  unsigned char* base = noalloc_scratch(s.device);
+  if (s.n == 0) {
+    fill_unfilled_kernel<<<std::min<size_t>(ceil_div(nq * k, 256), 4096), 256, 0, st>>>(
+        d_labels, d_dists, d_keys, nq * k);
+    check_launch("fill_unfilled_kernel");
+    return;
+  }
+  const int dim = static_cast<int>(s.dim);
+  const bool l2 = s.metric == QV_METRIC_L2;
+  float* qp = reinterpret_cast<float*>(base + L.qp);
+  float* qn2 = reinterpret_cast<float*>(base + L.qn2);
+  float* eps = reinterpret_cast<float*>(base + L.eps);
+  float* cand_d = reinterpret_cast<float*>(base + L.cand_d);
+  uint32_t* cand_r = reinterpret_cast<uint32_t*>(base + L.cand_r);
+  int* cand_n = reinterpret_cast<int*>(base + L.cand_n);
+  unsigned* thr = reinterpret_cast<unsigned*>(base + L.thr);
+  int* fail_count = reinterpret_cast<int*>(base + L.fail);
+  int* fail_q = fail_count + 1;
+  float* fail_dk = reinterpret_cast<float*>(fail_q + nq);
+  const size_t slots = nq * static_cast<size_t>(L.n_chunks);
+
+  const double u = std::ldexp(1.0, -24);
+  const double gamma = (dim + 2) * u / (1.0 - (dim + 2) * u);
+  EpsModel em;
+  em.c_l2 = static_cast<float>(2.0 * (2.0 * gamma + 4.0 * u));
+  em.c_ip = static_cast<float>(2.0 * (2.0 * gamma));
+  em.c_abs = static_cast<float>(2.0 * (2.0 * u));
+  prep_queries_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(d_queries, nq, dim, L.dpad,
+                                                       s.metric == QV_METRIC_COSINE, l2, em,
+                                                       s.max_norm, qp, qn2, eps);
+  check_launch("prep_queries_kernel");
+  // The scratch keeps the previous call's contents: reset what must start empty.
+  QV_CUDA(cudaMemsetAsync(cand_n, 0, slots * sizeof(int), st));
+  QV_CUDA(cudaMemsetAsync(fail_count, 0, sizeof(int), st));
+  fill_u32_kernel<<<std::min<size_t>(ceil_div(nq, 256), 1024), 256, 0, st>>>(thr, nq,
+                                                                             0xff800000u);
+  check_launch("fill_u32_kernel");
+
+  const size_t smem = kScreenRows * kScreenDChunk * sizeof(float) +
+                      static_cast<size_t>(L.kk) * L.qpb * (sizeof(float) + sizeof(uint32_t));
+  const dim3 grid(static_cast<unsigned>(L.n_qtiles * L.n_chunks));
+  if (l2) {
+    QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    flat_screen_simt_kernel<true><<<grid, 128, smem, st>>>(
+        qp, L.dpad, qn2, static_cast<int>(nq), L.qpb, s.x.get<float>(), dim,
+        s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, L.chunk_rows, L.n_qtiles,
+        L.n_chunks, L.kk, cand_d, cand_r, cand_n, thr);
+  } else {
+    QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    flat_screen_simt_kernel<false><<<grid, 128, smem, st>>>(
+        qp, L.dpad, qn2, static_cast<int>(nq), L.qpb, s.x.get<float>(), dim,
+        s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, L.chunk_rows, L.n_qtiles,
+        L.n_chunks, L.kk, cand_d, cand_r, cand_n, thr);
+  }
+  check_launch("flat_screen_simt_kernel");
+  const int pool = static_cast<int>(next_pow2(static_cast<size_t>(L.n_chunks) * L.kk));
+  const size_t fsmem = pool * (sizeof(float) + sizeof(uint64_t));
+  QV_CUDA(cudaFuncSetAttribute(flat_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)fsmem));
+  flat_finalize_kernel<<<static_cast<unsigned>(nq), kFinalizeThreads, fsmem, st>>>(
+      qp, L.dpad, eps, static_cast<int>(nq), s.x.get<float>(), dim, s.labels.get<uint64_t>(),
+      s.row_offset, l2, cand_d, cand_r, cand_n, L.n_chunks, L.kk, pool, static_cast<int>(k),
+      d_labels, d_dists, d_keys, fail_count, fail_q, fail_dk);
+  check_launch("flat_finalize_kernel");
+  const int cap = static_cast<int>(next_pow2(k + 256));
+  const size_t rsmem = cap * (sizeof(float) + sizeof(uint64_t));
+  QV_CUDA(cudaFuncSetAttribute(flat_rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)rsmem));
+  flat_rescan_kernel<<<static_cast<unsigned>(std::min<size_t>(nq, 2 * sm_count(s.device))), 256,
+                       rsmem, st>>>(qp, L.dpad, s.x.get<float>(), dim, static_cast<int64_t>(s.n),
+                                    s.labels.get<uint64_t>(), d_bitmap, s.row_offset, l2,
+                                    static_cast<int>(k), cap, fail_count, fail_q, fail_dk,
+                                    d_labels, d_dists, d_keys);
+  check_launch("flat_rescan_kernel");
 }
 
 }  // namespace qv
