@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=N_DB,
+                    help="database rows (default: config 1's 1,183,514; smaller for profiling)")
+    ap.add_argument("--queries", type=int, default=N_Q, help="queries per batch (default 10,000)")
     return ap.parse_args()
 
 
@@ -63,55 +66,102 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event (throttle) reasons sampled during the timed region.
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    Reads NVML every few milliseconds from a thread (the timed region can be well under a second),
+    on the NVML device matched to the CUDA device by PCI bus id; falls back to `nvidia-smi -lms`.
+    Reading only: no clock or other GPU setting is changed."""
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+
+    def __init__(self, cuda_device: int):
+        self.cuda_device = cuda_device
+        self.sm, self.smax, self.reasons = [], [], set()
+        self.stop_evt = threading.Event()
+        self.thread = None
         self.proc = None
-        self.lines = []
+        self.source = "none"
+
+    def _nvml_handle(self):
+        import pynvml
+        import torch
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(self.cuda_device)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        return pynvml, pynvml.nvmlDeviceGetHandleByPciBusId(bus)
 
     def start(self):
         try:
+            nv, h = self._nvml_handle()
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            masks = [(name, getattr(nv, attr)) for name, attr in self.REASONS]
+
+            def poll():
+                while not self.stop_evt.is_set():
+                    try:
+                        self.sm.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                        self.smax.append(float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)))
+                        bits = get_reasons(h)
+                        self.reasons.update(n for n, m in masks if bits & m)
+                    except Exception:  # noqa: BLE001 - a failed read only loses one sample
+                        pass
+                    self.stop_evt.wait(0.005)
+
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            self.source = "nvml"
+        except Exception:  # noqa: BLE001 - NVML missing or device not matched
+            self._start_smi()
+
+    def _start_smi(self):
+        fields = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", "-i", str(self.cuda_device), f"--query-gpu={fields}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            threading.Thread(target=self._read, daemon=True).start()
+            self.source = "nvidia-smi"
         except (OSError, ValueError):
             self.proc = None
+            return
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+        def read():
+            for line in self.proc.stdout:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    self.sm.append(float(parts[1]))
+                    self.smax.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for (n, _), v in zip(self.REASONS, parts[5:9]):
+                    if v.lower() == "active":
+                        self.reasons.add(n)
+
+        self.thread = threading.Thread(target=read, daemon=True)
+        self.thread.start()
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
+        self.stop_evt.set()
+        if self.proc is not None:
+            self.proc.terminate()
             try:
-                sm.append(float(parts[1]))
-                smax.append(float(parts[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        if not self.sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no clock samples"],
+                    "samples": 0, "source": self.source}
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": max(self.smax),
+                "reasons": sorted(self.reasons), "samples": len(self.sm), "source": self.source}
 
 
 def cpu_reference_qps(db, queries, seconds: float, threads: int = 0):
@@ -218,8 +268,9 @@ def main():
     from quiver_b200.distributed import ShardedFlatIndex
     from quiver_b200.synthetic import config1
 
-    db, q = config1(N_DB, N_Q)
-    lo, hi = rank * N_DB // world, (rank + 1) * N_DB // world
+    n_db, n_q = args.rows, args.queries
+    db, q = config1(n_db, n_q)
+    lo, hi = rank * n_db // world, (rank + 1) * n_db // world
     index = ShardedFlatIndex(DIM, "cosine", device=local)
     index.add_shard(db[lo:hi], np.arange(lo, hi, dtype=np.uint64), np.arange(lo, hi))
     dq = torch.from_numpy(q).cuda()
@@ -268,7 +319,7 @@ def main():
         dist.all_reduce(c, op=dist.ReduceOp.SUM)
         launches, rescans = int(c[0].item()), int(c[1].item())
     ms_per_step = elapsed / args.steps
-    value = N_Q * args.steps / (elapsed / 1000.0)
+    value = n_q * args.steps / (elapsed / 1000.0)
 
     # ---- e2e: public API, pinned host queries in, host results out ----
     def e2e_call():
@@ -288,9 +339,9 @@ def main():
         t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = {"value": N_Q * args.steps / e2e_s, "unit": "QPS",
-           "h2d_bytes_per_step": world * N_Q * DIM * 4,
-           "d2h_bytes_per_step": world * N_Q * K * (8 + 4)}
+    e2e = {"value": n_q * args.steps / e2e_s, "unit": "QPS",
+           "h2d_bytes_per_step": world * n_q * DIM * 4,
+           "d2h_bytes_per_step": world * n_q * K * (8 + 4)}
 
     hbm, tflops, peak_kind = load_peaks()
     launches_timed = max(1, args.steps)
@@ -298,14 +349,16 @@ def main():
     achieved = (kernel_work / launches_timed) / (avg_kernel_ms / 1000.0) / 1e12 if avg_kernel_ms else 0.0
     traffic = None
     tpath = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tpath):
+    if world == 1 and (n_db, n_q) == (N_DB, N_Q) and os.path.exists(tpath):
         with open(tpath) as fh:
             traffic = json.load(fh).get(kernel_name, {}).get("bytes_per_launch_c1_shard_1gpu")
     line = {
         "metric": METRIC, "value": value, "unit": "QPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "global_batch": N_Q, "k": K, "database_rows": N_DB,
+        "config": {"workload": WORKLOAD if (n_db, n_q) == (N_DB, N_Q) else
+                   f"FlatIndex cosine k=10, {n_db:,} x 100 mixture (reduced), {n_q:,} queries",
+                   "global_batch": n_q, "k": K, "database_rows": n_db,
                    "dim": DIM, "parallelism": f"id-range shards x{world}",
                    "l2": "inputs larger than L2 (473 MB database per pass)"},
         "gpu_launches": launches, "rescanned_queries": rescans,

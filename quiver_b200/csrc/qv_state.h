@@ -14,8 +14,8 @@ namespace qv {
 
 // ---- Flat --------------------------------------------------------------------------------------
 // Rows live in HBM row-major as float32 exactly as the reference stores them (normalized for
-// cosine), with their labels, a squared norm per row for the L2 screen, and a bfloat16 copy padded
-// to a multiple of 64 columns for the tensor-core screen.
+// cosine), with their labels, a squared norm per row for the L2 screen, and a scaled fp16 copy
+// padded to at least 64 columns for the tensor-core screen.
 struct FlatState {
   int device = 0;
   size_t dim = 0;
