@@ -13,7 +13,7 @@
 //   warp 0      TMA producer: the unit's query tile (A, resident) and a 4-stage ring of 128-row
 //               tiles of the database (B), 128-byte swizzled, no multicast.
 //   warp 1      MMA issuer: allocates TMEM, issues tcgen05.mma kind::f16 (M=128, N=128, K=16 steps)
-//               into one of two TMEM accumulators, commits to mbarriers.
+//               into one of four TMEM accumulators, commits to mbarriers.
 //   warps 2..5  epilogue: thread i of the 128 owns query i (= TMEM lane i), reads its 128 inner
 //               products with tcgen05.ld, and appends survivors of its running threshold to a
 //               private candidate buffer in shared memory (compacted warp-wide when it fills).
@@ -63,6 +63,8 @@ struct Args {
   int* cand_n;
   unsigned* thr_bits;
   unsigned* slots;  // nq x n_chunks: each unit's published rank-r distance (ordered bits)
+  float* gbest;     // nq x kKK: the kKK best distances output by the query's finished units
+  int* glock;       // nq: try-lock guarding gbest[q]
   int* err;
   bool qmajor;      // unit order: query-tile-major (true) or row-chunk-major (false)
 };
@@ -169,23 +171,6 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-      "%30, %31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   float (&lo)[32] = *reinterpret_cast<float(*)[32]>(v);
   float (&hi)[32] = *reinterpret_cast<float(*)[32]>(v + 32);
@@ -215,62 +200,32 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   }
 }
 
-__device__ __forceinline__ float tree_min64(const float (&v)[64]) {
-  float m[32];
-#pragma unroll
-  for (int i = 0; i < 32; ++i) m[i] = fminf(v[2 * i], v[2 * i + 1]);
-#pragma unroll
-  for (int w = 16; w > 0; w >>= 1)
-#pragma unroll
-    for (int i = 0; i < w; ++i) m[i] = fminf(m[i], m[i + w]);
-  return m[0];
+// Screen distance of one accumulator element: for L2 the element already is the distance; for
+// cosine / inner product it is the raw (scaled) inner product and the distance is 1 - dot * inv.
+// fmaf rounds once and is monotone in the element, so the best raw value gives the best distance.
+template <bool kL2>
+__device__ __forceinline__ float screen_value(float x, float inv) {
+  return kL2 ? x : fmaf(-x, inv, 1.0f);
 }
 
-__device__ __forceinline__ float tree_max64(const float (&v)[64]) {
-  float m[32];
+// best[g] = best of v[8g .. 8g+7] (max when kMax, else min), top = best of all 64, as a
+// contiguous pairwise tree (63 operations, depth 6).
+template <bool kMax>
+__device__ __forceinline__ void group_best8(const float (&v)[64], float (&best)[8], float& top) {
+  float m1[32], m2[16];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) m[i] = fmaxf(v[2 * i], v[2 * i + 1]);
+  for (int i = 0; i < 32; ++i) m1[i] = kMax ? fmaxf(v[2 * i], v[2 * i + 1]) : fminf(v[2 * i], v[2 * i + 1]);
 #pragma unroll
-  for (int w = 16; w > 0; w >>= 1)
+  for (int i = 0; i < 16; ++i) m2[i] = kMax ? fmaxf(m1[2 * i], m1[2 * i + 1]) : fminf(m1[2 * i], m1[2 * i + 1]);
 #pragma unroll
-    for (int i = 0; i < w; ++i) m[i] = fmaxf(m[i], m[i + w]);
-  return m[0];
-}
-
-// Minimum of 32 values as a 5-level tree (short dependency chains).
-__device__ __forceinline__ float tree_min32(const float (&v)[32]) {
-  float m[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) m[i] = fminf(v[2 * i], v[2 * i + 1]);
-#pragma unroll
-  for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-    for (int i = 0; i < w; ++i) m[i] = fminf(m[i], m[i + w]);
-  return m[0];
-}
-
-// Bit j set when v[j] <= thr and row cb + j is admitted by the position bitmap (OR tree).
-__device__ __forceinline__ uint32_t survivors32(const float (&v)[32], float thr,
-                                                const uint64_t* bitmap, int64_t cb) {
-  uint32_t b[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i)
-    b[i] = (v[2 * i] <= thr ? (1u << (2 * i)) : 0u) | (v[2 * i + 1] <= thr ? (2u << (2 * i)) : 0u);
-#pragma unroll
-  for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-    for (int i = 0; i < w; ++i) b[i] |= b[i + w];
-  uint32_t m = b[0];
-  if (bitmap != nullptr && m != 0) {
-    // The 32 rows span at most two 64-bit words of the bitmap.
-    const uint64_t w0 = bitmap[static_cast<uint64_t>(cb) >> 6];
-    const uint64_t last = static_cast<uint64_t>(cb + 31) >> 6;
-    const uint64_t w1 = last != (static_cast<uint64_t>(cb) >> 6) ? bitmap[last] : 0ull;
-    const int sh = static_cast<int>(cb & 63);
-    const uint64_t bits = (w0 >> sh) | (sh ? (w1 << (64 - sh)) : 0ull);
-    m &= static_cast<uint32_t>(bits);
-  }
-  return m;
+  for (int i = 0; i < 8; ++i) best[i] = kMax ? fmaxf(m2[2 * i], m2[2 * i + 1]) : fminf(m2[2 * i], m2[2 * i + 1]);
+  const float b0 = kMax ? fmaxf(best[0], best[1]) : fminf(best[0], best[1]);
+  const float b1 = kMax ? fmaxf(best[2], best[3]) : fminf(best[2], best[3]);
+  const float b2 = kMax ? fmaxf(best[4], best[5]) : fminf(best[4], best[5]);
+  const float b3 = kMax ? fmaxf(best[6], best[7]) : fminf(best[6], best[7]);
+  const float c0 = kMax ? fmaxf(b0, b1) : fminf(b0, b1);
+  const float c1 = kMax ? fmaxf(b2, b3) : fminf(b2, b3);
+  top = kMax ? fmaxf(c0, c1) : fminf(c0, c1);
 }
 
 // Sorts one query's buffer (its first `cnt` entries; the rest padded with +inf) by
@@ -453,11 +408,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue: thread = query ----------------
     // Each query keeps an unsorted candidate buffer of kCap (distance, row) entries in shared
-    // memory. Per 32-column chunk: screen distances in registers; a warp-uniform skip when no lane
-    // can improve on its threshold; else survivors are appended with predicated stores (no
-    // divergent branches). When any lane's buffer could overflow on the next chunk, the warp
-    // compacts together: every lane sorts its buffer and keeps the best kKK, which also tightens
-    // its threshold to the kKK-th distance.
+    // memory. Per 64 columns: one pairwise tree gives the best score of each 8-column group and
+    // of all 64; the warp skips the 64 columns when no lane can improve on its threshold (the
+    // common case). Otherwise it visits only the 8-column groups some lane can improve on, and
+    // lanes append their survivors. When any lane's buffer could overflow, the warp compacts
+    // together: every lane sorts its buffer and keeps the best kKK, which also tightens its
+    // threshold to the kKK-th distance.
     const int quarter = warp & 3;
     const int qi = quarter * 32 + lane;
     float* bd = buf_d + qi;
@@ -494,9 +450,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld64(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                         static_cast<uint32_t>(accb * kN + h * 64),
                     v);
-          const int64_t cb = row0 + h * 64;
+          const int64_t cb = row0 + h * 64;  // a multiple of 64: chunks are multiples of kN rows
           const int valid = static_cast<int>(r1 - cb < 64 ? r1 - cb : 64);  // rows of this chunk
-          bool may;
+          // best[g]: the best score among elements 8g..8g+7 (max inner product for cosine/IP,
+          // min distance for L2), from a contiguous pairwise tree; top: the best of all 64.
+          float best[8];
+          float top;
           if (kL2) {
             // v[j] := ||q||^2 + ||x||^2 - 2<q,x>; columns past the chunk end become +inf.
 #pragma unroll
@@ -504,43 +463,42 @@ __global__ void __launch_bounds__(kThreads, 1)
               const float xn = j < valid ? a.xnorm2[cb + j] : 0.0f;
               v[j] = j < valid ? fmaf(-2.0f * inv, v[j], qn + xn) : kInfF;
             }
-            may = active && tree_min64(v) <= thr;
+            group_best8<false>(v, best, top);
           } else {
-            // Skip test on the raw inner products: the best screen distance is 1 - max * inv.
             if (valid < 64) {
 #pragma unroll
               for (int j = 0; j < 64; ++j)
                 if (j >= valid) v[j] = -kInfF;
             }
-            may = active && 1.0f - tree_max64(v) * inv <= thr;
+            group_best8<true>(v, best, top);
           }
+          const bool may = active && screen_value<kL2>(top, inv) <= thr;
           if (!__any_sync(0xffffffffu, may)) continue;
-          if (!kL2) {
+          const uint64_t allowed =
+              a.bitmap != nullptr ? a.bitmap[static_cast<uint64_t>(cb) >> 6] : ~0ull;
+          // Survivor path, 8 rows at a time, entered only for groups some lane can improve on.
 #pragma unroll
-            for (int j = 0; j < 64; ++j) v[j] = 1.0f - v[j] * inv;  // screen distances (-inf -> +inf)
-          }
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            float (&w)[32] = *reinterpret_cast<float(*)[32]>(v + 32 * half);
-            const int64_t cbh = cb + 32 * half;
-            uint32_t mask = may ? survivors32(w, thr, a.bitmap, cbh) : 0u;
-            // Compact only when some lane's survivors would not fit.
-            if (__any_sync(0xffffffffu, cnt + __popc(mask) > kCap)) {
+          for (int g = 0; g < 8; ++g) {
+            bool sub = may && screen_value<kL2>(best[g], inv) <= thr;
+            if (!__any_sync(0xffffffffu, sub)) continue;
+            // Compact (all lanes together) when some lane's 8 new entries might not fit.
+            if (__any_sync(0xffffffffu, sub && cnt > kCap - 8)) {
               compact_buffer(bd, br, cnt, thr);
-              mask &= survivors32(w, thr, nullptr, cbh);
               if (active && cnt >= r_pub)
                 atomicMin(qslots + chunk, dev::ordered_bits(bd[(r_pub - 1) * kM]));
+              sub = sub && screen_value<kL2>(best[g], inv) <= thr;
             }
-            if (mask != 0) {
+            if (sub) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if ((mask >> j) & 1u) {
-                  const int pos = cnt + __popc(mask & ((1u << j) - 1u));
-                  bd[pos * kM] = w[j];
-                  br[pos * kM] = static_cast<uint32_t>(cbh + j);
+              for (int j = 0; j < 8; ++j) {
+                const int e = 8 * g + j;
+                const float d = screen_value<kL2>(v[e], inv);
+                if (d <= thr && ((allowed >> e) & 1ull)) {
+                  bd[cnt * kM] = d;
+                  br[cnt * kM] = static_cast<uint32_t>(cb + e);
+                  ++cnt;
                 }
               }
-              cnt += __popc(mask);
             }
           }
         }
@@ -572,6 +530,32 @@ __global__ void __launch_bounds__(kThreads, 1)
         a.cand_n[slot] = cnt;
         if (cnt >= r_pub) atomicMin(qslots + chunk, dev::ordered_bits(bd[(r_pub - 1) * kM]));
         if (cnt == kKK) atomicMin(a.thr_bits + q, dev::ordered_bits(bd[(kKK - 1) * kM]));
+        // Merge this unit's output into the query's running best-kKK list and publish its kKK-th
+        // value as the query's threshold: kKK distinct output candidates lie at or below it, which
+        // is all a threshold needs. Each unit merges once (its rows are disjoint from every other
+        // unit's), under a try-lock: when another unit holds it the merge is skipped, which only
+        // leaves the bound looser.
+        if (cnt > 0 && atomicCAS(a.glock + q, 0, 1) == 0) {
+          __threadfence();
+          volatile float* gq = a.gbest + static_cast<size_t>(q) * kKK;
+          float merged[kKK];
+          int gi = 0, bi = 0;
+#pragma unroll
+          for (int o = 0; o < kKK; ++o) {
+            const float gv = gi < kKK ? gq[gi] : kInfF;
+            const float bv = bi < cnt ? bd[bi * kM] : kInfF;
+            const bool take_b = bv < gv;
+            merged[o] = take_b ? bv : gv;
+            bi += take_b ? 1 : 0;
+            gi += take_b ? 0 : 1;
+          }
+#pragma unroll
+          for (int o = 0; o < kKK; ++o) gq[o] = merged[o];
+          __threadfence();
+          if (merged[kKK - 1] < kInfF)
+            atomicMin(a.thr_bits + q, dev::ordered_bits(merged[kKK - 1]));
+          atomicExch(a.glock + q, 0);
+        }
       }
     }
   }
@@ -582,6 +566,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
                  "r"(kAcc * kN));
   }
+}
+
+__global__ void fill_inf_kernel(float* p, size_t n) {
+  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  if (i < n) p[i] = __int_as_float(0x7f800000);
 }
 
 // ---- fp16 operands ---------------------------------------------------------------------------------
@@ -805,6 +794,13 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   DeviceBuffer slots(nq * static_cast<size_t>(n_chunks) * sizeof(unsigned), st);
   QV_CUDA(cudaMemsetAsync(slots.get(), 0xff, slots.bytes(), st));  // ~0u: larger than any bound
   a.slots = slots.get<unsigned>();
+  DeviceBuffer gbest(nq * tc::kKK * sizeof(float), st), glock(nq * sizeof(int), st);
+  tc::fill_inf_kernel<<<ceil_div(nq * tc::kKK, 256), 256, 0, st>>>(gbest.get<float>(),
+                                                                   nq * tc::kKK);
+  check_launch("fill_inf_kernel");
+  QV_CUDA(cudaMemsetAsync(glock.get(), 0, glock.bytes(), st));
+  a.gbest = gbest.get<float>();
+  a.glock = glock.get<int>();
   a.err = err;
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
   const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (1 + tc::kStages) +
