@@ -1,5 +1,5 @@
 #!/usr/bin/env python
-"""Benchmark of the hot path: exact FlatIndex cosine search, 10,000-query batches, k=10.
+"""Benchmark of the hot path. Default: exact FlatIndex cosine search, 10,000-query batches, k=10.
 
 Workload: 1,183,514 x 100 float32 vectors from a 1,000-component Gaussian
 mixture, L2-normalized; 10,000 queries drawn the same way (seeded synthetic data standing in for
@@ -9,6 +9,13 @@ k-way merge. A step is one search of the whole 10k batch. Total work is fixed, s
 scaling.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload c1|c2|c3] [--nprobe P] [--filter]
+
+``--workload c2`` / ``c3`` measure IVF-PQ search instead (BASELINE configs 2 and 3): the trained,
+empty index the reference saved (tests/golden/ivf_c{2,3}_trained.qvr) is loaded on every GPU,
+each rank adds its id range of the database on its GPU, and a step is one search of the 10k
+batch at ``--nprobe`` (config 3: refine_factor 8; ``--filter``: a seeded random 1 % allowed-id
+set).
 
 Rank 0 prints one JSON line. ``value`` is whole-job QPS with queries already on the GPUs;
 ``e2e`` is the same metric through the public Python API with the queries in pinned host memory
@@ -48,7 +55,30 @@ def parse():
     ap.add_argument("--rows", type=int, default=N_DB,
                     help="database rows (default: config 1's 1,183,514; smaller for profiling)")
     ap.add_argument("--queries", type=int, default=N_Q, help="queries per batch (default 10,000)")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3"], default="c1")
+    ap.add_argument("--nprobe", type=int, default=64, help="IVF-PQ workloads: lists probed")
+    ap.add_argument("--filter", action="store_true", help="IVF-PQ workloads: 1%% allowed ids")
     return ap.parse_args()
+
+
+IVF_WORKLOADS = {
+    # name: (trained file, metric, dim, refine_factor, rows, description)
+    "c2": ("ivf_c2_trained.qvr", "l2", 128, 0, 1_000_000,
+           "IvfPqIndex L2 nlist 2048 m 32, 1,000,000 x 128 skewed ints (BASELINE config 2)"),
+    "c3": ("ivf_c3_trained.qvr", "cosine", 100, 8, 1_183_514,
+           "IvfPqIndex cosine nlist 2048 m 25 refine 8, 1,183,514 x 100 mixture (BASELINE config 3)"),
+}
+
+
+def ivf_data(workload: str):
+    from quiver_b200.synthetic import config2, config3
+    return config2() if workload == "c2" else config3()
+
+
+def ivf_allowed(n: int) -> np.ndarray:
+    """The filtered run's allowed ids: a seeded random 1 % of [0, n)."""
+    rng = np.random.default_rng(7)
+    return np.sort(rng.choice(n, n // 100, replace=False)).astype(np.uint64)
 
 
 def env_rank():
@@ -204,8 +234,61 @@ def cpu_port_qps(db, queries, seconds: float):
     return n / dt, 1, f"{n} queries, single-threaded C restatement (oracle/qv_oracle.c)", "port"
 
 
+def ref_ivf_index(ref, workload: str, db):
+    """The reference's own IvfPqIndex: its trained file plus the database added on the CPU."""
+    ix = ref.ivf_load(os.path.join(ROOT, "tests", "golden", IVF_WORKLOADS[workload][0]))
+    ix.add(db)
+    return ix
+
+
+def cpu_reference_ivf_qps(ref, ix, queries, nprobe, refine, allowed, seconds: float):
+    ix.search(queries[:64], K, nprobe, refine, allowed)  # warm-up
+    t0 = time.perf_counter()
+    ix.search(queries[:256], K, nprobe, refine, allowed)
+    per_q = (time.perf_counter() - t0) / 256
+    n = int(min(len(queries), max(256, seconds / max(per_q, 1e-9))))
+    t0 = time.perf_counter()
+    ix.search(queries[:n], K, nprobe, refine, allowed)
+    return n / (time.perf_counter() - t0), n
+
+
 def run_reference_arm(args, rank, world):
     if rank != 0:
+        return
+    if args.workload != "c1":
+        from oracle.oracle import REF_SO, Reference
+        name = IVF_WORKLOADS[args.workload]
+        if not os.path.exists(REF_SO):
+            print(json.dumps({"impl": "reference",
+                              "unavailable": "reference library oracle/_ref was not built"}))
+            return
+        ref = Reference()
+        db, q = ivf_data(args.workload)
+        ix = ref_ivf_index(ref, args.workload, db)
+        allowed = ivf_allowed(len(db)) if args.filter else None
+        refine = name[3]
+        per_step = None
+        qps_list = []
+        for i in range(args.warmup + args.steps):
+            qps, n = cpu_reference_ivf_qps(ref, ix, q, args.nprobe, refine, allowed, 3.0)
+            if i >= args.warmup:
+                qps_list.append(qps)
+                per_step = n
+        qps = statistics.mean(qps_list)
+        sample = (f"{per_step} of the {N_Q} queries per step, IvfPqIndex::search_batch nprobe "
+                  f"{args.nprobe} refine {refine}{' filtered 1%' if args.filter else ''}, "
+                  f"{ref.threads} threads, ISA {ref.isa}")
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": qps, "unit": "QPS",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * N_Q / qps, "higher_is_better": True, "data": "synthetic",
+            "dtype": "f32", "config": {"workload": name[5], "nprobe": args.nprobe,
+                                       "filter": "1% ids" if args.filter else None,
+                                       "global_batch": N_Q, "k": K},
+            "cpu_baseline": {"value": qps, "unit": "QPS", "cores": ref.threads,
+                             "kind": "reference", "sample": sample},
+            "e2e": {"value": qps, "unit": "QPS", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}), flush=True)
         return
     from quiver_b200.synthetic import config1
     db, q = config1(N_DB, N_Q)
@@ -249,6 +332,115 @@ def run_reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_ivf(args, rank, world, local):
+    """IVF-PQ workloads (configs 2 and 3): value, e2e, roofline (HBM) and CPU baseline."""
+    import torch
+    import torch.distributed as dist
+    import quiver_b200 as qv
+    from quiver_b200 import _native
+    from quiver_b200.distributed import ShardedIvfPqIndex
+
+    fname, metric, dim, refine, rows, desc = IVF_WORKLOADS[args.workload]
+    db, q = ivf_data(args.workload)
+    n = len(db)
+    lo, hi = rank * n // world, (rank + 1) * n // world
+    index = ShardedIvfPqIndex.from_trained(os.path.join(ROOT, "tests", "golden", fname),
+                                           db[lo:hi], np.arange(lo, hi, dtype=np.uint64),
+                                           total=n, device=local)
+    allowed = ivf_allowed(n) if args.filter else None
+    bitmap = index.filter_bitmap(allowed)
+    dq = torch.from_numpy(q).cuda()
+    q_host = torch.from_numpy(q).pin_memory().numpy()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        index.search_device(dq, K, args.nprobe, refine, bitmap)
+    torch.cuda.synchronize()
+    _native.set_timing(True)
+    sampler = ClockSampler(local)
+    sampler.start()
+    launches, kernel_ms, kernel_bytes = 0, 0.0, 0.0
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        index.search_device(dq, K, args.nprobe, refine, bitmap)
+        st = qv.last_search_stats()
+        launches += st["kernel_launches"]
+        kernel_ms += st["dominant_kernel_ms"]
+        kernel_bytes += st["dominant_kernel_work"]
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    _native.set_timing(False)
+    elapsed = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([elapsed], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+        c = torch.tensor([launches], device="cuda", dtype=torch.float64)
+        dist.all_reduce(c, op=dist.ReduceOp.SUM)
+        launches = int(c[0].item())
+    value = N_Q * args.steps / (elapsed / 1000.0)
+
+    def e2e_call():
+        if world == 1:
+            return index.local.search(q_host, K, args.nprobe, refine, filter=allowed)
+        return index.search(q_host, K, args.nprobe, refine, filter=allowed)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_call()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_call()
+    e2e_s = time.perf_counter() - t0
+    barrier()
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    hbm, _, peak_kind = load_peaks()
+    avg_ms = kernel_ms / max(1, args.steps)
+    per_launch = kernel_bytes / max(1, args.steps)
+    achieved = per_launch / (avg_ms / 1000.0) / 1e9 if avg_ms else 0.0
+    line = {
+        "metric": METRIC, "value": value, "unit": "QPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": desc, "nprobe": args.nprobe, "refine_factor": refine,
+                   "filter": "1% ids" if args.filter else None, "global_batch": N_Q, "k": K,
+                   "database_rows": n, "parallelism": f"id-range shards x{world}",
+                   "l2": "codes (32 MB / 30 MB) are L2-resident; no flush between steps"},
+        "gpu_launches": launches,
+        "roofline": {"bound": "hbm", "kernel": "ivf_scan_kernel", "achieved": achieved,
+                     "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
+                     "peak_source": f"{peak_kind} HBM copy", "traffic": None,
+                     "avg_launch_ms": avg_ms, "work_per_launch": per_launch},
+        "clocks": clocks,
+        "e2e": {"value": N_Q * args.steps / e2e_s, "unit": "QPS",
+                "h2d_bytes_per_step": world * N_Q * dim * 4,
+                "d2h_bytes_per_step": world * N_Q * K * (8 + 4)},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.oracle import REF_SO, Reference
+        if os.path.exists(REF_SO):
+            ref = Reference()
+            ix = ref_ivf_index(ref, args.workload, db)
+            qps, nsamp = cpu_reference_ivf_qps(ref, ix, q, args.nprobe, refine, allowed, 15.0)
+            line["cpu_baseline"] = {
+                "value": qps, "unit": "QPS", "cores": ref.threads, "kind": "reference",
+                "sample": f"{nsamp} of the {N_Q} queries, IvfPqIndex::search_batch, "
+                          f"{ref.threads} threads, ISA {ref.isa}"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = env_rank()
@@ -263,6 +455,11 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device(f"cuda:{local}"))
+    if args.workload != "c1":
+        run_ivf(args, rank, world, local)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     import quiver_b200 as qv
     from quiver_b200 import _native
     from quiver_b200.distributed import ShardedFlatIndex

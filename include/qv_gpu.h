@@ -174,6 +174,10 @@ qv_status qv_ivfpq_load(int device, const char* path, int verify_checksums, qv_i
  * (list << 32 | offset-in-full-list) match the unsharded index. */
 qv_status qv_ivfpq_load_shard(int device, const char* path, int verify_checksums,
                               uint64_t label_begin, uint64_t label_end, qv_ivfpq** out);
+/* For a shard built by add() instead of load_shard: base[l] (nlist entries) = number of entries
+ * of list l held by the shards before this one, so that candidate keys match the unsharded
+ * index. No counterpart in the reference (which has no sharding). */
+qv_status qv_ivfpq_set_list_base(qv_ivfpq* index, const uint32_t* base);
 
 /* Device-resident stages for composing and for multi-GPU sharding (all pointers on the index's
  * GPU). qv_ivfpq_search_device runs the whole search. qv_ivfpq_candidates_device stops after the

@@ -80,6 +80,7 @@ _SIGNATURES = {
     "qv_ivfpq_save": (_int, [_vp, C.c_char_p]),
     "qv_ivfpq_load": (_int, [_int, C.c_char_p, _int, _PP]),
     "qv_ivfpq_load_shard": (_int, [_int, C.c_char_p, _int, _u64, _u64, _PP]),
+    "qv_ivfpq_set_list_base": (_int, [_vp, _vp]),
     "qv_merge_topk_device": (_int, [_int, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "qv_select_topk_device": (_int, [_int, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
 }

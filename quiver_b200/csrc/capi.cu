@@ -5,6 +5,7 @@
 #include <cstring>
 #include <limits>
 #include <map>
+#include <set>
 #include <memory>
 #include <mutex>
 #include <shared_mutex>
@@ -54,14 +55,37 @@ bool& thread_timing() {
   return on;
 }
 
+// Keeps freed stream-ordered allocations in the device's default memory pool instead of
+// returning them to the driver at every synchronization, so that the temporaries of one search
+// are reused by the next without remapping memory (a per-process setting of this context).
+void keep_pool_memory(int device) {
+  static std::mutex mu;
+  static std::set<int> done;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!done.insert(device).second) return;
+  cudaMemPool_t pool = nullptr;
+  if (cudaDeviceGetDefaultMemPool(&pool, device) == cudaSuccess) {
+    uint64_t keep = UINT64_MAX;
+    cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep);
+  }
+}
+
 cudaStream_t thread_stream(int device) {
   thread_local std::map<int, cudaStream_t> streams;
   auto it = streams.find(device);
   if (it != streams.end()) return it->second;
+  keep_pool_memory(device);
   cudaStream_t s = nullptr;
   QV_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
   streams[device] = s;
   return s;
+}
+
+// The caller's stream for a _device entry point, or the thread's own stream when it passes NULL.
+cudaStream_t pick_stream(void* stream, int device) {
+  if (stream == nullptr) return thread_stream(device);
+  keep_pool_memory(device);
+  return static_cast<cudaStream_t>(stream);
 }
 
 int sm_count(int device) {
@@ -77,9 +101,15 @@ int sm_count(int device) {
 }
 
 void check_finite(const float* v, size_t count) {
-  bool ok = true;
-  for (size_t i = 0; i < count; ++i) ok &= std::isfinite(v[i]);
-  QV_REQUIRE(ok, "vectors must not contain NaN or infinity");
+  // A float is NaN or infinite exactly when its exponent bits are all ones; the branch-free
+  // integer test vectorizes (the whole query batch is checked on every search).
+  uint32_t bad = 0;
+  for (size_t i = 0; i < count; ++i) {
+    uint32_t b;
+    std::memcpy(&b, v + i, sizeof(b));
+    bad |= static_cast<uint32_t>((b & 0x7f800000u) == 0x7f800000u);
+  }
+  QV_REQUIRE(bad == 0, "vectors must not contain NaN or infinity");
 }
 
 namespace {
@@ -443,7 +473,7 @@ qv_status qv_flat_search_device(const qv_flat* index, const float* queries, size
     const FlatState& s = index->s;
     std::shared_lock lock(index->mu);
     DeviceScope scope(s.device);
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(s.device);
+    cudaStream_t st = pick_stream(stream, s.device);
     flat_search(s, queries, nq, k, position_bitmap, labels, distances, keys, st);
   });
 }
@@ -462,7 +492,7 @@ qv_status qv_flat_search_device_noalloc(const qv_flat* index, const float* queri
     const FlatState& s = index->s;
     std::shared_lock lock(index->mu);
     DeviceScope scope(s.device);
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(s.device);
+    cudaStream_t st = pick_stream(stream, s.device);
     flat_search_noalloc(s, queries, nq, k, position_bitmap, labels, distances, keys, st);
   });
 }
@@ -736,7 +766,7 @@ qv_status qv_ivfpq_search_device(const qv_ivfpq* index, const float* queries, si
     const IvfState& s = index->s;
     std::shared_lock lock(index->mu);
     DeviceScope scope(s.device);
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(s.device);
+    cudaStream_t st = pick_stream(stream, s.device);
     ivf_search(s, queries, nq, k, nprobe, refine_factor, position_bitmap, labels, distances, st);
   });
 }
@@ -751,7 +781,7 @@ qv_status qv_ivfpq_candidates_device(const qv_ivfpq* index, const float* queries
     const IvfState& s = index->s;
     std::shared_lock lock(index->mu);
     DeviceScope scope(s.device);
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(s.device);
+    cudaStream_t st = pick_stream(stream, s.device);
     ivf_candidates(s, queries, nq, keep, nprobe, position_bitmap, distances, keys, labels, st);
   });
 }
@@ -763,7 +793,7 @@ qv_status qv_ivfpq_refine_device(const qv_ivfpq* index, const float* queries, si
     const IvfState& s = index->s;
     std::shared_lock lock(index->mu);
     DeviceScope scope(s.device);
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(s.device);
+    cudaStream_t st = pick_stream(stream, s.device);
     ivf_refine(s, queries, nq, keep, keys, exact, st);
   });
 }
@@ -868,6 +898,22 @@ qv_status qv_ivfpq_load_shard(int device, const char* path, int verify_checksums
   });
 }
 
+qv_status qv_ivfpq_set_list_base(qv_ivfpq* index, const uint32_t* base) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr && base != nullptr, "null argument");
+    std::unique_lock lock(index->mu);
+    IvfState& s = index->s;
+    QV_REQUIRE(s.trained, "IVF-PQ index must be trained before set_list_base()");
+    s.host_global_base.assign(base, base + s.nlist);
+    DeviceScope scope(s.device);
+    cudaStream_t st = thread_stream(s.device);
+    s.global_base.allocate(s.nlist * sizeof(uint32_t));
+    QV_CUDA(cudaMemcpyAsync(s.global_base.get(), s.host_global_base.data(),
+                            s.nlist * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+    QV_CUDA(cudaStreamSynchronize(st));
+  });
+}
+
 // ---- merge -------------------------------------------------------------------------------------
 
 qv_status qv_merge_topk_device(int device, size_t parts, size_t nq, size_t k,
@@ -877,7 +923,7 @@ qv_status qv_merge_topk_device(int device, size_t parts, size_t nq, size_t k,
   return guarded([&] {
     QV_REQUIRE(distances && keys && out_distances, "null argument");
     DeviceScope scope(device);
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(device);
+    cudaStream_t st = pick_stream(stream, device);
     merge_topk(parts, nq, k, distances, keys, labels, out_distances, out_keys, out_labels, st);
   });
 }
@@ -890,7 +936,7 @@ qv_status qv_select_topk_device(int device, size_t nq, size_t n, size_t k, const
     QV_REQUIRE(distances && keys && out_distances, "null argument");
     QV_REQUIRE(k <= n || n == 0, "select_topk: k > n");
     DeviceScope scope(device);
-    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : thread_stream(device);
+    cudaStream_t st = pick_stream(stream, device);
     select_topk(nq, n, k, distances, keys, labels, out_distances, out_keys, out_labels, st);
   });
 }

@@ -494,6 +494,21 @@ __global__ void ivf_refine_kernel(const float* __restrict__ qn, size_t nq, int d
   if (lane == 0) out[w] = e;
 }
 
+// Total length of the probed lists over all (query, probe) pairs: the number of codes a scan
+// reads, for the timing statistics' algorithmic bytes.
+__global__ void probed_codes_kernel(const uint32_t* __restrict__ probes, size_t total,
+                                    const uint64_t* __restrict__ offsets,
+                                    unsigned long long* __restrict__ out) {
+  unsigned long long acc = 0;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const uint32_t l = probes[i];
+    acc += offsets[l + 1] - offsets[l];
+  }
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0 && acc != 0) atomicAdd(out, acc);
+}
+
 __global__ void copy_queries_kernel(const float* q, size_t total, float* out) {
   for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<size_t>(gridDim.x) * blockDim.x)
@@ -574,8 +589,34 @@ void run_scan(const IvfState& s, const Prepared& p, size_t nq, size_t keep, size
   }
   QV_CUDA(cudaFuncSetAttribute(ivf_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem));
+  // With timing on: the scan's algorithmic bytes are the codes of the probed lists (m bytes
+  // each), the lookup-table source per probe (the precomputed slice for L2 with precomputed
+  // terms; the codebooks once per query otherwise), the query, and the stored vectors the
+  // refine gathers.
+  DeviceBuffer codes_read;
+  if (thread_timing()) {
+    codes_read.allocate(sizeof(unsigned long long), st);
+    QV_CUDA(cudaMemsetAsync(codes_read.get(), 0, sizeof(unsigned long long), st));
+    const size_t pairs = nq * static_cast<size_t>(p.nprobe);
+    probed_codes_kernel<<<static_cast<unsigned>(std::min<size_t>(ceil_div(pairs, 256), 1024)), 256,
+                          0, st>>>(p.probes.get<uint32_t>(), pairs, a.offsets,
+                                   codes_read.get<unsigned long long>());
+    check_launch("probed_codes_kernel");
+  }
+  KernelTimer timer(st, "ivf_scan_kernel", 0.0, true);
   ivf_scan_kernel<<<static_cast<unsigned>(nq), kScanThreads, smem, st>>>(a);
+  timer.stop();
   check_launch("ivf_scan_kernel");
+  if (timer.on()) {
+    unsigned long long codes = 0;
+    QV_CUDA(cudaMemcpyAsync(&codes, codes_read.get(), sizeof(codes), cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaStreamSynchronize(st));
+    const double lut = static_cast<double>(ts) * (a.use_pre ? p.nprobe : 1);
+    const double per_query = lut + s.dim * sizeof(float) +
+                             (refine ? static_cast<double>(keep) * s.dim * sizeof(float) : 0.0);
+    timer.set_work(static_cast<double>(codes) * s.m + per_query * static_cast<double>(nq));
+    timer.finish();
+  }
 }
 
 }  // namespace

@@ -167,6 +167,9 @@ class KernelTimer {
   void stop() {
     if (on_) cudaEventRecord(e1_, st_);
   }
+  // For work that is only known after the launch (e.g. the list lengths a scan visited).
+  void set_work(double work) { work_ = work; }
+  bool on() const { return on_; }
   void finish() {
     if (!on_) return;
     float ms = 0.0f;

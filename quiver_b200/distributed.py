@@ -40,9 +40,25 @@ def _stream_ptr() -> int:
 def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
     if world == 1:
         return t.unsqueeze(0)
-    out = torch.empty((world,) + tuple(t.shape), dtype=t.dtype, device=t.device)
-    dist.all_gather_into_tensor(out, t.contiguous(), group=group)
-    return out
+    t = t.contiguous()
+    # Concatenated along dim 0 (the form every backend accepts), then viewed per rank.
+    out = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(out, t, group=group)
+    return out.view((world,) + tuple(t.shape))
+
+
+def shard_range(n: int, rank: int, world: int):
+    """Rank `rank`'s id range [lo, hi) of n rows split over `world` ranks."""
+    return rank * n // world, (rank + 1) * n // world
+
+
+def list_bases(sizes: torch.Tensor, rank: int, world: int, group=None) -> torch.Tensor:
+    """Per IVF list, the number of entries held by the ranks below `rank` (an exclusive prefix
+    over ranks of every rank's list sizes, exchanged with one all-gather)."""
+    if world == 1:
+        return torch.zeros_like(sizes)
+    every = _all_gather(sizes, world, group)
+    return every[:rank].sum(dim=0)
 
 
 def _merge(parts_d, parts_k, parts_l, k, device):
@@ -53,8 +69,6 @@ def _merge(parts_d, parts_k, parts_l, k, device):
     check(lib().qv_merge_topk_device(device, world, nq, kk, parts_d.data_ptr(),
                                      parts_k.data_ptr(), parts_l.data_ptr(), od.data_ptr(),
                                      ok.data_ptr(), ol.data_ptr(), C.c_void_p(_stream_ptr())))
-    if k < kk:
-        pass
     return od, ok, ol
 
 
@@ -78,7 +92,7 @@ class ShardedFlatIndex:
         x = _as_matrix(vectors, self.dim)
         n = x.shape[0]
         la = _as_labels(labels, n)
-        lo, hi = self.rank * n // self.world, (self.rank + 1) * n // self.world
+        lo, hi = shard_range(n, self.rank, self.world)
         gids = np.arange(self.ntotal + lo, self.ntotal + hi, dtype=np.int64)
         mine = la[lo:hi] if la is not None else gids.astype(np.uint64)
         self.add_shard(x[lo:hi], mine, gids)
@@ -101,10 +115,10 @@ class ShardedFlatIndex:
         check(lib().qv_flat_search_device(self.local.handle, queries.data_ptr(), nq, k, None,
                                           lab.data_ptr(), d.data_ptr(), key.data_ptr(),
                                           C.c_void_p(_stream_ptr())))
-        valid = key >= 0  # unfilled slots carry key 2^64-1 (-1 as int64)
-        gkey = torch.where(valid, self._gid[key.clamp(min=0)], key)
         if self.world == 1:
             return d, lab
+        valid = key >= 0  # unfilled slots carry key 2^64-1 (-1 as int64)
+        gkey = torch.where(valid, self._gid[key.clamp(min=0)], key)
         od, _, ol = _merge(_all_gather(d, self.world, self.group),
                            _all_gather(gkey, self.world, self.group),
                            _all_gather(lab, self.world, self.group), k, self.device)
@@ -118,42 +132,84 @@ class ShardedFlatIndex:
 
 
 class ShardedIvfPqIndex:
-    """IVF-PQ search over an id-range-sharded .qvr (one shard per rank)."""
+    """IVF-PQ search over an id-range-sharded index (one shard per rank).
 
-    def __init__(self, path: str, *, total: int, device: Optional[int] = None, group=None):
+    Built either from a populated .qvr (each rank keeps the entries whose label lies in its id
+    range) or, with :meth:`from_trained`, from a trained .qvr plus each rank's own rows added on
+    its GPU."""
+
+    def __init__(self, path: Optional[str] = None, *, total: int, device: Optional[int] = None,
+                 group=None, local: Optional[IvfPqIndex] = None):
         self.rank, self.world = _world(group)
         self.group = group
         self.device = torch.cuda.current_device() if device is None else int(device)
-        lo, hi = self.rank * total // self.world, (self.rank + 1) * total // self.world
-        self.local = IvfPqIndex.load(path, device=self.device,
-                                     label_range=None if self.world == 1 else (lo, hi))
+        if local is None:
+            lo, hi = shard_range(total, self.rank, self.world)
+            local = IvfPqIndex.load(path, device=self.device,
+                                    label_range=None if self.world == 1 else (lo, hi))
+        self.local = local
         self.total = total
 
+    @classmethod
+    def from_trained(cls, path: str, vectors, labels, *, total: int,
+                     device: Optional[int] = None, group=None) -> "ShardedIvfPqIndex":
+        """Loads trained (empty) state from ``path`` on every rank and adds this rank's rows
+        (``labels`` = their global ids, in id order). Each list's entries of lower ranks are
+        counted so that candidate keys (list << 32 | offset in the full list) equal those of one
+        index holding every row in id order."""
+        rank, world = _world(group)
+        dev = torch.cuda.current_device() if device is None else int(device)
+        local = IvfPqIndex.load(path, device=dev)
+        local.add(vectors, labels)
+        if world > 1:
+            sizes = torch.tensor(local.list_sizes(), dtype=torch.int64, device=f"cuda:{dev}")
+            base = list_bases(sizes, rank, world, group).cpu().numpy().astype(np.uint32)
+            check(lib().qv_ivfpq_set_list_base(local.handle, base.ctypes.data))
+        return cls(total=total, device=dev, group=group, local=local)
+
+    def filter_bitmap(self, allowed) -> Optional[torch.Tensor]:
+        """Device position bitmap of this shard (bit i of word i >> 6 = stored entry i is
+        admitted) for a set of allowed labels, None for no filter. Built once on the host from
+        the shard's stored labels; pass it to :meth:`search_device` to keep it resident."""
+        if allowed is None:
+            return None
+        mask = np.isin(self.local.stored_labels(), _as_labels(allowed))
+        packed = np.packbits(mask, bitorder="little")
+        words = np.zeros(max(1, (mask.size + 63) // 64) * 8, np.uint8)
+        words[:packed.size] = packed
+        return torch.from_numpy(words.view(np.int64)).to(f"cuda:{self.device}")
+
     def search_device(self, queries: torch.Tensor, k: int, nprobe: int = 16,
-                      refine_factor: int = 0):
+                      refine_factor: int = 0, bitmap: Optional[torch.Tensor] = None):
         nq = queries.shape[0]
+        dev = queries.device
+        sp = C.c_void_p(_stream_ptr())
+        bm = bitmap.data_ptr() if bitmap is not None else None
+        if self.world == 1:
+            od = torch.empty((nq, k), dtype=torch.float32, device=dev)
+            ol = torch.empty((nq, k), dtype=torch.int64, device=dev)
+            check(lib().qv_ivfpq_search_device(self.local.handle, queries.data_ptr(), nq, k,
+                                               nprobe, refine_factor, bm, ol.data_ptr(),
+                                               od.data_ptr(), sp))
+            return od, ol
         refine = refine_factor > 0 and bool(self._store_vectors())
         factor = refine_factor if refine else 1
         keep = min(self.total, self.total if factor > self.total // max(k, 1) else k * factor)
-        dev = queries.device
         d = torch.empty((nq, keep), dtype=torch.float32, device=dev)
         key = torch.empty((nq, keep), dtype=torch.int64, device=dev)
         lab = torch.empty((nq, keep), dtype=torch.int64, device=dev)
-        sp = C.c_void_p(_stream_ptr())
         check(lib().qv_ivfpq_candidates_device(self.local.handle, queries.data_ptr(), nq, keep,
-                                               nprobe, None, d.data_ptr(), key.data_ptr(),
+                                               nprobe, bm, d.data_ptr(), key.data_ptr(),
                                                lab.data_ptr(), sp))
-        if self.world > 1:
-            d, key, lab = _merge(_all_gather(d, self.world, self.group),
-                                 _all_gather(key, self.world, self.group),
-                                 _all_gather(lab, self.world, self.group), keep, self.device)
+        d, key, lab = _merge(_all_gather(d, self.world, self.group),
+                             _all_gather(key, self.world, self.group),
+                             _all_gather(lab, self.world, self.group), keep, self.device)
         if not refine:
             return d[:, :k].contiguous(), lab[:, :k].contiguous()
         exact = torch.empty((nq, keep), dtype=torch.float32, device=dev)
         check(lib().qv_ivfpq_refine_device(self.local.handle, queries.data_ptr(), nq, keep,
                                            key.data_ptr(), exact.data_ptr(), sp))
-        if self.world > 1:
-            dist.all_reduce(exact, op=dist.ReduceOp.MIN, group=self.group)
+        dist.all_reduce(exact, op=dist.ReduceOp.MIN, group=self.group)
         od = torch.empty((nq, k), dtype=torch.float32, device=dev)
         ok = torch.empty((nq, k), dtype=torch.int64, device=dev)
         ol = torch.empty((nq, k), dtype=torch.int64, device=dev)
@@ -165,8 +221,10 @@ class ShardedIvfPqIndex:
     def _store_vectors(self) -> int:
         return self.local._info()[0].store_vectors
 
-    def search(self, queries, k: int = 10, nprobe: int = 16, refine_factor: int = 0):
+    def search(self, queries, k: int = 10, nprobe: int = 16, refine_factor: int = 0,
+               filter=None):
         q = _as_matrix(queries, self.local.dim)
         dq = torch.from_numpy(q).to(f"cuda:{self.device}", non_blocking=True)
-        d, lab = self.search_device(dq, int(k), int(nprobe), int(refine_factor))
+        d, lab = self.search_device(dq, int(k), int(nprobe), int(refine_factor),
+                                    self.filter_bitmap(filter))
         return lab.cpu().numpy(), d.cpu().numpy()

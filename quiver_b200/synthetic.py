@@ -68,6 +68,18 @@ def config1(n: int = 1_183_514, nq: int = 10_000):
     return db, q
 
 
+def config2(n: int = 1_000_000, nq: int = 10_000):
+    """IvfPqIndex L2 (nlist 2048, m 32): 1,000,000 x 128 skewed ints like config 0, 10,000 queries;
+    the first 100,000 rows are the training sample."""
+    return skewed_ints(n, 128, 2), skewed_ints(nq, 128, 3)
+
+
+def config3(n: int = 1_183_514, nq: int = 10_000):
+    """IvfPqIndex cosine (nlist 2048, m 25, refine 8): config 1's rows and queries; the first
+    100,000 rows are the training sample."""
+    return config1(n, nq)
+
+
 def config4_chunk(rows: int, chunk_index: int, dim: int = 768):
     """One chunk of config 4 (40M x 768 inner product, 4,096-component mixture, sigma 0.5*||c||)."""
     seed = np.random.SeedSequence(4).spawn(64)[chunk_index]
