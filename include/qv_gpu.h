@@ -12,8 +12,10 @@
  * Host-buffer entry points (no "_device" suffix) take caller-owned host memory that is valid only
  * for the call; they copy inputs to the index's GPU, run there, and copy results back before
  * returning. "_device" entry points take device pointers on the index's GPU plus a cudaStream_t
- * passed as void* (NULL = the calling thread's stream for that device) and return once the work is
- * enqueued. Index state is read-only during searches, so concurrent searches on one index are safe;
+ * passed as void* and return once the work is enqueued: results are ordered like work queued on
+ * that stream. NULL means CUDA's default stream (PyTorch's default stream too); the library then
+ * runs the work on its own stream between two event waits, so it is still ordered after earlier
+ * and before later default-stream work. Index state is read-only during searches, so concurrent searches on one index are safe;
  * add() must not run concurrently with other calls on the same index (the C++ wrapper serializes
  * it with a shared mutex, as the reference does).
  *

@@ -104,8 +104,11 @@ class FlatIndex:
     def __del__(self):
         h = getattr(self, "_h", None)
         if h:
-            lib().qv_flat_destroy(h)
             self._h = None
+            try:
+                lib().qv_flat_destroy(h)
+            except (TypeError, AttributeError):  # interpreter shutdown: module globals are gone
+                pass
 
     def _info(self):
         n, d, m = C.c_size_t(), C.c_size_t(), C.c_uint32()
@@ -189,8 +192,11 @@ class IvfPqIndex:
     def __del__(self):
         h = getattr(self, "_h", None)
         if h:
-            lib().qv_ivfpq_destroy(h)
             self._h = None
+            try:
+                lib().qv_ivfpq_destroy(h)
+            except (TypeError, AttributeError):  # interpreter shutdown: module globals are gone
+                pass
 
     def _info(self):
         p = _native.qv_ivfpq_params()

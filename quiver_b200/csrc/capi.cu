@@ -81,12 +81,44 @@ cudaStream_t thread_stream(int device) {
   return s;
 }
 
-// The caller's stream for a _device entry point, or the thread's own stream when it passes NULL.
-cudaStream_t pick_stream(void* stream, int device) {
-  if (stream == nullptr) return thread_stream(device);
-  keep_pool_memory(device);
-  return static_cast<cudaStream_t>(stream);
-}
+// The stream a _device entry point runs on. A caller's stream is used as it is. NULL means CUDA's
+// default (legacy) stream, as everywhere in the runtime API (it is also PyTorch's default stream);
+// the work then runs on this thread's own stream, ordered after everything already queued on the
+// default stream and before anything queued there after the call (two event waits), which keeps
+// the caller's ordering without running the search itself on the default stream.
+class CallerStream {
+ public:
+  CallerStream(void* stream, int device) {
+    keep_pool_memory(device);
+    st_ = static_cast<cudaStream_t>(stream);
+    if (st_ != nullptr) return;
+    st_ = thread_stream(device);
+    ev_ = thread_event(device);
+    QV_CUDA(cudaEventRecord(ev_, cudaStreamLegacy));
+    QV_CUDA(cudaStreamWaitEvent(st_, ev_, 0));
+  }
+  ~CallerStream() {
+    if (ev_ == nullptr) return;
+    // Also on failure: the default stream then waits for whatever was queued before it.
+    if (cudaEventRecord(ev_, st_) == cudaSuccess) cudaStreamWaitEvent(cudaStreamLegacy, ev_, 0);
+  }
+  CallerStream(const CallerStream&) = delete;
+  CallerStream& operator=(const CallerStream&) = delete;
+  cudaStream_t get() const { return st_; }
+
+ private:
+  static cudaEvent_t thread_event(int device) {
+    thread_local std::map<int, cudaEvent_t> events;
+    auto it = events.find(device);
+    if (it != events.end()) return it->second;
+    cudaEvent_t e = nullptr;
+    QV_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    events[device] = e;
+    return e;
+  }
+  cudaStream_t st_ = nullptr;
+  cudaEvent_t ev_ = nullptr;
+};
 
 int sm_count(int device) {
   static std::mutex mu;
@@ -432,6 +464,9 @@ qv_status qv_flat_add(qv_flat* index, const float* vectors, size_t n, const uint
     h2d(dl, lab.data(), n, st);
     flat_append(s, s.x.get<float>() + s.n * s.dim, dl.get<uint64_t>(), n, st);
     s.host_labels.insert(s.host_labels.end(), lab.begin(), lab.end());
+    // The rows are complete on the device when add() returns, as in the reference, so that a
+    // search on any stream (the _device entry points take the caller's) sees them.
+    QV_CUDA(cudaStreamSynchronize(st));
   });
 }
 
@@ -473,7 +508,8 @@ qv_status qv_flat_search_device(const qv_flat* index, const float* queries, size
     const FlatState& s = index->s;
     std::shared_lock lock(index->mu);
     DeviceScope scope(s.device);
-    cudaStream_t st = pick_stream(stream, s.device);
+    CallerStream call_stream(stream, s.device);
+    cudaStream_t st = call_stream.get();
     flat_search(s, queries, nq, k, position_bitmap, labels, distances, keys, st);
   });
 }
@@ -492,7 +528,8 @@ qv_status qv_flat_search_device_noalloc(const qv_flat* index, const float* queri
     const FlatState& s = index->s;
     std::shared_lock lock(index->mu);
     DeviceScope scope(s.device);
-    cudaStream_t st = pick_stream(stream, s.device);
+    CallerStream call_stream(stream, s.device);
+    cudaStream_t st = call_stream.get();
     flat_search_noalloc(s, queries, nq, k, position_bitmap, labels, distances, keys, st);
   });
 }
@@ -608,6 +645,7 @@ qv_status qv_flat_load(int device, const char* path, int verify_checksums, qv_fl
       flat_append(s, s.x.get<float>(), dl.get<uint64_t>(), meta.count, cs);
       s.metric = metric;
       s.host_labels.assign(l, l + meta.count);
+      QV_CUDA(cudaStreamSynchronize(cs));
     }
     *out = owner.release();
   });
@@ -766,7 +804,8 @@ qv_status qv_ivfpq_search_device(const qv_ivfpq* index, const float* queries, si
     const IvfState& s = index->s;
     std::shared_lock lock(index->mu);
     DeviceScope scope(s.device);
-    cudaStream_t st = pick_stream(stream, s.device);
+    CallerStream call_stream(stream, s.device);
+    cudaStream_t st = call_stream.get();
     ivf_search(s, queries, nq, k, nprobe, refine_factor, position_bitmap, labels, distances, st);
   });
 }
@@ -781,7 +820,8 @@ qv_status qv_ivfpq_candidates_device(const qv_ivfpq* index, const float* queries
     const IvfState& s = index->s;
     std::shared_lock lock(index->mu);
     DeviceScope scope(s.device);
-    cudaStream_t st = pick_stream(stream, s.device);
+    CallerStream call_stream(stream, s.device);
+    cudaStream_t st = call_stream.get();
     ivf_candidates(s, queries, nq, keep, nprobe, position_bitmap, distances, keys, labels, st);
   });
 }
@@ -793,7 +833,8 @@ qv_status qv_ivfpq_refine_device(const qv_ivfpq* index, const float* queries, si
     const IvfState& s = index->s;
     std::shared_lock lock(index->mu);
     DeviceScope scope(s.device);
-    cudaStream_t st = pick_stream(stream, s.device);
+    CallerStream call_stream(stream, s.device);
+    cudaStream_t st = call_stream.get();
     ivf_refine(s, queries, nq, keep, keys, exact, st);
   });
 }
@@ -923,7 +964,8 @@ qv_status qv_merge_topk_device(int device, size_t parts, size_t nq, size_t k,
   return guarded([&] {
     QV_REQUIRE(distances && keys && out_distances, "null argument");
     DeviceScope scope(device);
-    cudaStream_t st = pick_stream(stream, device);
+    CallerStream call_stream(stream, device);
+    cudaStream_t st = call_stream.get();
     merge_topk(parts, nq, k, distances, keys, labels, out_distances, out_keys, out_labels, st);
   });
 }
@@ -936,7 +978,8 @@ qv_status qv_select_topk_device(int device, size_t nq, size_t n, size_t k, const
     QV_REQUIRE(distances && keys && out_distances, "null argument");
     QV_REQUIRE(k <= n || n == 0, "select_topk: k > n");
     DeviceScope scope(device);
-    cudaStream_t st = pick_stream(stream, device);
+    CallerStream call_stream(stream, device);
+    cudaStream_t st = call_stream.get();
     select_topk(nq, n, k, distances, keys, labels, out_distances, out_keys, out_labels, st);
   });
 }

@@ -151,15 +151,16 @@ class ShardedIvfPqIndex:
         self.total = total
 
     @classmethod
-    def from_trained(cls, path: str, vectors, labels, *, total: int,
+    def from_trained(cls, trained, vectors, labels, *, total: int,
                      device: Optional[int] = None, group=None) -> "ShardedIvfPqIndex":
-        """Loads trained (empty) state from ``path`` on every rank and adds this rank's rows
-        (``labels`` = their global ids, in id order). Each list's entries of lower ranks are
-        counted so that candidate keys (list << 32 | offset in the full list) equal those of one
-        index holding every row in id order."""
+        """Starts every rank from trained, empty state (a .qvr path, or an IvfPqIndex already
+        trained on this rank's device) and adds this rank's rows (``labels`` = their global ids,
+        in id order). Each list's entries of lower ranks are counted so that candidate keys
+        (list << 32 | offset in the full list) equal those of one index holding every row in id
+        order."""
         rank, world = _world(group)
         dev = torch.cuda.current_device() if device is None else int(device)
-        local = IvfPqIndex.load(path, device=dev)
+        local = IvfPqIndex.load(trained, device=dev) if isinstance(trained, str) else trained
         local.add(vectors, labels)
         if world > 1:
             sizes = torch.tensor(local.list_sizes(), dtype=torch.int64, device=f"cuda:{dev}")
