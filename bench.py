@@ -342,6 +342,8 @@ def run_ivf(args, rank, world, local):
 
     fname, metric, dim, refine, rows, desc = IVF_WORKLOADS[args.workload]
     db, q = ivf_data(args.workload)
+    q = q[:args.queries]
+    nq = len(q)
     n = len(db)
     lo, hi = rank * n // world, (rank + 1) * n // world
     index = ShardedIvfPqIndex.from_trained(os.path.join(ROOT, "tests", "golden", fname),
@@ -386,7 +388,7 @@ def run_ivf(args, rank, world, local):
         c = torch.tensor([launches], device="cuda", dtype=torch.float64)
         dist.all_reduce(c, op=dist.ReduceOp.SUM)
         launches = int(c[0].item())
-    value = N_Q * args.steps / (elapsed / 1000.0)
+    value = nq * args.steps / (elapsed / 1000.0)
 
     def e2e_call():
         if world == 1:
@@ -414,7 +416,7 @@ def run_ivf(args, rank, world, local):
         "warmup": args.warmup, "ms_per_step": elapsed / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": desc, "nprobe": args.nprobe, "refine_factor": refine,
-                   "filter": "1% ids" if args.filter else None, "global_batch": N_Q, "k": K,
+                   "filter": "1% ids" if args.filter else None, "global_batch": nq, "k": K,
                    "database_rows": n, "parallelism": f"id-range shards x{world}",
                    "l2": "codes (32 MB / 30 MB) are L2-resident; no flush between steps"},
         "gpu_launches": launches,
@@ -423,9 +425,9 @@ def run_ivf(args, rank, world, local):
                      "peak_source": f"{peak_kind} HBM copy", "traffic": None,
                      "avg_launch_ms": avg_ms, "work_per_launch": per_launch},
         "clocks": clocks,
-        "e2e": {"value": N_Q * args.steps / e2e_s, "unit": "QPS",
-                "h2d_bytes_per_step": world * N_Q * dim * 4,
-                "d2h_bytes_per_step": world * N_Q * K * (8 + 4)},
+        "e2e": {"value": nq * args.steps / e2e_s, "unit": "QPS",
+                "h2d_bytes_per_step": world * nq * dim * 4,
+                "d2h_bytes_per_step": world * nq * K * (8 + 4)},
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle.oracle import REF_SO, Reference
@@ -435,7 +437,7 @@ def run_ivf(args, rank, world, local):
             qps, nsamp = cpu_reference_ivf_qps(ref, ix, q, args.nprobe, refine, allowed, 15.0)
             line["cpu_baseline"] = {
                 "value": qps, "unit": "QPS", "cores": ref.threads, "kind": "reference",
-                "sample": f"{nsamp} of the {N_Q} queries, IvfPqIndex::search_batch, "
+                "sample": f"{nsamp} of the {nq} queries, IvfPqIndex::search_batch, "
                           f"{ref.threads} threads, ISA {ref.isa}"}
     if rank == 0:
         print(json.dumps(line), flush=True)

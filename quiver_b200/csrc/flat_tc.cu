@@ -208,24 +208,41 @@ __device__ __forceinline__ float screen_value(float x, float inv) {
   return kL2 ? x : fmaf(-x, inv, 1.0f);
 }
 
-// best[g] = best of v[8g .. 8g+7] (max when kMax, else min), top = best of all 64, as a
-// contiguous pairwise tree (63 operations, depth 6).
+// Three-input max / min (one PTX instruction on sm_100a).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+__device__ __forceinline__ float min3f(float a, float b, float c) {
+  float d;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+template <bool kMax>
+__device__ __forceinline__ float best2(float a, float b) {
+  return kMax ? fmaxf(a, b) : fminf(a, b);
+}
+template <bool kMax>
+__device__ __forceinline__ float best3(float a, float b, float c) {
+  return kMax ? max3f(a, b, c) : min3f(a, b, c);
+}
+
+// best[g] = best of v[8g .. 8g+7] (max when kMax, else min), top = best of all 64, with
+// three-input operations: 4 per 8-element group and 4 for the top (36 in all, depth 3 + 3).
 template <bool kMax>
 __device__ __forceinline__ void group_best8(const float (&v)[64], float (&best)[8], float& top) {
-  float m1[32], m2[16];
 #pragma unroll
-  for (int i = 0; i < 32; ++i) m1[i] = kMax ? fmaxf(v[2 * i], v[2 * i + 1]) : fminf(v[2 * i], v[2 * i + 1]);
-#pragma unroll
-  for (int i = 0; i < 16; ++i) m2[i] = kMax ? fmaxf(m1[2 * i], m1[2 * i + 1]) : fminf(m1[2 * i], m1[2 * i + 1]);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) best[i] = kMax ? fmaxf(m2[2 * i], m2[2 * i + 1]) : fminf(m2[2 * i], m2[2 * i + 1]);
-  const float b0 = kMax ? fmaxf(best[0], best[1]) : fminf(best[0], best[1]);
-  const float b1 = kMax ? fmaxf(best[2], best[3]) : fminf(best[2], best[3]);
-  const float b2 = kMax ? fmaxf(best[4], best[5]) : fminf(best[4], best[5]);
-  const float b3 = kMax ? fmaxf(best[6], best[7]) : fminf(best[6], best[7]);
-  const float c0 = kMax ? fmaxf(b0, b1) : fminf(b0, b1);
-  const float c1 = kMax ? fmaxf(b2, b3) : fminf(b2, b3);
-  top = kMax ? fmaxf(c0, c1) : fminf(c0, c1);
+  for (int g = 0; g < 8; ++g) {
+    const float* e = v + 8 * g;
+    const float x = best3<kMax>(e[0], e[1], e[2]);
+    const float y = best3<kMax>(e[3], e[4], e[5]);
+    best[g] = best3<kMax>(x, y, best2<kMax>(e[6], e[7]));
+  }
+  const float x = best3<kMax>(best[0], best[1], best[2]);
+  const float y = best3<kMax>(best[3], best[4], best[5]);
+  top = best3<kMax>(x, y, best2<kMax>(best[6], best[7]));
 }
 
 // Sorts one query's buffer (its first `cnt` entries; the rest padded with +inf) by

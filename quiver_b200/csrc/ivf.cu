@@ -319,20 +319,86 @@ __device__ void scan_compact(float* bd, uint64_t* bk, uint64_t* bp, int cap, int
   __syncthreads();
 }
 
+// Code bytes of one entry held in registers: words[i] holds bytes 4i..4i+3 of the code.
+// M = 0: the code width is only known at run time; bytes are then read from global memory.
+template <int M>
+struct CodeWords;
+
+template <>
+struct CodeWords<0> {
+  const uint8_t* p;
+  __device__ __forceinline__ void load(const uint8_t* codes, uint64_t pos, int m) {
+    p = codes + pos * static_cast<uint64_t>(m);
+  }
+  __device__ __forceinline__ uint32_t byte(int j) const { return __ldg(p + j); }
+};
+
+template <int M>
+struct CodeWords {
+  static constexpr int kWords = (M + 3) / 4;
+  uint32_t w[kWords];
+  // Loads entry `pos` of a code array with M bytes per entry (16 bytes of slack after the array).
+  __device__ __forceinline__ void load(const uint8_t* codes, uint64_t pos, int /*m*/) {
+    const uint64_t start = pos * M;
+    if constexpr (M % 16 == 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(codes + start);
+#pragma unroll
+      for (int i = 0; i < M / 16; ++i) {
+        const uint4 v = __ldg(src + i);
+        w[4 * i] = v.x;
+        w[4 * i + 1] = v.y;
+        w[4 * i + 2] = v.z;
+        w[4 * i + 3] = v.w;
+      }
+    } else {
+      // Aligned 4-byte loads covering [start, start + M), then a funnel shift per word.
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(codes + (start & ~uint64_t{3}));
+      const uint32_t sh = static_cast<uint32_t>(start & 3) * 8;
+      uint32_t raw[kWords + 1];
+#pragma unroll
+      for (int i = 0; i <= kWords; ++i) raw[i] = __ldg(src + i);
+#pragma unroll
+      for (int i = 0; i < kWords; ++i) w[i] = __funnelshift_r(raw[i], raw[i + 1], sh);
+    }
+  }
+  __device__ __forceinline__ uint32_t byte(int j) const { return (w[j >> 2] >> ((j & 3) * 8)) & 0xffu; }
+};
+
+// ADC sums of two codes at once (two independent dependency chains): each in ascending j from
+// 0.0f with one rounding per addition, as ProductQuantizer::adc (src/product_quantizer.cc:188-217).
+template <int M>
+__device__ __forceinline__ void adc2(const float* table, const CodeWords<M>& c0,
+                                     const CodeWords<M>& c1, int m, float& s0, float& s1) {
+  s0 = 0.0f;
+  s1 = 0.0f;
+  if constexpr (M > 0) {
+#pragma unroll
+    for (int j = 0; j < M; ++j) {
+      s0 = __fadd_rn(s0, table[j * kSubCentroids + c0.byte(j)]);
+      s1 = __fadd_rn(s1, table[j * kSubCentroids + c1.byte(j)]);
+    }
+  } else {
+    for (int j = 0; j < m; ++j) {
+      s0 = __fadd_rn(s0, table[j * kSubCentroids + c0.byte(j)]);
+      s1 = __fadd_rn(s1, table[j * kSubCentroids + c1.byte(j)]);
+    }
+  }
+}
+
 // One block per query: lookup tables in shared memory, then every probed list in probe order.
-// Codes of a list are staged through shared memory with coalesced 16-byte loads; each thread sums
-// one code's m table entries in ascending j from 0.0f (ProductQuantizer::adc, src/
-// product_quantizer.cc:188-217) and forms dist = ip ? 1-(base+s) : base+s
+// Each thread takes two codes per pass, loaded straight from global memory into registers
+// (M = code bytes, a compile-time constant), and sums their m table entries in ascending j from
+// 0.0f (ProductQuantizer::adc, src/product_quantizer.cc:188-217); dist = ip ? 1-(base+s) : base+s
 // (src/ivfpq_index.cc:346). Survivors of the running threshold and the position bitmap go to a
-// block buffer that is compacted to the best `keep`.
+// block buffer that is compacted to the best `keep` after every pass of 2 x kScanThreads codes.
+template <int M>
 __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int ts = a.m * kSubCentroids;
+  const int ts = (M > 0 ? M : a.m) * kSubCentroids;
   float* table = reinterpret_cast<float*>(smem_raw);
   float* qtab = table + ts;                                // L2 precomputed only
   float* qv = qtab + (a.use_pre ? ts : 0);                 // dim (residual scratch for L2)
-  uint8_t* cstage = reinterpret_cast<uint8_t*>(qv + ((a.dim + 3) & ~3));  // kScanThreads x m
-  float* bd = reinterpret_cast<float*>(cstage + ((kScanThreads * a.m + 15) & ~15));
+  float* bd = qv + ((a.dim + 3) & ~3);
   uint64_t* bk = reinterpret_cast<uint64_t*>(bd + a.cap);
   uint64_t* bp = bk + a.cap;
   __shared__ int s_cnt;
@@ -351,17 +417,17 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
   if (a.ip || a.use_pre) {
     float* dst = a.ip ? table : qtab;
     for (int e = tid; e < ts; e += blockDim.x) {
-      const int j = e / kSubCentroids, c = e - j * kSubCentroids;
+      const int j = e / kSubCentroids;
       const float* cbv = a.cb + static_cast<size_t>(e) * a.dsub;
       const float* qs = qv + j * a.dsub;
-      float s = 0.0f;
-      for (int t = 0; t < a.dsub; ++t) s = __fadd_rn(s, __fmul_rn(qs[t], cbv[t]));
-      dst[e] = a.ip ? s : __fmul_rn(s, -2.0f);  // query_table = -2 * ip_table (:316-317)
-      (void)c;
+      float acc = 0.0f;
+      for (int t = 0; t < a.dsub; ++t) acc = __fadd_rn(acc, __fmul_rn(qs[t], cbv[t]));
+      dst[e] = a.ip ? acc : __fmul_rn(acc, -2.0f);  // query_table = -2 * ip_table (:316-317)
     }
   }
   __syncthreads();
 
+  float thr = kInf;
   for (int pi = 0; pi < a.nprobe; ++pi) {
     const uint32_t l = a.probes[q * a.nprobe + pi];
     const uint64_t off = a.offsets[l];
@@ -374,7 +440,7 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
       base = a.probe_d[q * a.nprobe + pi];
       const float* pre = a.pre + static_cast<size_t>(l) * ts;
       __syncthreads();
-      for (int e = tid; e < ts; e += blockDim.x) table[e] = __fadd_rn(pre[e], qtab[e]);
+      for (int e = tid; e < ts; e += blockDim.x) table[e] = __fadd_rn(__ldg(pre + e), qtab[e]);
       __syncthreads();
     } else {
       // Residual L2 table (src/ivfpq_index.cc:339-341 with compute_l2_table).
@@ -384,49 +450,48 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
       for (int e = tid; e < ts; e += blockDim.x) {
         const int j = e / kSubCentroids;
         const float* cbv = a.cb + static_cast<size_t>(e) * a.dsub;
-        float s = 0.0f;
+        float acc = 0.0f;
         for (int t = 0; t < a.dsub; ++t) {
           const int col = j * a.dsub + t;
           const float r = __fsub_rn(qv[col], c[col]);
           const float d = __fsub_rn(r, cbv[t]);
-          s = __fadd_rn(s, __fmul_rn(d, d));
+          acc = __fadd_rn(acc, __fmul_rn(d, d));
         }
-        table[e] = s;
+        table[e] = acc;
       }
       __syncthreads();
     }
     const uint64_t gbase = static_cast<uint64_t>(a.global_base[l]);
-    for (int64_t r0 = 0; r0 < len; r0 += kScanThreads) {
-      const int nr = static_cast<int>(len - r0 < kScanThreads ? len - r0 : kScanThreads);
-      // stage nr codes (nr*m bytes) with 16-byte loads where the source allows it
-      const uint8_t* src = a.codes + (off + r0) * a.m;
-      const int bytes = nr * a.m;
-      __syncthreads();
-      if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-        const int v16 = bytes >> 4;
-        for (int i = tid; i < v16; i += blockDim.x)
-          reinterpret_cast<uint4*>(cstage)[i] = reinterpret_cast<const uint4*>(src)[i];
-        for (int i = (v16 << 4) + tid; i < bytes; i += blockDim.x) cstage[i] = src[i];
-      } else {
-        for (int i = tid; i < bytes; i += blockDim.x) cstage[i] = src[i];
-      }
-      __syncthreads();
-      if (tid < nr) {
-        const uint8_t* code = cstage + tid * a.m;
-        float s = 0.0f;
-        for (int j = 0; j < a.m; ++j) s = __fadd_rn(s, table[j * kSubCentroids + code[j]]);
-        float dist = a.ip ? __fsub_rn(1.0f, __fadd_rn(base, s)) : __fadd_rn(base, s);
+    for (int64_t r0 = 0; r0 < len; r0 += 2 * kScanThreads) {
+      const int64_t i0 = r0 + tid, i1 = r0 + kScanThreads + tid;
+      const bool v0 = i0 < len, v1 = i1 < len;
+      CodeWords<M> c0, c1;
+      c0.load(a.codes, off + (v0 ? i0 : 0), a.m);
+      c1.load(a.codes, off + (v1 ? i1 : 0), a.m);
+      float s0, s1;
+      adc2<M>(table, c0, c1, a.m, s0, s1);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const bool valid = h == 0 ? v0 : v1;
+        const int64_t i = h == 0 ? i0 : i1;
+        const float sum = h == 0 ? s0 : s1;
+        float dist = a.ip ? __fsub_rn(1.0f, __fadd_rn(base, sum)) : __fadd_rn(base, sum);
         dist = dev::nan_to_inf(dist);
-        const uint64_t pos = off + r0 + tid;
-        if (dist <= s_thr && dev::bitmap_test(a.bitmap, pos)) {
+        const uint64_t pos = off + static_cast<uint64_t>(i);
+        if (valid && dist <= thr && dev::bitmap_test(a.bitmap, pos)) {
           const int slot = atomicAdd(&s_cnt, 1);
           bd[slot] = dist;
-          bk[slot] = (static_cast<uint64_t>(l) << 32) | (gbase + static_cast<uint64_t>(r0 + tid));
+          bk[slot] = (static_cast<uint64_t>(l) << 32) | (gbase + static_cast<uint64_t>(i));
           bp[slot] = pos;
         }
       }
+      // Every thread reads the count between two barriers, so no thread appends for the next
+      // pass before all have decided (together) whether to compact.
       __syncthreads();
-      if (s_cnt > a.cap - kScanThreads) scan_compact(bd, bk, bp, a.cap, a.keep, &s_cnt, &s_thr);
+      const int filled = s_cnt;
+      __syncthreads();
+      if (filled > a.cap - 2 * kScanThreads) scan_compact(bd, bk, bp, a.cap, a.keep, &s_cnt, &s_thr);
+      thr = s_thr;
     }
   }
   __syncthreads();
@@ -572,7 +637,7 @@ void run_scan(const IvfState& s, const Prepared& p, size_t nq, size_t keep, size
   a.nprobe = p.nprobe;
   a.keep = static_cast<int>(keep);
   a.k = static_cast<int>(k);
-  a.cap = static_cast<int>(std::max<size_t>(512, next_pow2(keep + kScanThreads)));
+  a.cap = static_cast<int>(std::max<size_t>(1024, next_pow2(keep + 2 * kScanThreads)));
   a.refine = refine;
   a.candidate_mode = candidate_mode;
   a.out_labels = out_labels;
@@ -580,15 +645,26 @@ void run_scan(const IvfState& s, const Prepared& p, size_t nq, size_t keep, size
   a.out_keys = out_keys;
   const size_t ts = s.m * kSubCentroids * sizeof(float);
   const size_t smem = ts * (a.use_pre ? 2 : 1) + ((s.dim + 3) & ~size_t{3}) * sizeof(float) +
-                      ((kScanThreads * s.m + 15) & ~size_t{15}) +
                       a.cap * (sizeof(float) + 2 * sizeof(uint64_t));
   if (smem > 227 * 1024) {
     fail(QV_ERR_UNSUPPORTED,
          "IVF-PQ search: m=" + std::to_string(s.m) + " with keep=" + std::to_string(keep) +
              " needs " + std::to_string(smem) + " bytes of shared memory per query (max 232448)");
   }
-  QV_CUDA(cudaFuncSetAttribute(ivf_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem));
+  // Code widths with a specialized kernel (codes held in registers); others read code bytes from
+  // global memory.
+  void (*kernel)(ScanArgs) = ivf_scan_kernel<0>;
+  switch (s.m) {
+    case 8: kernel = ivf_scan_kernel<8>; break;
+    case 10: kernel = ivf_scan_kernel<10>; break;
+    case 16: kernel = ivf_scan_kernel<16>; break;
+    case 25: kernel = ivf_scan_kernel<25>; break;
+    case 32: kernel = ivf_scan_kernel<32>; break;
+    case 48: kernel = ivf_scan_kernel<48>; break;
+    case 64: kernel = ivf_scan_kernel<64>; break;
+    default: break;
+  }
+  QV_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   // With timing on: the scan's algorithmic bytes are the codes of the probed lists (m bytes
   // each), the lookup-table source per probe (the precomputed slice for L2 with precomputed
   // terms; the codebooks once per query otherwise), the query, and the stored vectors the
@@ -604,7 +680,7 @@ void run_scan(const IvfState& s, const Prepared& p, size_t nq, size_t keep, size
     check_launch("probed_codes_kernel");
   }
   KernelTimer timer(st, "ivf_scan_kernel", 0.0, true);
-  ivf_scan_kernel<<<static_cast<unsigned>(nq), kScanThreads, smem, st>>>(a);
+  kernel<<<static_cast<unsigned>(nq), kScanThreads, smem, st>>>(a);
   timer.stop();
   check_launch("ivf_scan_kernel");
   if (timer.on()) {
@@ -681,7 +757,9 @@ void ivf_upload_lists(IvfState& s, cudaStream_t st) {
                           cudaMemcpyHostToDevice, st));
   QV_CUDA(cudaMemcpyAsync(s.global_base.get(), s.host_global_base.data(),
                           s.nlist * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
-  s.codes.allocate(std::max<size_t>(1, s.count * s.m));
+  // 16 bytes of slack: the scan reads each code with aligned 4- or 16-byte loads that may extend
+  // up to 15 bytes past the last code.
+  s.codes.allocate(s.count * s.m + 16);
   s.labels.allocate(std::max<size_t>(1, s.count) * sizeof(uint64_t));
   if (s.count > 0) {
     QV_CUDA(cudaMemcpyAsync(s.codes.get(), s.host_codes.data(), s.count * s.m,
