@@ -428,20 +428,46 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
   __syncthreads();
 
   float thr = kInf;
+  // With the L2 precomputed terms and a compile-time code width, each thread keeps its M
+  // entries of the next probed list's precomputed slice in registers: they are loaded while the
+  // current list is scanned and only added to the query's table after it.
+  constexpr bool kPrefetch = M > 0;
+  float pf[kPrefetch ? M : 1];
+  auto prefetch = [&](int pi) {
+    if constexpr (kPrefetch) {
+      const uint32_t l = a.probes[q * a.nprobe + pi];
+      const float* pre = a.pre + static_cast<size_t>(l) * ts;
+#pragma unroll
+      for (int i = 0; i < M; ++i) pf[i] = __ldg(pre + tid + i * kScanThreads);
+    }
+  };
+  if (a.use_pre && !a.ip) prefetch(0);
   for (int pi = 0; pi < a.nprobe; ++pi) {
     const uint32_t l = a.probes[q * a.nprobe + pi];
     const uint64_t off = a.offsets[l];
     const int64_t len = static_cast<int64_t>(a.offsets[l + 1] - off);
-    if (len == 0) continue;
+    if (len == 0) {
+      if (kPrefetch && a.use_pre && !a.ip && pi + 1 < a.nprobe) prefetch(pi + 1);
+      continue;
+    }
     float base;
     if (a.ip) {
       base = -a.probe_d[q * a.nprobe + pi];
     } else if (a.use_pre) {
       base = a.probe_d[q * a.nprobe + pi];
-      const float* pre = a.pre + static_cast<size_t>(l) * ts;
       __syncthreads();
-      for (int e = tid; e < ts; e += blockDim.x) table[e] = __fadd_rn(__ldg(pre + e), qtab[e]);
+      if constexpr (kPrefetch) {
+#pragma unroll
+        for (int i = 0; i < M; ++i) {
+          const int e = tid + i * kScanThreads;
+          table[e] = __fadd_rn(pf[i], qtab[e]);
+        }
+      } else {
+        const float* pre = a.pre + static_cast<size_t>(l) * ts;
+        for (int e = tid; e < ts; e += blockDim.x) table[e] = __fadd_rn(__ldg(pre + e), qtab[e]);
+      }
       __syncthreads();
+      if (pi + 1 < a.nprobe) prefetch(pi + 1);
     } else {
       // Residual L2 table (src/ivfpq_index.cc:339-341 with compute_l2_table).
       base = 0.0f;
