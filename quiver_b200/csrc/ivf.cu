@@ -302,14 +302,18 @@ struct ScanArgs {
 };
 
 // Compacts the block buffer to its best `keep` (distance, key) entries; updates the threshold.
+// Sorts only the filled part, rounded up to a power of two (at least `keep`'s).
 __device__ void scan_compact(float* bd, uint64_t* bk, uint64_t* bp, int cap, int keep, int* cnt,
                              float* thr) {
-  for (int i = *cnt + threadIdx.x; i < cap; i += blockDim.x) {
+  int n2 = 1;
+  while (n2 < *cnt || n2 < keep) n2 <<= 1;
+  n2 = min(n2, cap);
+  for (int i = *cnt + threadIdx.x; i < n2; i += blockDim.x) {
     bd[i] = kInf;
     bk[i] = ~0ull;
     bp[i] = ~0ull;
   }
-  dev::block_bitonic_sort<true>(bd, bk, bp, cap);
+  dev::block_bitonic_sort<true>(bd, bk, bp, n2);
   if (threadIdx.x == 0) {
     if (*cnt >= keep) {
       *cnt = keep;
@@ -512,11 +516,14 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
         }
       }
       // Every thread reads the count between two barriers, so no thread appends for the next
-      // pass before all have decided (together) whether to compact.
+      // pass before all have decided (together) whether to compact. The first compaction comes
+      // as soon as 8 x `keep` entries are held (the keep-th best of those is already a useful
+      // threshold), which gives small-keep scans a finite threshold after their first pass.
       __syncthreads();
       const int filled = s_cnt;
       __syncthreads();
-      if (filled > a.cap - 2 * kScanThreads) scan_compact(bd, bk, bp, a.cap, a.keep, &s_cnt, &s_thr);
+      if (filled > a.cap - 2 * kScanThreads || (thr == kInf && filled >= 8 * a.keep))
+        scan_compact(bd, bk, bp, a.cap, a.keep, &s_cnt, &s_thr);
       thr = s_thr;
     }
   }
