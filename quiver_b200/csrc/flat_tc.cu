@@ -62,7 +62,6 @@ struct Args {
   uint32_t* cand_r;
   int* cand_n;
   unsigned* thr_bits;
-  unsigned* slots;  // nq x n_chunks: each unit's published rank-r distance (ordered bits)
   float* gbest;     // nq x kKK: the kKK best distances output by the query's finished units
   int* glock;       // nq: try-lock guarding gbest[q]
   int* err;
@@ -171,6 +170,22 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
+// Starts a 64-column TMEM load (32 lanes x 64 columns, one value per column for this thread's
+// lane); the registers are valid only after tmem_wait_ld.
+__device__ __forceinline__ void tmem_ld64_issue(uint32_t taddr, uint32_t (&r)[64]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr));
+}
+// Waits for this thread's TMEM loads. The registers of the load being waited for pass through
+// the statement, so that no use of them is scheduled above the wait.
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[64]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]), "+r"(r[32]), "+r"(r[33]), "+r"(r[34]), "+r"(r[35]), "+r"(r[36]), "+r"(r[37]), "+r"(r[38]), "+r"(r[39]), "+r"(r[40]), "+r"(r[41]), "+r"(r[42]), "+r"(r[43]), "+r"(r[44]), "+r"(r[45]), "+r"(r[46]), "+r"(r[47]), "+r"(r[48]), "+r"(r[49]), "+r"(r[50]), "+r"(r[51]), "+r"(r[52]), "+r"(r[53]), "+r"(r[54]), "+r"(r[55]), "+r"(r[56]), "+r"(r[57]), "+r"(r[58]), "+r"(r[59]), "+r"(r[60]), "+r"(r[61]), "+r"(r[62]), "+r"(r[63])
+               :
+               : "memory");
+}
 __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   float (&lo)[32] = *reinterpret_cast<float(*)[32]>(v);
   float (&hi)[32] = *reinterpret_cast<float(*)[32]>(v + 32);
@@ -245,18 +260,14 @@ __device__ __forceinline__ void group_best8(const float (&v)[64], float (&best)[
   top = best3<kMax>(x, y, best2<kMax>(best[6], best[7]));
 }
 
-// Sorts one query's buffer (its first `cnt` entries; the rest padded with +inf) by
-// (distance, row), keeps the best kKK and tightens the threshold to the kKK-th distance when the
-// buffer holds that many. Entry i lives at i*kM. Called by all 32 lanes of a warp together (each
-// lane sorts its own column), so the network below runs without divergence.
-__device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, float& thr) {
-  for (int i = cnt; i < kCap; ++i) {
-    d[i * kM] = __int_as_float(0x7f800000);
-    r[i * kM] = 0xffffffffu;
-  }
-  for (int size = 2; size <= kCap; size <<= 1) {
+// Per-lane candidate lists: entry i of a query's list lives at i * kM (the lanes of a warp hold
+// adjacent queries, so their accesses never share a bank). Sorting is a bitonic network over
+// `n` (a power of two) entries by (distance, row); each lane sorts its own list, so the warp runs
+// the network without divergence.
+__device__ __noinline__ void sort_lane(float* d, uint32_t* r, int n) {
+  for (int size = 2; size <= n; size <<= 1) {
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = 0; i < kCap / 2; ++i) {
+      for (int i = 0; i < n / 2; ++i) {
         const int lo = 2 * i - (i & (stride - 1));
         const int hi = lo + stride;
         const bool up = (lo & size) == 0;
@@ -272,10 +283,53 @@ __device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, flo
       }
     }
   }
-  if (cnt >= kKK) {
-    cnt = kKK;
-    thr = fminf(thr, d[(kKK - 1) * kM]);
+}
+
+// Keeps the best kKK of a query's list. Layout: entries [0, sorted) are sorted, [sorted, cnt)
+// were appended since. Until the list has held kKK entries the whole buffer is sorted; after that
+// the sorted prefix is exactly kKK long, so only the appended part (at most kCap - kKK entries)
+// is sorted and then merged with the prefix (from the back, which never overwrites an unread
+// entry). Once kKK entries are kept, the threshold tightens to the kKK-th distance.
+__device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& sorted, int& cnt,
+                                            float& thr) {
+  const float inf = __int_as_float(0x7f800000);
+  if (cnt > sorted) {
+    for (int i = cnt; i < kCap; ++i) {
+      d[i * kM] = inf;
+      r[i * kM] = 0xffffffffu;
+    }
+    if (sorted < kKK) {
+      sort_lane(d, r, kCap);
+      cnt = min(cnt, kKK);
+    } else {
+      float* bd = d + kKK * kM;
+      uint32_t* br = r + kKK * kM;
+      const int nb = cnt - kKK;
+      sort_lane(bd, br, kCap - kKK);
+      int ia = 0, ib = 0;  // how many of the prefix / the appended part are among the best kKK
+      for (int o = 0; o < kKK; ++o) {
+        const bool take_b =
+            ib < nb && dev::key_less(bd[ib * kM], br[ib * kM], d[ia * kM], r[ia * kM]);
+        ib += take_b ? 1 : 0;
+        ia += take_b ? 0 : 1;
+      }
+      int pa = ia - 1, pb = ib - 1;
+      for (int o = kKK - 1; o >= 0; --o) {
+        const bool take_b =
+            pb >= 0 && (pa < 0 || dev::key_less(d[pa * kM], r[pa * kM], bd[pb * kM], br[pb * kM]));
+        const int ja = max(pa, 0), jb = max(pb, 0);
+        const float dv = take_b ? bd[jb * kM] : d[ja * kM];
+        const uint32_t rv = take_b ? br[jb * kM] : r[ja * kM];
+        d[o * kM] = dv;
+        r[o * kM] = rv;
+        pb -= take_b ? 1 : 0;
+        pa -= take_b ? 0 : 1;
+      }
+      cnt = kKK;
+    }
+    sorted = cnt;
   }
+  if (cnt >= kKK) thr = fminf(thr, d[(kKK - 1) * kM]);
 }
 
 template <int kAtoms, bool kL2>
@@ -424,13 +478,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue: thread = query ----------------
-    // Each query keeps an unsorted candidate buffer of kCap (distance, row) entries in shared
-    // memory. Per 64 columns: one pairwise tree gives the best score of each 8-column group and
-    // of all 64; the warp skips the 64 columns when no lane can improve on its threshold (the
-    // common case). Otherwise it visits only the 8-column groups some lane can improve on, and
-    // lanes append their survivors. When any lane's buffer could overflow, the warp compacts
-    // together: every lane sorts its buffer and keeps the best kKK, which also tightens its
-    // threshold to the kKK-th distance.
+    // Each query keeps a candidate list of kCap (distance, row) entries in shared memory (sorted
+    // best-kKK prefix + entries appended since). Per 64 columns: one three-input max/min tree
+    // gives the best score of each 8-column group and of all 64; the warp skips the 64 columns
+    // when no lane can improve on its threshold (the common case). Otherwise it visits only the
+    // 8-column groups some lane can improve on, and lanes append their survivors at positions
+    // from a prefix population count. When any lane's list could overflow, the warp compacts
+    // together, which tightens every full list's threshold to its kKK-th distance.
     const int quarter = warp & 3;
     const int qi = quarter * 32 + lane;
     float* bd = buf_d + qi;
@@ -438,11 +492,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float kInfF = __int_as_float(0x7f800000);
     int accb = 0;
     uint32_t acc_phase = 0;
-    // Units of one query tile run concurrently (query-tile-major order). Each publishes, after
-    // every compaction, its r_pub-th best distance into slots[q][chunk]; once every unit of the
-    // query has published, the union of their outputs holds >= n_chunks * r_pub >= kKK
-    // candidates no farther than the largest slot, so that value bounds every unit's threshold.
-    const int r_pub = (kKK + a.n_chunks - 1) / a.n_chunks;
     for (int u = blockIdx.x; u < a.total_units; u += gridDim.x) {
       int qtile, chunk;
       unit_coords(a, u, qtile, chunk);
@@ -451,74 +500,98 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
       const int q = qtile * kM + qi;
       const bool active = q < a.nq;
-      float thr = active ? dev::from_ordered_bits(a.thr_bits[q]) : -kInfF;
+      const unsigned* qthr = a.thr_bits + (active ? q : 0);
+      float thr = active ? dev::from_ordered_bits(*qthr) : -kInfF;
       const float inv = active ? a.qscale_inv[q] : 0.0f;
       const float qn = (active && kL2) ? a.qnorm2[q] : 0.0f;
-      unsigned* qslots = a.slots + static_cast<size_t>(active ? q : 0) * a.n_chunks;
-      int cnt = 0;
+      int cnt = 0, sorted = 0;
       bool ok = true;
-      for (int t = 0; t < ntiles; ++t) {
+      // One 64-column group of a tile: rows cb .. cb + 63 (cb a multiple of 64: chunks are
+      // multiples of kN rows).
+      auto group = [&](uint32_t (&r)[64], int64_t cb) {
+        float (&v)[64] = *reinterpret_cast<float(*)[64]>(r);  // the loaded bits, used in place
+        const int valid = static_cast<int>(r1 - cb < 64 ? r1 - cb : 64);  // rows of this chunk
+        // best[g]: the best score among elements 8g..8g+7 (max inner product for cosine/IP,
+        // min distance for L2); top: the best of all 64.
+        float best[8];
+        float top;
+        if (kL2) {
+          // v[j] := ||q||^2 + ||x||^2 - 2<q,x>; columns past the chunk end become +inf.
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            const float xn = j < valid ? a.xnorm2[cb + j] : 0.0f;
+            v[j] = j < valid ? fmaf(-2.0f * inv, v[j], qn + xn) : kInfF;
+          }
+          group_best8<false>(v, best, top);
+        } else {
+          if (valid < 64) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j)
+              if (j >= valid) v[j] = -kInfF;
+          }
+          group_best8<true>(v, best, top);
+        }
+        const bool may = active && screen_value<kL2>(top, inv) <= thr;
+        if (!__any_sync(0xffffffffu, may)) return;
+        // Only rows of this chunk that the filter admits are ever appended (columns past the
+        // chunk end can pass the test while the threshold is still +inf).
+        uint64_t allowed = valid >= 64 ? ~0ull : (valid > 0 ? (1ull << valid) - 1 : 0ull);
+        if (a.bitmap != nullptr && valid > 0) allowed &= a.bitmap[static_cast<uint64_t>(cb) >> 6];
+        // Which 8-column groups this lane can improve on, and their union over the warp.
+        uint32_t gm = 0;
+#pragma unroll
+        for (int g = 0; g < 8; ++g)
+          gm |= (may && screen_value<kL2>(best[g], inv) <= thr) ? (1u << g) : 0u;
+        const uint32_t wm = __reduce_or_sync(0xffffffffu, gm);
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          if (!((wm >> g) & 1u)) continue;  // warp-uniform
+          bool sub = (gm >> g) & 1u;
+          // Compact (all lanes together) when some lane's 8 new entries might not fit.
+          if (__any_sync(0xffffffffu, sub && cnt > kCap - 8)) {
+            compact_buffer(bd, br, sorted, cnt, thr);
+            sub = sub && screen_value<kL2>(best[g], inv) <= thr;
+          }
+          uint32_t m8 = 0;
+          if (sub) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int e = 8 * g + j;
+              m8 |= (screen_value<kL2>(v[e], inv) <= thr && ((allowed >> e) & 1ull)) ? (1u << j)
+                                                                                     : 0u;
+            }
+          }
+          if (m8 != 0) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              if ((m8 >> j) & 1u) {
+                const int pos = cnt + __popc(m8 & ((1u << j) - 1u));
+                bd[pos * kM] = screen_value<kL2>(v[8 * g + j], inv);
+                br[pos * kM] = static_cast<uint32_t>(cb + 8 * g + j);
+              }
+            }
+            cnt += __popc(m8);
+          }
+        }
+      };
+      // The TMEM loads run one 64-column group ahead of the processing: a group's values are
+      // being loaded while the previous group is screened.
+      uint32_t ra[64], rb[64];
+      if (ntiles > 0) {
         ok = mbar_wait(bar(ACC_FULL + accb), acc_phase, abort_flag, a.err);
         if (!ok) break;
         tc_fence_after();
+        tmem_ld64_issue(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(accb * kN), ra);
+        tmem_wait_ld(ra);
+      }
+      unsigned fresh = ~0u;  // the query's shared threshold, read early and applied later
+      for (int t = 0; t < ntiles; ++t) {
         const int64_t row0 = r0 + static_cast<int64_t>(t) * kN;
-        for (int h = 0; h < kN / 64; ++h) {
-          float v[64];
-          tmem_ld64(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                        static_cast<uint32_t>(accb * kN + h * 64),
-                    v);
-          const int64_t cb = row0 + h * 64;  // a multiple of 64: chunks are multiples of kN rows
-          const int valid = static_cast<int>(r1 - cb < 64 ? r1 - cb : 64);  // rows of this chunk
-          // best[g]: the best score among elements 8g..8g+7 (max inner product for cosine/IP,
-          // min distance for L2), from a contiguous pairwise tree; top: the best of all 64.
-          float best[8];
-          float top;
-          if (kL2) {
-            // v[j] := ||q||^2 + ||x||^2 - 2<q,x>; columns past the chunk end become +inf.
-#pragma unroll
-            for (int j = 0; j < 64; ++j) {
-              const float xn = j < valid ? a.xnorm2[cb + j] : 0.0f;
-              v[j] = j < valid ? fmaf(-2.0f * inv, v[j], qn + xn) : kInfF;
-            }
-            group_best8<false>(v, best, top);
-          } else {
-            if (valid < 64) {
-#pragma unroll
-              for (int j = 0; j < 64; ++j)
-                if (j >= valid) v[j] = -kInfF;
-            }
-            group_best8<true>(v, best, top);
-          }
-          const bool may = active && screen_value<kL2>(top, inv) <= thr;
-          if (!__any_sync(0xffffffffu, may)) continue;
-          const uint64_t allowed =
-              a.bitmap != nullptr ? a.bitmap[static_cast<uint64_t>(cb) >> 6] : ~0ull;
-          // Survivor path, 8 rows at a time, entered only for groups some lane can improve on.
-#pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            bool sub = may && screen_value<kL2>(best[g], inv) <= thr;
-            if (!__any_sync(0xffffffffu, sub)) continue;
-            // Compact (all lanes together) when some lane's 8 new entries might not fit.
-            if (__any_sync(0xffffffffu, sub && cnt > kCap - 8)) {
-              compact_buffer(bd, br, cnt, thr);
-              if (active && cnt >= r_pub)
-                atomicMin(qslots + chunk, dev::ordered_bits(bd[(r_pub - 1) * kM]));
-              sub = sub && screen_value<kL2>(best[g], inv) <= thr;
-            }
-            if (sub) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int e = 8 * g + j;
-                const float d = screen_value<kL2>(v[e], inv);
-                if (d <= thr && ((allowed >> e) & 1ull)) {
-                  bd[cnt * kM] = d;
-                  br[cnt * kM] = static_cast<uint32_t>(cb + e);
-                  ++cnt;
-                }
-              }
-            }
-          }
-        }
+        if ((t & 7) == 0 && active) fresh = *reinterpret_cast<const volatile unsigned*>(qthr);
+        tmem_ld64_issue(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(accb * kN + 64), rb);
+        group(ra, row0);
+        tmem_wait_ld(rb);
+        // Tile t is out of TMEM: hand its accumulator back to the MMA warp.
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(ACC_EMPTY + accb));
@@ -526,18 +599,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           accb = 0;
           acc_phase ^= 1;
         }
-        // Tighten with the bound from all units of this query and with finished units' values.
-        if ((t & 7) == 7 && active) {
-          unsigned worst = 0u;
-          for (int c2 = 0; c2 < a.n_chunks; ++c2)
-            worst = max(worst, *reinterpret_cast<volatile unsigned*>(qslots + c2));
-          thr = fminf(thr, dev::from_ordered_bits(worst));
-          thr = fminf(thr, dev::from_ordered_bits(
-                               *reinterpret_cast<volatile unsigned*>(a.thr_bits + q)));
+        const bool more = t + 1 < ntiles;
+        if (more) {
+          ok = mbar_wait(bar(ACC_FULL + accb), acc_phase, abort_flag, a.err);
+          if (!ok) break;
+          tc_fence_after();
+          tmem_ld64_issue(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(accb * kN), ra);
         }
+        group(rb, row0 + 64);
+        if (more) tmem_wait_ld(ra);
+        // Tighten with the query's bound from finished units (loaded 7 tiles ago).
+        if ((t & 7) == 7) thr = fminf(thr, dev::from_ordered_bits(fresh));
       }
       if (!ok) break;
-      compact_buffer(bd, br, cnt, thr);
+      compact_buffer(bd, br, sorted, cnt, thr);
       if (active) {
         const size_t slot = static_cast<size_t>(q) * a.n_chunks + chunk;
         for (int i = 0; i < cnt; ++i) {
@@ -545,32 +620,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           a.cand_r[slot * kKK + i] = br[i * kM];
         }
         a.cand_n[slot] = cnt;
-        if (cnt >= r_pub) atomicMin(qslots + chunk, dev::ordered_bits(bd[(r_pub - 1) * kM]));
         if (cnt == kKK) atomicMin(a.thr_bits + q, dev::ordered_bits(bd[(kKK - 1) * kM]));
         // Merge this unit's output into the query's running best-kKK list and publish its kKK-th
         // value as the query's threshold: kKK distinct output candidates lie at or below it, which
         // is all a threshold needs. Each unit merges once (its rows are disjoint from every other
         // unit's), under a try-lock: when another unit holds it the merge is skipped, which only
-        // leaves the bound looser.
+        // leaves the bound looser. The list is staged in the free upper half of this query's
+        // buffer, so that all its loads are issued at once.
         if (cnt > 0 && atomicCAS(a.glock + q, 0, 1) == 0) {
           __threadfence();
           volatile float* gq = a.gbest + static_cast<size_t>(q) * kKK;
-          float merged[kKK];
-          int gi = 0, bi = 0;
+          float* gs = bd + kKK * kM;
 #pragma unroll
+          for (int o = 0; o < kKK; ++o) gs[o * kM] = gq[o];
+          int gi = 0, bi = 0;
+          float kth = kInfF;
           for (int o = 0; o < kKK; ++o) {
-            const float gv = gi < kKK ? gq[gi] : kInfF;
+            const float gv = gi < kKK ? gs[gi * kM] : kInfF;
             const float bv = bi < cnt ? bd[bi * kM] : kInfF;
             const bool take_b = bv < gv;
-            merged[o] = take_b ? bv : gv;
+            kth = take_b ? bv : gv;
+            gq[o] = kth;
             bi += take_b ? 1 : 0;
             gi += take_b ? 0 : 1;
           }
-#pragma unroll
-          for (int o = 0; o < kKK; ++o) gq[o] = merged[o];
           __threadfence();
-          if (merged[kKK - 1] < kInfF)
-            atomicMin(a.thr_bits + q, dev::ordered_bits(merged[kKK - 1]));
+          if (kth < kInfF) atomicMin(a.thr_bits + q, dev::ordered_bits(kth));
           atomicExch(a.glock + q, 0);
         }
       }
@@ -808,9 +883,6 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   // together, sharing thresholds); the default row-chunk-major order shares row chunks in L2.
   const char* order = std::getenv("QV_FLAT_TC_ORDER");
   a.qmajor = order != nullptr && order[0] == 'q';
-  DeviceBuffer slots(nq * static_cast<size_t>(n_chunks) * sizeof(unsigned), st);
-  QV_CUDA(cudaMemsetAsync(slots.get(), 0xff, slots.bytes(), st));  // ~0u: larger than any bound
-  a.slots = slots.get<unsigned>();
   DeviceBuffer gbest(nq * tc::kKK * sizeof(float), st), glock(nq * sizeof(int), st);
   tc::fill_inf_kernel<<<ceil_div(nq * tc::kKK, 256), 256, 0, st>>>(gbest.get<float>(),
                                                                    nq * tc::kKK);
