@@ -261,75 +261,70 @@ __device__ __forceinline__ void group_best8(const float (&v)[64], float (&best)[
 }
 
 // Per-lane candidate lists: entry i of a query's list lives at i * kM (the lanes of a warp hold
-// adjacent queries, so their accesses never share a bank). Sorting is a bitonic network over
-// `n` (a power of two) entries by (distance, row); each lane sorts its own list, so the warp runs
-// the network without divergence.
-__device__ __noinline__ void sort_lane(float* d, uint32_t* r, int n) {
-  for (int size = 2; size <= n; size <<= 1) {
+// adjacent queries, so their accesses never share a bank). A list is a sorted prefix of exactly
+// kKK entries (padded with (+inf, ~0) at the start of a work unit) followed by up to
+// kCap - kKK entries appended since.
+constexpr int kAppend = kCap - kKK;
+
+// Sorts the kAppend appended entries by (distance, row): a fully unrolled bitonic network, each
+// lane on its own list (no divergence), so the loads of one stage's independent
+// compare-exchanges overlap.
+__device__ __noinline__ void sort_appended(float* d, uint32_t* r) {
+#pragma unroll
+  for (int size = 2; size <= kAppend; size <<= 1) {
+#pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = 0; i < n / 2; ++i) {
+#pragma unroll
+      for (int i = 0; i < kAppend / 2; ++i) {
         const int lo = 2 * i - (i & (stride - 1));
         const int hi = lo + stride;
         const bool up = (lo & size) == 0;
         const float dl = d[lo * kM], dh = d[hi * kM];
         const uint32_t rl = r[lo * kM], rh = r[hi * kM];
         const bool swap = up ? dev::key_less(dh, rh, dl, rl) : dev::key_less(dl, rl, dh, rh);
-        if (swap) {
-          d[lo * kM] = dh;
-          d[hi * kM] = dl;
-          r[lo * kM] = rh;
-          r[hi * kM] = rl;
-        }
+        d[lo * kM] = swap ? dh : dl;
+        d[hi * kM] = swap ? dl : dh;
+        r[lo * kM] = swap ? rh : rl;
+        r[hi * kM] = swap ? rl : rh;
       }
     }
   }
 }
 
-// Keeps the best kKK of a query's list. Layout: entries [0, sorted) are sorted, [sorted, cnt)
-// were appended since. Until the list has held kKK entries the whole buffer is sorted; after that
-// the sorted prefix is exactly kKK long, so only the appended part (at most kCap - kKK entries)
-// is sorted and then merged with the prefix (from the back, which never overwrites an unread
-// entry). Once kKK entries are kept, the threshold tightens to the kKK-th distance.
-__device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& sorted, int& cnt,
-                                            float& thr) {
-  const float inf = __int_as_float(0x7f800000);
-  if (cnt > sorted) {
+// Keeps the best kKK of a query's list: sorts the appended part and merges it into the sorted
+// prefix from the back (which never overwrites an entry not yet read). The threshold then tightens
+// to the kKK-th distance (+inf while fewer than kKK real entries were seen).
+__device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, float& thr) {
+  if (cnt > kKK) {
     for (int i = cnt; i < kCap; ++i) {
-      d[i * kM] = inf;
+      d[i * kM] = __int_as_float(0x7f800000);
       r[i * kM] = 0xffffffffu;
     }
-    if (sorted < kKK) {
-      sort_lane(d, r, kCap);
-      cnt = min(cnt, kKK);
-    } else {
-      float* bd = d + kKK * kM;
-      uint32_t* br = r + kKK * kM;
-      const int nb = cnt - kKK;
-      sort_lane(bd, br, kCap - kKK);
-      int ia = 0, ib = 0;  // how many of the prefix / the appended part are among the best kKK
-      for (int o = 0; o < kKK; ++o) {
-        const bool take_b =
-            ib < nb && dev::key_less(bd[ib * kM], br[ib * kM], d[ia * kM], r[ia * kM]);
-        ib += take_b ? 1 : 0;
-        ia += take_b ? 0 : 1;
-      }
-      int pa = ia - 1, pb = ib - 1;
-      for (int o = kKK - 1; o >= 0; --o) {
-        const bool take_b =
-            pb >= 0 && (pa < 0 || dev::key_less(d[pa * kM], r[pa * kM], bd[pb * kM], br[pb * kM]));
-        const int ja = max(pa, 0), jb = max(pb, 0);
-        const float dv = take_b ? bd[jb * kM] : d[ja * kM];
-        const uint32_t rv = take_b ? br[jb * kM] : r[ja * kM];
-        d[o * kM] = dv;
-        r[o * kM] = rv;
-        pb -= take_b ? 1 : 0;
-        pa -= take_b ? 0 : 1;
-      }
-      cnt = kKK;
+    float* bd = d + kKK * kM;
+    uint32_t* br = r + kKK * kM;
+    const int nb = cnt - kKK;
+    sort_appended(bd, br);
+    int ia = 0, ib = 0;  // how many of the prefix / the appended part are among the best kKK
+    for (int o = 0; o < kKK; ++o) {
+      const bool take_b = ib < nb && dev::key_less(bd[ib * kM], br[ib * kM], d[ia * kM], r[ia * kM]);
+      ib += take_b ? 1 : 0;
+      ia += take_b ? 0 : 1;
     }
-    sorted = cnt;
+    int pa = ia - 1, pb = ib - 1;
+    for (int o = kKK - 1; o >= 0; --o) {
+      const int ja = max(pa, 0), jb = max(pb, 0);
+      const bool take_b =
+          pb >= 0 && (pa < 0 || dev::key_less(d[ja * kM], r[ja * kM], bd[jb * kM], br[jb * kM]));
+      const float dv = take_b ? bd[jb * kM] : d[ja * kM];
+      const uint32_t rv = take_b ? br[jb * kM] : r[ja * kM];
+      d[o * kM] = dv;
+      r[o * kM] = rv;
+      pb -= take_b ? 1 : 0;
+      pa -= take_b ? 0 : 1;
+    }
+    cnt = kKK;
   }
-  if (cnt >= kKK) thr = fminf(thr, d[(kKK - 1) * kM]);
+  thr = fminf(thr, d[(kKK - 1) * kM]);
 }
 
 template <int kAtoms, bool kL2>
@@ -504,7 +499,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       float thr = active ? dev::from_ordered_bits(*qthr) : -kInfF;
       const float inv = active ? a.qscale_inv[q] : 0.0f;
       const float qn = (active && kL2) ? a.qnorm2[q] : 0.0f;
-      int cnt = 0, sorted = 0;
+      // Start from a prefix of kKK (+inf, ~0) entries; `seen` counts the real entries appended.
+#pragma unroll
+      for (int i = 0; i < kKK; ++i) {
+        bd[i * kM] = kInfF;
+        br[i * kM] = 0xffffffffu;
+      }
+      int cnt = kKK, seen = 0;
       bool ok = true;
       // One 64-column group of a tile: rows cb .. cb + 63 (cb a multiple of 64: chunks are
       // multiples of kN rows).
@@ -549,7 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           bool sub = (gm >> g) & 1u;
           // Compact (all lanes together) when some lane's 8 new entries might not fit.
           if (__any_sync(0xffffffffu, sub && cnt > kCap - 8)) {
-            compact_buffer(bd, br, sorted, cnt, thr);
+            compact_buffer(bd, br, cnt, thr);
             sub = sub && screen_value<kL2>(best[g], inv) <= thr;
           }
           uint32_t m8 = 0;
@@ -571,6 +572,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             cnt += __popc(m8);
+            seen += __popc(m8);
           }
         }
       };
@@ -612,7 +614,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if ((t & 7) == 7) thr = fminf(thr, dev::from_ordered_bits(fresh));
       }
       if (!ok) break;
-      compact_buffer(bd, br, sorted, cnt, thr);
+      compact_buffer(bd, br, cnt, thr);
+      cnt = min(seen, kKK);  // the real entries: they sort before the padding
       if (active) {
         const size_t slot = static_cast<size_t>(q) * a.n_chunks + chunk;
         for (int i = 0; i < cnt; ++i) {
