@@ -276,12 +276,18 @@ __global__ void __launch_bounds__(128) flat_screen_simt_kernel(
 
 // ---- finalize: merge, exact rerank, certificate ------------------------------------------------------
 
+// Candidates are rows (group_rows == 1, the SIMT screen) or groups of group_rows consecutive rows
+// (the tensor-core screen), each with the best screen distance among its admitted rows. The kk
+// best candidates are kept (their kk-th screen value is T); group candidates are expanded into
+// their admitted rows, and every kept row is recomputed exactly in the reference's order. Any row
+// left out has screen distance >= T, so T - eps >= (k-th exact distance) certifies the result.
 __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
     const float* __restrict__ qp, int dpad, const float* __restrict__ eps_q, int nq,
-    const float* __restrict__ x, int dim, const uint64_t* __restrict__ labels, uint64_t row_offset,
+    const float* __restrict__ x, int dim, int64_t nrows, const uint64_t* __restrict__ bitmap,
+    const uint64_t* __restrict__ labels, uint64_t row_offset,
     bool l2, const float* __restrict__ cand_d,
     const uint32_t* __restrict__ cand_r, const int* __restrict__ cand_n, int n_chunks, int kk,
-    int pool, int k, uint64_t* __restrict__ out_labels, float* __restrict__ out_d,
+    int group_rows, int pool, int k, uint64_t* __restrict__ out_labels, float* __restrict__ out_d,
     uint64_t* __restrict__ out_keys, int* __restrict__ fail_count, int* __restrict__ fail_q,
     float* __restrict__ fail_dk) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -311,14 +317,31 @@ __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
   }
   dev::block_bitonic_sort<false>(sd, sk, nullptr, pool);
   const int total = s_total;
-  const int m = min(total, kk);
   const float T = total >= kk ? sd[kk - 1] : kInf;
+  int m = min(total, kk);
   __syncthreads();
+  if (group_rows > 1) {
+    // Expand the m best groups into their rows; rows past the index or rejected by the filter
+    // become (+inf, ~0). The group ids move to registers first (m <= kk <= blockDim.x).
+    const uint64_t gid = threadIdx.x < m ? sk[threadIdx.x] : 0;
+    __syncthreads();
+    if (threadIdx.x < m) {
+      for (int j = 0; j < group_rows; ++j) {
+        const uint64_t row = gid * static_cast<uint64_t>(group_rows) + j;
+        const bool in = row < static_cast<uint64_t>(nrows) && dev::bitmap_test(bitmap, row);
+        sd[threadIdx.x * group_rows + j] = in ? 0.0f : kInf;
+        sk[threadIdx.x * group_rows + j] = in ? row : ~0ull;
+      }
+    }
+    m *= group_rows;
+    __syncthreads();
+  }
   // Exact rerank of the m best (reference AVX2 order), one warp per candidate.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const float* qrow = qp + static_cast<size_t>(q) * dpad;
   for (int i = warp; i < m; i += nwarps) {
     const uint64_t row = sk[i];
+    if (row == ~0ull) continue;  // an expanded slot without an admitted row
     const float e = dev::nan_to_inf(dev::warp_exact_distance(qrow, x + row * dim, dim, l2, lane));
     if (lane == 0) sd[i] = e;
   }
@@ -343,7 +366,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
   }
   for (int j = threadIdx.x; j < k; j += blockDim.x) {
     const size_t o = static_cast<size_t>(q) * k + j;
-    if (j < m) {
+    if (j < m && sk[j] != ~0ull) {
       out_d[o] = sd[j];
       out_labels[o] = labels[sk[j]];
       if (out_keys) out_keys[o] = row_offset + sk[j];
@@ -626,7 +649,10 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
     timer.finish();
   }
 
-  const int pool = static_cast<int>(next_pow2(static_cast<size_t>(n_chunks) * kk));
+  // The tensor-core screen keeps 8-row groups; the finalize expands the kk best into rows.
+  const int group_rows = tensor ? kTcGroupRows : 1;
+  const int pool = static_cast<int>(std::max(next_pow2(static_cast<size_t>(n_chunks) * kk),
+                                             next_pow2(static_cast<size_t>(kk) * group_rows)));
   DeviceBuffer fail(sizeof(int) + nq * (sizeof(int) + sizeof(float)), st);
   int* fail_count = fail.get<int>();
   int* fail_q = fail_count + 1;
@@ -637,9 +663,9 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
                                (int)fsmem));
   flat_finalize_kernel<<<static_cast<unsigned>(nq), kFinalizeThreads, fsmem, st>>>(
       qp.get<float>(), dpad, eps.get<float>(), static_cast<int>(nq), s.x.get<float>(), dim,
-      s.labels.get<uint64_t>(), s.row_offset, l2, cand_d.get<float>(), cand_r.get<uint32_t>(),
-      cand_n.get<int>(), n_chunks, kk, pool, static_cast<int>(k), d_labels, d_dists, d_keys,
-      fail_count, fail_q, fail_dk);
+      static_cast<int64_t>(s.n), d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2,
+      cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(), n_chunks, kk, group_rows,
+      pool, static_cast<int>(k), d_labels, d_dists, d_keys, fail_count, fail_q, fail_dk);
   check_launch("flat_finalize_kernel");
 
   const int cap = static_cast<int>(next_pow2(k + 256));
@@ -814,9 +840,10 @@ void flat_search_noalloc(const FlatState& s, const float* d_queries, size_t nq, 
   QV_CUDA(cudaFuncSetAttribute(flat_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)fsmem));
   flat_finalize_kernel<<<static_cast<unsigned>(nq), kFinalizeThreads, fsmem, st>>>(
-      qp, L.dpad, eps, static_cast<int>(nq), s.x.get<float>(), dim, s.labels.get<uint64_t>(),
-      s.row_offset, l2, cand_d, cand_r, cand_n, L.n_chunks, L.kk, pool, static_cast<int>(k),
-      d_labels, d_dists, d_keys, fail_count, fail_q, fail_dk);
+      qp, L.dpad, eps, static_cast<int>(nq), s.x.get<float>(), dim, static_cast<int64_t>(s.n),
+      d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, cand_d, cand_r, cand_n, L.n_chunks,
+      L.kk, 1, pool, static_cast<int>(k), d_labels, d_dists, d_keys, fail_count, fail_q,
+      fail_dk);
   check_launch("flat_finalize_kernel");
   const int cap = static_cast<int>(next_pow2(k + 256));
   const size_t rsmem = cap * (sizeof(float) + sizeof(uint64_t));

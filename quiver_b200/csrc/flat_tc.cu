@@ -473,13 +473,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------- epilogue: thread = query ----------------
-    // Each query keeps a candidate list of kCap (distance, row) entries in shared memory (sorted
-    // best-kKK prefix + entries appended since). Per 64 columns: one three-input max/min tree
-    // gives the best score of each 8-column group and of all 64; the warp skips the 64 columns
-    // when no lane can improve on its threshold (the common case). Otherwise it visits only the
-    // 8-column groups some lane can improve on, and lanes append their survivors at positions
-    // from a prefix population count. When any lane's list could overflow, the warp compacts
-    // together, which tightens every full list's threshold to its kKK-th distance.
+    // Each query keeps a candidate list of kCap (distance, group) entries in shared memory
+    // (sorted best-kKK prefix + entries appended since). Per 64 columns: one three-input
+    // max/min tree gives the best score of each 8-row group and of all 64; the warp skips the 64
+    // columns when no lane can improve on its threshold (the common case). Otherwise lanes append
+    // the groups they can improve on, one entry per group (its best screen distance). When any
+    // lane's list is full, the warp compacts together, which tightens every full list's threshold
+    // to its kKK-th entry: kKK groups, each holding a row at least that close.
     const int quarter = warp & 3;
     const int qi = quarter * 32 + lane;
     float* bd = buf_d + qi;
@@ -512,33 +512,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto group = [&](uint32_t (&r)[64], int64_t cb) {
         float (&v)[64] = *reinterpret_cast<float(*)[64]>(r);  // the loaded bits, used in place
         const int valid = static_cast<int>(r1 - cb < 64 ? r1 - cb : 64);  // rows of this chunk
+        // Rows past the chunk end and rows the filter rejects take the worst score, so that
+        // every group's best is the best of its admitted rows.
+        const uint64_t admitted =
+            (valid >= 64 ? ~0ull : (valid > 0 ? (1ull << valid) - 1 : 0ull)) &
+            (a.bitmap != nullptr && valid > 0 ? a.bitmap[static_cast<uint64_t>(cb) >> 6] : ~0ull);
         // best[g]: the best score among elements 8g..8g+7 (max inner product for cosine/IP,
         // min distance for L2); top: the best of all 64.
         float best[8];
         float top;
         if (kL2) {
-          // v[j] := ||q||^2 + ||x||^2 - 2<q,x>; columns past the chunk end become +inf.
+          // v[j] := ||q||^2 + ||x||^2 - 2<q,x>
 #pragma unroll
           for (int j = 0; j < 64; ++j) {
-            const float xn = j < valid ? a.xnorm2[cb + j] : 0.0f;
-            v[j] = j < valid ? fmaf(-2.0f * inv, v[j], qn + xn) : kInfF;
+            const bool in = (admitted >> j) & 1ull;
+            const float xn = in ? a.xnorm2[cb + j] : 0.0f;
+            v[j] = in ? fmaf(-2.0f * inv, v[j], qn + xn) : kInfF;
           }
           group_best8<false>(v, best, top);
         } else {
-          if (valid < 64) {
+          if (admitted != ~0ull) {
 #pragma unroll
             for (int j = 0; j < 64; ++j)
-              if (j >= valid) v[j] = -kInfF;
+              if (!((admitted >> j) & 1ull)) v[j] = -kInfF;
           }
           group_best8<true>(v, best, top);
         }
         const bool may = active && screen_value<kL2>(top, inv) <= thr;
         if (!__any_sync(0xffffffffu, may)) return;
-        // Only rows of this chunk that the filter admits are ever appended (columns past the
-        // chunk end can pass the test while the threshold is still +inf).
-        uint64_t allowed = valid >= 64 ? ~0ull : (valid > 0 ? (1ull << valid) - 1 : 0ull);
-        if (a.bitmap != nullptr && valid > 0) allowed &= a.bitmap[static_cast<uint64_t>(cb) >> 6];
-        // Which 8-column groups this lane can improve on, and their union over the warp.
+        static_assert(kTcGroupRows == 8, "the group tree is built for 8-row groups");
+        // Which 8-row groups this lane can improve on, and their union over the warp. A group
+        // enters the candidate list as one entry: its best screen value and its index (rows
+        // 8 * index .. 8 * index + 7); the exact re-rank expands it.
         uint32_t gm = 0;
 #pragma unroll
         for (int g = 0; g < 8; ++g)
@@ -548,31 +553,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int g = 0; g < 8; ++g) {
           if (!((wm >> g) & 1u)) continue;  // warp-uniform
           bool sub = (gm >> g) & 1u;
-          // Compact (all lanes together) when some lane's 8 new entries might not fit.
-          if (__any_sync(0xffffffffu, sub && cnt > kCap - 8)) {
+          const float bv = screen_value<kL2>(best[g], inv);
+          // Compact (all lanes together) when some lane's list is full.
+          if (__any_sync(0xffffffffu, sub && cnt >= kCap)) {
             compact_buffer(bd, br, cnt, thr);
-            sub = sub && screen_value<kL2>(best[g], inv) <= thr;
+            sub = sub && bv <= thr;
           }
-          uint32_t m8 = 0;
           if (sub) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int e = 8 * g + j;
-              m8 |= (screen_value<kL2>(v[e], inv) <= thr && ((allowed >> e) & 1ull)) ? (1u << j)
-                                                                                     : 0u;
-            }
-          }
-          if (m8 != 0) {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              if ((m8 >> j) & 1u) {
-                const int pos = cnt + __popc(m8 & ((1u << j) - 1u));
-                bd[pos * kM] = screen_value<kL2>(v[8 * g + j], inv);
-                br[pos * kM] = static_cast<uint32_t>(cb + 8 * g + j);
-              }
-            }
-            cnt += __popc(m8);
-            seen += __popc(m8);
+            bd[cnt * kM] = bv;
+            br[cnt * kM] = static_cast<uint32_t>(cb / kTcGroupRows + g);
+            ++cnt;
+            ++seen;
           }
         }
       };

@@ -39,6 +39,8 @@ void flat_search_noalloc(const FlatState& s, const float* d_queries, size_t nq, 
                          const uint64_t* d_bitmap, uint64_t* d_labels, float* d_dists,
                          uint64_t* d_keys, cudaStream_t st);
 size_t flat_noalloc_max_bytes();
+// The tensor-core screen's candidates are groups of this many consecutive rows.
+constexpr int kTcGroupRows = 8;
 bool flat_tc_eligible(const FlatState& s, size_t k);
 int flat_tc_kk();
 void flat_tc_prepare(FlatState& s, cudaStream_t st);
