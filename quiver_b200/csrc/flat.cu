@@ -339,11 +339,23 @@ __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
   // Exact rerank of the m best (reference AVX2 order), one warp per candidate.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const float* qrow = qp + static_cast<size_t>(q) * dpad;
-  for (int i = warp; i < m; i += nwarps) {
-    const uint64_t row = sk[i];
-    if (row == ~0ull) continue;  // an expanded slot without an admitted row
-    const float e = dev::nan_to_inf(dev::warp_exact_distance(qrow, x + row * dim, dim, l2, lane));
-    if (lane == 0) sd[i] = e;
+  // Four rows per warp at a time, so that their loads overlap; a slot without an admitted row
+  // (row ~0) keeps +inf.
+  for (int i0 = warp * 4; i0 < m; i0 += nwarps * 4) {
+    uint64_t row[4];
+    const float* xr[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      row[r] = i0 + r < m ? sk[i0 + r] : ~0ull;
+      xr[r] = x + (row[r] == ~0ull ? 0 : row[r]) * dim;
+    }
+    float e[4];
+    dev::warp_exact_distance_x4(qrow, xr, dim, l2, lane, e);
+    if (lane == 0) {
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        if (row[r] != ~0ull) sd[i0 + r] = dev::nan_to_inf(e[r]);
+    }
   }
   __syncthreads();
   // Re-sort the first m' = next_pow2(m) entries (the tail beyond m holds screen values; mask them).

@@ -296,6 +296,98 @@ __device__ __forceinline__ float warp_reduce_avx2(const float* __restrict__ a,
   return sum;
 }
 
+// The same reduction for four rows b[0..3] against one vector a, with the four rows' loads
+// interleaved so that their memory latencies overlap. Each result is bit-identical to
+// warp_reduce_avx2<kDiff>(a, b[r], dim, lane).
+template <bool kDiff>
+__device__ __forceinline__ void warp_reduce_avx2_x4(const float* __restrict__ a,
+                                                    const float* const (&b)[4], int dim,
+                                                    int lane, float (&out)[4]) {
+  float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  int i = 0;
+  for (; i + 32 <= dim; i += 32) {
+    const float u = a[i + lane];
+    float v[4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) v[r] = b[r][i + lane];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float x = u, y = v[r];
+      if (kDiff) {
+        x = __fsub_rn(u, v[r]);
+        y = x;
+      }
+      s[r] = __fmaf_rn(x, y, s[r]);
+    }
+  }
+  for (; i + 8 <= dim; i += 8) {
+    if (lane < 8) {
+      const float u = a[i + lane];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        float x = u, y = b[r][i + lane];
+        if (kDiff) {
+          x = __fsub_rn(u, y);
+          y = x;
+        }
+        s[r] = __fmaf_rn(x, y, s[r]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const float s1 = __shfl_down_sync(kFull, s[r], 8);
+    const float s2 = __shfl_down_sync(kFull, s[r], 16);
+    const float s3 = __shfl_down_sync(kFull, s[r], 24);
+    const float t = __fadd_rn(__fadd_rn(s[r], s1), __fadd_rn(s2, s3));
+    const float lo = __fadd_rn(t, __shfl_down_sync(kFull, t, 4));
+    const float lo1 = __shfl_down_sync(kFull, lo, 1);
+    const float lo2 = __shfl_down_sync(kFull, lo, 2);
+    const float lo3 = __shfl_down_sync(kFull, lo, 3);
+    out[r] = __shfl_sync(kFull, __fadd_rn(__fadd_rn(lo, lo1), __fadd_rn(lo2, lo3)), 0);
+  }
+  int j = i;
+  if (dim - i >= 4) {
+    for (; j < i + 4; ++j) {
+      const float u = a[j];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        float x = u, y = b[r][j];
+        if (kDiff) {
+          x = __fsub_rn(u, y);
+          y = x;
+        }
+        out[r] = __fadd_rn(out[r], __fmul_rn(x, y));
+      }
+    }
+  }
+  for (; j < dim; ++j) {
+    const float u = a[j];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float x = u, y = b[r][j];
+      if (kDiff) {
+        x = __fsub_rn(u, y);
+        y = x;
+      }
+      out[r] = __fmaf_rn(x, y, out[r]);
+    }
+  }
+}
+
+// warp_exact_distance for four rows at once (see warp_reduce_avx2_x4).
+__device__ __forceinline__ void warp_exact_distance_x4(const float* q, const float* const (&x)[4],
+                                                       int dim, bool l2, int lane,
+                                                       float (&out)[4]) {
+  if (l2) {
+    warp_reduce_avx2_x4<true>(q, x, dim, lane, out);
+  } else {
+    warp_reduce_avx2_x4<false>(q, x, dim, lane, out);
+#pragma unroll
+    for (int r = 0; r < 4; ++r) out[r] = __fsub_rn(1.0f, out[r]);
+  }
+}
+
 __device__ __forceinline__ float warp_dot_avx2(const float* a, const float* b, int dim, int lane) {
   return warp_reduce_avx2<false>(a, b, dim, lane);
 }
