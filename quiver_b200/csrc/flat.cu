@@ -598,7 +598,7 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
   int kk, n_qtiles, n_chunks, qpb = 0;
   int64_t chunk_rows = 0;
   if (tensor) {
-    kk = flat_tc_kk();
+    kk = flat_tc_kk(k);
     n_qtiles = static_cast<int>(ceil_div(nq, 128));
     n_chunks = choose_chunks(s.n, n_qtiles, std::max(1, kMaxCandidatesPerQuery / kk), nsm, 128,
                              &chunk_rows);
@@ -629,7 +629,7 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
       std::lock_guard<std::mutex> lock(ms.x16_mu);
       flat_tc_prepare(ms, st);
     }
-    flat_screen_tc(s, qp.get<float>(), dpad, nq, d_bitmap, n_chunks, chunk_rows,
+    flat_screen_tc(s, qp.get<float>(), dpad, nq, d_bitmap, n_chunks, chunk_rows, kk,
                    cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(),
                    thr.get<unsigned>(), eps.get<float>(), err.get<int>(), st);
   } else {

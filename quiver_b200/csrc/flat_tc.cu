@@ -39,8 +39,8 @@ constexpr int kAtomBytes = 128 * 128;  // one 128-row x 128-byte swizzle atom co
 constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr int kAcc = 4;          // TMEM accumulators of kN columns (4 x 128 = all 512 columns)
-constexpr int kKK = 32;          // candidates per query per unit
-constexpr int kCap = 64;         // candidate buffer entries per query
+constexpr int kAppend = 32;      // list entries appended between compactions
+constexpr int kMaxKK = 32;       // largest best-list length (candidates per query per unit)
 constexpr uint64_t kTimeoutNs = 2000000000ull;       // drain bound (global timer)
 constexpr long long kTimeoutCycles = 4000000000ll;     // ~2 s at 2 GHz (SM clock)
 constexpr uint32_t kSuspendHintNs = 100000;           // one sleeping try_wait: at most 0.1 ms
@@ -62,7 +62,7 @@ struct Args {
   uint32_t* cand_r;
   int* cand_n;
   unsigned* thr_bits;
-  float* gbest;     // nq x kKK: the kKK best distances output by the query's finished units
+  float* gbest;     // nq x KK: the KK best distances output by the query's finished units
   int* glock;       // nq: try-lock guarding gbest[q]
   int* err;
   bool qmajor;      // unit order: query-tile-major (true) or row-chunk-major (false)
@@ -262,9 +262,8 @@ __device__ __forceinline__ void group_best8(const float (&v)[64], float (&best)[
 
 // Per-lane candidate lists: entry i of a query's list lives at i * kM (the lanes of a warp hold
 // adjacent queries, so their accesses never share a bank). A list is a sorted prefix of exactly
-// kKK entries (padded with (+inf, ~0) at the start of a work unit) followed by up to
-// kCap - kKK entries appended since.
-constexpr int kAppend = kCap - kKK;
+// KK entries (padded with (+inf, ~0) at the start of a work unit) followed by up to kAppend
+// entries appended since (kCap = KK + kAppend in all).
 
 // Sorts the kAppend appended entries by (distance, row): a fully unrolled bitonic network, each
 // lane on its own list (no divergence), so the loads of one stage's independent
@@ -294,7 +293,9 @@ __device__ __noinline__ void sort_appended(float* d, uint32_t* r) {
 // Keeps the best kKK of a query's list: sorts the appended part and merges it into the sorted
 // prefix from the back (which never overwrites an entry not yet read). The threshold then tightens
 // to the kKK-th distance (+inf while fewer than kKK real entries were seen).
+template <int kKK>
 __device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, float& thr) {
+  constexpr int kCap = kKK + kAppend;
   if (cnt > kKK) {
     for (int i = cnt; i < kCap; ++i) {
       d[i * kM] = __int_as_float(0x7f800000);
@@ -327,10 +328,11 @@ __device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, flo
   thr = fminf(thr, d[(kKK - 1) * kM]);
 }
 
-template <int kAtoms, bool kL2>
+template <int kAtoms, bool kL2, int kKK>
 __global__ void __launch_bounds__(kThreads, 1)
     flat_screen_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                           const __grid_constant__ CUtensorMap tmap_x, const Args a) {
+  constexpr int kCap = kKK + kAppend;  // candidate list entries per query
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the swizzle atoms.
   unsigned char* base = reinterpret_cast<unsigned char*>(
@@ -556,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float bv = screen_value<kL2>(best[g], inv);
           // Compact (all lanes together) when some lane's list is full.
           if (__any_sync(0xffffffffu, sub && cnt >= kCap)) {
-            compact_buffer(bd, br, cnt, thr);
+            compact_buffer<kKK>(bd, br, cnt, thr);
             sub = sub && bv <= thr;
           }
           if (sub) {
@@ -605,7 +607,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if ((t & 7) == 7) thr = fminf(thr, dev::from_ordered_bits(fresh));
       }
       if (!ok) break;
-      compact_buffer(bd, br, cnt, thr);
+      compact_buffer<kKK>(bd, br, cnt, thr);
       cnt = min(seen, kKK);  // the real entries: they sort before the padding
       if (active) {
         const size_t slot = static_cast<size_t>(q) * a.n_chunks + chunk;
@@ -794,10 +796,13 @@ CUtensorMap make_map(const void* base, uint64_t rows, uint64_t kpad) {
 bool flat_tc_eligible(const FlatState& s, size_t k) {
   const char* e = std::getenv("QV_FLAT_SCREEN");
   if (e != nullptr && std::strcmp(e, "simt") == 0) return false;
-  return s.dim <= 128 && k + 8 <= static_cast<size_t>(tc::kKK) && s.n >= static_cast<size_t>(tc::kN);
+  return s.dim <= 128 && k + 8 <= static_cast<size_t>(tc::kMaxKK) &&
+         s.n >= static_cast<size_t>(tc::kN);
 }
 
-int flat_tc_kk() { return tc::kKK; }
+// Best-list length: k + 8 groups or more (the certificate's margin); 24 when that suffices,
+// which tightens thresholds and shortens the finalize's re-rank.
+int flat_tc_kk(size_t k) { return k + 8 <= 24 ? 24 : tc::kMaxKK; }
 
 // Builds (once per set of rows) the fp16 copy of the index and its error statistics.
 void flat_tc_prepare(FlatState& s, cudaStream_t st) {
@@ -838,9 +843,10 @@ void flat_tc_prepare(FlatState& s, cudaStream_t st) {
 // Runs the tensor-core screen for the queries in qp (normalized, dpad stride). Writes the per-query
 // candidates in the layout flat_finalize_kernel reads, and eps[q].
 void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
-                    const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, float* cand_d,
-                    uint32_t* cand_r, int* cand_n, unsigned* thr_bits, float* eps, int* err,
-                    cudaStream_t st) {
+                    const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, int kk,
+                    float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits, float* eps,
+                    int* err, cudaStream_t st) {
+  QV_REQUIRE(kk == 24 || kk == tc::kMaxKK, "tensor-core screen: unsupported best-list length");
   const int kpad = static_cast<int>(s.kpad);
   const bool l2 = s.metric == QV_METRIC_L2;
   // Whole 128-row query tiles (zero rows past nq), so no TMA box extends past the tensor.
@@ -877,9 +883,8 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   // together, sharing thresholds); the default row-chunk-major order shares row chunks in L2.
   const char* order = std::getenv("QV_FLAT_TC_ORDER");
   a.qmajor = order != nullptr && order[0] == 'q';
-  DeviceBuffer gbest(nq * tc::kKK * sizeof(float), st), glock(nq * sizeof(int), st);
-  tc::fill_inf_kernel<<<ceil_div(nq * tc::kKK, 256), 256, 0, st>>>(gbest.get<float>(),
-                                                                   nq * tc::kKK);
+  DeviceBuffer gbest(nq * kk * sizeof(float), st), glock(nq * sizeof(int), st);
+  tc::fill_inf_kernel<<<ceil_div(nq * kk, 256), 256, 0, st>>>(gbest.get<float>(), nq * kk);
   check_launch("fill_inf_kernel");
   QV_CUDA(cudaMemsetAsync(glock.get(), 0, glock.bytes(), st));
   a.gbest = gbest.get<float>();
@@ -887,7 +892,8 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   a.err = err;
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
   const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (1 + tc::kStages) +
-                      static_cast<size_t>(tc::kCap) * tc::kM * 8 + (2 * tc::kStages + 2 * tc::kAcc + 2) * 8;
+                      static_cast<size_t>(kk + tc::kAppend) * tc::kM * 8 +
+                      (2 * tc::kStages + 2 * tc::kAcc + 2) * 8;
   const int grid = std::min(a.total_units, sm_count(s.device));
   KernelTimer timer(st, "flat_screen_tc_kernel", 2.0 * nq * static_cast<double>(s.n) * s.dim,
                     false);
@@ -896,9 +902,17 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
     kernel<<<grid, tc::kThreads, smem, st>>>(mq, mx, a);
   };
   if (atoms == 2) {
-    if (l2) launch(tc::flat_screen_tc_kernel<2, true>); else launch(tc::flat_screen_tc_kernel<2, false>);
+    if (kk == 24) {
+      if (l2) launch(tc::flat_screen_tc_kernel<2, true, 24>); else launch(tc::flat_screen_tc_kernel<2, false, 24>);
+    } else {
+      if (l2) launch(tc::flat_screen_tc_kernel<2, true, 32>); else launch(tc::flat_screen_tc_kernel<2, false, 32>);
+    }
   } else {
-    if (l2) launch(tc::flat_screen_tc_kernel<1, true>); else launch(tc::flat_screen_tc_kernel<1, false>);
+    if (kk == 24) {
+      if (l2) launch(tc::flat_screen_tc_kernel<1, true, 24>); else launch(tc::flat_screen_tc_kernel<1, false, 24>);
+    } else {
+      if (l2) launch(tc::flat_screen_tc_kernel<1, true, 32>); else launch(tc::flat_screen_tc_kernel<1, false, 32>);
+    }
   }
   timer.stop();
   check_launch("flat_screen_tc_kernel");

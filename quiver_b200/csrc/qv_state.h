@@ -42,12 +42,12 @@ size_t flat_noalloc_max_bytes();
 // The tensor-core screen's candidates are groups of this many consecutive rows.
 constexpr int kTcGroupRows = 8;
 bool flat_tc_eligible(const FlatState& s, size_t k);
-int flat_tc_kk();
+int flat_tc_kk(size_t k);
 void flat_tc_prepare(FlatState& s, cudaStream_t st);
 void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
-                    const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, float* cand_d,
-                    uint32_t* cand_r, int* cand_n, unsigned* thr_bits, float* eps, int* err,
-                    cudaStream_t st);
+                    const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, int kk,
+                    float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits, float* eps,
+                    int* err, cudaStream_t st);
 
 void flat_reserve(FlatState& s, size_t rows, cudaStream_t st);
 // Appends n rows (device pointer, row-major) with labels (device pointer).

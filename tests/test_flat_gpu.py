@@ -158,14 +158,16 @@ def test_tensor_core_screen_equals_simt_screen(gpu, oracle, monkeypatch, metric)
     q = mixture(300, 100, 50, 0.35, 1.0, centre_seed=3, seed=5)
     ix = gpu.FlatIndex(100, metric)
     ix.add(base)
-    gpu._native.set_timing(True)
-    l1, d1 = ix.search(q, 10)
-    st = gpu.last_search_stats()
-    gpu._native.set_timing(False)
-    assert st["dominant_kernel"] == "flat_screen_tc_kernel"
-    monkeypatch.setenv("QV_FLAT_SCREEN", "simt")
-    l2_, d2 = ix.search(q, 10)
-    assert np.array_equal(d1, d2) and np.array_equal(l1, l2_)
     stored = oracle.normalize_rows(base) if metric == "cosine" else base
-    wl, wd = oracle.flat_search(stored, np.arange(20000, dtype=np.uint64), metric, q, 10)
-    assert_topk_parity(l1, d1, wl, wd, exact=True, what=f"tc {metric}")
+    for k in (10, 20):  # best lists of 24 and of 32 groups
+        monkeypatch.delenv("QV_FLAT_SCREEN", raising=False)
+        gpu._native.set_timing(True)
+        l1, d1 = ix.search(q, k)
+        st = gpu.last_search_stats()
+        gpu._native.set_timing(False)
+        assert st["dominant_kernel"] == "flat_screen_tc_kernel"
+        monkeypatch.setenv("QV_FLAT_SCREEN", "simt")
+        l2_, d2 = ix.search(q, k)
+        assert np.array_equal(d1, d2) and np.array_equal(l1, l2_)
+        wl, wd = oracle.flat_search(stored, np.arange(20000, dtype=np.uint64), metric, q, k)
+        assert_topk_parity(l1, d1, wl, wd, exact=True, what=f"tc {metric} k={k}")
