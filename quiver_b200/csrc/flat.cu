@@ -134,7 +134,6 @@ struct ThreadHeap {
   int n;
   int cap;
   __device__ float top_d() const { return d[0]; }
-  __device__ uint32_t top_r() const { return r[0]; }
   __device__ void push(float dist, uint32_t row) {
     if (n < cap) {  // sift up
       int i = n++;
@@ -386,6 +385,241 @@ __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
       out_d[o] = kInf;
       out_labels[o] = kInvalidLabel;
       if (out_keys) out_keys[o] = ~0ull;
+    }
+  }
+}
+
+// ---- finalize for group candidates: one warp per query -------------------------------------------
+
+// simd::avx2::dot / l2sqr (src/simd/kernels_avx2.cc:35-83) evaluated by ONE thread, in exactly the
+// order dev::warp_reduce_avx2 uses: accumulator s[a][l] takes elements i + 8a + l of every
+// 32-element block, 8-element blocks go to s[0][l], then (s0+s1)+(s2+s3) per l, the hsum
+// (t[l]+t[l+4]) and (lo0+lo1)+(lo2+lo3), then the scalar tail (the first 4 products rounded and
+// added in order when 4 or more remain, FMAs after). q is in shared memory (all lanes read the same
+// element: a broadcast), x is this thread's row. Bit-identical to the warp version.
+template <bool kDiff>
+__device__ __forceinline__ float lane_reduce_avx2(const float* __restrict__ q,
+                                                  const float* __restrict__ x, int dim) {
+  float s[4][8];
+#pragma unroll
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int l = 0; l < 8; ++l) s[a][l] = 0.0f;
+  auto acc = [&](float& dst, float u, float v) {
+    if (kDiff) {
+      u = __fsub_rn(u, v);
+      v = u;
+    }
+    dst = __fmaf_rn(u, v, dst);
+  };
+  int i = 0;
+  const bool vec = (dim & 3) == 0;  // rows and q start on 16-byte boundaries
+  for (; i + 32 <= dim; i += 32) {
+    if (vec) {
+#pragma unroll
+      for (int f = 0; f < 8; ++f) {
+        const float4 xv = __ldg(reinterpret_cast<const float4*>(x + i) + f);
+        const float4 qv = reinterpret_cast<const float4*>(q + i)[f];
+        const int e = 4 * f;
+        acc(s[(e + 0) >> 3][(e + 0) & 7], qv.x, xv.x);
+        acc(s[(e + 1) >> 3][(e + 1) & 7], qv.y, xv.y);
+        acc(s[(e + 2) >> 3][(e + 2) & 7], qv.z, xv.z);
+        acc(s[(e + 3) >> 3][(e + 3) & 7], qv.w, xv.w);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) acc(s[e >> 3][e & 7], q[i + e], __ldg(x + i + e));
+    }
+  }
+  for (; i + 8 <= dim; i += 8) {
+#pragma unroll
+    for (int l = 0; l < 8; ++l) acc(s[0][l], q[i + l], __ldg(x + i + l));
+  }
+  float t[8];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) t[l] = __fadd_rn(__fadd_rn(s[0][l], s[1][l]), __fadd_rn(s[2][l], s[3][l]));
+  float lo[4];
+#pragma unroll
+  for (int l = 0; l < 4; ++l) lo[l] = __fadd_rn(t[l], t[l + 4]);
+  float sum = __fadd_rn(__fadd_rn(lo[0], lo[1]), __fadd_rn(lo[2], lo[3]));
+  int j = i;
+  if (dim - i >= 4) {
+    for (; j < i + 4; ++j) {
+      float u = q[j], v = __ldg(x + j);
+      if (kDiff) {
+        u = __fsub_rn(u, v);
+        v = u;
+      }
+      sum = __fadd_rn(sum, __fmul_rn(u, v));
+    }
+  }
+  for (; j < dim; ++j) {
+    float u = q[j], v = __ldg(x + j);
+    if (kDiff) {
+      u = __fsub_rn(u, v);
+      v = u;
+    }
+    sum = __fmaf_rn(u, v, sum);
+  }
+  return sum;
+}
+
+__device__ __forceinline__ float lane_exact_distance(const float* q, const float* x, int dim,
+                                                     bool l2) {
+  return l2 ? lane_reduce_avx2<true>(q, x, dim) : __fsub_rn(1.0f, lane_reduce_avx2<false>(q, x, dim));
+}
+
+// One warp per query, for the tensor-core screen's group candidates (kk <= 32 groups per unit,
+// k <= kk). Each unit's list is sorted by (value, group), so the rank of a candidate in the union
+// is the sum over lists of how many entries precede it there (a binary search each): ranks below
+// kk select the kk best groups and rank kk - 1 gives T. The groups' admitted rows (8 * kk at most)
+// are then recomputed exactly, one row per lane, and the k best are picked by k rounds of a warp
+// minimum over (distance, row). Same results and certificate as flat_finalize_kernel.
+constexpr int kGroupFinalizeWarps = 4;
+
+// Shared memory of one warp of flat_finalize_groups_kernel (the layout the kernel carves).
+__host__ __device__ inline size_t group_finalize_bytes_per_warp(int dpad, int n_chunks, int kk,
+                                                                int group_rows) {
+  const size_t nl = static_cast<size_t>(n_chunks) * kk, nx = static_cast<size_t>(kk) * group_rows;
+  const size_t bytes = static_cast<size_t>(dpad) * 4 + nl * 8 + ((n_chunks + 1) & ~1) * 4 +
+                       static_cast<size_t>(kk) * 4 + nx * 12;
+  return (bytes + 15) / 16 * 16;
+}
+
+__global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_groups_kernel(
+    const float* __restrict__ qp, int dpad, const float* __restrict__ eps_q, int nq,
+    const float* __restrict__ x, int dim, int64_t nrows, const uint64_t* __restrict__ bitmap,
+    const uint64_t* __restrict__ labels, uint64_t row_offset, bool l2,
+    const float* __restrict__ cand_d, const uint32_t* __restrict__ cand_r,
+    const int* __restrict__ cand_n, int n_chunks, int kk, int group_rows, int k,
+    uint64_t* __restrict__ out_labels, float* __restrict__ out_d, uint64_t* __restrict__ out_keys,
+    int* __restrict__ fail_count, int* __restrict__ fail_q, float* __restrict__ fail_dk) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q = blockIdx.x * kGroupFinalizeWarps + warp;
+  // Per warp: the query (dpad floats), the lists (n_chunks x kk values and groups), their
+  // lengths, the selected groups (kk) and the expanded rows' exact distances (kk * group_rows).
+  const int nl = n_chunks * kk, nx = kk * group_rows;
+  const size_t per_warp = group_finalize_bytes_per_warp(dpad, n_chunks, kk, group_rows);
+  unsigned char* base = smem_raw + per_warp * warp;
+  float* sq = reinterpret_cast<float*>(base);
+  float* ld = sq + dpad;
+  uint32_t* lr = reinterpret_cast<uint32_t*>(ld + nl);
+  int* ln = reinterpret_cast<int*>(lr + nl);
+  uint32_t* sel = reinterpret_cast<uint32_t*>(ln + ((n_chunks + 1) & ~1));
+  float* ed = reinterpret_cast<float*>(sel + kk);
+  uint64_t* er = reinterpret_cast<uint64_t*>(ed + nx);  // 8-byte aligned: offsets are even words
+  if (q >= nq) return;
+  const float* qrow = qp + static_cast<size_t>(q) * dpad;
+  for (int i = lane; i < dpad; i += 32) sq[i] = qrow[i];
+  int total = 0;
+  for (int c = lane; c < n_chunks; c += 32) ln[c] = cand_n[static_cast<size_t>(q) * n_chunks + c];
+  __syncwarp();
+  for (int c = 0; c < n_chunks; ++c) total += ln[c];
+  for (int i = lane; i < nl; i += 32) {
+    const int c = i / kk, j = i - c * kk;
+    if (j < ln[c]) {
+      const size_t slot = static_cast<size_t>(q) * n_chunks + c;
+      ld[i] = cand_d[slot * kk + j];
+      lr[i] = cand_r[slot * kk + j];
+    }
+  }
+  __syncwarp();
+  // k-way merge of the sorted unit lists: each round, the warp's minimum over the lists' heads
+  // (lane l watches lists l and l + 32) is the next best candidate.
+  const int m = min(total, kk);
+  float T = kInf;
+  int h0 = 0, h1 = 0;
+  const int c0 = lane, c1 = lane + 32;
+  for (int r = 0; r < m; ++r) {
+    float bd = kInf;
+    uint32_t bg = 0xffffffffu;
+    int bl = -1;
+    if (c0 < n_chunks && h0 < ln[c0]) {
+      bd = ld[c0 * kk + h0];
+      bg = lr[c0 * kk + h0];
+      bl = c0;
+    }
+    if (c1 < n_chunks && h1 < ln[c1]) {
+      const float d1 = ld[c1 * kk + h1];
+      const uint32_t g1 = lr[c1 * kk + h1];
+      if (dev::key_less(d1, g1, bd, bg)) {
+        bd = d1;
+        bg = g1;
+        bl = c1;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float od = __shfl_xor_sync(kFull, bd, o);
+      const uint32_t og = __shfl_xor_sync(kFull, bg, o);
+      const int ol = __shfl_xor_sync(kFull, bl, o);
+      if (dev::key_less(od, og, bd, bg)) {
+        bd = od;
+        bg = og;
+        bl = ol;
+      }
+    }
+    if (lane == 0) sel[r] = bg;
+    if (r == kk - 1) T = bd;
+    h0 += bl == c0 ? 1 : 0;
+    h1 += bl == c1 ? 1 : 0;
+  }
+  __syncwarp();
+  // Exact distances of the selected groups' admitted rows, one row per lane.
+  for (int i = lane; i < m * group_rows; i += 32) {
+    const int g = i / group_rows, j = i - g * group_rows;
+    const uint64_t row = static_cast<uint64_t>(sel[g]) * group_rows + j;
+    const bool in = row < static_cast<uint64_t>(nrows) && dev::bitmap_test(bitmap, row);
+    ed[i] = in ? dev::nan_to_inf(lane_exact_distance(sq, x + row * dim, dim, l2)) : kInf;
+    er[i] = in ? row : ~0ull;
+  }
+  __syncwarp();
+  // The k best by (distance, row): k rounds of a warp minimum; each round's winner is removed.
+  float dk = kInf;
+  for (int r = 0; r < k; ++r) {
+    float bd = kInf;
+    uint64_t br = ~0ull;
+    int bi = -1;
+    for (int i = lane; i < m * group_rows; i += 32) {
+      if (dev::key_less(ed[i], er[i], bd, br)) {
+        bd = ed[i];
+        br = er[i];
+        bi = i;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float od = __shfl_xor_sync(kFull, bd, o);
+      const uint64_t orow = __shfl_xor_sync(kFull, br, o);
+      const int oi = __shfl_xor_sync(kFull, bi, o);
+      if (dev::key_less(od, orow, bd, br)) {
+        bd = od;
+        br = orow;
+        bi = oi;
+      }
+    }
+    const size_t o = static_cast<size_t>(q) * k + r;
+    if (lane == 0) {
+      const bool valid = br != ~0ull;
+      out_d[o] = valid ? bd : kInf;
+      out_labels[o] = valid ? labels[br] : kInvalidLabel;
+      if (out_keys) out_keys[o] = valid ? row_offset + br : ~0ull;
+      if (bi >= 0) {
+        ed[bi] = kInf;
+        er[bi] = ~0ull;
+      }
+    }
+    if (r == k - 1) dk = br != ~0ull ? bd : kInf;
+    __syncwarp();
+  }
+  if (lane == 0) {
+    bool ok = true;
+    if (total >= kk) ok = (T - eps_q[q]) >= dk;
+    if (!ok) {
+      const int slot = atomicAdd(fail_count, 1);
+      fail_q[slot] = q;
+      fail_dk[slot] = dk;
     }
   }
 }
@@ -670,15 +904,30 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
   int* fail_q = fail_count + 1;
   float* fail_dk = reinterpret_cast<float*>(fail_q + nq);
   QV_CUDA(cudaMemsetAsync(fail_count, 0, sizeof(int), st));
-  const size_t fsmem = pool * (sizeof(float) + sizeof(uint64_t));
-  QV_CUDA(cudaFuncSetAttribute(flat_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)fsmem));
-  flat_finalize_kernel<<<static_cast<unsigned>(nq), kFinalizeThreads, fsmem, st>>>(
-      qp.get<float>(), dpad, eps.get<float>(), static_cast<int>(nq), s.x.get<float>(), dim,
-      static_cast<int64_t>(s.n), d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2,
-      cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(), n_chunks, kk, group_rows,
-      pool, static_cast<int>(k), d_labels, d_dists, d_keys, fail_count, fail_q, fail_dk);
-  check_launch("flat_finalize_kernel");
+  if (tensor) {
+    QV_REQUIRE(n_chunks <= 64, "group finalize: more than 64 row chunks");
+    const size_t gsmem =
+        kGroupFinalizeWarps * group_finalize_bytes_per_warp(dpad, n_chunks, kk, group_rows);
+    QV_CUDA(cudaFuncSetAttribute(flat_finalize_groups_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsmem));
+    flat_finalize_groups_kernel<<<static_cast<unsigned>(ceil_div(nq, kGroupFinalizeWarps)),
+                                  32 * kGroupFinalizeWarps, gsmem, st>>>(
+        qp.get<float>(), dpad, eps.get<float>(), static_cast<int>(nq), s.x.get<float>(), dim,
+        static_cast<int64_t>(s.n), d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2,
+        cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(), n_chunks, kk, group_rows,
+        static_cast<int>(k), d_labels, d_dists, d_keys, fail_count, fail_q, fail_dk);
+    check_launch("flat_finalize_groups_kernel");
+  } else {
+    const size_t fsmem = pool * (sizeof(float) + sizeof(uint64_t));
+    QV_CUDA(cudaFuncSetAttribute(flat_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)fsmem));
+    flat_finalize_kernel<<<static_cast<unsigned>(nq), kFinalizeThreads, fsmem, st>>>(
+        qp.get<float>(), dpad, eps.get<float>(), static_cast<int>(nq), s.x.get<float>(), dim,
+        static_cast<int64_t>(s.n), d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2,
+        cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(), n_chunks, kk, group_rows,
+        pool, static_cast<int>(k), d_labels, d_dists, d_keys, fail_count, fail_q, fail_dk);
+    check_launch("flat_finalize_kernel");
+  }
 
   const int cap = static_cast<int>(next_pow2(k + 256));
   const size_t rsmem = cap * (sizeof(float) + sizeof(uint64_t));
