@@ -833,7 +833,7 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
   int64_t chunk_rows = 0;
   if (tensor) {
     kk = flat_tc_kk(k);
-    n_qtiles = static_cast<int>(ceil_div(nq, 128));
+    n_qtiles = static_cast<int>(ceil_div(nq, 256));  // work units cover query groups of 2 x 128
     n_chunks = choose_chunks(s.n, n_qtiles, std::max(1, kMaxCandidatesPerQuery / kk), nsm, 128,
                              &chunk_rows);
   } else {

@@ -36,10 +36,13 @@ constexpr int kM = 128;          // queries per unit = TMEM lanes
 constexpr int kN = 128;          // database rows per MMA tile
 constexpr int kAtomK = 64;       // fp16 elements per 128-byte swizzled row
 constexpr int kAtomBytes = 128 * 128;  // one 128-row x 128-byte swizzle atom column
-constexpr int kStages = 4;
-constexpr int kThreads = 192;
-constexpr int kAcc = 4;          // TMEM accumulators of kN columns (4 x 128 = all 512 columns)
-constexpr int kAppend = 32;      // list entries appended between compactions
+constexpr int kTiles = 2;        // query tiles per CTA: every row tile feeds one MMA per query tile
+constexpr int kStages = 2;       // row-tile ring depth
+constexpr int kEpiWarps = 4 * kTiles;  // one warp per (query tile, TMEM lane quarter)
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kAcc = 2;          // TMEM accumulator slots of kTiles x kN columns (all 512 columns)
+constexpr int kAppend = 16;      // list entries appended between compactions
+constexpr int kLS = kTiles * kM; // candidate-list stride: entry i of list l lives at i * kLS + l
 constexpr int kMaxKK = 32;       // largest best-list length (candidates per query per unit)
 constexpr uint64_t kTimeoutNs = 2000000000ull;       // drain bound (global timer)
 constexpr long long kTimeoutCycles = 4000000000ll;     // ~2 s at 2 GHz (SM clock)
@@ -51,7 +54,7 @@ constexpr uint32_t kIdesc = (1u << 4)            // D format f32
                             | ((kM >> 4) << 24); // M
 
 struct Args {
-  int nq, n_qtiles, n_chunks, total_units, ksteps;
+  int nq, n_qgroups, n_chunks, total_units, ksteps;  // a query group = kTiles tiles of kM
   int64_t nrows, chunk_rows;
   bool l2;
   const float* qscale_inv;  // per query: 1 / (s_q * s_x)
@@ -68,13 +71,13 @@ struct Args {
   bool qmajor;      // unit order: query-tile-major (true) or row-chunk-major (false)
 };
 
-__device__ __forceinline__ void unit_coords(const Args& a, int u, int& qtile, int& chunk) {
+__device__ __forceinline__ void unit_coords(const Args& a, int u, int& qgroup, int& chunk) {
   if (a.qmajor) {
-    qtile = u / a.n_chunks;
-    chunk = u - qtile * a.n_chunks;
+    qgroup = u / a.n_chunks;
+    chunk = u - qgroup * a.n_chunks;
   } else {
-    chunk = u / a.n_qtiles;
-    qtile = u - chunk * a.n_qtiles;
+    chunk = u / a.n_qgroups;
+    qgroup = u - chunk * a.n_qgroups;
   }
 }
 
@@ -260,8 +263,8 @@ __device__ __forceinline__ void group_best8(const float (&v)[64], float (&best)[
   top = best3<kMax>(x, y, best2<kMax>(best[6], best[7]));
 }
 
-// Per-lane candidate lists: entry i of a query's list lives at i * kM (the lanes of a warp hold
-// adjacent queries, so their accesses never share a bank). A list is a sorted prefix of exactly
+// Per-lane candidate lists: entry i of list l lives at i * kLS + l (the lanes of a warp hold
+// adjacent lists, so their accesses never share a bank). A list is a sorted prefix of exactly
 // KK entries (padded with (+inf, ~0) at the start of a work unit) followed by up to kAppend
 // entries appended since (kCap = KK + kAppend in all).
 
@@ -278,13 +281,13 @@ __device__ __noinline__ void sort_appended(float* d, uint32_t* r) {
         const int lo = 2 * i - (i & (stride - 1));
         const int hi = lo + stride;
         const bool up = (lo & size) == 0;
-        const float dl = d[lo * kM], dh = d[hi * kM];
-        const uint32_t rl = r[lo * kM], rh = r[hi * kM];
+        const float dl = d[lo * kLS], dh = d[hi * kLS];
+        const uint32_t rl = r[lo * kLS], rh = r[hi * kLS];
         const bool swap = up ? dev::key_less(dh, rh, dl, rl) : dev::key_less(dl, rl, dh, rh);
-        d[lo * kM] = swap ? dh : dl;
-        d[hi * kM] = swap ? dl : dh;
-        r[lo * kM] = swap ? rh : rl;
-        r[hi * kM] = swap ? rl : rh;
+        d[lo * kLS] = swap ? dh : dl;
+        d[hi * kLS] = swap ? dl : dh;
+        r[lo * kLS] = swap ? rh : rl;
+        r[hi * kLS] = swap ? rl : rh;
       }
     }
   }
@@ -298,16 +301,16 @@ __device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, flo
   constexpr int kCap = kKK + kAppend;
   if (cnt > kKK) {
     for (int i = cnt; i < kCap; ++i) {
-      d[i * kM] = __int_as_float(0x7f800000);
-      r[i * kM] = 0xffffffffu;
+      d[i * kLS] = __int_as_float(0x7f800000);
+      r[i * kLS] = 0xffffffffu;
     }
-    float* bd = d + kKK * kM;
-    uint32_t* br = r + kKK * kM;
+    float* bd = d + kKK * kLS;
+    uint32_t* br = r + kKK * kLS;
     const int nb = cnt - kKK;
     sort_appended(bd, br);
     int ia = 0, ib = 0;  // how many of the prefix / the appended part are among the best kKK
     for (int o = 0; o < kKK; ++o) {
-      const bool take_b = ib < nb && dev::key_less(bd[ib * kM], br[ib * kM], d[ia * kM], r[ia * kM]);
+      const bool take_b = ib < nb && dev::key_less(bd[ib * kLS], br[ib * kLS], d[ia * kLS], r[ia * kLS]);
       ib += take_b ? 1 : 0;
       ia += take_b ? 0 : 1;
     }
@@ -315,17 +318,17 @@ __device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, flo
     for (int o = kKK - 1; o >= 0; --o) {
       const int ja = max(pa, 0), jb = max(pb, 0);
       const bool take_b =
-          pb >= 0 && (pa < 0 || dev::key_less(d[ja * kM], r[ja * kM], bd[jb * kM], br[jb * kM]));
-      const float dv = take_b ? bd[jb * kM] : d[ja * kM];
-      const uint32_t rv = take_b ? br[jb * kM] : r[ja * kM];
-      d[o * kM] = dv;
-      r[o * kM] = rv;
+          pb >= 0 && (pa < 0 || dev::key_less(d[ja * kLS], r[ja * kLS], bd[jb * kLS], br[jb * kLS]));
+      const float dv = take_b ? bd[jb * kLS] : d[ja * kLS];
+      const uint32_t rv = take_b ? br[jb * kLS] : r[ja * kLS];
+      d[o * kLS] = dv;
+      r[o * kLS] = rv;
       pb -= take_b ? 1 : 0;
       pa -= take_b ? 0 : 1;
     }
     cnt = kKK;
   }
-  thr = fminf(thr, d[(kKK - 1) * kM]);
+  thr = fminf(thr, d[(kKK - 1) * kLS]);
 }
 
 template <int kAtoms, bool kL2, int kKK>
@@ -337,11 +340,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   // 1024-byte alignment for the swizzle atoms.
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  unsigned char* smem_a = base;                                  // kAtoms x 16 KB
-  unsigned char* smem_b = smem_a + kAtoms * kAtomBytes;          // kStages x kAtoms x 16 KB
-  float* buf_d = reinterpret_cast<float*>(smem_b + kStages * kAtoms * kAtomBytes);
-  uint32_t* buf_r = reinterpret_cast<uint32_t*>(buf_d + kCap * kM);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(buf_r + kCap * kM);
+  unsigned char* smem_a = base;                                  // kTiles x kAtoms x 16 KB
+  unsigned char* smem_b = smem_a + kTiles * kAtoms * kAtomBytes;  // kStages x kAtoms x 16 KB
+  float* buf_d = reinterpret_cast<float*>(smem_b + kStages * kAtoms * kAtomBytes);  // kCap x kLS
+  uint32_t* buf_r = reinterpret_cast<uint32_t*>(buf_d + kCap * kLS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(buf_r + kCap * kLS);
   // bars: full[kStages], empty[kStages], acc_full[kAcc], acc_empty[kAcc], a_full, a_empty
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
@@ -361,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < kAcc; ++b) {
       mbar_init(bar(ACC_FULL + b), 1);
-      mbar_init(bar(ACC_EMPTY + b), 4);  // one arrival per epilogue warp
+      mbar_init(bar(ACC_EMPTY + b), kEpiWarps);  // one arrival per epilogue warp
     }
     mbar_init(bar(A_FULL), 1);
     mbar_init(bar(A_EMPTY), 1);
@@ -370,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&s_tmem)),
-                 "r"(kAcc * kN));
+                 "r"(kAcc * kTiles * kN));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -387,8 +390,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       int issued = 0;
       bool first = true;
       for (int u = blockIdx.x; u < a.total_units && !*abort_flag; u += gridDim.x) {
-        int qtile, chunk;
-        unit_coords(a, u, qtile, chunk);
+        int qgroup, chunk;
+        unit_coords(a, u, qgroup, chunk);
         const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
         const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
         const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
@@ -397,10 +400,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           a_phase ^= 1;
         }
         first = false;
-        mbar_expect_tx(bar(A_FULL), kAtoms * kAtomBytes);
-        for (int at = 0; at < kAtoms; ++at)
-          tma_load_2d(smem_u32(smem_a + at * kAtomBytes), &tmap_q, at * kAtomK, qtile * kM,
-                      bar(A_FULL));
+        mbar_expect_tx(bar(A_FULL), kTiles * kAtoms * kAtomBytes);
+        for (int tq = 0; tq < kTiles; ++tq)
+          for (int at = 0; at < kAtoms; ++at)
+            tma_load_2d(smem_u32(smem_a + (tq * kAtoms + at) * kAtomBytes), &tmap_q, at * kAtomK,
+                        (qgroup * kTiles + tq) * kM, bar(A_FULL));
         for (int t = 0; t < ntiles; ++t) {
           if (!mbar_wait(bar(EMPTY + stage), phase ^ 1, abort_flag, a.err)) break;
           mbar_expect_tx(bar(FULL + stage), kAtoms * kAtomBytes);
@@ -433,8 +437,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0, acc_phase = 0, a_phase = 0;
       int consumed = 0;
       for (int u = blockIdx.x; u < a.total_units && !*abort_flag; u += gridDim.x) {
-        int qtile, chunk;
-        unit_coords(a, u, qtile, chunk);
+        int qgroup, chunk;
+        unit_coords(a, u, qgroup, chunk);
         const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
         const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
         const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
@@ -452,11 +456,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           s_consumed = ++consumed;
           tc_fence_after();
           const uint32_t b_addr = smem_u32(smem_b + stage * kAtoms * kAtomBytes);
-          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(accb * kN);
-          for (int ks = 0; ks < a.ksteps; ++ks) {
-            const int at = ks >> 2, kin = ks & 3;
-            const uint32_t off = static_cast<uint32_t>(at * kAtomBytes + kin * 32);
-            umma_f16(d_tmem, smem_desc(a_addr + off), smem_desc(b_addr + off), ks > 0 ? 1u : 0u);
+          for (int tq = 0; tq < kTiles; ++tq) {
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((accb * kTiles + tq) * kN);
+            const uint32_t at_addr = a_addr + static_cast<uint32_t>(tq * kAtoms * kAtomBytes);
+            for (int ks = 0; ks < a.ksteps; ++ks) {
+              const int at = ks >> 2, kin = ks & 3;
+              const uint32_t off = static_cast<uint32_t>(at * kAtomBytes + kin * 32);
+              umma_f16(d_tmem, smem_desc(at_addr + off), smem_desc(b_addr + off),
+                       ks > 0 ? 1u : 0u);
+            }
           }
           umma_commit(bar(EMPTY + stage));
           umma_commit(bar(ACC_FULL + accb));
@@ -483,19 +491,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     // lane's list is full, the warp compacts together, which tightens every full list's threshold
     // to its kKK-th entry: kKK groups, each holding a row at least that close.
     const int quarter = warp & 3;
+    const int tile = (warp - 2) >> 2;  // which query tile of the group
     const int qi = quarter * 32 + lane;
-    float* bd = buf_d + qi;
-    uint32_t* br = buf_r + qi;
+    float* bd = buf_d + tile * kM + qi;
+    uint32_t* br = buf_r + tile * kM + qi;
+    const uint32_t col0 = static_cast<uint32_t>(tile * kN);  // this tile's columns in a slot
     const float kInfF = __int_as_float(0x7f800000);
     int accb = 0;
     uint32_t acc_phase = 0;
     for (int u = blockIdx.x; u < a.total_units; u += gridDim.x) {
-      int qtile, chunk;
-      unit_coords(a, u, qtile, chunk);
+      int qgroup, chunk;
+      unit_coords(a, u, qgroup, chunk);
       const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
       const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
       const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
-      const int q = qtile * kM + qi;
+      const int q = (qgroup * kTiles + tile) * kM + qi;
       const bool active = q < a.nq;
       const unsigned* qthr = a.thr_bits + (active ? q : 0);
       float thr = active ? dev::from_ordered_bits(*qthr) : -kInfF;
@@ -504,8 +514,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Start from a prefix of kKK (+inf, ~0) entries; `seen` counts the real entries appended.
 #pragma unroll
       for (int i = 0; i < kKK; ++i) {
-        bd[i * kM] = kInfF;
-        br[i * kM] = 0xffffffffu;
+        bd[i * kLS] = kInfF;
+        br[i * kLS] = 0xffffffffu;
       }
       int cnt = kKK, seen = 0;
       bool ok = true;
@@ -562,47 +572,39 @@ __global__ void __launch_bounds__(kThreads, 1)
             sub = sub && bv <= thr;
           }
           if (sub) {
-            bd[cnt * kM] = bv;
-            br[cnt * kM] = static_cast<uint32_t>(cb / kTcGroupRows + g);
+            bd[cnt * kLS] = bv;
+            br[cnt * kLS] = static_cast<uint32_t>(cb / kTcGroupRows + g);
             ++cnt;
             ++seen;
           }
         }
       };
-      // The TMEM loads run one 64-column group ahead of the processing: a group's values are
-      // being loaded while the previous group is screened.
-      uint32_t ra[64], rb[64];
-      if (ntiles > 0) {
-        ok = mbar_wait(bar(ACC_FULL + accb), acc_phase, abort_flag, a.err);
-        if (!ok) break;
-        tc_fence_after();
-        tmem_ld64_issue(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(accb * kN), ra);
-        tmem_wait_ld(ra);
-      }
+      uint32_t ra[64];
       unsigned fresh = ~0u;  // the query's shared threshold, read early and applied later
       for (int t = 0; t < ntiles; ++t) {
         const int64_t row0 = r0 + static_cast<int64_t>(t) * kN;
         if ((t & 7) == 0 && active) fresh = *reinterpret_cast<const volatile unsigned*>(qthr);
-        tmem_ld64_issue(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(accb * kN + 64), rb);
-        group(ra, row0);
-        tmem_wait_ld(rb);
-        // Tile t is out of TMEM: hand its accumulator back to the MMA warp.
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bar(ACC_EMPTY + accb));
+        ok = mbar_wait(bar(ACC_FULL + accb), acc_phase, abort_flag, a.err);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + col0 +
+                               static_cast<uint32_t>(accb * kTiles * kN);
+#pragma unroll 1
+        for (int h = 0; h < kN / 64; ++h) {
+          tmem_ld64_issue(taddr + h * 64, ra);
+          tmem_wait_ld(ra);
+          if (h == kN / 64 - 1) {
+            // The tile is out of TMEM: hand its accumulator back to the MMA warp.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar(ACC_EMPTY + accb));
+          }
+          group(ra, row0 + h * 64);
+        }
         if (++accb == kAcc) {
           accb = 0;
           acc_phase ^= 1;
         }
-        const bool more = t + 1 < ntiles;
-        if (more) {
-          ok = mbar_wait(bar(ACC_FULL + accb), acc_phase, abort_flag, a.err);
-          if (!ok) break;
-          tc_fence_after();
-          tmem_ld64_issue(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(accb * kN), ra);
-        }
-        group(rb, row0 + 64);
-        if (more) tmem_wait_ld(ra);
         // Tighten with the query's bound from finished units (loaded 7 tiles ago).
         if ((t & 7) == 7) thr = fminf(thr, dev::from_ordered_bits(fresh));
       }
@@ -612,11 +614,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (active) {
         const size_t slot = static_cast<size_t>(q) * a.n_chunks + chunk;
         for (int i = 0; i < cnt; ++i) {
-          a.cand_d[slot * kKK + i] = bd[i * kM];
-          a.cand_r[slot * kKK + i] = br[i * kM];
+          a.cand_d[slot * kKK + i] = bd[i * kLS];
+          a.cand_r[slot * kKK + i] = br[i * kLS];
         }
         a.cand_n[slot] = cnt;
-        if (cnt == kKK) atomicMin(a.thr_bits + q, dev::ordered_bits(bd[(kKK - 1) * kM]));
+        if (cnt == kKK) atomicMin(a.thr_bits + q, dev::ordered_bits(bd[(kKK - 1) * kLS]));
         // Merge this unit's output into the query's running best-kKK list and publish its kKK-th
         // value as the query's threshold: kKK distinct output candidates lie at or below it, which
         // is all a threshold needs. Each unit merges once (its rows are disjoint from every other
@@ -626,19 +628,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (cnt > 0 && atomicCAS(a.glock + q, 0, 1) == 0) {
           __threadfence();
           volatile float* gq = a.gbest + static_cast<size_t>(q) * kKK;
-          float* gs = bd + kKK * kM;
+          // Both lists are sorted, so each entry's place in the merged list is its index plus
+          // the number of entries of the other list before it (the running list first on ties);
+          // entries placed at kKK or beyond drop out.
+          float g[kKK];
 #pragma unroll
-          for (int o = 0; o < kKK; ++o) gs[o * kM] = gq[o];
-          int gi = 0, bi = 0;
+          for (int o = 0; o < kKK; ++o) g[o] = gq[o];
           float kth = kInfF;
+#pragma unroll
           for (int o = 0; o < kKK; ++o) {
-            const float gv = gi < kKK ? gs[gi * kM] : kInfF;
-            const float bv = bi < cnt ? bd[bi * kM] : kInfF;
-            const bool take_b = bv < gv;
-            kth = take_b ? bv : gv;
-            gq[o] = kth;
-            bi += take_b ? 1 : 0;
-            gi += take_b ? 0 : 1;
+            int before = 0;
+            for (int j = 0; j < cnt; ++j) before += bd[j * kLS] < g[o] ? 1 : 0;
+            const int pos = o + before;
+            if (pos < kKK) gq[pos] = g[o];
+            if (pos == kKK - 1) kth = g[o];
+          }
+          for (int j = 0; j < cnt; ++j) {
+            const float dv = bd[j * kLS];
+            int before = 0;
+#pragma unroll
+            for (int o = 0; o < kKK; ++o) before += g[o] <= dv ? 1 : 0;
+            const int pos = j + before;
+            if (pos < kKK) gq[pos] = dv;
+            if (pos == kKK - 1) kth = dv;
           }
           __threadfence();
           if (kth < kInfF) atomicMin(a.thr_bits + q, dev::ordered_bits(kth));
@@ -652,7 +664,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(kAcc * kN));
+                 "r"(kAcc * kTiles * kN));
   }
 }
 
@@ -849,8 +861,10 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   QV_REQUIRE(kk == 24 || kk == tc::kMaxKK, "tensor-core screen: unsupported best-list length");
   const int kpad = static_cast<int>(s.kpad);
   const bool l2 = s.metric == QV_METRIC_L2;
-  // Whole 128-row query tiles (zero rows past nq), so no TMA box extends past the tensor.
-  const size_t nq_pad = ceil_div(nq, tc::kM) * tc::kM;
+  // Whole query groups of kTiles x 128 rows (zero rows past nq), so no TMA box extends past the
+  // tensor.
+  const size_t group_rows = static_cast<size_t>(tc::kTiles) * tc::kM;
+  const size_t nq_pad = ceil_div(nq, group_rows) * group_rows;
   DeviceBuffer q16(nq_pad * kpad * sizeof(__half), st), qinv(nq * sizeof(float), st),
       qn2(nq * sizeof(float), st);
   QV_CUDA(cudaMemsetAsync(q16.get(), 0, nq_pad * kpad * sizeof(__half), st));
@@ -864,9 +878,9 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   const CUtensorMap mx = tc::make_map(s.x16.get(), s.n, kpad);
   tc::Args a{};
   a.nq = static_cast<int>(nq);
-  a.n_qtiles = static_cast<int>(ceil_div(nq, tc::kM));
+  a.n_qgroups = static_cast<int>(ceil_div(nq, group_rows));
   a.n_chunks = n_chunks;
-  a.total_units = a.n_qtiles * n_chunks;
+  a.total_units = a.n_qgroups * n_chunks;
   a.ksteps = kpad / 16;
   a.nrows = static_cast<int64_t>(s.n);
   a.chunk_rows = chunk_rows;
@@ -891,8 +905,8 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   a.glock = glock.get<int>();
   a.err = err;
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
-  const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (1 + tc::kStages) +
-                      static_cast<size_t>(kk + tc::kAppend) * tc::kM * 8 +
+  const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (tc::kTiles + tc::kStages) +
+                      static_cast<size_t>(kk + tc::kAppend) * tc::kLS * 8 +
                       (2 * tc::kStages + 2 * tc::kAcc + 2) * 8;
   const int grid = std::min(a.total_units, sm_count(s.device));
   KernelTimer timer(st, "flat_screen_tc_kernel", 2.0 * nq * static_cast<double>(s.n) * s.dim,
