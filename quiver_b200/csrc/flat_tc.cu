@@ -9,14 +9,17 @@
 // and reference rounding), and any query whose candidate set cannot be proven complete is
 // rescanned exactly.
 //
-// Kernel structure (one CTA per SM, persistent over work units = (query tile of 128, row chunk)):
-//   warp 0      TMA producer: the unit's query tile (A, resident) and a 4-stage ring of 128-row
-//               tiles of the database (B), 128-byte swizzled, no multicast.
-//   warp 1      MMA issuer: allocates TMEM, issues tcgen05.mma kind::f16 (M=128, N=128, K=16 steps)
-//               into one of four TMEM accumulators, commits to mbarriers.
-//   warps 2..5  epilogue: thread i of the 128 owns query i (= TMEM lane i), reads its 128 inner
-//               products with tcgen05.ld, and appends survivors of its running threshold to a
-//               private candidate buffer in shared memory (compacted warp-wide when it fills).
+// Kernel structure (one CTA per SM, persistent over work units = (query group of 2 x 128, row
+// chunk), chunk-major so that the CTAs working on a chunk share its rows in L2):
+//   warp 0      TMA producer: the unit's two query tiles (A, resident) and a 2-stage ring of
+//               128-row tiles of the database (B), 128-byte swizzled, no multicast.
+//   warp 1      MMA issuer: allocates TMEM, issues tcgen05.mma kind::f16 (M=128, N=128, K=16
+//               steps) of each row tile against both query tiles into one of two accumulator
+//               slots (2 x 128 columns each), commits to mbarriers.
+//   warps 2..9  epilogue: warp (tile, lane quarter); thread i owns query i of its tile (= TMEM
+//               lane), screens the tile's 128 inner products in two 64-column groups, and appends
+//               the 8-row groups that beat its running threshold to a candidate list in shared
+//               memory (compacted warp-wide when one fills).
 // Every mbarrier wait is bounded (2 s of GPU time); on timeout the CTA raises an error flag,
 // drains its outstanding copies (again bounded), frees TMEM and exits.
 #include <cuda.h>
