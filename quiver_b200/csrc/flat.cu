@@ -781,7 +781,9 @@ static int choose_chunks(size_t nrows, int n_qtiles, int max_chunks, int grid, i
     const double units = static_cast<double>(c) * n_qtiles;
     const double waves = std::ceil(units / grid);
     const double eff = units / (waves * grid);
-    if (eff > best_eff + 1e-9 || (std::fabs(eff - best_eff) <= 1e-9 && c > best)) {
+    // The fewest chunks within 2 % of the best wave efficiency: every work unit has a fixed cost
+    // (operand loads, its first rows screened against the query's looser threshold, its output).
+    if (eff > best_eff + 0.02) {
       best_eff = eff;
       best = c;
     }
