@@ -192,35 +192,14 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[64]) {
                :
                : "memory");
 }
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
-  float (&lo)[32] = *reinterpret_cast<float(*)[32]>(v);
-  float (&hi)[32] = *reinterpret_cast<float(*)[32]>(v + 32);
-  uint32_t r[64];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
-      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
-      "%30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, "
-      "%48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
-        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
-        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
-        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]),
-        "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]),
-        "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]),
-        "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
-        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]),
-        "=r"(r[62]), "=r"(r[63])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    lo[i] = __uint_as_float(r[i]);
-    hi[i] = __uint_as_float(r[32 + i]);
-  }
+// Orders every later use of r after the preceding tmem_wait_ld (for a second load waited for
+// by the same wait).
+__device__ __forceinline__ void tmem_hold(uint32_t (&r)[64]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]), "+r"(r[32]), "+r"(r[33]), "+r"(r[34]), "+r"(r[35]), "+r"(r[36]), "+r"(r[37]), "+r"(r[38]), "+r"(r[39]), "+r"(r[40]), "+r"(r[41]), "+r"(r[42]), "+r"(r[43]), "+r"(r[44]), "+r"(r[45]), "+r"(r[46]), "+r"(r[47]), "+r"(r[48]), "+r"(r[49]), "+r"(r[50]), "+r"(r[51]), "+r"(r[52]), "+r"(r[53]), "+r"(r[54]), "+r"(r[55]), "+r"(r[56]), "+r"(r[57]), "+r"(r[58]), "+r"(r[59]), "+r"(r[60]), "+r"(r[61]), "+r"(r[62]), "+r"(r[63])
+               :
+               : "memory");
 }
-
 // Screen distance of one accumulator element: for L2 the element already is the distance; for
 // cosine / inner product it is the raw (scaled) inner product and the distance is 1 - dot * inv.
 // fmaf rounds once and is monotone in the element, so the best raw value gives the best distance.
@@ -462,11 +441,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int tq = 0; tq < kTiles; ++tq) {
             const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((accb * kTiles + tq) * kN);
             const uint32_t at_addr = a_addr + static_cast<uint32_t>(tq * kAtoms * kAtomBytes);
-            for (int ks = 0; ks < a.ksteps; ++ks) {
-              const int at = ks >> 2, kin = ks & 3;
-              const uint32_t off = static_cast<uint32_t>(at * kAtomBytes + kin * 32);
-              umma_f16(d_tmem, smem_desc(at_addr + off), smem_desc(b_addr + off),
-                       ks > 0 ? 1u : 0u);
+            // Unrolled over the largest K-step count: issued from a runtime loop, each MMA
+            // took longer to issue (~110 cycles) than the 64 cycles it executes in.
+#pragma unroll
+            for (int ks = 0; ks < kAtoms * 4; ++ks) {
+              if (ks < a.ksteps) {
+                const int at = ks >> 2, kin = ks & 3;
+                const uint32_t off = static_cast<uint32_t>(at * kAtomBytes + kin * 32);
+                umma_f16(d_tmem, smem_desc(at_addr + off), smem_desc(b_addr + off),
+                         ks > 0 ? 1u : 0u);
+              }
             }
           }
           umma_commit(bar(EMPTY + stage));
@@ -556,33 +540,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool may = active && screen_value<kL2>(top, inv) <= thr;
         if (!__any_sync(0xffffffffu, may)) return;
         static_assert(kTcGroupRows == 8, "the group tree is built for 8-row groups");
-        // Which 8-row groups this lane can improve on, and their union over the warp. A group
-        // enters the candidate list as one entry: its best screen value and its index (rows
-        // 8 * index .. 8 * index + 7); the exact re-rank expands it.
+        // Which 8-row groups this lane can improve on. A group enters the candidate list as one
+        // entry: its best screen value and its index (rows 8 * index .. 8 * index + 7); the exact
+        // re-rank expands it.
         uint32_t gm = 0;
 #pragma unroll
         for (int g = 0; g < 8; ++g)
           gm |= (may && screen_value<kL2>(best[g], inv) <= thr) ? (1u << g) : 0u;
-        const uint32_t wm = __reduce_or_sync(0xffffffffu, gm);
+        // Make room first (all lanes together) when some lane's appends would overflow its
+        // list; compaction tightens the threshold, so the groups are tested again.
+        if (__any_sync(0xffffffffu, cnt + __popc(gm) > kCap)) {
+          compact_buffer<kKK>(bd, br, cnt, thr);
+          uint32_t keep = 0;
+#pragma unroll
+          for (int g = 0; g < 8; ++g)
+            keep |= (screen_value<kL2>(best[g], inv) <= thr) ? (1u << g) : 0u;
+          gm &= keep;
+        }
+        // At most 8 appends and kAppend >= 8 free entries: no further checks.
+        static_assert(kAppend >= 8, "a 64-column group appends up to 8 entries");
 #pragma unroll
         for (int g = 0; g < 8; ++g) {
-          if (!((wm >> g) & 1u)) continue;  // warp-uniform
-          bool sub = (gm >> g) & 1u;
-          const float bv = screen_value<kL2>(best[g], inv);
-          // Compact (all lanes together) when some lane's list is full.
-          if (__any_sync(0xffffffffu, sub && cnt >= kCap)) {
-            compact_buffer<kKK>(bd, br, cnt, thr);
-            sub = sub && bv <= thr;
-          }
-          if (sub) {
-            bd[cnt * kLS] = bv;
+          if ((gm >> g) & 1u) {
+            bd[cnt * kLS] = screen_value<kL2>(best[g], inv);
             br[cnt * kLS] = static_cast<uint32_t>(cb / kTcGroupRows + g);
             ++cnt;
-            ++seen;
           }
         }
+        seen += __popc(gm);
       };
-      uint32_t ra[64];
+      uint32_t ra[64], rb[64];
       unsigned fresh = ~0u;  // the query's shared threshold, read early and applied later
       for (int t = 0; t < ntiles; ++t) {
         const int64_t row0 = r0 + static_cast<int64_t>(t) * kN;
@@ -592,18 +579,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + col0 +
                                static_cast<uint32_t>(accb * kTiles * kN);
-#pragma unroll 1
-        for (int h = 0; h < kN / 64; ++h) {
-          tmem_ld64_issue(taddr + h * 64, ra);
-          tmem_wait_ld(ra);
-          if (h == kN / 64 - 1) {
-            // The tile is out of TMEM: hand its accumulator back to the MMA warp.
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar(ACC_EMPTY + accb));
-          }
-          group(ra, row0 + h * 64);
-        }
+        // Both 64-column halves in one round trip; the accumulator goes back to the MMA warp
+        // before any screening, so the next MMAs into this slot wait only for the loads.
+        static_assert(kN == 128, "the epilogue loads a tile as two 64-column halves");
+        tmem_ld64_issue(taddr, ra);
+        tmem_ld64_issue(taddr + 64, rb);
+        tmem_wait_ld(ra);
+        tmem_hold(rb);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(ACC_EMPTY + accb));
+        group(ra, row0);
+        group(rb, row0 + 64);
         if (++accb == kAcc) {
           accb = 0;
           acc_phase ^= 1;
