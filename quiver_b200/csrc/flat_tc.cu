@@ -250,67 +250,78 @@ __device__ __forceinline__ void group_best8(const float (&v)[64], float (&best)[
 // KK entries (padded with (+inf, ~0) at the start of a work unit) followed by up to kAppend
 // entries appended since (kCap = KK + kAppend in all).
 
-// Sorts the kAppend appended entries by (distance, row): a fully unrolled bitonic network, each
-// lane on its own list (no divergence), so the loads of one stage's independent
-// compare-exchanges overlap.
-__device__ __noinline__ void sort_appended(float* d, uint32_t* r) {
+// Compare-exchange of two (distance, group) entries in registers: afterwards (da, ra) is the
+// smaller in (distance, group) order.
+__device__ __forceinline__ void cex(float& da, uint32_t& ra, float& db, uint32_t& rb) {
+  const bool sw = dev::key_less(db, rb, da, ra);
+  const float td = sw ? db : da;
+  const uint32_t tr = sw ? rb : ra;
+  db = sw ? da : db;
+  rb = sw ? ra : rb;
+  da = td;
+  ra = tr;
+}
+
+// Keeps the best kKK of a query's list, sorted, and tightens the threshold to the kKK-th distance
+// (+inf while fewer than kKK real entries were seen). The list is loaded into registers and
+// merged there by fixed networks (no per-lane branches, so the warp never diverges): the appended
+// entries (padded with (+inf, ~0)) are sorted by a 16-input bitonic network; with the prefix a
+// (sorted, padded to 32) and the sorted appended entries b (padded to 32), c[i] = min(a[i],
+// b[31 - i]) holds the 32 smallest of both as a bitonic sequence, which a 32-input bitonic merge
+// sorts.
+template <int kKK>
+__device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, float& thr) {
+  static_assert(kAppend == 16 && kKK <= 32, "networks sized for 16 appended, 32 kept");
+  const float kInf = __int_as_float(0x7f800000);
+  float bd[16];
+  uint32_t br[16];
 #pragma unroll
-  for (int size = 2; size <= kAppend; size <<= 1) {
+  for (int i = 0; i < 16; ++i) {
+    const bool in = kKK + i < cnt;
+    bd[i] = in ? d[(kKK + i) * kLS] : kInf;
+    br[i] = in ? r[(kKK + i) * kLS] : 0xffffffffu;
+  }
+#pragma unroll
+  for (int size = 2; size <= 16; size <<= 1) {
 #pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
 #pragma unroll
-      for (int i = 0; i < kAppend / 2; ++i) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool up = (lo & size) == 0;
-        const float dl = d[lo * kLS], dh = d[hi * kLS];
-        const uint32_t rl = r[lo * kLS], rh = r[hi * kLS];
-        const bool swap = up ? dev::key_less(dh, rh, dl, rl) : dev::key_less(dl, rl, dh, rh);
-        d[lo * kLS] = swap ? dh : dl;
-        d[hi * kLS] = swap ? dl : dh;
-        r[lo * kLS] = swap ? rh : rl;
-        r[hi * kLS] = swap ? rl : rh;
+      for (int i = 0; i < 8; ++i) {
+        const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+        if ((lo & size) == 0)
+          cex(bd[lo], br[lo], bd[hi], br[hi]);
+        else
+          cex(bd[hi], br[hi], bd[lo], br[lo]);
       }
     }
   }
-}
-
-// Keeps the best kKK of a query's list: sorts the appended part and merges it into the sorted
-// prefix from the back (which never overwrites an entry not yet read). The threshold then tightens
-// to the kKK-th distance (+inf while fewer than kKK real entries were seen).
-template <int kKK>
-__device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, float& thr) {
-  constexpr int kCap = kKK + kAppend;
-  if (cnt > kKK) {
-    for (int i = cnt; i < kCap; ++i) {
-      d[i * kLS] = __int_as_float(0x7f800000);
-      r[i * kLS] = 0xffffffffu;
+  float cd[32];
+  uint32_t cr[32];
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    cd[i] = i < kKK ? d[i * kLS] : kInf;
+    cr[i] = i < kKK ? r[i * kLS] : 0xffffffffu;
+    if (31 - i < 16) {
+      const bool tb = dev::key_less(bd[31 - i], br[31 - i], cd[i], cr[i]);
+      cd[i] = tb ? bd[31 - i] : cd[i];
+      cr[i] = tb ? br[31 - i] : cr[i];
     }
-    float* bd = d + kKK * kLS;
-    uint32_t* br = r + kKK * kLS;
-    const int nb = cnt - kKK;
-    sort_appended(bd, br);
-    int ia = 0, ib = 0;  // how many of the prefix / the appended part are among the best kKK
-    for (int o = 0; o < kKK; ++o) {
-      const bool take_b = ib < nb && dev::key_less(bd[ib * kLS], br[ib * kLS], d[ia * kLS], r[ia * kLS]);
-      ib += take_b ? 1 : 0;
-      ia += take_b ? 0 : 1;
-    }
-    int pa = ia - 1, pb = ib - 1;
-    for (int o = kKK - 1; o >= 0; --o) {
-      const int ja = max(pa, 0), jb = max(pb, 0);
-      const bool take_b =
-          pb >= 0 && (pa < 0 || dev::key_less(d[ja * kLS], r[ja * kLS], bd[jb * kLS], br[jb * kLS]));
-      const float dv = take_b ? bd[jb * kLS] : d[ja * kLS];
-      const uint32_t rv = take_b ? br[jb * kLS] : r[ja * kLS];
-      d[o * kLS] = dv;
-      r[o * kLS] = rv;
-      pb -= take_b ? 1 : 0;
-      pa -= take_b ? 0 : 1;
-    }
-    cnt = kKK;
   }
-  thr = fminf(thr, d[(kKK - 1) * kLS]);
+#pragma unroll
+  for (int stride = 16; stride > 0; stride >>= 1) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+      cex(cd[lo], cr[lo], cd[hi], cr[hi]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kKK; ++i) {
+    d[i * kLS] = cd[i];
+    r[i * kLS] = cr[i];
+  }
+  cnt = kKK;
+  thr = fminf(thr, cd[kKK - 1]);
 }
 
 template <int kAtoms, bool kL2, int kKK>
@@ -506,9 +517,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       int cnt = kKK, seen = 0;
       bool ok = true;
-      // One 64-column group of a tile: rows cb .. cb + 63 (cb a multiple of 64: chunks are
-      // multiples of kN rows).
-      auto group = [&](uint32_t (&r)[64], int64_t cb) {
+      // One 64-column half of a tile: rows cb .. cb + 63 (cb a multiple of 64: chunks are
+      // multiples of kN rows). best[g]: the best score among elements 8g..8g+7 (max inner product
+      // for cosine/IP, min distance for L2); top: the best of all 64.
+      auto tree = [&](uint32_t (&r)[64], int64_t cb, float (&best)[8], float& top) {
         float (&v)[64] = *reinterpret_cast<float(*)[64]>(r);  // the loaded bits, used in place
         const int valid = static_cast<int>(r1 - cb < 64 ? r1 - cb : 64);  // rows of this chunk
         // Rows past the chunk end and rows the filter rejects take the worst score, so that
@@ -516,10 +528,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t admitted =
             (valid >= 64 ? ~0ull : (valid > 0 ? (1ull << valid) - 1 : 0ull)) &
             (a.bitmap != nullptr && valid > 0 ? a.bitmap[static_cast<uint64_t>(cb) >> 6] : ~0ull);
-        // best[g]: the best score among elements 8g..8g+7 (max inner product for cosine/IP,
-        // min distance for L2); top: the best of all 64.
-        float best[8];
-        float top;
         if (kL2) {
           // v[j] := ||q||^2 + ||x||^2 - 2<q,x>
 #pragma unroll
@@ -537,12 +545,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           group_best8<true>(v, best, top);
         }
+      };
+      // Appends the 8-row groups of one half that this lane can improve on. A group enters the
+      // candidate list as one entry: its best screen value and its index (rows 8 * index ..
+      // 8 * index + 7); the exact re-rank expands it.
+      auto screen = [&](const float (&best)[8], float top, int64_t cb) {
         const bool may = active && screen_value<kL2>(top, inv) <= thr;
         if (!__any_sync(0xffffffffu, may)) return;
         static_assert(kTcGroupRows == 8, "the group tree is built for 8-row groups");
-        // Which 8-row groups this lane can improve on. A group enters the candidate list as one
-        // entry: its best screen value and its index (rows 8 * index .. 8 * index + 7); the exact
-        // re-rank expands it.
         uint32_t gm = 0;
 #pragma unroll
         for (int g = 0; g < 8; ++g)
@@ -557,17 +567,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             keep |= (screen_value<kL2>(best[g], inv) <= thr) ? (1u << g) : 0u;
           gm &= keep;
         }
-        // At most 8 appends and kAppend >= 8 free entries: no further checks.
+        // At most 8 appends and kAppend >= 8 free entries: no further checks. Each entry's
+        // position is cnt plus the number of groups before it, so the stores are independent.
         static_assert(kAppend >= 8, "a 64-column group appends up to 8 entries");
 #pragma unroll
         for (int g = 0; g < 8; ++g) {
           if ((gm >> g) & 1u) {
-            bd[cnt * kLS] = screen_value<kL2>(best[g], inv);
-            br[cnt * kLS] = static_cast<uint32_t>(cb / kTcGroupRows + g);
-            ++cnt;
+            const int pos = cnt + __popc(gm & ((1u << g) - 1u));
+            bd[pos * kLS] = screen_value<kL2>(best[g], inv);
+            br[pos * kLS] = static_cast<uint32_t>(cb / kTcGroupRows + g);
           }
         }
-        seen += __popc(gm);
+        const int np = __popc(gm);
+        cnt += np;
+        seen += np;
       };
       uint32_t ra[64], rb[64];
       unsigned fresh = ~0u;  // the query's shared threshold, read early and applied later
@@ -589,8 +602,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar(ACC_EMPTY + accb));
-        group(ra, row0);
-        group(rb, row0 + 64);
+        // Both trees first: the loaded values are dead before any list work (compaction needs
+        // the registers).
+        float best_a[8], best_b[8], top_a, top_b;
+        tree(ra, row0, best_a, top_a);
+        tree(rb, row0 + 64, best_b, top_b);
+        screen(best_a, top_a, row0);
+        screen(best_b, top_b, row0 + 64);
         if (++accb == kAcc) {
           accb = 0;
           acc_phase ^= 1;
