@@ -407,8 +407,10 @@ __device__ __forceinline__ float warp_exact_distance(const float* q, const float
 __device__ __forceinline__ float nan_to_inf(float d) { return d == d ? d : __int_as_float(0x7f800000); }
 
 // Strict weak order on (distance, key): the canonical tie-break used by every selection.
+// Bitwise, not short-circuit, operators: the compare stays branch-free (in the sorting networks
+// the short-circuit form was compiled to divergent branches and ran ~3x slower).
 __device__ __forceinline__ bool key_less(float da, uint64_t ka, float db, uint64_t kb) {
-  return da < db || (da == db && ka < kb);
+  return (da < db) | ((da == db) & (ka < kb));
 }
 
 // float -> uint32 whose unsigned order matches the float order (for atomicMin on thresholds).
