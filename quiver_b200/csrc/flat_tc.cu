@@ -324,6 +324,23 @@ __device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, flo
   thr = fminf(thr, cd[kKK - 1]);
 }
 
+// One row tile's MMAs against every query tile of the group, kSteps K-steps of 16 each, fully
+// unrolled: issued from a loop with a runtime trip count, each MMA took longer to issue than the
+// 64 cycles a 128 x 128 x 16 MMA executes in, and even a guarded unrolled loop cost ~10 %.
+template <int kAtoms, int kSteps>
+__device__ __forceinline__ void issue_tile(uint32_t d_base, uint32_t a_addr, uint32_t b_addr) {
+#pragma unroll
+  for (int tq = 0; tq < kTiles; ++tq) {
+#pragma unroll
+    for (int ks = 0; ks < kSteps; ++ks) {
+      const uint32_t off = static_cast<uint32_t>((ks >> 2) * kAtomBytes + (ks & 3) * 32);
+      umma_f16(d_base + static_cast<uint32_t>(tq * kN),
+               smem_desc(a_addr + static_cast<uint32_t>(tq * kAtoms * kAtomBytes) + off),
+               smem_desc(b_addr + off), ks > 0 ? 1u : 0u);
+    }
+  }
+}
+
 template <int kAtoms, bool kL2, int kKK>
 __global__ void __launch_bounds__(kThreads, 1)
     flat_screen_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
@@ -449,19 +466,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           s_consumed = ++consumed;
           tc_fence_after();
           const uint32_t b_addr = smem_u32(smem_b + stage * kAtoms * kAtomBytes);
-          for (int tq = 0; tq < kTiles; ++tq) {
-            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((accb * kTiles + tq) * kN);
-            const uint32_t at_addr = a_addr + static_cast<uint32_t>(tq * kAtoms * kAtomBytes);
-            // Unrolled over the largest K-step count: issued from a runtime loop, each MMA
-            // took longer to issue (~110 cycles) than the 64 cycles it executes in.
-#pragma unroll
-            for (int ks = 0; ks < kAtoms * 4; ++ks) {
-              if (ks < a.ksteps) {
-                const int at = ks >> 2, kin = ks & 3;
-                const uint32_t off = static_cast<uint32_t>(at * kAtomBytes + kin * 32);
-                umma_f16(d_tmem, smem_desc(at_addr + off), smem_desc(b_addr + off),
-                         ks > 0 ? 1u : 0u);
-              }
+          const uint32_t d_base = tmem_base + static_cast<uint32_t>(accb * kTiles * kN);
+          if (kAtoms == 1) {
+            issue_tile<1, 4>(d_base, a_addr, b_addr);
+          } else {
+            switch (a.ksteps) {
+              case 5: issue_tile<kAtoms, 5>(d_base, a_addr, b_addr); break;
+              case 6: issue_tile<kAtoms, 6>(d_base, a_addr, b_addr); break;
+              case 7: issue_tile<kAtoms, 7>(d_base, a_addr, b_addr); break;
+              default: issue_tile<kAtoms, 8>(d_base, a_addr, b_addr); break;
             }
           }
           umma_commit(bar(EMPTY + stage));

@@ -147,16 +147,18 @@ def test_config0_full_size_against_reference(gpu, reference):
     assert_topk_parity(l, d, rl, rd, exact=True, what="config0")
 
 
-@pytest.mark.parametrize("metric", ["l2", "ip", "cosine"])
-def test_tensor_core_screen_equals_simt_screen(gpu, oracle, monkeypatch, metric):
+# dim 50 pads to one 64-column atom (4 K-steps); 72, 96, 100 and 128 take 5, 6, 7 and 8.
+@pytest.mark.parametrize("metric,dim", [("l2", 100), ("ip", 100), ("cosine", 100), ("l2", 50),
+                                        ("ip", 72), ("cosine", 96), ("l2", 128)])
+def test_tensor_core_screen_equals_simt_screen(gpu, oracle, monkeypatch, metric, dim):
     """The tcgen05 fp16 screen and the float32 SIMT screen must produce identical final results
     (both are re-ranked exactly and certified)."""
     from quiver_b200.synthetic import mixture
-    base = mixture(20000, 100, 50, 0.35, 1.0, centre_seed=3, seed=4)
+    base = mixture(20000, dim, 50, 0.35, 1.0, centre_seed=3, seed=4)
     if metric != "cosine":
         base = base * np.float32(3.0)
-    q = mixture(300, 100, 50, 0.35, 1.0, centre_seed=3, seed=5)
-    ix = gpu.FlatIndex(100, metric)
+    q = mixture(300, dim, 50, 0.35, 1.0, centre_seed=3, seed=5)
+    ix = gpu.FlatIndex(dim, metric)
     ix.add(base)
     stored = oracle.normalize_rows(base) if metric == "cosine" else base
     for k in (10, 20):  # best lists of 24 and of 32 groups
