@@ -355,27 +355,30 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* buf_d = reinterpret_cast<float*>(smem_b + kStages * kAtoms * kAtomBytes);  // kCap x kLS
   uint32_t* buf_r = reinterpret_cast<uint32_t*>(buf_d + kCap * kLS);
   uint64_t* bars = reinterpret_cast<uint64_t*>(buf_r + kCap * kLS);
-  // bars: full[kStages], empty[kStages], acc_full[kAcc], acc_empty[kAcc], a_full, a_empty
+  // bars: full[kStages], empty[kStages], acc_full[kAcc], a_full, a_empty.
+  // full[s] also stands for "accumulator slot s is free": row tile t uses stage t % kStages and
+  // slot t % kAcc (kStages == kAcc), and full[s] completes only when the tile's bytes have
+  // landed AND every epilogue warp has read the slot's previous tile out of TMEM. The MMA warp
+  // then waits on one mbarrier per tile: each wait in the issuing thread costs the tensor pipe
+  // ~200 cycles of idle time, even on a phase that completed long before.
+  static_assert(kStages == kAcc, "stage and accumulator slot of a row tile coincide");
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ int s_consumed;  // B fills the MMA warp has waited for (for the abort drain)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   auto bar = [&](int i) { return smem_u32(bars + i); };
-  const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, ACC_EMPTY = 2 * kStages + kAcc,
-            A_FULL = 2 * kStages + 2 * kAcc, A_EMPTY = 2 * kStages + 2 * kAcc + 1;
+  const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, A_FULL = 2 * kStages + kAcc,
+            A_EMPTY = 2 * kStages + kAcc + 1;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
     s_consumed = 0;
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(FULL + s), 1);
+      mbar_init(bar(FULL + s), 1 + kEpiWarps);  // the producer's expect_tx + each epilogue warp
       mbar_init(bar(EMPTY + s), 1);
     }
-    for (int b = 0; b < kAcc; ++b) {
-      mbar_init(bar(ACC_FULL + b), 1);
-      mbar_init(bar(ACC_EMPTY + b), kEpiWarps);  // one arrival per epilogue warp
-    }
+    for (int b = 0; b < kAcc; ++b) mbar_init(bar(ACC_FULL + b), 1);
     mbar_init(bar(A_FULL), 1);
     mbar_init(bar(A_EMPTY), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -444,7 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       int stage = 0, accb = 0;
-      uint32_t phase = 0, acc_phase = 0, a_phase = 0;
+      uint32_t phase = 0, a_phase = 0;
       int consumed = 0;
       for (int u = blockIdx.x; u < a.total_units && !*abort_flag; u += gridDim.x) {
         int qgroup, chunk;
@@ -458,9 +461,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t a_addr = smem_u32(smem_a);
         bool ok = true;
         for (int t = 0; t < ntiles && ok; ++t) {
-          ok = mbar_wait(bar(ACC_EMPTY + accb), acc_phase ^ 1, abort_flag, a.err);
-          if (!ok) break;
-          tc_fence_after();
           ok = mbar_wait(bar(FULL + stage), phase, abort_flag, a.err);
           if (!ok) break;
           s_consumed = ++consumed;
@@ -483,10 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             stage = 0;
             phase ^= 1;
           }
-          if (++accb == kAcc) {
-            accb = 0;
-            acc_phase ^= 1;
-          }
+          if (++accb == kAcc) accb = 0;
         }
         if (!ok) break;
         umma_commit(bar(A_EMPTY));
@@ -510,6 +507,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float kInfF = __int_as_float(0x7f800000);
     int accb = 0;
     uint32_t acc_phase = 0;
+    // The first row tile of each slot has no previous tile to wait for.
+    if (lane == 0)
+      for (int b = 0; b < kAcc; ++b) mbar_arrive(bar(FULL + b));
     for (int u = blockIdx.x; u < a.total_units; u += gridDim.x) {
       int qgroup, chunk;
       unit_coords(a, u, qgroup, chunk);
@@ -614,7 +614,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_hold(rb);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(ACC_EMPTY + accb));
+        if (lane == 0) mbar_arrive(bar(FULL + accb));  // the slot is free for tile t + kAcc
         // Both trees first: the loaded values are dead before any list work (compaction needs
         // the registers).
         float best_a[8], best_b[8], top_a, top_b;
@@ -928,7 +928,7 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
   const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (tc::kTiles + tc::kStages) +
                       static_cast<size_t>(kk + tc::kAppend) * tc::kLS * 8 +
-                      (2 * tc::kStages + 2 * tc::kAcc + 2) * 8;
+                      (2 * tc::kStages + tc::kAcc + 2) * 8;
   const int grid = std::min(a.total_units, sm_count(s.device));
   KernelTimer timer(st, "flat_screen_tc_kernel", 2.0 * nq * static_cast<double>(s.n) * s.dim,
                     false);
