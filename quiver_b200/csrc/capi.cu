@@ -480,8 +480,10 @@ qv_status qv_flat_search(const qv_flat* index, const float* queries, size_t nq, 
                "search_batch: null buffer");
     const FlatState& s = index->s;
     const size_t total = result_size(nq, k);
-    check_finite(queries, nq * s.dim);
     std::shared_lock lock(index->mu);
+    // The search checks the queries for NaN and infinity on the device (and raises before any
+    // result is copied out); with no stored rows it launches nothing, so check here.
+    if (s.n == 0) check_finite(queries, nq * s.dim);
     DeviceScope scope(s.device);
     cudaStream_t st = thread_stream(s.device);
     DeviceBuffer dq, dl(total * sizeof(uint64_t), st), dd(total * sizeof(float), st);

@@ -100,14 +100,23 @@ struct EpsModel {
 
 // Queries -> zero-padded rows (dpad columns), normalized for cosine; squared norm, and the SIMT
 // screen's error bound eps[q] (the tensor-core screen overwrites eps with its own bound).
+// Raises *nonfinite (when given) if a query holds NaN or infinity: the reference rejects such
+// queries (src/flat_index.cc:131), and checking here, where the queries are read anyway, keeps the
+// host from scanning the batch before each search.
 __global__ void prep_queries_kernel(const float* q, size_t nq, int dim, int dpad, bool cosine,
                                     bool l2, EpsModel em, float xmax, float* qp, float* qnorm2,
-                                    float* eps) {
+                                    float* eps, int* nonfinite) {
   const int lane = threadIdx.x & 31;
   const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= nq) return;
   float* out = qp + row * dpad;
-  for (int i = lane; i < dpad; i += 32) out[i] = i < dim ? q[row * dim + i] : 0.0f;
+  bool bad = false;
+  for (int i = lane; i < dpad; i += 32) {
+    const float v = i < dim ? q[row * dim + i] : 0.0f;
+    bad |= (__float_as_uint(v) & 0x7f800000u) == 0x7f800000u;
+    out[i] = v;
+  }
+  if (nonfinite != nullptr && __any_sync(kFull, bad) && lane == 0) atomicOr(nonfinite, 1);
   __syncwarp();
   if (cosine) warp_normalize(out, dim, lane);
   float s = 0.0f;
@@ -821,10 +830,18 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
   em.c_abs = static_cast<float>(2.0 * (2.0 * u));
   DeviceBuffer qp(nq * dpad * sizeof(float), st), qn2(nq * sizeof(float), st),
       eps(nq * sizeof(float), st);
+  // [0] queries that were rescanned, [1] non-finite query flag, then the rescan list.
+  DeviceBuffer fail(2 * sizeof(int) + nq * (sizeof(int) + sizeof(float)), st);
+  int* fail_count = fail.get<int>();
+  int* nonfinite = fail_count + 1;
+  int* fail_q = fail_count + 2;
+  float* fail_dk = reinterpret_cast<float*>(fail_q + nq);
+  QV_CUDA(cudaMemsetAsync(fail_count, 0, 2 * sizeof(int), st));
   prep_queries_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(d_queries, nq, dim, dpad,
                                                        s.metric == QV_METRIC_COSINE, l2, em,
                                                        s.max_norm, qp.get<float>(),
-                                                       qn2.get<float>(), eps.get<float>());
+                                                       qn2.get<float>(), eps.get<float>(),
+                                                       nonfinite);
   check_launch("prep_queries_kernel");
 
   // QV_FLAT_KK overrides the candidate budget of the SIMT screen (any value >= k); small budgets
@@ -901,11 +918,6 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
   const int group_rows = tensor ? kTcGroupRows : 1;
   const int pool = static_cast<int>(std::max(next_pow2(static_cast<size_t>(n_chunks) * kk),
                                              next_pow2(static_cast<size_t>(kk) * group_rows)));
-  DeviceBuffer fail(sizeof(int) + nq * (sizeof(int) + sizeof(float)), st);
-  int* fail_count = fail.get<int>();
-  int* fail_q = fail_count + 1;
-  float* fail_dk = reinterpret_cast<float*>(fail_q + nq);
-  QV_CUDA(cudaMemsetAsync(fail_count, 0, sizeof(int), st));
   if (tensor) {
     QV_REQUIRE(n_chunks <= 64, "group finalize: more than 64 row chunks");
     const size_t gsmem =
@@ -940,10 +952,11 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
       s.labels.get<uint64_t>(), d_bitmap, s.row_offset, l2, static_cast<int>(k), cap, fail_count,
       fail_q, fail_dk, d_labels, d_dists, d_keys);
   check_launch("flat_rescan_kernel");
-  int nfail = 0;
-  QV_CUDA(cudaMemcpyAsync(&nfail, fail_count, sizeof(int), cudaMemcpyDeviceToHost, st));
+  int flags[2] = {0, 0};
+  QV_CUDA(cudaMemcpyAsync(flags, fail_count, sizeof(flags), cudaMemcpyDeviceToHost, st));
   QV_CUDA(cudaStreamSynchronize(st));
-  thread_stats().rescanned_queries += static_cast<uint64_t>(nfail);
+  QV_REQUIRE(flags[1] == 0, "vectors must not contain NaN or infinity");
+  thread_stats().rescanned_queries += static_cast<uint64_t>(flags[0]);
 }
 
 // ---- allocation-free search ------------------------------------------------------------------------
@@ -1070,7 +1083,7 @@ void flat_search_noalloc(const FlatState& s, const float* d_queries, size_t nq, 
   em.c_abs = static_cast<float>(2.0 * (2.0 * u));
   prep_queries_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(d_queries, nq, dim, L.dpad,
                                                        s.metric == QV_METRIC_COSINE, l2, em,
-                                                       s.max_norm, qp, qn2, eps);
+                                                       s.max_norm, qp, qn2, eps, nullptr);
   check_launch("prep_queries_kernel");
   // The scratch keeps the previous call's contents: reset what must start empty.
   QV_CUDA(cudaMemsetAsync(cand_n, 0, slots * sizeof(int), st));

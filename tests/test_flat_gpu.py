@@ -79,7 +79,7 @@ def test_fewer_than_k_and_filters(gpu):
     assert (l == -1).all()
 
 
-def test_empty_index_and_errors(gpu):
+def test_empty_index_and_errors(gpu, monkeypatch):
     ix = gpu.FlatIndex(4)
     l, d = ix.search(np.ones((2, 4)), 3)
     assert (l == -1).all() and np.isinf(d).all()
@@ -87,6 +87,20 @@ def test_empty_index_and_errors(gpu):
         ix.add(np.array([[1, np.nan, 0, 0]], np.float32))
     with pytest.raises(ValueError, match="NaN"):
         ix.search(np.array([[1, np.inf, 0, 0]], np.float32), 1)
+    # With rows stored the device search itself detects the non-finite query (and copies no
+    # results out); both the tensor-core and the SIMT screen paths.
+    full = gpu.FlatIndex(4)
+    full.add(np.random.default_rng(1).standard_normal((300, 4)).astype(np.float32))
+    for screen in ("", "simt"):
+        monkeypatch.setenv("QV_FLAT_SCREEN", screen)
+        for bad in (np.nan, np.inf, -np.inf):
+            q = np.ones((20, 4), np.float32)
+            q[7, 2] = bad
+            with pytest.raises(ValueError, match="NaN"):
+                full.search(q, 3)
+        l, _ = full.search(np.ones((20, 4), np.float32), 3)  # the index stays usable
+        assert (l >= 0).all()
+    monkeypatch.delenv("QV_FLAT_SCREEN")
     with pytest.raises(ValueError, match="2\\*\\*63"):
         ix.add(np.zeros((1, 4)), labels=[2**63])
     with pytest.raises(ValueError, match="dimension"):
