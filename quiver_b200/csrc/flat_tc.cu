@@ -42,7 +42,11 @@ constexpr int kAtomBytes = 128 * 128;  // one 128-row x 128-byte swizzle atom co
 constexpr int kTiles = 2;        // query tiles per CTA: every row tile feeds one MMA per query tile
 constexpr int kStages = 2;       // row-tile ring depth
 constexpr int kEpiWarps = 4 * kTiles;  // one warp per (query tile, TMEM lane quarter)
-constexpr int kThreads = 64 + 32 * kEpiWarps;
+// Warps: 0 TMA producer, 1 MMA issuer of even row tiles, 2 .. 1 + kEpiWarps epilogue, and
+// kIssuer2 MMA issuer of odd row tiles. Each mbarrier wait in an issuing thread leaves the tensor
+// pipe idle for ~200 cycles; with two issuers one waits while the other's MMAs run.
+constexpr int kIssuer2 = 2 + kEpiWarps;
+constexpr int kThreads = 32 * (kIssuer2 + 1);
 constexpr int kAcc = 2;          // TMEM accumulator slots of kTiles x kN columns (all 512 columns)
 constexpr int kAppend = 16;      // list entries appended between compactions
 constexpr int kLS = kTiles * kM; // candidate-list stride: entry i of list l lives at i * kLS + l
@@ -364,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(kStages == kAcc, "stage and accumulator slot of a row tile coincide");
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
-  __shared__ int s_consumed;  // B fills the MMA warp has waited for (for the abort drain)
+  __shared__ int s_consumed[2];  // B fills each MMA issuer has waited for (abort drain)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   auto bar = [&](int i) { return smem_u32(bars + i); };
@@ -373,14 +377,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     s_abort = 0;
-    s_consumed = 0;
+    s_consumed[0] = s_consumed[1] = 0;
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(FULL + s), 1 + kEpiWarps);  // the producer's expect_tx + each epilogue warp
       mbar_init(bar(EMPTY + s), 1);
     }
     for (int b = 0; b < kAcc; ++b) mbar_init(bar(ACC_FULL + b), 1);
     mbar_init(bar(A_FULL), 1);
-    mbar_init(bar(A_EMPTY), 1);
+    mbar_init(bar(A_EMPTY), 2);  // one commit per MMA issuer
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -435,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*abort_flag) {
         // Drain: wait (bounded) for every B fill the MMA warp did not consume.
         const uint64_t t0 = gtimer();
-        for (int f = s_consumed; f < issued; ++f) {
+        for (int f = s_consumed[0] + s_consumed[1]; f < issued; ++f) {
           const int s = f % kStages;
           const uint32_t par = (f / kStages) & 1;
           while (!mbar_test(bar(FULL + s), par) && gtimer() - t0 < kTimeoutNs) {
@@ -443,12 +447,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1 || warp == kIssuer2) {
+    // ---------------- MMA issuers ----------------
+    // Issuer `me` takes the row tiles whose index (counted over all of this CTA's units) has
+    // parity me, which are exactly the tiles of stage and accumulator slot me.
+    static_assert(kStages == 2, "one issuer per stage");
+    const int me = warp == 1 ? 0 : 1;
     if (lane == 0) {
-      int stage = 0, accb = 0;
+      const int stage = me, accb = me;
       uint32_t phase = 0, a_phase = 0;
-      int consumed = 0;
+      int consumed = 0, g = 0;
       for (int u = blockIdx.x; u < a.total_units && !*abort_flag; u += gridDim.x) {
         int qgroup, chunk;
         unit_coords(a, u, qgroup, chunk);
@@ -460,10 +468,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem_a);
         bool ok = true;
-        for (int t = 0; t < ntiles && ok; ++t) {
+        for (int t = (g & 1) == me ? 0 : 1; t < ntiles && ok; t += 2) {
           ok = mbar_wait(bar(FULL + stage), phase, abort_flag, a.err);
           if (!ok) break;
-          s_consumed = ++consumed;
+          s_consumed[me] = ++consumed;
           tc_fence_after();
           const uint32_t b_addr = smem_u32(smem_b + stage * kAtoms * kAtomBytes);
           const uint32_t d_base = tmem_base + static_cast<uint32_t>(accb * kTiles * kN);
@@ -479,17 +487,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           umma_commit(bar(EMPTY + stage));
           umma_commit(bar(ACC_FULL + accb));
-          if (++stage == kStages) {
-            stage = 0;
-            phase ^= 1;
-          }
-          if (++accb == kAcc) accb = 0;
+          phase ^= 1;
         }
         if (!ok) break;
-        umma_commit(bar(A_EMPTY));
+        g += ntiles;
+        umma_commit(bar(A_EMPTY));  // A_EMPTY completes once both issuers are done with the unit
       }
     }
-  } else {
+  } else if (warp < kIssuer2) {
     // ---------------- epilogue: thread = query ----------------
     // Each query keeps a candidate list of kCap (distance, group) entries in shared memory
     // (sorted best-kKK prefix + entries appended since). Per 64 columns: one three-input
