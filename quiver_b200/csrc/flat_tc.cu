@@ -40,7 +40,6 @@ constexpr int kN = 128;          // database rows per MMA tile
 constexpr int kAtomK = 64;       // fp16 elements per 128-byte swizzled row
 constexpr int kAtomBytes = 128 * 128;  // one 128-row x 128-byte swizzle atom column
 constexpr int kTiles = 2;        // query tiles per CTA: every row tile feeds one MMA per query tile
-constexpr int kStages = 2;       // row-tile ring depth
 constexpr int kEpiWarps = 4 * kTiles;  // one warp per (query tile, TMEM lane quarter)
 // Warps: 0 TMA producer, 1 MMA issuer of even row tiles, 2 .. 1 + kEpiWarps epilogue, and
 // kIssuer2 MMA issuer of odd row tiles. Each mbarrier wait in an issuing thread leaves the tensor
@@ -48,9 +47,17 @@ constexpr int kEpiWarps = 4 * kTiles;  // one warp per (query tile, TMEM lane qu
 constexpr int kIssuer2 = 2 + kEpiWarps;
 constexpr int kThreads = 32 * (kIssuer2 + 1);
 constexpr int kAcc = 2;          // TMEM accumulator slots of kTiles x kN columns (all 512 columns)
-constexpr int kAppend = 16;      // list entries appended between compactions
 constexpr int kLS = kTiles * kM; // candidate-list stride: entry i of list l lives at i * kLS + l
 constexpr int kMaxKK = 32;       // largest best-list length (candidates per query per unit)
+// Row-tile ring depth and list entries appended between compactions, by best-list length. A row
+// tile's stage is only refilled after its MMAs finish, so the next tile's copy has one tile time
+// (~900 cycles) to land with two stages, which L2 latency exceeds; three stages fit in shared
+// memory next to best lists of 24 when 8 (not 16) entries are appended between compactions.
+template <int kKK>
+struct Ring {
+  static constexpr int kStages = kKK <= 24 ? 3 : 2;
+  static constexpr int kAppend = kKK <= 24 ? 8 : 16;
+};
 constexpr uint64_t kTimeoutNs = 2000000000ull;       // drain bound (global timer)
 constexpr long long kTimeoutCycles = 4000000000ll;     // ~2 s at 2 GHz (SM clock)
 constexpr uint32_t kSuspendHintNs = 100000;           // one sleeping try_wait: at most 0.1 ms
@@ -252,7 +259,7 @@ __device__ __forceinline__ void group_best8(const float (&v)[64], float (&best)[
 // Per-lane candidate lists: entry i of list l lives at i * kLS + l (the lanes of a warp hold
 // adjacent lists, so their accesses never share a bank). A list is a sorted prefix of exactly
 // KK entries (padded with (+inf, ~0) at the start of a work unit) followed by up to kAppend
-// entries appended since (kCap = KK + kAppend in all).
+// entries appended since (kCap = KK + kAppend in all; Ring<KK>::kAppend).
 
 // Compare-exchange of two (distance, group) entries in registers: afterwards (da, ra) is the
 // smaller in (distance, group) order.
@@ -269,28 +276,29 @@ __device__ __forceinline__ void cex(float& da, uint32_t& ra, float& db, uint32_t
 // Keeps the best kKK of a query's list, sorted, and tightens the threshold to the kKK-th distance
 // (+inf while fewer than kKK real entries were seen). The list is loaded into registers and
 // merged there by fixed networks (no per-lane branches, so the warp never diverges): the appended
-// entries (padded with (+inf, ~0)) are sorted by a 16-input bitonic network; with the prefix a
-// (sorted, padded to 32) and the sorted appended entries b (padded to 32), c[i] = min(a[i],
+// entries (padded with (+inf, ~0)) are sorted by a kAppend-input bitonic network; with the prefix
+// a (sorted, padded to 32) and the sorted appended entries b (padded to 32), c[i] = min(a[i],
 // b[31 - i]) holds the 32 smallest of both as a bitonic sequence, which a 32-input bitonic merge
 // sorts.
 template <int kKK>
 __device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, float& thr) {
-  static_assert(kAppend == 16 && kKK <= 32, "networks sized for 16 appended, 32 kept");
+  constexpr int kA = Ring<kKK>::kAppend;
+  static_assert((kA & (kA - 1)) == 0 && kA <= 32 && kKK <= 32, "networks sized for 32 kept");
   const float kInf = __int_as_float(0x7f800000);
-  float bd[16];
-  uint32_t br[16];
+  float bd[kA];
+  uint32_t br[kA];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < kA; ++i) {
     const bool in = kKK + i < cnt;
     bd[i] = in ? d[(kKK + i) * kLS] : kInf;
     br[i] = in ? r[(kKK + i) * kLS] : 0xffffffffu;
   }
 #pragma unroll
-  for (int size = 2; size <= 16; size <<= 1) {
+  for (int size = 2; size <= kA; size <<= 1) {
 #pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < kA / 2; ++i) {
         const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
         if ((lo & size) == 0)
           cex(bd[lo], br[lo], bd[hi], br[hi]);
@@ -305,7 +313,7 @@ __device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, flo
   for (int i = 0; i < 32; ++i) {
     cd[i] = i < kKK ? d[i * kLS] : kInf;
     cr[i] = i < kKK ? r[i * kLS] : 0xffffffffu;
-    if (31 - i < 16) {
+    if (31 - i < kA) {
       const bool tb = dev::key_less(bd[31 - i], br[31 - i], cd[i], cr[i]);
       cd[i] = tb ? bd[31 - i] : cd[i];
       cr[i] = tb ? br[31 - i] : cr[i];
@@ -349,6 +357,8 @@ template <int kAtoms, bool kL2, int kKK>
 __global__ void __launch_bounds__(kThreads, 1)
     flat_screen_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                           const __grid_constant__ CUtensorMap tmap_x, const Args a) {
+  constexpr int kStages = Ring<kKK>::kStages;
+  constexpr int kAppend = Ring<kKK>::kAppend;
   constexpr int kCap = kKK + kAppend;  // candidate list entries per query
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the swizzle atoms.
@@ -360,12 +370,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* buf_r = reinterpret_cast<uint32_t*>(buf_d + kCap * kLS);
   uint64_t* bars = reinterpret_cast<uint64_t*>(buf_r + kCap * kLS);
   // bars: full[kStages], empty[kStages], acc_full[kAcc], a_full, a_empty.
-  // full[s] also stands for "accumulator slot s is free": row tile t uses stage t % kStages and
-  // slot t % kAcc (kStages == kAcc), and full[s] completes only when the tile's bytes have
-  // landed AND every epilogue warp has read the slot's previous tile out of TMEM. The MMA warp
-  // then waits on one mbarrier per tile: each wait in the issuing thread costs the tensor pipe
-  // ~200 cycles of idle time, even on a phase that completed long before.
-  static_assert(kStages == kAcc, "stage and accumulator slot of a row tile coincide");
+  // Row tile t (counted over all of this CTA's units) uses stage t % kStages and accumulator slot
+  // t % kAcc. full[t % kStages] also stands for "slot t % kAcc is free": it completes only when
+  // the tile's bytes have landed AND every epilogue warp has read tile t - kAcc out of the slot
+  // (the epilogue arrives on the stage of tile t + kAcc right after loading tile t). The MMA
+  // issuers then wait on one mbarrier per tile: each wait in an issuing thread costs the tensor
+  // pipe ~200 cycles of idle time, even on a phase that completed long before.
+  static_assert(kStages >= kAcc, "an epilogue arrival must never reach a phase still in use");
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ int s_consumed[2];  // B fills each MMA issuer has waited for (abort drain)
@@ -450,12 +461,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1 || warp == kIssuer2) {
     // ---------------- MMA issuers ----------------
     // Issuer `me` takes the row tiles whose index (counted over all of this CTA's units) has
-    // parity me, which are exactly the tiles of stage and accumulator slot me.
-    static_assert(kStages == 2, "one issuer per stage");
+    // parity me: those of accumulator slot me.
+    static_assert(kAcc == 2, "one issuer per accumulator slot");
     const int me = warp == 1 ? 0 : 1;
     if (lane == 0) {
-      const int stage = me, accb = me;
-      uint32_t phase = 0, a_phase = 0;
+      const int accb = me;
+      uint32_t a_phase = 0;
       int consumed = 0, g = 0;
       for (int u = blockIdx.x; u < a.total_units && !*abort_flag; u += gridDim.x) {
         int qgroup, chunk;
@@ -469,7 +480,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t a_addr = smem_u32(smem_a);
         bool ok = true;
         for (int t = (g & 1) == me ? 0 : 1; t < ntiles && ok; t += 2) {
-          ok = mbar_wait(bar(FULL + stage), phase, abort_flag, a.err);
+          const int gt = g + t;
+          const int stage = gt % kStages;
+          ok = mbar_wait(bar(FULL + stage), (gt / kStages) & 1, abort_flag, a.err);
           if (!ok) break;
           s_consumed[me] = ++consumed;
           tc_fence_after();
@@ -487,7 +500,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           umma_commit(bar(EMPTY + stage));
           umma_commit(bar(ACC_FULL + accb));
-          phase ^= 1;
         }
         if (!ok) break;
         g += ntiles;
@@ -510,9 +522,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* br = buf_r + tile * kM + qi;
     const uint32_t col0 = static_cast<uint32_t>(tile * kN);  // this tile's columns in a slot
     const float kInfF = __int_as_float(0x7f800000);
-    int accb = 0;
+    int accb = 0, gt = 0;  // gt: this CTA's row tiles so far
     uint32_t acc_phase = 0;
-    // The first row tile of each slot has no previous tile to wait for.
+    // Tiles 0 .. kAcc - 1 (stages 0 .. kAcc - 1) are the first in their slots: nothing to wait for.
     if (lane == 0)
       for (int b = 0; b < kAcc; ++b) mbar_arrive(bar(FULL + b));
     for (int u = blockIdx.x; u < a.total_units; u += gridDim.x) {
@@ -579,6 +591,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         // list; compaction tightens the threshold, so the groups are tested again.
         if (__any_sync(0xffffffffu, cnt + __popc(gm) > kCap)) {
           compact_buffer<kKK>(bd, br, cnt, thr);
+          // Publish the tightened bound to the units of other row chunks at once: this unit
+          // outputs kKK entries at or below it whatever it appends later.
+          if (active) atomicMin(a.thr_bits + q, dev::ordered_bits(thr));
           uint32_t keep = 0;
 #pragma unroll
           for (int g = 0; g < 8; ++g)
@@ -619,7 +634,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_hold(rb);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(FULL + accb));  // the slot is free for tile t + kAcc
+        // The slot is free for tile gt + kAcc.
+        if (lane == 0) mbar_arrive(bar(FULL + (gt + kAcc) % kStages));
+        ++gt;
         // Both trees first: the loaded values are dead before any list work (compaction needs
         // the registers).
         float best_a[8], best_b[8], top_a, top_b;
@@ -931,9 +948,12 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   a.glock = glock.get<int>();
   a.err = err;
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
-  const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (tc::kTiles + tc::kStages) +
-                      static_cast<size_t>(kk + tc::kAppend) * tc::kLS * 8 +
-                      (2 * tc::kStages + tc::kAcc + 2) * 8;
+  const int stages = kk == 24 ? tc::Ring<24>::kStages : tc::Ring<32>::kStages;
+  const int append = kk == 24 ? tc::Ring<24>::kAppend : tc::Ring<32>::kAppend;
+  const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (tc::kTiles + stages) +
+                      static_cast<size_t>(kk + append) * tc::kLS * 8 +
+                      (2 * stages + tc::kAcc + 2) * 8;
+  QV_REQUIRE(smem <= 227 * 1024, "tensor-core screen: shared memory layout too large");
   const int grid = std::min(a.total_units, sm_count(s.device));
   KernelTimer timer(st, "flat_screen_tc_kernel", 2.0 * nq * static_cast<double>(s.n) * s.dim,
                     false);
