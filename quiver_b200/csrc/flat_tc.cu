@@ -522,7 +522,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t* br = buf_r + tile * kM + qi;
     const uint32_t col0 = static_cast<uint32_t>(tile * kN);  // this tile's columns in a slot
     const float kInfF = __int_as_float(0x7f800000);
-    int accb = 0, gt = 0;  // gt: this CTA's row tiles so far
+    int accb = 0;
+    int free_stage = kAcc % kStages;  // stage of the tile that next reuses the slot just read
     uint32_t acc_phase = 0;
     // Tiles 0 .. kAcc - 1 (stages 0 .. kAcc - 1) are the first in their slots: nothing to wait for.
     if (lane == 0)
@@ -552,19 +553,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       // for cosine/IP, min distance for L2); top: the best of all 64.
       auto tree = [&](uint32_t (&r)[64], int64_t cb, float (&best)[8], float& top) {
         float (&v)[64] = *reinterpret_cast<float(*)[64]>(r);  // the loaded bits, used in place
-        const int valid = static_cast<int>(r1 - cb < 64 ? r1 - cb : 64);  // rows of this chunk
         // Rows past the chunk end and rows the filter rejects take the worst score, so that
-        // every group's best is the best of its admitted rows.
-        const uint64_t admitted =
-            (valid >= 64 ? ~0ull : (valid > 0 ? (1ull << valid) - 1 : 0ull)) &
-            (a.bitmap != nullptr && valid > 0 ? a.bitmap[static_cast<uint64_t>(cb) >> 6] : ~0ull);
+        // every group's best is the best of its admitted rows. Only halves that can hold such
+        // rows (warp-uniform test) pay for the mask.
+        const bool partial = a.bitmap != nullptr || r1 - cb < 64;
+        uint64_t admitted = ~0ull;
+        if (partial) {
+          const int valid = static_cast<int>(r1 - cb < 64 ? r1 - cb : 64);  // rows of this chunk
+          admitted = (valid >= 64 ? ~0ull : (valid > 0 ? (1ull << valid) - 1 : 0ull)) &
+                     (a.bitmap != nullptr && valid > 0 ? a.bitmap[static_cast<uint64_t>(cb) >> 6]
+                                                       : ~0ull);
+        }
         if (kL2) {
           // v[j] := ||q||^2 + ||x||^2 - 2<q,x>
+          if (!partial) {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) {
-            const bool in = (admitted >> j) & 1ull;
-            const float xn = in ? a.xnorm2[cb + j] : 0.0f;
-            v[j] = in ? fmaf(-2.0f * inv, v[j], qn + xn) : kInfF;
+            for (int j = 0; j < 64; ++j) v[j] = fmaf(-2.0f * inv, v[j], qn + a.xnorm2[cb + j]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              const bool in = (admitted >> j) & 1ull;
+              const float xn = in ? a.xnorm2[cb + j] : 0.0f;
+              v[j] = in ? fmaf(-2.0f * inv, v[j], qn + xn) : kInfF;
+            }
           }
           group_best8<false>(v, best, top);
         } else {
@@ -634,9 +645,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_hold(rb);
         tc_fence_before();
         __syncwarp();
-        // The slot is free for tile gt + kAcc.
-        if (lane == 0) mbar_arrive(bar(FULL + (gt + kAcc) % kStages));
-        ++gt;
+        // The slot is free for the tile kAcc later.
+        if (lane == 0) mbar_arrive(bar(FULL + free_stage));
+        if (++free_stage == kStages) free_stage = 0;
         // Both trees first: the loaded values are dead before any list work (compaction needs
         // the registers).
         float best_a[8], best_b[8], top_a, top_b;
