@@ -11,15 +11,18 @@
 //
 // Kernel structure (one CTA per SM, persistent over work units = (query group of 2 x 128, row
 // chunk), chunk-major so that the CTAs working on a chunk share its rows in L2):
-//   warp 0      TMA producer: the unit's two query tiles (A, resident) and a 2-stage ring of
-//               128-row tiles of the database (B), 128-byte swizzled, no multicast.
-//   warp 1      MMA issuer: allocates TMEM, issues tcgen05.mma kind::f16 (M=128, N=128, K=16
-//               steps) of each row tile against both query tiles into one of two accumulator
-//               slots (2 x 128 columns each), commits to mbarriers.
+//   warp 0      TMA producer: the unit's two query tiles (A, resident) and a ring of 128-row tiles
+//               of the database (B; 3 stages with best lists of 24, else 2), 128-byte swizzled, no
+//               multicast.
+//   warps 1, 10 MMA issuers (even / odd row tiles): tcgen05.mma kind::f16 (M=128, N=128, K=16
+//               steps, unrolled per K-step count) of each row tile against both query tiles into
+//               one of two TMEM accumulator slots (2 x 128 columns each); one mbarrier wait per
+//               tile, which covers both the tile's bytes and its slot being free.
 //   warps 2..9  epilogue: warp (tile, lane quarter); thread i owns query i of its tile (= TMEM
-//               lane), screens the tile's 128 inner products in two 64-column groups, and appends
-//               the 8-row groups that beat its running threshold to a candidate list in shared
-//               memory (compacted warp-wide when one fills).
+//               lane), loads the tile's 128 inner products, frees the slot, reduces each 8-row group
+//               to its best score with three-input max/min trees, and appends the groups that beat
+//               its running threshold to a candidate list in shared memory (compacted in registers
+//               by fixed sorting networks when one fills).
 // Every mbarrier wait is bounded (2 s of GPU time); on timeout the CTA raises an error flag,
 // drains its outstanding copies (again bounded), frees TMEM and exits.
 #include <cuda.h>
