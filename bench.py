@@ -3,13 +3,14 @@
 
 Workload: 1,183,514 x 100 float32 vectors from a 1,000-component Gaussian
 mixture, L2-normalized; 10,000 queries drawn the same way (seeded synthetic data standing in for
-GloVe-1.2M). The database is sharded by id range over the N GPUs (one process per GPU); every GPU
-gets the whole query batch and the per-GPU top-k are merged with one NCCL all-gather plus a device
-k-way merge. A step is one search of the whole 10k batch. Total work is fixed, so N>1 is strong
-scaling.
+GloVe-1.2M). On N GPUs (one process per GPU) every GPU holds the whole database (0.74 GB) and
+answers its 1/N slice of every query batch, with no exchange (``--shard queries``, the default);
+``--shard rows`` instead splits the database by id range, gives every GPU the whole batch and
+merges the per-GPU top-k with one NCCL all-gather plus a device k-way merge. A step is one search
+of the whole 10k batch. Total work is fixed, so N>1 is strong scaling.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c1|c2|c3] [--nprobe P] [--filter]
+                    [--workload c1|c2|c3] [--nprobe P] [--filter] [--shard queries|rows]
 
 ``--workload c2`` / ``c3`` measure IVF-PQ search instead (BASELINE configs 2 and 3): the trained,
 empty index the reference saved (tests/golden/ivf_c{2,3}_trained.qvr) is loaded on every GPU,
@@ -58,6 +59,9 @@ def parse():
     ap.add_argument("--workload", choices=["c1", "c2", "c3"], default="c1")
     ap.add_argument("--nprobe", type=int, default=64, help="IVF-PQ workloads: lists probed")
     ap.add_argument("--filter", action="store_true", help="IVF-PQ workloads: 1%% allowed ids")
+    ap.add_argument("--shard", choices=["rows", "queries"], default="queries",
+                    help="Flat on N GPUs: id-range row shards + all-gather merge, or the rows "
+                         "replicated and each batch's queries split by rank (no exchange)")
     return ap.parse_args()
 
 
@@ -464,14 +468,19 @@ def main():
         return
     import quiver_b200 as qv
     from quiver_b200 import _native
-    from quiver_b200.distributed import ShardedFlatIndex
+    from quiver_b200.distributed import ReplicatedFlatIndex, ShardedFlatIndex
     from quiver_b200.synthetic import config1
 
     n_db, n_q = args.rows, args.queries
     db, q = config1(n_db, n_q)
-    lo, hi = rank * n_db // world, (rank + 1) * n_db // world
-    index = ShardedFlatIndex(DIM, "cosine", device=local)
-    index.add_shard(db[lo:hi], np.arange(lo, hi, dtype=np.uint64), np.arange(lo, hi))
+    by_queries = args.shard == "queries" and world > 1
+    if by_queries:
+        index = ReplicatedFlatIndex(DIM, "cosine", device=local)
+        index.add(db)
+    else:
+        lo, hi = rank * n_db // world, (rank + 1) * n_db // world
+        index = ShardedFlatIndex(DIM, "cosine", device=local)
+        index.add_shard(db[lo:hi], np.arange(lo, hi, dtype=np.uint64), np.arange(lo, hi))
     dq = torch.from_numpy(q).cuda()
     q_pinned = torch.from_numpy(q).pin_memory()
     q_host = q_pinned.numpy()
@@ -538,9 +547,10 @@ def main():
         t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
+    copies = 1 if by_queries else world  # query slices, or the whole batch on every rank
     e2e = {"value": n_q * args.steps / e2e_s, "unit": "QPS",
-           "h2d_bytes_per_step": world * n_q * DIM * 4,
-           "d2h_bytes_per_step": world * n_q * K * (8 + 4)}
+           "h2d_bytes_per_step": copies * n_q * DIM * 4,
+           "d2h_bytes_per_step": copies * n_q * K * (8 + 4)}
 
     hbm, tflops, peak_kind = load_peaks()
     launches_timed = max(1, args.steps)
@@ -558,7 +568,8 @@ def main():
         "config": {"workload": WORKLOAD if (n_db, n_q) == (N_DB, N_Q) else
                    f"FlatIndex cosine k=10, {n_db:,} x 100 mixture (reduced), {n_q:,} queries",
                    "global_batch": n_q, "k": K, "database_rows": n_db,
-                   "dim": DIM, "parallelism": f"id-range shards x{world}",
+                   "dim": DIM, "parallelism": (f"query slices x{world}, rows replicated"
+                                               if by_queries else f"id-range shards x{world}"),
                    "l2": "inputs larger than L2 (473 MB database per pass)"},
         "gpu_launches": launches, "rescanned_queries": rescans,
         "roofline": {"bound": "tensor", "kernel": kernel_name, "achieved": achieved,

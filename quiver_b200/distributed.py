@@ -131,6 +131,73 @@ class ShardedFlatIndex:
         return lab.cpu().numpy(), d.cpu().numpy()
 
 
+class ReplicatedFlatIndex:
+    """Exact Flat search with the collection replicated on every rank and each query batch split
+    by rank: rank r answers queries [r*nq/W, (r+1)*nq/W) of every batch from its own full copy.
+    No exchange on the search path; the answers are the single-index answers (every rank holds
+    every row in the same order). Memory per GPU is the whole collection (C1: 0.74 GB)."""
+
+    def __init__(self, dim: int, metric: str = "l2", *, device: Optional[int] = None, group=None):
+        self.rank, self.world = _world(group)
+        self.group = group
+        self.device = torch.cuda.current_device() if device is None else int(device)
+        self.local = FlatIndex(dim, metric, device=self.device)
+
+    @property
+    def dim(self) -> int:
+        return self.local.dim
+
+    def add(self, vectors, labels=None) -> None:
+        """Every rank passes the same batch and keeps all of it."""
+        self.local.add(vectors, labels)
+
+    def query_range(self, nq: int):
+        return shard_range(nq, self.rank, self.world)
+
+    def search_device(self, queries: torch.Tensor, k: int):
+        """Queries of the whole batch on this rank's GPU (float32 [nq, dim]); returns device
+        (dists, labels) of this rank's slice of the batch (rows query_range(nq))."""
+        lo, hi = self.query_range(queries.shape[0])
+        mine = queries[lo:hi]
+        d = torch.empty((hi - lo, k), dtype=torch.float32, device=queries.device)
+        lab = torch.empty((hi - lo, k), dtype=torch.int64, device=queries.device)
+        if hi > lo:
+            check(lib().qv_flat_search_device(self.local.handle, mine.data_ptr(), hi - lo, k,
+                                              None, lab.data_ptr(), d.data_ptr(), None,
+                                              C.c_void_p(_stream_ptr())))
+        return d, lab
+
+    def search(self, queries, k: int = 10, gather: bool = False):
+        """Host API: this rank answers its slice of the batch (labels, distances as numpy); with
+        gather=True the slices are all-gathered so every rank returns the whole batch's answers."""
+        q = _as_matrix(queries, self.dim)
+        lo, hi = self.query_range(q.shape[0])
+        lab, d = self.local.search(q[lo:hi], int(k))
+        if not gather or self.world == 1:
+            return lab, d
+        dev = torch.device(f"cuda:{self.device}")
+        return gather_query_slices(torch.from_numpy(d).to(dev), torch.from_numpy(lab).to(dev),
+                                   q.shape[0], self.world, self.group)
+
+
+def gather_query_slices(d: torch.Tensor, lab: torch.Tensor, nq: int, world: int, group=None):
+    """All-gathers every rank's (distances, labels) answers for its query slice shard_range(nq,
+    rank, world) and returns the whole batch's answers in query order (numpy labels, distances).
+    Slices differ in length by at most one row; each is padded to the longest for the exchange."""
+    k = d.shape[1]
+    parts = [shard_range(nq, r, world) for r in range(world)]
+    width = max(hi - lo for lo, hi in parts)
+    pd = torch.full((width, k), float("inf"), dtype=torch.float32, device=d.device)
+    pl = torch.full((width, k), -1, dtype=torch.int64, device=d.device)
+    pd[:d.shape[0]] = d
+    pl[:lab.shape[0]] = lab
+    gd = _all_gather(pd, world, group).cpu().numpy()
+    gl = _all_gather(pl, world, group).cpu().numpy()
+    out_d = np.concatenate([gd[r, :hi - lo] for r, (lo, hi) in enumerate(parts)])
+    out_l = np.concatenate([gl[r, :hi - lo] for r, (lo, hi) in enumerate(parts)])
+    return out_l, out_d
+
+
 class ShardedIvfPqIndex:
     """IVF-PQ search over an id-range-sharded index (one shard per rank).
 

@@ -121,6 +121,18 @@ def _ivf_keys_match_unsharded(rank, world):
     return all(want[row] == key for row, key in keys)
 
 
+def _query_slices_gathered(rank, world):
+    """Rows replicated, queries split by rank: each rank answers its slice of an odd-sized batch
+    (slices differ in length); the gathered answers come back in query order on every rank."""
+    from quiver_b200.distributed import gather_query_slices, shard_range
+    nq, k = 7, 3
+    lo, hi = shard_range(nq, rank, world)
+    rows = np.arange(lo, hi)
+    d = torch.from_numpy((rows[:, None] * 10 + np.arange(k)[None, :]).astype(np.float32))
+    lab = torch.from_numpy((rows[:, None] * 100 + np.arange(k)[None, :]).astype(np.int64))
+    return gather_query_slices(d, lab, nq, world, None)
+
+
 # ---- tests ---------------------------------------------------------------------------------------
 
 def test_shard_ranges_partition_the_ids():
@@ -160,3 +172,12 @@ def test_sharded_topk_merge_equals_single_index():
 def test_ivf_shard_keys_equal_unsharded_keys():
     res = _run("_ivf_keys_match_unsharded")
     assert all(res[r] for r in range(WORLD))
+
+
+def test_query_slices_gather_in_query_order():
+    res = _run("_query_slices_gathered")
+    want_d = (np.arange(7)[:, None] * 10 + np.arange(3)[None, :]).astype(np.float32)
+    want_l = (np.arange(7)[:, None] * 100 + np.arange(3)[None, :]).astype(np.int64)
+    for rank in range(WORLD):
+        lab, d = res[rank]
+        assert np.array_equal(d, want_d) and np.array_equal(lab, want_l)

@@ -30,7 +30,7 @@ def _flat_worker(rank, world, port, out_q):
                             device_id=torch.device(f"cuda:{rank}"))
     try:
         import quiver_b200 as qv
-        from quiver_b200.distributed import ShardedFlatIndex
+        from quiver_b200.distributed import ReplicatedFlatIndex, ShardedFlatIndex
         from quiver_b200.synthetic import mixture
         out = {}
         for metric in ("cosine", "l2", "ip"):
@@ -43,6 +43,14 @@ def _flat_worker(rank, world, port, out_q):
             full.add(db)
             fl, fd = full.search(q, 10)
             out[metric] = (d.cpu().numpy(), lab.cpu().numpy(), fd, fl)
+            # Rows replicated, queries split by rank: each rank's slice, and the gathered batch.
+            rep = ReplicatedFlatIndex(100, metric, device=rank)
+            rep.add(db)
+            sd, sl = rep.search_device(torch.from_numpy(q).cuda(), 10)
+            gl, gd = rep.search(q, 10, gather=True)
+            lo, hi = rep.query_range(len(q))
+            out[metric + "/slice"] = (sd.cpu().numpy(), sl.cpu().numpy(), fd[lo:hi], fl[lo:hi])
+            out[metric + "/gathered"] = (gd, gl, fd, fl)
         out_q.put((rank, out, None))
     except Exception as e:  # noqa: BLE001
         out_q.put((rank, None, repr(e)))
