@@ -216,6 +216,107 @@ __global__ void select_probes_kernel(const float* __restrict__ coarse, size_t nl
   }
 }
 
+// The same selection for nprobe <= kRadixProbeMax without sorting all nlist candidates: a radix
+// select on the 64-bit composite (order-preserving bits of the distance, with -0 read as +0 since
+// the reference compares distances with <) << 32 | list id, eight bits a pass from the top, one
+// shared 256-bin histogram per pass, until the nprobe-th smallest composite is known. Composites
+// are distinct, so exactly nprobe of them lie at or below it; those are gathered and sorted.
+constexpr int kRadixProbeMax = 1024;
+constexpr int kRadixThreads = 256;
+
+__global__ void __launch_bounds__(kRadixThreads) select_probes_radix_kernel(
+    const float* __restrict__ coarse, size_t nlist, int nprobe, int id_passes, int sort_n,
+    uint32_t* __restrict__ probes, float* __restrict__ probe_d) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  uint64_t* comp = reinterpret_cast<uint64_t*>(smem_raw);  // nlist composites
+  uint64_t* sel = comp + nlist;                            // sort_n selected (padded with ~0)
+  __shared__ unsigned hist[256];
+  __shared__ uint64_t s_prefix;
+  __shared__ unsigned s_need;
+  __shared__ int s_count;
+  const size_t q = blockIdx.x;
+  const float* row = coarse + q * nlist;
+  for (size_t i = threadIdx.x; i < nlist; i += kRadixThreads) {
+    const float d = row[i] + 0.0f;  // -0 -> +0
+    comp[i] = (static_cast<uint64_t>(dev::ordered_bits(d)) << 32) | i;
+  }
+  uint64_t prefix = 0;
+  unsigned need = static_cast<unsigned>(nprobe);  // rank (1-based) of the target among matches
+  const int passes = 4 + id_passes;
+  static_assert(kRadixThreads == 256, "one histogram bin per thread");
+  for (int p = 0; p < passes; ++p) {
+    // Distance bytes from the top, then the id's bytes below 256^id_passes (the higher id bytes
+    // are zero in every composite).
+    const int shift = p < 4 ? 56 - 8 * p : 8 * (id_passes - 1 - (p - 4));
+    hist[threadIdx.x] = 0;
+    __syncthreads();
+    const uint64_t above = p == 0 ? 0ull : ~0ull << (shift + 8);
+    for (size_t i = threadIdx.x; i < nlist; i += kRadixThreads) {
+      const uint64_t c = comp[i];
+      if ((c & above) == prefix) atomicAdd(&hist[(c >> shift) & 255], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      unsigned h[8], sum = 0;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        h[b] = hist[lane * 8 + b];
+        sum += h[b];
+      }
+      unsigned incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      unsigned cum = incl - sum;  // matches in the bins before this lane's
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        if (cum < need && need <= cum + h[b]) {
+          s_prefix = prefix | (static_cast<uint64_t>(lane * 8 + b) << shift);
+          s_need = need - cum;
+        }
+        cum += h[b];
+      }
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    need = s_need;
+  }
+  // prefix is now the nprobe-th smallest composite.
+  if (threadIdx.x == 0) s_count = 0;
+  for (int i = threadIdx.x; i < sort_n; i += kRadixThreads) sel[i] = ~0ull;
+  __syncthreads();
+  for (size_t i = threadIdx.x; i < nlist; i += kRadixThreads) {
+    const uint64_t c = comp[i];
+    if (c <= prefix) {
+      const int at = atomicAdd(&s_count, 1);
+      if (at < sort_n) sel[at] = c;  // exactly nprobe <= sort_n arrive
+    }
+  }
+  __syncthreads();
+  for (int size = 2; size <= sort_n; size <<= 1) {
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      for (int i = threadIdx.x; i < sort_n / 2; i += kRadixThreads) {
+        const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+        const bool up = (lo & size) == 0;
+        const uint64_t a = sel[lo], b = sel[hi];
+        if ((a > b) == up) {
+          sel[lo] = b;
+          sel[hi] = a;
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = threadIdx.x; i < nprobe; i += kRadixThreads) {
+    const uint32_t l = static_cast<uint32_t>(sel[i] & 0xffffffffu);
+    probes[q * nprobe + i] = l;
+    probe_d[q * nprobe + i] = row[l];
+  }
+}
+
 // ---- encode ------------------------------------------------------------------------------------------
 
 // residual = v - c_l (src/ivfpq_index.cc:243)
@@ -636,6 +737,19 @@ Prepared prepare_search(const IvfState& s, const float* d_queries, size_t nq, si
   const int pool = static_cast<int>(next_pow2(s.nlist));
   p.probes.allocate(nq * p.nprobe * sizeof(uint32_t), st);
   p.probe_d.allocate(nq * p.nprobe * sizeof(float), st);
+  if (p.nprobe <= kRadixProbeMax) {
+    int id_passes = 1;
+    while (id_passes < 4 && (s.nlist - 1) >> (8 * id_passes) != 0) ++id_passes;
+    const int sort_n = static_cast<int>(next_pow2(static_cast<size_t>(p.nprobe)));
+    const size_t smem = (s.nlist + sort_n) * sizeof(uint64_t);
+    QV_CUDA(cudaFuncSetAttribute(select_probes_radix_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    select_probes_radix_kernel<<<static_cast<unsigned>(nq), kRadixThreads, smem, st>>>(
+        p.coarse.get<float>(), s.nlist, p.nprobe, id_passes, sort_n, p.probes.get<uint32_t>(),
+        p.probe_d.get<float>());
+    check_launch("select_probes_radix_kernel");
+    return p;
+  }
   const size_t smem = pool * (sizeof(float) + sizeof(uint64_t));
   QV_CUDA(cudaFuncSetAttribute(select_probes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem));
