@@ -160,35 +160,71 @@ __global__ void __launch_bounds__(256) coarse_assign_kernel(const float* __restr
 
 // Search-time coarse distances (src/ivfpq_index.cc:285-297 with CentroidTable::l2 / ::dot):
 // L2: sum_j (q_j - c_j)^2; IP/cosine: -(sum_j q_j c_j), j ascending, separately rounded.
-__global__ void __launch_bounds__(256) coarse_dist_kernel(const float* __restrict__ q, size_t nq,
-                                                          const float* __restrict__ cents,
-                                                          size_t nlist, int dim, bool ip,
-                                                          float* __restrict__ out) {
-  __shared__ float xs_t[kTileD * kTileP];
-  __shared__ float cs[kTileC * (kTileD + 1)];
-  const int p = threadIdx.x & 31, cl = threadIdx.x >> 5;
-  const size_t p0 = static_cast<size_t>(blockIdx.x) * kTileP;
-  const size_t c0 = static_cast<size_t>(blockIdx.y) * kTileC;
-  float acc[8];
+// 4 queries x 8 centroids per thread (a block covers 128 queries x 64 centroids): each dimension
+// step issues three 16-byte shared loads for 32 (query, centroid) updates. Each sum is sequential
+// in j with every operation rounded separately.
+constexpr int kTileP4 = 128;  // queries per block (4 per thread)
+constexpr int kTileC4 = 64;   // centroids per block (8 per thread)
+constexpr int kTileD4 = 32;   // dimensions per shared tile
+constexpr int kXs4 = kTileP4 + 4;  // padded row strides (16-byte aligned, 4-way store conflicts)
+constexpr int kCs4 = kTileC4 + 4;
+
+__global__ void __launch_bounds__(256) coarse_dist_kernel4(const float* __restrict__ q, size_t nq,
+                                                           const float* __restrict__ cents,
+                                                           size_t nlist, int dim, bool ip,
+                                                           float* __restrict__ out) {
+  __shared__ __align__(16) float xs[kTileD4 * kXs4];  // xs[j][p]
+  __shared__ __align__(16) float cs[kTileD4 * kCs4];  // cs[j][c]
+  const int pl = threadIdx.x & 31, cl = threadIdx.x >> 5;  // queries 4pl.., centroids 8cl..
+  const size_t p0 = static_cast<size_t>(blockIdx.x) * kTileP4;
+  const size_t c0 = static_cast<size_t>(blockIdx.y) * kTileC4;
+  float acc[4][8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-  for (int d0 = 0; d0 < dim; d0 += kTileD) {
-    const int nd = min(kTileD, dim - d0);
+  for (int a = 0; a < 4; ++a)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[a][i] = 0.0f;
+  for (int d0 = 0; d0 < dim; d0 += kTileD4) {
+    const int nd = min(kTileD4, dim - d0);
     __syncthreads();
-    load_coarse_tiles(q, nq, cents, nlist, dim, p0, c0, d0, nd, xs_t, cs);
+    for (int idx = threadIdx.x; idx < kTileP4 * kTileD4; idx += 256) {
+      const int p = idx / kTileD4, j = idx - p * kTileD4;
+      const size_t gp = p0 + p;
+      xs[j * kXs4 + p] = (gp < nq && j < nd) ? q[gp * dim + d0 + j] : 0.0f;
+    }
+    for (int idx = threadIdx.x; idx < kTileC4 * kTileD4; idx += 256) {
+      const int c = idx / kTileD4, j = idx - c * kTileD4;
+      const size_t gc = c0 + c;
+      cs[j * kCs4 + c] = (gc < nlist && j < nd) ? cents[gc * dim + d0 + j] : 0.0f;
+    }
     __syncthreads();
-    if (ip) {
-      coarse_tile<kDot>(xs_t, cs, nd, p, cl, acc);
-    } else {
-      coarse_tile<kL2Diff>(xs_t, cs, nd, p, cl, acc);
+    for (int j = 0; j < nd; ++j) {
+      const float4 xq = *reinterpret_cast<const float4*>(xs + j * kXs4 + 4 * pl);
+      const float4 c_lo = *reinterpret_cast<const float4*>(cs + j * kCs4 + 8 * cl);
+      const float4 c_hi = *reinterpret_cast<const float4*>(cs + j * kCs4 + 8 * cl + 4);
+      const float xv[4] = {xq.x, xq.y, xq.z, xq.w};
+      const float cv[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (ip) {
+            acc[a][i] = __fadd_rn(acc[a][i], __fmul_rn(xv[a], cv[i]));
+          } else {
+            const float d = __fsub_rn(xv[a], cv[i]);
+            acc[a][i] = __fadd_rn(acc[a][i], __fmul_rn(d, d));
+          }
+        }
+      }
     }
   }
-  const size_t gp = p0 + p;
-  if (gp >= nq) return;
+  const size_t cb = c0 + 8 * static_cast<size_t>(cl);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const size_t c = c0 + cl + 8 * i;
-    if (c < nlist) out[gp * nlist + c] = ip ? -acc[i] : acc[i];
+  for (int a = 0; a < 4; ++a) {
+    const size_t gp = p0 + 4 * pl + a;
+    if (gp >= nq) continue;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (cb + i < nlist) out[gp * nlist + cb + i] = ip ? -acc[a][i] : acc[a][i];
   }
 }
 
@@ -729,11 +765,12 @@ Prepared prepare_search(const IvfState& s, const float* d_queries, size_t nq, si
   check_launch("copy_queries_kernel");
   if (s.metric == QV_METRIC_COSINE) normalize_rows_device(p.qn.get<float>(), nq, s.dim, st);
   p.coarse.allocate(nq * s.nlist * sizeof(float), st);
-  dim3 grid(static_cast<unsigned>(ceil_div(nq, kTileP)), static_cast<unsigned>(ceil_div(s.nlist, kTileC)));
-  coarse_dist_kernel<<<grid, 256, 0, st>>>(p.qn.get<float>(), nq, s.centroids.get<float>(),
-                                           s.nlist, static_cast<int>(s.dim), s.ip(),
-                                           p.coarse.get<float>());
-  check_launch("coarse_dist_kernel");
+  dim3 grid(static_cast<unsigned>(ceil_div(nq, kTileP4)),
+            static_cast<unsigned>(ceil_div(s.nlist, kTileC4)));
+  coarse_dist_kernel4<<<grid, 256, 0, st>>>(p.qn.get<float>(), nq, s.centroids.get<float>(),
+                                            s.nlist, static_cast<int>(s.dim), s.ip(),
+                                            p.coarse.get<float>());
+  check_launch("coarse_dist_kernel4");
   const int pool = static_cast<int>(next_pow2(s.nlist));
   p.probes.allocate(nq * p.nprobe * sizeof(uint32_t), st);
   p.probe_d.allocate(nq * p.nprobe * sizeof(float), st);
