@@ -775,9 +775,9 @@ qv_status qv_ivfpq_search(const qv_ivfpq* index, const float* queries, size_t nq
                "search_batch: null buffer");
     const IvfState& s = index->s;
     const size_t total = result_size(nq, k);
-    check_finite(queries, nq * s.dim);
     std::shared_lock lock(index->mu);
     if (!s.trained || s.count == 0) {
+      check_finite(queries, nq * s.dim);
       fill_unfilled(labels, distances, total);
       return;
     }
@@ -788,6 +788,14 @@ qv_status qv_ivfpq_search(const qv_ivfpq* index, const float* queries, size_t nq
     DeviceBuffer bm = device_filter(s.labels.get<uint64_t>(), s.count, filter, st);
     ivf_search(s, dq.get<float>(), nq, k, nprobe, refine_factor, bm.get<uint64_t>(),
                dl.get<uint64_t>(), dd.get<float>(), st);
+    // The reference rejects non-finite queries before searching (src/ivfpq_index.cc:428):
+    // the host scans the batch while the device searches, and on failure nothing is copied out.
+    try {
+      check_finite(queries, nq * s.dim);
+    } catch (...) {
+      cudaStreamSynchronize(st);
+      throw;
+    }
     QV_CUDA(cudaMemcpyAsync(labels, dl.get(), total * sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
     QV_CUDA(cudaMemcpyAsync(distances, dd.get(), total * sizeof(float), cudaMemcpyDeviceToHost, st));
     QV_CUDA(cudaStreamSynchronize(st));

@@ -98,6 +98,17 @@ def test_errors_and_roundtrip(gpu, tmp_path, manifest):
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
     l, _ = loaded.search(base[5], 1, nprobe=case["nlist"], refine_factor=2)
     assert l[0, 0] == 5  # self-match (tests/test_quantizer.cc:258)
+    # Non-finite queries are rejected (src/ivfpq_index.cc:428) by a trained, filled index and by
+    # an untrained one; the index stays usable.
+    for bad in (np.nan, np.inf):
+        qb = q[:6].copy()
+        qb[3, 1] = bad
+        with pytest.raises(ValueError, match="NaN"):
+            loaded.search(qb, 5, nprobe=8, refine_factor=2)
+        with pytest.raises(ValueError, match="NaN"):
+            ix.search(qb, 5)
+    c = loaded.search(q, 5, nprobe=8, refine_factor=2)
+    assert np.array_equal(c[0], b[0]) and np.array_equal(c[1], b[1])
     assert loaded.memory_bytes > 0
 
 
