@@ -491,7 +491,7 @@ __host__ __device__ inline size_t group_finalize_bytes_per_warp(int dpad, int n_
                                                                 int group_rows) {
   const size_t nl = static_cast<size_t>(n_chunks) * kk, nx = static_cast<size_t>(kk) * group_rows;
   const size_t bytes = static_cast<size_t>(dpad) * 4 + nl * 8 + ((n_chunks + 1) & ~1) * 4 +
-                       static_cast<size_t>(kk) * 4 + nx * 12;
+                       static_cast<size_t>(kk) * 8 + nx * 12;
   return (bytes + 15) / 16 * 16;
 }
 
@@ -516,7 +516,8 @@ __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_gro
   uint32_t* lr = reinterpret_cast<uint32_t*>(ld + nl);
   int* ln = reinterpret_cast<int*>(lr + nl);
   uint32_t* sel = reinterpret_cast<uint32_t*>(ln + ((n_chunks + 1) & ~1));
-  float* ed = reinterpret_cast<float*>(sel + kk);
+  float* sv = reinterpret_cast<float*>(sel + kk);  // the selected groups' screen values
+  float* ed = sv + kk;
   uint64_t* er = reinterpret_cast<uint64_t*>(ed + nx);  // 8-byte aligned: offsets are even words
   if (q >= nq) return;
   const float* qrow = qp + static_cast<size_t>(q) * dpad;
@@ -569,28 +570,86 @@ __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_gro
         bl = ol;
       }
     }
-    if (lane == 0) sel[r] = bg;
+    if (lane == 0) {
+      sel[r] = bg;
+      sv[r] = bd;
+    }
     if (r == kk - 1) T = bd;
     h0 += bl == c0 ? 1 : 0;
     h1 += bl == c1 ? 1 : 0;
   }
   __syncwarp();
   // Exact distances of the selected groups' admitted rows, one row per lane.
-  for (int i = lane; i < m * group_rows; i += 32) {
-    const int g = i / group_rows, j = i - g * group_rows;
-    const uint64_t row = static_cast<uint64_t>(sel[g]) * group_rows + j;
-    const bool in = row < static_cast<uint64_t>(nrows) && dev::bitmap_test(bitmap, row);
-    ed[i] = in ? dev::nan_to_inf(lane_exact_distance(sq, x + row * dim, dim, l2)) : kInf;
-    er[i] = in ? row : ~0ull;
+  auto exact_rows = [&](int g0, int g1) {
+    for (int i = g0 * group_rows + lane; i < g1 * group_rows; i += 32) {
+      const int g = i / group_rows, j = i - g * group_rows;
+      const uint64_t row = static_cast<uint64_t>(sel[g]) * group_rows + j;
+      const bool in = row < static_cast<uint64_t>(nrows) && dev::bitmap_test(bitmap, row);
+      ed[i] = in ? dev::nan_to_inf(lane_exact_distance(sq, x + row * dim, dim, l2)) : kInf;
+      er[i] = in ? row : ~0ull;
+    }
+    __syncwarp();
+  };
+  // Groups come in ascending screen value, and every row of group g has an exact distance of at
+  // least sv[g] - eps. So the first kFirstGroups groups are expanded, the k-th best exact distance
+  // dk1 among them is found, and the remaining groups are expanded only when the first of them
+  // could still hold a row at or below dk1; otherwise none of their rows can enter the top k
+  // (their exact distances all exceed dk1 >= the final k-th distance).
+  constexpr int kFirstGroups = 16;
+  int ng = m;
+  if (group_rows > 1 && m > kFirstGroups && k <= 32) {  // lane r keeps round r's winner
+    exact_rows(0, kFirstGroups);
+    // k-th smallest (distance, row) among them: k rounds of a warp minimum with removal, then
+    // the removed entries are put back.
+    float win_d = kInf, dk1 = kInf;
+    int win_i = -1;
+    for (int r = 0; r < k; ++r) {
+      float bd = kInf;
+      uint64_t br = ~0ull;
+      int bi = -1;
+      for (int i = lane; i < kFirstGroups * group_rows; i += 32) {
+        if (dev::key_less(ed[i], er[i], bd, br)) {
+          bd = ed[i];
+          br = er[i];
+          bi = i;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float od = __shfl_xor_sync(kFull, bd, o);
+        const uint64_t orow = __shfl_xor_sync(kFull, br, o);
+        const int oi = __shfl_xor_sync(kFull, bi, o);
+        if (dev::key_less(od, orow, bd, br)) {
+          bd = od;
+          br = orow;
+          bi = oi;
+        }
+      }
+      if (lane == r) {
+        win_d = bd;
+        win_i = bi;
+      }
+      if (lane == 0 && bi >= 0) ed[bi] = kInf;
+      if (r == k - 1) dk1 = bd;
+      __syncwarp();
+    }
+    if (lane < k && win_i >= 0) ed[win_i] = win_d;
+    __syncwarp();
+    if (dk1 < kInf && sv[kFirstGroups] - eps_q[q] > dk1) {
+      ng = kFirstGroups;
+    } else {
+      exact_rows(kFirstGroups, m);
+    }
+  } else {
+    exact_rows(0, m);
   }
-  __syncwarp();
   // The k best by (distance, row): k rounds of a warp minimum; each round's winner is removed.
   float dk = kInf;
   for (int r = 0; r < k; ++r) {
     float bd = kInf;
     uint64_t br = ~0ull;
     int bi = -1;
-    for (int i = lane; i < m * group_rows; i += 32) {
+    for (int i = lane; i < ng * group_rows; i += 32) {
       if (dev::key_less(ed[i], er[i], bd, br)) {
         bd = ed[i];
         br = er[i];
