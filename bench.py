@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the hot path. Default: exact FlatIndex cosine search, 10,000-query batches, k=10.
 
-Workload: 1,183,514 x 100 float32 vectors from a 1,000-component Gaussian
+Workload (benchmark config 1): 1,183,514 x 100 float32 vectors from a 1,000-component Gaussian
 mixture, L2-normalized; 10,000 queries drawn the same way (seeded synthetic data standing in for
 GloVe-1.2M). On N GPUs (one process per GPU) every GPU holds the whole database (0.74 GB) and
 answers its 1/N slice of every query batch, with no exchange (``--shard queries``, the default);
@@ -12,7 +12,7 @@ of the whole 10k batch. Total work is fixed, so N>1 is strong scaling.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload c1|c2|c3] [--nprobe P] [--filter] [--shard queries|rows]
 
-``--workload c2`` / ``c3`` measure IVF-PQ search instead (BASELINE configs 2 and 3): the trained,
+``--workload c2`` / ``c3`` measure IVF-PQ search instead (benchmark configs 2 and 3): the trained,
 empty index the reference saved (tests/golden/ivf_c{2,3}_trained.qvr) is loaded on every GPU,
 each rank adds its id range of the database on its GPU, and a step is one search of the 10k
 batch at ``--nprobe`` (config 3: refine_factor 8; ``--filter``: a seeded random 1 % allowed-id

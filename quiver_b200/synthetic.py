@@ -54,7 +54,7 @@ def clustered(n: int, dim: int, clusters: int, seed: int) -> np.ndarray:
     return (centres[a] + rng.standard_normal((n, dim), dtype=np.float32)).astype(np.float32)
 
 
-# ---- benchmark configurations (BASELINE configs[0..4]) ----------------------------------------------
+# ---- benchmark configurations 0..4 ------------------------------------------------------------------
 
 def config0(seed_db: int = 0, seed_q: int = 1):
     """FlatIndex L2, k=10: 100,000 x 128 skewed ints, 1,000 queries."""

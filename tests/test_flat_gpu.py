@@ -149,7 +149,7 @@ def test_save_load_roundtrip_and_reference_format(gpu, tmp_path, reference):
 
 
 def test_config0_full_size_against_reference(gpu, reference):
-    """BASELINE config 0 at its full size (100k x 128 skewed ints, 1,000 queries, k=10)."""
+    """Benchmark config 0 at its full size (100k x 128 skewed ints, 1,000 queries, k=10)."""
     from quiver_b200.synthetic import config0
     base, q = config0()
     ix = gpu.FlatIndex(128, "l2")
