@@ -295,12 +295,15 @@ def run_reference_arm(args, rank, world):
                     "d2h_bytes_per_step": 0}}), flush=True)
         return
     from quiver_b200.synthetic import config1
-    db, q = config1(N_DB, N_Q)
+    n_db, n_q = args.rows, args.queries
+    db, q = config1(n_db, n_q)
     from oracle.oracle import REF_SO, Reference
     line = {"impl": "reference", "metric": METRIC, "unit": "QPS", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "data": "synthetic", "dtype": "f32",
-            "config": {"workload": WORKLOAD, "global_batch": N_Q, "k": K}}
+            "config": {"workload": WORKLOAD if (n_db, n_q) == (N_DB, N_Q) else
+                       f"FlatIndex cosine k=10, {n_db:,} x 100 mixture (reduced), {n_q:,} queries",
+                       "global_batch": n_q, "k": K}}
     if not os.path.exists(REF_SO):
         print(json.dumps({"impl": "reference",
                           "unavailable": "reference library oracle/_ref was not built"}))
@@ -316,19 +319,19 @@ def run_reference_arm(args, rank, world):
     t0 = time.perf_counter()
     f.search(q[:64], K)
     per_q = (time.perf_counter() - t0) / 64
-    per_step = int(min(N_Q, max(64, 4.0 / max(per_q, 1e-9))))  # about 4 s of CPU per step
+    per_step = int(min(n_q, max(64, 4.0 / max(per_q, 1e-9))))  # about 4 s of CPU per step
     for i in range(args.warmup):
         f.search(q[:per_step], K)
     times = []
     for i in range(args.steps):
-        lo = (i * per_step) % max(1, N_Q - per_step + 1)
+        lo = (i * per_step) % max(1, n_q - per_step + 1)
         t0 = time.perf_counter()
         f.search(q[lo:lo + per_step], K)
         times.append(time.perf_counter() - t0)
     qps = per_step * len(times) / sum(times)
-    sample = (f"{per_step} queries per step against the full {N_DB:,}-row database, "
+    sample = (f"{per_step} queries per step against the full {n_db:,}-row database, "
               f"FlatIndex::search_batch, {cores} threads, ISA {ref.isa}")
-    line.update({"value": qps, "ms_per_step": 1000.0 * N_Q / qps,
+    line.update({"value": qps, "ms_per_step": 1000.0 * n_q / qps,
                  "cpu_baseline": {"value": qps, "unit": "QPS", "cores": cores,
                                   "kind": "reference", "sample": sample},
                  "e2e": {"value": qps, "unit": "QPS", "h2d_bytes_per_step": 0,
