@@ -515,9 +515,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (sorted best-kKK prefix + entries appended since). Per 64 columns: one three-input
     // max/min tree gives the best score of each 8-row group and of all 64; the warp skips the 64
     // columns when no lane can improve on its threshold (the common case). Otherwise lanes append
-    // the groups they can improve on, one entry per group (its best screen distance). When any
-    // lane's list is full, the warp compacts together, which tightens every full list's threshold
-    // to its kKK-th entry: kKK groups, each holding a row at least that close.
+    // the groups they can improve on, one entry per group (its best screen distance). When some
+    // lane's appends would overflow its list, the warp compacts together first, which tightens
+    // every list's threshold to its kKK-th entry: kKK groups, each holding a row at least that
+    // close.
     const int quarter = warp & 3;
     const int tile = (warp - 2) >> 2;  // which query tile of the group
     const int qi = quarter * 32 + lane;
