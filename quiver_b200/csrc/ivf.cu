@@ -257,25 +257,31 @@ __global__ void select_probes_kernel(const float* __restrict__ coarse, size_t nl
 // the reference compares distances with <) << 32 | list id, eight bits a pass from the top, one
 // shared 256-bin histogram per pass, until the nprobe-th smallest composite is known. Composites
 // are distinct, so exactly nprobe of them lie at or below it; those are gathered and sorted.
+// kShared keeps the composites in shared memory; without it (nlist too large for that) every pass
+// recomputes them from the coarse distances in global memory.
 constexpr int kRadixProbeMax = 1024;
 constexpr int kRadixThreads = 256;
+constexpr size_t kRadixSharedMax = 160 * 1024;  // composites held in shared memory up to this
 
+template <bool kShared>
 __global__ void __launch_bounds__(kRadixThreads) select_probes_radix_kernel(
     const float* __restrict__ coarse, size_t nlist, int nprobe, int id_passes, int sort_n,
     uint32_t* __restrict__ probes, float* __restrict__ probe_d) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  uint64_t* comp = reinterpret_cast<uint64_t*>(smem_raw);  // nlist composites
-  uint64_t* sel = comp + nlist;                            // sort_n selected (padded with ~0)
+  uint64_t* sel = reinterpret_cast<uint64_t*>(smem_raw);   // sort_n selected (padded with ~0)
+  uint64_t* comp = sel + sort_n;                           // nlist composites (kShared)
   __shared__ unsigned hist[256];
   __shared__ uint64_t s_prefix;
   __shared__ unsigned s_need;
   __shared__ int s_count;
   const size_t q = blockIdx.x;
   const float* row = coarse + q * nlist;
-  for (size_t i = threadIdx.x; i < nlist; i += kRadixThreads) {
+  auto composite = [&](size_t i) {
     const float d = row[i] + 0.0f;  // -0 -> +0
-    comp[i] = (static_cast<uint64_t>(dev::ordered_bits(d)) << 32) | i;
-  }
+    return (static_cast<uint64_t>(dev::ordered_bits(d)) << 32) | i;
+  };
+  if (kShared)
+    for (size_t i = threadIdx.x; i < nlist; i += kRadixThreads) comp[i] = composite(i);
   uint64_t prefix = 0;
   unsigned need = static_cast<unsigned>(nprobe);  // rank (1-based) of the target among matches
   const int passes = 4 + id_passes;
@@ -288,7 +294,7 @@ __global__ void __launch_bounds__(kRadixThreads) select_probes_radix_kernel(
     __syncthreads();
     const uint64_t above = p == 0 ? 0ull : ~0ull << (shift + 8);
     for (size_t i = threadIdx.x; i < nlist; i += kRadixThreads) {
-      const uint64_t c = comp[i];
+      const uint64_t c = kShared ? comp[i] : composite(i);
       if ((c & above) == prefix) atomicAdd(&hist[(c >> shift) & 255], 1u);
     }
     __syncthreads();
@@ -325,7 +331,7 @@ __global__ void __launch_bounds__(kRadixThreads) select_probes_radix_kernel(
   for (int i = threadIdx.x; i < sort_n; i += kRadixThreads) sel[i] = ~0ull;
   __syncthreads();
   for (size_t i = threadIdx.x; i < nlist; i += kRadixThreads) {
-    const uint64_t c = comp[i];
+    const uint64_t c = kShared ? comp[i] : composite(i);
     if (c <= prefix) {
       const int at = atomicAdd(&s_count, 1);
       if (at < sort_n) sel[at] = c;  // exactly nprobe <= sort_n arrive
@@ -793,16 +799,18 @@ Prepared prepare_search(const IvfState& s, const float* d_queries, size_t nq, si
     int id_passes = 1;
     while (id_passes < 4 && (s.nlist - 1) >> (8 * id_passes) != 0) ++id_passes;
     const int sort_n = static_cast<int>(next_pow2(static_cast<size_t>(p.nprobe)));
-    const size_t smem = (s.nlist + sort_n) * sizeof(uint64_t);
-    QV_CUDA(cudaFuncSetAttribute(select_probes_radix_kernel,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    select_probes_radix_kernel<<<static_cast<unsigned>(nq), kRadixThreads, smem, st>>>(
+    const bool shared = s.nlist * sizeof(uint64_t) <= kRadixSharedMax;
+    const size_t smem = (sort_n + (shared ? s.nlist : 0)) * sizeof(uint64_t);
+    auto kernel = shared ? select_probes_radix_kernel<true> : select_probes_radix_kernel<false>;
+    QV_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kernel<<<static_cast<unsigned>(nq), kRadixThreads, smem, st>>>(
         p.coarse.get<float>(), s.nlist, p.nprobe, id_passes, sort_n, p.probes.get<uint32_t>(),
         p.probe_d.get<float>());
     check_launch("select_probes_radix_kernel");
     return p;
   }
   const size_t smem = pool * (sizeof(float) + sizeof(uint64_t));
+  QV_REQUIRE(smem <= 227 * 1024, "IVF-PQ search: nprobe above 1024 needs nlist <= 16384");
   QV_CUDA(cudaFuncSetAttribute(select_probes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)smem));
   select_probes_kernel<<<static_cast<unsigned>(nq), 512, smem, st>>>(

@@ -142,3 +142,27 @@ def test_sharded_load_merges_to_unsharded(gpu, manifest):
     torch.cuda.synchronize()
     wl, wd = whole.search(q, keep, nprobe=8)
     assert_topk_parity(ol.cpu().numpy(), od.cpu().numpy(), wl, wd, exact=True, what="sharded")
+
+
+def test_many_lists_probe_selection(gpu, oracle, tmp_path):
+    """nlist = 40,000: the probe selection reads its composites from global memory (too many
+    lists for shared memory); results equal the oracle's on the saved index."""
+    from oracle.oracle import QvrIvf
+    rng = np.random.default_rng(17)
+    dim, nlist, m = 16, 40_000, 4
+    cents = rng.standard_normal((nlist, dim)).astype(np.float32)
+    books = rng.standard_normal((m, 256, dim // m)).astype(np.float32) * np.float32(0.3)
+    base = (cents[rng.integers(0, nlist, 60_000)] +
+            rng.standard_normal((60_000, dim)).astype(np.float32) * np.float32(0.2))
+    q = cents[rng.integers(0, nlist, 64)] + rng.standard_normal((64, dim)).astype(np.float32) * 0.2
+    q = q.astype(np.float32)
+    ix = gpu.IvfPqIndex(dim, "l2", nlist, m, store_vectors=True)
+    ix.set_trained(cents, books)
+    ix.add(base)
+    path = tmp_path / "many.qvr"
+    ix.save(path)
+    qv = QvrIvf(path)
+    for nprobe, rf in [(1, 0), (16, 0), (40, 2)]:
+        l, d = ix.search(q, 10, nprobe=nprobe, refine_factor=rf)
+        wl, wd = oracle.ivf_search(qv, q, 10, nprobe, rf)
+        assert_topk_parity(l, d, wl, wd, exact=True, what=f"nlist {nlist} nprobe {nprobe} {rf}")
