@@ -1,8 +1,8 @@
 #!/usr/bin/env python
 """Benchmark of the hot path. Default: exact FlatIndex cosine search, 10,000-query batches, k=10.
 
-Workload (benchmark config 1): 1,183,514 x 100 float32 vectors from a 1,000-component Gaussian
-mixture, L2-normalized; 10,000 queries drawn the same way (seeded synthetic data standing in for
+Workload: 1,183,514 x 100 float32 vectors from a 1,000-component Gaussian mixture,
+L2-normalized; 10,000 queries drawn the same way (seeded synthetic data standing in for
 GloVe-1.2M). On N GPUs (one process per GPU) every GPU holds the whole database (0.74 GB) and
 answers its 1/N slice of every query batch, with no exchange (``--shard queries``, the default);
 ``--shard rows`` instead splits the database by id range, gives every GPU the whole batch and
@@ -12,11 +12,11 @@ of the whole 10k batch. Total work is fixed, so N>1 is strong scaling.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload c1|c2|c3] [--nprobe P] [--filter] [--shard queries|rows]
 
-``--workload c2`` / ``c3`` measure IVF-PQ search instead (benchmark configs 2 and 3): the trained,
+``--workload c2`` / ``c3`` measure IVF-PQ search instead (L2 nlist 2048 m 32 over 1M skewed-int
+rows; cosine nlist 2048 m 25 refine 8 over the 1.18M mixture rows): the trained,
 empty index the reference saved (tests/golden/ivf_c{2,3}_trained.qvr) is loaded on every GPU,
 each rank adds its id range of the database on its GPU, and a step is one search of the 10k
-batch at ``--nprobe`` (config 3: refine_factor 8; ``--filter``: a seeded random 1 % allowed-id
-set).
+batch at ``--nprobe`` (c3: refine_factor 8; ``--filter``: a seeded random 1 % allowed-id set).
 
 Rank 0 prints one JSON line. ``value`` is whole-job QPS with queries already on the GPUs;
 ``e2e`` is the same metric through the public Python API with the queries in pinned host memory
@@ -42,7 +42,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "QPS (10k-query batch, k=10) at 1/2/4/8 B200; % of HBM/tensor roofline"
-WORKLOAD = "FlatIndex cosine k=10, 1,183,514 x 100 mixture (BASELINE config 1), 10,000 queries"
+WORKLOAD = "FlatIndex cosine k=10, 1,183,514 x 100 Gaussian-mixture rows, 10,000 queries"
 N_DB, N_Q, DIM, K = 1_183_514, 10_000, 100, 10
 
 
@@ -54,7 +54,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--rows", type=int, default=N_DB,
-                    help="database rows (default: config 1's 1,183,514; smaller for profiling)")
+                    help="database rows (default: the workload's 1,183,514; smaller for "
+                         "profiling)")
     ap.add_argument("--queries", type=int, default=N_Q, help="queries per batch (default 10,000)")
     ap.add_argument("--workload", choices=["c1", "c2", "c3"], default="c1")
     ap.add_argument("--nprobe", type=int, default=64, help="IVF-PQ workloads: lists probed")
@@ -68,9 +69,10 @@ def parse():
 IVF_WORKLOADS = {
     # name: (trained file, metric, dim, refine_factor, rows, description)
     "c2": ("ivf_c2_trained.qvr", "l2", 128, 0, 1_000_000,
-           "IvfPqIndex L2 nlist 2048 m 32, 1,000,000 x 128 skewed ints (BASELINE config 2)"),
+           "IvfPqIndex L2 nlist 2048 m 32, 1,000,000 x 128 skewed-int rows, 10,000 queries"),
     "c3": ("ivf_c3_trained.qvr", "cosine", 100, 8, 1_183_514,
-           "IvfPqIndex cosine nlist 2048 m 25 refine 8, 1,183,514 x 100 mixture (BASELINE config 3)"),
+           "IvfPqIndex cosine nlist 2048 m 25 refine 8, 1,183,514 x 100 Gaussian-mixture rows, "
+           "10,000 queries"),
 }
 
 
@@ -198,6 +200,26 @@ class ClockSampler:
                 "reasons": sorted(self.reasons), "samples": len(self.sm), "source": self.source}
 
 
+def flat_config(args) -> dict:
+    """The Flat workload's description (identical in both arms' JSON lines)."""
+    n_db, n_q = args.rows, args.queries
+    full = (n_db, n_q) == (N_DB, N_Q)
+    return {"workload": WORKLOAD if full else
+            f"FlatIndex cosine k=10, {n_db:,} x 100 Gaussian-mixture rows (reduced), "
+            f"{n_q:,} queries",
+            "global_batch": n_q, "k": K, "database_rows": n_db, "dim": DIM, "metric": "cosine",
+            "l2": "inputs larger than L2 (473 MB database read per pass)"}
+
+
+def ivf_config(args) -> dict:
+    """The IVF-PQ workload's description (identical in both arms' JSON lines)."""
+    fname, metric, dim, refine, rows, desc = IVF_WORKLOADS[args.workload]
+    return {"workload": desc, "nprobe": args.nprobe, "refine_factor": refine,
+            "filter": "1% ids" if args.filter else None, "global_batch": min(args.queries, N_Q),
+            "k": K, "database_rows": rows, "dim": dim, "metric": metric,
+            "l2": "codes (32 MB / 30 MB) are L2-resident; no flush between steps"}
+
+
 def cpu_reference_qps(db, queries, seconds: float, threads: int = 0):
     """Times the reference's own FlatIndex::search_batch (oracle/_ref) on host cores for about
     `seconds`. Returns (qps, cores, sample description, kind) or None if unavailable."""
@@ -219,7 +241,7 @@ def cpu_reference_qps(db, queries, seconds: float, threads: int = 0):
     t0 = time.perf_counter()
     f.search(queries[:n], K, threads=threads)
     dt = time.perf_counter() - t0
-    sample = (f"{n} of the {N_Q} queries against the full {N_DB:,}-row database, "
+    sample = (f"{n} of the {len(queries)} queries against the full {len(db):,}-row database, "
               f"FlatIndex::search_batch with {cores} threads, ISA {ref.isa}")
     return n / dt, cores, sample, "reference"
 
@@ -256,54 +278,17 @@ def cpu_reference_ivf_qps(ref, ix, queries, nprobe, refine, allowed, seconds: fl
     return n / (time.perf_counter() - t0), n
 
 
+REF_STEP_SECONDS = 3.0  # CPU time of one reference step: a bounded sample of the batch
+
+
 def run_reference_arm(args, rank, world):
+    """The reference's own CPU search (oracle/_ref, compiled from the reference sources) on the
+    host cores, same workload and metric. Each step searches a bounded sample of the batch
+    (about REF_STEP_SECONDS of CPU) against the whole database; the line reports the sample size
+    and the measured time per step."""
     if rank != 0:
         return
-    if args.workload != "c1":
-        from oracle.oracle import REF_SO, Reference
-        name = IVF_WORKLOADS[args.workload]
-        if not os.path.exists(REF_SO):
-            print(json.dumps({"impl": "reference",
-                              "unavailable": "reference library oracle/_ref was not built"}))
-            return
-        ref = Reference()
-        db, q = ivf_data(args.workload)
-        ix = ref_ivf_index(ref, args.workload, db)
-        allowed = ivf_allowed(len(db)) if args.filter else None
-        refine = name[3]
-        per_step = None
-        qps_list = []
-        for i in range(args.warmup + args.steps):
-            qps, n = cpu_reference_ivf_qps(ref, ix, q, args.nprobe, refine, allowed, 3.0)
-            if i >= args.warmup:
-                qps_list.append(qps)
-                per_step = n
-        qps = statistics.mean(qps_list)
-        sample = (f"{per_step} of the {N_Q} queries per step, IvfPqIndex::search_batch nprobe "
-                  f"{args.nprobe} refine {refine}{' filtered 1%' if args.filter else ''}, "
-                  f"{ref.threads} threads, ISA {ref.isa}")
-        print(json.dumps({
-            "impl": "reference", "metric": METRIC, "value": qps, "unit": "QPS",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * N_Q / qps, "higher_is_better": True, "data": "synthetic",
-            "dtype": "f32", "config": {"workload": name[5], "nprobe": args.nprobe,
-                                       "filter": "1% ids" if args.filter else None,
-                                       "global_batch": N_Q, "k": K},
-            "cpu_baseline": {"value": qps, "unit": "QPS", "cores": ref.threads,
-                             "kind": "reference", "sample": sample},
-            "e2e": {"value": qps, "unit": "QPS", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}), flush=True)
-        return
-    from quiver_b200.synthetic import config1
-    n_db, n_q = args.rows, args.queries
-    db, q = config1(n_db, n_q)
     from oracle.oracle import REF_SO, Reference
-    line = {"impl": "reference", "metric": METRIC, "unit": "QPS", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "data": "synthetic", "dtype": "f32",
-            "config": {"workload": WORKLOAD if (n_db, n_q) == (N_DB, N_Q) else
-                       f"FlatIndex cosine k=10, {n_db:,} x 100 mixture (reduced), {n_q:,} queries",
-                       "global_batch": n_q, "k": K}}
     if not os.path.exists(REF_SO):
         print(json.dumps({"impl": "reference",
                           "unavailable": "reference library oracle/_ref was not built"}))
@@ -313,30 +298,51 @@ def run_reference_arm(args, rank, world):
     except OSError as e:
         print(json.dumps({"impl": "reference", "unavailable": f"oracle/_ref not loadable: {e}"}))
         return
-    f = ref.flat(DIM, "cosine")
-    f.add(db)
-    cores = ref.threads
+    if args.workload == "c1":
+        from quiver_b200.synthetic import config1
+        db, q = config1(args.rows, args.queries)
+        config = flat_config(args)
+        f = ref.flat(DIM, "cosine")
+        f.add(db)
+        search = lambda qs: f.search(qs, K)  # noqa: E731
+        what = "FlatIndex::search_batch"
+    else:
+        db, q = ivf_data(args.workload)
+        q = q[:args.queries]
+        config = ivf_config(args)
+        ix = ref_ivf_index(ref, args.workload, db)
+        allowed = ivf_allowed(len(db)) if args.filter else None
+        refine = IVF_WORKLOADS[args.workload][3]
+        search = lambda qs: ix.search(qs, K, args.nprobe, refine, allowed)  # noqa: E731
+        what = (f"IvfPqIndex::search_batch nprobe {args.nprobe} refine {refine}"
+                f"{' filtered 1%' if args.filter else ''}")
+    n_q = len(q)
     t0 = time.perf_counter()
-    f.search(q[:64], K)
+    search(q[:64])
     per_q = (time.perf_counter() - t0) / 64
-    per_step = int(min(n_q, max(64, 4.0 / max(per_q, 1e-9))))  # about 4 s of CPU per step
-    for i in range(args.warmup):
-        f.search(q[:per_step], K)
+    per_step = int(min(n_q, max(64, REF_STEP_SECONDS / max(per_q, 1e-9))))
+    for _ in range(args.warmup):
+        search(q[:per_step])
     times = []
     for i in range(args.steps):
         lo = (i * per_step) % max(1, n_q - per_step + 1)
         t0 = time.perf_counter()
-        f.search(q[lo:lo + per_step], K)
+        search(q[lo:lo + per_step])
         times.append(time.perf_counter() - t0)
-    qps = per_step * len(times) / sum(times)
-    sample = (f"{per_step} queries per step against the full {n_db:,}-row database, "
-              f"FlatIndex::search_batch, {cores} threads, ISA {ref.isa}")
-    line.update({"value": qps, "ms_per_step": 1000.0 * n_q / qps,
-                 "cpu_baseline": {"value": qps, "unit": "QPS", "cores": cores,
-                                  "kind": "reference", "sample": sample},
-                 "e2e": {"value": qps, "unit": "QPS", "h2d_bytes_per_step": 0,
-                         "d2h_bytes_per_step": 0}})
-    print(json.dumps(line), flush=True)
+    step_s = statistics.mean(times)
+    qps = per_step / step_s
+    sample = (f"{per_step} of the {n_q:,} queries per step against the full {len(db):,}-row "
+              f"database, {what}, {ref.threads} threads, ISA {ref.isa}")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": qps, "unit": "QPS",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * step_s, "queries_per_step": per_step, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config, "parallelism": f"{ref.threads} host threads (reference thread pool)",
+        "cpu_baseline": {"value": qps, "unit": "QPS", "cores": ref.threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": qps, "unit": "QPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
 
 
 def run_ivf(args, rank, world, local):
@@ -371,21 +377,22 @@ def run_ivf(args, rank, world, local):
     _native.set_timing(True)
     sampler = ClockSampler(local)
     sampler.start()
-    launches, kernel_ms, kernel_bytes = 0, 0.0, 0.0
+    qv.last_search_stats()  # start the accumulation here
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
         index.search_device(dq, K, args.nprobe, refine, bitmap)
-        st = qv.last_search_stats()
-        launches += st["kernel_launches"]
-        kernel_ms += st["dominant_kernel_ms"]
-        kernel_bytes += st["dominant_kernel_work"]
     e1.record()
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()
+    # With timing on, the library recorded CUDA events around each step's scan on its stream and
+    # counted launches; reading the stats resolves them (after the timed region).
+    st = qv.last_search_stats()
+    launches, kernel_ms, kernel_bytes = (st["kernel_launches"], st["dominant_kernel_ms"],
+                                         st["dominant_kernel_work"])
     _native.set_timing(False)
     elapsed = e0.elapsed_time(e1)
     if world > 1:
@@ -422,10 +429,7 @@ def run_ivf(args, rank, world, local):
         "metric": METRIC, "value": value, "unit": "QPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": elapsed / args.steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": desc, "nprobe": args.nprobe, "refine_factor": refine,
-                   "filter": "1% ids" if args.filter else None, "global_batch": nq, "k": K,
-                   "database_rows": n, "parallelism": f"id-range shards x{world}",
-                   "l2": "codes (32 MB / 30 MB) are L2-resident; no flush between steps"},
+        "config": ivf_config(args), "parallelism": f"id-range shards x{world}",
         "gpu_launches": launches,
         "roofline": {"bound": "hbm", "kernel": "ivf_scan_kernel", "achieved": achieved,
                      "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
@@ -499,27 +503,23 @@ def main():
     _native.set_timing(True)
     sampler = ClockSampler(local)
     sampler.start()
-    launches = 0
-    kernel_ms = 0.0
-    kernel_work = 0.0
-    kernel_name = ""
-    rescans = 0
+    qv.last_search_stats()  # start the accumulation here
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(args.steps):
-        index.search_device(dq, K)
-        st = qv.last_search_stats()
-        launches += st["kernel_launches"]
-        kernel_ms += st["dominant_kernel_ms"]
-        kernel_work += st["dominant_kernel_work"]
-        kernel_name = st["dominant_kernel"]
-        rescans += st["rescanned_queries"]
+        index.search_device(dq, K)  # enqueues only: no host round trip per step
     e1.record()
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop()
+    # With timing on, the library recorded CUDA events around each step's screen on its stream,
+    # counted launches and rescans; reading the stats resolves them (after the timed region).
+    st = qv.last_search_stats()
+    launches, kernel_ms, kernel_work = (st["kernel_launches"], st["dominant_kernel_ms"],
+                                        st["dominant_kernel_work"])
+    kernel_name, rescans = st["dominant_kernel"], st["rescanned_queries"]
     _native.set_timing(False)
     elapsed = e0.elapsed_time(e1)
     if world > 1:
@@ -568,12 +568,9 @@ def main():
         "metric": METRIC, "value": value, "unit": "QPS", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": WORKLOAD if (n_db, n_q) == (N_DB, N_Q) else
-                   f"FlatIndex cosine k=10, {n_db:,} x 100 mixture (reduced), {n_q:,} queries",
-                   "global_batch": n_q, "k": K, "database_rows": n_db,
-                   "dim": DIM, "parallelism": (f"query slices x{world}, rows replicated"
-                                               if by_queries else f"id-range shards x{world}"),
-                   "l2": "inputs larger than L2 (473 MB database per pass)"},
+        "config": flat_config(args),
+        "parallelism": (f"query slices x{world}, rows replicated" if by_queries
+                        else f"id-range shards x{world}"),
         "gpu_launches": launches, "rescanned_queries": rescans,
         "roofline": {"bound": "tensor", "kernel": kernel_name, "achieved": achieved,
                      "peak": tflops, "unit": "TFLOP/s", "frac": achieved / tflops,

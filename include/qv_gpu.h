@@ -12,12 +12,18 @@
  * Host-buffer entry points (no "_device" suffix) take caller-owned host memory that is valid only
  * for the call; they copy inputs to the index's GPU, run there, and copy results back before
  * returning. "_device" entry points take device pointers on the index's GPU plus a cudaStream_t
- * passed as void* and return once the work is enqueued: results are ordered like work queued on
- * that stream. NULL means CUDA's default stream (PyTorch's default stream too); the library then
- * runs the work on its own stream between two event waits, so it is still ordered after earlier
- * and before later default-stream work. Index state is read-only during searches, so concurrent searches on one index are safe;
- * add() must not run concurrently with other calls on the same index (the C++ wrapper serializes
- * it with a shared mutex, as the reference does).
+ * passed as void* and return once the work is enqueued, without waiting for the GPU: results are
+ * ordered like work queued on that stream. NULL means CUDA's default stream (PyTorch's default
+ * stream too); the library then runs the work on the calling thread's own stream between two
+ * event waits, so it is still ordered after earlier and before later default-stream work (NULL
+ * calls from different host threads therefore run on different streams and may overlap).
+ * Conditions a _device search can only detect on the GPU do not fail the call: a query holding
+ * NaN or infinity gets no results (QV_INVALID_LABEL with a NaN distance) where the host-buffer
+ * entry point fails with the reference's error. Index state is read-only during searches, so
+ * concurrent searches on one index are safe; add() must not run concurrently with other calls on
+ * the same index (the C++ wrapper serializes it with a shared mutex, as the reference does), and
+ * with _device searches it must also not start before their GPU work has finished (synchronize
+ * their streams first).
  *
  * Distances follow quiver::Metric (include/quiver/common.h:25-29): squared L2, 1 - <q,x> for inner
  * product, 1 - cos for cosine; smaller is closer. Unfilled result slots get label
@@ -110,15 +116,18 @@ qv_status qv_flat_set_row_offset(qv_flat* index, uint64_t row_offset);
  * exists for callers that must not allocate device memory while they search (a serving loop with
  * a fixed device-memory budget, or code running where cudaMalloc/cudaFree are not allowed, e.g.
  * from a driver callback or while another thread holds the allocator). Same arguments and the same
- * results as qv_flat_search_device (it screens on the CUDA cores and re-ranks and certifies
- * exactly the same way), and it calls no cudaMalloc, cudaFree or other allocating routine: every
- * temporary lives in one fixed scratch array of qv_flat_noalloc_max_bytes() bytes (64 MiB) that
- * each GPU loading the library holds until the process exits. A call whose temporaries would not
- * fit (roughly nq * (dim + n_chunks * KK * 8) bytes) fails with QV_ERR_INVALID; split the queries.
- * The first call on a device looks up the scratch's device address (cudaGetSymbolAddress), so make
- * that first call before any stream capture. All calls share the scratch and it keeps the last
- * call's contents: calls whose work overlaps on the GPU (different streams, or another index on
- * the same device) race; serialize them, e.g. on one stream. */
+ * results as qv_flat_search_device, queries holding NaN or infinity included (it screens on the
+ * CUDA cores and re-ranks and certifies exactly the same way), and it calls no cudaMalloc,
+ * cudaFree or other allocating routine: every temporary lives in one fixed scratch array of
+ * qv_flat_noalloc_max_bytes() bytes (64 MiB) that each GPU loading the library holds until the
+ * process exits. A call whose temporaries would not fit (roughly nq * (dim + n_chunks * KK * 8)
+ * bytes) fails with QV_ERR_INVALID; split the queries. It does not feed qv_last_search_stats.
+ * The first call on a device looks up the scratch's device address (cudaGetSymbolAddress) and
+ * caches it for the life of the process, so make that first call before any stream capture and
+ * do not reset that device afterwards. All calls share the scratch and it keeps the last call's
+ * contents: calls whose work overlaps on the GPU (different streams, another index on the same
+ * device, or NULL-stream calls from different host threads, which run on different streams) race;
+ * serialize them by passing one explicit stream, or call from one thread. */
 qv_status qv_flat_search_device_noalloc(const qv_flat* index, const float* queries, size_t nq,
                                         size_t k, const uint64_t* position_bitmap,
                                         uint64_t* labels, float* distances, uint64_t* keys,
@@ -220,11 +229,14 @@ qv_status qv_select_topk_device(int device, size_t nq, size_t n, size_t k, const
                                 float* out_distances, uint64_t* out_keys, uint64_t* out_labels,
                                 void* stream);
 
-/* Counters of the last search on the calling thread (for the bench and tests): kernel launches
- * issued, queries whose screen could not be certified and were rescanned exactly, and, when timing
- * is enabled, the device time of the search's dominant kernel (measured with CUDA events on the
- * stream it runs on), its name and its algorithmic work (FLOPs for the distance screen, bytes for
- * scans) so callers can compute a roofline fraction. */
+/* Counters of the calling thread's searches (for the bench and tests): kernel launches issued,
+ * queries whose screen could not be certified and were rescanned exactly, and, when timing is
+ * enabled, the device time of the searches' dominant kernel (CUDA events recorded on the stream
+ * it runs on), its name and its algorithmic work (FLOPs for the distance screen, bytes for scans)
+ * so callers can compute a roofline fraction. With timing disabled they describe the last search;
+ * with timing enabled they accumulate over every search since timing was enabled or since the
+ * previous call, which resolves the recorded events (waiting for them) and starts again. The
+ * rescan count of a _device Flat search is read after waiting for that search to finish. */
 typedef struct qv_search_stats {
   uint64_t kernel_launches;
   uint64_t rescanned_queries;

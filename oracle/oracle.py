@@ -38,7 +38,10 @@ _sz = C.c_size_t
 def build(ref_root: Optional[str] = None) -> None:
     """Builds the C restatement, and the reference library when its sources are present."""
     subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
-    ref_root = ref_root or os.environ.get("QUIVER_REFERENCE", "/root/reference")
+    # The reference checkout: QUIVER_REFERENCE when set, else a "reference" directory beside
+    # this repository.
+    ref_root = ref_root or os.environ.get(
+        "QUIVER_REFERENCE", os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
     if os.path.isdir(os.path.join(ref_root, "src")):
         subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref_root}"], check=True)
 

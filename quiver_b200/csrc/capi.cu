@@ -55,6 +55,78 @@ bool& thread_timing() {
   return on;
 }
 
+namespace {
+thread_local std::vector<PendingTimer> t_pending;
+// The report words of this thread's last _device Flat search (read by qv_last_search_stats),
+// or nullptr.
+thread_local SearchFlags* t_flags = nullptr;
+
+// Applies the report words of a host-buffer search that has completed to this thread's stats and
+// turns them into the reference's errors.
+void report_flags(const int* f) {
+  t_stats.rescanned_queries += static_cast<uint64_t>(f[kFlagRescanned]);
+  QV_REQUIRE(f[kFlagNonFinite] == 0, "vectors must not contain NaN or infinity");
+  if (f[kFlagTimeout] != 0)
+    fail(QV_ERR_DEVICE, "tensor-core screen timed out waiting on a pipeline barrier");
+}
+}  // namespace
+
+void begin_search_stats() {
+  if (!thread_timing()) t_stats = SearchStats{};
+}
+
+void defer_timer(const PendingTimer& t) { t_pending.push_back(t); }
+
+void resolve_timers() {
+  for (const PendingTimer& t : t_pending) {
+    float ms = 0.0f;
+    if (cudaEventSynchronize(t.e1) == cudaSuccess &&
+        cudaEventElapsedTime(&ms, t.e0, t.e1) == cudaSuccess) {
+      t_stats.dominant_ms += ms;
+      t_stats.dominant_work += t.work + (t.count ? static_cast<double>(*t.count) * t.per_count : 0.0);
+      t_stats.work_is_bytes = t.bytes;
+      t_stats.dominant_name = t.name;
+    }
+    cudaEventDestroy(t.e0);
+    cudaEventDestroy(t.e1);
+  }
+  t_pending.clear();
+}
+
+unsigned long long* timing_count_slot() {
+  constexpr size_t kSlots = 4096;
+  thread_local unsigned long long* slots = nullptr;
+  thread_local size_t next = 0;
+  if (slots == nullptr) {
+    void* p = nullptr;
+    QV_CUDA(cudaHostAlloc(&p, kSlots * sizeof(unsigned long long), cudaHostAllocPortable));
+    slots = static_cast<unsigned long long*>(p);
+  }
+  unsigned long long* s = slots + next;
+  next = (next + 1) % kSlots;
+  return s;
+}
+
+// Per-thread device words that a _device search's kernels report into (rescanned queries,
+// non-finite queries, screen timeouts), and a pinned host copy of them queued at the end of each
+// search, read by qv_last_search_stats once the search's stream has completed.
+SearchFlags& thread_search_flags(int device) {
+  thread_local std::map<int, SearchFlags> flags;
+  auto it = flags.find(device);
+  if (it != flags.end()) return it->second;
+  SearchFlags f;
+  QV_CUDA(cudaMalloc(&f.dev, 2 * kSearchFlagWords * sizeof(int)));
+  QV_CUDA(cudaMemset(f.dev, 0, 2 * kSearchFlagWords * sizeof(int)));
+  void* h = nullptr;
+  QV_CUDA(cudaHostAlloc(&h, 2 * kSearchFlagWords * sizeof(int), cudaHostAllocPortable));
+  f.host = static_cast<int*>(h);
+  std::memset(f.host, 0, 2 * kSearchFlagWords * sizeof(int));
+  f.sync_dev = f.dev + kSearchFlagWords;
+  f.sync_host = f.host + kSearchFlagWords;
+  QV_CUDA(cudaEventCreateWithFlags(&f.done, cudaEventDisableTiming));
+  return flags.emplace(device, f).first->second;
+}
+
 // Keeps freed stream-ordered allocations in the device's default memory pool instead of
 // returning them to the driver at every synchronization, so that the temporaries of one search
 // are reused by the next without remapping memory (a per-process setting of this context).
@@ -394,6 +466,18 @@ qv_status qv_last_search_stats(qv_search_stats* stats) {
   return guarded([&] {
     QV_REQUIRE(stats != nullptr, "null argument");
     std::memset(stats, 0, sizeof(*stats));
+    if (thread_timing()) resolve_timers();
+    // The rescan count of this thread's _device Flat searches (the last one, or with timing on
+    // every one since the previous read), once their report words have come back.
+    if (t_flags != nullptr) {
+      QV_CUDA(cudaEventSynchronize(t_flags->done));
+      t_stats.rescanned_queries += static_cast<uint64_t>(t_flags->host[kFlagRescanned]);
+      if (thread_timing()) {  // the words accumulate while timing is on: start again
+        QV_CUDA(cudaMemset(t_flags->dev, 0, kSearchFlagWords * sizeof(int)));
+        std::memset(t_flags->host, 0, kSearchFlagWords * sizeof(int));
+      }
+      t_flags = nullptr;
+    }
     stats->kernel_launches = t_stats.kernel_launches;
     stats->rescanned_queries = t_stats.rescanned_queries;
     stats->dominant_kernel_ms = t_stats.dominant_ms;
@@ -401,11 +485,16 @@ qv_status qv_last_search_stats(qv_search_stats* stats) {
     stats->dominant_work_is_bytes = t_stats.work_is_bytes ? 1u : 0u;
     std::strncpy(stats->dominant_kernel, t_stats.dominant_name.c_str(),
                  sizeof(stats->dominant_kernel) - 1);
+    if (thread_timing()) t_stats = SearchStats{};  // accumulated since the previous read
   });
 }
 
 qv_status qv_set_timing(int enable) {
-  return guarded([&] { thread_timing() = enable != 0; });
+  return guarded([&] {
+    if (thread_timing() && enable == 0) resolve_timers();  // release pending events
+    if (enable != 0 && !thread_timing()) t_stats = SearchStats{};
+    thread_timing() = enable != 0;
+  });
 }
 
 qv_status qv_device_free(int device, void* ptr) {
@@ -473,7 +562,7 @@ qv_status qv_flat_add(qv_flat* index, const float* vectors, size_t n, const uint
 qv_status qv_flat_search(const qv_flat* index, const float* queries, size_t nq, size_t k,
                          const qv_filter* filter, uint64_t* labels, float* distances) {
   return guarded([&] {
-    t_stats = SearchStats{};
+    begin_search_stats();
     QV_REQUIRE(index != nullptr, "null index");
     if (nq == 0 || k == 0) return;  // src/flat_index.cc:128
     QV_REQUIRE(queries != nullptr && labels != nullptr && distances != nullptr,
@@ -481,19 +570,23 @@ qv_status qv_flat_search(const qv_flat* index, const float* queries, size_t nq, 
     const FlatState& s = index->s;
     const size_t total = result_size(nq, k);
     std::shared_lock lock(index->mu);
-    // The search checks the queries for NaN and infinity on the device (and raises before any
-    // result is copied out); with no stored rows it launches nothing, so check here.
-    if (s.n == 0) check_finite(queries, nq * s.dim);
     DeviceScope scope(s.device);
     cudaStream_t st = thread_stream(s.device);
+    // The device search marks queries holding NaN or infinity (the reference rejects them,
+    // src/flat_index.cc:131); the report words come back with the results, in one round trip.
+    SearchFlags& flags = thread_search_flags(s.device);
     DeviceBuffer dq, dl(total * sizeof(uint64_t), st), dd(total * sizeof(float), st);
+    QV_CUDA(cudaMemsetAsync(flags.sync_dev, 0, kSearchFlagWords * sizeof(int), st));
     h2d(dq, queries, nq * s.dim, st);
     DeviceBuffer bm = device_filter(s.labels.get<uint64_t>(), s.n, filter, st);
     flat_search(s, dq.get<float>(), nq, k, bm.get<uint64_t>(), dl.get<uint64_t>(),
-                dd.get<float>(), nullptr, st);
+                dd.get<float>(), nullptr, flags.sync_dev, st);
+    QV_CUDA(cudaMemcpyAsync(flags.sync_host, flags.sync_dev, kSearchFlagWords * sizeof(int),
+                            cudaMemcpyDeviceToHost, st));
     QV_CUDA(cudaMemcpyAsync(labels, dl.get(), total * sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
     QV_CUDA(cudaMemcpyAsync(distances, dd.get(), total * sizeof(float), cudaMemcpyDeviceToHost, st));
     QV_CUDA(cudaStreamSynchronize(st));
+    report_flags(flags.sync_host);
   });
 }
 
@@ -501,7 +594,7 @@ qv_status qv_flat_search_device(const qv_flat* index, const float* queries, size
                                 const uint64_t* position_bitmap, uint64_t* labels,
                                 float* distances, uint64_t* keys, void* stream) {
   return guarded([&] {
-    t_stats = SearchStats{};
+    begin_search_stats();
     QV_REQUIRE(index != nullptr, "null index");
     if (nq == 0 || k == 0) return;
     QV_REQUIRE(queries != nullptr && labels != nullptr && distances != nullptr,
@@ -512,7 +605,17 @@ qv_status qv_flat_search_device(const qv_flat* index, const float* queries, size
     DeviceScope scope(s.device);
     CallerStream call_stream(stream, s.device);
     cudaStream_t st = call_stream.get();
-    flat_search(s, queries, nq, k, position_bitmap, labels, distances, keys, st);
+    // Nothing here waits for the GPU: device-detected conditions (queries holding NaN or
+    // infinity, a screen that gave up on a barrier, rescans) land in this thread's report words,
+    // whose host copy qv_last_search_stats reads once the stream has completed.
+    SearchFlags& flags = thread_search_flags(s.device);
+    if (!thread_timing())
+      QV_CUDA(cudaMemsetAsync(flags.dev, 0, kSearchFlagWords * sizeof(int), st));
+    flat_search(s, queries, nq, k, position_bitmap, labels, distances, keys, flags.dev, st);
+    QV_CUDA(cudaMemcpyAsync(flags.host, flags.dev, kSearchFlagWords * sizeof(int),
+                            cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaEventRecord(flags.done, st));
+    t_flags = &flags;
   });
 }
 
@@ -521,7 +624,7 @@ qv_status qv_flat_search_device_noalloc(const qv_flat* index, const float* queri
                                         uint64_t* labels, float* distances, uint64_t* keys,
                                         void* stream) {
   return guarded([&] {
-    t_stats = SearchStats{};
+    begin_search_stats();
     QV_REQUIRE(index != nullptr, "null index");
     if (nq == 0 || k == 0) return;
     QV_REQUIRE(queries != nullptr && labels != nullptr && distances != nullptr,
@@ -768,7 +871,7 @@ qv_status qv_ivfpq_search(const qv_ivfpq* index, const float* queries, size_t nq
                           size_t nprobe, size_t refine_factor, const qv_filter* filter,
                           uint64_t* labels, float* distances) {
   return guarded([&] {
-    t_stats = SearchStats{};
+    begin_search_stats();
     QV_REQUIRE(index != nullptr, "null index");
     if (nq == 0 || k == 0) return;  // src/ivfpq_index.cc:424
     QV_REQUIRE(queries != nullptr && labels != nullptr && distances != nullptr,
@@ -807,7 +910,7 @@ qv_status qv_ivfpq_search_device(const qv_ivfpq* index, const float* queries, si
                                  const uint64_t* position_bitmap, uint64_t* labels,
                                  float* distances, void* stream) {
   return guarded([&] {
-    t_stats = SearchStats{};
+    begin_search_stats();
     QV_REQUIRE(index != nullptr, "null index");
     if (nq == 0 || k == 0) return;
     result_size(nq, k);
@@ -825,7 +928,7 @@ qv_status qv_ivfpq_candidates_device(const qv_ivfpq* index, const float* queries
                                      float* distances, uint64_t* keys, uint64_t* labels,
                                      void* stream) {
   return guarded([&] {
-    t_stats = SearchStats{};
+    begin_search_stats();
     QV_REQUIRE(index != nullptr && distances && keys && labels, "null argument");
     const IvfState& s = index->s;
     std::shared_lock lock(index->mu);

@@ -100,12 +100,13 @@ struct EpsModel {
 
 // Queries -> zero-padded rows (dpad columns), normalized for cosine; squared norm, and the SIMT
 // screen's error bound eps[q] (the tensor-core screen overwrites eps with its own bound).
-// Raises *nonfinite (when given) if a query holds NaN or infinity: the reference rejects such
-// queries (src/flat_index.cc:131), and checking here, where the queries are read anyway, keeps the
-// host from scanning the batch before each search.
+// A query holding NaN or infinity is marked in qbad[q] and counted in *nonfinite: the reference
+// rejects such queries (src/flat_index.cc:131). Checking here, where the queries are read anyway,
+// keeps the host from scanning the batch before each search; the finalize gives such a query
+// no results (QV_INVALID_LABEL with a NaN distance) and the host-buffer entry point raises.
 __global__ void prep_queries_kernel(const float* q, size_t nq, int dim, int dpad, bool cosine,
                                     bool l2, EpsModel em, float xmax, float* qp, float* qnorm2,
-                                    float* eps, int* nonfinite) {
+                                    float* eps, int* qbad, int* nonfinite) {
   const int lane = threadIdx.x & 31;
   const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= nq) return;
@@ -116,7 +117,11 @@ __global__ void prep_queries_kernel(const float* q, size_t nq, int dim, int dpad
     bad |= (__float_as_uint(v) & 0x7f800000u) == 0x7f800000u;
     out[i] = v;
   }
-  if (nonfinite != nullptr && __any_sync(kFull, bad) && lane == 0) atomicOr(nonfinite, 1);
+  bad = __any_sync(kFull, bad);
+  if (lane == 0) {
+    qbad[row] = bad ? 1 : 0;
+    if (bad) atomicAdd(nonfinite, 1);
+  }
   __syncwarp();
   if (cosine) warp_normalize(out, dim, lane);
   float s = 0.0f;
@@ -131,6 +136,35 @@ __global__ void prep_queries_kernel(const float* q, size_t nq, int dim, int dpad
     } else {
       eps[row] = em.c_ip * qn * xmax + em.c_abs * (1.0f + qn * xmax);
     }
+  }
+}
+
+// The result slot of a query that holds NaN or infinity: no label, NaN distance.
+__device__ __forceinline__ void write_invalid(uint64_t* labels, float* dists, uint64_t* keys,
+                                              size_t o) {
+  labels[o] = kInvalidLabel;
+  dists[o] = __int_as_float(0x7fc00000);
+  if (keys) keys[o] = ~0ull;
+}
+
+// Results of a search over an empty index: every slot unfilled (QV_INVALID_LABEL, +inf), or
+// invalid (NaN distance) for a query holding NaN or infinity, which is also counted. One warp
+// per query.
+__global__ void empty_results_kernel(const float* q, size_t nq, int dim, int k, uint64_t* labels,
+                                     float* dists, uint64_t* keys, int* nonfinite) {
+  const int lane = threadIdx.x & 31;
+  const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= nq) return;
+  bool bad = false;
+  for (int i = lane; i < dim; i += 32)
+    bad |= (__float_as_uint(q[row * dim + i]) & 0x7f800000u) == 0x7f800000u;
+  bad = __any_sync(kFull, bad);
+  if (bad && lane == 0) atomicAdd(nonfinite, 1);
+  for (int j = lane; j < k; j += 32) {
+    const size_t o = row * k + j;
+    labels[o] = kInvalidLabel;
+    dists[o] = bad ? __int_as_float(0x7fc00000) : kInf;
+    if (keys) keys[o] = ~0ull;
   }
 }
 
@@ -296,14 +330,19 @@ __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
     bool l2, const float* __restrict__ cand_d,
     const uint32_t* __restrict__ cand_r, const int* __restrict__ cand_n, int n_chunks, int kk,
     int group_rows, int pool, int k, uint64_t* __restrict__ out_labels, float* __restrict__ out_d,
-    uint64_t* __restrict__ out_keys, int* __restrict__ fail_count, int* __restrict__ fail_q,
-    float* __restrict__ fail_dk) {
+    uint64_t* __restrict__ out_keys, const int* __restrict__ qbad, int* __restrict__ fail_count,
+    int* __restrict__ fail_q, float* __restrict__ fail_dk, int* __restrict__ flags) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* sd = reinterpret_cast<float*>(smem_raw);               // pool
   uint64_t* sk = reinterpret_cast<uint64_t*>(sd + pool);        // pool (8-byte aligned: pool%2==0)
   __shared__ int s_total;
   const int q = blockIdx.x;
   if (q >= nq) return;
+  if (qbad[q]) {  // NaN or infinity in the query: no results
+    for (int j = threadIdx.x; j < k; j += blockDim.x)
+      write_invalid(out_labels, out_d, out_keys, static_cast<size_t>(q) * k + j);
+    return;
+  }
   if (threadIdx.x == 0) {
     int tot = 0;
     for (int c = 0; c < n_chunks; ++c) tot += cand_n[static_cast<size_t>(q) * n_chunks + c];
@@ -382,6 +421,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
       const int slot = atomicAdd(fail_count, 1);
       fail_q[slot] = q;
       fail_dk[slot] = dk;
+      atomicAdd(flags + kFlagRescanned, 1);
     }
   }
   for (int j = threadIdx.x; j < k; j += blockDim.x) {
@@ -502,7 +542,9 @@ __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_gro
     const float* __restrict__ cand_d, const uint32_t* __restrict__ cand_r,
     const int* __restrict__ cand_n, int n_chunks, int kk, int group_rows, int k,
     uint64_t* __restrict__ out_labels, float* __restrict__ out_d, uint64_t* __restrict__ out_keys,
-    int* __restrict__ fail_count, int* __restrict__ fail_q, float* __restrict__ fail_dk) {
+    const int* __restrict__ qbad, const int* __restrict__ screen_err,
+    int* __restrict__ fail_count, int* __restrict__ fail_q, float* __restrict__ fail_dk,
+    int* __restrict__ flags) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q = blockIdx.x * kGroupFinalizeWarps + warp;
@@ -520,6 +562,15 @@ __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_gro
   float* ed = sv + kk;
   uint64_t* er = reinterpret_cast<uint64_t*>(ed + nx);  // 8-byte aligned: offsets are even words
   if (q >= nq) return;
+  // A screen that gave up waiting on a pipeline barrier left its candidates incomplete: every
+  // query then fails the certificate and is answered by the exact rescan.
+  const bool aborted = *screen_err != 0;
+  if (aborted && q == 0 && lane == 0) atomicAdd(flags + kFlagTimeout, 1);
+  if (qbad[q]) {  // NaN or infinity in the query: no results
+    for (int j = lane; j < k; j += 32)
+      write_invalid(out_labels, out_d, out_keys, static_cast<size_t>(q) * k + j);
+    return;
+  }
   const float* qrow = qp + static_cast<size_t>(q) * dpad;
   for (int i = lane; i < dpad; i += 32) sq[i] = qrow[i];
   int total = 0;
@@ -682,12 +733,13 @@ __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_gro
     __syncwarp();
   }
   if (lane == 0) {
-    bool ok = true;
-    if (total >= kk) ok = (T - eps_q[q]) >= dk;
+    bool ok = !aborted;
+    if (ok && total >= kk) ok = (T - eps_q[q]) >= dk;
     if (!ok) {
       const int slot = atomicAdd(fail_count, 1);
       fail_q[slot] = q;
       fail_dk[slot] = dk;
+      atomicAdd(flags + kFlagRescanned, 1);
     }
   }
 }
@@ -766,12 +818,6 @@ __global__ void __launch_bounds__(256) flat_rescan_kernel(
       }
     }
   }
-}
-
-__global__ void fill_u32_kernel(unsigned* p, size_t n, unsigned v) {
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x)
-    p[i] = v;
 }
 
 int env_int(const char* name, int dflt) {
@@ -860,145 +906,171 @@ static int choose_chunks(size_t nrows, int n_qtiles, int max_chunks, int grid, i
   return static_cast<int>(ceil_div(nrows, static_cast<size_t>(*chunk_rows)));
 }
 
-void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k,
-                 const uint64_t* d_bitmap, uint64_t* d_labels, float* d_dists, uint64_t* d_keys,
-                 cudaStream_t st) {
-  if (nq == 0 || k == 0) return;
-  QV_REQUIRE(k <= 1024, "k > 1024 is not supported by the GPU FlatIndex");
-  const int dim = static_cast<int>(s.dim);
-  const int dpad = static_cast<int>(ceil_div(s.dim, 32) * 32);
+// Sizes and layout of one search's temporaries, carved from one device block (offsets in bytes,
+// each 256-byte aligned).
+struct FlatPlan {
+  bool tensor = false;
+  int dim = 0, dpad = 0, kk = 0, n_qtiles = 0, n_chunks = 0, qpb = 0, group_rows = 1;
+  int64_t chunk_rows = 0;
+  size_t slots = 0;
+  size_t qp = 0, qn2 = 0, eps = 0, qbad = 0, fail = 0, cand_d = 0, cand_r = 0, cand_n = 0,
+         thr = 0, tc = 0, flags = 0, total = 0;
+};
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
+
+// allow_tensor: the tensor-core screen may be used (the allocation-free entry point screens on
+// the CUDA cores only); own_flags: the block also holds the kSearchFlagWords report words.
+static FlatPlan plan_search(const FlatState& s, size_t nq, size_t k, bool allow_tensor,
+                            bool own_flags) {
+  FlatPlan P;
+  P.dim = static_cast<int>(s.dim);
+  P.dpad = static_cast<int>(ceil_div(s.dim, 32) * 32);
+  const int nsm = sm_count(s.device);
+  // QV_FLAT_KK overrides the candidate budget of the SIMT screen (any value >= k); small budgets
+  // exercise the exact rescan. QV_FLAT_SCREEN=simt selects the SIMT screen.
+  const int forced_kk = env_int("QV_FLAT_KK", 0);
+  P.tensor = allow_tensor && forced_kk == 0 && flat_tc_eligible(s, k);
+  const size_t nrows = std::max<size_t>(s.n, 1);
+  if (P.tensor) {
+    P.kk = flat_tc_kk(k);
+    P.n_qtiles = static_cast<int>(ceil_div(nq, 256));  // work units cover query groups of 2 x 128
+    P.n_chunks = choose_chunks(nrows, P.n_qtiles, std::max(1, kMaxCandidatesPerQuery / P.kk),
+                               nsm, 128, &P.chunk_rows);
+    P.group_rows = kTcGroupRows;
+  } else {
+    P.kk = static_cast<int>(next_pow2(k + std::max<size_t>(8, k / 4)));
+    if (forced_kk > 0) P.kk = std::max<int>(static_cast<int>(k), forced_kk);
+    const int heap_budget = 64 * 1024;
+    P.qpb = std::min<int>(128, heap_budget / (P.kk * 8));
+    if (P.qpb >= 32) P.qpb = P.qpb / 32 * 32;
+    P.qpb = std::max(1, P.qpb);
+    P.n_qtiles = static_cast<int>(ceil_div(nq, P.qpb));
+    P.n_chunks = choose_chunks(nrows, P.n_qtiles, std::max(1, kMaxCandidatesPerQuery / P.kk),
+                               3 * nsm, kScreenRows, &P.chunk_rows);
+    P.group_rows = 1;
+  }
+  P.slots = nq * static_cast<size_t>(P.n_chunks);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = align256(off + bytes);
+    return at;
+  };
+  P.qp = take(nq * P.dpad * sizeof(float));
+  P.qn2 = take(nq * sizeof(float));
+  P.eps = take(nq * sizeof(float));
+  P.qbad = take(nq * sizeof(int));
+  P.fail = take(2 * sizeof(int) + nq * (sizeof(int) + sizeof(float)));
+  P.cand_d = take(P.slots * P.kk * sizeof(float));
+  P.cand_r = take(P.slots * P.kk * sizeof(uint32_t));
+  P.cand_n = take(P.slots * sizeof(int));
+  P.thr = take(nq * sizeof(unsigned));
+  if (P.tensor) P.tc = take(flat_tc_scratch_bytes(s, nq, P.kk));
+  if (own_flags) P.flags = take(kSearchFlagWords * sizeof(int));
+  P.total = off;
+  return P;
+}
+
+// Resets what every search's temporaries must start from: no candidates per (query, chunk),
+// +inf thresholds, the rescan list's count and the screen's error word, and (when given) the
+// report words.
+__global__ void init_search_kernel(int* cand_n, size_t slots, unsigned* thr, size_t nq,
+                                   int* fail_hdr, int* flags) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const size_t i0 = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  for (size_t i = i0; i < slots; i += stride) cand_n[i] = 0;
+  for (size_t i = i0; i < nq; i += stride) thr[i] = 0xff800000u;  // ordered bits of +inf
+  if (i0 < 2) fail_hdr[i0] = 0;
+  if (flags != nullptr && i0 < kSearchFlagWords) flags[i0] = 0;
+}
+
+// The whole search on stream `st`, temporaries at `base` (plan P). No host synchronization.
+static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* base,
+                       const float* d_queries, size_t nq, size_t k, const uint64_t* d_bitmap,
+                       uint64_t* d_labels, float* d_dists, uint64_t* d_keys, int* d_flags,
+                       cudaStream_t st) {
+  const int dim = P.dim, dpad = P.dpad, kk = P.kk;
   const bool l2 = s.metric == QV_METRIC_L2;
   const int nsm = sm_count(s.device);
+  float* qp = reinterpret_cast<float*>(base + P.qp);
+  float* qn2 = reinterpret_cast<float*>(base + P.qn2);
+  float* eps = reinterpret_cast<float*>(base + P.eps);
+  int* qbad = reinterpret_cast<int*>(base + P.qbad);
+  int* fail_count = reinterpret_cast<int*>(base + P.fail);
+  int* screen_err = fail_count + 1;
+  int* fail_q = fail_count + 2;
+  float* fail_dk = reinterpret_cast<float*>(fail_q + nq);
+  float* cand_d = reinterpret_cast<float*>(base + P.cand_d);
+  uint32_t* cand_r = reinterpret_cast<uint32_t*>(base + P.cand_r);
+  int* cand_n = reinterpret_cast<int*>(base + P.cand_n);
+  unsigned* thr = reinterpret_cast<unsigned*>(base + P.thr);
 
-  if (s.n == 0) {  // nothing stored: every slot unfilled
-    std::vector<float> inf(nq * k, INFINITY);
-    std::vector<uint64_t> inv(nq * k, kInvalidLabel);
-    QV_CUDA(cudaMemcpyAsync(d_dists, inf.data(), nq * k * sizeof(float), cudaMemcpyHostToDevice, st));
-    QV_CUDA(cudaMemcpyAsync(d_labels, inv.data(), nq * k * sizeof(uint64_t), cudaMemcpyHostToDevice, st));
-    if (d_keys)
-      QV_CUDA(cudaMemcpyAsync(d_keys, inv.data(), nq * k * sizeof(uint64_t), cudaMemcpyHostToDevice, st));
-    QV_CUDA(cudaStreamSynchronize(st));
-    return;
-  }
-
+  init_search_kernel<<<static_cast<unsigned>(std::min<size_t>(
+                           ceil_div(std::max(P.slots, nq), 256), 4 * static_cast<size_t>(nsm))),
+                       256, 0, st>>>(cand_n, P.slots, thr, nq, fail_count,
+                                     P.flags ? d_flags : nullptr);
+  check_launch("init_search_kernel");
   const double u = std::ldexp(1.0, -24);
   const double gamma = (dim + 2) * u / (1.0 - (dim + 2) * u);
   EpsModel em;
   em.c_l2 = static_cast<float>(2.0 * (2.0 * gamma + 4.0 * u));
   em.c_ip = static_cast<float>(2.0 * (2.0 * gamma));
   em.c_abs = static_cast<float>(2.0 * (2.0 * u));
-  DeviceBuffer qp(nq * dpad * sizeof(float), st), qn2(nq * sizeof(float), st),
-      eps(nq * sizeof(float), st);
-  // [0] queries that were rescanned, [1] non-finite query flag, then the rescan list.
-  DeviceBuffer fail(2 * sizeof(int) + nq * (sizeof(int) + sizeof(float)), st);
-  int* fail_count = fail.get<int>();
-  int* nonfinite = fail_count + 1;
-  int* fail_q = fail_count + 2;
-  float* fail_dk = reinterpret_cast<float*>(fail_q + nq);
-  QV_CUDA(cudaMemsetAsync(fail_count, 0, 2 * sizeof(int), st));
   prep_queries_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(d_queries, nq, dim, dpad,
                                                        s.metric == QV_METRIC_COSINE, l2, em,
-                                                       s.max_norm, qp.get<float>(),
-                                                       qn2.get<float>(), eps.get<float>(),
-                                                       nonfinite);
+                                                       s.max_norm, qp, qn2, eps, qbad,
+                                                       d_flags + kFlagNonFinite);
   check_launch("prep_queries_kernel");
 
-  // QV_FLAT_KK overrides the candidate budget of the SIMT screen (any value >= k); small budgets
-  // exercise the exact rescan. QV_FLAT_SCREEN=simt selects the SIMT screen.
-  const int forced_kk = env_int("QV_FLAT_KK", 0);
-  const bool tensor = forced_kk == 0 && flat_tc_eligible(s, k);
-  int kk, n_qtiles, n_chunks, qpb = 0;
-  int64_t chunk_rows = 0;
-  if (tensor) {
-    kk = flat_tc_kk(k);
-    n_qtiles = static_cast<int>(ceil_div(nq, 256));  // work units cover query groups of 2 x 128
-    n_chunks = choose_chunks(s.n, n_qtiles, std::max(1, kMaxCandidatesPerQuery / kk), nsm, 128,
-                             &chunk_rows);
-  } else {
-    kk = static_cast<int>(next_pow2(k + std::max<size_t>(8, k / 4)));
-    if (forced_kk > 0) kk = std::max<int>(static_cast<int>(k), forced_kk);
-    const int heap_budget = 64 * 1024;
-    qpb = std::min<int>(128, heap_budget / (kk * 8));
-    if (qpb >= 32) qpb = qpb / 32 * 32;
-    qpb = std::max(1, qpb);
-    n_qtiles = static_cast<int>(ceil_div(nq, qpb));
-    n_chunks = choose_chunks(s.n, n_qtiles, std::max(1, kMaxCandidatesPerQuery / kk), 3 * nsm,
-                             kScreenRows, &chunk_rows);
-  }
-
-  const size_t slots = nq * static_cast<size_t>(n_chunks);
-  DeviceBuffer cand_d(slots * kk * sizeof(float), st), cand_r(slots * kk * sizeof(uint32_t), st),
-      cand_n(slots * sizeof(int), st), thr(nq * sizeof(unsigned), st), err(sizeof(int), st);
-  QV_CUDA(cudaMemsetAsync(cand_n.get(), 0, slots * sizeof(int), st));
-  QV_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
-  fill_u32_kernel<<<std::min<size_t>(ceil_div(nq, 256), 1024), 256, 0, st>>>(
-      thr.get<unsigned>(), nq, 0xff800000u /* ordered bits of +inf */);
-  check_launch("fill_u32_kernel");
-
-  if (tensor) {
+  if (P.tensor) {
     {
       FlatState& ms = const_cast<FlatState&>(s);  // the fp16 copy is a cache of the rows
       std::lock_guard<std::mutex> lock(ms.x16_mu);
       flat_tc_prepare(ms, st);
     }
-    flat_screen_tc(s, qp.get<float>(), dpad, nq, d_bitmap, n_chunks, chunk_rows, kk,
-                   cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(),
-                   thr.get<unsigned>(), eps.get<float>(), err.get<int>(), st);
+    flat_screen_tc(s, qp, dpad, nq, d_bitmap, P.n_chunks, P.chunk_rows, kk, cand_d, cand_r,
+                   cand_n, thr, eps, screen_err, base + P.tc, st);
   } else {
     const size_t smem = kScreenRows * kScreenDChunk * sizeof(float) +
-                        static_cast<size_t>(kk) * qpb * (sizeof(float) + sizeof(uint32_t));
-    const dim3 grid(static_cast<unsigned>(n_qtiles * n_chunks));
+                        static_cast<size_t>(kk) * P.qpb * (sizeof(float) + sizeof(uint32_t));
+    const dim3 grid(static_cast<unsigned>(P.n_qtiles * P.n_chunks));
     KernelTimer timer(st, "flat_screen_simt_kernel", 2.0 * nq * static_cast<double>(s.n) * dim,
                       false);
-    if (l2) {
-      QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<true>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      flat_screen_simt_kernel<true><<<grid, 128, smem, st>>>(
-          qp.get<float>(), dpad, qn2.get<float>(), static_cast<int>(nq), qpb, s.x.get<float>(),
-          dim, s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, chunk_rows, n_qtiles,
-          n_chunks, kk, cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(),
-          thr.get<unsigned>());
-    } else {
-      QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<false>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      flat_screen_simt_kernel<false><<<grid, 128, smem, st>>>(
-          qp.get<float>(), dpad, qn2.get<float>(), static_cast<int>(nq), qpb, s.x.get<float>(),
-          dim, s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, chunk_rows, n_qtiles,
-          n_chunks, kk, cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(),
-          thr.get<unsigned>());
-    }
+    auto kernel = l2 ? flat_screen_simt_kernel<true> : flat_screen_simt_kernel<false>;
+    QV_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kernel<<<grid, 128, smem, st>>>(qp, dpad, qn2, static_cast<int>(nq), P.qpb, s.x.get<float>(),
+                                    dim, s.xnorm2.get<float>(), static_cast<int64_t>(s.n),
+                                    d_bitmap, P.chunk_rows, P.n_qtiles, P.n_chunks, kk, cand_d,
+                                    cand_r, cand_n, thr);
     timer.stop();
     check_launch("flat_screen_simt_kernel");
-    QV_CUDA(cudaStreamSynchronize(st));
-    timer.finish();
   }
 
-  // The tensor-core screen keeps 8-row groups; the finalize expands the kk best into rows.
-  const int group_rows = tensor ? kTcGroupRows : 1;
-  const int pool = static_cast<int>(std::max(next_pow2(static_cast<size_t>(n_chunks) * kk),
-                                             next_pow2(static_cast<size_t>(kk) * group_rows)));
-  if (tensor) {
-    QV_REQUIRE(n_chunks <= 64, "group finalize: more than 64 row chunks");
+  if (P.tensor) {
+    // The tensor-core screen keeps 8-row groups; the finalize expands the kk best into rows.
+    QV_REQUIRE(P.n_chunks <= 64, "group finalize: more than 64 row chunks");
     const size_t gsmem =
-        kGroupFinalizeWarps * group_finalize_bytes_per_warp(dpad, n_chunks, kk, group_rows);
+        kGroupFinalizeWarps * group_finalize_bytes_per_warp(dpad, P.n_chunks, kk, P.group_rows);
     QV_CUDA(cudaFuncSetAttribute(flat_finalize_groups_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsmem));
     flat_finalize_groups_kernel<<<static_cast<unsigned>(ceil_div(nq, kGroupFinalizeWarps)),
                                   32 * kGroupFinalizeWarps, gsmem, st>>>(
-        qp.get<float>(), dpad, eps.get<float>(), static_cast<int>(nq), s.x.get<float>(), dim,
-        static_cast<int64_t>(s.n), d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2,
-        cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(), n_chunks, kk, group_rows,
-        static_cast<int>(k), d_labels, d_dists, d_keys, fail_count, fail_q, fail_dk);
+        qp, dpad, eps, static_cast<int>(nq), s.x.get<float>(), dim, static_cast<int64_t>(s.n),
+        d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, cand_d, cand_r, cand_n, P.n_chunks,
+        kk, P.group_rows, static_cast<int>(k), d_labels, d_dists, d_keys, qbad, screen_err,
+        fail_count, fail_q, fail_dk, d_flags);
     check_launch("flat_finalize_groups_kernel");
   } else {
+    const int pool = static_cast<int>(next_pow2(static_cast<size_t>(P.n_chunks) * kk));
     const size_t fsmem = pool * (sizeof(float) + sizeof(uint64_t));
     QV_CUDA(cudaFuncSetAttribute(flat_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)fsmem));
     flat_finalize_kernel<<<static_cast<unsigned>(nq), kFinalizeThreads, fsmem, st>>>(
-        qp.get<float>(), dpad, eps.get<float>(), static_cast<int>(nq), s.x.get<float>(), dim,
-        static_cast<int64_t>(s.n), d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2,
-        cand_d.get<float>(), cand_r.get<uint32_t>(), cand_n.get<int>(), n_chunks, kk, group_rows,
-        pool, static_cast<int>(k), d_labels, d_dists, d_keys, fail_count, fail_q, fail_dk);
+        qp, dpad, eps, static_cast<int>(nq), s.x.get<float>(), dim, static_cast<int64_t>(s.n),
+        d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, cand_d, cand_r, cand_n, P.n_chunks,
+        kk, 1, pool, static_cast<int>(k), d_labels, d_dists, d_keys, qbad, fail_count, fail_q,
+        fail_dk, d_flags);
     check_launch("flat_finalize_kernel");
   }
 
@@ -1007,15 +1079,30 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
   QV_CUDA(cudaFuncSetAttribute(flat_rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)rsmem));
   flat_rescan_kernel<<<static_cast<unsigned>(std::min<size_t>(nq, 2 * nsm)), 256, rsmem, st>>>(
-      qp.get<float>(), dpad, s.x.get<float>(), dim, static_cast<int64_t>(s.n),
-      s.labels.get<uint64_t>(), d_bitmap, s.row_offset, l2, static_cast<int>(k), cap, fail_count,
-      fail_q, fail_dk, d_labels, d_dists, d_keys);
+      qp, dpad, s.x.get<float>(), dim, static_cast<int64_t>(s.n), s.labels.get<uint64_t>(),
+      d_bitmap, s.row_offset, l2, static_cast<int>(k), cap, fail_count, fail_q, fail_dk, d_labels,
+      d_dists, d_keys);
   check_launch("flat_rescan_kernel");
-  int flags[2] = {0, 0};
-  QV_CUDA(cudaMemcpyAsync(flags, fail_count, sizeof(flags), cudaMemcpyDeviceToHost, st));
-  QV_CUDA(cudaStreamSynchronize(st));
-  QV_REQUIRE(flags[1] == 0, "vectors must not contain NaN or infinity");
-  thread_stats().rescanned_queries += static_cast<uint64_t>(flags[0]);
+}
+
+void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k,
+                 const uint64_t* d_bitmap, uint64_t* d_labels, float* d_dists, uint64_t* d_keys,
+                 int* d_flags, cudaStream_t st) {
+  if (nq == 0 || k == 0) return;
+  QV_REQUIRE(k <= 1024, "k > 1024 is not supported by the GPU FlatIndex");
+  if (s.n == 0) {  // nothing stored: every slot unfilled
+    empty_results_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(d_queries, nq, static_cast<int>(s.dim),
+                                                          static_cast<int>(k), d_labels, d_dists,
+                                                          d_keys, d_flags + kFlagNonFinite);
+    check_launch("empty_results_kernel");
+    return;
+  }
+  const FlatPlan P = plan_search(s, nq, k, /*allow_tensor=*/true, /*own_flags=*/false);
+  // One stream-ordered block for every temporary (returned to the device's memory pool, which
+  // keeps it for the next search, when the work queued before the free has run).
+  DeviceBuffer arena(P.total, st);
+  run_search(s, P, arena.get<unsigned char>(), d_queries, nq, k, d_bitmap, d_labels, d_dists,
+             d_keys, d_flags, st);
 }
 
 // ---- allocation-free search ------------------------------------------------------------------------
@@ -1029,53 +1116,6 @@ void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k
 constexpr size_t kNoAllocScratchBytes = size_t{64} << 20;  // per device, held until exit
 constexpr int kNoAllocMaxDevices = 64;
 
-struct NoAllocLayout {
-  size_t qp, qn2, eps, cand_d, cand_r, cand_n, thr, fail, total;
-  int dpad, kk, qpb, n_qtiles, n_chunks;
-  int64_t chunk_rows;
-};
-
-static size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
-
-static NoAllocLayout noalloc_layout(const FlatState& s, size_t nq, size_t k) {
-  NoAllocLayout L{};
-  L.dpad = static_cast<int>(ceil_div(s.dim, 32) * 32);
-  L.kk = static_cast<int>(next_pow2(k + std::max<size_t>(8, k / 4)));
-  L.qpb = std::min<int>(128, (64 * 1024) / (L.kk * 8));
-  if (L.qpb >= 32) L.qpb = L.qpb / 32 * 32;
-  L.qpb = std::max(1, L.qpb);
-  L.n_qtiles = static_cast<int>(ceil_div(nq, L.qpb));
-  L.n_chunks = choose_chunks(std::max<size_t>(s.n, 1), L.n_qtiles,
-                             std::max(1, kMaxCandidatesPerQuery / L.kk), 3 * sm_count(s.device),
-                             kScreenRows, &L.chunk_rows);
-  const size_t slots = nq * static_cast<size_t>(L.n_chunks);
-  size_t off = 0;
-  auto take = [&](size_t bytes) {
-    const size_t at = off;
-    off = align256(off + bytes);
-    return at;
-  };
-  L.qp = take(nq * L.dpad * sizeof(float));
-  L.qn2 = take(nq * sizeof(float));
-  L.eps = take(nq * sizeof(float));
-  L.cand_d = take(slots * L.kk * sizeof(float));
-  L.cand_r = take(slots * L.kk * sizeof(uint32_t));
-  L.cand_n = take(slots * sizeof(int));
-  L.thr = take(nq * sizeof(unsigned));
-  L.fail = take(sizeof(int) + nq * (sizeof(int) + sizeof(float)));
-  L.total = off;
-  return L;
-}
-
-__global__ void fill_unfilled_kernel(uint64_t* labels, float* dists, uint64_t* keys, size_t n) {
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    labels[i] = kInvalidLabel;
-    dists[i] = __int_as_float(0x7f800000);
-    if (keys) keys[i] = ~0ull;
-  }
-}
-
 }  // namespace qv
 
 // The scratch itself. In host code this name is only a handle for cudaGetSymbolAddress.
@@ -1084,6 +1124,8 @@ static __device__ __align__(256) unsigned char g_flat_noalloc_scratch[qv::kNoAll
 namespace qv {
 
 // Device address of the scratch on `device` (which must be current), resolved once per device.
+// The address is cached for the life of the process: a device reset after the first call would
+// leave it stale, so a process that uses this entry point must not reset that device.
 static unsigned char* noalloc_scratch(int device) {
   static std::mutex mu;
   static void* addr[kNoAllocMaxDevices] = {};
@@ -1101,95 +1143,33 @@ static unsigned char* noalloc_scratch(int device) {
 
 size_t flat_noalloc_max_bytes() { return kNoAllocScratchBytes; }
 
+// The same search as flat_search, screened on the CUDA cores, with every temporary (the report
+// words included) carved from the fixed scratch. Results equal flat_search's, also for queries
+// holding NaN or infinity (QV_INVALID_LABEL with a NaN distance).
 void flat_search_noalloc(const FlatState& s, const float* d_queries, size_t nq, size_t k,
                          const uint64_t* d_bitmap, uint64_t* d_labels, float* d_dists,
                          uint64_t* d_keys, cudaStream_t st) {
   if (nq == 0 || k == 0) return;
   QV_REQUIRE(k <= 1024, "k > 1024 is not supported by the GPU FlatIndex");
-  const NoAllocLayout L = noalloc_layout(s, nq, k);
-  if (L.total > kNoAllocScratchBytes)
-    fail(QV_ERR_INVALID, "allocation-free search needs " + std::to_string(L.total) +
+  const FlatPlan P = plan_search(s, nq, k, /*allow_tensor=*/false, /*own_flags=*/true);
+  if (P.total > kNoAllocScratchBytes)
+    fail(QV_ERR_INVALID, "allocation-free search needs " + std::to_string(P.total) +
                              " bytes of scratch for nq=" + std::to_string(nq) +
                              ", k=" + std::to_string(k) + "; its fixed scratch holds " +
                              std::to_string(kNoAllocScratchBytes) + " bytes (search fewer queries "
                              "per call)");
   unsigned char* base = noalloc_scratch(s.device);
+  int* flags = reinterpret_cast<int*>(base + P.flags);
   if (s.n == 0) {
-    fill_unfilled_kernel<<<std::min<size_t>(ceil_div(nq * k, 256), 4096), 256, 0, st>>>(
-        d_labels, d_dists, d_keys, nq * k);
-    check_launch("fill_unfilled_kernel");
+    empty_results_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(d_queries, nq, static_cast<int>(s.dim),
+                                                          static_cast<int>(k), d_labels, d_dists,
+                                                          d_keys, flags + kFlagNonFinite);
+    check_launch("empty_results_kernel");
     return;
   }
-  const int dim = static_cast<int>(s.dim);
-  const bool l2 = s.metric == QV_METRIC_L2;
-  float* qp = reinterpret_cast<float*>(base + L.qp);
-  float* qn2 = reinterpret_cast<float*>(base + L.qn2);
-  float* eps = reinterpret_cast<float*>(base + L.eps);
-  float* cand_d = reinterpret_cast<float*>(base + L.cand_d);
-  uint32_t* cand_r = reinterpret_cast<uint32_t*>(base + L.cand_r);
-  int* cand_n = reinterpret_cast<int*>(base + L.cand_n);
-  unsigned* thr = reinterpret_cast<unsigned*>(base + L.thr);
-  int* fail_count = reinterpret_cast<int*>(base + L.fail);
-  int* fail_q = fail_count + 1;
-  float* fail_dk = reinterpret_cast<float*>(fail_q + nq);
-  const size_t slots = nq * static_cast<size_t>(L.n_chunks);
-
-  const double u = std::ldexp(1.0, -24);
-  const double gamma = (dim + 2) * u / (1.0 - (dim + 2) * u);
-  EpsModel em;
-  em.c_l2 = static_cast<float>(2.0 * (2.0 * gamma + 4.0 * u));
-  em.c_ip = static_cast<float>(2.0 * (2.0 * gamma));
-  em.c_abs = static_cast<float>(2.0 * (2.0 * u));
-  prep_queries_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(d_queries, nq, dim, L.dpad,
-                                                       s.metric == QV_METRIC_COSINE, l2, em,
-                                                       s.max_norm, qp, qn2, eps, nullptr);
-  check_launch("prep_queries_kernel");
-  // The scratch keeps the previous call's contents: reset what must start empty.
-  QV_CUDA(cudaMemsetAsync(cand_n, 0, slots * sizeof(int), st));
-  QV_CUDA(cudaMemsetAsync(fail_count, 0, sizeof(int), st));
-  fill_u32_kernel<<<std::min<size_t>(ceil_div(nq, 256), 1024), 256, 0, st>>>(thr, nq,
-                                                                             0xff800000u);
-  check_launch("fill_u32_kernel");
-
-  const size_t smem = kScreenRows * kScreenDChunk * sizeof(float) +
-                      static_cast<size_t>(L.kk) * L.qpb * (sizeof(float) + sizeof(uint32_t));
-  const dim3 grid(static_cast<unsigned>(L.n_qtiles * L.n_chunks));
-  if (l2) {
-    QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<true>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    flat_screen_simt_kernel<true><<<grid, 128, smem, st>>>(
-        qp, L.dpad, qn2, static_cast<int>(nq), L.qpb, s.x.get<float>(), dim,
-        s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, L.chunk_rows, L.n_qtiles,
-        L.n_chunks, L.kk, cand_d, cand_r, cand_n, thr);
-  } else {
-    QV_CUDA(cudaFuncSetAttribute(flat_screen_simt_kernel<false>,
-                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    flat_screen_simt_kernel<false><<<grid, 128, smem, st>>>(
-        qp, L.dpad, qn2, static_cast<int>(nq), L.qpb, s.x.get<float>(), dim,
-        s.xnorm2.get<float>(), static_cast<int64_t>(s.n), d_bitmap, L.chunk_rows, L.n_qtiles,
-        L.n_chunks, L.kk, cand_d, cand_r, cand_n, thr);
-  }
-  check_launch("flat_screen_simt_kernel");
-  const int pool = static_cast<int>(next_pow2(static_cast<size_t>(L.n_chunks) * L.kk));
-  const size_t fsmem = pool * (sizeof(float) + sizeof(uint64_t));
-  QV_CUDA(cudaFuncSetAttribute(flat_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)fsmem));
-  flat_finalize_kernel<<<static_cast<unsigned>(nq), kFinalizeThreads, fsmem, st>>>(
-      qp, L.dpad, eps, static_cast<int>(nq), s.x.get<float>(), dim, static_cast<int64_t>(s.n),
-      d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, cand_d, cand_r, cand_n, L.n_chunks,
-      L.kk, 1, pool, static_cast<int>(k), d_labels, d_dists, d_keys, fail_count, fail_q,
-      fail_dk);
-  check_launch("flat_finalize_kernel");
-  const int cap = static_cast<int>(next_pow2(k + 256));
-  const size_t rsmem = cap * (sizeof(float) + sizeof(uint64_t));
-  QV_CUDA(cudaFuncSetAttribute(flat_rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)rsmem));
-  flat_rescan_kernel<<<static_cast<unsigned>(std::min<size_t>(nq, 2 * sm_count(s.device))), 256,
-                       rsmem, st>>>(qp, L.dpad, s.x.get<float>(), dim, static_cast<int64_t>(s.n),
-                                    s.labels.get<uint64_t>(), d_bitmap, s.row_offset, l2,
-                                    static_cast<int>(k), cap, fail_count, fail_q, fail_dk,
-                                    d_labels, d_dists, d_keys);
-  check_launch("flat_rescan_kernel");
+  // The scratch keeps the previous call's contents: run_search's first kernel resets what must
+  // start empty (the report words included).
+  run_search(s, P, base, d_queries, nq, k, d_bitmap, d_labels, d_dists, d_keys, flags, st);
 }
 
 }  // namespace qv

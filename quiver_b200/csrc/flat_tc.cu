@@ -726,9 +726,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-__global__ void fill_inf_kernel(float* p, size_t n) {
-  const size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
-  if (i < n) p[i] = __int_as_float(0x7f800000);
+// The query-wide best lists start at +inf, unlocked.
+__global__ void init_best_kernel(float* gbest, size_t n, int* glock, size_t nq) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const size_t i0 = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  for (size_t i = i0; i < n; i += stride) gbest[i] = __int_as_float(0x7f800000);
+  for (size_t i = i0; i < nq; i += stride) glock[i] = 0;
 }
 
 // ---- fp16 operands ---------------------------------------------------------------------------------
@@ -743,13 +746,15 @@ __device__ __forceinline__ float pow2_scale_for(float maxabs) {
   return ldexpf(1.0f, 13 - e);
 }
 
-// Rows -> fp16 (kpad columns, zero padded) with one scale for the whole index; max row error.
+// Rows -> fp16 (kpad columns, zero padded) with one scale for the whole index (from the max |x|
+// in stats[0]); max row error into stats[1].
 __global__ void rows_to_f16_kernel(const float* __restrict__ x, size_t n, int dim, int kpad,
-                                   float scale, __half* __restrict__ out,
-                                   unsigned* __restrict__ max_err_bits) {
+                                   __half* __restrict__ out, unsigned* __restrict__ stats) {
   const int lane = threadIdx.x & 31;
   const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= n) return;
+  unsigned* max_err_bits = stats + 1;
+  const float scale = pow2_scale_for(__uint_as_float(stats[0]));
   const float inv = 1.0f / scale;
   double e2 = 0.0;
   for (int c = lane; c < kpad; c += 32) {
@@ -773,15 +778,23 @@ __global__ void max_abs_kernel(const float* __restrict__ x, size_t total, unsign
 }
 
 // Queries (already normalized rows of qp, stride dpad) -> fp16 with a per-query power-of-two
-// scale; 1/(s_q s_x); and the screen's error bound eps[q] against the reference's distance.
-__global__ void queries_to_f16_kernel(const float* __restrict__ qp, int nq, int dim, int dpad,
-                                      int kpad, float x_scale, float x_err, float x_max_norm,
-                                      bool l2, float gamma, __half* __restrict__ q16,
-                                      float* __restrict__ qscale_inv, float* __restrict__ qnorm2,
-                                      float* __restrict__ eps) {
+// scale; 1/(s_q s_x); and the screen's error bound eps[q] against the reference's distance. Rows
+// nq .. nq_pad - 1 of q16 (padding up to whole query tiles) are zeroed. x_stats: the fp16 copy's
+// words (max |x|, max row error).
+__global__ void queries_to_f16_kernel(const float* __restrict__ qp, int nq, int nq_pad, int dim,
+                                      int dpad, int kpad, const unsigned* __restrict__ x_stats,
+                                      float x_max_norm, bool l2, float gamma,
+                                      __half* __restrict__ q16, float* __restrict__ qscale_inv,
+                                      float* __restrict__ qnorm2, float* __restrict__ eps) {
   const int lane = threadIdx.x & 31;
   const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (q >= nq) return;
+  if (q >= nq_pad) return;
+  if (q >= nq) {
+    for (int c = lane; c < kpad; c += 32) q16[static_cast<size_t>(q) * kpad + c] = __float2half_rn(0.0f);
+    return;
+  }
+  const float x_scale = pow2_scale_for(__uint_as_float(x_stats[0]));
+  const float x_err = __uint_as_float(x_stats[1]);
   const float* v = qp + static_cast<size_t>(q) * dpad;
   float mx = 0.0f;
   for (int c = lane; c < dim; c += 32) mx = fmaxf(mx, fabsf(v[c]));
@@ -874,40 +887,59 @@ bool flat_tc_eligible(const FlatState& s, size_t k) {
 // which tightens thresholds and shortens the finalize's re-rank.
 int flat_tc_kk(size_t k) { return k + 8 <= 24 ? 24 : tc::kMaxKK; }
 
-// Builds (once per set of rows) the fp16 copy of the index and its error statistics.
+// Builds (once per set of rows) the fp16 copy of the index and its error statistics, entirely on
+// the device: nothing here waits for the GPU. Searches on other streams wait for the copy through
+// the x16_ready event.
 void flat_tc_prepare(FlatState& s, cudaStream_t st) {
-  if (s.x16.bytes() != 0 && s.x16_rows == s.n) return;
+  if (s.x16.bytes() != 0 && s.x16_rows == s.n) {
+    QV_CUDA(cudaStreamWaitEvent(st, s.x16_ready, 0));
+    return;
+  }
   // At least one full 64-column swizzle atom, so a TMA box never extends past a row.
   const int kpad = static_cast<int>(std::max<size_t>(64, ceil_div(s.dim, 16) * 16));
-  DeviceBuffer bits(2 * sizeof(unsigned), st);
-  QV_CUDA(cudaMemsetAsync(bits.get(), 0, 2 * sizeof(unsigned), st));
-  tc::max_abs_kernel<<<std::min<size_t>(ceil_div(s.n * s.dim, 256), 4096), 256, 0, st>>>(
-      s.x.get<float>(), s.n * s.dim, bits.get<unsigned>());
-  check_launch("max_abs_kernel");
-  unsigned mb = 0;
-  QV_CUDA(cudaMemcpyAsync(&mb, bits.get(), sizeof(mb), cudaMemcpyDeviceToHost, st));
-  QV_CUDA(cudaStreamSynchronize(st));
-  float maxabs;
-  std::memcpy(&maxabs, &mb, sizeof(maxabs));
-  float scale = 1.0f;
-  if (maxabs > 0.0f) {
-    int e;
-    std::frexp(maxabs, &e);
-    if (e < -7 || e > 14) scale = std::ldexp(1.0f, 13 - e);
-  }
+  if (s.x16_ready == nullptr) QV_CUDA(cudaEventCreateWithFlags(&s.x16_ready, cudaEventDisableTiming));
+  if (s.x16_stats.bytes() == 0) s.x16_stats.allocate(2 * sizeof(unsigned));
   s.x16.allocate(s.n * kpad * sizeof(__half));
+  QV_CUDA(cudaMemsetAsync(s.x16_stats.get(), 0, 2 * sizeof(unsigned), st));
+  tc::max_abs_kernel<<<std::min<size_t>(ceil_div(s.n * s.dim, 256), 4096), 256, 0, st>>>(
+      s.x.get<float>(), s.n * s.dim, s.x16_stats.get<unsigned>());
+  check_launch("max_abs_kernel");
   tc::rows_to_f16_kernel<<<ceil_div(s.n, 8), 256, 0, st>>>(s.x.get<float>(), s.n,
-                                                          static_cast<int>(s.dim), kpad, scale,
+                                                          static_cast<int>(s.dim), kpad,
                                                           s.x16.get<__half>(),
-                                                          bits.get<unsigned>() + 1);
+                                                          s.x16_stats.get<unsigned>());
   check_launch("rows_to_f16_kernel");
-  unsigned eb = 0;
-  QV_CUDA(cudaMemcpyAsync(&eb, bits.get<unsigned>() + 1, sizeof(eb), cudaMemcpyDeviceToHost, st));
-  QV_CUDA(cudaStreamSynchronize(st));
-  std::memcpy(&s.x16_err, &eb, sizeof(float));
-  s.x16_scale = scale;
+  QV_CUDA(cudaEventRecord(s.x16_ready, st));
   s.kpad = static_cast<size_t>(kpad);
   s.x16_rows = s.n;
+}
+
+// Scratch layout of one tensor-core screen (offsets into the block flat_tc_scratch_bytes sizes).
+struct TcScratch {
+  size_t q16, qinv, qn2, gbest, glock, total;
+};
+static TcScratch tc_scratch_layout(size_t kpad, size_t nq, int kk) {
+  const size_t group_rows = static_cast<size_t>(tc::kTiles) * tc::kM;
+  const size_t nq_pad = ceil_div(nq, group_rows) * group_rows;
+  TcScratch L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = (off + bytes + 255) & ~size_t{255};
+    return at;
+  };
+  L.q16 = take(nq_pad * kpad * sizeof(__half));
+  L.qinv = take(nq * sizeof(float));
+  L.qn2 = take(nq * sizeof(float));
+  L.gbest = take(nq * static_cast<size_t>(kk) * sizeof(float));
+  L.glock = take(nq * sizeof(int));
+  L.total = off;
+  return L;
+}
+
+size_t flat_tc_scratch_bytes(const FlatState& s, size_t nq, int kk) {
+  const size_t kpad = std::max<size_t>(64, ceil_div(s.dim, 16) * 16);
+  return tc_scratch_layout(kpad, nq, kk).total;
 }
 
 // Runs the tensor-core screen for the queries in qp (normalized, dpad stride). Writes the per-query
@@ -915,7 +947,7 @@ void flat_tc_prepare(FlatState& s, cudaStream_t st) {
 void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
                     const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, int kk,
                     float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits, float* eps,
-                    int* err, cudaStream_t st) {
+                    int* err, void* scratch, cudaStream_t st) {
   QV_REQUIRE(kk == 24 || kk == tc::kMaxKK, "tensor-core screen: unsupported best-list length");
   const int kpad = static_cast<int>(s.kpad);
   const bool l2 = s.metric == QV_METRIC_L2;
@@ -923,16 +955,22 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   // tensor.
   const size_t group_rows = static_cast<size_t>(tc::kTiles) * tc::kM;
   const size_t nq_pad = ceil_div(nq, group_rows) * group_rows;
-  DeviceBuffer q16(nq_pad * kpad * sizeof(__half), st), qinv(nq * sizeof(float), st),
-      qn2(nq * sizeof(float), st);
-  QV_CUDA(cudaMemsetAsync(q16.get(), 0, nq_pad * kpad * sizeof(__half), st));
+  const TcScratch L = tc_scratch_layout(s.kpad, nq, kk);
+  unsigned char* base = static_cast<unsigned char*>(scratch);
+  __half* q16 = reinterpret_cast<__half*>(base + L.q16);
+  float* qinv = reinterpret_cast<float*>(base + L.qinv);
+  float* qn2 = reinterpret_cast<float*>(base + L.qn2);
+  float* gbest = reinterpret_cast<float*>(base + L.gbest);
+  int* glock = reinterpret_cast<int*>(base + L.glock);
   const double gamma = (kpad + 2) * std::ldexp(1.0, -23);
-  tc::queries_to_f16_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(
-      qp, static_cast<int>(nq), static_cast<int>(s.dim), dpad, kpad, s.x16_scale, s.x16_err,
-      s.max_norm, l2, static_cast<float>(gamma), q16.get<__half>(), qinv.get<float>(),
-      qn2.get<float>(), eps);
+  tc::queries_to_f16_kernel<<<ceil_div(nq_pad, 8), 256, 0, st>>>(
+      qp, static_cast<int>(nq), static_cast<int>(nq_pad), static_cast<int>(s.dim), dpad, kpad,
+      s.x16_stats.get<unsigned>(), s.max_norm, l2, static_cast<float>(gamma), q16, qinv, qn2, eps);
   check_launch("queries_to_f16_kernel");
-  const CUtensorMap mq = tc::make_map(q16.get(), nq_pad, kpad);
+  tc::init_best_kernel<<<static_cast<unsigned>(std::min<size_t>(ceil_div(nq * kk, 256), 1024)),
+                         256, 0, st>>>(gbest, nq * kk, glock, nq);
+  check_launch("init_best_kernel");
+  const CUtensorMap mq = tc::make_map(q16, nq_pad, kpad);
   const CUtensorMap mx = tc::make_map(s.x16.get(), s.n, kpad);
   tc::Args a{};
   a.nq = static_cast<int>(nq);
@@ -943,8 +981,8 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   a.nrows = static_cast<int64_t>(s.n);
   a.chunk_rows = chunk_rows;
   a.l2 = l2;
-  a.qscale_inv = qinv.get<float>();
-  a.qnorm2 = qn2.get<float>();
+  a.qscale_inv = qinv;
+  a.qnorm2 = qn2;
   a.xnorm2 = s.xnorm2.get<float>();
   a.bitmap = d_bitmap;
   a.cand_d = cand_d;
@@ -955,12 +993,8 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   // together, sharing thresholds); the default row-chunk-major order shares row chunks in L2.
   const char* order = std::getenv("QV_FLAT_TC_ORDER");
   a.qmajor = order != nullptr && order[0] == 'q';
-  DeviceBuffer gbest(nq * kk * sizeof(float), st), glock(nq * sizeof(int), st);
-  tc::fill_inf_kernel<<<ceil_div(nq * kk, 256), 256, 0, st>>>(gbest.get<float>(), nq * kk);
-  check_launch("fill_inf_kernel");
-  QV_CUDA(cudaMemsetAsync(glock.get(), 0, glock.bytes(), st));
-  a.gbest = gbest.get<float>();
-  a.glock = glock.get<int>();
+  a.gbest = gbest;
+  a.glock = glock;
   a.err = err;
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
   const int stages = kk == 24 ? tc::Ring<24>::kStages : tc::Ring<32>::kStages;
@@ -991,11 +1025,8 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   }
   timer.stop();
   check_launch("flat_screen_tc_kernel");
-  int e = 0;
-  QV_CUDA(cudaMemcpyAsync(&e, err, sizeof(int), cudaMemcpyDeviceToHost, st));
-  QV_CUDA(cudaStreamSynchronize(st));
-  timer.finish();
-  if (e != 0) fail(QV_ERR_DEVICE, "tensor-core screen timed out waiting on a pipeline barrier");
+  // A barrier timeout is reported through *err: the finalize then sends every query to the exact
+  // rescan and counts the timeout in the search's report words.
 }
 
 }  // namespace qv

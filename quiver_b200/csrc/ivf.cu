@@ -876,30 +876,28 @@ void run_scan(const IvfState& s, const Prepared& p, size_t nq, size_t keep, size
   // each), the lookup-table source per probe (the precomputed slice for L2 with precomputed
   // terms; the codebooks once per query otherwise), the query, and the stored vectors the
   // refine gathers.
-  DeviceBuffer codes_read;
+  const double lut = static_cast<double>(ts) * (a.use_pre ? p.nprobe : 1);
+  const double per_query = lut + s.dim * sizeof(float) +
+                           (refine ? static_cast<double>(keep) * s.dim * sizeof(float) : 0.0);
+  unsigned long long* slot = nullptr;
   if (thread_timing()) {
-    codes_read.allocate(sizeof(unsigned long long), st);
+    // The codes of the probed lists are counted on the device and copied to a pinned slot that
+    // is read when the timer is resolved; the search itself does not wait.
+    DeviceBuffer codes_read(sizeof(unsigned long long), st);
     QV_CUDA(cudaMemsetAsync(codes_read.get(), 0, sizeof(unsigned long long), st));
     const size_t pairs = nq * static_cast<size_t>(p.nprobe);
     probed_codes_kernel<<<static_cast<unsigned>(std::min<size_t>(ceil_div(pairs, 256), 1024)), 256,
                           0, st>>>(p.probes.get<uint32_t>(), pairs, a.offsets,
                                    codes_read.get<unsigned long long>());
     check_launch("probed_codes_kernel");
+    slot = timing_count_slot();
+    QV_CUDA(cudaMemcpyAsync(slot, codes_read.get(), sizeof(*slot), cudaMemcpyDeviceToHost, st));
   }
-  KernelTimer timer(st, "ivf_scan_kernel", 0.0, true);
+  KernelTimer timer(st, "ivf_scan_kernel", per_query * static_cast<double>(nq), true);
+  if (slot != nullptr) timer.set_device_count(slot, static_cast<double>(s.m));
   kernel<<<static_cast<unsigned>(nq), kScanThreads, smem, st>>>(a);
   timer.stop();
   check_launch("ivf_scan_kernel");
-  if (timer.on()) {
-    unsigned long long codes = 0;
-    QV_CUDA(cudaMemcpyAsync(&codes, codes_read.get(), sizeof(codes), cudaMemcpyDeviceToHost, st));
-    QV_CUDA(cudaStreamSynchronize(st));
-    const double lut = static_cast<double>(ts) * (a.use_pre ? p.nprobe : 1);
-    const double per_query = lut + s.dim * sizeof(float) +
-                             (refine ? static_cast<double>(keep) * s.dim * sizeof(float) : 0.0);
-    timer.set_work(static_cast<double>(codes) * s.m + per_query * static_cast<double>(nq));
-    timer.finish();
-  }
 }
 
 }  // namespace

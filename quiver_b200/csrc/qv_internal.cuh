@@ -152,52 +152,70 @@ struct SearchStats {
 SearchStats& thread_stats();
 bool& thread_timing();  // qv_set_timing
 
-// Brackets one launch with CUDA events when timing is on; finish() (after the stream has been
-// synchronized) adds the elapsed time and work to the thread's stats.
+// Starts a new search's accounting: with timing off the counters describe the last search only;
+// with timing on they accumulate until qv_last_search_stats reads (and resets) them.
+void begin_search_stats();
+
+// A timed launch whose CUDA events have not been read yet. `count` (a pinned host slot, filled by
+// a copy queued on the launch's stream, or nullptr) adds count * per_count to the work once the
+// events have completed (work that is only known on the device, e.g. the list lengths a scan
+// visited).
+struct PendingTimer {
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  const char* name = "";
+  double work = 0.0;
+  bool bytes = false;
+  const unsigned long long* count = nullptr;
+  double per_count = 0.0;
+};
+// Queues a timed launch; resolve_timers() waits for the queued events, adds their elapsed time
+// and work to the thread's stats and releases them.
+void defer_timer(const PendingTimer& t);
+void resolve_timers();
+// A pinned host slot for a device-side work counter of a timed launch (per thread, reused
+// round-robin; valid until several thousand later timed launches).
+unsigned long long* timing_count_slot();
+
+// Brackets one launch with CUDA events when timing is on. Nothing waits for them here: stop()
+// queues them, so timing adds no host synchronization to the search.
 class KernelTimer {
  public:
   KernelTimer(cudaStream_t st, const char* name, double work, bool is_bytes)
-      : st_(st), name_(name), work_(work), bytes_(is_bytes), on_(thread_timing()) {
+      : st_(st), on_(thread_timing()) {
+    t_.name = name;
+    t_.work = work;
+    t_.bytes = is_bytes;
     if (on_) {
-      cudaEventCreate(&e0_);
-      cudaEventCreate(&e1_);
-      cudaEventRecord(e0_, st_);
+      cudaEventCreate(&t_.e0);
+      cudaEventCreate(&t_.e1);
+      cudaEventRecord(t_.e0, st_);
     }
   }
-  void stop() {
-    if (on_) cudaEventRecord(e1_, st_);
+  // Work counted on the device: count (a timing_count_slot filled on the stream) * per_count.
+  void set_device_count(const unsigned long long* count, double per_count) {
+    t_.count = count;
+    t_.per_count = per_count;
   }
-  // For work that is only known after the launch (e.g. the list lengths a scan visited).
-  void set_work(double work) { work_ = work; }
   bool on() const { return on_; }
-  void finish() {
+  void stop() {
     if (!on_) return;
-    float ms = 0.0f;
-    if (cudaEventElapsedTime(&ms, e0_, e1_) == cudaSuccess) {
-      SearchStats& s = thread_stats();
-      s.dominant_ms += ms;
-      s.dominant_work += work_;
-      s.work_is_bytes = bytes_;
-      s.dominant_name = name_;
-    }
-    cudaEventDestroy(e0_);
-    cudaEventDestroy(e1_);
+    cudaEventRecord(t_.e1, st_);
+    defer_timer(t_);
     on_ = false;
   }
   ~KernelTimer() {
-    if (on_) {
-      cudaEventDestroy(e0_);
-      cudaEventDestroy(e1_);
+    if (on_) {  // not stopped (the launch failed)
+      cudaEventDestroy(t_.e0);
+      cudaEventDestroy(t_.e1);
     }
   }
+  KernelTimer(const KernelTimer&) = delete;
+  KernelTimer& operator=(const KernelTimer&) = delete;
 
  private:
   cudaStream_t st_;
-  const char* name_;
-  double work_;
-  bool bytes_;
   bool on_;
-  cudaEvent_t e0_ = nullptr, e1_ = nullptr;
+  PendingTimer t_;
 };
 inline void count_launch(uint64_t n = 1) { thread_stats().kernel_launches += n; }
 

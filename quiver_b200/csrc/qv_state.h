@@ -31,9 +31,36 @@ struct FlatState {
   // first search after rows change; x16_err = max ||x - x16/scale|| over rows.
   DeviceBuffer x16;
   size_t kpad = 0, x16_rows = 0;
-  float x16_scale = 1.0f, x16_err = 0.0f;
+  // Device words of the fp16 copy: [0] bits of max |x| (the copy's power-of-two scale follows
+  // from it), [1] bits of max ||x - x16 / scale||. Read by the kernels only, so building the copy
+  // needs no host round trip.
+  DeviceBuffer x16_stats;
+  // Recorded after the copy's kernels; searches on other streams wait for it.
+  cudaEvent_t x16_ready = nullptr;
   std::mutex x16_mu;
+  FlatState() = default;
+  FlatState(const FlatState&) = delete;
+  FlatState& operator=(const FlatState&) = delete;
+  ~FlatState() {
+    if (x16_ready != nullptr) cudaEventDestroy(x16_ready);
+  }
 };
+
+// Words a search's kernels report into (device int array, accumulated with atomics):
+// [0] queries the certificate rejected and the exact rescan answered, [1] queries holding NaN or
+// infinity (their results are QV_INVALID_LABEL with a NaN distance), [2] tensor-core screen
+// launches that gave up waiting on a pipeline barrier (their queries were all rescanned exactly).
+constexpr int kSearchFlagWords = 4;
+enum { kFlagRescanned = 0, kFlagNonFinite = 1, kFlagTimeout = 2 };
+struct SearchFlags {
+  int* dev = nullptr;        // kSearchFlagWords device ints for _device searches
+  int* host = nullptr;       // their pinned host copy, queued after each _device search
+  cudaEvent_t done = nullptr;  // recorded after that copy
+  int* sync_dev = nullptr;   // the same for the host-buffer entry points (which wait)
+  int* sync_host = nullptr;
+};
+// This thread's report words on `device` (allocated on first use).
+SearchFlags& thread_search_flags(int device);
 
 void flat_search_noalloc(const FlatState& s, const float* d_queries, size_t nq, size_t k,
                          const uint64_t* d_bitmap, uint64_t* d_labels, float* d_dists,
@@ -44,18 +71,22 @@ constexpr int kTcGroupRows = 8;
 bool flat_tc_eligible(const FlatState& s, size_t k);
 int flat_tc_kk(size_t k);
 void flat_tc_prepare(FlatState& s, cudaStream_t st);
+// Device scratch the tensor-core screen needs for nq queries with best lists of kk.
+size_t flat_tc_scratch_bytes(const FlatState& s, size_t nq, int kk);
 void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
                     const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, int kk,
                     float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits, float* eps,
-                    int* err, cudaStream_t st);
+                    int* err, void* scratch, cudaStream_t st);
 
 void flat_reserve(FlatState& s, size_t rows, cudaStream_t st);
 // Appends n rows (device pointer, row-major) with labels (device pointer).
 void flat_append(FlatState& s, const float* d_rows, const uint64_t* d_labels, size_t n,
                  cudaStream_t st);
+// Enqueues an exact search on `st` and returns without waiting for it. The kernels add their
+// reports into d_flags (kSearchFlagWords device ints, see kFlag*).
 void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k,
                  const uint64_t* d_bitmap, uint64_t* d_labels, float* d_dists, uint64_t* d_keys,
-                 cudaStream_t st);
+                 int* d_flags, cudaStream_t st);
 
 // ---- IVF-PQ ------------------------------------------------------------------------------------
 // Inverted lists are stored list-major and contiguous in HBM (codes count x m bytes, labels,

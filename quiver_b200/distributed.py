@@ -2,8 +2,8 @@
 
 Every rank holds one contiguous id range of the collection on its own GPU and receives the whole
 query batch. Each rank computes its local top-k (Flat) or top-``keep`` ADC candidates (IVF-PQ) with
-the CUDA library, the per-rank (distance, key, label) triples are exchanged with one NCCL
-all-gather over NVLink (``torch.distributed`` is only the transport), and a device k-way merge
+the CUDA library, the per-rank (distance, key, label) triples are packed into one buffer and
+exchanged with one NCCL all-gather over NVLink (``torch.distributed`` is only the transport), and a device k-way merge
 (``qv_merge_topk_device``) produces the global result. Keys are global row ids (Flat) or
 ``list << 32 | offset-in-full-list`` (IVF-PQ), so ties break exactly as on one GPU.
 
@@ -45,6 +45,26 @@ def _all_gather(t: torch.Tensor, world: int, group) -> torch.Tensor:
     out = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
     dist.all_gather_into_tensor(out, t, group=group)
     return out.view((world,) + tuple(t.shape))
+
+
+def _all_gather_triples(d: torch.Tensor, key: torch.Tensor, lab: torch.Tensor, world: int,
+                        group):
+    """All-gathers per-rank (distance float32, key int64, label int64) arrays of one shape with ONE
+    collective: the three are packed bit for bit into a single int32 buffer (5 words per entry),
+    exchanged, and unpacked per rank as contiguous [world, ...] arrays."""
+    if world == 1:
+        return d.unsqueeze(0), key.unsqueeze(0), lab.unsqueeze(0)
+    n = d.numel()
+    buf = torch.empty(5 * n, dtype=torch.int32, device=d.device)
+    buf[:n] = d.contiguous().view(torch.int32).reshape(-1)
+    buf[n:3 * n] = key.contiguous().view(torch.int32).reshape(-1)
+    buf[3 * n:] = lab.contiguous().view(torch.int32).reshape(-1)
+    out = _all_gather(buf, world, group)  # [world, 5n]
+    shape = (world,) + tuple(d.shape)
+    gd = out[:, :n].contiguous().view(torch.float32).view(shape)
+    gk = out[:, n:3 * n].contiguous().view(torch.int64).view(shape)
+    gl = out[:, 3 * n:].contiguous().view(torch.int64).view(shape)
+    return gd, gk, gl
 
 
 def shard_range(n: int, rank: int, world: int):
@@ -119,9 +139,8 @@ class ShardedFlatIndex:
             return d, lab
         valid = key >= 0  # unfilled slots carry key 2^64-1 (-1 as int64)
         gkey = torch.where(valid, self._gid[key.clamp(min=0)], key)
-        od, _, ol = _merge(_all_gather(d, self.world, self.group),
-                           _all_gather(gkey, self.world, self.group),
-                           _all_gather(lab, self.world, self.group), k, self.device)
+        od, _, ol = _merge(*_all_gather_triples(d, gkey, lab, self.world, self.group), k,
+                           self.device)
         return od, ol
 
     def search(self, queries, k: int = 10):
@@ -269,9 +288,8 @@ class ShardedIvfPqIndex:
         check(lib().qv_ivfpq_candidates_device(self.local.handle, queries.data_ptr(), nq, keep,
                                                nprobe, bm, d.data_ptr(), key.data_ptr(),
                                                lab.data_ptr(), sp))
-        d, key, lab = _merge(_all_gather(d, self.world, self.group),
-                             _all_gather(key, self.world, self.group),
-                             _all_gather(lab, self.world, self.group), keep, self.device)
+        d, key, lab = _merge(*_all_gather_triples(d, key, lab, self.world, self.group), keep,
+                             self.device)
         if not refine:
             return d[:, :k].contiguous(), lab[:, :k].contiguous()
         exact = torch.empty((nq, keep), dtype=torch.float32, device=dev)

@@ -74,7 +74,7 @@ def _list_bases(rank, world):
 def _sharded_exact_topk(rank, world):
     """Each rank: exact L2 top-k over its id range with global ids as keys; all-gather; merge by
     (distance, key). Integer data makes ties frequent, so the key order is what is tested."""
-    from quiver_b200.distributed import _all_gather, shard_range
+    from quiver_b200.distributed import _all_gather_triples, shard_range
     rng = np.random.default_rng(5)
     n, nq, dim, k = 1001, 7, 6, 12
     db = rng.integers(0, 3, (n, dim)).astype(np.float32)
@@ -85,8 +85,10 @@ def _sharded_exact_topk(rank, world):
     order = np.lexsort((np.broadcast_to(keys, d.shape), d), axis=1)[:, :k]
     ld = np.take_along_axis(d, order, 1).astype(np.float32)
     lk = keys[order].astype(np.int64)
-    gd = _all_gather(torch.from_numpy(ld), world, None).numpy()
-    gk = _all_gather(torch.from_numpy(lk), world, None).numpy()
+    gd, gk, gl = _all_gather_triples(torch.from_numpy(ld), torch.from_numpy(lk),
+                                     torch.from_numpy(lk * 3 + 1), world, None)
+    gd, gk = gd.numpy(), gk.numpy()
+    assert np.array_equal(gl.numpy(), gk * 3 + 1)  # labels travel with their entries
     # merge by (distance, key) across ranks
     cd = np.concatenate(list(gd), axis=1)
     ck = np.concatenate(list(gk), axis=1)
@@ -131,6 +133,37 @@ def _query_slices_gathered(rank, world):
     d = torch.from_numpy((rows[:, None] * 10 + np.arange(k)[None, :]).astype(np.float32))
     lab = torch.from_numpy((rows[:, None] * 100 + np.arange(k)[None, :]).astype(np.int64))
     return gather_query_slices(d, lab, nq, world, None)
+
+
+def _triples_bit_exact(rank, world):
+    """The packed exchange keeps every bit: signed zeros, infinities, NaN payloads, keys and
+    labels near 2^63 and the -1 padding."""
+    from quiver_b200.distributed import _all_gather_triples
+    d = torch.tensor([[0.5 + rank, float("inf"), -0.0], [float("nan"), -1e-38, 3.0]])
+    key = torch.tensor([[2**62 + rank, -1, 5], [0, 2**63 - 1, -2]], dtype=torch.int64)
+    lab = torch.tensor([[7, -1, 2**63 - 1 - rank], [1, 2, 3 + rank]], dtype=torch.int64)
+    gd, gk, gl = _all_gather_triples(d, key, lab, world, None)
+    return gd.view(torch.int32).numpy(), gk.numpy(), gl.numpy(), d.view(torch.int32).numpy()
+
+
+def _collective_timeout_entry(rank, world, port, out_q):
+    """Rank 1 never joins the collective; rank 0 must get an error from its process group's
+    short timeout instead of waiting for ever."""
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=2))
+    if rank == 1:
+        time.sleep(8)  # absent from the collective until rank 0 has given up
+        os._exit(0)
+    t0 = time.time()
+    try:
+        from quiver_b200.distributed import _all_gather
+        _all_gather(torch.zeros(4), world, None)
+        out_q.put((rank, "no error", time.time() - t0))
+    except Exception as e:  # noqa: BLE001 - the failure being tested
+        out_q.put((rank, repr(e), time.time() - t0))
+    os._exit(0)
 
 
 # ---- tests ---------------------------------------------------------------------------------------
@@ -181,3 +214,32 @@ def test_query_slices_gather_in_query_order():
     for rank in range(WORLD):
         lab, d = res[rank]
         assert np.array_equal(d, want_d) and np.array_equal(lab, want_l)
+
+
+def test_packed_triples_exchange_is_bit_exact():
+    res = _run("_triples_bit_exact")
+    for rank in range(WORLD):
+        gd, gk, gl, _ = res[rank]
+        for r in range(WORLD):
+            assert np.array_equal(gd[r], res[r][3])
+            assert gk[r, 0, 0] == 2**62 + r and gk[r, 0, 1] == -1 and gk[r, 1, 1] == 2**63 - 1
+            assert gl[r, 0, 2] == 2**63 - 1 - r and gl[r, 1, 2] == 3 + r
+
+
+def test_a_rank_missing_from_a_collective_is_detected_by_timeout():
+    """Failure detection on the host: a rank that never arrives makes the other rank's collective
+    fail after the process group's short timeout (no GPU involved)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_collective_timeout_entry, args=(r, WORLD, port, q))
+             for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    rank, err, waited = q.get(timeout=60)
+    assert rank == 0 and err != "no error", "the collective returned without its peer"
+    assert waited < 30, f"the failure took {waited:.1f} s to surface"
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()

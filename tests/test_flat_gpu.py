@@ -187,3 +187,41 @@ def test_tensor_core_screen_equals_simt_screen(gpu, oracle, monkeypatch, metric,
         assert np.array_equal(d1, d2) and np.array_equal(l1, l2_)
         wl, wd = oracle.flat_search(stored, np.arange(20000, dtype=np.uint64), metric, q, k)
         assert_topk_parity(l1, d1, wl, wd, exact=True, what=f"tc {metric} k={k}")
+
+
+def test_device_searches_are_asynchronous_and_ordered(gpu, oracle):
+    """qv_flat_search_device only enqueues: two searches queued back to back on one stream (and
+    a third on the CUDA default stream, NULL) all return correct results after one
+    synchronization; a query holding NaN gets no results (QV_INVALID_LABEL, NaN distance) and the
+    other queries of its batch are answered."""
+    import ctypes as C
+    import torch
+    from quiver_b200.synthetic import mixture
+    base = mixture(50_000, 100, 80, 0.35, 1.0, centre_seed=9, seed=10)
+    ix = gpu.FlatIndex(100, "cosine")
+    ix.add(base)
+    lib = gpu.lib()
+    stream = torch.cuda.Stream()
+    batches = [mixture(nq, 100, 80, 0.35, 1.0, centre_seed=9, seed=s)
+               for nq, s in [(700, 11), (333, 12), (64, 13)]]
+    batches[1][5, 7] = np.nan
+    outs = []
+    for i, q in enumerate(batches):
+        dq = torch.from_numpy(q).cuda()
+        lab = torch.empty((len(q), 10), dtype=torch.int64, device="cuda")
+        dst = torch.empty((len(q), 10), dtype=torch.float32, device="cuda")
+        s = C.c_void_p(stream.cuda_stream) if i < 2 else None
+        if i < 2:
+            stream.wait_stream(torch.cuda.current_stream())
+        gpu._native.check(lib.qv_flat_search_device(ix.handle, dq.data_ptr(), len(q), 10, None,
+                                                    lab.data_ptr(), dst.data_ptr(), None, s))
+        outs.append((dq, lab, dst))
+    torch.cuda.synchronize()
+    stored = oracle.normalize_rows(base)
+    ids = np.arange(len(base), dtype=np.uint64)
+    for i, (q, (_, lab, dst)) in enumerate(zip(batches, outs)):
+        l, d = lab.cpu().numpy(), dst.cpu().numpy()
+        good = np.isfinite(q).all(axis=1)
+        wl, wd = oracle.flat_search(stored, ids, "cosine", q[good], 10)
+        assert_topk_parity(l[good], d[good], wl, wd, exact=True, what=f"async batch {i}")
+        assert (l[~good] == -1).all() and np.isnan(d[~good]).all()
