@@ -933,8 +933,9 @@ static FlatPlan plan_search(const FlatState& s, size_t nq, size_t k, bool allow_
   P.tensor = allow_tensor && forced_kk == 0 && flat_tc_eligible(s, k);
   const size_t nrows = std::max<size_t>(s.n, 1);
   if (P.tensor) {
-    P.kk = flat_tc_kk(k);
-    P.n_qtiles = static_cast<int>(ceil_div(nq, 256));  // work units cover query groups of 2 x 128
+    P.kk = flat_tc_kk(s, k);
+    // Work units cover query groups of 2 x 128 (narrow screen) or one 128-query tile (wide).
+    P.n_qtiles = static_cast<int>(ceil_div(nq, flat_tc_is_wide(s, k) ? 128 : 256));
     P.n_chunks = choose_chunks(nrows, P.n_qtiles, std::max(1, kMaxCandidatesPerQuery / P.kk),
                                nsm, 128, &P.chunk_rows);
     P.group_rows = kTcGroupRows;

@@ -695,16 +695,26 @@ CUtensorMap make_map(const void* base, uint64_t rows, uint64_t kpad) {
 
 // ---- host side ------------------------------------------------------------------------------------
 
+// The narrow screen (this file) takes dim <= 128 and k <= 24; the wide screen (flat_tc_wide.cu)
+// dim <= 768 and k <= 120.
+bool flat_tc_is_wide(const FlatState& s, size_t k) {
+  return s.dim > 128 || k + 8 > static_cast<size_t>(tc::kMaxKK);
+}
+
 bool flat_tc_eligible(const FlatState& s, size_t k) {
   const char* e = std::getenv("QV_FLAT_SCREEN");
   if (e != nullptr && std::strcmp(e, "simt") == 0) return false;
-  return s.dim <= 128 && k + 8 <= static_cast<size_t>(tc::kMaxKK) &&
-         s.n >= static_cast<size_t>(tc::kN);
+  if (s.n < static_cast<size_t>(tc::kN)) return false;
+  return flat_tc_is_wide(s, k) ? flat_tc_wide_fits(s, k) : true;
 }
 
 // Best-list length: k + 8 groups or more (the certificate's margin); 24 when that suffices,
-// which tightens thresholds and shortens the finalize's re-rank.
-int flat_tc_kk(size_t k) { return k + 8 <= 24 ? 24 : tc::kMaxKK; }
+// which tightens thresholds and shortens the finalize's re-rank; the wide screen rounds k + 8 up
+// to a multiple of 16 (its lists are merged in 16-entry chunks).
+int flat_tc_kk(const FlatState& s, size_t k) {
+  if (flat_tc_is_wide(s, k)) return flat_tc_wide_kk(k);
+  return k + 8 <= 24 ? 24 : tc::kMaxKK;
+}
 
 // Builds (once per set of rows) the fp16 copy of the index and its error statistics, entirely on
 // the device: nothing here waits for the GPU. Searches on other streams wait for the copy through
@@ -735,9 +745,9 @@ void flat_tc_prepare(FlatState& s, cudaStream_t st) {
 
 // Scratch layout of one tensor-core screen (offsets into the block flat_tc_scratch_bytes sizes).
 struct TcScratch {
-  size_t q16, qinv, qn2, gbest, glock, total;
+  size_t q16, qinv, qn2, gbest, glock, lists, total;
 };
-static TcScratch tc_scratch_layout(size_t kpad, size_t nq, int kk) {
+static TcScratch tc_scratch_layout(size_t kpad, size_t nq, int kk, size_t list_bytes) {
   const size_t group_rows = static_cast<size_t>(tc::kTiles) * tc::kM;
   const size_t nq_pad = ceil_div(nq, group_rows) * group_rows;
   TcScratch L{};
@@ -752,13 +762,20 @@ static TcScratch tc_scratch_layout(size_t kpad, size_t nq, int kk) {
   L.qn2 = take(nq * sizeof(float));
   L.gbest = take(nq * static_cast<size_t>(kk) * sizeof(float));
   L.glock = take(nq * sizeof(int));
+  L.lists = take(list_bytes);
   L.total = off;
   return L;
 }
 
+// The wide screen's per-CTA working lists (none for the narrow screen, whose lists live in
+// shared memory).
+static size_t tc_list_bytes(const FlatState& s, int kk) {
+  return kk > tc::kMaxKK || s.dim > 128 ? flat_tc_wide_list_bytes(s, kk) : 0;
+}
+
 size_t flat_tc_scratch_bytes(const FlatState& s, size_t nq, int kk) {
   const size_t kpad = std::max<size_t>(64, ceil_div(s.dim, 16) * 16);
-  return tc_scratch_layout(kpad, nq, kk).total;
+  return tc_scratch_layout(kpad, nq, kk, tc_list_bytes(s, kk)).total;
 }
 
 // Runs the tensor-core screen for the queries in qp (normalized, dpad stride). Writes the per-query
@@ -767,14 +784,16 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
                     const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, int kk,
                     float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits, float* eps,
                     int* err, void* scratch, cudaStream_t st) {
-  QV_REQUIRE(kk == 24 || kk == tc::kMaxKK, "tensor-core screen: unsupported best-list length");
+  const bool wide = kk > tc::kMaxKK || s.dim > 128;
+  QV_REQUIRE(wide || kk == 24 || kk == tc::kMaxKK,
+             "tensor-core screen: unsupported best-list length");
   const int kpad = static_cast<int>(s.kpad);
   const bool l2 = s.metric == QV_METRIC_L2;
   // Whole query groups of kTiles x 128 rows (zero rows past nq), so no TMA box extends past the
   // tensor.
   const size_t group_rows = static_cast<size_t>(tc::kTiles) * tc::kM;
   const size_t nq_pad = ceil_div(nq, group_rows) * group_rows;
-  const TcScratch L = tc_scratch_layout(s.kpad, nq, kk);
+  const TcScratch L = tc_scratch_layout(s.kpad, nq, kk, tc_list_bytes(s, kk));
   unsigned char* base = static_cast<unsigned char*>(scratch);
   __half* q16 = reinterpret_cast<__half*>(base + L.q16);
   float* qinv = reinterpret_cast<float*>(base + L.qinv);
@@ -786,6 +805,12 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
       qp, static_cast<int>(nq), static_cast<int>(nq_pad), static_cast<int>(s.dim), dpad, kpad,
       s.x16_stats.get<unsigned>(), s.max_norm, l2, static_cast<float>(gamma), q16, qinv, qn2, eps);
   check_launch("queries_to_f16_kernel");
+  if (wide) {
+    const CUtensorMap mq = tc::make_map(q16, nq_pad, kpad);
+    flat_screen_tc_wide(s, qp, dpad, nq, d_bitmap, n_chunks, chunk_rows, kk, cand_d, cand_r,
+                        cand_n, thr_bits, eps, err, mq, qinv, qn2, base + L.lists, st);
+    return;
+  }
   tc::init_best_kernel<<<static_cast<unsigned>(std::min<size_t>(ceil_div(nq * kk, 256), 1024)),
                          256, 0, st>>>(gbest, nq * kk, glock, nq);
   check_launch("init_best_kernel");

@@ -1,0 +1,480 @@
+// Tensor-core (tcgen05) screen for wide rows and large k: dimensions up to 768 (fp16 operands
+// padded to whole 64-column atoms) and best lists of up to 128 groups (k up to 120).
+//
+// Same arithmetic and certificate as the screen in flat_tc.cu (fp16 MMA with float32
+// accumulation in TMEM, 8-row groups, per-query best lists, exact re-rank and certificate in
+// flat.cu); what changes is the data movement, which the row width dictates:
+//   * one 128-query tile per unit (the tile's 128 x kpad fp16 operand, up to 192 KB, stays in
+//     shared memory for the whole unit), and row tiles streamed one 64-column K atom at a time
+//     through a ring of 16 KB stages, so a row tile is kAtoms stages and each stage feeds four
+//     128 x 128 x 16 MMAs;
+//   * accumulator slots (128 columns each, two of them) are released by their own barrier,
+//     because a stage no longer covers a whole row tile;
+//   * best lists live in global memory (L2-resident, one region per CTA, entry i of query lane l
+//     at i * 128 + l, so a warp's accesses coalesce): 128 queries x up to 144 entries do not fit
+//     next to the operands. A list is compacted (sorted, cut to its KK best) by merging 16-entry
+//     chunks in registers, which happens rarely once the query's threshold has settled.
+//
+// Warps: 0 TMA producer, 1 MMA issuer (and TMEM owner), 2..5 epilogue (warp w reads TMEM lanes
+// 32 * (w % 4) .. + 31; thread = query). Every mbarrier wait is bounded (a kernel argument); on
+// timeout the CTA raises the launch's error word, drains its copies in flight (bounded), frees
+// TMEM and exits, and the finalize sends every query to the exact rescan.
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "qv_state.h"
+#include "tc_common.cuh"
+
+namespace qv {
+namespace tcw {
+
+using namespace qv::tc;
+
+constexpr int kEpiWarps = 4;
+constexpr int kThreads = 32 * (2 + kEpiWarps);
+constexpr int kAcc = 2;           // accumulator slots of kN columns
+constexpr int kLS = kM;           // list stride: entry i of query lane l at i * kLS + l
+constexpr int kAppend = 16;       // entries appended between compactions (two 64-column halves)
+constexpr int kMaxAtoms = 12;     // kpad <= 768
+constexpr int kMaxStages = 8;
+
+struct Args {
+  int nq, n_qtiles, n_chunks, total_units, atoms, stages, kk;
+  int64_t nrows, chunk_rows;
+  const float* qscale_inv;  // per query: 1 / (s_q * s_x)
+  const float* qnorm2;      // per query ||q||^2 (L2)
+  const float* xnorm2;      // per row ||x||^2 (L2)
+  const uint64_t* bitmap;
+  float* cand_d;
+  uint32_t* cand_r;
+  int* cand_n;
+  unsigned* thr_bits;
+  float* list_d;            // per CTA: (kk + kAppend) x kLS working lists
+  uint32_t* list_r;
+  int* err;
+  long long wait_cycles;
+  uint64_t drain_ns;
+};
+
+// Sorts 16 (distance, group) entries ascending in registers (bitonic network).
+__device__ __forceinline__ void sort16(float (&d)[16], uint32_t (&r)[16]) {
+#pragma unroll
+  for (int size = 2; size <= 16; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+        if ((lo & size) == 0)
+          cex(d[lo], r[lo], d[hi], r[hi]);
+        else
+          cex(d[hi], r[hi], d[lo], r[lo]);
+      }
+    }
+  }
+}
+
+// Keeps the best kk entries of a query's list (a sorted prefix of kk, then up to kAppend
+// appended entries), sorted, and tightens the threshold to the kk-th. The appended entries are
+// sorted in registers (carry), then merged into the prefix 16 entries at a time: the chunk and
+// the carry (both sorted) form a 32-entry bitonic sequence; after a bitonic merge the lower 16
+// are the chunk's new contents and the upper 16 the carry into the next chunk. The last carry
+// (entries beyond kk) is dropped. The warp's lanes run the same fixed sequence (no divergence).
+__device__ __noinline__ void compact_wide(float* d, uint32_t* r, int kk, int& cnt, float& thr) {
+  const float kInf = __int_as_float(0x7f800000);
+  float cd[16];
+  uint32_t cr[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const bool in = kk + i < cnt;
+    cd[i] = in ? d[(kk + i) * kLS] : kInf;
+    cr[i] = in ? r[(kk + i) * kLS] : 0xffffffffu;
+  }
+  sort16(cd, cr);
+  float last = kInf;
+  for (int c = 0; c < kk; c += 16) {
+    float xd[32];
+    uint32_t xr[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      xd[i] = d[(c + i) * kLS];
+      xr[i] = r[(c + i) * kLS];
+      xd[31 - i] = cd[i];
+      xr[31 - i] = cr[i];
+    }
+#pragma unroll
+    for (int stride = 16; stride > 0; stride >>= 1) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+        cex(xd[lo], xr[lo], xd[hi], xr[hi]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      d[(c + i) * kLS] = xd[i];
+      r[(c + i) * kLS] = xr[i];
+      cd[i] = xd[16 + i];
+      cr[i] = xr[16 + i];
+    }
+    last = xd[15];
+  }
+  cnt = kk;
+  thr = fminf(thr, last);
+}
+
+template <bool kL2>
+__global__ void __launch_bounds__(kThreads, 1)
+    flat_screen_tc_wide_kernel(const __grid_constant__ CUtensorMap tmap_q,
+                               const __grid_constant__ CUtensorMap tmap_x, const Args a) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int atoms = a.atoms, stages = a.stages, kk = a.kk;
+  unsigned char* smem_a = base;                         // atoms x 16 KB (the query tile)
+  unsigned char* smem_b = smem_a + atoms * kAtomBytes;  // stages x 16 KB (row-tile K atoms)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + stages * kAtomBytes);
+  // bars: full[stages], empty[stages], acc_full[kAcc], acc_empty[kAcc], a_full, a_empty.
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  __shared__ int s_consumed;  // B fills the MMA issuer has waited for (abort drain)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int FULL = 0, EMPTY = stages, ACC_FULL = 2 * stages, ACC_EMPTY = 2 * stages + kAcc,
+            A_FULL = 2 * stages + 2 * kAcc, A_EMPTY = A_FULL + 1;
+  auto bar = [&](int i) { return smem_u32(bars + i); };
+
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    s_consumed = 0;
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(bar(FULL + s), 1);   // the producer's expect_tx
+      mbar_init(bar(EMPTY + s), 1);  // the MMA commit
+    }
+    for (int b = 0; b < kAcc; ++b) {
+      mbar_init(bar(ACC_FULL + b), 1);
+      mbar_init(bar(ACC_EMPTY + b), kEpiWarps);
+    }
+    mbar_init(bar(A_FULL), 1);
+    mbar_init(bar(A_EMPTY), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&s_tmem)),
+                 "r"(kAcc * kN));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s_tmem;
+  volatile int* abort_flag = &s_abort;
+
+  auto unit_rows = [&](int u, int& qtile, int& chunk, int64_t& r0, int64_t& r1) {
+    chunk = u / a.n_qtiles;  // chunk-major: CTAs running together share row chunks in L2
+    qtile = u - chunk * a.n_qtiles;
+    r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
+    r1 = min(a.nrows, r0 + a.chunk_rows);
+  };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0, issued = 0;
+      uint32_t phase = 0, a_phase = 0;
+      bool first = true, ok = true;
+      for (int u = blockIdx.x; u < a.total_units && ok && !*abort_flag; u += gridDim.x) {
+        int qtile, chunk;
+        int64_t r0, r1;
+        unit_rows(u, qtile, chunk, r0, r1);
+        const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
+        if (!first) {
+          if (!mbar_wait(bar(A_EMPTY), a_phase, abort_flag, a.err, a.wait_cycles)) break;
+          a_phase ^= 1;
+        }
+        first = false;
+        mbar_expect_tx(bar(A_FULL), static_cast<uint32_t>(atoms * kAtomBytes));
+        for (int at = 0; at < atoms; ++at)
+          tma_load_2d(smem_u32(smem_a + at * kAtomBytes), &tmap_q, at * kAtomK, qtile * kM,
+                      bar(A_FULL));
+        for (int t = 0; t < ntiles && ok; ++t) {
+          const int y = static_cast<int>(r0 + static_cast<int64_t>(t) * kN);
+          for (int at = 0; at < atoms; ++at) {
+            ok = mbar_wait(bar(EMPTY + stage), phase ^ 1, abort_flag, a.err, a.wait_cycles);
+            if (!ok) break;
+            mbar_expect_tx(bar(FULL + stage), kAtomBytes);
+            tma_load_2d(smem_u32(smem_b + stage * kAtomBytes), &tmap_x, at * kAtomK, y,
+                        bar(FULL + stage));
+            ++issued;
+            if (++stage == stages) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+        }
+      }
+      if (*abort_flag) {
+        // Drain: wait (bounded) for every B fill the MMA issuer did not consume. Each fill's
+        // barrier phase completes when its bytes have landed.
+        const uint64_t t0 = gtimer();
+        for (int f = *reinterpret_cast<volatile int*>(&s_consumed); f < issued; ++f) {
+          const int s = f % stages;
+          const uint32_t par = (f / stages) & 1;
+          while (!mbar_test(bar(FULL + s), par) && gtimer() - t0 < a.drain_ns) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      int stage = 0, g = 0;  // g: row tiles issued by this CTA so far (slot g & 1)
+      uint32_t phase = 0, a_phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < a.total_units && ok && !*abort_flag; u += gridDim.x) {
+        int qtile, chunk;
+        int64_t r0, r1;
+        unit_rows(u, qtile, chunk, r0, r1);
+        const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
+        if (!mbar_wait(bar(A_FULL), a_phase, abort_flag, a.err, a.wait_cycles)) break;
+        a_phase ^= 1;
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(smem_a);
+        for (int t = 0; t < ntiles && ok; ++t, ++g) {
+          const int slot = g & 1;
+          // The slot's previous tile (g - 2) must have been read out by the epilogue.
+          ok = mbar_wait(bar(ACC_EMPTY + slot), ((g >> 1) & 1) ^ 1, abort_flag, a.err,
+                         a.wait_cycles);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * kN);
+          for (int at = 0; at < atoms; ++at) {
+            ok = mbar_wait(bar(FULL + stage), phase, abort_flag, a.err, a.wait_cycles);
+            if (!ok) break;
+            *reinterpret_cast<volatile int*>(&s_consumed) += 1;
+            tc_fence_after();
+            const uint32_t b_addr = smem_u32(smem_b + stage * kAtomBytes);
+            const uint32_t aa = a_addr + static_cast<uint32_t>(at * kAtomBytes);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+              umma_f16(d_tmem, smem_desc(aa + ks * 32), smem_desc(b_addr + ks * 32),
+                       (at | ks) != 0 ? 1u : 0u);
+            umma_commit(bar(EMPTY + stage));  // the stage is free once these MMAs have read it
+            if (++stage == stages) {
+              stage = 0;
+              phase ^= 1;
+            }
+          }
+          if (!ok) break;
+          umma_commit(bar(ACC_FULL + slot));
+        }
+        if (!ok) break;
+        umma_commit(bar(A_EMPTY));  // the query tile may be replaced once every MMA has run
+      }
+    }
+  } else {
+    // ---------------- epilogue: thread = query ----------------
+    const int quarter = warp & 3;  // TMEM lanes this warp may read
+    const int qi = quarter * 32 + lane;
+    float* ld = a.list_d + static_cast<size_t>(blockIdx.x) * (kk + kAppend) * kLS + qi;
+    uint32_t* lr = a.list_r + static_cast<size_t>(blockIdx.x) * (kk + kAppend) * kLS + qi;
+    const int cap = kk + kAppend;
+    const float kInfF = __int_as_float(0x7f800000);
+    int g = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < a.total_units && ok; u += gridDim.x) {
+      int qtile, chunk;
+      int64_t r0, r1;
+      unit_rows(u, qtile, chunk, r0, r1);
+      const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
+      const int q = qtile * kM + qi;
+      const bool active = q < a.nq;
+      const unsigned* qthr = a.thr_bits + (active ? q : 0);
+      float thr = active ? dev::from_ordered_bits(*qthr) : -kInfF;
+      const float inv = active ? a.qscale_inv[q] : 0.0f;
+      const float qn = (active && kL2) ? a.qnorm2[q] : 0.0f;
+      for (int i = 0; i < kk; ++i) {
+        ld[i * kLS] = kInfF;
+        lr[i * kLS] = 0xffffffffu;
+      }
+      int cnt = kk, seen = 0;
+      // best[j]: best score of the 8-row group j of a 64-column half (max inner product for
+      // cosine/IP, min distance for L2); rows past the chunk or rejected by the filter count as
+      // the worst score.
+      auto tree = [&](uint32_t (&r)[64], int64_t cb, float (&best)[8], float& top) {
+        float (&v)[64] = *reinterpret_cast<float(*)[64]>(r);
+        const bool partial = a.bitmap != nullptr || r1 - cb < 64;
+        uint64_t admitted = ~0ull;
+        if (partial) {
+          const int valid = static_cast<int>(r1 - cb < 64 ? r1 - cb : 64);
+          admitted = (valid >= 64 ? ~0ull : (valid > 0 ? (1ull << valid) - 1 : 0ull)) &
+                     (a.bitmap != nullptr && valid > 0 ? a.bitmap[static_cast<uint64_t>(cb) >> 6]
+                                                       : ~0ull);
+        }
+        if (kL2) {
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            const bool in = (admitted >> j) & 1ull;
+            const float xn = in ? a.xnorm2[cb + j] : 0.0f;
+            v[j] = in ? fmaf(-2.0f * inv, v[j], qn + xn) : kInfF;
+          }
+          group_best8<false>(v, best, top);
+        } else {
+          if (admitted != ~0ull) {
+#pragma unroll
+            for (int j = 0; j < 64; ++j)
+              if (!((admitted >> j) & 1ull)) v[j] = -kInfF;
+          }
+          group_best8<true>(v, best, top);
+        }
+      };
+      auto screen = [&](const float (&best)[8], float top, int64_t cb) {
+        const bool may = active && screen_value<kL2>(top, inv) <= thr;
+        if (!__any_sync(0xffffffffu, may)) return;
+        uint32_t gm = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          gm |= (may && screen_value<kL2>(best[j], inv) <= thr) ? (1u << j) : 0u;
+        if (__any_sync(0xffffffffu, cnt + __popc(gm) > cap)) {
+          compact_wide(ld, lr, kk, cnt, thr);
+          if (active) atomicMin(a.thr_bits + q, dev::ordered_bits(thr));
+          uint32_t keep = 0;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            keep |= (screen_value<kL2>(best[j], inv) <= thr) ? (1u << j) : 0u;
+          gm &= keep;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if ((gm >> j) & 1u) {
+            const int pos = cnt + __popc(gm & ((1u << j) - 1u));
+            ld[pos * kLS] = screen_value<kL2>(best[j], inv);
+            lr[pos * kLS] = static_cast<uint32_t>(cb / kTcGroupRows + j);
+          }
+        }
+        const int np = __popc(gm);
+        cnt += np;
+        seen += np;
+      };
+      uint32_t ra[64], rb[64];
+      unsigned fresh = ~0u;
+      for (int t = 0; t < ntiles; ++t, ++g) {
+        const int slot = g & 1;
+        const int64_t row0 = r0 + static_cast<int64_t>(t) * kN;
+        if ((t & 7) == 0 && active) fresh = *reinterpret_cast<const volatile unsigned*>(qthr);
+        ok = mbar_wait(bar(ACC_FULL + slot), (g >> 1) & 1, abort_flag, a.err, a.wait_cycles);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t taddr =
+            tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(slot * kN);
+        tmem_ld64_issue(taddr, ra);
+        tmem_ld64_issue(taddr + 64, rb);
+        tmem_wait_ld(ra);
+        tmem_hold(rb);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(ACC_EMPTY + slot));
+        float best_a[8], best_b[8], top_a, top_b;
+        tree(ra, row0, best_a, top_a);
+        tree(rb, row0 + 64, best_b, top_b);
+        screen(best_a, top_a, row0);
+        screen(best_b, top_b, row0 + 64);
+        if ((t & 7) == 7) thr = fminf(thr, dev::from_ordered_bits(fresh));
+      }
+      if (!ok) break;
+      compact_wide(ld, lr, kk, cnt, thr);
+      cnt = min(seen, kk);
+      if (active) {
+        const size_t slot = static_cast<size_t>(q) * a.n_chunks + chunk;
+        for (int i = 0; i < cnt; ++i) {
+          a.cand_d[slot * kk + i] = ld[i * kLS];
+          a.cand_r[slot * kk + i] = lr[i * kLS];
+        }
+        a.cand_n[slot] = cnt;
+        if (cnt == kk) atomicMin(a.thr_bits + q, dev::ordered_bits(ld[(kk - 1) * kLS]));
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"(kAcc * kN));
+  }
+}
+
+}  // namespace tcw
+
+// ---- host side ------------------------------------------------------------------------------------
+
+bool flat_tc_wide_fits(const FlatState& s, size_t k) {
+  const size_t kpad = std::max<size_t>(64, ceil_div(s.dim, 16) * 16);
+  return ceil_div(kpad, tc::kAtomK) <= static_cast<size_t>(tcw::kMaxAtoms) && k + 8 <= 128;
+}
+
+int flat_tc_wide_kk(size_t k) { return static_cast<int>(ceil_div(k + 8, 16) * 16); }
+
+size_t flat_tc_wide_list_bytes(const FlatState& s, int kk) {
+  return static_cast<size_t>(sm_count(s.device)) * (kk + tcw::kAppend) * tcw::kLS * 8;
+}
+
+void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t nq,
+                         const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, int kk,
+                         float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits,
+                         float* eps, int* err, const CUtensorMap& mq, const float* qinv,
+                         const float* qn2, void* lists, cudaStream_t st) {
+  QV_REQUIRE(kk % 16 == 0 && kk <= 128, "wide tensor-core screen: unsupported best-list length");
+  const int kpad = static_cast<int>(s.kpad);
+  const int atoms = static_cast<int>(ceil_div(static_cast<size_t>(kpad), tc::kAtomK));
+  QV_REQUIRE(atoms <= tcw::kMaxAtoms, "wide tensor-core screen: rows wider than 768");
+  const CUtensorMap mx = tc::make_map(s.x16.get(), s.n, kpad);
+  tcw::Args a{};
+  a.nq = static_cast<int>(nq);
+  a.n_qtiles = static_cast<int>(ceil_div(nq, tc::kM));
+  a.n_chunks = n_chunks;
+  a.total_units = a.n_qtiles * n_chunks;
+  a.atoms = atoms;
+  a.kk = kk;
+  a.nrows = static_cast<int64_t>(s.n);
+  a.chunk_rows = chunk_rows;
+  a.qscale_inv = qinv;
+  a.qnorm2 = qn2;
+  a.xnorm2 = s.xnorm2.get<float>();
+  a.bitmap = d_bitmap;
+  a.cand_d = cand_d;
+  a.cand_r = cand_r;
+  a.cand_n = cand_n;
+  a.thr_bits = thr_bits;
+  a.list_d = static_cast<float*>(lists);
+  const int grid = std::min(a.total_units, sm_count(s.device));
+  a.list_r = reinterpret_cast<uint32_t*>(static_cast<float*>(lists) +
+                                         static_cast<size_t>(grid) * (kk + tcw::kAppend) * tcw::kLS);
+  a.err = err;
+  a.wait_cycles = tc::wait_limit_cycles();
+  a.drain_ns = tc::kTimeoutNs;
+  // Shared memory: the query tile, as many 16 KB stages as fit (2 at kpad 768), barriers.
+  constexpr size_t kSmemMax = 227 * 1024 - 1024;  // per block, less the kernel's static part
+  const size_t fixed = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes + 256;
+  const int stages = static_cast<int>(std::min<size_t>(tcw::kMaxStages,
+                                                        (kSmemMax - fixed) / tc::kAtomBytes));
+  QV_REQUIRE(stages >= 2, "wide tensor-core screen: no room for two row stages");
+  a.stages = stages;
+  const size_t smem = fixed + static_cast<size_t>(stages) * tc::kAtomBytes;
+  KernelTimer timer(st, "flat_screen_tc_wide_kernel",
+                    2.0 * nq * static_cast<double>(s.n) * s.dim, false);
+  auto kernel = s.metric == QV_METRIC_L2 ? tcw::flat_screen_tc_wide_kernel<true>
+                                          : tcw::flat_screen_tc_wide_kernel<false>;
+  QV_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kernel<<<grid, tcw::kThreads, smem, st>>>(mq, mx, a);
+  timer.stop();
+  check_launch("flat_screen_tc_wide_kernel");
+  (void)eps;
+}
+
+}  // namespace qv

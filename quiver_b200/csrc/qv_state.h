@@ -68,8 +68,14 @@ void flat_search_noalloc(const FlatState& s, const float* d_queries, size_t nq, 
 size_t flat_noalloc_max_bytes();
 // The tensor-core screen's candidates are groups of this many consecutive rows.
 constexpr int kTcGroupRows = 8;
+// The tensor-core screen applies (flat_tc_eligible); the wide variant (dim > 128 or k > 24)
+// handles it (flat_tc_is_wide); best-list length in 8-row groups (flat_tc_kk).
 bool flat_tc_eligible(const FlatState& s, size_t k);
-int flat_tc_kk(size_t k);
+bool flat_tc_is_wide(const FlatState& s, size_t k);
+int flat_tc_kk(const FlatState& s, size_t k);
+bool flat_tc_wide_fits(const FlatState& s, size_t k);
+int flat_tc_wide_kk(size_t k);
+size_t flat_tc_wide_list_bytes(const FlatState& s, int kk);
 void flat_tc_prepare(FlatState& s, cudaStream_t st);
 // Device scratch the tensor-core screen needs for nq queries with best lists of kk.
 size_t flat_tc_scratch_bytes(const FlatState& s, size_t nq, int kk);

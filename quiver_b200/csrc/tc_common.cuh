@@ -213,4 +213,13 @@ long long wait_limit_cycles();
 CUtensorMap make_map(const void* base, uint64_t rows, uint64_t kpad);
 
 }  // namespace tc
+
+// The wide screen (flat_tc_wide.cu): rows up to 768 columns, best lists up to 128 groups. mq is
+// the queries' tensor map; qinv / qn2 as the screen in flat_tc.cu computes them; lists is
+// flat_tc_wide_list_bytes of scratch.
+void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t nq,
+                         const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, int kk,
+                         float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits,
+                         float* eps, int* err, const CUtensorMap& mq, const float* qinv,
+                         const float* qn2, void* lists, cudaStream_t st);
 }  // namespace qv
