@@ -57,7 +57,7 @@ def parse():
                     help="database rows (default: the workload's 1,183,514; smaller for "
                          "profiling)")
     ap.add_argument("--queries", type=int, default=N_Q, help="queries per batch (default 10,000)")
-    ap.add_argument("--workload", choices=["c1", "c2", "c3"], default="c1")
+    ap.add_argument("--workload", choices=["c1", "c2", "c3", "c4"], default="c1")
     ap.add_argument("--nprobe", type=int, default=64, help="IVF-PQ workloads: lists probed")
     ap.add_argument("--filter", action="store_true", help="IVF-PQ workloads: 1%% allowed ids")
     ap.add_argument("--shard", choices=["rows", "queries"], default="queries",
@@ -298,6 +298,7 @@ def run_reference_arm(args, rank, world):
     except OSError as e:
         print(json.dumps({"impl": "reference", "unavailable": f"oracle/_ref not loadable: {e}"}))
         return
+    scale = 1.0  # the reference scans a row sample; QPS scales linearly to the whole collection
     if args.workload == "c1":
         from quiver_b200.synthetic import config1
         db, q = config1(args.rows, args.queries)
@@ -306,6 +307,19 @@ def run_reference_arm(args, rank, world):
         f.add(db)
         search = lambda qs: f.search(qs, K)  # noqa: E731
         what = "FlatIndex::search_batch"
+    elif args.workload == "c4":
+        from quiver_b200.synthetic import C4_ROWS, config4_chunk
+        rows = C4_ROWS if args.rows == N_DB else args.rows
+        sample_rows = min(200_000, rows)
+        db = config4_chunk(sample_rows, 0)
+        q = config4_chunk(4096, 63)
+        config = c4_config(args, rows)
+        f = ref.flat(768, "ip")
+        f.add(db)
+        search = lambda qs: f.search(qs, C4_K)  # noqa: E731
+        scale = sample_rows / rows
+        what = (f"FlatIndex::search_batch over a {sample_rows:,}-row sample of the {rows:,} rows, "
+                f"QPS scaled by the row ratio")
     else:
         db, q = ivf_data(args.workload)
         q = q[:args.queries]
@@ -330,19 +344,146 @@ def run_reference_arm(args, rank, world):
         search(q[lo:lo + per_step])
         times.append(time.perf_counter() - t0)
     step_s = statistics.mean(times)
-    qps = per_step / step_s
+    qps = per_step / step_s * scale
     sample = (f"{per_step} of the {n_q:,} queries per step against the full {len(db):,}-row "
               f"database, {what}, {ref.threads} threads, ISA {ref.isa}")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": qps, "unit": "QPS",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * step_s, "queries_per_step": per_step, "higher_is_better": True,
+        "ms_per_step": 1000.0 * step_s, "queries_per_step": per_step,
+        "rows_per_step": len(db), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config, "parallelism": f"{ref.threads} host threads (reference thread pool)",
         "cpu_baseline": {"value": qps, "unit": "QPS", "cores": ref.threads, "kind": "reference",
                          "sample": sample},
         "e2e": {"value": qps, "unit": "QPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
+
+
+C4_Q, C4_K = 16_384, 100
+C4_DESC = ("FlatIndex inner product k=100, 40,000,000 x 768 Gaussian-mixture rows "
+           "(4,096 components), 16,384-query batches")
+
+
+def c4_config(args, rows) -> dict:
+    return {"workload": C4_DESC if rows == 40_000_000 else
+            f"FlatIndex inner product k=100, {rows:,} x 768 Gaussian-mixture rows (reduced), "
+            f"{C4_Q:,}-query batches",
+            "global_batch": C4_Q, "k": C4_K, "database_rows": rows, "dim": 768, "metric": "ip",
+            "l2": "inputs larger than L2 (the fp16 rows of a shard are read once per pass)"}
+
+
+def run_c4(args, rank, world, local):
+    """The 40M x 768 inner-product collection, id-range sharded (rank r holds rows
+    [r*N/W, (r+1)*N/W), generated on its GPU), every rank searching the whole 16,384-query batch
+    with the tensor-core screen, one packed NCCL all-gather and a device merge per step."""
+    import torch
+    import torch.distributed as dist
+    import quiver_b200 as qv
+    from quiver_b200 import _native
+    from quiver_b200.distributed import ShardedFlatIndex, shard_range
+    from quiver_b200.synthetic import C4_ROWS, config4_device
+
+    rows = C4_ROWS if args.rows == N_DB else args.rows
+    lo, hi = shard_range(rows, rank, world)
+    dev = torch.device(f"cuda:{local}")
+    index = ShardedFlatIndex(768, "ip", device=local)
+    index.local.reserve(hi - lo)
+    for first, x in config4_device(lo, hi, dev):
+        index.add_range_device(x, first)
+        del x
+    q = next(config4_device(0, C4_Q, dev, queries=True))[1]
+    torch.cuda.empty_cache()
+    q_host = q.cpu().pin_memory().numpy()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        index.search_device(q, C4_K)
+    torch.cuda.synchronize()
+    _native.set_timing(True)
+    qv.last_search_stats()
+    sampler = ClockSampler(local)
+    sampler.start()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        index.search_device(q, C4_K)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop()
+    st = qv.last_search_stats()
+    _native.set_timing(False)
+    elapsed = e0.elapsed_time(e1)
+    launches, rescans = st["kernel_launches"], st["rescanned_queries"]
+    if world > 1:
+        t = torch.tensor([elapsed], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+        c = torch.tensor([launches, rescans], device=dev, dtype=torch.float64)
+        dist.all_reduce(c, op=dist.ReduceOp.SUM)
+        launches, rescans = int(c[0].item()), int(c[1].item())
+    value = C4_Q * args.steps / (elapsed / 1000.0)
+
+    for _ in range(max(1, args.warmup)):
+        index.search(q_host, C4_K)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        index.search(q_host, C4_K)
+    e2e_s = time.perf_counter() - t0
+    barrier()
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+
+    hbm, tflops, peak_kind = load_peaks()
+    avg_ms = st["dominant_kernel_ms"] / max(1, args.steps)
+    work = st["dominant_kernel_work"] / max(1, args.steps)
+    achieved = work / (avg_ms / 1000.0) / 1e12 if avg_ms else 0.0
+    line = {
+        "metric": METRIC, "value": value, "unit": "QPS", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": elapsed / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": c4_config(args, rows), "parallelism": f"id-range shards x{world}",
+        "gpu_launches": launches, "rescanned_queries": rescans,
+        "roofline": {"bound": "tensor", "kernel": st["dominant_kernel"], "achieved": achieved,
+                     "peak": tflops, "unit": "TFLOP/s", "frac": achieved / tflops,
+                     "peak_source": f"{peak_kind} bf16 dense (burst)", "traffic": None,
+                     "avg_launch_ms": avg_ms, "work_per_launch": work},
+        "clocks": clocks,
+        "e2e": {"value": C4_Q * args.steps / e2e_s, "unit": "QPS",
+                "h2d_bytes_per_step": world * C4_Q * 768 * 4,
+                "d2h_bytes_per_step": world * C4_Q * C4_K * (8 + 4)},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        # The reference on a bounded sample: 64 queries against the first 1,000,000 rows, scaled
+        # linearly to the whole collection (its scan is linear in rows).
+        from oracle.oracle import REF_SO, Reference
+        if os.path.exists(REF_SO):
+            ref = Reference()
+            sample_rows = min(1_000_000, hi - lo)
+            x0 = next(config4_device(0, sample_rows, dev))[1].cpu().numpy()
+            f = ref.flat(768, "ip")
+            f.add(x0)
+            f.search(q_host[:8], C4_K)
+            t0 = time.perf_counter()
+            f.search(q_host[:64], C4_K)
+            dt = time.perf_counter() - t0
+            line["cpu_baseline"] = {
+                "value": 64 / dt * sample_rows / rows, "unit": "QPS", "cores": ref.threads,
+                "kind": "reference",
+                "sample": f"64 queries against the first {sample_rows:,} rows with "
+                          f"FlatIndex::search_batch ({ref.threads} threads, ISA {ref.isa}), "
+                          f"scaled by {sample_rows:,} / {rows:,} rows"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
 
 
 def run_ivf(args, rank, world, local):
@@ -468,6 +609,11 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device(f"cuda:{local}"))
+    if args.workload == "c4":
+        run_c4(args, rank, world, local)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     if args.workload != "c1":
         run_ivf(args, rank, world, local)
         if world > 1:

@@ -89,6 +89,16 @@ qv_status qv_flat_destroy(qv_flat* index);
  * NULL (row i gets label size()+i). Cosine rows are normalized on the GPU exactly as
  * simd::normalize does it. */
 qv_status qv_flat_add(qv_flat* index, const float* vectors, size_t n, const uint64_t* labels);
+/* Large collections (no counterpart in the reference, whose rows live in a growing std::vector):
+ * qv_flat_reserve sizes the row storage for n rows at once (an add past the capacity otherwise
+ * grows it by half and copies, which needs both copies on the GPU at once), and
+ * qv_flat_add_device appends n rows that are already in device memory on the index's GPU
+ * (vectors row-major, labels NULL or n device labels), with add()'s checks done on the device,
+ * so a collection larger than host memory can be built chunk by chunk. It returns with the rows
+ * resident, like add(). */
+qv_status qv_flat_reserve(qv_flat* index, size_t n);
+qv_status qv_flat_add_device(qv_flat* index, const float* vectors, size_t n,
+                             const uint64_t* labels, void* stream);
 /* search_batch(queries, nq, k, labels, distances, filter, pool): include/quiver/flat_index.h:34-36
  * (src/flat_index.cc:126-140). Writes nq*k results, closest first. */
 qv_status qv_flat_search(const qv_flat* index, const float* queries, size_t nq, size_t k,

@@ -120,6 +120,25 @@ class FlatIndex:
         la = _as_labels(labels, x.shape[0])
         check(lib().qv_flat_add(self._h, ptr(x), x.shape[0], ptr(la)))
 
+    def reserve(self, n: int) -> None:
+        """Sizes the GPU row storage for n rows at once (no counterpart in the reference)."""
+        check(lib().qv_flat_reserve(self._h, int(n)))
+
+    def add_device(self, vectors, labels=None, stream=None) -> None:
+        """Appends rows already in GPU memory: ``vectors`` a contiguous float32 CUDA tensor
+        [n, dim] on this index's device, ``labels`` None or a contiguous int64 CUDA tensor [n];
+        the same checks and results as :meth:`add` (no counterpart in the reference)."""
+        if vectors.dim() != 2 or vectors.shape[1] != self.dim or not vectors.is_contiguous():
+            raise ValueError(f"expected a contiguous [n, {self.dim}] tensor")
+        n = int(vectors.shape[0])
+        lp = None
+        if labels is not None:
+            if labels.numel() != n or not labels.is_contiguous():
+                raise ValueError("labels must be a contiguous tensor of n entries")
+            lp = labels.data_ptr()
+        check(lib().qv_flat_add_device(self._h, vectors.data_ptr(), n, lp,
+                                       C.c_void_p(stream) if stream else None))
+
     def search(self, queries: ArrayLike, k: int = 10, filter: Optional[ArrayLike] = None,
                num_threads: int = 0) -> Tuple[np.ndarray, np.ndarray]:
         """k-NN search. Returns (labels int64 [nq, k], distances float32 [nq, k]).

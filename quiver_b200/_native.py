@@ -52,6 +52,8 @@ _SIGNATURES = {
     "qv_flat_create": (_int, [_int, _sz, _u32, _PP]),
     "qv_flat_destroy": (_int, [_vp]),
     "qv_flat_add": (_int, [_vp, _vp, _sz, _vp]),
+    "qv_flat_reserve": (_int, [_vp, _sz]),
+    "qv_flat_add_device": (_int, [_vp, _vp, _sz, _vp, _vp]),
     "qv_flat_search": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _vp]),
     "qv_flat_search_device": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp, _vp]),
     "qv_flat_set_row_offset": (_int, [_vp, _u64]),

@@ -559,6 +559,57 @@ qv_status qv_flat_add(qv_flat* index, const float* vectors, size_t n, const uint
   });
 }
 
+qv_status qv_flat_reserve(qv_flat* index, size_t n) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr, "null index");
+    FlatState& s = index->s;
+    QV_REQUIRE(n <= std::numeric_limits<uint32_t>::max(), "FlatIndex holds at most 2^32 vectors");
+    std::unique_lock lock(index->mu);
+    DeviceScope scope(s.device);
+    flat_reserve(s, n, thread_stream(s.device));
+  });
+}
+
+qv_status qv_flat_add_device(qv_flat* index, const float* vectors, size_t n,
+                             const uint64_t* labels, void* stream) {
+  return guarded([&] {
+    QV_REQUIRE(index != nullptr, "null index");
+    if (n == 0) return;  // src/flat_index.cc:50
+    QV_REQUIRE(vectors != nullptr, "vectors must not be null");
+    FlatState& s = index->s;
+    std::unique_lock lock(index->mu);
+    QV_REQUIRE(s.n + n <= std::numeric_limits<uint32_t>::max(),
+               "FlatIndex holds at most 2^32 vectors");
+    DeviceScope scope(s.device);
+    CallerStream call_stream(stream, s.device);
+    cudaStream_t st = call_stream.get();
+    // The reference's checks (src/flat_index.cc:51-57), on the device, before the index changes.
+    DeviceBuffer flags(2 * sizeof(int), st);
+    QV_CUDA(cudaMemsetAsync(flags.get(), 0, 2 * sizeof(int), st));
+    flat_check_rows(vectors, n * s.dim, labels, n, flags.get<int>(), st);
+    int h[2] = {0, 0};
+    QV_CUDA(cudaMemcpyAsync(h, flags.get(), sizeof(h), cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaStreamSynchronize(st));
+    QV_REQUIRE(h[0] == 0, "vectors must not contain NaN or infinity");
+    QV_REQUIRE(h[1] == 0, "label 2^64-1 is reserved (it marks empty result slots)");
+    flat_reserve(s, s.n + n, st);
+    float* dst = s.x.get<float>() + s.n * s.dim;
+    QV_CUDA(cudaMemcpyAsync(dst, vectors, n * s.dim * sizeof(float), cudaMemcpyDeviceToDevice, st));
+    DeviceBuffer dl(n * sizeof(uint64_t), st);
+    if (labels != nullptr) {
+      QV_CUDA(cudaMemcpyAsync(dl.get(), labels, n * sizeof(uint64_t), cudaMemcpyDeviceToDevice, st));
+    } else {
+      sequential_labels(dl.get<uint64_t>(), n, s.n, st);
+    }
+    const size_t first = s.host_labels.size();
+    s.host_labels.resize(first + n);
+    QV_CUDA(cudaMemcpyAsync(s.host_labels.data() + first, dl.get(), n * sizeof(uint64_t),
+                            cudaMemcpyDeviceToHost, st));
+    flat_append(s, dst, dl.get<uint64_t>(), n, st);  // normalizes cosine rows; waits for the GPU
+    QV_CUDA(cudaStreamSynchronize(st));
+  });
+}
+
 qv_status qv_flat_search(const qv_flat* index, const float* queries, size_t nq, size_t k,
                          const qv_filter* filter, uint64_t* labels, float* distances) {
   return guarded([&] {

@@ -837,6 +837,43 @@ void normalize_rows_device(float* d_x, size_t n, size_t dim, cudaStream_t st) {
   check_launch("normalize_rows_kernel");
 }
 
+namespace {
+// flags[0] = some value is NaN or infinite; flags[1] = some label is the reserved 2^64-1.
+__global__ void check_rows_kernel(const float* __restrict__ x, size_t count,
+                                  const uint64_t* __restrict__ labels, size_t n, int* flags) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const size_t i0 = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  bool bad = false;
+  for (size_t i = i0; i < count; i += stride)
+    bad |= (__float_as_uint(x[i]) & 0x7f800000u) == 0x7f800000u;
+  if (__any_sync(kFull, bad) && (threadIdx.x & 31) == 0) atomicOr(flags, 1);
+  bool bad_label = false;
+  if (labels != nullptr)
+    for (size_t i = i0; i < n; i += stride) bad_label |= labels[i] == kInvalidLabel;
+  if (__any_sync(kFull, bad_label) && (threadIdx.x & 31) == 0) atomicOr(flags + 1, 1);
+}
+
+__global__ void sequential_labels_kernel(uint64_t* out, size_t n, uint64_t first) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n; i += stride)
+    out[i] = first + i;
+}
+}  // namespace
+
+void flat_check_rows(const float* d_x, size_t count, const uint64_t* d_labels, size_t n,
+                     int* d_flags, cudaStream_t st) {
+  const unsigned grid =
+      static_cast<unsigned>(std::min<size_t>(ceil_div(std::max(count, n), 256), 16384));
+  check_rows_kernel<<<std::max(grid, 1u), 256, 0, st>>>(d_x, count, d_labels, n, d_flags);
+  check_launch("check_rows_kernel");
+}
+
+void sequential_labels(uint64_t* d_out, size_t n, uint64_t first, cudaStream_t st) {
+  const unsigned grid = static_cast<unsigned>(std::min<size_t>(ceil_div(n, 256), 16384));
+  sequential_labels_kernel<<<std::max(grid, 1u), 256, 0, st>>>(d_out, n, first);
+  check_launch("sequential_labels_kernel");
+}
+
 void flat_reserve(FlatState& s, size_t rows, cudaStream_t st) {
   if (rows <= s.cap) return;
   size_t cap = std::max<size_t>(rows, s.cap + s.cap / 2);

@@ -85,6 +85,12 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
                     int* err, void* scratch, cudaStream_t st);
 
 void flat_reserve(FlatState& s, size_t rows, cudaStream_t st);
+// Device-side input checks for an add from device memory: d_flags[0] is set when a value is NaN
+// or infinite, d_flags[1] when a label is 2^64-1 (d_labels may be null).
+void flat_check_rows(const float* d_x, size_t count, const uint64_t* d_labels, size_t n,
+                     int* d_flags, cudaStream_t st);
+// d_out[i] = first + i.
+void sequential_labels(uint64_t* d_out, size_t n, uint64_t first, cudaStream_t st);
 // Appends n rows (device pointer, row-major) with labels (device pointer).
 void flat_append(FlatState& s, const float* d_rows, const uint64_t* d_labels, size_t n,
                  cudaStream_t st);

@@ -102,6 +102,7 @@ class ShardedFlatIndex:
         self.local = FlatIndex(dim, metric, device=self.device)
         self.ntotal = 0
         self._gid = torch.empty(0, dtype=torch.int64, device=f"cuda:{self.device}")
+        self._range = None  # [first, end) when rows were added by add_range_device
 
     @property
     def dim(self) -> int:
@@ -118,8 +119,27 @@ class ShardedFlatIndex:
         self.add_shard(x[lo:hi], mine, gids)
         self.ntotal += n
 
+    def add_range_device(self, vectors: torch.Tensor, first_id: int) -> None:
+        """Appends rows already on this rank's GPU whose global ids, and labels, are first_id,
+        first_id + 1, ...: consecutive calls extend one contiguous id range (this rank's shard).
+        The index then reports global row ids as its keys itself (no per-row id table), so a
+        shard of tens of millions of rows needs no host copy."""
+        n = int(vectors.shape[0])
+        if self._range is None:
+            if len(self.local) != 0:
+                raise ValueError("add_range_device cannot follow add_shard")
+            check(lib().qv_flat_set_row_offset(self.local.handle, int(first_id)))
+            self._range = [int(first_id), int(first_id)]
+        if int(first_id) != self._range[1]:
+            raise ValueError(f"rows must extend the id range [{self._range[0]}, {self._range[1]})")
+        ids = torch.arange(first_id, first_id + n, dtype=torch.int64, device=vectors.device)
+        self.local.add_device(vectors, ids)
+        self._range[1] += n
+
     def add_shard(self, vectors, labels, global_ids) -> None:
         """Appends this rank's rows directly (labels and global row ids given per row)."""
+        if self._range is not None:
+            raise ValueError("add_shard cannot follow add_range_device")
         self.local.add(vectors, labels)
         g = torch.as_tensor(np.ascontiguousarray(global_ids, dtype=np.int64),
                             device=self._gid.device)
@@ -137,8 +157,11 @@ class ShardedFlatIndex:
                                           C.c_void_p(_stream_ptr())))
         if self.world == 1:
             return d, lab
-        valid = key >= 0  # unfilled slots carry key 2^64-1 (-1 as int64)
-        gkey = torch.where(valid, self._gid[key.clamp(min=0)], key)
+        if self._range is not None:
+            gkey = key  # the index's row offset already made the keys global ids
+        else:
+            valid = key >= 0  # unfilled slots carry key 2^64-1 (-1 as int64)
+            gkey = torch.where(valid, self._gid[key.clamp(min=0)], key)
         od, _, ol = _merge(*_all_gather_triples(d, gkey, lab, self.world, self.group), k,
                            self.device)
         return od, ol

@@ -85,3 +85,42 @@ def config4_chunk(rows: int, chunk_index: int, dim: int = 768):
     seed = np.random.SeedSequence(4).spawn(64)[chunk_index]
     return mixture(rows, dim, 4096, 0.5, 1.0 / np.sqrt(dim), centre_seed=44,
                    seed=int(seed.generate_state(1)[0]), sigma_from_centre_norm=True)
+
+
+C4_ROWS, C4_DIM, C4_COMPONENTS = 40_000_000, 768, 4096
+C4_CHUNK = 1_000_000  # rows per generation chunk; shard boundaries of 1/2/4/8 ranks fall on them
+
+
+def config4_centres(dim: int = C4_DIM):
+    """Config 4's mixture centres N(0, 1/dim) and per-component sigma 0.5 * ||centre|| (numpy)."""
+    rc = np.random.default_rng(44)
+    centres = (rc.standard_normal((C4_COMPONENTS, dim)) / np.sqrt(dim)).astype(np.float32)
+    return centres, (0.5 * np.linalg.norm(centres, axis=1)).astype(np.float32)
+
+
+def config4_device(first: int, end: int, device, queries: bool = False):
+    """Config 4 rows [first, end) generated on a CUDA device in chunks of C4_CHUNK rows, yielded
+    as (first id, float32 tensor [rows, 768]), L2-normalized. Each chunk's values depend only on
+    its global position (a generator seeded per chunk), so every sharding of the 40M rows sees
+    the same collection. ``queries``: the query stream instead (another seed family)."""
+    import torch
+    centres, sig = config4_centres()
+    c = torch.from_numpy(centres).to(device)
+    s = torch.from_numpy(sig).to(device)
+    pos = first
+    while pos < end:
+        chunk = pos // C4_CHUNK
+        stop = min(end, (chunk + 1) * C4_CHUNK)
+        g = torch.Generator(device=device)
+        g.manual_seed((9_000_000 if queries else 4_000_000) + chunk)
+        # Draw the whole chunk, then keep the part in [pos, stop): the values of a row do not
+        # depend on which part of its chunk is requested.
+        full = C4_CHUNK
+        a = torch.randint(0, C4_COMPONENTS, (full,), generator=g, device=device)
+        x = torch.randn((full, C4_DIM), generator=g, device=device)
+        lo, hi = pos - chunk * C4_CHUNK, stop - chunk * C4_CHUNK
+        a, x = a[lo:hi], x[lo:hi]
+        x.mul_(s[a, None]).add_(c[a])
+        x.div_(torch.linalg.vector_norm(x, dim=1, keepdim=True))
+        yield pos, x.contiguous()
+        pos = stop

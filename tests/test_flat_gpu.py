@@ -225,3 +225,36 @@ def test_device_searches_are_asynchronous_and_ordered(gpu, oracle):
         wl, wd = oracle.flat_search(stored, ids, "cosine", q[good], 10)
         assert_topk_parity(l[good], d[good], wl, wd, exact=True, what=f"async batch {i}")
         assert (l[~good] == -1).all() and np.isnan(d[~good]).all()
+
+
+def test_add_from_device_memory_equals_host_add(gpu):
+    """reserve + add_device (rows already on the GPU, added in chunks) store exactly what add()
+    stores, search identically, and reject NaN values and the reserved label as add() does."""
+    import torch
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((5000, 72)).astype(np.float32)
+    labels = rng.permutation(5000).astype(np.uint64) * 3
+    host = gpu.FlatIndex(72, "cosine")
+    host.add(x, labels)
+    dev = gpu.FlatIndex(72, "cosine")
+    dev.reserve(5000)
+    dx = torch.from_numpy(x).cuda()
+    dl = torch.from_numpy(labels.astype(np.int64)).cuda()
+    dev.add_device(dx[:1234], dl[:1234])
+    dev.add_device(dx[1234:], dl[1234:])
+    hv, hl = host.rows()
+    dv, dlab = dev.rows()
+    assert np.array_equal(hv, dv) and np.array_equal(hl, dlab)
+    q = rng.standard_normal((50, 72)).astype(np.float32)
+    a, b = host.search(q, 10), dev.search(q, 10)
+    assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+    seq = gpu.FlatIndex(72, "l2")
+    seq.add_device(dx[:10])  # no labels: size() + i
+    assert np.array_equal(seq.rows()[1], np.arange(10, dtype=np.uint64))
+    bad = dx[:4].clone()
+    bad[2, 3] = float("nan")
+    with pytest.raises(ValueError, match="NaN"):
+        dev.add_device(bad)
+    with pytest.raises(ValueError, match="2\\^64-1"):
+        dev.add_device(dx[:2], torch.tensor([1, -1], dtype=torch.int64, device="cuda"))
+    assert len(dev) == 5000  # a rejected add leaves the index unchanged
