@@ -696,7 +696,7 @@ CUtensorMap make_map(const void* base, uint64_t rows, uint64_t kpad) {
 // ---- host side ------------------------------------------------------------------------------------
 
 // The narrow screen (this file) takes dim <= 128 and k <= 24; the wide screen (flat_tc_wide.cu)
-// dim <= 768 and k <= 120.
+// dim <= 768 and k <= 204.
 bool flat_tc_is_wide(const FlatState& s, size_t k) {
   return s.dim > 128 || k + 8 > static_cast<size_t>(tc::kMaxKK);
 }

@@ -1,5 +1,5 @@
 // Tensor-core (tcgen05) screen for wide rows and large k: dimensions up to 768 (fp16 operands
-// padded to whole 64-column atoms) and best lists of up to 128 groups (k up to 120).
+// padded to whole 64-column atoms) and best lists of up to 256 groups (k up to 204).
 //
 // Same arithmetic and certificate as the screen in flat_tc.cu (fp16 MMA with float32
 // accumulation in TMEM, 8-row groups, per-query best lists, exact re-rank and certificate in
@@ -11,7 +11,7 @@
 //   * accumulator slots (128 columns each, two of them) are released by their own barrier,
 //     because a stage no longer covers a whole row tile;
 //   * best lists live in global memory (L2-resident, one region per CTA, entry i of query lane l
-//     at i * 128 + l, so a warp's accesses coalesce): 128 queries x up to 144 entries do not fit
+//     at i * 128 + l, so a warp's accesses coalesce): 128 queries x up to 272 entries do not fit
 //     next to the operands. A list is compacted (sorted, cut to its KK best) by merging 16-entry
 //     chunks in registers, which happens rarely once the query's threshold has settled.
 //
@@ -41,6 +41,7 @@ constexpr int kLS = kM;           // list stride: entry i of query lane l at i *
 constexpr int kAppend = 16;       // entries appended between compactions (two 64-column halves)
 constexpr int kMaxAtoms = 12;     // kpad <= 768
 constexpr int kMaxStages = 8;
+constexpr int kMaxKK = 256;       // longest best list (k up to 204)
 
 struct Args {
   int nq, n_qtiles, n_chunks, total_units, atoms, stages, kk;
@@ -413,12 +414,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---- host side ------------------------------------------------------------------------------------
 
-bool flat_tc_wide_fits(const FlatState& s, size_t k) {
-  const size_t kpad = std::max<size_t>(64, ceil_div(s.dim, 16) * 16);
-  return ceil_div(kpad, tc::kAtomK) <= static_cast<size_t>(tcw::kMaxAtoms) && k + 8 <= 128;
+// Best-list length of the wide screen: k plus a margin of max(8, k / 4) groups, in whole 16-entry
+// chunks. The certificate needs the list's last value to clear the k-th exact distance by the
+// screen's error bound; for large k over dense data (768-dim inner product, k = 100) the
+// distances near rank k are packed so closely that a margin of 8 left about one query in eight
+// uncertified, while k / 4 clears it by several error bounds.
+int flat_tc_wide_kk(size_t k) {
+  return static_cast<int>(ceil_div(k + std::max<size_t>(8, (k + 3) / 4), 16) * 16);
 }
 
-int flat_tc_wide_kk(size_t k) { return static_cast<int>(ceil_div(k + 8, 16) * 16); }
+bool flat_tc_wide_fits(const FlatState& s, size_t k) {
+  const size_t kpad = std::max<size_t>(64, ceil_div(s.dim, 16) * 16);
+  return ceil_div(kpad, tc::kAtomK) <= static_cast<size_t>(tcw::kMaxAtoms) &&
+         flat_tc_wide_kk(k) <= tcw::kMaxKK;
+}
 
 size_t flat_tc_wide_list_bytes(const FlatState& s, int kk) {
   return static_cast<size_t>(sm_count(s.device)) * (kk + tcw::kAppend) * tcw::kLS * 8;
@@ -429,7 +438,8 @@ void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t n
                          float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits,
                          float* eps, int* err, const CUtensorMap& mq, const float* qinv,
                          const float* qn2, void* lists, cudaStream_t st) {
-  QV_REQUIRE(kk % 16 == 0 && kk <= 128, "wide tensor-core screen: unsupported best-list length");
+  QV_REQUIRE(kk % 16 == 0 && kk <= tcw::kMaxKK,
+             "wide tensor-core screen: unsupported best-list length");
   const int kpad = static_cast<int>(s.kpad);
   const int atoms = static_cast<int>(ceil_div(static_cast<size_t>(kpad), tc::kAtomK));
   QV_REQUIRE(atoms <= tcw::kMaxAtoms, "wide tensor-core screen: rows wider than 768");
