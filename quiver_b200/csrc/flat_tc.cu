@@ -808,7 +808,7 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   if (wide) {
     const CUtensorMap mq = tc::make_map(q16, nq_pad, kpad);
     flat_screen_tc_wide(s, qp, dpad, nq, d_bitmap, n_chunks, chunk_rows, kk, cand_d, cand_r,
-                        cand_n, thr_bits, eps, err, mq, qinv, qn2, base + L.lists, st);
+                        cand_n, thr_bits, eps, err, mq, q16, qinv, qn2, base + L.lists, st);
     return;
   }
   tc::init_best_kernel<<<static_cast<unsigned>(std::min<size_t>(ceil_div(nq * kk, 256), 1024)),

@@ -4,10 +4,13 @@
 // Same arithmetic and certificate as the screen in flat_tc.cu (fp16 MMA with float32
 // accumulation in TMEM, 8-row groups, per-query best lists, exact re-rank and certificate in
 // flat.cu); what changes is the data movement, which the row width dictates:
-//   * one 128-query tile per unit (the tile's 128 x kpad fp16 operand, up to 192 KB, stays in
-//     shared memory for the whole unit), and row tiles streamed one 64-column K atom at a time
-//     through a ring of 16 KB stages, so a row tile is kAtoms stages and each stage feeds four
-//     128 x 128 x 16 MMAs;
+//   * one 128-query tile per unit, whose 128 x kpad fp16 operand (up to 192 KB) stays on chip for
+//     the whole unit: its first 512 columns in tensor memory (the 256 TMEM columns the two
+//     accumulator slots leave free; the epilogue warps store them there with tcgen05.st, and the
+//     MMAs read A from TMEM), the rest (columns 512..767) in shared memory. That leaves shared
+//     memory to a deep ring of 16 KB stages (10 at kpad 768) through which row tiles stream one
+//     64-column K atom at a time, enough copies in flight to cover L2 latency; a row tile is
+//     kAtoms stages and each stage feeds four 128 x 128 x 16 MMAs;
 //   * accumulator slots (128 columns each, two of them) are released by their own barrier,
 //     because a stage no longer covers a whole row tile;
 //   * best lists live in global memory (L2-resident, one region per CTA, entry i of query lane l
@@ -40,11 +43,16 @@ constexpr int kAcc = 2;           // accumulator slots of kN columns
 constexpr int kLS = kM;           // list stride: entry i of query lane l at i * kLS + l
 constexpr int kAppend = 16;       // entries appended between compactions (two 64-column halves)
 constexpr int kMaxAtoms = 12;     // kpad <= 768
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 12;
+constexpr int kTmemAtoms = 8;     // query-tile K atoms held in TMEM (columns 256..511)
+constexpr int kTmemCols = 512;
 constexpr int kMaxKK = 256;       // longest best list (k up to 204)
 
 struct Args {
   int nq, n_qtiles, n_chunks, total_units, atoms, stages, kk;
+  int a_tmem_atoms;         // leading K atoms of the query tile held in TMEM (the rest in smem)
+  int kpad;
+  const __half* q16;        // the queries' fp16 rows (kpad columns, zero rows past nq)
   int64_t nrows, chunk_rows;
   const float* qscale_inv;  // per query: 1 / (s_q * s_x)
   const float* qnorm2;      // per query ||q||^2 (L2)
@@ -135,18 +143,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  const int atoms = a.atoms, stages = a.stages, kk = a.kk;
-  unsigned char* smem_a = base;                         // atoms x 16 KB (the query tile)
-  unsigned char* smem_b = smem_a + atoms * kAtomBytes;  // stages x 16 KB (row-tile K atoms)
+  const int atoms = a.atoms, stages = a.stages, kk = a.kk, ta = a.a_tmem_atoms;
+  unsigned char* smem_a = base;  // atoms - ta atoms x 16 KB (the query tile past TMEM's part)
+  unsigned char* smem_b = smem_a + (atoms - ta) * kAtomBytes;  // stages x 16 KB (row-tile atoms)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + stages * kAtomBytes);
-  // bars: full[stages], empty[stages], acc_full[kAcc], acc_empty[kAcc], a_full, a_empty.
+  // bars: full[stages], empty[stages], acc_full[kAcc], acc_empty[kAcc], a_full (smem part of
+  // the query tile landed), a_empty (the unit's MMAs are done with the query tile), a_tfull
+  // (the epilogue warps stored the TMEM part).
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ int s_consumed;  // B fills the MMA issuer has waited for (abort drain)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int FULL = 0, EMPTY = stages, ACC_FULL = 2 * stages, ACC_EMPTY = 2 * stages + kAcc,
-            A_FULL = 2 * stages + 2 * kAcc, A_EMPTY = A_FULL + 1;
+            A_FULL = 2 * stages + 2 * kAcc, A_EMPTY = A_FULL + 1, A_TFULL = A_FULL + 2;
   auto bar = [&](int i) { return smem_u32(bars + i); };
 
   if (threadIdx.x == 0) {
@@ -162,12 +172,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(bar(A_FULL), 1);
     mbar_init(bar(A_EMPTY), 1);
+    mbar_init(bar(A_TFULL), kEpiWarps);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      smem_u32(&s_tmem)),
-                 "r"(kAcc * kN));
+                 "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -199,10 +210,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           a_phase ^= 1;
         }
         first = false;
-        mbar_expect_tx(bar(A_FULL), static_cast<uint32_t>(atoms * kAtomBytes));
-        for (int at = 0; at < atoms; ++at)
-          tma_load_2d(smem_u32(smem_a + at * kAtomBytes), &tmap_q, at * kAtomK, qtile * kM,
-                      bar(A_FULL));
+        // The query tile's atoms past the TMEM part (none when kpad <= 512: the arrival alone
+        // completes the phase).
+        mbar_expect_tx(bar(A_FULL), static_cast<uint32_t>((atoms - ta) * kAtomBytes));
+        for (int at = ta; at < atoms; ++at)
+          tma_load_2d(smem_u32(smem_a + (at - ta) * kAtomBytes), &tmap_q, at * kAtomK,
+                      qtile * kM, bar(A_FULL));
         for (int t = 0; t < ntiles && ok; ++t) {
           const int y = static_cast<int>(r0 + static_cast<int64_t>(t) * kN);
           for (int at = 0; at < atoms; ++at) {
@@ -243,9 +256,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         unit_rows(u, qtile, chunk, r0, r1);
         const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
         if (!mbar_wait(bar(A_FULL), a_phase, abort_flag, a.err, a.wait_cycles)) break;
+        if (!mbar_wait(bar(A_TFULL), a_phase, abort_flag, a.err, a.wait_cycles)) break;
         a_phase ^= 1;
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem_a);
+        const uint32_t a_tmem = tmem_base + static_cast<uint32_t>(kAcc * kN);
         for (int t = 0; t < ntiles && ok; ++t, ++g) {
           const int slot = g & 1;
           // The slot's previous tile (g - 2) must have been read out by the epilogue.
@@ -260,11 +275,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             *reinterpret_cast<volatile int*>(&s_consumed) += 1;
             tc_fence_after();
             const uint32_t b_addr = smem_u32(smem_b + stage * kAtomBytes);
-            const uint32_t aa = a_addr + static_cast<uint32_t>(at * kAtomBytes);
+            if (at < ta) {  // A from TMEM: 64 fp16 per atom = 32 columns, 8 per K step
+              const uint32_t at_tmem = a_tmem + static_cast<uint32_t>(at * 32);
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks)
-              umma_f16(d_tmem, smem_desc(aa + ks * 32), smem_desc(b_addr + ks * 32),
-                       (at | ks) != 0 ? 1u : 0u);
+              for (int ks = 0; ks < 4; ++ks)
+                umma_f16_ts(d_tmem, at_tmem + ks * 8, smem_desc(b_addr + ks * 32),
+                            (at | ks) != 0 ? 1u : 0u);
+            } else {
+              const uint32_t aa = a_addr + static_cast<uint32_t>((at - ta) * kAtomBytes);
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks)
+                umma_f16(d_tmem, smem_desc(aa + ks * 32), smem_desc(b_addr + ks * 32),
+                         (at | ks) != 0 ? 1u : 0u);
+            }
             umma_commit(bar(EMPTY + stage));  // the stage is free once these MMAs have read it
             if (++stage == stages) {
               stage = 0;
@@ -287,13 +310,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int cap = kk + kAppend;
     const float kInfF = __int_as_float(0x7f800000);
     int g = 0;
-    bool ok = true;
+    uint32_t a_phase = 0;
+    bool ok = true, first = true;
     for (int u = blockIdx.x; u < a.total_units && ok; u += gridDim.x) {
       int qtile, chunk;
       int64_t r0, r1;
       unit_rows(u, qtile, chunk, r0, r1);
       const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
       const int q = qtile * kM + qi;
+      // The query tile's first ta atoms into this warp's 32 TMEM lanes (columns 256 + 32 * atom),
+      // once the previous unit's MMAs have finished reading them.
+      if (!first) {
+        ok = mbar_wait(bar(A_EMPTY), a_phase, abort_flag, a.err, a.wait_cycles);
+        if (!ok) break;
+        a_phase ^= 1;
+        tc_fence_after();
+      }
+      first = false;
+      {
+        const uint4* row = reinterpret_cast<const uint4*>(
+            a.q16 + static_cast<size_t>(qtile * kM + qi) * a.kpad);
+        const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(kAcc * kN);
+        for (int at = 0; at < ta; ++at) {
+          uint32_t w[32];
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            const int h = at * kAtomK + v * 8;  // first fp16 element of this 16-byte piece
+            const uint4 x = h < a.kpad ? __ldg(row + h / 8) : make_uint4(0, 0, 0, 0);
+            w[4 * v] = x.x;
+            w[4 * v + 1] = x.y;
+            w[4 * v + 2] = x.z;
+            w[4 * v + 3] = x.w;
+          }
+          tmem_st32(tbase + static_cast<uint32_t>(at * 32), w);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(A_TFULL));
+      }
       const bool active = q < a.nq;
       const unsigned* qthr = a.thr_bits + (active ? q : 0);
       float thr = active ? dev::from_ordered_bits(*qthr) : -kInfF;
@@ -406,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   if (warp == 1) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(kAcc * kN));
+                 "r"(kTmemCols));
   }
 }
 
@@ -436,8 +492,8 @@ size_t flat_tc_wide_list_bytes(const FlatState& s, int kk) {
 void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t nq,
                          const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, int kk,
                          float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits,
-                         float* eps, int* err, const CUtensorMap& mq, const float* qinv,
-                         const float* qn2, void* lists, cudaStream_t st) {
+                         float* eps, int* err, const CUtensorMap& mq, const __half* q16,
+                         const float* qinv, const float* qn2, void* lists, cudaStream_t st) {
   QV_REQUIRE(kk % 16 == 0 && kk <= tcw::kMaxKK,
              "wide tensor-core screen: unsupported best-list length");
   const int kpad = static_cast<int>(s.kpad);
@@ -468,14 +524,20 @@ void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t n
   a.err = err;
   a.wait_cycles = tc::wait_limit_cycles();
   a.drain_ns = tc::kTimeoutNs;
-  // Shared memory: the query tile, as many 16 KB stages as fit (2 at kpad 768), barriers.
+  a.a_tmem_atoms = std::min(atoms, tcw::kTmemAtoms);
+  a.kpad = kpad;
+  a.q16 = q16;
+  // Shared memory: the query tile's atoms past TMEM's part, as many 16 KB stages as fit (10 at
+  // kpad 768), barriers; never less than half the SM's shared memory, so that one CTA (and its
+  // 512 TMEM columns) runs per SM.
   constexpr size_t kSmemMax = 227 * 1024 - 1024;  // per block, less the kernel's static part
-  const size_t fixed = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes + 256;
+  const size_t fixed = 1024 + static_cast<size_t>(atoms - a.a_tmem_atoms) * tc::kAtomBytes + 256;
   const int stages = static_cast<int>(std::min<size_t>(tcw::kMaxStages,
                                                         (kSmemMax - fixed) / tc::kAtomBytes));
   QV_REQUIRE(stages >= 2, "wide tensor-core screen: no room for two row stages");
   a.stages = stages;
-  const size_t smem = fixed + static_cast<size_t>(stages) * tc::kAtomBytes;
+  const size_t smem = std::max<size_t>(fixed + static_cast<size_t>(stages) * tc::kAtomBytes,
+                                       120 * 1024);
   KernelTimer timer(st, "flat_screen_tc_wide_kernel",
                     2.0 * nq * static_cast<double>(s.n) * s.dim, false);
   auto kernel = s.metric == QV_METRIC_L2 ? tcw::flat_screen_tc_wide_kernel<true>

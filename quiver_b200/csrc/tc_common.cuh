@@ -248,6 +248,6 @@ CUtensorMap make_map(const void* base, uint64_t rows, uint64_t kpad);
 void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t nq,
                          const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, int kk,
                          float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits,
-                         float* eps, int* err, const CUtensorMap& mq, const float* qinv,
-                         const float* qn2, void* lists, cudaStream_t st);
+                         float* eps, int* err, const CUtensorMap& mq, const __half* q16,
+                         const float* qinv, const float* qn2, void* lists, cudaStream_t st);
 }  // namespace qv
