@@ -27,6 +27,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "qv_state.h"
@@ -50,6 +51,7 @@ constexpr int kMaxKK = 256;       // longest best list (k up to 204)
 
 struct Args {
   int nq, n_qtiles, n_chunks, total_units, atoms, stages, kk;
+  int stage_atoms;          // K atoms of a row tile per ring stage (the tile's last may hold fewer)
   int a_tmem_atoms;         // leading K atoms of the query tile held in TMEM (the rest in smem)
   int kpad;
   const __half* q16;        // the queries' fp16 rows (kpad columns, zero rows past nq)
@@ -144,9 +146,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int atoms = a.atoms, stages = a.stages, kk = a.kk, ta = a.a_tmem_atoms;
+  const int sa = a.stage_atoms;
   unsigned char* smem_a = base;  // atoms - ta atoms x 16 KB (the query tile past TMEM's part)
-  unsigned char* smem_b = smem_a + (atoms - ta) * kAtomBytes;  // stages x 16 KB (row-tile atoms)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + stages * kAtomBytes);
+  unsigned char* smem_b = smem_a + (atoms - ta) * kAtomBytes;  // stages x sa x 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + stages * sa * kAtomBytes);
   // bars: full[stages], empty[stages], acc_full[kAcc], acc_empty[kAcc], a_full (smem part of
   // the query tile landed), a_empty (the unit's MMAs are done with the query tile), a_tfull
   // (the epilogue warps stored the TMEM part).
@@ -218,12 +221,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                       qtile * kM, bar(A_FULL));
         for (int t = 0; t < ntiles && ok; ++t) {
           const int y = static_cast<int>(r0 + static_cast<int64_t>(t) * kN);
-          for (int at = 0; at < atoms; ++at) {
+          for (int at0 = 0; at0 < atoms; at0 += sa) {
+            const int n_at = min(sa, atoms - at0);
             ok = mbar_wait(bar(EMPTY + stage), phase ^ 1, abort_flag, a.err, a.wait_cycles);
             if (!ok) break;
-            mbar_expect_tx(bar(FULL + stage), kAtomBytes);
-            tma_load_2d(smem_u32(smem_b + stage * kAtomBytes), &tmap_x, at * kAtomK, y,
-                        bar(FULL + stage));
+            mbar_expect_tx(bar(FULL + stage), static_cast<uint32_t>(n_at * kAtomBytes));
+            for (int i = 0; i < n_at; ++i)
+              tma_load_2d(smem_u32(smem_b + (stage * sa + i) * kAtomBytes), &tmap_x,
+                          (at0 + i) * kAtomK, y, bar(FULL + stage));
             ++issued;
             if (++stage == stages) {
               stage = 0;
@@ -269,24 +274,28 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * kN);
-          for (int at = 0; at < atoms; ++at) {
+          for (int at0 = 0; at0 < atoms; at0 += sa) {
+            const int n_at = min(sa, atoms - at0);
             ok = mbar_wait(bar(FULL + stage), phase, abort_flag, a.err, a.wait_cycles);
             if (!ok) break;
             *reinterpret_cast<volatile int*>(&s_consumed) += 1;
             tc_fence_after();
-            const uint32_t b_addr = smem_u32(smem_b + stage * kAtomBytes);
-            if (at < ta) {  // A from TMEM: 64 fp16 per atom = 32 columns, 8 per K step
-              const uint32_t at_tmem = a_tmem + static_cast<uint32_t>(at * 32);
+            for (int i = 0; i < n_at; ++i) {
+              const int at = at0 + i;
+              const uint32_t b_addr = smem_u32(smem_b + (stage * sa + i) * kAtomBytes);
+              if (at < ta) {  // A from TMEM: 64 fp16 per atom = 32 columns, 8 per K step
+                const uint32_t at_tmem = a_tmem + static_cast<uint32_t>(at * 32);
 #pragma unroll
-              for (int ks = 0; ks < 4; ++ks)
-                umma_f16_ts(d_tmem, at_tmem + ks * 8, smem_desc(b_addr + ks * 32),
-                            (at | ks) != 0 ? 1u : 0u);
-            } else {
-              const uint32_t aa = a_addr + static_cast<uint32_t>((at - ta) * kAtomBytes);
+                for (int ks = 0; ks < 4; ++ks)
+                  umma_f16_ts(d_tmem, at_tmem + ks * 8, smem_desc(b_addr + ks * 32),
+                              (at | ks) != 0 ? 1u : 0u);
+              } else {
+                const uint32_t aa = a_addr + static_cast<uint32_t>((at - ta) * kAtomBytes);
 #pragma unroll
-              for (int ks = 0; ks < 4; ++ks)
-                umma_f16(d_tmem, smem_desc(aa + ks * 32), smem_desc(b_addr + ks * 32),
-                         (at | ks) != 0 ? 1u : 0u);
+                for (int ks = 0; ks < 4; ++ks)
+                  umma_f16(d_tmem, smem_desc(aa + ks * 32), smem_desc(b_addr + ks * 32),
+                           (at | ks) != 0 ? 1u : 0u);
+              }
             }
             umma_commit(bar(EMPTY + stage));  // the stage is free once these MMAs have read it
             if (++stage == stages) {
@@ -532,12 +541,19 @@ void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t n
   // 512 TMEM columns) runs per SM.
   constexpr size_t kSmemMax = 227 * 1024 - 1024;  // per block, less the kernel's static part
   const size_t fixed = 1024 + static_cast<size_t>(atoms - a.a_tmem_atoms) * tc::kAtomBytes + 256;
-  const int stages = static_cast<int>(std::min<size_t>(tcw::kMaxStages,
-                                                        (kSmemMax - fixed) / tc::kAtomBytes));
+  const size_t room = (kSmemMax - fixed) / tc::kAtomBytes;  // 16 KB atoms the ring can hold
+  // Two atoms per stage (eight MMAs per barrier wait in the issuing thread) while that still
+  // leaves four stages; QV_TC_WIDE_STAGE_ATOMS (1..4) overrides, for tuning.
+  int sa = room >= 8 ? 2 : 1;
+  if (const char* e = std::getenv("QV_TC_WIDE_STAGE_ATOMS"); e != nullptr && *e != '\0')
+    sa = std::max(1, std::min(4, std::atoi(e)));
+  sa = std::min(sa, atoms);
+  const int stages = static_cast<int>(std::min<size_t>(tcw::kMaxStages, room / sa));
   QV_REQUIRE(stages >= 2, "wide tensor-core screen: no room for two row stages");
   a.stages = stages;
-  const size_t smem = std::max<size_t>(fixed + static_cast<size_t>(stages) * tc::kAtomBytes,
-                                       120 * 1024);
+  a.stage_atoms = sa;
+  const size_t smem = std::max<size_t>(
+      fixed + static_cast<size_t>(stages) * sa * tc::kAtomBytes, 120 * 1024);
   KernelTimer timer(st, "flat_screen_tc_wide_kernel",
                     2.0 * nq * static_cast<double>(s.n) * s.dim, false);
   auto kernel = s.metric == QV_METRIC_L2 ? tcw::flat_screen_tc_wide_kernel<true>
