@@ -8,9 +8,8 @@
 //     the whole unit: its first 512 columns in tensor memory (the 256 TMEM columns the two
 //     accumulator slots leave free; the epilogue warps store them there with tcgen05.st, and the
 //     MMAs read A from TMEM), the rest (columns 512..767) in shared memory. That leaves shared
-//     memory to a deep ring of 16 KB stages (10 at kpad 768) through which row tiles stream one
-//     64-column K atom at a time, enough copies in flight to cover L2 latency; a row tile is
-//     kAtoms stages and each stage feeds four 128 x 128 x 16 MMAs;
+//     memory to a ring of stages of up to four 64-column K atoms of a row tile (two 64 KB stages
+//     at kpad 768), so the issuing thread waits on one barrier per sixteen 128 x 128 x 16 MMAs;
 //   * accumulator slots (128 columns each, two of them) are released by their own barrier,
 //     because a stage no longer covers a whole row tile;
 //   * best lists live in global memory (L2-resident, one region per CTA, entry i of query lane l
@@ -542,9 +541,10 @@ void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t n
   constexpr size_t kSmemMax = 227 * 1024 - 1024;  // per block, less the kernel's static part
   const size_t fixed = 1024 + static_cast<size_t>(atoms - a.a_tmem_atoms) * tc::kAtomBytes + 256;
   const size_t room = (kSmemMax - fixed) / tc::kAtomBytes;  // 16 KB atoms the ring can hold
-  // Two atoms per stage (eight MMAs per barrier wait in the issuing thread) while that still
-  // leaves four stages; QV_TC_WIDE_STAGE_ATOMS (1..4) overrides, for tuning.
-  int sa = room >= 8 ? 2 : 1;
+  // Four atoms per stage (sixteen MMAs per barrier wait in the issuing thread) while that still
+  // leaves two stages: on the 768-dim workload one-, two-, three- and four-atom stages took 311,
+  // 238, 202 and 202 M SM cycles per 16,384 x 5M batch. QV_TC_WIDE_STAGE_ATOMS (1..4) overrides.
+  int sa = room >= 8 ? 4 : (room >= 4 ? 2 : 1);
   if (const char* e = std::getenv("QV_TC_WIDE_STAGE_ATOMS"); e != nullptr && *e != '\0')
     sa = std::max(1, std::min(4, std::atoi(e)));
   sa = std::min(sa, atoms);
