@@ -75,7 +75,8 @@ struct Args {
   int* err;
   bool qmajor;      // unit order: query-tile-major (true) or row-chunk-major (false)
   long long wait_cycles;  // bound of every mbarrier wait (SM clock cycles)
-  uint64_t drain_ns;      // bound of the abort path's wait for copies in flight (global timer)
+  uint64_t drain_ns;      // bound of the abort path's waits for work in flight (global timer)
+  int skip_fill;          // failure-detection test hook: CTA 0 skips this ring fill (-1: none)
 };
 
 __device__ __forceinline__ void unit_coords(const Args& a, int u, int& qgroup, int& chunk) {
@@ -184,7 +185,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* buf_d = reinterpret_cast<float*>(smem_b + kStages * kAtoms * kAtomBytes);  // kCap x kLS
   uint32_t* buf_r = reinterpret_cast<uint32_t*>(buf_d + kCap * kLS);
   uint64_t* bars = reinterpret_cast<uint64_t*>(buf_r + kCap * kLS);
-  // bars: full[kStages], empty[kStages], acc_full[kAcc], a_full, a_empty.
+  // bars: full[kStages], empty[kStages], acc_full[kAcc], a_full, a_empty, drain[2] (one per
+  // issuer: on abort, a final commit there tells when its MMAs in flight have finished).
   // Row tile t (counted over all of this CTA's units) uses stage t % kStages and accumulator slot
   // t % kAcc. full[t % kStages] also stands for "slot t % kAcc is free": it completes only when
   // the tile's bytes have landed AND every epilogue warp has read tile t - kAcc out of the slot
@@ -199,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   auto bar = [&](int i) { return smem_u32(bars + i); };
   const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, A_FULL = 2 * kStages + kAcc,
-            A_EMPTY = 2 * kStages + kAcc + 1;
+            A_EMPTY = 2 * kStages + kAcc + 1, DRAIN = 2 * kStages + kAcc + 2;
 
   if (threadIdx.x == 0) {
     s_abort = 0;
@@ -211,6 +213,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < kAcc; ++b) mbar_init(bar(ACC_FULL + b), 1);
     mbar_init(bar(A_FULL), 1);
     mbar_init(bar(A_EMPTY), 2);  // one commit per MMA issuer
+    mbar_init(bar(DRAIN), 1);
+    mbar_init(bar(DRAIN + 1), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -250,12 +254,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                         (qgroup * kTiles + tq) * kM, bar(A_FULL));
         for (int t = 0; t < ntiles; ++t) {
           if (!mbar_wait(bar(EMPTY + stage), phase ^ 1, abort_flag, a.err, a.wait_cycles)) break;
-          mbar_expect_tx(bar(FULL + stage), kAtoms * kAtomBytes);
-          unsigned char* dst = smem_b + stage * kAtoms * kAtomBytes;
-          for (int at = 0; at < kAtoms; ++at)
-            tma_load_2d(smem_u32(dst + at * kAtomBytes), &tmap_x, at * kAtomK,
-                        static_cast<int>(r0 + static_cast<int64_t>(t) * kN), bar(FULL + stage));
-          ++issued;
+          if (blockIdx.x != 0 || issued != a.skip_fill) {
+            mbar_expect_tx(bar(FULL + stage), kAtoms * kAtomBytes);
+            unsigned char* dst = smem_b + stage * kAtoms * kAtomBytes;
+            for (int at = 0; at < kAtoms; ++at)
+              tma_load_2d(smem_u32(dst + at * kAtomBytes), &tmap_x, at * kAtomK,
+                          static_cast<int>(r0 + static_cast<int64_t>(t) * kN), bar(FULL + stage));
+          }
+          ++issued;  // ring fills, the skipped one (test hook) included
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1;
@@ -266,6 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Drain: wait (bounded) for every B fill the MMA warp did not consume.
         const uint64_t t0 = gtimer();
         for (int f = s_consumed[0] + s_consumed[1]; f < issued; ++f) {
+          if (blockIdx.x == 0 && f == a.skip_fill) continue;
           const int s = f % kStages;
           const uint32_t par = (f / kStages) & 1;
           while (!mbar_test(bar(FULL + s), par) && gtimer() - t0 < a.drain_ns) {
@@ -319,6 +326,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         g += ntiles;
         umma_commit(bar(A_EMPTY));  // A_EMPTY completes once both issuers are done with the unit
+      }
+      if (*abort_flag) {
+        // Wait (bounded) for this issuer's MMAs in flight before the accumulators are freed.
+        umma_commit(bar(DRAIN + me));
+        const uint64_t t0 = gtimer();
+        while (!mbar_test(bar(DRAIN + me), 0) && gtimer() - t0 < a.drain_ns) {
+        }
       }
     }
   } else if (warp < kIssuer2) {
@@ -668,6 +682,17 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+uint64_t drain_limit_ns() {
+  // Copies and MMAs in flight finish within microseconds; 10 ms, or the wait bound if longer.
+  const uint64_t wait_ns = static_cast<uint64_t>(wait_limit_cycles() / 2);
+  return std::min<uint64_t>(kTimeoutNs, std::max<uint64_t>(10000000ull, wait_ns));
+}
+
+int test_skip_fill() {
+  const char* e = std::getenv("QV_TC_TEST_SKIP_FILL");
+  return (e == nullptr || *e == '\0') ? -1 : std::atoi(e);
+}
+
 long long wait_limit_cycles() {
   const char* e = std::getenv("QV_TC_WAIT_LIMIT_US");
   if (e == nullptr || *e == '\0') return kTimeoutCycles;
@@ -841,13 +866,14 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   a.glock = glock;
   a.err = err;
   a.wait_cycles = tc::wait_limit_cycles();
-  a.drain_ns = tc::kTimeoutNs;
+  a.drain_ns = tc::drain_limit_ns();
+  a.skip_fill = tc::test_skip_fill();
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
   const int stages = kk == 24 ? tc::Ring<24>::kStages : tc::Ring<32>::kStages;
   const int append = kk == 24 ? tc::Ring<24>::kAppend : tc::Ring<32>::kAppend;
   const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (tc::kTiles + stages) +
                       static_cast<size_t>(kk + append) * tc::kLS * 8 +
-                      (2 * stages + tc::kAcc + 2) * 8;
+                      (2 * stages + tc::kAcc + 4) * 8;
   QV_REQUIRE(smem <= 227 * 1024, "tensor-core screen: shared memory layout too large");
   const int grid = std::min(a.total_units, sm_count(s.device));
   KernelTimer timer(st, "flat_screen_tc_kernel", 2.0 * nq * static_cast<double>(s.n) * s.dim,

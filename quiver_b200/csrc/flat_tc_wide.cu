@@ -68,6 +68,7 @@ struct Args {
   int* err;
   long long wait_cycles;
   uint64_t drain_ns;
+  int skip_fill;            // failure-detection test hook: CTA 0 skips this ring fill (-1: none)
 };
 
 // Sorts 16 (distance, group) entries ascending in registers (bitonic network).
@@ -151,14 +152,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + stages * sa * kAtomBytes);
   // bars: full[stages], empty[stages], acc_full[kAcc], acc_empty[kAcc], a_full (smem part of
   // the query tile landed), a_empty (the unit's MMAs are done with the query tile), a_tfull
-  // (the epilogue warps stored the TMEM part).
+  // (the epilogue warps stored the TMEM part), drain (on abort, a final commit there tells
+  // when the MMAs in flight have finished).
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   __shared__ int s_consumed;  // B fills the MMA issuer has waited for (abort drain)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int FULL = 0, EMPTY = stages, ACC_FULL = 2 * stages, ACC_EMPTY = 2 * stages + kAcc,
-            A_FULL = 2 * stages + 2 * kAcc, A_EMPTY = A_FULL + 1, A_TFULL = A_FULL + 2;
+            A_FULL = 2 * stages + 2 * kAcc, A_EMPTY = A_FULL + 1, A_TFULL = A_FULL + 2,
+            DRAIN = A_FULL + 3;
   auto bar = [&](int i) { return smem_u32(bars + i); };
 
   if (threadIdx.x == 0) {
@@ -175,6 +178,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar(A_FULL), 1);
     mbar_init(bar(A_EMPTY), 1);
     mbar_init(bar(A_TFULL), kEpiWarps);
+    mbar_init(bar(DRAIN), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -224,11 +228,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int n_at = min(sa, atoms - at0);
             ok = mbar_wait(bar(EMPTY + stage), phase ^ 1, abort_flag, a.err, a.wait_cycles);
             if (!ok) break;
-            mbar_expect_tx(bar(FULL + stage), static_cast<uint32_t>(n_at * kAtomBytes));
-            for (int i = 0; i < n_at; ++i)
-              tma_load_2d(smem_u32(smem_b + (stage * sa + i) * kAtomBytes), &tmap_x,
-                          (at0 + i) * kAtomK, y, bar(FULL + stage));
-            ++issued;
+            if (blockIdx.x != 0 || issued != a.skip_fill) {
+              mbar_expect_tx(bar(FULL + stage), static_cast<uint32_t>(n_at * kAtomBytes));
+              for (int i = 0; i < n_at; ++i)
+                tma_load_2d(smem_u32(smem_b + (stage * sa + i) * kAtomBytes), &tmap_x,
+                            (at0 + i) * kAtomK, y, bar(FULL + stage));
+            }
+            ++issued;  // ring fills, the skipped one (test hook) included
             if (++stage == stages) {
               stage = 0;
               phase ^= 1;
@@ -241,6 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // barrier phase completes when its bytes have landed.
         const uint64_t t0 = gtimer();
         for (int f = *reinterpret_cast<volatile int*>(&s_consumed); f < issued; ++f) {
+          if (blockIdx.x == 0 && f == a.skip_fill) continue;
           const int s = f % stages;
           const uint32_t par = (f / stages) & 1;
           while (!mbar_test(bar(FULL + s), par) && gtimer() - t0 < a.drain_ns) {
@@ -307,6 +314,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         umma_commit(bar(A_EMPTY));  // the query tile may be replaced once every MMA has run
+      }
+      if (*abort_flag) {
+        // Wait (bounded) for the MMAs in flight before the accumulators are freed.
+        umma_commit(bar(DRAIN));
+        const uint64_t t0 = gtimer();
+        while (!mbar_test(bar(DRAIN), 0) && gtimer() - t0 < a.drain_ns) {
+        }
       }
     }
   } else {
@@ -531,7 +545,8 @@ void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t n
                                          static_cast<size_t>(grid) * (kk + tcw::kAppend) * tcw::kLS);
   a.err = err;
   a.wait_cycles = tc::wait_limit_cycles();
-  a.drain_ns = tc::kTimeoutNs;
+  a.drain_ns = tc::drain_limit_ns();
+  a.skip_fill = tc::test_skip_fill();
   a.a_tmem_atoms = std::min(atoms, tcw::kTmemAtoms);
   a.kpad = kpad;
   a.q16 = q16;

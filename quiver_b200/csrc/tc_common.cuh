@@ -235,6 +235,12 @@ __device__ __forceinline__ void cex(float& da, uint32_t& ra, float& db, uint32_t
 // (counted at 2 GHz) when set, else kTimeoutCycles (~2 s). A short bound lets a test make a wait
 // run out and check that the search reports it and the context stays usable.
 long long wait_limit_cycles();
+// Bound of the abort path's waits for copies and MMAs in flight (global-timer nanoseconds).
+uint64_t drain_limit_ns();
+// Failure-detection test hook: QV_TC_TEST_SKIP_FILL=n makes CTA 0's producer skip its n-th ring
+// fill (no copy, no arrival), so that a barrier wait runs out and the abort path is exercised;
+// -1 (unset) in normal use.
+int test_skip_fill();
 
 // Tensor maps (host): 2-D fp16 tensor [rows][kpad], boxes of 64 columns x 128 rows, 128-byte
 // swizzle, zero fill past the tensor's edges.

@@ -258,3 +258,32 @@ def test_add_from_device_memory_equals_host_add(gpu):
     with pytest.raises(ValueError, match="2\\^64-1"):
         dev.add_device(dx[:2], torch.tensor([1, -1], dtype=torch.int64, device="cuda"))
     assert len(dev) == 5000  # a rejected add leaves the index unchanged
+
+
+@pytest.mark.parametrize("dim", [100, 256])  # the narrow and the wide tensor-core screens
+def test_screen_barrier_timeout_is_reported_and_the_index_stays_usable(gpu, oracle, monkeypatch,
+                                                                        dim):
+    """Failure detection without a GPU fault: the test hook makes CTA 0's TMA producer skip one
+    ring fill, so the MMA issuer's bounded barrier wait (shortened to 2 ms) runs out. The kernel
+    must raise its error word, drain its work in flight, free TMEM and exit; the search reports
+    QV_ERR_DEVICE (its queries were answered by the exact rescan), and the next search on the
+    same index and context is exact."""
+    from quiver_b200.synthetic import mixture
+    base = mixture(20000, dim, 50, 0.35, 1.0, centre_seed=3, seed=4)
+    q = mixture(300, dim, 50, 0.35, 1.0, centre_seed=3, seed=5)
+    ix = gpu.FlatIndex(dim, "cosine")
+    ix.add(base)
+    monkeypatch.setenv("QV_TC_WAIT_LIMIT_US", "2000")
+    monkeypatch.setenv("QV_TC_TEST_SKIP_FILL", "2")
+    with pytest.raises(RuntimeError, match="timed out"):
+        ix.search(q, 10)
+    monkeypatch.delenv("QV_TC_TEST_SKIP_FILL")
+    monkeypatch.delenv("QV_TC_WAIT_LIMIT_US")
+    gpu._native.set_timing(True)
+    l, d = ix.search(q, 10)
+    st = gpu.last_search_stats()
+    gpu._native.set_timing(False)
+    assert st["dominant_kernel"].startswith("flat_screen_tc")
+    wl, wd = oracle.flat_search(oracle.normalize_rows(base), np.arange(20000, dtype=np.uint64),
+                                "cosine", q, 10)
+    assert_topk_parity(l, d, wl, wd, exact=True, what="after a screen timeout")
