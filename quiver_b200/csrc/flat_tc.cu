@@ -700,13 +700,13 @@ long long wait_limit_cycles() {
   return us > 0 ? us * 2000 : kTimeoutCycles;
 }
 
-// 2-D fp16 tensor [rows][kpad], boxes of 64 columns x 128 rows, 128-byte swizzle, zero fill.
-CUtensorMap make_map(const void* base, uint64_t rows, uint64_t kpad) {
+// 2-D fp16 tensor [rows][kpad], boxes of 64 columns x box_rows rows, 128-byte swizzle, zero fill.
+CUtensorMap make_map(const void* base, uint64_t rows, uint64_t kpad, uint32_t box_rows) {
   CUtensorMap m;
   std::memset(&m, 0, sizeof(m));
   const cuuint64_t dims[2] = {kpad, rows};
   const cuuint64_t strides[1] = {kpad * sizeof(__half)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kAtomK), static_cast<cuuint32_t>(kM)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(kAtomK), static_cast<cuuint32_t>(box_rows)};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base),
                                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,

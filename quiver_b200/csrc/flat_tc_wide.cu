@@ -138,7 +138,16 @@ __device__ __noinline__ void compact_wide(float* d, uint32_t* r, int kk, int& cn
   thr = fminf(thr, last);
 }
 
-template <bool kL2>
+// kPair: the kernel runs as clusters of two CTAs (tcgen05 cta_group::2). A pair works on one
+// unit at a time: a 256-query group (128 queries per CTA, each CTA's own A and its own best
+// lists) against the unit's rows, each CTA loading 64 of every 128-row tile's rows; the even CTA
+// (the leader) issues MMAs of M = 256, N = 128, so every row byte a CTA loads into shared memory
+// feeds both CTAs' tensor cores. That halves the shared-memory traffic per MMA (the screen's
+// limit with one CTA: ~128 B/clk of the SM's 128 B/clk for B's copies in and its reads out).
+// Barriers both CTAs' producers, epilogues and copies report to (full, a_full, a_tfull,
+// acc_empty, drain) live in the leader; the leader's commits arrive on both CTAs' copies of the
+// others (empty, acc_full, a_empty) by multicast.
+template <bool kL2, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     flat_screen_tc_wide_kernel(const __grid_constant__ CUtensorMap tmap_q,
                                const __grid_constant__ CUtensorMap tmap_x, const Args a) {
@@ -147,9 +156,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int atoms = a.atoms, stages = a.stages, kk = a.kk, ta = a.a_tmem_atoms;
   const int sa = a.stage_atoms;
+  // A row-tile K atom in shared memory: 128 rows (16 KB), or this CTA's 64 rows in a pair.
+  constexpr int kBAtomBytes = kPair ? kAtomBytes / 2 : kAtomBytes;
+  constexpr int kBRows = kPair ? kN / 2 : kN;
   unsigned char* smem_a = base;  // atoms - ta atoms x 16 KB (the query tile past TMEM's part)
-  unsigned char* smem_b = smem_a + (atoms - ta) * kAtomBytes;  // stages x sa x 16 KB
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + stages * sa * kAtomBytes);
+  unsigned char* smem_b = smem_a + (atoms - ta) * kAtomBytes;  // stages x sa x kBAtomBytes
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_b + stages * sa * kBAtomBytes);
   // bars: full[stages], empty[stages], acc_full[kAcc], acc_empty[kAcc], a_full (smem part of
   // the query tile landed), a_empty (the unit's MMAs are done with the query tile), a_tfull
   // (the epilogue warps stored the TMEM part), drain (on abort, a final commit there tells
@@ -163,76 +175,125 @@ __global__ void __launch_bounds__(kThreads, 1)
             A_FULL = 2 * stages + 2 * kAcc, A_EMPTY = A_FULL + 1, A_TFULL = A_FULL + 2,
             DRAIN = A_FULL + 3;
   auto bar = [&](int i) { return smem_u32(bars + i); };
+  const uint32_t rank = kPair ? cluster_ctarank() : 0;
+  const bool leader = rank == 0;
+  // The leader's copy of barrier i, as a shared::cluster address (pair) or this CTA's (single).
+  auto lbar = [&](int i) { return kPair ? mapa_shared(bar(i), 0) : bar(i); };
+  auto wait = [&](uint32_t b, uint32_t parity, volatile int* abort_flag) {
+    return kPair ? mbar_wait_cluster(b, parity, abort_flag, a.err, a.wait_cycles)
+                 : mbar_wait(b, parity, abort_flag, a.err, a.wait_cycles);
+  };
+  auto arrive_leader = [&](int i) {
+    if (kPair) {
+      mbar_arrive_cluster(lbar(i));
+    } else {
+      mbar_arrive(bar(i));
+    }
+  };
+  auto commit_both = [&](int i) {  // the MMAs issued so far have completed
+    if (kPair) {
+      umma_commit_pair_mc(bar(i), 0x3);
+    } else {
+      umma_commit(bar(i));
+    }
+  };
 
   if (threadIdx.x == 0) {
     s_abort = 0;
     s_consumed = 0;
     for (int s = 0; s < stages; ++s) {
-      mbar_init(bar(FULL + s), 1);   // the producer's expect_tx
+      mbar_init(bar(FULL + s), 1);   // the (leader's) producer's expect_tx
       mbar_init(bar(EMPTY + s), 1);  // the MMA commit
     }
     for (int b = 0; b < kAcc; ++b) {
       mbar_init(bar(ACC_FULL + b), 1);
-      mbar_init(bar(ACC_EMPTY + b), kEpiWarps);
+      mbar_init(bar(ACC_EMPTY + b), (kPair ? 2 : 1) * kEpiWarps);
     }
     mbar_init(bar(A_FULL), 1);
     mbar_init(bar(A_EMPTY), 1);
-    mbar_init(bar(A_TFULL), kEpiWarps);
+    mbar_init(bar(A_TFULL), (kPair ? 2 : 1) * kEpiWarps);
     mbar_init(bar(DRAIN), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(&s_tmem)),
-                 "r"(kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (kPair) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&s_tmem)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&s_tmem)),
+                   "r"(kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (kPair) cluster_sync();  // both CTAs' barriers are initialized before either uses them
   tc_fence_after();
   const uint32_t tmem_base = s_tmem;
   volatile int* abort_flag = &s_abort;
 
+  // Units: (query group, row chunk), chunk-major so that CTAs running together share row chunks
+  // in L2. A group is one 128-query tile, or two (one per CTA) in a pair.
+  const int worker = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int workers = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int n_groups = kPair ? (a.n_qtiles + 1) / 2 : a.n_qtiles;
   auto unit_rows = [&](int u, int& qtile, int& chunk, int64_t& r0, int64_t& r1) {
-    chunk = u / a.n_qtiles;  // chunk-major: CTAs running together share row chunks in L2
-    qtile = u - chunk * a.n_qtiles;
+    chunk = u / n_groups;
+    const int group = u - chunk * n_groups;
+    qtile = kPair ? 2 * group + static_cast<int>(rank) : group;
     r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
     r1 = min(a.nrows, r0 + a.chunk_rows);
   };
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer (both CTAs of a pair) ----------------
     if (lane == 0) {
       int stage = 0, issued = 0;
       uint32_t phase = 0, a_phase = 0;
       bool first = true, ok = true;
-      for (int u = blockIdx.x; u < a.total_units && ok && !*abort_flag; u += gridDim.x) {
+      for (int u = worker; u < a.total_units && ok && !*abort_flag; u += workers) {
         int qtile, chunk;
         int64_t r0, r1;
         unit_rows(u, qtile, chunk, r0, r1);
         const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
         if (!first) {
-          if (!mbar_wait(bar(A_EMPTY), a_phase, abort_flag, a.err, a.wait_cycles)) break;
+          if (!wait(bar(A_EMPTY), a_phase, abort_flag)) break;
           a_phase ^= 1;
         }
         first = false;
         // The query tile's atoms past the TMEM part (none when kpad <= 512: the arrival alone
-        // completes the phase).
-        mbar_expect_tx(bar(A_FULL), static_cast<uint32_t>((atoms - ta) * kAtomBytes));
-        for (int at = ta; at < atoms; ++at)
-          tma_load_2d(smem_u32(smem_a + (at - ta) * kAtomBytes), &tmap_q, at * kAtomK,
-                      qtile * kM, bar(A_FULL));
+        // completes the phase). In a pair, both CTAs' copies count on the leader's barrier.
+        if (leader)
+          mbar_expect_tx(bar(A_FULL),
+                         static_cast<uint32_t>((kPair ? 2 : 1) * (atoms - ta) * kAtomBytes));
+        for (int at = ta; at < atoms; ++at) {
+          const uint32_t dst = smem_u32(smem_a + (at - ta) * kAtomBytes);
+          if (kPair)
+            tma_load_2d_pair(dst, &tmap_q, at * kAtomK, qtile * kM, lbar(A_FULL));
+          else
+            tma_load_2d(dst, &tmap_q, at * kAtomK, qtile * kM, bar(A_FULL));
+        }
         for (int t = 0; t < ntiles && ok; ++t) {
-          const int y = static_cast<int>(r0 + static_cast<int64_t>(t) * kN);
+          const int y = static_cast<int>(r0 + static_cast<int64_t>(t) * kN) +
+                        static_cast<int>(rank) * kBRows;
           for (int at0 = 0; at0 < atoms; at0 += sa) {
             const int n_at = min(sa, atoms - at0);
-            ok = mbar_wait(bar(EMPTY + stage), phase ^ 1, abort_flag, a.err, a.wait_cycles);
+            ok = wait(bar(EMPTY + stage), phase ^ 1, abort_flag);
             if (!ok) break;
             if (blockIdx.x != 0 || issued != a.skip_fill) {
-              mbar_expect_tx(bar(FULL + stage), static_cast<uint32_t>(n_at * kAtomBytes));
-              for (int i = 0; i < n_at; ++i)
-                tma_load_2d(smem_u32(smem_b + (stage * sa + i) * kAtomBytes), &tmap_x,
-                            (at0 + i) * kAtomK, y, bar(FULL + stage));
+              if (leader)
+                mbar_expect_tx(bar(FULL + stage),
+                               static_cast<uint32_t>((kPair ? 2 : 1) * n_at * kBAtomBytes));
+              for (int i = 0; i < n_at; ++i) {
+                const uint32_t dst = smem_u32(smem_b + (stage * sa + i) * kBAtomBytes);
+                if (kPair)
+                  tma_load_2d_pair(dst, &tmap_x, (at0 + i) * kAtomK, y, lbar(FULL + stage));
+                else
+                  tma_load_2d(dst, &tmap_x, (at0 + i) * kAtomK, y, bar(FULL + stage));
+              }
             }
             ++issued;  // ring fills, the skipped one (test hook) included
             if (++stage == stages) {
@@ -243,88 +304,106 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (*abort_flag) {
-        // Drain: wait (bounded) for every B fill the MMA issuer did not consume. Each fill's
-        // barrier phase completes when its bytes have landed.
         const uint64_t t0 = gtimer();
-        for (int f = *reinterpret_cast<volatile int*>(&s_consumed); f < issued; ++f) {
-          if (blockIdx.x == 0 && f == a.skip_fill) continue;
-          const int s = f % stages;
-          const uint32_t par = (f / stages) & 1;
-          while (!mbar_test(bar(FULL + s), par) && gtimer() - t0 < a.drain_ns) {
+        if (kPair) {
+          // A pair's copies complete on the leader's barriers, which the peer cannot poll: wait
+          // out the drain bound, far longer than any copy in flight takes.
+          while (gtimer() - t0 < a.drain_ns) {
+          }
+        } else {
+          // Wait (bounded) for every B fill the MMA issuer did not consume: each fill's barrier
+          // phase completes when its bytes have landed.
+          for (int f = *reinterpret_cast<volatile int*>(&s_consumed); f < issued; ++f) {
+            if (blockIdx.x == 0 && f == a.skip_fill) continue;
+            const int s = f % stages;
+            const uint32_t par = (f / stages) & 1;
+            while (!mbar_test(bar(FULL + s), par) && gtimer() - t0 < a.drain_ns) {
+            }
           }
         }
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer (the leader of a pair) ----------------
+    if (lane == 0 && leader) {
       int stage = 0, g = 0;  // g: row tiles issued by this CTA so far (slot g & 1)
       uint32_t phase = 0, a_phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < a.total_units && ok && !*abort_flag; u += gridDim.x) {
+      for (int u = worker; u < a.total_units && ok && !*abort_flag; u += workers) {
         int qtile, chunk;
         int64_t r0, r1;
         unit_rows(u, qtile, chunk, r0, r1);
         const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
-        if (!mbar_wait(bar(A_FULL), a_phase, abort_flag, a.err, a.wait_cycles)) break;
-        if (!mbar_wait(bar(A_TFULL), a_phase, abort_flag, a.err, a.wait_cycles)) break;
+        if (!wait(bar(A_FULL), a_phase, abort_flag)) break;
+        if (!wait(bar(A_TFULL), a_phase, abort_flag)) break;
         a_phase ^= 1;
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem_a);
         const uint32_t a_tmem = tmem_base + static_cast<uint32_t>(kAcc * kN);
         for (int t = 0; t < ntiles && ok; ++t, ++g) {
           const int slot = g & 1;
-          // The slot's previous tile (g - 2) must have been read out by the epilogue.
-          ok = mbar_wait(bar(ACC_EMPTY + slot), ((g >> 1) & 1) ^ 1, abort_flag, a.err,
-                         a.wait_cycles);
+          // The slot's previous tile (g - 2) must have been read out by the epilogue(s).
+          ok = wait(bar(ACC_EMPTY + slot), ((g >> 1) & 1) ^ 1, abort_flag);
           if (!ok) break;
           tc_fence_after();
           const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(slot * kN);
           for (int at0 = 0; at0 < atoms; at0 += sa) {
             const int n_at = min(sa, atoms - at0);
-            ok = mbar_wait(bar(FULL + stage), phase, abort_flag, a.err, a.wait_cycles);
+            ok = wait(bar(FULL + stage), phase, abort_flag);
             if (!ok) break;
             *reinterpret_cast<volatile int*>(&s_consumed) += 1;
             tc_fence_after();
             for (int i = 0; i < n_at; ++i) {
               const int at = at0 + i;
-              const uint32_t b_addr = smem_u32(smem_b + (stage * sa + i) * kAtomBytes);
+              const uint32_t b_addr = smem_u32(smem_b + (stage * sa + i) * kBAtomBytes);
               if (at < ta) {  // A from TMEM: 64 fp16 per atom = 32 columns, 8 per K step
                 const uint32_t at_tmem = a_tmem + static_cast<uint32_t>(at * 32);
 #pragma unroll
-                for (int ks = 0; ks < 4; ++ks)
-                  umma_f16_ts(d_tmem, at_tmem + ks * 8, smem_desc(b_addr + ks * 32),
-                              (at | ks) != 0 ? 1u : 0u);
+                for (int ks = 0; ks < 4; ++ks) {
+                  const uint32_t acc = (at | ks) != 0 ? 1u : 0u;
+                  if (kPair)
+                    umma_f16_ts_pair(d_tmem, at_tmem + ks * 8, smem_desc(b_addr + ks * 32), acc);
+                  else
+                    umma_f16_ts(d_tmem, at_tmem + ks * 8, smem_desc(b_addr + ks * 32), acc);
+                }
               } else {
                 const uint32_t aa = a_addr + static_cast<uint32_t>((at - ta) * kAtomBytes);
 #pragma unroll
-                for (int ks = 0; ks < 4; ++ks)
-                  umma_f16(d_tmem, smem_desc(aa + ks * 32), smem_desc(b_addr + ks * 32),
-                           (at | ks) != 0 ? 1u : 0u);
+                for (int ks = 0; ks < 4; ++ks) {
+                  const uint32_t acc = (at | ks) != 0 ? 1u : 0u;
+                  if (kPair)
+                    umma_f16_pair(d_tmem, smem_desc(aa + ks * 32), smem_desc(b_addr + ks * 32),
+                                  acc);
+                  else
+                    umma_f16(d_tmem, smem_desc(aa + ks * 32), smem_desc(b_addr + ks * 32), acc);
+                }
               }
             }
-            umma_commit(bar(EMPTY + stage));  // the stage is free once these MMAs have read it
+            commit_both(EMPTY + stage);  // the stage is free once these MMAs have read it
             if (++stage == stages) {
               stage = 0;
               phase ^= 1;
             }
           }
           if (!ok) break;
-          umma_commit(bar(ACC_FULL + slot));
+          commit_both(ACC_FULL + slot);
         }
         if (!ok) break;
-        umma_commit(bar(A_EMPTY));  // the query tile may be replaced once every MMA has run
+        commit_both(A_EMPTY);  // the query tile may be replaced once every MMA has run
       }
       if (*abort_flag) {
         // Wait (bounded) for the MMAs in flight before the accumulators are freed.
-        umma_commit(bar(DRAIN));
+        if (kPair)
+          umma_commit_pair_mc(bar(DRAIN), 0x1);
+        else
+          umma_commit(bar(DRAIN));
         const uint64_t t0 = gtimer();
         while (!mbar_test(bar(DRAIN), 0) && gtimer() - t0 < a.drain_ns) {
         }
       }
     }
   } else {
-    // ---------------- epilogue: thread = query ----------------
+    // ---------------- epilogue: thread = query (both CTAs of a pair) ----------------
     const int quarter = warp & 3;  // TMEM lanes this warp may read
     const int qi = quarter * 32 + lane;
     float* ld = a.list_d + static_cast<size_t>(blockIdx.x) * (kk + kAppend) * kLS + qi;
@@ -334,7 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int g = 0;
     uint32_t a_phase = 0;
     bool ok = true, first = true;
-    for (int u = blockIdx.x; u < a.total_units && ok; u += gridDim.x) {
+    for (int u = worker; u < a.total_units && ok; u += workers) {
       int qtile, chunk;
       int64_t r0, r1;
       unit_rows(u, qtile, chunk, r0, r1);
@@ -343,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // The query tile's first ta atoms into this warp's 32 TMEM lanes (columns 256 + 32 * atom),
       // once the previous unit's MMAs have finished reading them.
       if (!first) {
-        ok = mbar_wait(bar(A_EMPTY), a_phase, abort_flag, a.err, a.wait_cycles);
+        ok = wait(bar(A_EMPTY), a_phase, abort_flag);
         if (!ok) break;
         a_phase ^= 1;
         tc_fence_after();
@@ -370,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(A_TFULL));
+        if (lane == 0) arrive_leader(A_TFULL);
       }
       const bool active = q < a.nq;
       const unsigned* qthr = a.thr_bits + (active ? q : 0);
@@ -446,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int slot = g & 1;
         const int64_t row0 = r0 + static_cast<int64_t>(t) * kN;
         if ((t & 7) == 0 && active) fresh = *reinterpret_cast<const volatile unsigned*>(qthr);
-        ok = mbar_wait(bar(ACC_FULL + slot), (g >> 1) & 1, abort_flag, a.err, a.wait_cycles);
+        ok = wait(bar(ACC_FULL + slot), (g >> 1) & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
         const uint32_t taddr =
@@ -457,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_hold(rb);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar(ACC_EMPTY + slot));
+        if (lane == 0) arrive_leader(ACC_EMPTY + slot);
         float best_a[8], best_b[8], top_a, top_b;
         tree(ra, row0, best_a, top_a);
         tree(rb, row0 + 64, best_b, top_b);
@@ -481,10 +560,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  // In a pair, neither CTA frees its tensor memory or leaves while the other may still reach
+  // its barriers or the leader's MMAs its memory.
+  if (kPair) cluster_sync();
   tc_fence_after();
   if (warp == 1) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(kTmemCols));
+    if (kPair) {
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(kTmemCols));
+    } else {
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(kTmemCols));
+    }
   }
 }
 
@@ -521,12 +608,17 @@ void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t n
   const int kpad = static_cast<int>(s.kpad);
   const int atoms = static_cast<int>(ceil_div(static_cast<size_t>(kpad), tc::kAtomK));
   QV_REQUIRE(atoms <= tcw::kMaxAtoms, "wide tensor-core screen: rows wider than 768");
-  const CUtensorMap mx = tc::make_map(s.x16.get(), s.n, kpad);
+  // CTA pairs (tcgen05 cta_group::2) unless QV_TC_WIDE_PAIR=0 selects single CTAs.
+  const char* pe = std::getenv("QV_TC_WIDE_PAIR");
+  const bool pair = !(pe != nullptr && pe[0] == '0');
+  const int nsm = sm_count(s.device);
+  // A pair's CTAs each load 64 rows of every 128-row tile.
+  const CUtensorMap mx = tc::make_map(s.x16.get(), s.n, kpad, pair ? tc::kN / 2 : tc::kN);
   tcw::Args a{};
   a.nq = static_cast<int>(nq);
   a.n_qtiles = static_cast<int>(ceil_div(nq, tc::kM));
   a.n_chunks = n_chunks;
-  a.total_units = a.n_qtiles * n_chunks;
+  a.total_units = (pair ? (a.n_qtiles + 1) / 2 : a.n_qtiles) * n_chunks;
   a.atoms = atoms;
   a.kk = kk;
   a.nrows = static_cast<int64_t>(s.n);
@@ -540,7 +632,7 @@ void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t n
   a.cand_n = cand_n;
   a.thr_bits = thr_bits;
   a.list_d = static_cast<float*>(lists);
-  const int grid = std::min(a.total_units, sm_count(s.device));
+  const int grid = pair ? 2 * std::min(a.total_units, nsm / 2) : std::min(a.total_units, nsm);
   a.list_r = reinterpret_cast<uint32_t*>(static_cast<float*>(lists) +
                                          static_cast<size_t>(grid) * (kk + tcw::kAppend) * tcw::kLS);
   a.err = err;
@@ -550,15 +642,17 @@ void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t n
   a.a_tmem_atoms = std::min(atoms, tcw::kTmemAtoms);
   a.kpad = kpad;
   a.q16 = q16;
-  // Shared memory: the query tile's atoms past TMEM's part, as many 16 KB stages as fit (10 at
-  // kpad 768), barriers; never less than half the SM's shared memory, so that one CTA (and its
-  // 512 TMEM columns) runs per SM.
+  // Shared memory: the query tile's atoms past TMEM's part, a ring of row-tile K atoms (16 KB, or
+  // 8 KB for a pair's 64-row halves), barriers; never less than half the SM's shared memory, so
+  // that one CTA (and its 512 TMEM columns) runs per SM.
   constexpr size_t kSmemMax = 227 * 1024 - 1024;  // per block, less the kernel's static part
+  const size_t b_atom = pair ? tc::kAtomBytes / 2 : tc::kAtomBytes;
   const size_t fixed = 1024 + static_cast<size_t>(atoms - a.a_tmem_atoms) * tc::kAtomBytes + 256;
-  const size_t room = (kSmemMax - fixed) / tc::kAtomBytes;  // 16 KB atoms the ring can hold
+  const size_t room = (kSmemMax - fixed) / b_atom;  // row-tile K atoms the ring can hold
   // Four atoms per stage (sixteen MMAs per barrier wait in the issuing thread) while that still
-  // leaves two stages: on the 768-dim workload one-, two-, three- and four-atom stages took 311,
-  // 238, 202 and 202 M SM cycles per 16,384 x 5M batch. QV_TC_WIDE_STAGE_ATOMS (1..4) overrides.
+  // leaves two stages: on the 768-dim workload (single CTAs) one-, two-, three- and four-atom
+  // stages took 311, 238, 202 and 202 M SM cycles per 16,384 x 5M batch.
+  // QV_TC_WIDE_STAGE_ATOMS (1..4) overrides.
   int sa = room >= 8 ? 4 : (room >= 4 ? 2 : 1);
   if (const char* e = std::getenv("QV_TC_WIDE_STAGE_ATOMS"); e != nullptr && *e != '\0')
     sa = std::max(1, std::min(4, std::atoi(e)));
@@ -567,14 +661,34 @@ void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t n
   QV_REQUIRE(stages >= 2, "wide tensor-core screen: no room for two row stages");
   a.stages = stages;
   a.stage_atoms = sa;
-  const size_t smem = std::max<size_t>(
-      fixed + static_cast<size_t>(stages) * sa * tc::kAtomBytes, 120 * 1024);
+  const size_t smem =
+      std::max<size_t>(fixed + static_cast<size_t>(stages) * sa * b_atom, 120 * 1024);
   KernelTimer timer(st, "flat_screen_tc_wide_kernel",
                     2.0 * nq * static_cast<double>(s.n) * s.dim, false);
-  auto kernel = s.metric == QV_METRIC_L2 ? tcw::flat_screen_tc_wide_kernel<true>
-                                          : tcw::flat_screen_tc_wide_kernel<false>;
-  QV_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kernel<<<grid, tcw::kThreads, smem, st>>>(mq, mx, a);
+  const bool l2 = s.metric == QV_METRIC_L2;
+  if (pair) {
+    auto kernel = l2 ? tcw::flat_screen_tc_wide_kernel<true, true>
+                     : tcw::flat_screen_tc_wide_kernel<false, true>;
+    QV_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(tcw::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    QV_CUDA(cudaLaunchKernelEx(&cfg, kernel, mq, mx, a));
+  } else {
+    auto kernel = l2 ? tcw::flat_screen_tc_wide_kernel<true, false>
+                     : tcw::flat_screen_tc_wide_kernel<false, false>;
+    QV_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kernel<<<grid, tcw::kThreads, smem, st>>>(mq, mx, a);
+  }
   timer.stop();
   check_launch("flat_screen_tc_wide_kernel");
   (void)eps;

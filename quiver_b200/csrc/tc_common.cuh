@@ -242,9 +242,106 @@ uint64_t drain_limit_ns();
 // -1 (unset) in normal use.
 int test_skip_fill();
 
+// ---- CTA pairs (cluster of two CTAs, tcgen05 cta_group::2) ----------------------------------------
+// In a pair, the even CTA (rank 0) issues MMAs of M = 256 rows: each CTA holds its own 128 rows
+// of A and half of B's N rows, and its own half of D in its TMEM. Barriers the pair shares live
+// in the leader's shared memory; the peer reaches them through shared::cluster addresses.
+constexpr uint32_t kIdescPair = (1u << 4)               // D format f32
+                                | ((kN >> 3) << 17)     // N = 128 (64 rows from each CTA)
+                                | ((2 * kM >> 4) << 24);  // M = 256 (128 rows from each CTA)
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// The shared::cluster address of `addr` (a shared::cta address of this CTA) in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Arrive on a barrier of the pair (a shared::cluster address), releasing at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx_cluster(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+// try_wait acquiring at cluster scope (the barrier's arrivals may come from the peer CTA).
+__device__ __forceinline__ bool mbar_test_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
+                                                  volatile int* abort_flag, int* err,
+                                                  long long limit) {
+  if (mbar_test_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    if (mbar_test_cluster(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > limit) {
+      *abort_flag = 1;
+      atomicExch(err, 1);
+      return false;
+    }
+  }
+}
+// TMA load into this CTA's shared memory whose completion is counted on a barrier of the pair
+// (cluster_bar: a shared::cluster address, the leader's barrier). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                                 uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(cluster_bar)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a, uint64_t b,
+                                              uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(kIdescPair), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void umma_f16_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t b,
+                                                 uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b), "r"(kIdescPair), "r"(acc)
+      : "memory");
+}
+// Arrives on the barrier at offset `bar` in every CTA of `mask` once the pair's MMAs issued so
+// far have completed.
+__device__ __forceinline__ void umma_commit_pair_mc(uint32_t bar, uint16_t mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 "
+      "[%0], %1;" ::"r"(bar),
+      "h"(mask)
+      : "memory");
+}
+
 // Tensor maps (host): 2-D fp16 tensor [rows][kpad], boxes of 64 columns x 128 rows, 128-byte
 // swizzle, zero fill past the tensor's edges.
-CUtensorMap make_map(const void* base, uint64_t rows, uint64_t kpad);
+CUtensorMap make_map(const void* base, uint64_t rows, uint64_t kpad, uint32_t box_rows = kM);
 
 }  // namespace tc
 
