@@ -138,6 +138,39 @@ __device__ __noinline__ void compact_wide(float* d, uint32_t* r, int kk, int& cn
   thr = fminf(thr, last);
 }
 
+// One ring stage's MMAs: kAtomsN K atoms x 4 K steps, fully unrolled, with the descriptors
+// advanced by constant offsets (a descriptor's start-address field is the byte address >> 4 in
+// its low 14 bits, which a shared-memory address below 256 KB never carries out of). kTs: A from
+// TMEM (a = its first column) or from shared memory (a = its byte address). first: the stage
+// starts the tile's accumulation.
+template <bool kPair, bool kTs, int kAtomsN, int kBAtomBytes>
+__device__ __forceinline__ void issue_stage(uint32_t d_tmem, uint32_t a, uint32_t b_addr,
+                                            bool first) {
+  const uint64_t bd = smem_desc(b_addr);
+  const uint64_t ad = kTs ? 0 : smem_desc(a);
+#pragma unroll
+  for (int i = 0; i < kAtomsN; ++i) {
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const uint32_t acc = (first && i == 0 && ks == 0) ? 0u : 1u;
+      const uint64_t b = bd + static_cast<uint64_t>((i * kBAtomBytes + ks * 32) >> 4);
+      if (kTs) {
+        const uint32_t at = a + static_cast<uint32_t>(i * 32 + ks * 8);
+        if (kPair)
+          umma_f16_ts_pair(d_tmem, at, b, acc);
+        else
+          umma_f16_ts(d_tmem, at, b, acc);
+      } else {
+        const uint64_t ai = ad + static_cast<uint64_t>((i * kAtomBytes + ks * 32) >> 4);
+        if (kPair)
+          umma_f16_pair(d_tmem, ai, b, acc);
+        else
+          umma_f16(d_tmem, ai, b, acc);
+      }
+    }
+  }
+}
+
 // kPair: the kernel runs as clusters of two CTAs (tcgen05 cta_group::2). A pair works on one
 // unit at a time: a 256-query group (128 queries per CTA, each CTA's own A and its own best
 // lists) against the unit's rows, each CTA loading 64 of every 128-row tile's rows; the even CTA
@@ -353,30 +386,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) break;
             *reinterpret_cast<volatile int*>(&s_consumed) += 1;
             tc_fence_after();
-            for (int i = 0; i < n_at; ++i) {
-              const int at = at0 + i;
-              const uint32_t b_addr = smem_u32(smem_b + (stage * sa + i) * kBAtomBytes);
-              if (at < ta) {  // A from TMEM: 64 fp16 per atom = 32 columns, 8 per K step
-                const uint32_t at_tmem = a_tmem + static_cast<uint32_t>(at * 32);
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) {
-                  const uint32_t acc = (at | ks) != 0 ? 1u : 0u;
-                  if (kPair)
-                    umma_f16_ts_pair(d_tmem, at_tmem + ks * 8, smem_desc(b_addr + ks * 32), acc);
-                  else
-                    umma_f16_ts(d_tmem, at_tmem + ks * 8, smem_desc(b_addr + ks * 32), acc);
-                }
-              } else {
-                const uint32_t aa = a_addr + static_cast<uint32_t>((at - ta) * kAtomBytes);
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks) {
-                  const uint32_t acc = (at | ks) != 0 ? 1u : 0u;
-                  if (kPair)
-                    umma_f16_pair(d_tmem, smem_desc(aa + ks * 32), smem_desc(b_addr + ks * 32),
-                                  acc);
-                  else
-                    umma_f16(d_tmem, smem_desc(aa + ks * 32), smem_desc(b_addr + ks * 32), acc);
-                }
+            const uint32_t b_stage = smem_u32(smem_b + stage * sa * kBAtomBytes);
+            if (n_at == 4 && (at0 + 4 <= ta || at0 >= ta)) {
+              // The common case: four atoms all from TMEM or all from shared memory.
+              if (at0 < ta)
+                issue_stage<kPair, true, 4, kBAtomBytes>(
+                    d_tmem, a_tmem + static_cast<uint32_t>(at0 * 32), b_stage, at0 == 0);
+              else
+                issue_stage<kPair, false, 4, kBAtomBytes>(
+                    d_tmem, a_addr + static_cast<uint32_t>((at0 - ta) * kAtomBytes), b_stage,
+                    at0 == 0);
+            } else {
+              for (int i = 0; i < n_at; ++i) {
+                const int at = at0 + i;
+                const uint32_t b_addr = b_stage + static_cast<uint32_t>(i * kBAtomBytes);
+                if (at < ta)  // A from TMEM: 64 fp16 per atom = 32 columns, 8 per K step
+                  issue_stage<kPair, true, 1, kBAtomBytes>(
+                      d_tmem, a_tmem + static_cast<uint32_t>(at * 32), b_addr, at == 0);
+                else
+                  issue_stage<kPair, false, 1, kBAtomBytes>(
+                      d_tmem, a_addr + static_cast<uint32_t>((at - ta) * kAtomBytes), b_addr,
+                      at == 0);
               }
             }
             commit_both(EMPTY + stage);  // the stage is free once these MMAs have read it
