@@ -385,7 +385,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = wait(bar(FULL + stage), phase, abort_flag);
             if (!ok) break;
             *reinterpret_cast<volatile int*>(&s_consumed) += 1;
-            tc_fence_after();
+            // No tcgen05 fence here: the stage's bytes come from the TMA (async proxy) and its
+            // barrier's completion orders them before the MMAs that read them; only the TMEM
+            // hand-offs between threads (accumulator slot, query tile) need the fence.
             const uint32_t b_stage = smem_u32(smem_b + stage * sa * kBAtomBytes);
             if (n_at == 4 && (at0 + 4 <= ta || at0 >= ta)) {
               // The common case: four atoms all from TMEM or all from shared memory.
@@ -638,9 +640,11 @@ void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t n
   const int kpad = static_cast<int>(s.kpad);
   const int atoms = static_cast<int>(ceil_div(static_cast<size_t>(kpad), tc::kAtomK));
   QV_REQUIRE(atoms <= tcw::kMaxAtoms, "wide tensor-core screen: rows wider than 768");
-  // CTA pairs (tcgen05 cta_group::2) unless QV_TC_WIDE_PAIR=0 selects single CTAs.
+  // Single CTAs unless QV_TC_WIDE_PAIR=1 selects CTA pairs (tcgen05 cta_group::2). On the 768-dim
+  // workload (16,384 queries x 5M rows, power-capped clocks) both ran in 165-200 M SM cycles
+  // against a 104 M-cycle MMA floor; pairs halve the L2-to-SM traffic but did not run faster.
   const char* pe = std::getenv("QV_TC_WIDE_PAIR");
-  const bool pair = !(pe != nullptr && pe[0] == '0');
+  const bool pair = pe != nullptr && pe[0] == '1';
   const int nsm = sm_count(s.device);
   // A pair's CTAs each load 64 rows of every 128-row tile.
   const CUtensorMap mx = tc::make_map(s.x16.get(), s.n, kpad, pair ? tc::kN / 2 : tc::kN);
