@@ -287,3 +287,27 @@ def test_screen_barrier_timeout_is_reported_and_the_index_stays_usable(gpu, orac
     wl, wd = oracle.flat_search(oracle.normalize_rows(base), np.arange(20000, dtype=np.uint64),
                                 "cosine", q, 10)
     assert_topk_parity(l, d, wl, wd, exact=True, what="after a screen timeout")
+
+
+@pytest.mark.parametrize("pair", ["0", "1"])
+@pytest.mark.parametrize("metric,dim,k", [("ip", 768, 100), ("l2", 256, 10), ("cosine", 520, 40)])
+def test_wide_screen_equals_simt_screen(gpu, oracle, monkeypatch, pair, metric, dim, k):
+    """The wide tensor-core screen (dim > 128 or k > 24), in single CTAs and in CTA pairs
+    (tcgen05 cta_group::2), gives the SIMT screen's exact results, certifying every query."""
+    from quiver_b200.synthetic import mixture
+    base = mixture(30000, dim, 40, 0.35, 1.0, centre_seed=5, seed=6)
+    if metric == "l2":
+        base = base * np.float32(2.0)
+    q = mixture(257, dim, 40, 0.35, 1.0, centre_seed=5, seed=7)
+    ix = gpu.FlatIndex(dim, metric)
+    ix.add(base)
+    monkeypatch.setenv("QV_TC_WIDE_PAIR", pair)
+    gpu._native.set_timing(True)
+    l1, d1 = ix.search(q, k)
+    st = gpu.last_search_stats()
+    gpu._native.set_timing(False)
+    assert st["dominant_kernel"] == "flat_screen_tc_wide_kernel"
+    assert st["rescanned_queries"] == 0
+    monkeypatch.setenv("QV_FLAT_SCREEN", "simt")
+    l2_, d2 = ix.search(q, k)
+    assert np.array_equal(d1, d2) and np.array_equal(l1, l2_)
