@@ -97,6 +97,36 @@ def _ivf_worker(rank, world, port, out_q, case):
         dist.destroy_process_group()
 
 
+def _wide_worker(rank, world, port, out_q):
+    """Config 4's layout at test size: 768-dim inner product, k=100, each rank's id range added
+    from device memory (add_range_device), the wide tensor-core screen, one packed all-gather and
+    the device merge."""
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device(f"cuda:{rank}"))
+    try:
+        import quiver_b200 as qv
+        from quiver_b200.distributed import ShardedFlatIndex, shard_range
+        from quiver_b200.synthetic import config4_chunk
+        db = config4_chunk(60000, 1)
+        q = config4_chunk(200, 62)
+        lo, hi = shard_range(len(db), rank, world)
+        sharded = ShardedFlatIndex(768, "ip", device=rank)
+        sharded.add_range_device(torch.from_numpy(db[lo:hi]).cuda(), lo)
+        d, lab = sharded.search_device(torch.from_numpy(q).cuda(), 100)
+        full = qv.FlatIndex(768, "ip", device=rank)
+        full.add(db)
+        fl, fd = full.search(q, 100)
+        out_q.put((rank, {"wide": (d.cpu().numpy(), lab.cpu().numpy(), fd, fl)}, None))
+    except Exception as e:  # noqa: BLE001
+        out_q.put((rank, None, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
 def _spawn(target, *extra):
     import torch
     import torch.multiprocessing as mp
@@ -139,6 +169,13 @@ def test_sharded_flat_equals_one_index():
 @pytest.mark.parametrize("idx", range(3))
 def test_sharded_ivf_equals_one_index(manifest, idx):
     res = _spawn(_ivf_worker, manifest["ivf"][idx])
+    for rank in range(WORLD):
+        for key, (d, lab, fd, fl) in res[rank].items():
+            _same(d, lab, fd, fl, f"rank {rank} {key}")
+
+
+def test_sharded_wide_flat_equals_one_index():
+    res = _spawn(_wide_worker)
     for rank in range(WORLD):
         for key, (d, lab, fd, fl) in res[rank].items():
             _same(d, lab, fd, fl, f"rank {rank} {key}")
