@@ -64,3 +64,14 @@ def test_matrix_coercion():
         _as_matrix(np.zeros((2, 3)), 4)
     with pytest.raises(ValueError):
         _as_matrix(np.zeros((2, 3, 4)), 3)
+
+
+def test_quiver_alias_package_is_the_gpu_build():
+    """`import quiver` resolves to this build's classes (the reference's package name)."""
+    import quiver
+    import quiver_b200
+    assert quiver.FlatIndex is quiver_b200.FlatIndex
+    assert quiver.IvfPqIndex is quiver_b200.IvfPqIndex
+    import pytest
+    with pytest.raises(AttributeError, match="not part of the GPU build"):
+        quiver.HnswIndex  # noqa: B018
