@@ -4,9 +4,9 @@
 // lookup tables, the ADC scan and the optional exact re-rank there (qv_ivfpq_* in
 // include/qv_gpu.h), with the reference's assignments, codes and distances.
 //
-// Training is not part of the GPU path: train() throws. A trained index comes from load() of a
-// .qvr file written by the reference (or by save()), or from set_trained() with centroids and
-// codebooks trained elsewhere.
+// train() gives the reference's centroids and codebooks bit for bit, with its k-means assignment
+// steps on the GPU. A trained index can also come from load() of a .qvr file written by the
+// reference (or by save()), or from set_trained() with centroids and codebooks trained elsewhere.
 //
 // Thread-safe: searches may run concurrently; add() encodes outside the lock and excludes
 // searches only while it appends.

@@ -46,7 +46,7 @@ typedef enum qv_status {
   QV_ERR_OOM = 3,         /* device or host allocation failed */
   QV_ERR_IO = 4,          /* file could not be read or written, or is corrupt */
   QV_ERR_STATE = 5,       /* e.g. add() before the index holds trained centroids */
-  QV_ERR_UNSUPPORTED = 6, /* outside the GPU path (IVF training) */
+  QV_ERR_UNSUPPORTED = 6, /* outside the GPU path's limits */
   QV_ERR_DEVICE = 7       /* a kernel reported an error through its status word */
 } qv_status;
 
@@ -161,8 +161,12 @@ typedef struct qv_ivfpq_params {
 /* IvfPqIndex(params): include/quiver/ivfpq_index.h:46 (src/ivfpq_index.cc:95-103). */
 qv_status qv_ivfpq_create(int device, const qv_ivfpq_params* params, qv_ivfpq** out);
 qv_status qv_ivfpq_destroy(qv_ivfpq* index);
-/* train(): include/quiver/ivfpq_index.h:53. Training is not part of the GPU path; this returns
- * QV_ERR_UNSUPPORTED. Trained state comes from qv_ivfpq_load or qv_ivfpq_set_trained. */
+/* train(vectors, n, pool): include/quiver/ivfpq_index.h:53 (src/ivfpq_index.cc:144-206,
+ * src/product_quantizer.cc:29-153). The coarse k-means and the PQ sub-space k-means run with their
+ * assignment steps on the GPU and the reference's random draws, double-precision cluster sums and
+ * empty-cluster splitting on the host, so the centroids and codebooks are bit-identical to the
+ * reference's for the same rows and parameters. Trained state can also come from qv_ivfpq_load or
+ * qv_ivfpq_set_trained. */
 qv_status qv_ivfpq_train(qv_ivfpq* index, const float* vectors, size_t n);
 /* Installs trained state (nlist x dim centroids, m x 256 x dsub codebooks), as load() does
  * (src/ivfpq_index.cc:531-543), including the L2 precomputed term table. */

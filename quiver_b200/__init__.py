@@ -194,8 +194,9 @@ class FlatIndex:
 
 class IvfPqIndex:
     """Inverted-file index over product-quantized residuals (reference:
-    include/quiver/ivfpq_index.h). Trained state comes from :meth:`load` (a ``.qvr`` written by the
-    reference or by :meth:`save`) or :meth:`set_trained`; training itself is not on the GPU path."""
+    include/quiver/ivfpq_index.h). :meth:`train` gives the reference's centroids and codebooks
+    bit for bit (its k-means assignment steps run on the GPU); trained state can also come from
+    :meth:`load` (a ``.qvr`` written by the reference or by :meth:`save`) or :meth:`set_trained`."""
 
     def __init__(self, dim: int, metric: str = "l2", nlist: int = 1024, m: int = 16,
                  store_vectors: bool = False, train_iterations: int = 20, seed: int = 1234,
@@ -224,6 +225,7 @@ class IvfPqIndex:
         return p, n.value, mem.value
 
     def train(self, vectors: ArrayLike, num_threads: int = 0) -> None:
+        """IvfPqIndex::train; ``num_threads`` is accepted for compatibility."""
         x = _as_matrix(vectors, self.dim)
         check(lib().qv_ivfpq_train(self._h, ptr(x), x.shape[0]))
 

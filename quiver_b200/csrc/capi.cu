@@ -830,11 +830,15 @@ qv_status qv_ivfpq_destroy(qv_ivfpq* index) {
 qv_status qv_ivfpq_train(qv_ivfpq* index, const float* vectors, size_t n) {
   return guarded([&] {
     QV_REQUIRE(index != nullptr, "null index");
-    (void)vectors;
-    (void)n;
-    fail(QV_ERR_UNSUPPORTED,
-         "IVF-PQ training is not part of the GPU search path: load a trained index (.qvr) or "
-         "install centroids and codebooks with set_trained");
+    QV_REQUIRE(vectors != nullptr || n == 0, "vectors must not be null");
+    IvfState& s = index->s;
+    QV_REQUIRE(n >= s.nlist && n >= static_cast<size_t>(kSubCentroids),
+               "IVF-PQ training needs at least max(nlist, 256) vectors");
+    check_finite(vectors, n * s.dim);  // src/ivfpq_index.cc:147
+    std::unique_lock lock(index->mu);
+    QV_REQUIRE(!s.trained, "index is already trained");
+    DeviceScope scope(s.device);
+    ivf_train(s, vectors, n, thread_stream(s.device));
   });
 }
 

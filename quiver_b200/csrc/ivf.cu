@@ -933,6 +933,18 @@ void ivf_set_trained(IvfState& s, const float* h_centroids, const float* h_codeb
   s.trained = true;
 }
 
+void nearest_centroids_device(const float* d_x, size_t n, const float* d_cents, size_t k,
+                              size_t dim, bool by_ip, float* d_cnorm2, uint32_t* d_assign,
+                              cudaStream_t st) {
+  if (n == 0) return;
+  centroid_norms_kernel<<<ceil_div(k, 256), 256, 0, st>>>(d_cents, k, static_cast<int>(dim),
+                                                          d_cnorm2);
+  check_launch("centroid_norms_kernel");
+  coarse_assign_kernel<<<ceil_div(n, kTileP), 256, 0, st>>>(d_x, n, d_cents, d_cnorm2, k,
+                                                            static_cast<int>(dim), by_ip, d_assign);
+  check_launch("coarse_assign_kernel");
+}
+
 void ivf_encode_device(const IvfState& s, const float* d_x, size_t n, uint32_t* d_assign,
                        uint8_t* d_codes, cudaStream_t st) {
   if (n == 0) return;

@@ -137,6 +137,15 @@ void ivf_set_trained(IvfState& s, const float* h_centroids, const float* h_codeb
 // Coarse assignment + PQ encode of n device rows (already normalized for cosine when needed).
 void ivf_encode_device(const IvfState& s, const float* d_x, size_t n, uint32_t* d_assign,
                        uint8_t* d_codes, cudaStream_t st);
+// CentroidTable::nearest_batch (src/internal/centroid_table.h:94-144) of n device rows against k
+// device centroids, bit-identical: ||c||^2 - 2<x,c> (or -<x,c> by_ip), first minimum. d_cnorm2:
+// k floats of scratch.
+void nearest_centroids_device(const float* d_x, size_t n, const float* d_cents, size_t k,
+                              size_t dim, bool by_ip, float* d_cnorm2, uint32_t* d_assign,
+                              cudaStream_t st);
+// IvfPqIndex::train (src/ivfpq_index.cc:144-206) with the assignments on the GPU; installs the
+// trained state. h_in: n x dim host rows.
+void ivf_train(IvfState& s, const float* h_in, size_t n, cudaStream_t st);
 // Normalizes n rows in place with simd::normalize semantics (cosine).
 void normalize_rows_device(float* d_x, size_t n, size_t dim, cudaStream_t st);
 // Rebuilds device list arrays from the host mirrors (+ optional device vectors in storage order).

@@ -2,8 +2,8 @@
 //
 // The cases restate the behaviour the reference's own C++ tests check (tests/test_flat.cc,
 // tests/test_thread_pool.cc, tests/test_regressions.cc, tests/test_quantizer.cc:140-175) against
-// this build; IVF-PQ cases start from a trained .qvr file because training is not part of the GPU
-// path. The program also has two dump modes that run FlatIndex / IvfPqIndex searches on inputs
+// this build; most IVF-PQ cases start from a trained .qvr file (training itself is checked bit for
+// bit against the reference in tests/test_ivf_gpu.py). The program also has two dump modes that run FlatIndex / IvfPqIndex searches on inputs
 // written by tests/test_cpp_api.py, which compares the outputs with the reference's results.
 //
 //   api_test cpu                 host-only cases (thread pool, filters, metrics, no-GPU errors)
@@ -399,7 +399,7 @@ void ivf_untrained_and_train(const std::string&) {
   EXPECT(!index.is_trained());
   const auto base = normal_rows(300, 16, 8);
   EXPECT_ERROR(index.add(base.data(), 1));  // untrained
-  EXPECT_ERROR(index.train(base.data(), 300));  // training is not on the GPU path
+  EXPECT_ERROR(index.train(base.data(), 200));  // fewer than max(nlist, 256) rows
   EXPECT(index.size() == 0 && index.dim() == 16 && index.params().nlist == 32);
   std::vector<Label> out(3);
   std::vector<float> dist(3);
@@ -408,6 +408,12 @@ void ivf_untrained_and_train(const std::string&) {
   IvfPqParams bad = p;
   bad.m = 5;  // does not divide dim
   EXPECT_ERROR(IvfPqIndex{bad});
+  index.train(base.data(), 300);  // trains (assignments on the GPU)
+  EXPECT(index.is_trained());
+  EXPECT_ERROR(index.train(base.data(), 300));  // already trained
+  index.add(base.data(), 300);
+  index.search_batch(base.data(), 1, 3, out.data(), dist.data());
+  EXPECT(out[0] == 0 && dist[0] >= 0.0f);  // the row itself is its own nearest neighbour
 }
 
 void ivf_filter_save_load(const std::string& qvr, const std::string& tmp) {

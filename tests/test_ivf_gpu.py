@@ -83,8 +83,8 @@ def test_errors_and_roundtrip(gpu, tmp_path, manifest):
     assert not ix.is_trained
     with pytest.raises(ValueError, match="trained"):
         ix.add(base[:3])
-    with pytest.raises(NotImplementedError):
-        ix.train(base)
+    with pytest.raises(ValueError, match="max\\(nlist, 256\\)"):
+        ix.train(base[:100])  # too few rows (src/ivfpq_index.cc:145)
     with pytest.raises(ValueError):
         gpu.IvfPqIndex(10, m=3)
     l, d = ix.search(q[:2], 4)
@@ -166,3 +166,35 @@ def test_many_lists_probe_selection(gpu, oracle, tmp_path):
         l, d = ix.search(q, 10, nprobe=nprobe, refine_factor=rf)
         wl, wd = oracle.ivf_search(qv, q, 10, nprobe, rf)
         assert_topk_parity(l, d, wl, wd, exact=True, what=f"nlist {nlist} nprobe {nprobe} {rf}")
+
+
+@pytest.mark.parametrize("metric,n,nlist,m,iters", [("l2", 20000, 128, 16, 6),
+                                                    ("cosine", 9000, 16, 8, 5),
+                                                    ("ip", 70000, 64, 4, 3)])
+def test_train_bit_exact_against_reference(gpu, reference, tmp_path, metric, n, nlist, m, iters):
+    """IvfPqIndex::train with the assignments on the GPU gives the reference's coarse centroids
+    and PQ codebooks bit for bit (src/ivfpq_index.cc:144-206, src/product_quantizer.cc:29-153):
+    empty clusters split (nlist 128 over 30 clusters), the k * 256 subsample (nlist 16 and 64),
+    cosine normalization, and the 65,536-row PQ subsample with inner-product cells (n = 70,000).
+    The trained index then adds and searches like the reference's."""
+    from oracle.oracle import QvrIvf
+    from quiver_b200.synthetic import clustered
+    base = clustered(n, 64, 30, 5)
+    q = clustered(64, 64, 30, 6)
+    ix = gpu.IvfPqIndex(64, metric, nlist, m, store_vectors=True, train_iterations=iters, seed=77)
+    ix.train(base)
+    assert ix.is_trained
+    with pytest.raises(ValueError, match="already trained"):
+        ix.train(base)
+    r = reference.ivf(64, metric, nlist, m, store_vectors=True, train_iterations=iters, seed=77)
+    r.train(base)
+    ix.save(tmp_path / "gpu.qvr")
+    r.save(tmp_path / "ref.qvr")
+    g, w = QvrIvf(tmp_path / "gpu.qvr"), QvrIvf(tmp_path / "ref.qvr")
+    assert np.array_equal(g.centroids, w.centroids), "coarse centroids differ"
+    assert np.array_equal(g.codebooks, w.codebooks), "PQ codebooks differ"
+    ix.add(base[:5000])
+    r.add(base[:5000])
+    l, d = ix.search(q, 10, nprobe=8, refine_factor=2)
+    rl, rd = r.search(q, 10, 8, 2)
+    assert_topk_parity(l, d, rl, rd, exact=True, what=f"trained {metric}")
