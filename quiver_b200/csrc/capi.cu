@@ -492,7 +492,10 @@ qv_status qv_last_search_stats(qv_search_stats* stats) {
 qv_status qv_set_timing(int enable) {
   return guarded([&] {
     if (thread_timing() && enable == 0) resolve_timers();  // release pending events
-    if (enable != 0 && !thread_timing()) t_stats = SearchStats{};
+    if (enable != 0 && !thread_timing()) {
+      t_stats = SearchStats{};
+      timing_count_slot();  // allocate the pinned slots now, not inside a timed search
+    }
     thread_timing() = enable != 0;
   });
 }
