@@ -70,7 +70,8 @@ struct Args {
   uint32_t* cand_r;
   int* cand_n;
   unsigned* thr_bits;
-  float* gbest;     // nq x KK: the KK best distances output by the query's finished units
+  float* gbest;     // nq x kMaxKK: the KK best distances output by the query's finished
+                    // units, sorted, padded with +inf
   int* glock;       // nq: try-lock guarding gbest[q]
   int* err;
   bool qmajor;      // unit order: query-tile-major (true) or row-chunk-major (false)
@@ -311,7 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = smem_u32(smem_b + stage * kAtoms * kAtomBytes);
           const uint32_t d_base = tmem_base + static_cast<uint32_t>(accb * kTiles * kN);
           if (kAtoms == 1) {
-            issue_tile<1, 4>(d_base, a_addr, b_addr);
+            switch (a.ksteps) {
+              case 1: issue_tile<1, 1>(d_base, a_addr, b_addr); break;
+              case 2: issue_tile<1, 2>(d_base, a_addr, b_addr); break;
+              case 3: issue_tile<1, 3>(d_base, a_addr, b_addr); break;
+              default: issue_tile<1, 4>(d_base, a_addr, b_addr); break;
+            }
           } else {
             switch (a.ksteps) {
               case 5: issue_tile<kAtoms, 5>(d_base, a_addr, b_addr); break;
@@ -496,10 +502,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       compact_buffer<kKK>(bd, br, cnt, thr);
       cnt = min(seen, kKK);  // the real entries: they sort before the padding
       if (active) {
+        // The whole list, padding included (the finalize reads cand_n entries), as 16-byte
+        // stores: a lane's list is contiguous in global memory, strided across lanes.
         const size_t slot = static_cast<size_t>(q) * a.n_chunks + chunk;
-        for (int i = 0; i < cnt; ++i) {
-          a.cand_d[slot * kKK + i] = bd[i * kLS];
-          a.cand_r[slot * kKK + i] = br[i * kLS];
+        static_assert(kKK % 4 == 0, "lists are written as float4 / uint4");
+        float4* cd = reinterpret_cast<float4*>(a.cand_d + slot * kKK);
+        uint4* cr = reinterpret_cast<uint4*>(a.cand_r + slot * kKK);
+#pragma unroll
+        for (int i = 0; i < kKK; i += 4) {
+          cd[i / 4] = make_float4(bd[i * kLS], bd[(i + 1) * kLS], bd[(i + 2) * kLS],
+                                  bd[(i + 3) * kLS]);
+          cr[i / 4] = make_uint4(br[i * kLS], br[(i + 1) * kLS], br[(i + 2) * kLS],
+                                 br[(i + 3) * kLS]);
         }
         a.cand_n[slot] = cnt;
         if (cnt == kKK) atomicMin(a.thr_bits + q, dev::ordered_bits(bd[(kKK - 1) * kLS]));
@@ -507,37 +521,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         // value as the query's threshold: kKK distinct output candidates lie at or below it, which
         // is all a threshold needs. Each unit merges once (its rows are disjoint from every other
         // unit's), under a try-lock: when another unit holds it the merge is skipped, which only
-        // leaves the bound looser. The list is staged in the free upper half of this query's
-        // buffer, so that all its loads are issued at once.
+        // leaves the bound looser.
         if (cnt > 0 && atomicCAS(a.glock + q, 0, 1) == 0) {
           __threadfence();
-          volatile float* gq = a.gbest + static_cast<size_t>(q) * kKK;
-          // Both lists are sorted, so each entry's place in the merged list is its index plus
-          // the number of entries of the other list before it (the running list first on ties);
-          // entries placed at kKK or beyond drop out.
-          float g[kKK];
+          volatile float* gq = a.gbest + static_cast<size_t>(q) * kMaxKK;
+          // Both lists are sorted ascending and padded with +inf to 32, so c[i] = min(g[i],
+          // b[31 - i]) holds the 32 smallest of both as a bitonic sequence, which a 32-input
+          // bitonic merge (distances only) sorts; its first kKK are the new running list.
+          float c[32];
 #pragma unroll
-          for (int o = 0; o < kKK; ++o) g[o] = gq[o];
-          float kth = kInfF;
-#pragma unroll
-          for (int o = 0; o < kKK; ++o) {
-            int before = 0;
-            for (int j = 0; j < cnt; ++j) before += bd[j * kLS] < g[o] ? 1 : 0;
-            const int pos = o + before;
-            if (pos < kKK) gq[pos] = g[o];
-            if (pos == kKK - 1) kth = g[o];
+          for (int i = 0; i < 32; ++i) {
+            const float gi = i < kKK ? gq[i] : kInfF;
+            const float bi = 31 - i < kKK ? bd[(31 - i) * kLS] : kInfF;
+            c[i] = fminf(gi, bi);
           }
-          for (int j = 0; j < cnt; ++j) {
-            const float dv = bd[j * kLS];
-            int before = 0;
 #pragma unroll
-            for (int o = 0; o < kKK; ++o) before += g[o] <= dv ? 1 : 0;
-            const int pos = j + before;
-            if (pos < kKK) gq[pos] = dv;
-            if (pos == kKK - 1) kth = dv;
+          for (int stride = 16; stride > 0; stride >>= 1) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int lo = 2 * i - (i & (stride - 1)), hi = lo + stride;
+              const float x = fminf(c[lo], c[hi]);
+              c[hi] = fmaxf(c[lo], c[hi]);
+              c[lo] = x;
+            }
           }
+#pragma unroll
+          for (int i = 0; i < kKK; ++i) gq[i] = c[i];
           __threadfence();
-          if (kth < kInfF) atomicMin(a.thr_bits + q, dev::ordered_bits(kth));
+          if (c[kKK - 1] < kInfF) atomicMin(a.thr_bits + q, dev::ordered_bits(c[kKK - 1]));
           atomicExch(a.glock + q, 0);
         }
       }
@@ -785,7 +796,7 @@ static TcScratch tc_scratch_layout(size_t kpad, size_t nq, int kk, size_t list_b
   L.q16 = take(nq_pad * kpad * sizeof(__half));
   L.qinv = take(nq * sizeof(float));
   L.qn2 = take(nq * sizeof(float));
-  L.gbest = take(nq * static_cast<size_t>(kk) * sizeof(float));
+  L.gbest = take(nq * static_cast<size_t>(std::max(kk, tc::kMaxKK)) * sizeof(float));
   L.glock = take(nq * sizeof(int));
   L.lists = take(list_bytes);
   L.total = off;
@@ -836,8 +847,9 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
                         cand_n, thr_bits, eps, err, mq, q16, qinv, qn2, base + L.lists, st);
     return;
   }
-  tc::init_best_kernel<<<static_cast<unsigned>(std::min<size_t>(ceil_div(nq * kk, 256), 1024)),
-                         256, 0, st>>>(gbest, nq * kk, glock, nq);
+  tc::init_best_kernel<<<static_cast<unsigned>(
+                             std::min<size_t>(ceil_div(nq * tc::kMaxKK, 256), 1024)),
+                         256, 0, st>>>(gbest, nq * tc::kMaxKK, glock, nq);
   check_launch("init_best_kernel");
   const CUtensorMap mq = tc::make_map(q16, nq_pad, kpad);
   const CUtensorMap mx = tc::make_map(s.x16.get(), s.n, kpad);
@@ -846,7 +858,9 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   a.n_qgroups = static_cast<int>(ceil_div(nq, group_rows));
   a.n_chunks = n_chunks;
   a.total_units = a.n_qgroups * n_chunks;
-  a.ksteps = kpad / 16;
+  // K steps of 16 elements cover the dimension; the zero padding beyond the last one (up to the
+  // 64-element atom) adds nothing to the products and is not multiplied.
+  a.ksteps = static_cast<int>(ceil_div(static_cast<size_t>(s.dim), 16));
   a.nrows = static_cast<int64_t>(s.n);
   a.chunk_rows = chunk_rows;
   a.l2 = l2;

@@ -161,9 +161,11 @@ def test_config0_full_size_against_reference(gpu, reference):
     assert_topk_parity(l, d, rl, rd, exact=True, what="config0")
 
 
-# dim 50 pads to one 64-column atom (4 K-steps); 72, 96, 100 and 128 take 5, 6, 7 and 8.
+# The MMAs take ceil(dim / 16) K-steps of 16: dims 20, 40 and 50 take 2, 3 and 4 in one
+# 64-column atom; 72, 96, 100 and 128 take 5, 6, 7 and 8 in two.
 @pytest.mark.parametrize("metric,dim", [("l2", 100), ("ip", 100), ("cosine", 100), ("l2", 50),
-                                        ("ip", 72), ("cosine", 96), ("l2", 128)])
+                                        ("ip", 72), ("cosine", 96), ("l2", 128), ("ip", 40),
+                                        ("cosine", 20)])
 def test_tensor_core_screen_equals_simt_screen(gpu, oracle, monkeypatch, metric, dim):
     """The tcgen05 fp16 screen and the float32 SIMT screen must produce identical final results
     (both are re-ranked exactly and certified)."""
