@@ -144,6 +144,63 @@ qv_status qv_flat_search_device_noalloc(const qv_flat* index, const float* queri
                                         void* stream);
 size_t qv_flat_noalloc_max_bytes(void);
 
+/* ---- HNSW vector storage and its filtered exact scan -------------------------------------------
+ * The part of quiver::HnswIndex (include/quiver/hnsw_index.h:53-121) that the GPU serves: the
+ * stored vectors (float32, or 8-bit scalar-quantized) and the exact scan HnswIndex::search takes
+ * when a filter admits at most exact_scan_threshold of the live vectors (search_exact,
+ * src/hnsw_index.cc:723-760). The graph walk stays with the host index. Nodes are numbered in
+ * insertion order (HNSW's NodeId). storage: QV_STORAGE_FLOAT32 or QV_STORAGE_SQ8
+ * (quiver::Storage, include/quiver/hnsw_index.h:25-28). */
+enum { QV_STORAGE_FLOAT32 = 0, QV_STORAGE_SQ8 = 1 };
+typedef struct qv_hnsw_store qv_hnsw_store;
+
+/* HnswIndex(params) storage part: include/quiver/hnsw_index.h:55 (src/hnsw_index.cc:791-812). */
+qv_status qv_hnsw_store_create(int device, size_t dim, uint32_t metric, uint32_t storage,
+                               qv_hnsw_store** out);
+qv_status qv_hnsw_store_destroy(qv_hnsw_store* store);
+/* train(vectors, n): include/quiver/hnsw_index.h:63 (src/hnsw_index.cc:1018-1028, :541-551,
+ * src/scalar_quantizer.cc:9-34): SQ8 only, once; the per-dimension ranges of the prepared
+ * (cosine: normalized) vectors, computed on the GPU. */
+qv_status qv_hnsw_store_train(qv_hnsw_store* store, const float* vectors, size_t n);
+qv_status qv_hnsw_store_is_trained(const qv_hnsw_store* store, int* trained);
+/* add(vectors, n, labels) storage part: include/quiver/hnsw_index.h:71-72 (src/hnsw_index.cc:
+ * 644-694, :553-564, :582-596): the reference's checks (finite values, the reserved label,
+ * duplicates in the call, labels already present and not removed), an untrained SQ8 store trains
+ * on a first batch of at least 256 vectors, then each vector is prepared (normalized for cosine)
+ * and stored or SQ8-encoded (src/scalar_quantizer.cc:46-52) on the GPU. labels NULL: node i of
+ * all ever inserted gets label i. */
+qv_status qv_hnsw_store_add(qv_hnsw_store* store, const float* vectors, size_t n,
+                            const uint64_t* labels);
+/* remove(label): include/quiver/hnsw_index.h:76 (src/hnsw_index.cc:1030-1042): soft delete;
+ * *removed = 1 when the label was present and live. */
+qv_status qv_hnsw_store_remove(qv_hnsw_store* store, uint64_t label, int* removed);
+/* size() (live vectors), number of nodes (removed included), dim(), metric(), storage(). */
+qv_status qv_hnsw_store_info(const qv_hnsw_store* store, size_t* live, size_t* nodes, size_t* dim,
+                             uint32_t* metric, uint32_t* storage);
+/* get_vector(label): include/quiver/hnsw_index.h:79-80: the stored vector (decoded for SQ8,
+ * normalized for cosine). */
+qv_status qv_hnsw_store_vector(const qv_hnsw_store* store, uint64_t label, float* vector);
+/* The stored SQ8 codes of nodes [first, first+count) (dim bytes each), and the trained
+ * (vmin, vscale) (dim floats each; either may be NULL). */
+qv_status qv_hnsw_store_codes(const qv_hnsw_store* store, size_t first, size_t count,
+                              uint8_t* codes);
+qv_status qv_hnsw_store_sq8_params(const qv_hnsw_store* store, float* vmin, float* vscale);
+/* The exact scan of HnswIndex::search_batch with a filter (src/hnsw_index.cc:723-760, :743-768):
+ * for each query (normalized for cosine) the k closest live nodes among those whose label the
+ * filter admits, with the storage's distance (l2sqr / 1 - dot, or l2sqr_sq8 / 1 - dot_sq8 for SQ8:
+ * the same bits), closest first, unfilled slots QV_INVALID_LABEL / +inf. A NULL filter scans every
+ * live node. The label set crosses as in qv_flat_search (QV_FILTER_POSITION_BITMAP: one bit per
+ * node). */
+qv_status qv_hnsw_store_search(const qv_hnsw_store* store, const float* queries, size_t nq,
+                               size_t k, const qv_filter* filter, uint64_t* labels,
+                               float* distances);
+/* The same with device buffers on the store's GPU; position_bitmap (one bit per node, may be
+ * NULL) is read, not modified; node_ids (may be NULL) receive each result's node id (UINT64_MAX
+ * when unfilled). It returns after a short host round trip that counts the admitted nodes. */
+qv_status qv_hnsw_store_search_device(const qv_hnsw_store* store, const float* queries, size_t nq,
+                                      size_t k, const uint64_t* position_bitmap, uint64_t* labels,
+                                      float* distances, uint64_t* node_ids, void* stream);
+
 /* ---- IvfPqIndex -------------------------------------------------------------------------------- */
 typedef struct qv_ivfpq qv_ivfpq;
 

@@ -91,6 +91,13 @@ class Oracle:
         L.qvo_l2_table.argtypes = [_f32p, _sz, _sz, _f32p, _f32p]
         L.qvo_ivf_search.argtypes = [C.c_void_p, _f32p, _sz, _sz, _sz, _sz, C.c_void_p,
                                      C.c_uint64, C.c_int, _u64p, _f32p]
+        for fn in (L.qvo_l2sqr_sq8, L.qvo_dot_sq8):
+            fn.restype = C.c_float
+            fn.argtypes = [_f32p, _u8p, _f32p, _f32p, _sz]
+        L.qvo_sq8_train.argtypes = [_f32p, _sz, _sz, _f32p, _f32p]
+        L.qvo_sq8_encode.argtypes = [_f32p, _f32p, _sz, _f32p, _sz, _u8p]
+        L.qvo_exact_scan.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, _sz, C.c_int,
+                                     _u32p, _sz, _f32p, _sz, _sz, _u32p, _f32p]
 
     def dot(self, a, b, order=ORDER_AVX2) -> float:
         a, b = _f32(a), _f32(b)
@@ -118,6 +125,49 @@ class Oracle:
                                       None if bm is None else bm.ctypes.data, universe, out_l, out_d)
         assert rc == 0
         return out_l, out_d
+
+    def l2sqr_sq8(self, q, code, vmin, vscale) -> float:
+        q, code = _f32(q), np.ascontiguousarray(code, dtype=np.uint8)
+        return float(self.lib.qvo_l2sqr_sq8(q, code, _f32(vmin), _f32(vscale), q.size))
+
+    def dot_sq8(self, q, code, vmin, vscale) -> float:
+        q, code = _f32(q), np.ascontiguousarray(code, dtype=np.uint8)
+        return float(self.lib.qvo_dot_sq8(q, code, _f32(vmin), _f32(vscale), q.size))
+
+    def sq8_train(self, x):
+        x = _f32(x)
+        vmin = np.empty(x.shape[1], np.float32)
+        vscale = np.empty(x.shape[1], np.float32)
+        assert self.lib.qvo_sq8_train(x, x.shape[0], x.shape[1], vmin, vscale) == 0
+        return vmin, vscale
+
+    def sq8_encode(self, vmin, vscale, x) -> np.ndarray:
+        x = _f32(x)
+        out = np.empty(x.shape, np.uint8)
+        self.lib.qvo_sq8_encode(_f32(vmin), _f32(vscale), x.shape[1], x, x.shape[0], out)
+        return out
+
+    def exact_scan(self, metric, queries, k, ids, rows=None, codes=None, vmin=None, vscale=None):
+        """HNSW's filtered exact scan over the listed node ids, on float32 rows or SQ8 codes
+        (stored as the index holds them: prepared for cosine). Returns (node ids, distances)."""
+        queries = _f32(queries)
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        nq = queries.shape[0]
+        out_i = np.empty((nq, k), np.uint32)
+        out_d = np.empty((nq, k), np.float32)
+        if codes is None:
+            data, storage = _f32(rows), 0
+            vmin = vscale = None
+            ptrs = (None, None)
+        else:
+            data, storage = np.ascontiguousarray(codes, dtype=np.uint8), 1
+            vmin, vscale = _f32(vmin), _f32(vscale)
+            ptrs = (vmin.ctypes.data, vscale.ctypes.data)
+        rc = self.lib.qvo_exact_scan(storage, data.ctypes.data, ptrs[0], ptrs[1], data.shape[1],
+                                     metric_code(metric), ids, ids.size, queries, nq, k, out_i,
+                                     out_d)
+        assert rc == 0
+        return out_i, out_d
 
     def coarse_assign(self, cents, x, by_ip=False) -> np.ndarray:
         cents, x = _f32(cents), _f32(x)
@@ -231,6 +281,19 @@ class Reference:
         L.qvref_nearest_batch.argtypes = [_f32p, _sz, _sz, _f32p, _sz, C.c_int, _u32p]
         L.qvref_pq_encode.argtypes = [_f32p, _sz, _sz, _f32p, _sz, _u8p]
         L.qvref_pq_tables.argtypes = [_f32p, _sz, _sz, _f32p, _f32p, _f32p]
+        for fn in (L.qvref_l2sqr_sq8, L.qvref_dot_sq8):
+            fn.restype = C.c_float
+            fn.argtypes = [_f32p, _u8p, _f32p, _f32p, _sz]
+        L.qvref_sq8_train.argtypes = [_f32p, _sz, _sz, _f32p, _f32p]
+        L.qvref_sq8_encode.argtypes = [_f32p, _f32p, _sz, _f32p, _sz, _u8p]
+        L.qvref_hnsw_new.argtypes = [_sz, C.c_uint32, C.c_uint32, _sz, _sz, C.c_uint64, vp]
+        L.qvref_hnsw_free.argtypes = [C.c_void_p]
+        L.qvref_hnsw_train.argtypes = [C.c_void_p, _f32p, _sz]
+        L.qvref_hnsw_add.argtypes = [C.c_void_p, _f32p, _sz, C.c_void_p, C.c_int]
+        L.qvref_hnsw_remove.argtypes = [C.c_void_p, C.c_uint64]
+        L.qvref_hnsw_vector.argtypes = [C.c_void_p, C.c_uint64, _f32p]
+        L.qvref_hnsw_search.argtypes = [C.c_void_p, _f32p, _sz, _sz, _sz, C.c_void_p, _sz,
+                                        C.c_int, C.c_double, C.c_int, _u64p, _f32p]
 
     def _check(self, rc: int) -> None:
         if rc != 0:
@@ -276,6 +339,31 @@ class Reference:
         l2 = np.empty((m, 256), np.float32)
         self._check(self.lib.qvref_pq_tables(_f32(codebooks), q.size, m, q, ip, l2))
         return ip, l2
+
+    def l2sqr_sq8(self, q, code, vmin, vscale) -> float:
+        q, code = _f32(q), np.ascontiguousarray(code, dtype=np.uint8)
+        return float(self.lib.qvref_l2sqr_sq8(q, code, _f32(vmin), _f32(vscale), q.size))
+
+    def dot_sq8(self, q, code, vmin, vscale) -> float:
+        q, code = _f32(q), np.ascontiguousarray(code, dtype=np.uint8)
+        return float(self.lib.qvref_dot_sq8(q, code, _f32(vmin), _f32(vscale), q.size))
+
+    def sq8_train(self, x):
+        x = _f32(x)
+        vmin = np.empty(x.shape[1], np.float32)
+        vscale = np.empty(x.shape[1], np.float32)
+        self._check(self.lib.qvref_sq8_train(x, x.shape[0], x.shape[1], vmin, vscale))
+        return vmin, vscale
+
+    def sq8_encode(self, vmin, vscale, x) -> np.ndarray:
+        x = _f32(x)
+        out = np.empty(x.shape, np.uint8)
+        self._check(self.lib.qvref_sq8_encode(_f32(vmin), _f32(vscale), x.shape[1], x,
+                                              x.shape[0], out))
+        return out
+
+    def hnsw(self, dim, metric, storage="float32", M=16, ef_construction=200, seed=0x5eed):
+        return RefHnsw(self, dim, metric, storage, M, ef_construction, seed)
 
     def flat(self, dim, metric):
         return RefFlat(self, dim, metric)
@@ -340,6 +428,50 @@ class RefFlat:
 
     def save(self, path):
         self.ref._check(self.ref.lib.qvref_flat_save(self.h, str(path).encode()))
+
+
+class RefHnsw:
+    """The reference HnswIndex; used for its filtered exact scan (exact_scan_threshold)."""
+
+    def __init__(self, ref: Reference, dim, metric, storage, M, ef_construction, seed):
+        self.ref, self.dim = ref, dim
+        self.h = C.c_void_p()
+        st = {"float32": 0, "sq8": 1}[storage]
+        ref._check(ref.lib.qvref_hnsw_new(dim, metric_code(metric), st, M, ef_construction, seed,
+                                          C.byref(self.h)))
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            self.ref.lib.qvref_hnsw_free(self.h)
+            self.h = None
+
+    def train(self, x):
+        x = _f32(x)
+        self.ref._check(self.ref.lib.qvref_hnsw_train(self.h, x, x.shape[0]))
+
+    def add(self, x, labels=None, threads=0):
+        x = _f32(x)
+        la, lp = _label_args(labels, x.shape[0])
+        self.ref._check(self.ref.lib.qvref_hnsw_add(self.h, x, x.shape[0], lp, threads))
+
+    def remove(self, label) -> bool:
+        return bool(self.ref.lib.qvref_hnsw_remove(self.h, int(label)))
+
+    def vector(self, label) -> np.ndarray:
+        out = np.empty(self.dim, np.float32)
+        self.ref._check(self.ref.lib.qvref_hnsw_vector(self.h, int(label), out))
+        return out
+
+    def search(self, q, k, allowed=None, ef=64, exact_scan_threshold=0.02, threads=0):
+        q = _f32(q)
+        nq = q.shape[0]
+        out_l = np.empty((nq, k), np.uint64)
+        out_d = np.empty((nq, k), np.float32)
+        a, ap, na, has = _filter_args(allowed)
+        self.ref._check(self.ref.lib.qvref_hnsw_search(self.h, q, nq, k, ef, ap, na, has,
+                                                       exact_scan_threshold, threads, out_l,
+                                                       out_d))
+        return out_l, out_d
 
 
 class RefIvf:

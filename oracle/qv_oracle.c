@@ -215,6 +215,148 @@ int qvo_flat_search(const float* base, const uint64_t* labels, size_t n, size_t 
   return 0;
 }
 
+/* ---- SQ8 storage and HNSW's filtered exact scan ------------------------------------------------
+ * src/scalar_quantizer.cc (train/encode/decode), src/simd/kernels_avx2.cc:25-31 (sq8_decode8),
+ * :85-129 (l2sqr_sq8, dot_sq8), src/hnsw_index.cc:541-551 (train on prepared vectors),
+ * :553-564 (init_node stores or encodes the prepared vector), :723-741 (search_exact). */
+
+/* One decoded component, vmin + code * vscale as one FMA (sq8_decode8's _mm256_fmadd_ps; GCC also
+ * contracts the scalar tail's decode into an FMA under the reference's flags). */
+static float sq8_dec(uint8_t c, float vmin, float vscale) { return fmaf((float)c, vscale, vmin); }
+
+/* src/simd/kernels_avx2.cc:85-106: two 8-lane FMA accumulators over 16-element blocks, then
+ * 8-element blocks into the first, lane-wise s0+s1, hsum, then the scalar tail, every element of
+ * which is (decode FMA, subtract, FMA into the sum): checked bit for bit against the compiled
+ * reference for every dim in 1..200. */
+float qvo_l2sqr_sq8(const float* q, const uint8_t* code, const float* vmin, const float* vscale,
+                    size_t dim) {
+  float s0[8], s1[8];
+  memset(s0, 0, sizeof(s0));
+  memset(s1, 0, sizeof(s1));
+  size_t i = 0;
+  for (; i + 16 <= dim; i += 16)
+    for (int l = 0; l < 8; ++l) {
+      const float d0 = q[i + l] - sq8_dec(code[i + l], vmin[i + l], vscale[i + l]);
+      const float d1 = q[i + 8 + l] - sq8_dec(code[i + 8 + l], vmin[i + 8 + l], vscale[i + 8 + l]);
+      s0[l] = fmaf(d0, d0, s0[l]);
+      s1[l] = fmaf(d1, d1, s1[l]);
+    }
+  for (; i + 8 <= dim; i += 8)
+    for (int l = 0; l < 8; ++l) {
+      const float d0 = q[i + l] - sq8_dec(code[i + l], vmin[i + l], vscale[i + l]);
+      s0[l] = fmaf(d0, d0, s0[l]);
+    }
+  float t[8];
+  for (int l = 0; l < 8; ++l) t[l] = s0[l] + s1[l];
+  float sum = hsum8(t);
+  for (; i < dim; ++i) {
+    const float d = q[i] - sq8_dec(code[i], vmin[i], vscale[i]);
+    sum = fmaf(d, d, sum);
+  }
+  return sum;
+}
+
+/* src/simd/kernels_avx2.cc:108-129, the same structure with q * decoded products. */
+float qvo_dot_sq8(const float* q, const uint8_t* code, const float* vmin, const float* vscale,
+                  size_t dim) {
+  float s0[8], s1[8];
+  memset(s0, 0, sizeof(s0));
+  memset(s1, 0, sizeof(s1));
+  size_t i = 0;
+  for (; i + 16 <= dim; i += 16)
+    for (int l = 0; l < 8; ++l) {
+      s0[l] = fmaf(q[i + l], sq8_dec(code[i + l], vmin[i + l], vscale[i + l]), s0[l]);
+      s1[l] = fmaf(q[i + 8 + l], sq8_dec(code[i + 8 + l], vmin[i + 8 + l], vscale[i + 8 + l]),
+                   s1[l]);
+    }
+  for (; i + 8 <= dim; i += 8)
+    for (int l = 0; l < 8; ++l)
+      s0[l] = fmaf(q[i + l], sq8_dec(code[i + l], vmin[i + l], vscale[i + l]), s0[l]);
+  float t[8];
+  for (int l = 0; l < 8; ++l) t[l] = s0[l] + s1[l];
+  float sum = hsum8(t);
+  for (; i < dim; ++i) sum = fmaf(q[i], sq8_dec(code[i], vmin[i], vscale[i]), sum);
+  return sum;
+}
+
+/* src/scalar_quantizer.cc:9-34: per-dimension [min, max]; scale = range / 255 (1 for a constant
+ * dimension). Returns -1 when the data holds NaN or infinity (the reference throws). */
+int qvo_sq8_train(const float* x, size_t n, size_t dim, float* vmin, float* vscale) {
+  int finite = 1;
+  for (size_t j = 0; j < dim; ++j) {
+    vmin[j] = INFINITY;
+    vscale[j] = -INFINITY; /* holds the maximum until the end */
+  }
+  for (size_t i = 0; i < n; ++i)
+    for (size_t j = 0; j < dim; ++j) {
+      const float v = x[i * dim + j];
+      finite &= isfinite(v) != 0;
+      if (v < vmin[j]) vmin[j] = v; /* std::min(lo, v) */
+      if (vscale[j] < v) vscale[j] = v; /* std::max(hi, v) */
+    }
+  if (!finite) return -1;
+  for (size_t j = 0; j < dim; ++j) {
+    const float range = vscale[j] - vmin[j];
+    if (!isfinite(range)) return -1;
+    vscale[j] = range > 0.0f ? range / 255.0f : 1.0f;
+  }
+  return 0;
+}
+
+/* src/scalar_quantizer.cc:46-52: round-to-nearest-even of (v - vmin) / vscale, clamped to 0..255
+ * (NaN lands on 0). */
+void qvo_sq8_encode(const float* vmin, const float* vscale, size_t dim, const float* x, size_t n,
+                    uint8_t* codes) {
+  for (size_t i = 0; i < n; ++i)
+    for (size_t j = 0; j < dim; ++j) {
+      const float t = nearbyintf((x[i * dim + j] - vmin[j]) / vscale[j]);
+      codes[i * dim + j] = (uint8_t)(t >= 255.0f ? 255.0f : (t > 0.0f ? t : 0.0f));
+    }
+}
+
+/* src/hnsw_index.cc:723-741 (search_exact) with FloatSpace / Sq8Space distances (:179-233): for
+ * each query (normalized first for cosine, :334-339), every listed node's distance (l2sqr, or
+ * 1 - dot for inner product and cosine; NaN -> +inf), the k best kept and sorted ascending,
+ * unfilled slots (UINT32_MAX, +inf). storage: 0 float32 rows (data = n x dim floats), 1 SQ8
+ * codes (data = n x dim bytes, vmin / vscale per dimension). out_ids are node ids. */
+int qvo_exact_scan(int storage, const void* data, const float* vmin, const float* vscale,
+                   size_t dim, int metric, const uint32_t* ids, size_t n_ids,
+                   const float* queries, size_t nq, size_t k, uint32_t* out_ids,
+                   float* out_dists) {
+  if (nq == 0 || k == 0) return 0;
+  float* q = (float*)malloc(dim * sizeof(float));
+  cand* heap = (cand*)malloc((k < n_ids ? k : n_ids) * sizeof(cand) + sizeof(cand));
+  if (!q || !heap) { free(q); free(heap); return -1; }
+  for (size_t qi = 0; qi < nq; ++qi) {
+    memcpy(q, queries + qi * dim, dim * sizeof(float));
+    if (metric == 2) normalize(q, dim, 2);
+    topk t = {heap, 0, k < n_ids ? k : n_ids};
+    for (size_t i = 0; i < n_ids; ++i) {
+      const size_t id = ids[i];
+      float d;
+      if (storage == 0) {
+        const float* x = (const float*)data + id * dim;
+        d = metric == 0 ? qvo_l2sqr(q, x, dim, 2) : 1.0f - qvo_dot(q, x, dim, 2);
+      } else {
+        const uint8_t* c = (const uint8_t*)data + id * dim;
+        d = metric == 0 ? qvo_l2sqr_sq8(q, c, vmin, vscale, dim)
+                        : 1.0f - qvo_dot_sq8(q, c, vmin, vscale, dim);
+      }
+      if (d != d) d = INFINITY;
+      cand c = {d, id};
+      topk_push(&t, c);
+    }
+    qsort(t.h, t.n, sizeof(cand), cand_cmp);
+    for (size_t j = 0; j < k; ++j) {
+      out_ids[qi * k + j] = j < t.n ? (uint32_t)t.h[j].id : UINT32_MAX;
+      out_dists[qi * k + j] = j < t.n ? t.h[j].d : INFINITY;
+    }
+  }
+  free(q);
+  free(heap);
+  return 0;
+}
+
 /* ---- CentroidTable: src/internal/centroid_table.h:43-59 (reset), :65-75 (l2), :78-85 (dot),
  *      :94-144 (nearest_batch), :155-170 (argmin_n) -------------------------------------------- */
 

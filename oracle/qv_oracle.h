@@ -28,6 +28,18 @@ int qvo_flat_search(const float* base, const uint64_t* labels, size_t n, size_t 
                     int order, const float* queries, size_t nq, size_t k, const uint64_t* bitmap,
                     uint64_t universe, uint64_t* out_labels, float* out_dists);
 
+float qvo_l2sqr_sq8(const float* q, const uint8_t* code, const float* vmin, const float* vscale,
+                    size_t dim);
+float qvo_dot_sq8(const float* q, const uint8_t* code, const float* vmin, const float* vscale,
+                  size_t dim);
+int qvo_sq8_train(const float* x, size_t n, size_t dim, float* vmin, float* vscale);
+void qvo_sq8_encode(const float* vmin, const float* vscale, size_t dim, const float* x, size_t n,
+                    uint8_t* codes);
+int qvo_exact_scan(int storage, const void* data, const float* vmin, const float* vscale,
+                   size_t dim, int metric, const uint32_t* ids, size_t n_ids,
+                   const float* queries, size_t nq, size_t k, uint32_t* out_ids,
+                   float* out_dists);
+
 void qvo_centroid_norms(const float* cents, size_t k, size_t dim, float* norms);
 void qvo_coarse_assign(const float* cents, size_t nlist, size_t dim, const float* x, size_t n,
                        int by_ip, uint32_t* out);

@@ -15,6 +15,7 @@
 #include "quiver/distance.h"
 #include "quiver/filter.h"
 #include "quiver/flat_index.h"
+#include "quiver/hnsw_index.h"
 #include "quiver/ivfpq_index.h"
 #include "quiver/quantizer.h"
 #include "quiver/thread_pool.h"
@@ -201,6 +202,93 @@ int qvref_pq_tables(const float* codebooks, std::size_t dim, std::size_t m, cons
     pq.set_centroids(std::vector<float>(codebooks, codebooks + 256 * dim));
     pq.compute_ip_table(q, ip_table);
     pq.compute_l2_table(q, l2_table);
+  });
+}
+
+// ---- SQ8 kernels, ScalarQuantizer and HnswIndex (the filtered exact-scan fallback) --------------
+
+float qvref_l2sqr_sq8(const float* q, const std::uint8_t* code, const float* vmin,
+                      const float* vscale, std::size_t dim) {
+  return quiver::simd::active().l2sqr_sq8(q, code, vmin, vscale, dim);
+}
+
+float qvref_dot_sq8(const float* q, const std::uint8_t* code, const float* vmin,
+                    const float* vscale, std::size_t dim) {
+  return quiver::simd::active().dot_sq8(q, code, vmin, vscale, dim);
+}
+
+int qvref_sq8_train(const float* x, std::size_t n, std::size_t dim, float* vmin, float* vscale) {
+  return guard([&] {
+    quiver::ScalarQuantizer sq(dim);
+    sq.train(x, n);
+    std::memcpy(vmin, sq.vmin(), dim * sizeof(float));
+    std::memcpy(vscale, sq.vscale(), dim * sizeof(float));
+  });
+}
+
+int qvref_sq8_encode(const float* vmin, const float* vscale, std::size_t dim, const float* x,
+                     std::size_t n, std::uint8_t* codes) {
+  return guard([&] {
+    quiver::ScalarQuantizer sq(dim);
+    sq.set_params(std::vector<float>(vmin, vmin + dim), std::vector<float>(vscale, vscale + dim));
+    for (std::size_t i = 0; i < n; ++i) sq.encode(x + i * dim, codes + i * dim);
+  });
+}
+
+// storage: 0 = float32, 1 = SQ8 (quiver::Storage).
+int qvref_hnsw_new(std::size_t dim, std::uint32_t metric, std::uint32_t storage, std::size_t M,
+                   std::size_t ef_construction, std::uint64_t seed, void** out) {
+  return guard([&] {
+    quiver::HnswParams p;
+    p.dim = dim;
+    p.metric = static_cast<quiver::Metric>(metric);
+    p.storage = static_cast<quiver::Storage>(storage);
+    p.M = M;
+    p.ef_construction = ef_construction;
+    p.seed = seed;
+    *out = new quiver::HnswIndex(p);
+  });
+}
+
+void qvref_hnsw_free(void* h) { delete static_cast<quiver::HnswIndex*>(h); }
+
+int qvref_hnsw_train(void* h, const float* x, std::size_t n) {
+  return guard([&] { static_cast<quiver::HnswIndex*>(h)->train(x, n); });
+}
+
+int qvref_hnsw_add(void* h, const float* x, std::size_t n, const std::uint64_t* labels,
+                   int threads) {
+  return guard(
+      [&] { static_cast<quiver::HnswIndex*>(h)->add(x, n, labels, pool_for(threads)); });
+}
+
+int qvref_hnsw_remove(void* h, std::uint64_t label) {
+  return static_cast<quiver::HnswIndex*>(h)->remove(label) ? 1 : 0;
+}
+
+// The stored vector of `label` as the index holds it (decoded for SQ8, normalized for cosine).
+int qvref_hnsw_vector(void* h, std::uint64_t label, float* out) {
+  return guard([&] {
+    const std::vector<float> v = static_cast<quiver::HnswIndex*>(h)->get_vector(label);
+    std::memcpy(out, v.data(), v.size() * sizeof(float));
+  });
+}
+
+// Searches with an allowed-label filter; exact_scan_threshold as HnswSearchParams (1.0 makes every
+// filter whose cardinality is known take the exact scan).
+int qvref_hnsw_search(void* h, const float* q, std::size_t nq, std::size_t k, std::size_t ef,
+                      const std::uint64_t* allowed, std::size_t n_allowed, int has_filter,
+                      double exact_scan_threshold, int threads, std::uint64_t* labels,
+                      float* dists) {
+  return guard([&] {
+    std::unique_ptr<quiver::Filter> f;
+    if (has_filter) f = make_filter(allowed, n_allowed);
+    quiver::HnswSearchParams p;
+    p.ef = ef;
+    p.filter = f.get();
+    p.exact_scan_threshold = exact_scan_threshold;
+    static_cast<quiver::HnswIndex*>(h)->search_batch(q, nq, k, labels, dists, p,
+                                                     pool_for(threads));
   });
 }
 

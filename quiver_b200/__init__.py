@@ -23,7 +23,8 @@ import numpy as np
 from . import _native
 from ._native import QuiverError, check, device_count, last_search_stats, lib, make_filter, ptr
 
-__all__ = ["FlatIndex", "IvfPqIndex", "QuiverError", "device_count", "last_search_stats"]
+__all__ = ["FlatIndex", "IvfPqIndex", "HnswStore", "QuiverError", "device_count",
+           "last_search_stats"]
 __version__ = "0.1.0"
 
 ArrayLike = Union[np.ndarray, Iterable]
@@ -328,3 +329,115 @@ class IvfPqIndex:
 
     def __repr__(self) -> str:
         return f"IvfPqIndex(dim={self.dim}, nlist={self.nlist}, m={self.m}, size={len(self)})"
+
+
+class HnswStore:
+    """The vector storage of an HNSW index on one GPU and the exact scan ``HnswIndex.search``
+    falls back to when a filter admits few vectors (reference: include/quiver/hnsw_index.h:25-121,
+    src/hnsw_index.cc:723-760). ``storage`` is ``"float32"`` or ``"sq8"`` (8-bit scalar
+    quantization, trained once on prepared vectors). Nodes are numbered in insertion order.
+    :meth:`search` returns what the reference's filtered search returns when it takes the exact
+    scan, bit for bit."""
+
+    def __init__(self, dim: int, metric: str = "l2", storage: str = "float32", *,
+                 device: int = 0):
+        if storage not in _native.STORAGE_CODES:
+            raise ValueError(f"unknown storage '{storage}' (expected float32 or sq8)")
+        self._h = C.c_void_p()
+        check(lib().qv_hnsw_store_create(int(device), int(dim), _metric_code(metric),
+                                         _native.STORAGE_CODES[storage], C.byref(self._h)))
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            self._h = None
+            try:
+                lib().qv_hnsw_store_destroy(h)
+            except (TypeError, AttributeError):
+                pass
+
+    def _info(self):
+        live, nodes, d = C.c_size_t(), C.c_size_t(), C.c_size_t()
+        m, st = C.c_uint32(), C.c_uint32()
+        check(lib().qv_hnsw_store_info(self._h, C.byref(live), C.byref(nodes), C.byref(d),
+                                       C.byref(m), C.byref(st)))
+        return live.value, nodes.value, d.value, m.value, st.value
+
+    def train(self, vectors: ArrayLike) -> None:
+        x = _as_matrix(vectors, self.dim)
+        check(lib().qv_hnsw_store_train(self._h, ptr(x), x.shape[0]))
+
+    @property
+    def is_trained(self) -> bool:
+        t = C.c_int()
+        check(lib().qv_hnsw_store_is_trained(self._h, C.byref(t)))
+        return bool(t.value)
+
+    def add(self, vectors: ArrayLike, labels: Optional[ArrayLike] = None) -> None:
+        x = _as_matrix(vectors, self.dim)
+        la = _as_labels(labels, x.shape[0])
+        check(lib().qv_hnsw_store_add(self._h, ptr(x), x.shape[0], ptr(la)))
+
+    def remove(self, label: int) -> bool:
+        r = C.c_int()
+        check(lib().qv_hnsw_store_remove(self._h, int(label), C.byref(r)))
+        return bool(r.value)
+
+    def get_vector(self, label: int) -> np.ndarray:
+        """The stored vector (decoded for SQ8, normalized for cosine)."""
+        out = np.empty(self.dim, np.float32)
+        check(lib().qv_hnsw_store_vector(self._h, int(label), ptr(out)))
+        return out
+
+    def codes(self, first: int = 0, count: Optional[int] = None) -> np.ndarray:
+        """SQ8 codes of nodes [first, first + count)."""
+        n = self.num_nodes
+        count = n - first if count is None else count
+        out = np.empty((count, self.dim), np.uint8)
+        check(lib().qv_hnsw_store_codes(self._h, int(first), int(count), ptr(out)))
+        return out
+
+    def sq8_params(self) -> Tuple[np.ndarray, np.ndarray]:
+        vmin = np.empty(self.dim, np.float32)
+        vscale = np.empty(self.dim, np.float32)
+        check(lib().qv_hnsw_store_sq8_params(self._h, ptr(vmin), ptr(vscale)))
+        return vmin, vscale
+
+    def search(self, queries: ArrayLike, k: int = 10, filter: Optional[ArrayLike] = None
+               ) -> Tuple[np.ndarray, np.ndarray]:
+        """Exact scan over the live vectors whose label ``filter`` admits (every live vector when
+        None). Returns (labels int64 [nq, k], distances float32 [nq, k])."""
+        q = _as_matrix(queries, self.dim)
+        if k <= 0:
+            raise ValueError("k must be positive")
+        allowed = _as_labels(filter) if filter is not None else None
+        f, keep = make_filter(allowed)
+        labels, dists = _result_arrays(q.shape[0], int(k))
+        check(lib().qv_hnsw_store_search(self._h, ptr(q), q.shape[0], int(k),
+                                         C.byref(f) if f is not None else None, ptr(labels),
+                                         ptr(dists)))
+        del keep
+        return _results(labels, dists)
+
+    def __len__(self) -> int:
+        return self._info()[0]
+
+    @property
+    def num_nodes(self) -> int:
+        return self._info()[1]
+
+    @property
+    def dim(self) -> int:
+        return self._info()[2]
+
+    @property
+    def metric(self) -> str:
+        return _native.METRIC_NAMES[self._info()[3]]
+
+    @property
+    def storage(self) -> str:
+        return _native.STORAGE_NAMES[self._info()[4]]
+
+    def __repr__(self) -> str:
+        return (f"HnswStore(dim={self.dim}, metric={self.metric!r}, storage={self.storage!r}, "
+                f"size={len(self)})")

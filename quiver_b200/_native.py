@@ -21,6 +21,8 @@ QV_FILTER_LABEL_SET, QV_FILTER_LABEL_BITMAP, QV_FILTER_POSITION_BITMAP = 1, 2, 3
 METRIC_CODES = {"l2": 0, "euclidean": 0, "ip": 1, "inner_product": 1, "dot": 1, "cosine": 2,
                 "cos": 2, "angular": 2}
 METRIC_NAMES = {0: "l2", 1: "ip", 2: "cosine"}
+STORAGE_CODES = {"float32": 0, "sq8": 1}
+STORAGE_NAMES = {0: "float32", 1: "sq8"}
 
 
 class qv_filter(C.Structure):
@@ -83,6 +85,19 @@ _SIGNATURES = {
     "qv_ivfpq_load": (_int, [_int, C.c_char_p, _int, _PP]),
     "qv_ivfpq_load_shard": (_int, [_int, C.c_char_p, _int, _u64, _u64, _PP]),
     "qv_ivfpq_set_list_base": (_int, [_vp, _vp]),
+    "qv_hnsw_store_create": (_int, [_int, _sz, _u32, _u32, _PP]),
+    "qv_hnsw_store_destroy": (_int, [_vp]),
+    "qv_hnsw_store_train": (_int, [_vp, _vp, _sz]),
+    "qv_hnsw_store_is_trained": (_int, [_vp, C.POINTER(_int)]),
+    "qv_hnsw_store_add": (_int, [_vp, _vp, _sz, _vp]),
+    "qv_hnsw_store_remove": (_int, [_vp, _u64, C.POINTER(_int)]),
+    "qv_hnsw_store_info": (_int, [_vp, C.POINTER(_sz), C.POINTER(_sz), C.POINTER(_sz),
+                                  C.POINTER(_u32), C.POINTER(_u32)]),
+    "qv_hnsw_store_vector": (_int, [_vp, _u64, _vp]),
+    "qv_hnsw_store_codes": (_int, [_vp, _sz, _sz, _vp]),
+    "qv_hnsw_store_sq8_params": (_int, [_vp, _vp, _vp]),
+    "qv_hnsw_store_search": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _vp]),
+    "qv_hnsw_store_search_device": (_int, [_vp, _vp, _sz, _sz, _vp, _vp, _vp, _vp, _vp]),
     "qv_merge_topk_device": (_int, [_int, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "qv_select_topk_device": (_int, [_int, _sz, _sz, _sz, _vp, _vp, _vp, _vp, _vp, _vp, _vp]),
 }

@@ -26,6 +26,11 @@ struct qv_ivfpq {
   mutable std::shared_mutex mu;
 };
 
+struct qv_hnsw_store {
+  qv::HnswStoreState s;
+  mutable std::shared_mutex mu;  // searches shared; add, train and remove exclusive
+};
+
 namespace qv {
 
 namespace {
@@ -1123,6 +1128,264 @@ qv_status qv_ivfpq_set_list_base(qv_ivfpq* index, const uint32_t* base) {
     QV_CUDA(cudaMemcpyAsync(s.global_base.get(), s.host_global_base.data(),
                             s.nlist * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
     QV_CUDA(cudaStreamSynchronize(st));
+  });
+}
+
+// ---- HNSW storage and exact scan -------------------------------------------------------------------
+
+qv_status qv_hnsw_store_create(int device, size_t dim, uint32_t metric, uint32_t storage,
+                               qv_hnsw_store** out) {
+  return guarded([&] {
+    QV_REQUIRE(out != nullptr, "null argument");
+    QV_REQUIRE(dim >= 1 && dim <= kMaxDimension,
+               "dimension must be in [1, " + std::to_string(kMaxDimension) + "]");
+    check_metric(metric);
+    QV_REQUIRE(storage == QV_STORAGE_FLOAT32 || storage == QV_STORAGE_SQ8, "unknown storage");
+    int ndev = 0;
+    QV_CUDA(cudaGetDeviceCount(&ndev));
+    QV_REQUIRE(device >= 0 && device < ndev, "no CUDA device " + std::to_string(device));
+    auto h = std::make_unique<qv_hnsw_store>();
+    h->s.flat.device = device;
+    h->s.flat.dim = dim;
+    h->s.flat.metric = metric;
+    h->s.storage = storage;
+    h->s.flat.sum_order = storage == QV_STORAGE_SQ8 ? kSumOrderSq8 : kSumOrderF32;
+    *out = h.release();
+  });
+}
+
+qv_status qv_hnsw_store_destroy(qv_hnsw_store* store) {
+  return guarded([&] {
+    if (store == nullptr) return;
+    DeviceScope scope(store->s.flat.device);
+    delete store;
+  });
+}
+
+namespace {
+// Uploads n host rows and prepares them as HnswIndex does (src/hnsw_index.cc:334-339).
+DeviceBuffer upload_prepared(const HnswStoreState& s, const float* vectors, size_t n,
+                             cudaStream_t st) {
+  DeviceBuffer d;
+  h2d(d, vectors, n * s.flat.dim, st);
+  if (s.flat.metric == QV_METRIC_COSINE) normalize_rows_device(d.get<float>(), n, s.flat.dim, st);
+  return d;
+}
+}  // namespace
+
+qv_status qv_hnsw_store_train(qv_hnsw_store* store, const float* vectors, size_t n) {
+  return guarded([&] {
+    QV_REQUIRE(store != nullptr, "null store");
+    HnswStoreState& s = store->s;
+    QV_REQUIRE(s.storage == QV_STORAGE_SQ8, "train() only applies to SQ8 storage");
+    QV_REQUIRE(vectors != nullptr && n > 0, "train() needs at least one vector");
+    check_finite(vectors, n * s.flat.dim);
+    std::unique_lock lock(store->mu);
+    QV_REQUIRE(!s.trained, "index is already trained (SQ8 parameters cannot change once set)");
+    DeviceScope scope(s.flat.device);
+    cudaStream_t st = thread_stream(s.flat.device);
+    DeviceBuffer d = upload_prepared(s, vectors, n, st);
+    hnsw_sq8_train(s, d.get<float>(), n, st);
+  });
+}
+
+qv_status qv_hnsw_store_is_trained(const qv_hnsw_store* store, int* trained) {
+  return guarded([&] {
+    QV_REQUIRE(store != nullptr && trained != nullptr, "null argument");
+    std::shared_lock lock(store->mu);
+    *trained = store->s.storage == QV_STORAGE_FLOAT32 || store->s.trained ? 1 : 0;
+  });
+}
+
+qv_status qv_hnsw_store_add(qv_hnsw_store* store, const float* vectors, size_t n,
+                            const uint64_t* labels) {
+  return guarded([&] {
+    QV_REQUIRE(store != nullptr, "null store");
+    if (n == 0) return;
+    QV_REQUIRE(vectors != nullptr, "vectors must not be null");
+    HnswStoreState& s = store->s;
+    check_finite(vectors, n * s.flat.dim);
+    check_labels(labels, n);
+    if (labels != nullptr && n > 1) {
+      std::vector<uint64_t> sorted(labels, labels + n);
+      std::sort(sorted.begin(), sorted.end());
+      QV_REQUIRE(std::adjacent_find(sorted.begin(), sorted.end()) == sorted.end(),
+                 "duplicate labels within one add() call");
+    }
+    std::unique_lock lock(store->mu);
+    DeviceScope scope(s.flat.device);
+    cudaStream_t st = thread_stream(s.flat.device);
+    const size_t base = s.flat.n;
+    QV_REQUIRE(base + n <= std::numeric_limits<uint32_t>::max(),
+               "index is full (maximum " + std::to_string(std::numeric_limits<uint32_t>::max()) +
+                   " vectors)");
+    std::vector<uint64_t> lab(n);
+    for (size_t i = 0; i < n; ++i) lab[i] = labels ? labels[i] : base + i;
+    // Validate everything before changing anything (src/hnsw_index.cc:588-596): a label may map
+    // to a removed node (the mapping is replaced), not to a live one.
+    for (uint64_t l : lab) {
+      const auto it = s.label_to_id.find(l);
+      QV_REQUIRE(it == s.label_to_id.end() ||
+                     ((s.host_removed[it->second >> 6] >> (it->second & 63)) & 1ull) != 0,
+                 "label " + std::to_string(l) + " is already in the index");
+    }
+    DeviceBuffer d = upload_prepared(s, vectors, n, st);
+    if (s.storage == QV_STORAGE_SQ8 && !s.trained) {
+      QV_REQUIRE(n >= 256,
+                 "SQ8 index is untrained: call train() with a representative sample, or make the "
+                 "first add() at least 256 vectors");
+      hnsw_sq8_train(s, d.get<float>(), n, st);
+    }
+    DeviceBuffer dl;
+    h2d(dl, lab.data(), n, st);
+    hnsw_store_append(s, d.get<float>(), dl.get<uint64_t>(), n, st);  // waits for the GPU
+    s.flat.host_labels.insert(s.flat.host_labels.end(), lab.begin(), lab.end());
+    for (size_t i = 0; i < n; ++i) s.label_to_id[lab[i]] = static_cast<uint32_t>(base + i);
+    QV_CUDA(cudaStreamSynchronize(st));
+  });
+}
+
+qv_status qv_hnsw_store_remove(qv_hnsw_store* store, uint64_t label, int* removed) {
+  return guarded([&] {
+    QV_REQUIRE(store != nullptr, "null store");
+    HnswStoreState& s = store->s;
+    std::unique_lock lock(store->mu);
+    int done = 0;
+    const auto it = s.label_to_id.find(label);
+    if (it != s.label_to_id.end()) {
+      const uint32_t id = it->second;
+      if (((s.host_removed[id >> 6] >> (id & 63)) & 1ull) == 0) {
+        DeviceScope scope(s.flat.device);
+        hnsw_store_mark_removed(s, id, thread_stream(s.flat.device));
+        done = 1;
+      }
+    }
+    if (removed) *removed = done;
+  });
+}
+
+qv_status qv_hnsw_store_info(const qv_hnsw_store* store, size_t* live, size_t* nodes, size_t* dim,
+                             uint32_t* metric, uint32_t* storage) {
+  return guarded([&] {
+    QV_REQUIRE(store != nullptr, "null store");
+    std::shared_lock lock(store->mu);
+    const HnswStoreState& s = store->s;
+    if (live) *live = s.flat.n - s.removed_count;
+    if (nodes) *nodes = s.flat.n;
+    if (dim) *dim = s.flat.dim;
+    if (metric) *metric = s.flat.metric;
+    if (storage) *storage = s.storage;
+  });
+}
+
+qv_status qv_hnsw_store_vector(const qv_hnsw_store* store, uint64_t label, float* vector) {
+  return guarded([&] {
+    QV_REQUIRE(store != nullptr && vector != nullptr, "null argument");
+    std::shared_lock lock(store->mu);
+    const HnswStoreState& s = store->s;
+    const auto it = s.label_to_id.find(label);
+    QV_REQUIRE(it != s.label_to_id.end() &&
+                   ((s.host_removed[it->second >> 6] >> (it->second & 63)) & 1ull) == 0,
+               "label " + std::to_string(label) + " is not in the index");
+    DeviceScope scope(s.flat.device);
+    cudaStream_t st = thread_stream(s.flat.device);
+    QV_CUDA(cudaMemcpyAsync(vector, s.flat.x.get<float>() + it->second * s.flat.dim,
+                            s.flat.dim * sizeof(float), cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaStreamSynchronize(st));
+  });
+}
+
+qv_status qv_hnsw_store_codes(const qv_hnsw_store* store, size_t first, size_t count,
+                              uint8_t* codes) {
+  return guarded([&] {
+    QV_REQUIRE(store != nullptr && codes != nullptr, "null argument");
+    std::shared_lock lock(store->mu);
+    const HnswStoreState& s = store->s;
+    QV_REQUIRE(s.storage == QV_STORAGE_SQ8, "the store does not hold SQ8 codes");
+    QV_REQUIRE(first <= s.flat.n && count <= s.flat.n - first, "node range out of bounds");
+    if (count == 0) return;
+    DeviceScope scope(s.flat.device);
+    cudaStream_t st = thread_stream(s.flat.device);
+    QV_CUDA(cudaMemcpyAsync(codes, s.codes.get<uint8_t>() + first * s.flat.dim,
+                            count * s.flat.dim, cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaStreamSynchronize(st));
+  });
+}
+
+qv_status qv_hnsw_store_sq8_params(const qv_hnsw_store* store, float* vmin, float* vscale) {
+  return guarded([&] {
+    QV_REQUIRE(store != nullptr, "null store");
+    std::shared_lock lock(store->mu);
+    const HnswStoreState& s = store->s;
+    QV_REQUIRE(s.storage == QV_STORAGE_SQ8 && s.trained, "the store holds no SQ8 parameters");
+    if (vmin) std::memcpy(vmin, s.host_vmin.data(), s.flat.dim * sizeof(float));
+    if (vscale) std::memcpy(vscale, s.host_vscale.data(), s.flat.dim * sizeof(float));
+  });
+}
+
+qv_status qv_hnsw_store_search(const qv_hnsw_store* store, const float* queries, size_t nq,
+                               size_t k, const qv_filter* filter, uint64_t* labels,
+                               float* distances) {
+  return guarded([&] {
+    begin_search_stats();
+    QV_REQUIRE(store != nullptr, "null store");
+    if (nq == 0 || k == 0) return;
+    QV_REQUIRE(queries != nullptr && labels != nullptr && distances != nullptr,
+               "search_batch: null buffer");
+    const HnswStoreState& s = store->s;
+    const size_t total = result_size(nq, k);
+    std::shared_lock lock(store->mu);
+    DeviceScope scope(s.flat.device);
+    cudaStream_t st = thread_stream(s.flat.device);
+    SearchFlags& flags = thread_search_flags(s.flat.device);
+    DeviceBuffer dq, dl(total * sizeof(uint64_t), st), dd(total * sizeof(float), st);
+    QV_CUDA(cudaMemsetAsync(flags.sync_dev, 0, kSearchFlagWords * sizeof(int), st));
+    h2d(dq, queries, nq * s.flat.dim, st);
+    DeviceBuffer bm = s.flat.n > 0 ? device_filter(s.flat.labels.get<uint64_t>(), s.flat.n,
+                                                   filter, st)
+                                   : DeviceBuffer();
+    if (bm.bytes() == 0) bm.allocate(std::max<size_t>(1, (s.flat.n + 63) / 64) * 8, st);
+    hnsw_store_search(s, dq.get<float>(), nq, k, bm.get<uint64_t>(), filter != nullptr,
+                      dl.get<uint64_t>(), dd.get<float>(), nullptr, flags.sync_dev, st);
+    QV_CUDA(cudaMemcpyAsync(flags.sync_host, flags.sync_dev, kSearchFlagWords * sizeof(int),
+                            cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaMemcpyAsync(labels, dl.get(), total * sizeof(uint64_t), cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaMemcpyAsync(distances, dd.get(), total * sizeof(float), cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaStreamSynchronize(st));
+    report_flags(flags.sync_host);
+  });
+}
+
+qv_status qv_hnsw_store_search_device(const qv_hnsw_store* store, const float* queries, size_t nq,
+                                      size_t k, const uint64_t* position_bitmap, uint64_t* labels,
+                                      float* distances, uint64_t* node_ids, void* stream) {
+  return guarded([&] {
+    begin_search_stats();
+    QV_REQUIRE(store != nullptr, "null store");
+    if (nq == 0 || k == 0) return;
+    QV_REQUIRE(queries != nullptr && labels != nullptr && distances != nullptr,
+               "search_batch: null buffer");
+    result_size(nq, k);
+    const HnswStoreState& s = store->s;
+    std::shared_lock lock(store->mu);
+    DeviceScope scope(s.flat.device);
+    CallerStream call_stream(stream, s.flat.device);
+    cudaStream_t st = call_stream.get();
+    SearchFlags& flags = thread_search_flags(s.flat.device);
+    if (!thread_timing())
+      QV_CUDA(cudaMemsetAsync(flags.dev, 0, kSearchFlagWords * sizeof(int), st));
+    // The caller's bitmap is read only: the live-node mask is applied to a copy.
+    const size_t words = std::max<size_t>(1, (s.flat.n + 63) / 64);
+    DeviceBuffer bm(words * sizeof(uint64_t), st);
+    if (position_bitmap != nullptr)
+      QV_CUDA(cudaMemcpyAsync(bm.get(), position_bitmap, words * sizeof(uint64_t),
+                              cudaMemcpyDeviceToDevice, st));
+    hnsw_store_search(s, queries, nq, k, bm.get<uint64_t>(), position_bitmap != nullptr, labels,
+                      distances, node_ids, flags.dev, st);
+    QV_CUDA(cudaMemcpyAsync(flags.host, flags.dev, kSearchFlagWords * sizeof(int),
+                            cudaMemcpyDeviceToHost, st));
+    QV_CUDA(cudaEventRecord(flags.done, st));
+    t_flags = &flags;
   });
 }
 

@@ -327,7 +327,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
     const float* __restrict__ qp, int dpad, const float* __restrict__ eps_q, int nq,
     const float* __restrict__ x, int dim, int64_t nrows, const uint64_t* __restrict__ bitmap,
     const uint64_t* __restrict__ labels, uint64_t row_offset,
-    bool l2, const float* __restrict__ cand_d,
+    bool l2, bool sq8, const float* __restrict__ cand_d,
     const uint32_t* __restrict__ cand_r, const int* __restrict__ cand_n, int n_chunks, int kk,
     int group_rows, int pool, int k, uint64_t* __restrict__ out_labels, float* __restrict__ out_d,
     uint64_t* __restrict__ out_keys, const int* __restrict__ qbad, int* __restrict__ fail_count,
@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
       xr[r] = x + (row[r] == ~0ull ? 0 : row[r]) * dim;
     }
     float e[4];
-    dev::warp_exact_distance_x4(qrow, xr, dim, l2, lane, e);
+    dev::warp_exact_distance_x4(qrow, xr, dim, l2, lane, e, sq8);
     if (lane == 0) {
 #pragma unroll
       for (int r = 0; r < 4; ++r)
@@ -513,8 +513,65 @@ __device__ __forceinline__ float lane_reduce_avx2(const float* __restrict__ q,
   return sum;
 }
 
+// simd::avx2::l2sqr_sq8 / dot_sq8 (src/simd/kernels_avx2.cc:85-129) on a decoded row x, evaluated
+// by ONE thread in the order dev::warp_reduce_sq8 uses: accumulator s[a][l] takes elements
+// i + 8a + l of every 16-element block, 8-element blocks go to s[0][l], then s0 + s1 per l, the
+// hsum, and the scalar tail (one FMA per element). Bit-identical to the warp version.
+template <bool kDiff>
+__device__ __forceinline__ float lane_reduce_sq8(const float* __restrict__ q,
+                                                 const float* __restrict__ x, int dim) {
+  float s[2][8];
+#pragma unroll
+  for (int a = 0; a < 2; ++a)
+#pragma unroll
+    for (int l = 0; l < 8; ++l) s[a][l] = 0.0f;
+  auto acc = [&](float& dst, float u, float v) {
+    if (kDiff) {
+      u = __fsub_rn(u, v);
+      v = u;
+    }
+    dst = __fmaf_rn(u, v, dst);
+  };
+  int i = 0;
+  const bool vec = (dim & 3) == 0;  // rows and q start on 16-byte boundaries
+  for (; i + 16 <= dim; i += 16) {
+    if (vec) {
+#pragma unroll
+      for (int f = 0; f < 4; ++f) {
+        const float4 xv = __ldg(reinterpret_cast<const float4*>(x + i) + f);
+        const float4 qv = reinterpret_cast<const float4*>(q + i)[f];
+        const int e = 4 * f;
+        acc(s[(e + 0) >> 3][(e + 0) & 7], qv.x, xv.x);
+        acc(s[(e + 1) >> 3][(e + 1) & 7], qv.y, xv.y);
+        acc(s[(e + 2) >> 3][(e + 2) & 7], qv.z, xv.z);
+        acc(s[(e + 3) >> 3][(e + 3) & 7], qv.w, xv.w);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc(s[e >> 3][e & 7], q[i + e], __ldg(x + i + e));
+    }
+  }
+  for (; i + 8 <= dim; i += 8) {
+#pragma unroll
+    for (int l = 0; l < 8; ++l) acc(s[0][l], q[i + l], __ldg(x + i + l));
+  }
+  float t[8];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) t[l] = __fadd_rn(s[0][l], s[1][l]);
+  float lo[4];
+#pragma unroll
+  for (int l = 0; l < 4; ++l) lo[l] = __fadd_rn(t[l], t[l + 4]);
+  float sum = __fadd_rn(__fadd_rn(lo[0], lo[1]), __fadd_rn(lo[2], lo[3]));
+  for (; i < dim; ++i) acc(sum, q[i], __ldg(x + i));
+  return sum;
+}
+
+// The exact distance of the stored row x: the float32 kernels' order (src/flat_index.cc:87), or
+// with sq8 the SQ8 kernels' (src/hnsw_index.cc:202-218; x is then the decoded codes).
 __device__ __forceinline__ float lane_exact_distance(const float* q, const float* x, int dim,
-                                                     bool l2) {
+                                                     bool l2, bool sq8) {
+  if (sq8)
+    return l2 ? lane_reduce_sq8<true>(q, x, dim) : __fsub_rn(1.0f, lane_reduce_sq8<false>(q, x, dim));
   return l2 ? lane_reduce_avx2<true>(q, x, dim) : __fsub_rn(1.0f, lane_reduce_avx2<false>(q, x, dim));
 }
 
@@ -538,7 +595,7 @@ __host__ __device__ inline size_t group_finalize_bytes_per_warp(int dpad, int n_
 __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_groups_kernel(
     const float* __restrict__ qp, int dpad, const float* __restrict__ eps_q, int nq,
     const float* __restrict__ x, int dim, int64_t nrows, const uint64_t* __restrict__ bitmap,
-    const uint64_t* __restrict__ labels, uint64_t row_offset, bool l2,
+    const uint64_t* __restrict__ labels, uint64_t row_offset, bool l2, bool sq8,
     const float* __restrict__ cand_d, const uint32_t* __restrict__ cand_r,
     const int* __restrict__ cand_n, int n_chunks, int kk, int group_rows, int k,
     uint64_t* __restrict__ out_labels, float* __restrict__ out_d, uint64_t* __restrict__ out_keys,
@@ -636,7 +693,7 @@ __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_gro
       const int g = i / group_rows, j = i - g * group_rows;
       const uint64_t row = static_cast<uint64_t>(sel[g]) * group_rows + j;
       const bool in = row < static_cast<uint64_t>(nrows) && dev::bitmap_test(bitmap, row);
-      ed[i] = in ? dev::nan_to_inf(lane_exact_distance(sq, x + row * dim, dim, l2)) : kInf;
+      ed[i] = in ? dev::nan_to_inf(lane_exact_distance(sq, x + row * dim, dim, l2, sq8)) : kInf;
       er[i] = in ? row : ~0ull;
     }
     __syncwarp();
@@ -750,7 +807,7 @@ __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_gro
 __global__ void __launch_bounds__(256) flat_rescan_kernel(
     const float* __restrict__ qp, int dpad, const float* __restrict__ x, int dim, int64_t nrows,
     const uint64_t* __restrict__ labels, const uint64_t* __restrict__ bitmap, uint64_t row_offset,
-    bool l2, int k, int cap, const int* __restrict__ fail_count, const int* __restrict__ fail_q,
+    bool l2, bool sq8, int k, int cap, const int* __restrict__ fail_count, const int* __restrict__ fail_q,
     const float* __restrict__ fail_dk, uint64_t* __restrict__ out_labels,
     float* __restrict__ out_d, uint64_t* __restrict__ out_keys) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -778,7 +835,7 @@ __global__ void __launch_bounds__(256) flat_rescan_kernel(
         if (row >= nrows) break;
         if (!dev::bitmap_test(bitmap, static_cast<uint64_t>(row))) continue;
         const float e =
-            dev::nan_to_inf(dev::warp_exact_distance(qrow, x + row * dim, dim, l2, lane));
+            dev::nan_to_inf(dev::warp_exact_distance(qrow, x + row * dim, dim, l2, lane, sq8));
         if (lane == 0 && e <= thr) {
           const int slot = atomicAdd(&s_cnt, 1);
           bd[slot] = e;
@@ -895,7 +952,7 @@ void flat_reserve(FlatState& s, size_t rows, cudaStream_t st) {
 }
 
 void flat_append(FlatState& s, const float* d_rows, const uint64_t* d_labels, size_t n,
-                 cudaStream_t st) {
+                 cudaStream_t st, bool normalize) {
   if (n == 0) return;
   flat_reserve(s, s.n + n, st);
   float* dst = s.x.get<float>() + s.n * s.dim;
@@ -903,7 +960,7 @@ void flat_append(FlatState& s, const float* d_rows, const uint64_t* d_labels, si
     QV_CUDA(cudaMemcpyAsync(dst, d_rows, n * s.dim * sizeof(float), cudaMemcpyDeviceToDevice, st));
   QV_CUDA(cudaMemcpyAsync(s.labels.get<uint64_t>() + s.n, d_labels, n * sizeof(uint64_t),
                           cudaMemcpyDeviceToDevice, st));
-  if (s.metric == QV_METRIC_COSINE) normalize_rows_device(dst, n, s.dim, st);
+  if (normalize && s.metric == QV_METRIC_COSINE) normalize_rows_device(dst, n, s.dim, st);
   DeviceBuffer maxbits(sizeof(unsigned), st);
   QV_CUDA(cudaMemsetAsync(maxbits.get(), 0, sizeof(unsigned), st));
   row_stats_kernel<<<ceil_div(n, 8), 256, 0, st>>>(dst, n, static_cast<int>(s.dim),
@@ -1030,6 +1087,7 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
                        cudaStream_t st) {
   const int dim = P.dim, dpad = P.dpad, kk = P.kk;
   const bool l2 = s.metric == QV_METRIC_L2;
+  const bool sq8 = s.sum_order == kSumOrderSq8;
   const int nsm = sm_count(s.device);
   float* qp = reinterpret_cast<float*>(base + P.qp);
   float* qn2 = reinterpret_cast<float*>(base + P.qn2);
@@ -1095,8 +1153,8 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
     flat_finalize_groups_kernel<<<static_cast<unsigned>(ceil_div(nq, kGroupFinalizeWarps)),
                                   32 * kGroupFinalizeWarps, gsmem, st>>>(
         qp, dpad, eps, static_cast<int>(nq), s.x.get<float>(), dim, static_cast<int64_t>(s.n),
-        d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, cand_d, cand_r, cand_n, P.n_chunks,
-        kk, P.group_rows, static_cast<int>(k), d_labels, d_dists, d_keys, qbad, screen_err,
+        d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, sq8, cand_d, cand_r, cand_n,
+        P.n_chunks, kk, P.group_rows, static_cast<int>(k), d_labels, d_dists, d_keys, qbad, screen_err,
         fail_count, fail_q, fail_dk, d_flags);
     check_launch("flat_finalize_groups_kernel");
   } else {
@@ -1106,8 +1164,8 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
                                  (int)fsmem));
     flat_finalize_kernel<<<static_cast<unsigned>(nq), kFinalizeThreads, fsmem, st>>>(
         qp, dpad, eps, static_cast<int>(nq), s.x.get<float>(), dim, static_cast<int64_t>(s.n),
-        d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, cand_d, cand_r, cand_n, P.n_chunks,
-        kk, 1, pool, static_cast<int>(k), d_labels, d_dists, d_keys, qbad, fail_count, fail_q,
+        d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, sq8, cand_d, cand_r, cand_n,
+        P.n_chunks, kk, 1, pool, static_cast<int>(k), d_labels, d_dists, d_keys, qbad, fail_count, fail_q,
         fail_dk, d_flags);
     check_launch("flat_finalize_kernel");
   }
@@ -1118,7 +1176,7 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
                                (int)rsmem));
   flat_rescan_kernel<<<static_cast<unsigned>(std::min<size_t>(nq, 2 * nsm)), 256, rsmem, st>>>(
       qp, dpad, s.x.get<float>(), dim, static_cast<int64_t>(s.n), s.labels.get<uint64_t>(),
-      d_bitmap, s.row_offset, l2, static_cast<int>(k), cap, fail_count, fail_q, fail_dk, d_labels,
+      d_bitmap, s.row_offset, l2, sq8, static_cast<int>(k), cap, fail_count, fail_q, fail_dk, d_labels,
       d_dists, d_keys);
   check_launch("flat_rescan_kernel");
 }

@@ -393,11 +393,69 @@ __device__ __forceinline__ void warp_reduce_avx2_x4(const float* __restrict__ a,
   }
 }
 
-// warp_exact_distance for four rows at once (see warp_reduce_avx2_x4).
+// simd::avx2::l2sqr_sq8 / dot_sq8 (src/simd/kernels_avx2.cc:85-129) evaluated by one warp on
+// the decoded row b (b[i] = vmin[i] + code[i] * vscale[i] rounded once, the FMA those kernels
+// decode with): lane l < 16 owns accumulator s[l >> 3][l & 7] of the 16-element blocks,
+// 8-element blocks go to s0 (lanes 0..7), then s0 + s1 per lane, the hsum (:17-23), and the
+// scalar tail, every element of which is one FMA. All lanes return the same value.
+template <bool kDiff>
+__device__ __forceinline__ float warp_reduce_sq8(const float* __restrict__ a,
+                                                 const float* __restrict__ b, int dim, int lane) {
+  float s = 0.0f;
+  int i = 0;
+  for (; i + 16 <= dim; i += 16) {
+    if (lane < 16) {
+      float u = a[i + lane], v = b[i + lane];
+      if (kDiff) {
+        u = __fsub_rn(u, v);
+        v = u;
+      }
+      s = __fmaf_rn(u, v, s);
+    }
+  }
+  for (; i + 8 <= dim; i += 8) {
+    if (lane < 8) {
+      float u = a[i + lane], v = b[i + lane];
+      if (kDiff) {
+        u = __fsub_rn(u, v);
+        v = u;
+      }
+      s = __fmaf_rn(u, v, s);
+    }
+  }
+  const float t = __fadd_rn(s, __shfl_down_sync(kFull, s, 8));
+  const float lo = __fadd_rn(t, __shfl_down_sync(kFull, t, 4));
+  const float lo1 = __shfl_down_sync(kFull, lo, 1);
+  const float lo2 = __shfl_down_sync(kFull, lo, 2);
+  const float lo3 = __shfl_down_sync(kFull, lo, 3);
+  float sum = __shfl_sync(kFull, __fadd_rn(__fadd_rn(lo, lo1), __fadd_rn(lo2, lo3)), 0);
+  for (; i < dim; ++i) {
+    float u = a[i], v = b[i];
+    if (kDiff) {
+      u = __fsub_rn(u, v);
+      v = u;
+    }
+    sum = __fmaf_rn(u, v, sum);
+  }
+  return sum;
+}
+
+// The SQ8 kernels' distance (src/hnsw_index.cc:202-218): l2sqr_sq8, or 1 - dot_sq8.
+__device__ __forceinline__ float warp_exact_distance_sq8(const float* q, const float* x, int dim,
+                                                         bool l2, int lane) {
+  if (l2) return warp_reduce_sq8<true>(q, x, dim, lane);
+  return __fsub_rn(1.0f, warp_reduce_sq8<false>(q, x, dim, lane));
+}
+
+// warp_exact_distance for four rows at once (see warp_reduce_avx2_x4); sq8 selects the SQ8
+// kernels' order (rows are then decoded SQ8 codes).
 __device__ __forceinline__ void warp_exact_distance_x4(const float* q, const float* const (&x)[4],
                                                        int dim, bool l2, int lane,
-                                                       float (&out)[4]) {
-  if (l2) {
+                                                       float (&out)[4], bool sq8 = false) {
+  if (sq8) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) out[r] = warp_exact_distance_sq8(q, x[r], dim, l2, lane);
+  } else if (l2) {
     warp_reduce_avx2_x4<true>(q, x, dim, lane, out);
   } else {
     warp_reduce_avx2_x4<false>(q, x, dim, lane, out);
@@ -414,9 +472,11 @@ __device__ __forceinline__ float warp_l2sqr_avx2(const float* a, const float* b,
   return warp_reduce_avx2<true>(a, b, dim, lane);
 }
 
-// The reference's exact distance (src/flat_index.cc:87, src/ivfpq_index.cc:138-142).
+// The reference's exact distance (src/flat_index.cc:87, src/ivfpq_index.cc:138-142); sq8: the SQ8
+// kernels' order on a decoded row (src/hnsw_index.cc:202-218).
 __device__ __forceinline__ float warp_exact_distance(const float* q, const float* x, int dim,
-                                                     bool l2, int lane) {
+                                                     bool l2, int lane, bool sq8 = false) {
+  if (sq8) return warp_exact_distance_sq8(q, x, dim, l2, lane);
   if (l2) return warp_l2sqr_avx2(q, x, dim, lane);
   return __fsub_rn(1.0f, warp_dot_avx2(q, x, dim, lane));
 }

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <mutex>
+#include <unordered_map>
 #include <vector>
 
 #include "qv_internal.cuh"
@@ -16,10 +17,15 @@ namespace qv {
 // Rows live in HBM row-major as float32 exactly as the reference stores them (normalized for
 // cosine), with their labels, a squared norm per row for the L2 screen, and a scaled fp16 copy
 // padded to at least 64 columns for the tensor-core screen.
+// Summation order of the exact distances of a FlatState's rows: the reference's float32 kernels
+// (FlatIndex), or its SQ8 kernels (an HNSW SQ8 store, whose rows are the decoded codes).
+enum : uint32_t { kSumOrderF32 = 0, kSumOrderSq8 = 1 };
+
 struct FlatState {
   int device = 0;
   size_t dim = 0;
   uint32_t metric = 0;
+  uint32_t sum_order = kSumOrderF32;
   uint64_t row_offset = 0;
   size_t n = 0, cap = 0;
   DeviceBuffer x;         // cap x dim f32
@@ -91,14 +97,41 @@ void flat_check_rows(const float* d_x, size_t count, const uint64_t* d_labels, s
                      int* d_flags, cudaStream_t st);
 // d_out[i] = first + i.
 void sequential_labels(uint64_t* d_out, size_t n, uint64_t first, cudaStream_t st);
-// Appends n rows (device pointer, row-major) with labels (device pointer).
+// Appends n rows (device pointer, row-major) with labels (device pointer); cosine rows are
+// normalized unless `normalize` is false (rows that are already prepared).
 void flat_append(FlatState& s, const float* d_rows, const uint64_t* d_labels, size_t n,
-                 cudaStream_t st);
+                 cudaStream_t st, bool normalize = true);
 // Enqueues an exact search on `st` and returns without waiting for it. The kernels add their
 // reports into d_flags (kSearchFlagWords device ints, see kFlag*).
 void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k,
                  const uint64_t* d_bitmap, uint64_t* d_labels, float* d_dists, uint64_t* d_keys,
                  int* d_flags, cudaStream_t st);
+
+// ---- HNSW vector storage and its filtered exact scan (hnsw_store.cu) ---------------------------
+enum : uint32_t { kStorageF32 = 0, kStorageSq8 = 1 };  // quiver::Storage
+struct HnswStoreState {
+  FlatState flat;            // rows the scan reads: prepared float32, or decoded SQ8; labels
+  uint32_t storage = kStorageF32;
+  bool trained = false;      // SQ8 parameters set (once)
+  DeviceBuffer vmin, vscale;  // dim f32 each (SQ8)
+  std::vector<float> host_vmin, host_vscale;
+  DeviceBuffer codes;        // n x dim u8 (SQ8), node order
+  DeviceBuffer removed;      // one bit per node: soft-deleted
+  std::vector<uint64_t> host_removed;
+  size_t removed_count = 0;
+  std::unordered_map<uint64_t, uint32_t> label_to_id;  // a label's current node
+};
+// ScalarQuantizer::train on n prepared device rows: sets vmin / vscale (device and host copies).
+void hnsw_sq8_train(HnswStoreState& s, const float* d_x, size_t n, cudaStream_t st);
+// Appends n prepared device rows (SQ8: encoded, and d_x overwritten with the decoded rows).
+void hnsw_store_append(HnswStoreState& s, float* d_x, const uint64_t* d_labels, size_t n,
+                       cudaStream_t st);
+void hnsw_store_mark_removed(HnswStoreState& s, uint32_t id, cudaStream_t st);
+// The exact scan over the live nodes the position bitmap admits (d_bitmap: ceil(n / 64) words,
+// the filter's when have_filter, else scratch; overwritten). d_keys (optional) get node ids.
+void hnsw_store_search(const HnswStoreState& s, const float* d_queries, size_t nq, size_t k,
+                       uint64_t* d_bitmap, bool have_filter, uint64_t* d_labels, float* d_dists,
+                       uint64_t* d_keys, int* d_flags, cudaStream_t st);
 
 // ---- IVF-PQ ------------------------------------------------------------------------------------
 // Inverted lists are stored list-major and contiguous in HBM (codes count x m bytes, labels,
