@@ -1028,10 +1028,11 @@ static FlatPlan plan_search(const FlatState& s, size_t nq, size_t k, bool allow_
   const size_t nrows = std::max<size_t>(s.n, 1);
   if (P.tensor) {
     P.kk = flat_tc_kk(s, k);
-    // Work units cover query groups of 2 x 128 (narrow screen) or one 128-query tile (wide).
-    P.n_qtiles = static_cast<int>(ceil_div(nq, flat_tc_is_wide(s, k) ? 128 : 256));
+    // Work units cover query groups of 2 x 128 (narrow screen), 4 x 128 (narrow screen in CTA
+    // pairs) or one 128-query tile (wide).
+    P.n_qtiles = static_cast<int>(ceil_div(nq, static_cast<size_t>(flat_tc_group_rows(s, k))));
     P.n_chunks = choose_chunks(nrows, P.n_qtiles, std::max(1, kMaxCandidatesPerQuery / P.kk),
-                               nsm, 128, &P.chunk_rows);
+                               flat_tc_workers(s, k), 128, &P.chunk_rows);
     P.group_rows = kTcGroupRows;
   } else {
     P.kk = static_cast<int>(next_pow2(k + std::max<size_t>(8, k / 4)));
@@ -1061,7 +1062,7 @@ static FlatPlan plan_search(const FlatState& s, size_t nq, size_t k, bool allow_
   P.cand_r = take(P.slots * P.kk * sizeof(uint32_t));
   P.cand_n = take(P.slots * sizeof(int));
   P.thr = take(nq * sizeof(unsigned));
-  if (P.tensor) P.tc = take(flat_tc_scratch_bytes(s, nq, P.kk));
+  if (P.tensor) P.tc = take(flat_tc_scratch_bytes(s, nq, k, P.kk));
   if (own_flags) P.flags = take(kSearchFlagWords * sizeof(int));
   P.total = off;
   return P;
@@ -1125,7 +1126,7 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
       std::lock_guard<std::mutex> lock(ms.x16_mu);
       flat_tc_prepare(ms, st);
     }
-    flat_screen_tc(s, qp, dpad, nq, d_bitmap, P.n_chunks, P.chunk_rows, kk, cand_d, cand_r,
+    flat_screen_tc(s, qp, dpad, nq, k, d_bitmap, P.n_chunks, P.chunk_rows, kk, cand_d, cand_r,
                    cand_n, thr, eps, screen_err, base + P.tc, st);
   } else {
     const size_t smem = kScreenRows * kScreenDChunk * sizeof(float) +

@@ -32,6 +32,7 @@
 #include <cmath>
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "qv_state.h"
 #include "tc_common.cuh"
@@ -53,10 +54,13 @@ constexpr int kMaxKK = 32;       // largest best-list length (candidates per que
 // tile's stage is only refilled after its MMAs finish, so the next tile's copy has one tile time
 // (~900 cycles) to land with two stages, which L2 latency exceeds; three stages fit in shared
 // memory next to best lists of 24 when 8 (not 16) entries are appended between compactions.
-template <int kKK>
+// In CTA pairs (kPair) a CTA holds only half of each row tile (64 rows, 8 KB per K atom), which
+// leaves room for a deeper ring and longer append runs (fewer list compactions).
+template <int kKK, bool kPair = false, int kAtoms = 2>
 struct Ring {
-  static constexpr int kStages = kKK <= 24 ? 3 : 2;
-  static constexpr int kAppend = kKK <= 24 ? 8 : 16;
+  static constexpr int kStages = kPair ? (kAtoms == 1 ? 8 : (kKK <= 24 ? 5 : 4))
+                                       : (kKK <= 24 ? 3 : 2);
+  static constexpr int kAppend = kPair ? 16 : (kKK <= 24 ? 8 : 16);
 };
 struct Args {
   int nq, n_qgroups, n_chunks, total_units, ksteps;  // a query group = kTiles tiles of kM
@@ -97,9 +101,8 @@ __device__ __forceinline__ void unit_coords(const Args& a, int u, int& qgroup, i
 // a (sorted, padded to 32) and the sorted appended entries b (padded to 32), c[i] = min(a[i],
 // b[31 - i]) holds the 32 smallest of both as a bitonic sequence, which a 32-input bitonic merge
 // sorts.
-template <int kKK>
+template <int kKK, int kA>
 __device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, float& thr) {
-  constexpr int kA = Ring<kKK>::kAppend;
   static_assert((kA & (kA - 1)) == 0 && kA <= 32 && kKK <= 32, "networks sized for 32 kept");
   const float kInf = __int_as_float(0x7f800000);
   float bd[kA];
@@ -156,34 +159,51 @@ __device__ __noinline__ void compact_buffer(float* d, uint32_t* r, int& cnt, flo
 // One row tile's MMAs against every query tile of the group, kSteps K-steps of 16 each, fully
 // unrolled: issued from a loop with a runtime trip count, each MMA took longer to issue than the
 // 64 cycles a 128 x 128 x 16 MMA executes in, and even a guarded unrolled loop cost ~10 %.
-template <int kAtoms, int kSteps>
+// kPair: MMAs of M = 256 (cta_group::2, issued by the pair's leader), B's K atoms being this
+// CTA's 64-row halves (8 KB apart instead of 16 KB).
+template <int kAtoms, int kSteps, bool kPair>
 __device__ __forceinline__ void issue_tile(uint32_t d_base, uint32_t a_addr, uint32_t b_addr) {
+  constexpr int kBAtom = kPair ? kAtomBytes / 2 : kAtomBytes;
 #pragma unroll
   for (int tq = 0; tq < kTiles; ++tq) {
 #pragma unroll
     for (int ks = 0; ks < kSteps; ++ks) {
-      const uint32_t off = static_cast<uint32_t>((ks >> 2) * kAtomBytes + (ks & 3) * 32);
-      umma_f16(d_base + static_cast<uint32_t>(tq * kN),
-               smem_desc(a_addr + static_cast<uint32_t>(tq * kAtoms * kAtomBytes) + off),
-               smem_desc(b_addr + off), ks > 0 ? 1u : 0u);
+      const uint32_t off_a = static_cast<uint32_t>((ks >> 2) * kAtomBytes + (ks & 3) * 32);
+      const uint32_t off_b = static_cast<uint32_t>((ks >> 2) * kBAtom + (ks & 3) * 32);
+      const uint64_t da = smem_desc(a_addr + static_cast<uint32_t>(tq * kAtoms * kAtomBytes) + off_a);
+      const uint64_t db = smem_desc(b_addr + off_b);
+      if (kPair)
+        umma_f16_pair(d_base + static_cast<uint32_t>(tq * kN), da, db, ks > 0 ? 1u : 0u);
+      else
+        umma_f16(d_base + static_cast<uint32_t>(tq * kN), da, db, ks > 0 ? 1u : 0u);
     }
   }
 }
 
-template <int kAtoms, bool kL2, int kKK>
+// kPair: the kernel runs as clusters of two CTAs (tcgen05 cta_group::2). A pair works on units of
+// a 512-query group (two 128-query tiles per CTA, each CTA's own A, lists and accumulators)
+// against a row chunk; each CTA loads 64 rows of every 128-row tile, and the even CTA (the
+// leader) issues MMAs of M = 256 (both CTAs' query tile tq) x N = 128, so every row byte a CTA
+// brings into shared memory feeds both tensor cores: per MMA an SM reads 6 KB of shared memory
+// (its 4 KB of A, its 2 KB of B) instead of 8 KB, the copies in halve, and the ring covers twice
+// the time for the same bytes. Barriers that both CTAs report to (full, a_full, drain) live in the
+// leader; the leader's commits arrive on both CTAs' copies of empty, acc_full and a_empty.
+template <int kAtoms, bool kL2, int kKK, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     flat_screen_tc_kernel(const __grid_constant__ CUtensorMap tmap_q,
                           const __grid_constant__ CUtensorMap tmap_x, const Args a) {
-  constexpr int kStages = Ring<kKK>::kStages;
-  constexpr int kAppend = Ring<kKK>::kAppend;
+  constexpr int kStages = Ring<kKK, kPair, kAtoms>::kStages;
+  constexpr int kAppend = Ring<kKK, kPair, kAtoms>::kAppend;
   constexpr int kCap = kKK + kAppend;  // candidate list entries per query
+  constexpr int kBAtomBytes = kPair ? kAtomBytes / 2 : kAtomBytes;  // one row-tile K atom here
+  constexpr int kBRows = kPair ? kN / 2 : kN;                       // rows of a tile loaded here
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   // 1024-byte alignment for the swizzle atoms.
   unsigned char* base = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   unsigned char* smem_a = base;                                  // kTiles x kAtoms x 16 KB
-  unsigned char* smem_b = smem_a + kTiles * kAtoms * kAtomBytes;  // kStages x kAtoms x 16 KB
-  float* buf_d = reinterpret_cast<float*>(smem_b + kStages * kAtoms * kAtomBytes);  // kCap x kLS
+  unsigned char* smem_b = smem_a + kTiles * kAtoms * kAtomBytes;  // kStages x kAtoms x kBAtomBytes
+  float* buf_d = reinterpret_cast<float*>(smem_b + kStages * kAtoms * kBAtomBytes);  // kCap x kLS
   uint32_t* buf_r = reinterpret_cast<uint32_t*>(buf_d + kCap * kLS);
   uint64_t* bars = reinterpret_cast<uint64_t*>(buf_r + kCap * kLS);
   // bars: full[kStages], empty[kStages], acc_full[kAcc], a_full, a_empty, drain[2] (one per
@@ -203,12 +223,33 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar = [&](int i) { return smem_u32(bars + i); };
   const int FULL = 0, EMPTY = kStages, ACC_FULL = 2 * kStages, A_FULL = 2 * kStages + kAcc,
             A_EMPTY = 2 * kStages + kAcc + 1, DRAIN = 2 * kStages + kAcc + 2;
+  const uint32_t rank = kPair ? cluster_ctarank() : 0;
+  const bool leader = rank == 0;
+  // The leader's copy of barrier i (a shared::cluster address in a pair).
+  auto lbar = [&](int i) { return kPair ? mapa_shared(bar(i), 0) : bar(i); };
+  auto wait = [&](uint32_t b, uint32_t parity, volatile int* abort_flag) {
+    return kPair ? mbar_wait_cluster(b, parity, abort_flag, a.err, a.wait_cycles)
+                 : mbar_wait(b, parity, abort_flag, a.err, a.wait_cycles);
+  };
+  auto arrive_leader = [&](int i) {
+    if (kPair)
+      mbar_arrive_cluster(lbar(i));
+    else
+      mbar_arrive(bar(i));
+  };
+  auto commit_both = [&](int i) {  // the MMAs issued so far have completed
+    if (kPair)
+      umma_commit_pair_mc(bar(i), 0x3);
+    else
+      umma_commit(bar(i));
+  };
 
   if (threadIdx.x == 0) {
     s_abort = 0;
     s_consumed[0] = s_consumed[1] = 0;
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(FULL + s), 1 + kEpiWarps);  // the producer's expect_tx + each epilogue warp
+      // The (leader's) producer's expect_tx + each epilogue warp (of both CTAs in a pair).
+      mbar_init(bar(FULL + s), 1 + (kPair ? 2 : 1) * kEpiWarps);
       mbar_init(bar(EMPTY + s), 1);
     }
     for (int b = 0; b < kAcc; ++b) mbar_init(bar(ACC_FULL + b), 1);
@@ -219,16 +260,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_u32(&s_tmem)),
-                 "r"(kAcc * kTiles * kN));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if (kPair) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&s_tmem)),
+                   "r"(kAcc * kTiles * kN));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&s_tmem)),
+                   "r"(kAcc * kTiles * kN));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (kPair) cluster_sync();  // both CTAs' barriers are initialized before either uses them
   tc_fence_after();
   const uint32_t tmem_base = s_tmem;
   volatile int* abort_flag = &s_abort;
+  // Work units (query group, row chunk): a group is kTiles query tiles, or 2 x kTiles in a pair
+  // (CTA rank r holds tiles 2r .. 2r + 1 of the group). Pairs are numbered by blockIdx.x / 2.
+  const int worker = kPair ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int workers = kPair ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  auto first_tile = [&](int qgroup) {  // this CTA's first query tile of the group
+    return (kPair ? 2 * qgroup + static_cast<int>(rank) : qgroup) * kTiles;
+  };
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -237,30 +293,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0, a_phase = 0;
       int issued = 0;
       bool first = true;
-      for (int u = blockIdx.x; u < a.total_units && !*abort_flag; u += gridDim.x) {
+      for (int u = worker; u < a.total_units && !*abort_flag; u += workers) {
         int qgroup, chunk;
         unit_coords(a, u, qgroup, chunk);
         const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
         const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
         const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
         if (!first) {
-          if (!mbar_wait(bar(A_EMPTY), a_phase, abort_flag, a.err, a.wait_cycles)) break;
+          if (!wait(bar(A_EMPTY), a_phase, abort_flag)) break;
           a_phase ^= 1;
         }
         first = false;
-        mbar_expect_tx(bar(A_FULL), kTiles * kAtoms * kAtomBytes);
+        // In a pair both CTAs' query tiles complete on the leader's barrier.
+        if (leader) mbar_expect_tx(bar(A_FULL), (kPair ? 2 : 1) * kTiles * kAtoms * kAtomBytes);
+        const int qt0 = first_tile(qgroup);
         for (int tq = 0; tq < kTiles; ++tq)
-          for (int at = 0; at < kAtoms; ++at)
-            tma_load_2d(smem_u32(smem_a + (tq * kAtoms + at) * kAtomBytes), &tmap_q, at * kAtomK,
-                        (qgroup * kTiles + tq) * kM, bar(A_FULL));
+          for (int at = 0; at < kAtoms; ++at) {
+            const uint32_t dst = smem_u32(smem_a + (tq * kAtoms + at) * kAtomBytes);
+            if (kPair)
+              tma_load_2d_pair(dst, &tmap_q, at * kAtomK, (qt0 + tq) * kM, lbar(A_FULL));
+            else
+              tma_load_2d(dst, &tmap_q, at * kAtomK, (qt0 + tq) * kM, bar(A_FULL));
+          }
         for (int t = 0; t < ntiles; ++t) {
-          if (!mbar_wait(bar(EMPTY + stage), phase ^ 1, abort_flag, a.err, a.wait_cycles)) break;
+          if (!wait(bar(EMPTY + stage), phase ^ 1, abort_flag)) break;
           if (blockIdx.x != 0 || issued != a.skip_fill) {
-            mbar_expect_tx(bar(FULL + stage), kAtoms * kAtomBytes);
-            unsigned char* dst = smem_b + stage * kAtoms * kAtomBytes;
-            for (int at = 0; at < kAtoms; ++at)
-              tma_load_2d(smem_u32(dst + at * kAtomBytes), &tmap_x, at * kAtomK,
-                          static_cast<int>(r0 + static_cast<int64_t>(t) * kN), bar(FULL + stage));
+            if (leader)
+              mbar_expect_tx(bar(FULL + stage), (kPair ? 2 : 1) * kAtoms * kBAtomBytes);
+            unsigned char* dst = smem_b + stage * kAtoms * kBAtomBytes;
+            const int y = static_cast<int>(r0 + static_cast<int64_t>(t) * kN) +
+                          static_cast<int>(rank) * kBRows;
+            for (int at = 0; at < kAtoms; ++at) {
+              if (kPair)
+                tma_load_2d_pair(smem_u32(dst + at * kBAtomBytes), &tmap_x, at * kAtomK, y,
+                                 lbar(FULL + stage));
+              else
+                tma_load_2d(smem_u32(dst + at * kBAtomBytes), &tmap_x, at * kAtomK, y,
+                            bar(FULL + stage));
+            }
           }
           ++issued;  // ring fills, the skipped one (test hook) included
           if (++stage == kStages) {
@@ -269,7 +339,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (*abort_flag) {
+      if (*abort_flag && kPair) {
+        // A pair's copies complete on the leader's barriers, which the peer cannot poll: wait
+        // out the drain bound, far longer than any copy in flight takes.
+        const uint64_t t0 = gtimer();
+        while (gtimer() - t0 < a.drain_ns) {
+        }
+      } else if (*abort_flag) {
         // Drain: wait (bounded) for every B fill the MMA warp did not consume.
         const uint64_t t0 = gtimer();
         for (int f = s_consumed[0] + s_consumed[1]; f < issued; ++f) {
@@ -287,17 +363,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     // parity me: those of accumulator slot me.
     static_assert(kAcc == 2, "one issuer per accumulator slot");
     const int me = warp == 1 ? 0 : 1;
-    if (lane == 0) {
+    if (lane == 0 && leader) {  // in a pair, the leader issues for both CTAs
       const int accb = me;
       uint32_t a_phase = 0;
       int consumed = 0, g = 0;
-      for (int u = blockIdx.x; u < a.total_units && !*abort_flag; u += gridDim.x) {
+      for (int u = worker; u < a.total_units && !*abort_flag; u += workers) {
         int qgroup, chunk;
         unit_coords(a, u, qgroup, chunk);
         const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
         const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
         const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
-        if (!mbar_wait(bar(A_FULL), a_phase, abort_flag, a.err, a.wait_cycles)) break;
+        if (!wait(bar(A_FULL), a_phase, abort_flag)) break;
         a_phase ^= 1;
         tc_fence_after();
         const uint32_t a_addr = smem_u32(smem_a);
@@ -305,37 +381,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = (g & 1) == me ? 0 : 1; t < ntiles && ok; t += 2) {
           const int gt = g + t;
           const int stage = gt % kStages;
-          ok = mbar_wait(bar(FULL + stage), (gt / kStages) & 1, abort_flag, a.err, a.wait_cycles);
+          ok = wait(bar(FULL + stage), (gt / kStages) & 1, abort_flag);
           if (!ok) break;
           s_consumed[me] = ++consumed;
           tc_fence_after();
-          const uint32_t b_addr = smem_u32(smem_b + stage * kAtoms * kAtomBytes);
+          const uint32_t b_addr = smem_u32(smem_b + stage * kAtoms * kBAtomBytes);
           const uint32_t d_base = tmem_base + static_cast<uint32_t>(accb * kTiles * kN);
           if (kAtoms == 1) {
             switch (a.ksteps) {
-              case 1: issue_tile<1, 1>(d_base, a_addr, b_addr); break;
-              case 2: issue_tile<1, 2>(d_base, a_addr, b_addr); break;
-              case 3: issue_tile<1, 3>(d_base, a_addr, b_addr); break;
-              default: issue_tile<1, 4>(d_base, a_addr, b_addr); break;
+              case 1: issue_tile<1, 1, kPair>(d_base, a_addr, b_addr); break;
+              case 2: issue_tile<1, 2, kPair>(d_base, a_addr, b_addr); break;
+              case 3: issue_tile<1, 3, kPair>(d_base, a_addr, b_addr); break;
+              default: issue_tile<1, 4, kPair>(d_base, a_addr, b_addr); break;
             }
           } else {
             switch (a.ksteps) {
-              case 5: issue_tile<kAtoms, 5>(d_base, a_addr, b_addr); break;
-              case 6: issue_tile<kAtoms, 6>(d_base, a_addr, b_addr); break;
-              case 7: issue_tile<kAtoms, 7>(d_base, a_addr, b_addr); break;
-              default: issue_tile<kAtoms, 8>(d_base, a_addr, b_addr); break;
+              case 5: issue_tile<kAtoms, 5, kPair>(d_base, a_addr, b_addr); break;
+              case 6: issue_tile<kAtoms, 6, kPair>(d_base, a_addr, b_addr); break;
+              case 7: issue_tile<kAtoms, 7, kPair>(d_base, a_addr, b_addr); break;
+              default: issue_tile<kAtoms, 8, kPair>(d_base, a_addr, b_addr); break;
             }
           }
-          umma_commit(bar(EMPTY + stage));
-          umma_commit(bar(ACC_FULL + accb));
+          commit_both(EMPTY + stage);
+          commit_both(ACC_FULL + accb);
         }
         if (!ok) break;
         g += ntiles;
-        umma_commit(bar(A_EMPTY));  // A_EMPTY completes once both issuers are done with the unit
+        commit_both(A_EMPTY);  // A_EMPTY completes once both issuers are done with the unit
       }
       if (*abort_flag) {
         // Wait (bounded) for this issuer's MMAs in flight before the accumulators are freed.
-        umma_commit(bar(DRAIN + me));
+        if (kPair)
+          umma_commit_pair_mc(bar(DRAIN + me), 0x1);
+        else
+          umma_commit(bar(DRAIN + me));
         const uint64_t t0 = gtimer();
         while (!mbar_test(bar(DRAIN + me), 0) && gtimer() - t0 < a.drain_ns) {
         }
@@ -363,14 +442,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     // Tiles 0 .. kAcc - 1 (stages 0 .. kAcc - 1) are the first in their slots: nothing to wait for.
     if (lane == 0)
-      for (int b = 0; b < kAcc; ++b) mbar_arrive(bar(FULL + b));
-    for (int u = blockIdx.x; u < a.total_units; u += gridDim.x) {
+      for (int b = 0; b < kAcc; ++b) arrive_leader(FULL + b);
+    for (int u = worker; u < a.total_units; u += workers) {
       int qgroup, chunk;
       unit_coords(a, u, qgroup, chunk);
       const int64_t r0 = static_cast<int64_t>(chunk) * a.chunk_rows;
       const int64_t r1 = min(a.nrows, r0 + a.chunk_rows);
       const int ntiles = static_cast<int>((r1 - r0 + kN - 1) / kN);
-      const int q = (qgroup * kTiles + tile) * kM + qi;
+      const int q = (first_tile(qgroup) + tile) * kM + qi;
       const bool active = q < a.nq;
       const unsigned* qthr = a.thr_bits + (active ? q : 0);
       float thr = active ? dev::from_ordered_bits(*qthr) : -kInfF;
@@ -437,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Make room first (all lanes together) when some lane's appends would overflow its
         // list; compaction tightens the threshold, so the groups are tested again.
         if (__any_sync(0xffffffffu, cnt + __popc(gm) > kCap)) {
-          compact_buffer<kKK>(bd, br, cnt, thr);
+          compact_buffer<kKK, kAppend>(bd, br, cnt, thr);
           // Publish the tightened bound to the units of other row chunks at once: this unit
           // outputs kKK entries at or below it whatever it appends later.
           if (active) atomicMin(a.thr_bits + q, dev::ordered_bits(thr));
@@ -467,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < ntiles; ++t) {
         const int64_t row0 = r0 + static_cast<int64_t>(t) * kN;
         if ((t & 7) == 0 && active) fresh = *reinterpret_cast<const volatile unsigned*>(qthr);
-        ok = mbar_wait(bar(ACC_FULL + accb), acc_phase, abort_flag, a.err, a.wait_cycles);
+        ok = wait(bar(ACC_FULL + accb), acc_phase, abort_flag);
         if (!ok) break;
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + col0 +
@@ -482,7 +561,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         // The slot is free for the tile kAcc later.
-        if (lane == 0) mbar_arrive(bar(FULL + free_stage));
+        if (lane == 0) arrive_leader(FULL + free_stage);
         if (++free_stage == kStages) free_stage = 0;
         // Both trees first: the loaded values are dead before any list work (compaction needs
         // the registers).
@@ -499,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if ((t & 7) == 7) thr = fminf(thr, dev::from_ordered_bits(fresh));
       }
       if (!ok) break;
-      compact_buffer<kKK>(bd, br, cnt, thr);
+      compact_buffer<kKK, kAppend>(bd, br, cnt, thr);
       cnt = min(seen, kKK);  // the real entries: they sort before the padding
       if (active) {
         // The whole list, padding included (the finalize reads cand_n entries), as 16-byte
@@ -556,10 +635,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
+  // In a pair, neither CTA frees its tensor memory or leaves while the other may still reach its
+  // barriers or the leader's MMAs its memory.
+  if (kPair) cluster_sync();
   tc_fence_after();
   if (warp == 1) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"(kAcc * kTiles * kN));
+    if (kPair)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(kAcc * kTiles * kN));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"(kAcc * kTiles * kN));
   }
 }
 
@@ -744,6 +830,27 @@ bool flat_tc_eligible(const FlatState& s, size_t k) {
   return flat_tc_is_wide(s, k) ? flat_tc_wide_fits(s, k) : true;
 }
 
+// The narrow screen runs in single CTAs unless QV_TC_PAIR=1 selects CTA pairs (tcgen05
+// cta_group::2); both give identical results. On config 1 (1,183,514 x 100 cosine, 10,000
+// queries) pairs took 3.20 ms against 2.18 ms: with the epilogue's work switched off the pair's
+// copy and MMA pipeline alone took 2.16 ms against 1.60 ms, and 1.82 ms even without MMAs, so
+// the cross-CTA barrier hand-offs per row tile, not shared-memory bandwidth, set its pace.
+bool flat_tc_pair(const FlatState& s, size_t k) {
+  if (flat_tc_is_wide(s, k)) return false;
+  const char* e = std::getenv("QV_TC_PAIR");
+  if (e == nullptr || e[0] != '1') return false;
+  return sm_count(s.device) >= 2;
+}
+
+// Queries per work unit's query group and the number of concurrent workers (CTAs, or pairs).
+int flat_tc_group_rows(const FlatState& s, size_t k) {
+  if (flat_tc_is_wide(s, k)) return tc::kM;
+  return (flat_tc_pair(s, k) ? 2 : 1) * tc::kTiles * tc::kM;
+}
+int flat_tc_workers(const FlatState& s, size_t k) {
+  return flat_tc_pair(s, k) ? sm_count(s.device) / 2 : sm_count(s.device);
+}
+
 // Best-list length: k + 8 groups or more (the certificate's margin); 24 when that suffices,
 // which tightens thresholds and shortens the finalize's re-rank; the wide screen rounds k + 8 up
 // to a multiple of 16 (its lists are merged in 16-entry chunks).
@@ -783,8 +890,10 @@ void flat_tc_prepare(FlatState& s, cudaStream_t st) {
 struct TcScratch {
   size_t q16, qinv, qn2, gbest, glock, lists, total;
 };
-static TcScratch tc_scratch_layout(size_t kpad, size_t nq, int kk, size_t list_bytes) {
-  const size_t group_rows = static_cast<size_t>(tc::kTiles) * tc::kM;
+// group_rows: queries per unit's group (the fp16 queries are padded to whole groups, so that no
+// TMA box extends past the tensor).
+static TcScratch tc_scratch_layout(size_t kpad, size_t nq, int kk, size_t list_bytes,
+                                   size_t group_rows) {
   const size_t nq_pad = ceil_div(nq, group_rows) * group_rows;
   TcScratch L{};
   size_t off = 0;
@@ -809,14 +918,16 @@ static size_t tc_list_bytes(const FlatState& s, int kk) {
   return kk > tc::kMaxKK || s.dim > 128 ? flat_tc_wide_list_bytes(s, kk) : 0;
 }
 
-size_t flat_tc_scratch_bytes(const FlatState& s, size_t nq, int kk) {
+size_t flat_tc_scratch_bytes(const FlatState& s, size_t nq, size_t k, int kk) {
   const size_t kpad = std::max<size_t>(64, ceil_div(s.dim, 16) * 16);
-  return tc_scratch_layout(kpad, nq, kk, tc_list_bytes(s, kk)).total;
+  return tc_scratch_layout(kpad, nq, kk, tc_list_bytes(s, kk),
+                           static_cast<size_t>(std::max(flat_tc_group_rows(s, k), 2 * tc::kM)))
+      .total;
 }
 
 // Runs the tensor-core screen for the queries in qp (normalized, dpad stride). Writes the per-query
 // candidates in the layout flat_finalize_kernel reads, and eps[q].
-void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
+void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq, size_t k,
                     const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, int kk,
                     float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits, float* eps,
                     int* err, void* scratch, cudaStream_t st) {
@@ -825,11 +936,13 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
              "tensor-core screen: unsupported best-list length");
   const int kpad = static_cast<int>(s.kpad);
   const bool l2 = s.metric == QV_METRIC_L2;
-  // Whole query groups of kTiles x 128 rows (zero rows past nq), so no TMA box extends past the
-  // tensor.
-  const size_t group_rows = static_cast<size_t>(tc::kTiles) * tc::kM;
+  const bool pair = !wide && flat_tc_pair(s, k);
+  // Whole query groups (zero rows past nq), so no TMA box extends past the tensor; the scratch
+  // pads to at least two query tiles for every screen.
+  const size_t group_rows =
+      static_cast<size_t>(std::max(flat_tc_group_rows(s, k), 2 * tc::kM));
   const size_t nq_pad = ceil_div(nq, group_rows) * group_rows;
-  const TcScratch L = tc_scratch_layout(s.kpad, nq, kk, tc_list_bytes(s, kk));
+  const TcScratch L = tc_scratch_layout(s.kpad, nq, kk, tc_list_bytes(s, kk), group_rows);
   unsigned char* base = static_cast<unsigned char*>(scratch);
   __half* q16 = reinterpret_cast<__half*>(base + L.q16);
   float* qinv = reinterpret_cast<float*>(base + L.qinv);
@@ -852,10 +965,11 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
                          256, 0, st>>>(gbest, nq * tc::kMaxKK, glock, nq);
   check_launch("init_best_kernel");
   const CUtensorMap mq = tc::make_map(q16, nq_pad, kpad);
-  const CUtensorMap mx = tc::make_map(s.x16.get(), s.n, kpad);
+  // A pair's CTAs each load 64 rows of every 128-row tile.
+  const CUtensorMap mx = tc::make_map(s.x16.get(), s.n, kpad, pair ? tc::kN / 2 : tc::kN);
   tc::Args a{};
   a.nq = static_cast<int>(nq);
-  a.n_qgroups = static_cast<int>(ceil_div(nq, group_rows));
+  a.n_qgroups = static_cast<int>(ceil_div(nq, static_cast<size_t>(flat_tc_group_rows(s, k))));
   a.n_chunks = n_chunks;
   a.total_units = a.n_qgroups * n_chunks;
   // K steps of 16 elements cover the dimension; the zero padding beyond the last one (up to the
@@ -883,31 +997,66 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
   a.drain_ns = tc::drain_limit_ns();
   a.skip_fill = tc::test_skip_fill();
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
-  const int stages = kk == 24 ? tc::Ring<24>::kStages : tc::Ring<32>::kStages;
-  const int append = kk == 24 ? tc::Ring<24>::kAppend : tc::Ring<32>::kAppend;
-  const size_t smem = 1024 + static_cast<size_t>(atoms) * tc::kAtomBytes * (tc::kTiles + stages) +
-                      static_cast<size_t>(kk + append) * tc::kLS * 8 +
-                      (2 * stages + tc::kAcc + 4) * 8;
-  QV_REQUIRE(smem <= 227 * 1024, "tensor-core screen: shared memory layout too large");
-  const int grid = std::min(a.total_units, sm_count(s.device));
+  const int workers = std::min(a.total_units, flat_tc_workers(s, k));
+  const int grid = pair ? 2 * workers : workers;
   KernelTimer timer(st, "flat_screen_tc_kernel", 2.0 * nq * static_cast<double>(s.n) * s.dim,
                     false);
-  auto launch = [&](auto kernel) {
-    QV_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    kernel<<<grid, tc::kThreads, smem, st>>>(mq, mx, a);
+  // Shared memory of one instantiation: alignment slack, the query tiles, the row ring, the
+  // candidate lists and the barriers.
+  auto smem_of = [&](auto ring, int at) {
+    using R = decltype(ring);
+    const size_t b_atom = pair ? tc::kAtomBytes / 2 : tc::kAtomBytes;
+    return 1024 + static_cast<size_t>(at) * tc::kAtomBytes * tc::kTiles +
+           static_cast<size_t>(R::kStages) * at * b_atom +
+           static_cast<size_t>(kk + R::kAppend) * tc::kLS * 8 + (2 * R::kStages + tc::kAcc + 4) * 8;
   };
+  auto launch = [&](auto kernel, size_t smem) {
+    QV_REQUIRE(smem <= 227 * 1024, "tensor-core screen: shared memory layout too large");
+    QV_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (!pair) {
+      kernel<<<grid, tc::kThreads, smem, st>>>(mq, mx, a);
+      return;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(tc::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    QV_CUDA(cudaLaunchKernelEx(&cfg, kernel, mq, mx, a));
+  };
+  // One instantiation per (atoms, metric, best-list length, pair).
+  auto pick = [&](auto atoms_c, auto kk_c, auto pair_c) {
+    constexpr int kA = decltype(atoms_c)::value, kK = decltype(kk_c)::value;
+    constexpr bool kP = decltype(pair_c)::value;
+    const size_t smem = smem_of(tc::Ring<kK, kP, kA>{}, kA);
+    if (l2)
+      launch(tc::flat_screen_tc_kernel<kA, true, kK, kP>, smem);
+    else
+      launch(tc::flat_screen_tc_kernel<kA, false, kK, kP>, smem);
+  };
+  using A1 = std::integral_constant<int, 1>;
+  using A2 = std::integral_constant<int, 2>;
+  using K24 = std::integral_constant<int, 24>;
+  using K32 = std::integral_constant<int, 32>;
+  using P0 = std::false_type;
+  using P1 = std::true_type;
   if (atoms == 2) {
-    if (kk == 24) {
-      if (l2) launch(tc::flat_screen_tc_kernel<2, true, 24>); else launch(tc::flat_screen_tc_kernel<2, false, 24>);
-    } else {
-      if (l2) launch(tc::flat_screen_tc_kernel<2, true, 32>); else launch(tc::flat_screen_tc_kernel<2, false, 32>);
-    }
+    if (kk == 24)
+      pair ? pick(A2{}, K24{}, P1{}) : pick(A2{}, K24{}, P0{});
+    else
+      pair ? pick(A2{}, K32{}, P1{}) : pick(A2{}, K32{}, P0{});
   } else {
-    if (kk == 24) {
-      if (l2) launch(tc::flat_screen_tc_kernel<1, true, 24>); else launch(tc::flat_screen_tc_kernel<1, false, 24>);
-    } else {
-      if (l2) launch(tc::flat_screen_tc_kernel<1, true, 32>); else launch(tc::flat_screen_tc_kernel<1, false, 32>);
-    }
+    if (kk == 24)
+      pair ? pick(A1{}, K24{}, P1{}) : pick(A1{}, K24{}, P0{});
+    else
+      pair ? pick(A1{}, K32{}, P1{}) : pick(A1{}, K32{}, P0{});
   }
   timer.stop();
   check_launch("flat_screen_tc_kernel");

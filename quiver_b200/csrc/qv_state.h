@@ -83,9 +83,13 @@ bool flat_tc_wide_fits(const FlatState& s, size_t k);
 int flat_tc_wide_kk(size_t k);
 size_t flat_tc_wide_list_bytes(const FlatState& s, int kk);
 void flat_tc_prepare(FlatState& s, cudaStream_t st);
-// Device scratch the tensor-core screen needs for nq queries with best lists of kk.
-size_t flat_tc_scratch_bytes(const FlatState& s, size_t nq, int kk);
-void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq,
+// Work units cover query groups of flat_tc_group_rows queries; flat_tc_workers of them (CTAs, or
+// CTA pairs) run at once.
+int flat_tc_group_rows(const FlatState& s, size_t k);
+int flat_tc_workers(const FlatState& s, size_t k);
+// Device scratch the tensor-core screen needs for nq queries, k results, best lists of kk.
+size_t flat_tc_scratch_bytes(const FlatState& s, size_t nq, size_t k, int kk);
+void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq, size_t k,
                     const uint64_t* d_bitmap, int n_chunks, int64_t chunk_rows, int kk,
                     float* cand_d, uint32_t* cand_r, int* cand_n, unsigned* thr_bits, float* eps,
                     int* err, void* scratch, cudaStream_t st);

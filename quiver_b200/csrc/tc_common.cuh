@@ -286,13 +286,26 @@ __device__ __forceinline__ bool mbar_test_cluster(uint32_t bar, uint32_t parity)
       : "memory");
   return ok != 0;
 }
+// The same with a suspend-time hint: a waiting thread sleeps in hardware until the phase completes
+// (or the hint elapses) instead of spinning, leaving issue slots to the warps that share it.
+__device__ __forceinline__ bool mbar_sleep_test_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
                                                   volatile int* abort_flag, int* err,
                                                   long long limit) {
   if (mbar_test_cluster(bar, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
-    if (mbar_test_cluster(bar, parity)) return true;
+    if (mbar_sleep_test_cluster(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > limit) {
       *abort_flag = 1;

@@ -163,12 +163,15 @@ def test_config0_full_size_against_reference(gpu, reference):
 
 # The MMAs take ceil(dim / 16) K-steps of 16: dims 20, 40 and 50 take 2, 3 and 4 in one
 # 64-column atom; 72, 96, 100 and 128 take 5, 6, 7 and 8 in two.
-@pytest.mark.parametrize("metric,dim", [("l2", 100), ("ip", 100), ("cosine", 100), ("l2", 50),
-                                        ("ip", 72), ("cosine", 96), ("l2", 128), ("ip", 40),
-                                        ("cosine", 20)])
-def test_tensor_core_screen_equals_simt_screen(gpu, oracle, monkeypatch, metric, dim):
-    """The tcgen05 fp16 screen and the float32 SIMT screen must produce identical final results
-    (both are re-ranked exactly and certified)."""
+@pytest.mark.parametrize("metric,dim,pair", [
+    ("l2", 100, "0"), ("ip", 100, "0"), ("cosine", 100, "0"), ("l2", 50, "0"), ("ip", 72, "0"),
+    ("cosine", 96, "0"), ("l2", 128, "0"), ("ip", 40, "0"), ("cosine", 20, "0"),
+    ("cosine", 100, "1"), ("l2", 128, "1"), ("ip", 40, "1")])
+def test_tensor_core_screen_equals_simt_screen(gpu, oracle, monkeypatch, metric, dim, pair):
+    """The tcgen05 fp16 screen (in single CTAs, and in CTA pairs with QV_TC_PAIR=1) and the
+    float32 SIMT screen must produce identical final results (both are re-ranked exactly and
+    certified)."""
+    monkeypatch.setenv("QV_TC_PAIR", pair)
     from quiver_b200.synthetic import mixture
     base = mixture(20000, dim, 50, 0.35, 1.0, centre_seed=3, seed=4)
     if metric != "cosine":
