@@ -50,6 +50,7 @@ constexpr int kThreads = 32 * (kIssuer2 + 1);
 constexpr int kAcc = 2;          // TMEM accumulator slots of kTiles x kN columns (all 512 columns)
 constexpr int kLS = kTiles * kM; // candidate-list stride: entry i of list l lives at i * kLS + l
 constexpr int kMaxKK = 32;       // largest best-list length (candidates per query per unit)
+constexpr int kMergeTries = 256; // attempts to take a query's running-list lock at a unit's end
 // Row-tile ring depth and list entries appended between compactions, by best-list length. A row
 // tile's stage is only refilled after its MMAs finish, so the next tile's copy has one tile time
 // (~900 cycles) to land with two stages, which L2 latency exceeds; three stages fit in shared
@@ -82,6 +83,9 @@ struct Args {
   long long wait_cycles;  // bound of every mbarrier wait (SM clock cycles)
   uint64_t drain_ns;      // bound of the abort path's waits for work in flight (global timer)
   int skip_fill;          // failure-detection test hook: CTA 0 skips this ring fill (-1: none)
+  // Threshold seeding launch: units only publish their lists' kKK-th values as the queries'
+  // thresholds (no candidate lists, no running best-list merge).
+  bool seed_only;
 };
 
 __device__ __forceinline__ void unit_coords(const Args& a, int u, int& qgroup, int& chunk) {
@@ -580,7 +584,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       compact_buffer<kKK, kAppend>(bd, br, cnt, thr);
       cnt = min(seen, kKK);  // the real entries: they sort before the padding
-      if (active) {
+      if (a.seed_only) {
+        // The main launch recomputes these groups bit for bit in the units of the row chunks
+        // holding them, and those units together output at least kKK groups at or below this
+        // list's kKK-th value: a valid threshold for every unit of the query.
+        if (active && cnt == kKK)
+          atomicMin(a.thr_bits + q, dev::ordered_bits(bd[(kKK - 1) * kLS]));
+      } else if (active) {
         // The whole list, padding included (the finalize reads cand_n entries), as 16-byte
         // stores: a lane's list is contiguous in global memory, strided across lanes.
         const size_t slot = static_cast<size_t>(q) * a.n_chunks + chunk;
@@ -599,9 +609,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Merge this unit's output into the query's running best-kKK list and publish its kKK-th
         // value as the query's threshold: kKK distinct output candidates lie at or below it, which
         // is all a threshold needs. Each unit merges once (its rows are disjoint from every other
-        // unit's), under a try-lock: when another unit holds it the merge is skipped, which only
-        // leaves the bound looser.
-        if (cnt > 0 && atomicCAS(a.glock + q, 0, 1) == 0) {
+        // unit's), under a lock taken with a bounded number of tries: the units of a wave finish
+        // together, and a merge skipped after the last try only leaves the bound looser (every
+        // later unit of the query then appends more of the groups it sees).
+        bool locked = false;
+        if (cnt > 0) {
+          for (int tries = 0; tries < kMergeTries && !locked; ++tries) {
+            locked = atomicCAS(a.glock + q, 0, 1) == 0;
+            if (!locked) __nanosleep(64);
+          }
+        }
+        if (locked) {
           __threadfence();
           volatile float* gq = a.gbest + static_cast<size_t>(q) * kMaxKK;
           // Both lists are sorted ascending and padded with +inf to 32, so c[i] = min(g[i],
@@ -996,9 +1014,34 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq, si
   a.wait_cycles = tc::wait_limit_cycles();
   a.drain_ns = tc::drain_limit_ns();
   a.skip_fill = tc::test_skip_fill();
+  a.seed_only = false;
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
-  const int workers = std::min(a.total_units, flat_tc_workers(s, k));
+  const int max_workers = flat_tc_workers(s, k);
+  const int workers = std::min(a.total_units, max_workers);
   const int grid = pair ? 2 * workers : workers;
+  // Threshold seeding (QV_TC_SEED=1): in the main launch's first wave every query has several
+  // units running at once, all starting from an infinite threshold. A short first launch over a
+  // few 4096-row sub-chunks (as many per query group as fill the GPU, together at most an eighth
+  // of the rows) publishes each query's kKK-th best group there as its starting threshold. Off
+  // by default: on config 1 the screen took 2.25 ms with it against 2.19 ms without, so the
+  // first wave's appends are not what the candidate work costs.
+  constexpr int64_t kSeedRows = 4096;
+  tc::Args seed = a;
+  const char* seed_env = std::getenv("QV_TC_SEED");
+  const int seed_chunks = static_cast<int>(std::min<int64_t>(
+      std::max(1, max_workers / std::max(1, a.n_qgroups)),
+      static_cast<int64_t>(s.n) / (8 * kSeedRows)));
+  const bool seeding = n_chunks > 1 && seed_chunks >= 1 && seed_env != nullptr &&
+                       seed_env[0] == '1';
+  if (seeding) {
+    seed.seed_only = true;
+    seed.skip_fill = -1;
+    seed.n_chunks = seed_chunks;
+    seed.chunk_rows = kSeedRows;
+    seed.nrows = kSeedRows * seed_chunks;
+    seed.total_units = a.n_qgroups * seed_chunks;
+  }
+  const int seed_workers = std::min(seed.total_units, max_workers);
   KernelTimer timer(st, "flat_screen_tc_kernel", 2.0 * nq * static_cast<double>(s.n) * s.dim,
                     false);
   // Shared memory of one instantiation: alignment slack, the query tiles, the row ring, the
@@ -1010,15 +1053,15 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq, si
            static_cast<size_t>(R::kStages) * at * b_atom +
            static_cast<size_t>(kk + R::kAppend) * tc::kLS * 8 + (2 * R::kStages + tc::kAcc + 4) * 8;
   };
-  auto launch = [&](auto kernel, size_t smem) {
+  auto launch = [&](auto kernel, size_t smem, const tc::Args& args, int grid_) {
     QV_REQUIRE(smem <= 227 * 1024, "tensor-core screen: shared memory layout too large");
     QV_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (!pair) {
-      kernel<<<grid, tc::kThreads, smem, st>>>(mq, mx, a);
+      kernel<<<grid_, tc::kThreads, smem, st>>>(mq, mx, args);
       return;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.gridDim = dim3(static_cast<unsigned>(grid_));
     cfg.blockDim = dim3(tc::kThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -1029,17 +1072,17 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq, si
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    QV_CUDA(cudaLaunchKernelEx(&cfg, kernel, mq, mx, a));
+    QV_CUDA(cudaLaunchKernelEx(&cfg, kernel, mq, mx, args));
   };
   // One instantiation per (atoms, metric, best-list length, pair).
   auto pick = [&](auto atoms_c, auto kk_c, auto pair_c) {
     constexpr int kA = decltype(atoms_c)::value, kK = decltype(kk_c)::value;
     constexpr bool kP = decltype(pair_c)::value;
     const size_t smem = smem_of(tc::Ring<kK, kP, kA>{}, kA);
-    if (l2)
-      launch(tc::flat_screen_tc_kernel<kA, true, kK, kP>, smem);
-    else
-      launch(tc::flat_screen_tc_kernel<kA, false, kK, kP>, smem);
+    auto kernel = l2 ? tc::flat_screen_tc_kernel<kA, true, kK, kP>
+                     : tc::flat_screen_tc_kernel<kA, false, kK, kP>;
+    if (seeding) launch(kernel, smem, seed, pair ? 2 * seed_workers : seed_workers);
+    launch(kernel, smem, a, grid);
   };
   using A1 = std::integral_constant<int, 1>;
   using A2 = std::integral_constant<int, 2>;
