@@ -2,6 +2,7 @@
 // reference's error wording, host<->device staging, and the .qvr load/save of both index types.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <limits>
 #include <map>
@@ -871,13 +872,75 @@ qv_status qv_ivfpq_is_trained(const qv_ivfpq* index, int* trained) {
   });
 }
 
+namespace {
+constexpr size_t kAddChunkBytes = size_t{64} << 20;  // rows per streamed add() chunk: 64 MiB
+
+// This thread's pinned staging buffer for streamed uploads (grown on demand, kept for reuse).
+unsigned char* thread_staging(size_t bytes) {
+  struct Staging {
+    void* p = nullptr;
+    size_t bytes = 0;
+    ~Staging() {
+      if (p != nullptr) cudaFreeHost(p);
+    }
+  };
+  thread_local Staging st;
+  if (st.bytes < bytes) {
+    if (st.p != nullptr) QV_CUDA(cudaFreeHost(st.p));
+    st.p = nullptr;
+    st.bytes = 0;
+    QV_CUDA(cudaHostAlloc(&st.p, bytes, cudaHostAllocPortable));
+    st.bytes = bytes;
+  }
+  return static_cast<unsigned char*>(st.p);
+}
+}  // namespace
+
+// add()'s assignment and PQ encode of n host rows (src/ivfpq_index.cc:234-246), streamed: chunks
+// of kAddChunkBytes (QV_IVF_ADD_CHUNK_ROWS rows when set) are copied into one of two pinned
+// staging halves on the host while the GPU uploads, normalizes (cosine) and encodes the previous
+// chunk. The rows stay on the device (dx) only when the index stores vectors; otherwise the
+// device holds two chunks, so a batch larger than the GPU's memory can be added. Every row is
+// encoded on its own, so the chunking does not change any code or assignment.
 static void ivf_encode_host(const IvfState& s, const float* vectors, size_t n, cudaStream_t st,
                             DeviceBuffer& dx, std::vector<uint32_t>& assign,
                             std::vector<uint8_t>& codes) {
-  h2d(dx, vectors, n * s.dim, st);
-  if (s.metric == QV_METRIC_COSINE) normalize_rows_device(dx.get<float>(), n, s.dim, st);
+  const size_t row_bytes = s.dim * sizeof(float);
+  size_t chunk = std::max<size_t>(1, kAddChunkBytes / row_bytes);
+  if (const char* e = std::getenv("QV_IVF_ADD_CHUNK_ROWS"); e != nullptr && *e != '\0')
+    chunk = static_cast<size_t>(std::max(1LL, std::atoll(e)));
+  chunk = std::min(chunk, n);
   DeviceBuffer da(n * sizeof(uint32_t), st), dc(n * s.m, st);
-  ivf_encode_device(s, dx.get<float>(), n, da.get<uint32_t>(), dc.get<uint8_t>(), st);
+  DeviceBuffer dchunk[2];
+  if (s.store_vectors) {
+    dx.allocate(n * row_bytes, st);
+  } else {
+    dchunk[0].allocate(chunk * row_bytes, st);
+    if (chunk < n) dchunk[1].allocate(chunk * row_bytes, st);
+  }
+  unsigned char* stage = thread_staging(2 * chunk * row_bytes);
+  cudaEvent_t uploaded[2] = {nullptr, nullptr};  // a staging half's upload has finished
+  for (cudaEvent_t& e : uploaded) QV_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  try {
+    for (size_t c = 0, i = 0; c < n; c += chunk, ++i) {
+      const size_t rows = std::min(chunk, n - c);
+      const int b = static_cast<int>(i & 1);
+      unsigned char* half = stage + b * chunk * row_bytes;
+      if (i >= 2) QV_CUDA(cudaEventSynchronize(uploaded[b]));
+      std::memcpy(half, vectors + c * s.dim, rows * row_bytes);
+      float* dst = s.store_vectors ? dx.get<float>() + c * s.dim : dchunk[b].get<float>();
+      QV_CUDA(cudaMemcpyAsync(dst, half, rows * row_bytes, cudaMemcpyHostToDevice, st));
+      QV_CUDA(cudaEventRecord(uploaded[b], st));
+      if (s.metric == QV_METRIC_COSINE) normalize_rows_device(dst, rows, s.dim, st);
+      ivf_encode_device(s, dst, rows, da.get<uint32_t>() + c, dc.get<uint8_t>() + c * s.m, st);
+    }
+    QV_CUDA(cudaStreamSynchronize(st));
+  } catch (...) {
+    cudaStreamSynchronize(st);
+    for (cudaEvent_t e : uploaded) cudaEventDestroy(e);
+    throw;
+  }
+  for (cudaEvent_t e : uploaded) cudaEventDestroy(e);
   assign.resize(n);
   codes.resize(n * s.m);
   QV_CUDA(cudaMemcpyAsync(assign.data(), da.get(), n * sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
