@@ -22,9 +22,6 @@ namespace {
 constexpr float kInf = __builtin_huge_valf();
 constexpr size_t kMaxPrecomputedBytes = size_t{256} << 20;  // src/ivfpq_index.cc:74
 constexpr int kScanThreads = 256;
-constexpr int kTileP = 32;  // points (or queries) per coarse tile
-constexpr int kTileC = 64;  // centroids per coarse tile
-constexpr int kTileD = 64;  // dims per coarse tile
 
 // ---- trained state -------------------------------------------------------------------------------
 
@@ -58,105 +55,7 @@ __global__ void precompute_kernel(const float* cents, size_t nlist, const float*
   pre[i] = v;
 }
 
-// ---- coarse: shared tile machinery -----------------------------------------------------------------
-// A block covers kTileP points x all centroids; 256 threads = 32 points x 8 centroid lanes. Each
-// thread accumulates 8 centroids (c = cbase + lane8 + 8*i) over dims in ascending order, so each
-// (point, centroid) sum is sequential in j exactly like CentroidTable.
-enum CoarseMode { kDot = 0, kL2Diff = 1 };
-
-template <int kMode>
-__device__ __forceinline__ void coarse_tile(const float* __restrict__ xs_t /*kTileD x kTileP*/,
-                                            const float* __restrict__ cs /*kTileC x kTileD*/,
-                                            int nd, int p, int cl, float acc[8]) {
-  for (int j = 0; j < nd; ++j) {
-    const float xv = xs_t[j * kTileP + p];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float cv = cs[(cl + 8 * i) * (kTileD + 1) + j];
-      if (kMode == kDot) {
-        acc[i] = __fadd_rn(acc[i], __fmul_rn(xv, cv));
-      } else {
-        const float d = __fsub_rn(xv, cv);
-        acc[i] = __fadd_rn(acc[i], __fmul_rn(d, d));
-      }
-    }
-  }
-}
-
-// Loads points [p0, p0+kTileP) x dims [d0, d0+nd) transposed, and centroids [c0, c0+kTileC).
-__device__ __forceinline__ void load_coarse_tiles(const float* __restrict__ x, size_t n,
-                                                  const float* __restrict__ cents, size_t nlist,
-                                                  int dim, size_t p0, size_t c0, int d0, int nd,
-                                                  float* xs_t, float* cs) {
-  for (int idx = threadIdx.x; idx < kTileP * kTileD; idx += blockDim.x) {
-    const int p = idx / kTileD, j = idx - p * kTileD;
-    const size_t gp = p0 + p;
-    xs_t[j * kTileP + p] = (gp < n && j < nd) ? x[gp * dim + d0 + j] : 0.0f;
-  }
-  for (int idx = threadIdx.x; idx < kTileC * kTileD; idx += blockDim.x) {
-    const int c = idx / kTileD, j = idx - c * kTileD;
-    const size_t gc = c0 + c;
-    cs[c * (kTileD + 1) + j] = (gc < nlist && j < nd) ? cents[gc * dim + d0 + j] : 0.0f;
-  }
-}
-
-// CentroidTable::nearest_batch (src/internal/centroid_table.h:94-144): d = ||c||^2 - 2<x,c> (or
-// -<x,c> for max inner product), first strict minimum over ascending c.
-__global__ void __launch_bounds__(256) coarse_assign_kernel(const float* __restrict__ x, size_t n,
-                                                            const float* __restrict__ cents,
-                                                            const float* __restrict__ cnorm2,
-                                                            size_t nlist, int dim, bool by_ip,
-                                                            uint32_t* __restrict__ out) {
-  __shared__ float xs_t[kTileD * kTileP];
-  __shared__ float cs[kTileC * (kTileD + 1)];
-  __shared__ float bd[8][kTileP];
-  __shared__ uint32_t bc[8][kTileP];
-  const int p = threadIdx.x & 31, cl = threadIdx.x >> 5;
-  const size_t p0 = static_cast<size_t>(blockIdx.x) * kTileP;
-  // (best distance, centroid) starts at (+inf, 0) like the reference's zero-initialized output.
-  float best_d = kInf;
-  uint32_t best_c = 0;
-  for (size_t c0 = 0; c0 < nlist; c0 += kTileC) {
-    float acc[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-    for (int d0 = 0; d0 < dim; d0 += kTileD) {
-      const int nd = min(kTileD, dim - d0);
-      __syncthreads();
-      load_coarse_tiles(x, n, cents, nlist, dim, p0, c0, d0, nd, xs_t, cs);
-      __syncthreads();
-      coarse_tile<kDot>(xs_t, cs, nd, p, cl, acc);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const size_t c = c0 + cl + 8 * i;
-      if (c < nlist) {
-        const float d = by_ip ? -acc[i] : __fsub_rn(cnorm2[c], __fmul_rn(2.0f, acc[i]));
-        if (d < best_d) {  // ascending c within this thread: strict < keeps the first minimum
-          best_d = d;
-          best_c = static_cast<uint32_t>(c);
-        }
-      }
-    }
-  }
-  bd[cl][p] = best_d;
-  bc[cl][p] = best_c;
-  __syncthreads();
-  if (cl == 0) {
-    float d = bd[0][p];
-    uint32_t c = bc[0][p];
-    for (int i = 1; i < 8; ++i) {
-      const float di = bd[i][p];
-      const uint32_t ci = bc[i][p];
-      if (di < d || (di == d && ci < c)) {
-        d = di;
-        c = ci;
-      }
-    }
-    const size_t gp = p0 + p;
-    if (gp < n) out[gp] = c;
-  }
-}
+// ---- coarse distances and assignment ---------------------------------------------------------------
 
 // Search-time coarse distances (src/ivfpq_index.cc:285-297 with CentroidTable::l2 / ::dot):
 // L2: sum_j (q_j - c_j)^2; IP/cosine: -(sum_j q_j c_j), j ascending, separately rounded.
@@ -225,6 +124,104 @@ __global__ void __launch_bounds__(256) coarse_dist_kernel4(const float* __restri
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       if (cb + i < nlist) out[gp * nlist + cb + i] = ip ? -acc[a][i] : acc[a][i];
+  }
+}
+
+// CentroidTable::nearest_batch (src/internal/centroid_table.h:94-144) with the register tiling of
+// coarse_dist_kernel4: a block covers 128 points and loops over every 64-centroid tile; a thread
+// accumulates <x, c> for 4 points x 8 centroids (each sum sequential in the dimension, separately
+// rounded), turns them into d = ||c||^2 - 2<x,c> (or -<x,c> by_ip) and keeps, per point, the
+// first strict minimum over its ascending centroids; the 8 centroid lanes are then merged by
+// (distance, centroid), which keeps the lowest centroid among equal minima. (+inf, 0) start, as
+// the reference's zero-initialized output, so a point whose every distance is +inf or NaN gets 0.
+__global__ void __launch_bounds__(256) coarse_assign_kernel4(const float* __restrict__ x, size_t n,
+                                                             const float* __restrict__ cents,
+                                                             const float* __restrict__ cnorm2,
+                                                             size_t nlist, int dim, bool by_ip,
+                                                             uint32_t* __restrict__ out) {
+  __shared__ __align__(16) float xs[kTileD4 * kXs4];  // xs[j][p]
+  __shared__ __align__(16) float cs[kTileD4 * kCs4];  // cs[j][c]
+  __shared__ float rbd[8][kTileP4];
+  __shared__ uint32_t rbc[8][kTileP4];
+  const int pl = threadIdx.x & 31, cl = threadIdx.x >> 5;  // points 4pl.., centroids 8cl..
+  const size_t p0 = static_cast<size_t>(blockIdx.x) * kTileP4;
+  float best_d[4];
+  uint32_t best_c[4];
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    best_d[a] = kInf;
+    best_c[a] = 0;
+  }
+  for (size_t c0 = 0; c0 < nlist; c0 += kTileC4) {
+    float acc[4][8];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[a][i] = 0.0f;
+    for (int d0 = 0; d0 < dim; d0 += kTileD4) {
+      const int nd = min(kTileD4, dim - d0);
+      __syncthreads();
+      for (int idx = threadIdx.x; idx < kTileP4 * kTileD4; idx += 256) {
+        const int p = idx / kTileD4, j = idx - p * kTileD4;
+        const size_t gp = p0 + p;
+        xs[j * kXs4 + p] = (gp < n && j < nd) ? x[gp * dim + d0 + j] : 0.0f;
+      }
+      for (int idx = threadIdx.x; idx < kTileC4 * kTileD4; idx += 256) {
+        const int c = idx / kTileD4, j = idx - c * kTileD4;
+        const size_t gc = c0 + c;
+        cs[j * kCs4 + c] = (gc < nlist && j < nd) ? cents[gc * dim + d0 + j] : 0.0f;
+      }
+      __syncthreads();
+      for (int j = 0; j < nd; ++j) {
+        const float4 xq = *reinterpret_cast<const float4*>(xs + j * kXs4 + 4 * pl);
+        const float4 c_lo = *reinterpret_cast<const float4*>(cs + j * kCs4 + 8 * cl);
+        const float4 c_hi = *reinterpret_cast<const float4*>(cs + j * kCs4 + 8 * cl + 4);
+        const float xv[4] = {xq.x, xq.y, xq.z, xq.w};
+        const float cv[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[a][i] = __fadd_rn(acc[a][i], __fmul_rn(xv[a], cv[i]));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const size_t c = c0 + 8 * static_cast<size_t>(cl) + i;
+      if (c >= nlist) continue;
+      const float cn = by_ip ? 0.0f : cnorm2[c];
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        const float d = by_ip ? -acc[a][i] : __fsub_rn(cn, __fmul_rn(2.0f, acc[a][i]));
+        if (d < best_d[a]) {  // ascending c within this thread: strict < keeps the first minimum
+          best_d[a] = d;
+          best_c[a] = static_cast<uint32_t>(c);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int a = 0; a < 4; ++a) {
+    rbd[cl][4 * pl + a] = best_d[a];
+    rbc[cl][4 * pl + a] = best_c[a];
+  }
+  __syncthreads();
+  if (cl == 0) {
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+      const int p = 4 * pl + a;
+      float d = rbd[0][p];
+      uint32_t c = rbc[0][p];
+      for (int i = 1; i < 8; ++i) {
+        const float di = rbd[i][p];
+        const uint32_t ci = rbc[i][p];
+        if (di < d || (di == d && ci < c)) {
+          d = di;
+          c = ci;
+        }
+      }
+      const size_t gp = p0 + p;
+      if (gp < n) out[gp] = c;
+    }
   }
 }
 
@@ -374,11 +371,15 @@ __global__ void residual_kernel(const float* __restrict__ x, size_t n, int dim,
 
 // ProductQuantizer::encode (src/product_quantizer.cc:165-171): per sub-space the first index of
 // the minimum of sum_t (r_t - cb_t)^2 (CentroidTable::l2 + argmin_n). grid.y = sub-space.
+// kD = the sub-space width when it is a compile-time constant (the thread's residual slice then
+// stays in registers for all 256 sub-centroids), 0 for any other width.
+template <int kD>
 __global__ void pq_encode_kernel(const float* __restrict__ resid, size_t n, int dim, int m,
-                                 int dsub, const float* __restrict__ cb,
+                                 int dsub_rt, const float* __restrict__ cb,
                                  uint8_t* __restrict__ codes) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* sc = reinterpret_cast<float*>(smem_raw);  // 256 x dsub
+  const int dsub = kD > 0 ? kD : dsub_rt;
   const int j = blockIdx.y;
   for (int i = threadIdx.x; i < kSubCentroids * dsub; i += blockDim.x)
     sc[i] = cb[static_cast<size_t>(j) * kSubCentroids * dsub + i];
@@ -386,16 +387,35 @@ __global__ void pq_encode_kernel(const float* __restrict__ resid, size_t n, int 
   const size_t row = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
   if (row >= n) return;
   const float* r = resid + row * dim + static_cast<size_t>(j) * dsub;
+  float rr[kD > 0 ? kD : 1];  // the residual slice, read once (compile-time widths)
+  if constexpr (kD > 0) {
+#pragma unroll
+    for (int t = 0; t < kD; ++t) rr[t] = r[t];
+  }
+  // The squared distance to sub-centroid c, sequential in t, separately rounded.
+  auto dist = [&](int c) {
+    float s = 0.0f;
+    if constexpr (kD > 0) {
+#pragma unroll
+      for (int t = 0; t < kD; ++t) {
+        const float d = __fsub_rn(rr[t], sc[c * kD + t]);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+      }
+    } else {
+      for (int t = 0; t < dsub; ++t) {
+        const float d = __fsub_rn(r[t], sc[c * dsub + t]);
+        s = __fadd_rn(s, __fmul_rn(d, d));
+      }
+    }
+    return s;
+  };
   // argmin_n: the minimum m (NaN never wins), then the first index holding m. A strict-< scan
   // finds that index whenever m is finite; only when m = +inf is a second pass needed.
   float best = kInf;
   int code = 0;
+#pragma unroll 4
   for (int c = 0; c < kSubCentroids; ++c) {
-    float s = 0.0f;
-    for (int t = 0; t < dsub; ++t) {
-      const float d = __fsub_rn(r[t], sc[c * dsub + t]);
-      s = __fadd_rn(s, __fmul_rn(d, d));
-    }
+    const float s = dist(c);
     if (s < best) {
       best = s;
       code = c;
@@ -403,12 +423,7 @@ __global__ void pq_encode_kernel(const float* __restrict__ resid, size_t n, int 
   }
   if (best == kInf) {
     for (int c = 0; c < kSubCentroids; ++c) {
-      float s = 0.0f;
-      for (int t = 0; t < dsub; ++t) {
-        const float d = __fsub_rn(r[t], sc[c * dsub + t]);
-        s = __fadd_rn(s, __fmul_rn(d, d));
-      }
-      if (s == kInf) {
+      if (dist(c) == kInf) {
         code = c;
         break;
       }
@@ -940,30 +955,40 @@ void nearest_centroids_device(const float* d_x, size_t n, const float* d_cents, 
   centroid_norms_kernel<<<ceil_div(k, 256), 256, 0, st>>>(d_cents, k, static_cast<int>(dim),
                                                           d_cnorm2);
   check_launch("centroid_norms_kernel");
-  coarse_assign_kernel<<<ceil_div(n, kTileP), 256, 0, st>>>(d_x, n, d_cents, d_cnorm2, k,
-                                                            static_cast<int>(dim), by_ip, d_assign);
-  check_launch("coarse_assign_kernel");
+  coarse_assign_kernel4<<<ceil_div(n, kTileP4), 256, 0, st>>>(d_x, n, d_cents, d_cnorm2, k,
+                                                              static_cast<int>(dim), by_ip,
+                                                              d_assign);
+  check_launch("coarse_assign_kernel4");
 }
 
 void ivf_encode_device(const IvfState& s, const float* d_x, size_t n, uint32_t* d_assign,
                        uint8_t* d_codes, cudaStream_t st) {
   if (n == 0) return;
-  coarse_assign_kernel<<<ceil_div(n, kTileP), 256, 0, st>>>(
+  coarse_assign_kernel4<<<ceil_div(n, kTileP4), 256, 0, st>>>(
       d_x, n, s.centroids.get<float>(), s.cnorm2.get<float>(), s.nlist, static_cast<int>(s.dim),
       s.metric == QV_METRIC_IP, d_assign);  // assign_by_ip (src/ivfpq_index.cc:107)
-  check_launch("coarse_assign_kernel");
+  check_launch("coarse_assign_kernel4");
   DeviceBuffer resid(n * s.dim * sizeof(float), st);
   residual_kernel<<<ceil_div(n * s.dim, 256), 256, 0, st>>>(
       d_x, n, static_cast<int>(s.dim), s.centroids.get<float>(), d_assign, resid.get<float>());
   check_launch("residual_kernel");
   const size_t smem = kSubCentroids * s.dsub * sizeof(float);
   QV_REQUIRE(smem <= 227 * 1024, "PQ sub-space too wide for the GPU encoder");
-  QV_CUDA(cudaFuncSetAttribute(pq_encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)smem));
+  void (*encode)(const float*, size_t, int, int, int, const float*, uint8_t*) =
+      pq_encode_kernel<0>;
+  switch (s.dsub) {
+    case 1: encode = pq_encode_kernel<1>; break;
+    case 2: encode = pq_encode_kernel<2>; break;
+    case 4: encode = pq_encode_kernel<4>; break;
+    case 8: encode = pq_encode_kernel<8>; break;
+    case 16: encode = pq_encode_kernel<16>; break;
+    default: break;
+  }
+  QV_CUDA(cudaFuncSetAttribute(encode, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   dim3 grid(static_cast<unsigned>(ceil_div(n, 256)), static_cast<unsigned>(s.m));
-  pq_encode_kernel<<<grid, 256, smem, st>>>(resid.get<float>(), n, static_cast<int>(s.dim),
-                                            static_cast<int>(s.m), static_cast<int>(s.dsub),
-                                            s.codebooks.get<float>(), d_codes);
+  encode<<<grid, 256, smem, st>>>(resid.get<float>(), n, static_cast<int>(s.dim),
+                                  static_cast<int>(s.m), static_cast<int>(s.dsub),
+                                  s.codebooks.get<float>(), d_codes);
   check_launch("pq_encode_kernel");
 }
 

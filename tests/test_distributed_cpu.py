@@ -236,7 +236,9 @@ def test_a_rank_missing_from_a_collective_is_detected_by_timeout():
              for r in range(WORLD)]
     for p in procs:
         p.start()
-    rank, err, waited = q.get(timeout=60)
+    # Generous: the spawned ranks first import torch, slow on a loaded host; the failure latency
+    # itself is measured inside the rank (`waited`).
+    rank, err, waited = q.get(timeout=240)
     assert rank == 0 and err != "no error", "the collective returned without its peer"
     assert waited < 30, f"the failure took {waited:.1f} s to surface"
     for p in procs:
