@@ -147,19 +147,25 @@ def _triples_bit_exact(rank, world):
 
 
 def _collective_timeout_entry(rank, world, port, out_q):
-    """Rank 1 never joins the collective; rank 0 must get an error from its process group's
-    short timeout instead of waiting for ever."""
+    """Rank 1 never joins the collective; rank 0 must get an error from its group's short timeout
+    instead of waiting for ever. The rendezvous itself has a long timeout (a spawned rank can take
+    a while to import torch on a loaded host); the collective runs on a subgroup with a 2 s one."""
     import time
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=2))
+    try:
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=180))
+        short = dist.new_group(list(range(world)), timeout=timedelta(seconds=2), backend="gloo")
+    except Exception as e:  # noqa: BLE001 - reported to the test instead of a silent exit
+        out_q.put((rank, "setup failed: " + repr(e), -1.0))
+        os._exit(1)
     if rank == 1:
         time.sleep(8)  # absent from the collective until rank 0 has given up
         os._exit(0)
     t0 = time.time()
     try:
         from quiver_b200.distributed import _all_gather
-        _all_gather(torch.zeros(4), world, None)
+        _all_gather(torch.zeros(4), world, short)
         out_q.put((rank, "no error", time.time() - t0))
     except Exception as e:  # noqa: BLE001 - the failure being tested
         out_q.put((rank, repr(e), time.time() - t0))
@@ -239,6 +245,7 @@ def test_a_rank_missing_from_a_collective_is_detected_by_timeout():
     # Generous: the spawned ranks first import torch, slow on a loaded host; the failure latency
     # itself is measured inside the rank (`waited`).
     rank, err, waited = q.get(timeout=240)
+    assert not err.startswith("setup failed"), err
     assert rank == 0 and err != "no error", "the collective returned without its peer"
     assert waited < 30, f"the failure took {waited:.1f} s to surface"
     for p in procs:
