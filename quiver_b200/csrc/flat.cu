@@ -105,8 +105,8 @@ struct EpsModel {
 // keeps the host from scanning the batch before each search; the finalize gives such a query
 // no results (QV_INVALID_LABEL with a NaN distance) and the host-buffer entry point raises.
 __global__ void prep_queries_kernel(const float* q, size_t nq, int dim, int dpad, bool cosine,
-                                    bool l2, EpsModel em, float xmax, float* qp, float* qnorm2,
-                                    float* eps, int* qbad, int* nonfinite) {
+                                    bool l2, bool drop_qnorm, EpsModel em, float xmax, float* qp,
+                                    float* qnorm2, float* eps, int* qbad, int* nonfinite) {
   const int lane = threadIdx.x & 31;
   const size_t row = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= nq) return;
@@ -128,7 +128,7 @@ __global__ void prep_queries_kernel(const float* q, size_t nq, int dim, int dpad
   for (int i = lane; i < dim; i += 32) s = fmaf(out[i], out[i], s);
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(kFull, s, o);
   if (lane == 0) {
-    qnorm2[row] = s;
+    qnorm2[row] = drop_qnorm ? 0.0f : s;
     const float qn = sqrtf(s) * 1.0001f;
     if (l2) {
       const float t = qn + xmax;
@@ -223,14 +223,15 @@ struct ThreadHeap {
 // ---- SIMT screen ---------------------------------------------------------------------------------
 // Unit u: chunk = u / n_qtiles, query tile = u % n_qtiles (chunk-major, so concurrently running
 // units share row chunks in L2). Thread t owns query qtile*qpb + t. Screen distance:
-//   L2: ||q||^2 + ||x||^2 - 2<q,x>,  IP/cosine: 1 - <q,x>,  float32 with FMA.
+//   L2: ||q||^2 + ||x||^2 - 2<q,x>,  IP/cosine: ip_one - <q,x> (ip_one 1, or 0 for -<q,x>),
+//   float32 with FMA.
 template <bool kL2>
 __global__ void __launch_bounds__(128) flat_screen_simt_kernel(
     const float* __restrict__ qp, int dpad, const float* __restrict__ qnorm2, int nq, int qpb,
     const float* __restrict__ x, int dim, const float* __restrict__ xnorm2, int64_t nrows,
     const uint64_t* __restrict__ bitmap, int64_t chunk_rows, int n_qtiles, int n_chunks, int kk,
     float* __restrict__ cand_d, uint32_t* __restrict__ cand_r, int* __restrict__ cand_n,
-    unsigned* __restrict__ thr_bits) {
+    unsigned* __restrict__ thr_bits, float ip_one) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* xs = reinterpret_cast<float*>(smem_raw);  // kScreenRows x kScreenDChunk
   float* hd = xs + kScreenRows * kScreenDChunk;     // kk x qpb
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(128) flat_screen_simt_kernel(
     for (int r = 0; r < kScreenRows; ++r) {
       if (r < nr) {
         const int64_t row = rb + r;
-        float dist = kL2 ? fmaf(-2.0f, acc[r], qn + xnorm2[row]) : 1.0f - acc[r];
+        float dist = kL2 ? fmaf(-2.0f, acc[r], qn + xnorm2[row]) : ip_one - acc[r];
         dist = dev::nan_to_inf(dist);
         if (dist <= thr && dev::bitmap_test(bitmap, static_cast<uint64_t>(row))) {
           heap.push(dist, static_cast<uint32_t>(row));
@@ -327,7 +328,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
     const float* __restrict__ qp, int dpad, const float* __restrict__ eps_q, int nq,
     const float* __restrict__ x, int dim, int64_t nrows, const uint64_t* __restrict__ bitmap,
     const uint64_t* __restrict__ labels, uint64_t row_offset,
-    bool l2, bool sq8, const float* __restrict__ cand_d,
+    bool l2, int kind, const float* __restrict__ cand_d,
     const uint32_t* __restrict__ cand_r, const int* __restrict__ cand_n, int n_chunks, int kk,
     int group_rows, int pool, int k, uint64_t* __restrict__ out_labels, float* __restrict__ out_d,
     uint64_t* __restrict__ out_keys, const int* __restrict__ qbad, int* __restrict__ fail_count,
@@ -397,7 +398,7 @@ __global__ void __launch_bounds__(kFinalizeThreads) flat_finalize_kernel(
       xr[r] = x + (row[r] == ~0ull ? 0 : row[r]) * dim;
     }
     float e[4];
-    dev::warp_exact_distance_x4(qrow, xr, dim, l2, lane, e, sq8);
+    dev::warp_exact_distance_x4(qrow, xr, dim, l2, lane, e, kind);
     if (lane == 0) {
 #pragma unroll
       for (int r = 0; r < 4; ++r)
@@ -566,22 +567,67 @@ __device__ __forceinline__ float lane_reduce_sq8(const float* __restrict__ q,
   return sum;
 }
 
-// The exact distance of the stored row x: the float32 kernels' order (src/flat_index.cc:87), or
-// with sq8 the SQ8 kernels' (src/hnsw_index.cc:202-218; x is then the decoded codes).
+// CentroidTable's sequential sums (src/internal/centroid_table.h:65-144) evaluated by ONE thread:
+// the same rounded operations in the same order as dev::seq_reduce / dev::seq_norm_minus_2dot,
+// with the row read 16 bytes at a time when the rows allow it (q is in shared memory, where all
+// lanes read the same element). kNorm: ||x||^2 - 2<q,x> (L2 only).
+template <bool kDiff, bool kNorm>
+__device__ __forceinline__ float lane_reduce_seq(const float* __restrict__ q,
+                                                 const float* __restrict__ x, int dim) {
+  float s = 0.0f, nn = 0.0f;
+  auto acc = [&](float u, float v) {
+    if (kNorm) nn = __fadd_rn(nn, __fmul_rn(v, v));
+    if (kDiff) {
+      u = __fsub_rn(u, v);
+      v = u;
+    }
+    s = __fadd_rn(s, __fmul_rn(u, v));
+  };
+  int i = 0;
+  if ((dim & 3) == 0) {  // rows and q start on 16-byte boundaries
+    for (; i < dim; i += 4) {
+      const float4 xv = __ldg(reinterpret_cast<const float4*>(x + i));
+      const float4 qv = *reinterpret_cast<const float4*>(q + i);
+      acc(qv.x, xv.x);
+      acc(qv.y, xv.y);
+      acc(qv.z, xv.z);
+      acc(qv.w, xv.w);
+    }
+  }
+  for (; i < dim; ++i) acc(q[i], __ldg(x + i));
+  return kNorm ? __fsub_rn(nn, __fmul_rn(2.0f, s)) : s;
+}
+
+// The exact distance of the stored row x for an exact-distance kind (summation order |
+// kKindNegIp): the float32 kernels' order (src/flat_index.cc:87), the SQ8 kernels'
+// (src/hnsw_index.cc:202-218; x is then the decoded codes), CentroidTable's sequential sums
+// (src/internal/centroid_table.h:65-85), or for L2 its ||x||^2 - 2<q,x> (:94-144); inner
+// product as 1 - <q,x>, or -<q,x> with kKindNegIp.
 __device__ __forceinline__ float lane_exact_distance(const float* q, const float* x, int dim,
-                                                     bool l2, bool sq8) {
-  if (sq8)
-    return l2 ? lane_reduce_sq8<true>(q, x, dim) : __fsub_rn(1.0f, lane_reduce_sq8<false>(q, x, dim));
-  return l2 ? lane_reduce_avx2<true>(q, x, dim) : __fsub_rn(1.0f, lane_reduce_avx2<false>(q, x, dim));
+                                                     bool l2, int kind) {
+  const int order = kind & 3;
+  float s;
+  if (order == 3 && l2) return lane_reduce_seq<false, true>(q, x, dim);
+  if (order == 1)
+    s = l2 ? lane_reduce_sq8<true>(q, x, dim) : lane_reduce_sq8<false>(q, x, dim);
+  else if (order >= 2)
+    s = l2 ? lane_reduce_seq<true, false>(q, x, dim) : lane_reduce_seq<false, false>(q, x, dim);
+  else
+    s = l2 ? lane_reduce_avx2<true>(q, x, dim) : lane_reduce_avx2<false>(q, x, dim);
+  if (l2) return s;
+  return (kind & kKindNegIp) ? -s : __fsub_rn(1.0f, s);
 }
 
 // One warp per query, for the tensor-core screen's group candidates (kk <= 32 groups per unit,
-// k <= kk). Each unit's list is sorted by (value, group), so the rank of a candidate in the union
-// is the sum over lists of how many entries precede it there (a binary search each): ranks below
-// kk select the kk best groups and rank kk - 1 gives T. The groups' admitted rows (8 * kk at most)
-// are then recomputed exactly, one row per lane, and the k best are picked by k rounds of a warp
-// minimum over (distance, row). Same results and certificate as flat_finalize_kernel.
+// k <= kk). Each unit's list is sorted by (value, group). With few lists the rank of a candidate
+// in the union is the sum over lists of how many entries precede it there (a binary search each);
+// with more, a k-way merge takes the warp's minimum over the lists' heads kk times. Either way
+// the kk best groups are selected and the kk-th gives T. The groups' admitted rows (8 * kk at
+// most) are then recomputed exactly in batches, one row per lane, and the k best are picked by k
+// rounds of a warp minimum over (distance, row). Same results and certificate as
+// flat_finalize_kernel.
 constexpr int kGroupFinalizeWarps = 4;
+constexpr int kRankMergeChunks = 3;
 
 // Shared memory of one warp of flat_finalize_groups_kernel (the layout the kernel carves).
 __host__ __device__ inline size_t group_finalize_bytes_per_warp(int dpad, int n_chunks, int kk,
@@ -592,12 +638,12 @@ __host__ __device__ inline size_t group_finalize_bytes_per_warp(int dpad, int n_
   return (bytes + 15) / 16 * 16;
 }
 
-__global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_groups_kernel(
+__global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 6) flat_finalize_groups_kernel(
     const float* __restrict__ qp, int dpad, const float* __restrict__ eps_q, int nq,
     const float* __restrict__ x, int dim, int64_t nrows, const uint64_t* __restrict__ bitmap,
-    const uint64_t* __restrict__ labels, uint64_t row_offset, bool l2, bool sq8,
+    const uint64_t* __restrict__ labels, uint64_t row_offset, bool l2, int kind,
     const float* __restrict__ cand_d, const uint32_t* __restrict__ cand_r,
-    const int* __restrict__ cand_n, int n_chunks, int kk, int group_rows, int k,
+    const int* __restrict__ cand_n, int n_chunks, int kk, int group_rows, int k, bool rank_merge,
     uint64_t* __restrict__ out_labels, float* __restrict__ out_d, uint64_t* __restrict__ out_keys,
     const int* __restrict__ qbad, const int* __restrict__ screen_err,
     int* __restrict__ fail_count, int* __restrict__ fail_q, float* __restrict__ fail_dk,
@@ -643,10 +689,42 @@ __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_gro
     }
   }
   __syncwarp();
-  // k-way merge of the sorted unit lists: each round, the warp's minimum over the lists' heads
-  // (lane l watches lists l and l + 32) is the next best candidate.
   const int m = min(total, kk);
   float T = kInf;
+  if (rank_merge) {
+    // Few lists: each entry's rank in the union is its index in its own list plus, for every
+    // other list, the number of entries there that precede it by (value, group) (a binary search;
+    // groups are distinct across lists, so ranks are distinct). Ranks below kk are the kk best.
+    for (int i = lane; i < nl; i += 32) {
+      const int c = i / kk, j = i - c * kk;
+      if (j >= ln[c]) continue;
+      const float d = ld[i];
+      const uint32_t g = lr[i];
+      int rank = j;
+      for (int c2 = 0; c2 < n_chunks && rank < m; ++c2) {
+        if (c2 == c) continue;
+        const float* L = ld + c2 * kk;
+        const uint32_t* R = lr + c2 * kk;
+        int lo = 0, hi = ln[c2];
+        while (lo < hi) {
+          const int mid = (lo + hi) >> 1;
+          if (dev::key_less(L[mid], R[mid], d, g))
+            lo = mid + 1;
+          else
+            hi = mid;
+        }
+        rank += lo;
+      }
+      if (rank < m) {
+        sel[rank] = g;
+        sv[rank] = d;
+      }
+    }
+    __syncwarp();
+    if (m == kk) T = sv[kk - 1];
+  } else {
+  // k-way merge of the sorted unit lists: each round, the warp's minimum over the lists' heads
+  // (lane l watches lists l and l + 32) is the next best candidate.
   int h0 = 0, h1 = 0;
   const int c0 = lane, c1 = lane + 32;
   for (int r = 0; r < m; ++r) {
@@ -687,66 +765,75 @@ __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_gro
     h1 += bl == c1 ? 1 : 0;
   }
   __syncwarp();
+  }
   // Exact distances of the selected groups' admitted rows, one row per lane.
   auto exact_rows = [&](int g0, int g1) {
     for (int i = g0 * group_rows + lane; i < g1 * group_rows; i += 32) {
       const int g = i / group_rows, j = i - g * group_rows;
       const uint64_t row = static_cast<uint64_t>(sel[g]) * group_rows + j;
       const bool in = row < static_cast<uint64_t>(nrows) && dev::bitmap_test(bitmap, row);
-      ed[i] = in ? dev::nan_to_inf(lane_exact_distance(sq, x + row * dim, dim, l2, sq8)) : kInf;
+      ed[i] = in ? dev::nan_to_inf(lane_exact_distance(sq, x + row * dim, dim, l2, kind)) : kInf;
       er[i] = in ? row : ~0ull;
     }
     __syncwarp();
   };
   // Groups come in ascending screen value, and every row of group g has an exact distance of at
-  // least sv[g] - eps. So the first kFirstGroups groups are expanded, the k-th best exact distance
-  // dk1 among them is found, and the remaining groups are expanded only when the first of them
-  // could still hold a row at or below dk1; otherwise none of their rows can enter the top k
-  // (their exact distances all exceed dk1 >= the final k-th distance).
-  constexpr int kFirstGroups = 16;
+  // least sv[g] - eps. So the groups are expanded in batches: after each, the k-th best exact
+  // distance dk among the expanded rows is found, and the next group is expanded only when it
+  // could still hold a row at or below dk; otherwise none of the remaining groups' rows can enter
+  // the top k (their exact distances all exceed dk >= the final k-th distance). The first batch
+  // holds one group for k <= 2 (the best group usually holds the answer), else about 2k groups
+  // (at least 4, at most 16); later batches 8.
   int ng = m;
-  if (group_rows > 1 && m > kFirstGroups && k <= 32) {  // lane r keeps round r's winner
-    exact_rows(0, kFirstGroups);
-    // k-th smallest (distance, row) among them: k rounds of a warp minimum with removal, then
-    // the removed entries are put back.
-    float win_d = kInf, dk1 = kInf;
-    int win_i = -1;
-    for (int r = 0; r < k; ++r) {
-      float bd = kInf;
-      uint64_t br = ~0ull;
-      int bi = -1;
-      for (int i = lane; i < kFirstGroups * group_rows; i += 32) {
-        if (dev::key_less(ed[i], er[i], bd, br)) {
-          bd = ed[i];
-          br = er[i];
-          bi = i;
+  const int first = k <= 2 ? 1 : min(16, max(4, (2 * k + 3) / 4 * 4));
+  if (group_rows > 1 && m > first && k <= 32) {
+    exact_rows(0, first);
+    ng = first;
+    // k-th smallest (distance, row) among the expanded rows: k rounds of a warp minimum with
+    // removal (lane r keeps round r's winner), then the removed entries are put back.
+    auto kth_best = [&]() {
+      float win_d = kInf, kth = kInf;
+      int win_i = -1;
+      for (int r = 0; r < k; ++r) {
+        float bd = kInf;
+        uint64_t br = ~0ull;
+        int bi = -1;
+        for (int i = lane; i < ng * group_rows; i += 32) {
+          if (dev::key_less(ed[i], er[i], bd, br)) {
+            bd = ed[i];
+            br = er[i];
+            bi = i;
+          }
         }
-      }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float od = __shfl_xor_sync(kFull, bd, o);
-        const uint64_t orow = __shfl_xor_sync(kFull, br, o);
-        const int oi = __shfl_xor_sync(kFull, bi, o);
-        if (dev::key_less(od, orow, bd, br)) {
-          bd = od;
-          br = orow;
-          bi = oi;
+        for (int o = 16; o > 0; o >>= 1) {
+          const float od = __shfl_xor_sync(kFull, bd, o);
+          const uint64_t orow = __shfl_xor_sync(kFull, br, o);
+          const int oi = __shfl_xor_sync(kFull, bi, o);
+          if (dev::key_less(od, orow, bd, br)) {
+            bd = od;
+            br = orow;
+            bi = oi;
+          }
         }
+        if (lane == r) {
+          win_d = bd;
+          win_i = bi;
+        }
+        if (lane == 0 && bi >= 0) ed[bi] = kInf;
+        if (r == k - 1) kth = bd;
+        __syncwarp();
       }
-      if (lane == r) {
-        win_d = bd;
-        win_i = bi;
-      }
-      if (lane == 0 && bi >= 0) ed[bi] = kInf;
-      if (r == k - 1) dk1 = bd;
+      if (lane < k && win_i >= 0) ed[win_i] = win_d;
       __syncwarp();
-    }
-    if (lane < k && win_i >= 0) ed[win_i] = win_d;
-    __syncwarp();
-    if (dk1 < kInf && sv[kFirstGroups] - eps_q[q] > dk1) {
-      ng = kFirstGroups;
-    } else {
-      exact_rows(kFirstGroups, m);
+      return kth;
+    };
+    while (ng < m) {
+      const float dk1 = kth_best();
+      if (dk1 < kInf && sv[ng] - eps_q[q] > dk1) break;
+      const int next = min(m, ng + 8);
+      exact_rows(ng, next);
+      ng = next;
     }
   } else {
     exact_rows(0, m);
@@ -807,7 +894,7 @@ __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 4) flat_finalize_gro
 __global__ void __launch_bounds__(256) flat_rescan_kernel(
     const float* __restrict__ qp, int dpad, const float* __restrict__ x, int dim, int64_t nrows,
     const uint64_t* __restrict__ labels, const uint64_t* __restrict__ bitmap, uint64_t row_offset,
-    bool l2, bool sq8, int k, int cap, const int* __restrict__ fail_count, const int* __restrict__ fail_q,
+    bool l2, int kind, int k, int cap, const int* __restrict__ fail_count, const int* __restrict__ fail_q,
     const float* __restrict__ fail_dk, uint64_t* __restrict__ out_labels,
     float* __restrict__ out_d, uint64_t* __restrict__ out_keys) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -835,7 +922,7 @@ __global__ void __launch_bounds__(256) flat_rescan_kernel(
         if (row >= nrows) break;
         if (!dev::bitmap_test(bitmap, static_cast<uint64_t>(row))) continue;
         const float e =
-            dev::nan_to_inf(dev::warp_exact_distance(qrow, x + row * dim, dim, l2, lane, sq8));
+            dev::nan_to_inf(dev::warp_exact_distance_kind(qrow, x + row * dim, dim, l2, lane, kind));
         if (lane == 0 && e <= thr) {
           const int slot = atomicAdd(&s_cnt, 1);
           bd[slot] = e;
@@ -985,7 +1072,7 @@ static int choose_chunks(size_t nrows, int n_qtiles, int max_chunks, int grid, i
   const int limit = static_cast<int>(std::min<size_t>(max_chunks, ceil_div(nrows, align)));
   int best = 1;
   double best_eff = -1.0;
-  for (int c = std::max(1, limit / 2); c <= limit; ++c) {
+  for (int c = 1; c <= limit; ++c) {
     const double units = static_cast<double>(c) * n_qtiles;
     const double waves = std::ceil(units / grid);
     const double eff = units / (waves * grid);
@@ -1088,7 +1175,7 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
                        cudaStream_t st) {
   const int dim = P.dim, dpad = P.dpad, kk = P.kk;
   const bool l2 = s.metric == QV_METRIC_L2;
-  const bool sq8 = s.sum_order == kSumOrderSq8;
+  const int kind = static_cast<int>(s.sum_order) | (s.neg_ip ? kKindNegIp : 0);
   const int nsm = sm_count(s.device);
   float* qp = reinterpret_cast<float*>(base + P.qp);
   float* qn2 = reinterpret_cast<float*>(base + P.qn2);
@@ -1115,7 +1202,8 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
   em.c_ip = static_cast<float>(2.0 * (2.0 * gamma));
   em.c_abs = static_cast<float>(2.0 * (2.0 * u));
   prep_queries_kernel<<<ceil_div(nq, 8), 256, 0, st>>>(d_queries, nq, dim, dpad,
-                                                       s.metric == QV_METRIC_COSINE, l2, em,
+                                                       s.metric == QV_METRIC_COSINE, l2,
+                                                       s.drop_qnorm, em,
                                                        s.max_norm, qp, qn2, eps, qbad,
                                                        d_flags + kFlagNonFinite);
   check_launch("prep_queries_kernel");
@@ -1139,7 +1227,7 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
     kernel<<<grid, 128, smem, st>>>(qp, dpad, qn2, static_cast<int>(nq), P.qpb, s.x.get<float>(),
                                     dim, s.xnorm2.get<float>(), static_cast<int64_t>(s.n),
                                     d_bitmap, P.chunk_rows, P.n_qtiles, P.n_chunks, kk, cand_d,
-                                    cand_r, cand_n, thr);
+                                    cand_r, cand_n, thr, s.neg_ip ? 0.0f : 1.0f);
     timer.stop();
     check_launch("flat_screen_simt_kernel");
   }
@@ -1147,6 +1235,11 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
   if (P.tensor) {
     // The tensor-core screen keeps 8-row groups; the finalize expands the kk best into rows.
     QV_REQUIRE(P.n_chunks <= 64, "group finalize: more than 64 row chunks");
+    // Up to kRankMergeChunks unit lists per query are merged by ranks, more by rounds of a warp
+    // minimum (QV_FINALIZE_MERGE=rounds: always by rounds; both select the same groups).
+    const char* merge_env = std::getenv("QV_FINALIZE_MERGE");
+    const bool rank_merge = P.n_chunks <= kRankMergeChunks &&
+                            !(merge_env != nullptr && std::strcmp(merge_env, "rounds") == 0);
     const size_t gsmem =
         kGroupFinalizeWarps * group_finalize_bytes_per_warp(dpad, P.n_chunks, kk, P.group_rows);
     QV_CUDA(cudaFuncSetAttribute(flat_finalize_groups_kernel,
@@ -1154,8 +1247,9 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
     flat_finalize_groups_kernel<<<static_cast<unsigned>(ceil_div(nq, kGroupFinalizeWarps)),
                                   32 * kGroupFinalizeWarps, gsmem, st>>>(
         qp, dpad, eps, static_cast<int>(nq), s.x.get<float>(), dim, static_cast<int64_t>(s.n),
-        d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, sq8, cand_d, cand_r, cand_n,
-        P.n_chunks, kk, P.group_rows, static_cast<int>(k), d_labels, d_dists, d_keys, qbad, screen_err,
+        d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, kind, cand_d, cand_r, cand_n,
+        P.n_chunks, kk, P.group_rows, static_cast<int>(k), rank_merge, d_labels, d_dists, d_keys,
+        qbad, screen_err,
         fail_count, fail_q, fail_dk, d_flags);
     check_launch("flat_finalize_groups_kernel");
   } else {
@@ -1165,7 +1259,7 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
                                  (int)fsmem));
     flat_finalize_kernel<<<static_cast<unsigned>(nq), kFinalizeThreads, fsmem, st>>>(
         qp, dpad, eps, static_cast<int>(nq), s.x.get<float>(), dim, static_cast<int64_t>(s.n),
-        d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, sq8, cand_d, cand_r, cand_n,
+        d_bitmap, s.labels.get<uint64_t>(), s.row_offset, l2, kind, cand_d, cand_r, cand_n,
         P.n_chunks, kk, 1, pool, static_cast<int>(k), d_labels, d_dists, d_keys, qbad, fail_count, fail_q,
         fail_dk, d_flags);
     check_launch("flat_finalize_kernel");
@@ -1177,7 +1271,7 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
                                (int)rsmem));
   flat_rescan_kernel<<<static_cast<unsigned>(std::min<size_t>(nq, 2 * nsm)), 256, rsmem, st>>>(
       qp, dpad, s.x.get<float>(), dim, static_cast<int64_t>(s.n), s.labels.get<uint64_t>(),
-      d_bitmap, s.row_offset, l2, sq8, static_cast<int>(k), cap, fail_count, fail_q, fail_dk, d_labels,
+      d_bitmap, s.row_offset, l2, kind, static_cast<int>(k), cap, fail_count, fail_q, fail_dk, d_labels,
       d_dists, d_keys);
   check_launch("flat_rescan_kernel");
 }

@@ -83,6 +83,7 @@ struct Args {
   long long wait_cycles;  // bound of every mbarrier wait (SM clock cycles)
   uint64_t drain_ns;      // bound of the abort path's waits for work in flight (global timer)
   int skip_fill;          // failure-detection test hook: CTA 0 skips this ring fill (-1: none)
+  float ip_one;           // inner-product screen values are ip_one - <q,x> (1, or 0 for -<q,x>)
   // Threshold seeding launch: units only publish their lists' kKK-th values as the queries'
   // thresholds (no candidate lists, no running best-list merge).
   bool seed_only;
@@ -510,13 +511,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // candidate list as one entry: its best screen value and its index (rows 8 * index ..
       // 8 * index + 7); the exact re-rank expands it.
       auto screen = [&](const float (&best)[8], float top, int64_t cb) {
-        const bool may = active && screen_value<kL2>(top, inv) <= thr;
+        const bool may = active && screen_value<kL2>(top, inv, a.ip_one) <= thr;
         if (!__any_sync(0xffffffffu, may)) return;
         static_assert(kTcGroupRows == 8, "the group tree is built for 8-row groups");
         uint32_t gm = 0;
 #pragma unroll
         for (int g = 0; g < 8; ++g)
-          gm |= (may && screen_value<kL2>(best[g], inv) <= thr) ? (1u << g) : 0u;
+          gm |= (may && screen_value<kL2>(best[g], inv, a.ip_one) <= thr) ? (1u << g) : 0u;
         // Make room first (all lanes together) when some lane's appends would overflow its
         // list; compaction tightens the threshold, so the groups are tested again.
         if (__any_sync(0xffffffffu, cnt + __popc(gm) > kCap)) {
@@ -527,7 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t keep = 0;
 #pragma unroll
           for (int g = 0; g < 8; ++g)
-            keep |= (screen_value<kL2>(best[g], inv) <= thr) ? (1u << g) : 0u;
+            keep |= (screen_value<kL2>(best[g], inv, a.ip_one) <= thr) ? (1u << g) : 0u;
           gm &= keep;
         }
         // At most 8 appends and kAppend >= 8 free entries: no further checks. Each entry's
@@ -537,7 +538,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int g = 0; g < 8; ++g) {
           if ((gm >> g) & 1u) {
             const int pos = cnt + __popc(gm & ((1u << g) - 1u));
-            bd[pos * kLS] = screen_value<kL2>(best[g], inv);
+            bd[pos * kLS] = screen_value<kL2>(best[g], inv, a.ip_one);
             br[pos * kLS] = static_cast<uint32_t>(cb / kTcGroupRows + g);
           }
         }
@@ -724,7 +725,7 @@ __global__ void max_abs_kernel(const float* __restrict__ x, size_t total, unsign
 // words (max |x|, max row error).
 __global__ void queries_to_f16_kernel(const float* __restrict__ qp, int nq, int nq_pad, int dim,
                                       int dpad, int kpad, const unsigned* __restrict__ x_stats,
-                                      float x_max_norm, bool l2, float gamma,
+                                      float x_max_norm, bool l2, bool drop_qnorm, float gamma,
                                       __half* __restrict__ q16, float* __restrict__ qscale_inv,
                                       float* __restrict__ qnorm2, float* __restrict__ eps) {
   const int lane = threadIdx.x & 31;
@@ -771,7 +772,7 @@ __global__ void queries_to_f16_kernel(const float* __restrict__ qp, int nq, int 
     }
     eps[q] = static_cast<float>(e * 1.01 + 1e-30);
     qscale_inv[q] = 1.0f / (s * x_scale);
-    qnorm2[q] = static_cast<float>(n2);
+    qnorm2[q] = drop_qnorm ? 0.0f : static_cast<float>(n2);
   }
 }
 
@@ -970,7 +971,8 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq, si
   const double gamma = (kpad + 2) * std::ldexp(1.0, -23);
   tc::queries_to_f16_kernel<<<ceil_div(nq_pad, 8), 256, 0, st>>>(
       qp, static_cast<int>(nq), static_cast<int>(nq_pad), static_cast<int>(s.dim), dpad, kpad,
-      s.x16_stats.get<unsigned>(), s.max_norm, l2, static_cast<float>(gamma), q16, qinv, qn2, eps);
+      s.x16_stats.get<unsigned>(), s.max_norm, l2, s.drop_qnorm, static_cast<float>(gamma), q16,
+      qinv, qn2, eps);
   check_launch("queries_to_f16_kernel");
   if (wide) {
     const CUtensorMap mq = tc::make_map(q16, nq_pad, kpad);
@@ -1014,6 +1016,7 @@ void flat_screen_tc(const FlatState& s, const float* qp, int dpad, size_t nq, si
   a.wait_cycles = tc::wait_limit_cycles();
   a.drain_ns = tc::drain_limit_ns();
   a.skip_fill = tc::test_skip_fill();
+  a.ip_one = s.neg_ip ? 0.0f : 1.0f;
   a.seed_only = false;
   const int atoms = kpad > tc::kAtomK ? 2 : 1;
   const int max_workers = flat_tc_workers(s, k);

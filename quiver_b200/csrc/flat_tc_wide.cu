@@ -69,6 +69,7 @@ struct Args {
   long long wait_cycles;
   uint64_t drain_ns;
   int skip_fill;            // failure-detection test hook: CTA 0 skips this ring fill (-1: none)
+  float ip_one;             // inner-product screen values are ip_one - <q,x> (1, or 0 for -<q,x>)
 };
 
 // Sorts 16 (distance, group) entries ascending in registers (bitonic network).
@@ -524,26 +525,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
       auto screen = [&](const float (&best)[8], float top, int64_t cb) {
-        const bool may = active && screen_value<kL2>(top, inv) <= thr;
+        const bool may = active && screen_value<kL2>(top, inv, a.ip_one) <= thr;
         if (!__any_sync(0xffffffffu, may)) return;
         uint32_t gm = 0;
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          gm |= (may && screen_value<kL2>(best[j], inv) <= thr) ? (1u << j) : 0u;
+          gm |= (may && screen_value<kL2>(best[j], inv, a.ip_one) <= thr) ? (1u << j) : 0u;
         if (__any_sync(0xffffffffu, cnt + __popc(gm) > cap)) {
           compact_wide(ld, lr, kk, cnt, thr);
           if (active) atomicMin(a.thr_bits + q, dev::ordered_bits(thr));
           uint32_t keep = 0;
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            keep |= (screen_value<kL2>(best[j], inv) <= thr) ? (1u << j) : 0u;
+            keep |= (screen_value<kL2>(best[j], inv, a.ip_one) <= thr) ? (1u << j) : 0u;
           gm &= keep;
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           if ((gm >> j) & 1u) {
             const int pos = cnt + __popc(gm & ((1u << j) - 1u));
-            ld[pos * kLS] = screen_value<kL2>(best[j], inv);
+            ld[pos * kLS] = screen_value<kL2>(best[j], inv, a.ip_one);
             lr[pos * kLS] = static_cast<uint32_t>(cb / kTcGroupRows + j);
           }
         }
@@ -673,6 +674,7 @@ void flat_screen_tc_wide(const FlatState& s, const float* qp, int dpad, size_t n
   a.wait_cycles = tc::wait_limit_cycles();
   a.drain_ns = tc::drain_limit_ns();
   a.skip_fill = tc::test_skip_fill();
+  a.ip_one = s.neg_ip ? 0.0f : 1.0f;
   a.a_tmem_atoms = std::min(atoms, tcw::kTmemAtoms);
   a.kpad = kpad;
   a.q16 = q16;

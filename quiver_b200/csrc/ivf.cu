@@ -11,7 +11,9 @@
 // reference leaves both unspecified.
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <vector>
 
 #include "qv_state.h"
@@ -791,6 +793,72 @@ struct Prepared {
   int nprobe = 1;
 };
 
+// Centroid tables: k centroids (device rows) as Flat rows labelled 0..k-1, scored with
+// CentroidTable's arithmetic, so that an exact Flat search of a table (tensor-core screen, exact
+// re-rank in that arithmetic, certificate) returns what CentroidTable's full scan returns:
+//   kProbeL2  sum_j (q_j - c_j)^2, sequential (CentroidTable::l2: the L2 coarse probe);
+//   kNegIp    -(sum_j q_j c_j), sequential (CentroidTable::dot: the IP and cosine probes, and the
+//             inner-product assignment);
+//   kAssignL2 ||c||^2 - 2<x,c>, both sequential (CentroidTable::nearest_batch: the L2 and cosine
+//             assignment), its screens leaving out the constant ||x||^2.
+enum class TableKind { kProbeL2, kNegIp, kAssignL2 };
+std::unique_ptr<FlatState> centroid_table(const float* d_cents, size_t k, size_t dim, int device,
+                                          TableKind kind, cudaStream_t st) {
+  auto t = std::make_unique<FlatState>();
+  t->device = device;
+  t->dim = dim;
+  t->metric = kind == TableKind::kNegIp ? QV_METRIC_IP : QV_METRIC_L2;
+  t->sum_order = kind == TableKind::kAssignL2 ? kSumOrderNormDot : kSumOrderSeq;
+  t->neg_ip = kind == TableKind::kNegIp;
+  t->drop_qnorm = kind == TableKind::kAssignL2;
+  DeviceBuffer ids(k * sizeof(uint64_t), st);
+  sequential_labels(ids.get<uint64_t>(), k, 0, st);
+  flat_append(*t, d_cents, ids.get<uint64_t>(), k, st, /*normalize=*/false);  // waits on st
+  return t;
+}
+
+// Probe lists from a centroid table's Flat search: labels are list ids. A query without results
+// (one holding NaN or infinity, which the host entry points reject before searching) gets lists
+// 0..k-1, as the selection over its all-NaN distances would.
+__global__ void probes_from_labels_kernel(const uint64_t* __restrict__ labels, size_t total,
+                                          int k, size_t nlist, uint32_t* __restrict__ probes) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const uint64_t l = labels[i];
+    probes[i] = static_cast<uint32_t>(l < nlist ? l : i % static_cast<size_t>(k));
+  }
+}
+
+// A centroid table is searched on the tensor cores where that screen applies and k stays within
+// its narrow best lists; QV_IVF_COARSE=simt keeps the float32 CUDA-core kernels (distance table
+// plus radix selection for the probe, the register-tiled scan for the assignment) everywhere.
+// Both give the same lists and distances: the same sums, ordered by (distance, list id).
+constexpr size_t kTableMaxK = 24;
+constexpr size_t kTableMinRows = 128;
+bool table_on_tensor_cores(const FlatState* t, size_t k) {
+  if (t == nullptr || t->n < kTableMinRows || k > kTableMaxK) return false;
+  const char* e = std::getenv("QV_IVF_COARSE");
+  if (e != nullptr && std::strcmp(e, "simt") == 0) return false;
+  return flat_tc_eligible(*t, k) && !flat_tc_is_wide(*t, k);
+}
+
+// The k nearest table rows of n device rows: ids (n x k, u32) and, when d_dist is not null, their
+// distances.
+void table_nearest(const FlatState& t, const float* d_x, size_t n, size_t k, uint32_t* d_ids,
+                   float* d_dist, cudaStream_t st) {
+  const size_t total = n * k;
+  DeviceBuffer labels(total * sizeof(uint64_t), st);
+  DeviceBuffer dist(d_dist == nullptr ? total * sizeof(float) : 0, st);
+  DeviceBuffer flags(kSearchFlagWords * sizeof(int), st);
+  QV_CUDA(cudaMemsetAsync(flags.get(), 0, kSearchFlagWords * sizeof(int), st));
+  flat_search(t, d_x, n, k, nullptr, labels.get<uint64_t>(),
+              d_dist != nullptr ? d_dist : dist.get<float>(), nullptr, flags.get<int>(), st);
+  probes_from_labels_kernel<<<static_cast<unsigned>(std::min<size_t>(ceil_div(total, 256), 4096)),
+                              256, 0, st>>>(labels.get<uint64_t>(), total, static_cast<int>(k),
+                                            t.n, d_ids);
+  check_launch("probes_from_labels_kernel");
+}
+
 Prepared prepare_search(const IvfState& s, const float* d_queries, size_t nq, size_t nprobe,
                         cudaStream_t st) {
   Prepared p;
@@ -800,6 +868,13 @@ Prepared prepare_search(const IvfState& s, const float* d_queries, size_t nq, si
       d_queries, nq * s.dim, p.qn.get<float>());
   check_launch("copy_queries_kernel");
   if (s.metric == QV_METRIC_COSINE) normalize_rows_device(p.qn.get<float>(), nq, s.dim, st);
+  p.probes.allocate(nq * p.nprobe * sizeof(uint32_t), st);
+  p.probe_d.allocate(nq * p.nprobe * sizeof(float), st);
+  if (table_on_tensor_cores(s.coarse_table.get(), static_cast<size_t>(p.nprobe))) {
+    table_nearest(*s.coarse_table, p.qn.get<float>(), nq, static_cast<size_t>(p.nprobe),
+                  p.probes.get<uint32_t>(), p.probe_d.get<float>(), st);
+    return p;
+  }
   p.coarse.allocate(nq * s.nlist * sizeof(float), st);
   dim3 grid(static_cast<unsigned>(ceil_div(nq, kTileP4)),
             static_cast<unsigned>(ceil_div(s.nlist, kTileC4)));
@@ -808,8 +883,6 @@ Prepared prepare_search(const IvfState& s, const float* d_queries, size_t nq, si
                                             p.coarse.get<float>());
   check_launch("coarse_dist_kernel4");
   const int pool = static_cast<int>(next_pow2(s.nlist));
-  p.probes.allocate(nq * p.nprobe * sizeof(uint32_t), st);
-  p.probe_d.allocate(nq * p.nprobe * sizeof(float), st);
   if (p.nprobe <= kRadixProbeMax) {
     int id_passes = 1;
     while (id_passes < 4 && (s.nlist - 1) >> (8 * id_passes) != 0) ++id_passes;
@@ -944,6 +1017,13 @@ void ivf_set_trained(IvfState& s, const float* h_centroids, const float* h_codeb
         static_cast<int>(s.dsub), s.precomputed.get<float>());
     check_launch("precompute_kernel");
   }
+  // The centroid tables of the coarse probe and of add()'s assignment.
+  s.coarse_table = centroid_table(s.centroids.get<float>(), s.nlist, s.dim, s.device,
+                                  s.ip() ? TableKind::kNegIp : TableKind::kProbeL2, st);
+  s.l2_assign_table.reset();
+  if (s.metric != QV_METRIC_IP)
+    s.l2_assign_table = centroid_table(s.centroids.get<float>(), s.nlist, s.dim, s.device,
+                                       TableKind::kAssignL2, st);
   QV_CUDA(cudaStreamSynchronize(st));
   s.trained = true;
 }
@@ -952,6 +1032,16 @@ void nearest_centroids_device(const float* d_x, size_t n, const float* d_cents, 
                               size_t dim, bool by_ip, float* d_cnorm2, uint32_t* d_assign,
                               cudaStream_t st) {
   if (n == 0) return;
+  if (k >= kTableMinRows) {
+    int device = 0;
+    QV_CUDA(cudaGetDevice(&device));
+    const std::unique_ptr<FlatState> t = centroid_table(
+        d_cents, k, dim, device, by_ip ? TableKind::kNegIp : TableKind::kAssignL2, st);
+    if (table_on_tensor_cores(t.get(), 1)) {
+      table_nearest(*t, d_x, n, 1, d_assign, nullptr, st);
+      return;
+    }
+  }
   centroid_norms_kernel<<<ceil_div(k, 256), 256, 0, st>>>(d_cents, k, static_cast<int>(dim),
                                                           d_cnorm2);
   check_launch("centroid_norms_kernel");
@@ -964,10 +1054,15 @@ void nearest_centroids_device(const float* d_x, size_t n, const float* d_cents, 
 void ivf_encode_device(const IvfState& s, const float* d_x, size_t n, uint32_t* d_assign,
                        uint8_t* d_codes, cudaStream_t st) {
   if (n == 0) return;
-  coarse_assign_kernel4<<<ceil_div(n, kTileP4), 256, 0, st>>>(
-      d_x, n, s.centroids.get<float>(), s.cnorm2.get<float>(), s.nlist, static_cast<int>(s.dim),
-      s.metric == QV_METRIC_IP, d_assign);  // assign_by_ip (src/ivfpq_index.cc:107)
-  check_launch("coarse_assign_kernel4");
+  // assign_by_ip for the inner-product metric (src/ivfpq_index.cc:107)
+  if (table_on_tensor_cores(s.assign_table(), 1)) {
+    table_nearest(*s.assign_table(), d_x, n, 1, d_assign, nullptr, st);
+  } else {
+    coarse_assign_kernel4<<<ceil_div(n, kTileP4), 256, 0, st>>>(
+        d_x, n, s.centroids.get<float>(), s.cnorm2.get<float>(), s.nlist,
+        static_cast<int>(s.dim), s.metric == QV_METRIC_IP, d_assign);
+    check_launch("coarse_assign_kernel4");
+  }
   DeviceBuffer resid(n * s.dim * sizeof(float), st);
   residual_kernel<<<ceil_div(n * s.dim, 256), 256, 0, st>>>(
       d_x, n, static_cast<int>(s.dim), s.centroids.get<float>(), d_assign, resid.get<float>());

@@ -447,14 +447,60 @@ __device__ __forceinline__ float warp_exact_distance_sq8(const float* q, const f
   return __fsub_rn(1.0f, warp_reduce_sq8<false>(q, x, dim, lane));
 }
 
-// warp_exact_distance for four rows at once (see warp_reduce_avx2_x4); sq8 selects the SQ8
-// kernels' order (rows are then decoded SQ8 codes).
+// CentroidTable::l2 / ::dot (src/internal/centroid_table.h:65-85): one sequential sum from 0.0f,
+// every multiply and add rounded on its own. Every lane computes the same sum.
+template <bool kDiff>
+__device__ __forceinline__ float seq_reduce(const float* __restrict__ a, const float* __restrict__ b,
+                                            int dim) {
+  float s = 0.0f;
+  for (int i = 0; i < dim; ++i) {
+    float u = a[i], v = b[i];
+    if (kDiff) {
+      u = __fsub_rn(u, v);
+      v = u;
+    }
+    s = __fadd_rn(s, __fmul_rn(u, v));
+  }
+  return s;
+}
+
+// CentroidTable::nearest_batch's distance (src/internal/centroid_table.h:94-144): ||x||^2 and
+// <q,x> as sequential, separately rounded sums, then ||x||^2 - 2<q,x> rounded once.
+__device__ __forceinline__ float seq_norm_minus_2dot(const float* __restrict__ q,
+                                                     const float* __restrict__ x, int dim) {
+  float dot = 0.0f, nn = 0.0f;
+  for (int i = 0; i < dim; ++i) {
+    const float v = x[i];
+    dot = __fadd_rn(dot, __fmul_rn(q[i], v));
+    nn = __fadd_rn(nn, __fmul_rn(v, v));
+  }
+  return __fsub_rn(nn, __fmul_rn(2.0f, dot));
+}
+
+// The exact distance of one row for an exact-distance kind (summation order | kKindNegIp).
+__device__ __forceinline__ float warp_exact_distance_kind(const float* q, const float* x, int dim,
+                                                          bool l2, int lane, int kind) {
+  const int order = kind & 3;
+  if (order == 1) return warp_exact_distance_sq8(q, x, dim, l2, lane);
+  if (order == 3 && l2) return seq_norm_minus_2dot(q, x, dim);
+  if (order >= 2) {
+    if (l2) return seq_reduce<true>(q, x, dim);
+    const float s = seq_reduce<false>(q, x, dim);
+    return (kind & 4) ? -s : __fsub_rn(1.0f, s);
+  }
+  if (l2) return warp_reduce_avx2<true>(q, x, dim, lane);
+  const float s = warp_reduce_avx2<false>(q, x, dim, lane);
+  return (kind & 4) ? -s : __fsub_rn(1.0f, s);
+}
+
+// warp_exact_distance for four rows at once (see warp_reduce_avx2_x4); kind as
+// warp_exact_distance_kind (the float32 kernels' order, 1 - <q,x>, by default).
 __device__ __forceinline__ void warp_exact_distance_x4(const float* q, const float* const (&x)[4],
                                                        int dim, bool l2, int lane,
-                                                       float (&out)[4], bool sq8 = false) {
-  if (sq8) {
+                                                       float (&out)[4], int kind = 0) {
+  if (kind != 0) {
 #pragma unroll
-    for (int r = 0; r < 4; ++r) out[r] = warp_exact_distance_sq8(q, x[r], dim, l2, lane);
+    for (int r = 0; r < 4; ++r) out[r] = warp_exact_distance_kind(q, x[r], dim, l2, lane, kind);
   } else if (l2) {
     warp_reduce_avx2_x4<true>(q, x, dim, lane, out);
   } else {
@@ -472,11 +518,9 @@ __device__ __forceinline__ float warp_l2sqr_avx2(const float* a, const float* b,
   return warp_reduce_avx2<true>(a, b, dim, lane);
 }
 
-// The reference's exact distance (src/flat_index.cc:87, src/ivfpq_index.cc:138-142); sq8: the SQ8
-// kernels' order on a decoded row (src/hnsw_index.cc:202-218).
+// The reference's exact distance (src/flat_index.cc:87, src/ivfpq_index.cc:138-142).
 __device__ __forceinline__ float warp_exact_distance(const float* q, const float* x, int dim,
-                                                     bool l2, int lane, bool sq8 = false) {
-  if (sq8) return warp_exact_distance_sq8(q, x, dim, l2, lane);
+                                                     bool l2, int lane) {
   if (l2) return warp_l2sqr_avx2(q, x, dim, lane);
   return __fsub_rn(1.0f, warp_dot_avx2(q, x, dim, lane));
 }

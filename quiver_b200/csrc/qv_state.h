@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <memory>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -18,14 +19,23 @@ namespace qv {
 // cosine), with their labels, a squared norm per row for the L2 screen, and a scaled fp16 copy
 // padded to at least 64 columns for the tensor-core screen.
 // Summation order of the exact distances of a FlatState's rows: the reference's float32 kernels
-// (FlatIndex), or its SQ8 kernels (an HNSW SQ8 store, whose rows are the decoded codes).
-enum : uint32_t { kSumOrderF32 = 0, kSumOrderSq8 = 1 };
+// (FlatIndex), its SQ8 kernels (an HNSW SQ8 store, whose rows are the decoded codes), or plain
+// sequential sums with every multiply and add rounded (CentroidTable::l2 / ::dot: the IVF-PQ
+// coarse probe over the centroids), or, for L2, ||x||^2 - 2<q,x> from two such sums
+// (CentroidTable::nearest_batch: the coarse assignment of rows to lists).
+enum : uint32_t { kSumOrderF32 = 0, kSumOrderSq8 = 1, kSumOrderSeq = 2, kSumOrderNormDot = 3 };
+// The exact-distance kind the re-rank kernels take: the summation order, plus kKindNegIp when an
+// inner-product distance is -<q,x> (the coarse probe's) instead of 1 - <q,x>.
+constexpr int kKindNegIp = 4;
 
 struct FlatState {
   int device = 0;
   size_t dim = 0;
   uint32_t metric = 0;
   uint32_t sum_order = kSumOrderF32;
+  bool neg_ip = false;  // inner-product distances are -<q,x> (screens score them the same way)
+  // L2 screens leave out ||q||^2 (distances are ||x||^2 - 2<q,x>, kSumOrderNormDot).
+  bool drop_qnorm = false;
   uint64_t row_offset = 0;
   size_t n = 0, cap = 0;
   DeviceBuffer x;         // cap x dim f32
@@ -165,6 +175,15 @@ struct IvfState {
   std::vector<uint32_t> host_global_base;
   std::vector<uint8_t> host_codes;
   std::vector<uint64_t> host_labels;
+  // The centroids as a Flat table (labels 0..nlist-1, CentroidTable's sequential summation,
+  // inner products scored -<q,c>): the coarse probe's tensor-core path searches it.
+  std::unique_ptr<FlatState> coarse_table;
+  // The same rows scored as add() assigns them (||c||^2 - 2<x,c>) for the L2 and cosine metrics;
+  // the inner-product metric assigns by -<x,c>, as coarse_table scores.
+  std::unique_ptr<FlatState> l2_assign_table;
+  const FlatState* assign_table() const {
+    return metric == QV_METRIC_IP ? coarse_table.get() : l2_assign_table.get();
+  }
   bool ip() const { return metric != 0; }
   bool use_precomputed() const { return precomputed.bytes() != 0; }
 };

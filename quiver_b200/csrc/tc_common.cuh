@@ -170,11 +170,12 @@ __device__ __forceinline__ void tmem_hold(uint32_t (&r)[64]) {
                : "memory");
 }
 // Screen distance of one accumulator element: for L2 the element already is the distance; for
-// cosine / inner product it is the raw (scaled) inner product and the distance is 1 - dot * inv.
+// cosine / inner product it is the raw (scaled) inner product and the distance is
+// one - dot * inv (one = 1, or 0 where inner-product distances are -<q,x>).
 // fmaf rounds once and is monotone in the element, so the best raw value gives the best distance.
 template <bool kL2>
-__device__ __forceinline__ float screen_value(float x, float inv) {
-  return kL2 ? x : fmaf(-x, inv, 1.0f);
+__device__ __forceinline__ float screen_value(float x, float inv, float one) {
+  return kL2 ? x : fmaf(-x, inv, one);
 }
 
 // Three-input max / min (one PTX instruction on sm_100a).

@@ -227,3 +227,50 @@ def test_train_bit_exact_against_reference(gpu, reference, tmp_path, metric, n, 
     l, d = ix.search(q, 10, nprobe=8, refine_factor=2)
     rl, rd = r.search(q, 10, 8, 2)
     assert_topk_parity(l, d, rl, rd, exact=True, what=f"trained {metric}")
+
+
+@pytest.mark.parametrize("metric", ["l2", "ip", "cosine"])
+def test_coarse_probe_paths_agree_with_ties(gpu, oracle, tmp_path, monkeypatch, metric):
+    """The coarse probe's two paths (the centroid table searched as an exact Flat index on the
+    tensor cores, and the float32 distance table with the radix selection, QV_IVF_COARSE=simt)
+    pick the same lists with the same distances, including among exactly tied centroids (each
+    centroid row appears four times, and some queries sit on a centroid): ties go to the lower
+    list id, as CentroidTable's stable selection does (src/ivfpq_index.cc:285-297). Both equal
+    the oracle."""
+    from oracle.oracle import QvrIvf
+    rng = np.random.default_rng(41)
+    dim, nlist, m = 32, 256, 8
+    distinct = rng.standard_normal((nlist // 4, dim)).astype(np.float32)
+    cents = distinct[rng.permutation(np.repeat(np.arange(nlist // 4), 4))]
+    books = rng.standard_normal((m, 256, dim // m)).astype(np.float32) * 0.3
+    base = (cents[rng.integers(0, nlist, 6000)] +
+            rng.standard_normal((6000, dim)).astype(np.float32) * 0.2)
+    q = np.concatenate([cents[rng.integers(0, nlist, 40)],
+                        rng.standard_normal((160, dim)).astype(np.float32)])
+    if metric == "cosine":  # centroids of a cosine index are trained on normalized rows
+        cents = cents / np.linalg.norm(cents, axis=1, keepdims=True)
+    ix = gpu.IvfPqIndex(dim, metric, nlist, m, store_vectors=True)
+    ix.set_trained(cents, books)
+    ix.add(base)
+    ix.save(tmp_path / "ties.qvr")
+    qv = QvrIvf(tmp_path / "ties.qvr")
+    for nprobe, rf in [(1, 0), (3, 0), (8, 2), (24, 0)]:
+        monkeypatch.delenv("QV_IVF_COARSE", raising=False)
+        tl, td = ix.search(q, 10, nprobe=nprobe, refine_factor=rf)
+        monkeypatch.setenv("QV_IVF_COARSE", "simt")
+        sl, sd = ix.search(q, 10, nprobe=nprobe, refine_factor=rf)
+        what = f"{metric} nprobe {nprobe} rf {rf}"
+        assert np.array_equal(tl, sl), what
+        assert np.array_equal(td.view(np.uint32), sd.view(np.uint32)), what
+        wl, wd = oracle.ivf_search(qv, q, 10, nprobe, rf)
+        assert_topk_parity(tl, td, wl, wd, exact=True, what="oracle " + what)
+    # add()'s assignment takes the same two paths (CentroidTable::nearest_batch: ||c||^2 - 2<x,c>,
+    # or -<x,c> for the inner-product metric); rows sitting on a centroid tie with its copies.
+    rows = np.concatenate([cents[rng.integers(0, nlist, 300)], base[:700]])
+    monkeypatch.delenv("QV_IVF_COARSE", raising=False)
+    ta, tc_codes = ix.encode(rows)
+    monkeypatch.setenv("QV_IVF_COARSE", "simt")
+    sa, s_codes = ix.encode(rows)
+    assert np.array_equal(ta, sa) and np.array_equal(tc_codes, s_codes)
+    # the index's lists (filled by add() on the default path) hold the same cells
+    assert np.array_equal(qv.assignments()[np.argsort(qv.labels)][:700], sa[300:])
