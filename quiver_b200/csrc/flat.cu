@@ -889,41 +889,48 @@ __global__ void __launch_bounds__(32 * kGroupFinalizeWarps, 6) flat_finalize_gro
 }
 
 // ---- exact rescan of uncertified queries -------------------------------------------------------------
-// Block-wide threshold buffer: rows whose exact distance is <= the running threshold are appended;
-// when the buffer might overflow it is sorted and cut to k, which tightens the threshold.
+// A query that fails the certificate is rescanned over every row, split into `slices` row ranges
+// taken by different blocks (one block alone would stream the rows at a single SM's bandwidth):
+// the grid walks the (failed query, slice) pairs. A block keeps a threshold buffer: rows whose
+// exact distance is <= the running threshold (first the k-th exact distance the finalize found,
+// an upper bound of the true one) are appended; when the buffer might overflow it is sorted and
+// cut to k, which tightens the threshold. One row per thread, exact distances in the row kind's
+// order (lane_exact_distance, the query staged in shared memory). With one slice the k best go
+// straight to the output; otherwise each slice's k best (sorted by (distance, row), padded with
+// (+inf, ~0)) go to sl_d / sl_r and flat_rescan_merge_kernel merges them.
 __global__ void __launch_bounds__(256) flat_rescan_kernel(
     const float* __restrict__ qp, int dpad, const float* __restrict__ x, int dim, int64_t nrows,
     const uint64_t* __restrict__ labels, const uint64_t* __restrict__ bitmap, uint64_t row_offset,
-    bool l2, int kind, int k, int cap, const int* __restrict__ fail_count, const int* __restrict__ fail_q,
-    const float* __restrict__ fail_dk, uint64_t* __restrict__ out_labels,
+    bool l2, int kind, int k, int cap, int slices, const int* __restrict__ fail_count,
+    const int* __restrict__ fail_q, const float* __restrict__ fail_dk,
+    float* __restrict__ sl_d, uint64_t* __restrict__ sl_r, uint64_t* __restrict__ out_labels,
     float* __restrict__ out_d, uint64_t* __restrict__ out_keys) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float* bd = reinterpret_cast<float*>(smem_raw);
+  float* sq = reinterpret_cast<float*>(smem_raw);  // dpad floats (16-byte multiple)
+  float* bd = sq + dpad;
   uint64_t* bk = reinterpret_cast<uint64_t*>(bd + cap);
   __shared__ int s_cnt;
   __shared__ float s_thr;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   const int nfail = *fail_count;
-  for (int f = blockIdx.x; f < nfail; f += gridDim.x) {
+  const int64_t pairs = static_cast<int64_t>(nfail) * slices;
+  for (int64_t p = blockIdx.x; p < pairs; p += gridDim.x) {
+    const int f = static_cast<int>(p / slices), sl = static_cast<int>(p - static_cast<int64_t>(f) * slices);
     const int q = fail_q[f];
-    const float* qrow = qp + static_cast<size_t>(q) * dpad;
+    const int64_t lo = nrows * sl / slices, hi = nrows * (sl + 1) / slices;
     __syncthreads();
+    for (int i = threadIdx.x; i < dpad; i += blockDim.x) sq[i] = qp[static_cast<size_t>(q) * dpad + i];
     if (threadIdx.x == 0) {
       s_cnt = 0;
       s_thr = fail_dk[f];
     }
     __syncthreads();
-    const int64_t per_round = static_cast<int64_t>(nwarps) * 32;
-    for (int64_t rb = 0; rb < nrows; rb += per_round) {
+    const int64_t per_round = blockDim.x;
+    for (int64_t rb = lo; rb < hi; rb += per_round) {
       const float thr = s_thr;
-      const int64_t w0 = rb + static_cast<int64_t>(warp) * 32;
-      for (int i = 0; i < 32; ++i) {
-        const int64_t row = w0 + i;
-        if (row >= nrows) break;
-        if (!dev::bitmap_test(bitmap, static_cast<uint64_t>(row))) continue;
-        const float e =
-            dev::nan_to_inf(dev::warp_exact_distance_kind(qrow, x + row * dim, dim, l2, lane, kind));
-        if (lane == 0 && e <= thr) {
+      const int64_t row = rb + threadIdx.x;
+      if (row < hi && dev::bitmap_test(bitmap, static_cast<uint64_t>(row))) {
+        const float e = dev::nan_to_inf(lane_exact_distance(sq, x + row * dim, dim, l2, kind));
+        if (e <= thr) {
           const int slot = atomicAdd(&s_cnt, 1);
           bd[slot] = e;
           bk[slot] = static_cast<uint64_t>(row);
@@ -949,9 +956,54 @@ __global__ void __launch_bounds__(256) flat_rescan_kernel(
     }
     dev::block_bitonic_sort<false>(bd, bk, nullptr, cap);
     const int m = min(s_cnt, k);
+    if (slices > 1) {
+      const size_t o = static_cast<size_t>(p) * k;
+      for (int j = threadIdx.x; j < k; j += blockDim.x) {
+        sl_d[o + j] = j < m ? bd[j] : kInf;
+        sl_r[o + j] = j < m ? bk[j] : ~0ull;
+      }
+      continue;
+    }
     for (int j = threadIdx.x; j < k; j += blockDim.x) {
       const size_t o = static_cast<size_t>(q) * k + j;
       if (j < m) {
+        out_d[o] = bd[j];
+        out_labels[o] = labels[bk[j]];
+        if (out_keys) out_keys[o] = row_offset + bk[j];
+      } else {
+        out_d[o] = kInf;
+        out_labels[o] = kInvalidLabel;
+        if (out_keys) out_keys[o] = ~0ull;
+      }
+    }
+  }
+}
+
+// The k best (distance, row) of a failed query's slices (slices * k entries, sorted per slice)
+// into the output; pool = next_pow2(slices * k).
+__global__ void __launch_bounds__(256) flat_rescan_merge_kernel(
+    const int* __restrict__ fail_count, const int* __restrict__ fail_q, int slices, int k,
+    int pool, const float* __restrict__ sl_d, const uint64_t* __restrict__ sl_r,
+    const uint64_t* __restrict__ labels, uint64_t row_offset, uint64_t* __restrict__ out_labels,
+    float* __restrict__ out_d, uint64_t* __restrict__ out_keys) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* bd = reinterpret_cast<float*>(smem_raw);
+  uint64_t* bk = reinterpret_cast<uint64_t*>(bd + pool);  // pool is a power of two >= 2
+  const int nfail = *fail_count;
+  const int n = slices * k;
+  for (int f = blockIdx.x; f < nfail; f += gridDim.x) {
+    const int q = fail_q[f];
+    __syncthreads();
+    for (int i = threadIdx.x; i < pool; i += blockDim.x) {
+      const size_t src = static_cast<size_t>(f) * n + i;
+      bd[i] = i < n ? sl_d[src] : kInf;
+      bk[i] = i < n ? sl_r[src] : ~0ull;
+    }
+    dev::block_bitonic_sort<false>(bd, bk, nullptr, pool);
+    __syncthreads();
+    for (int j = threadIdx.x; j < k; j += blockDim.x) {
+      const size_t o = static_cast<size_t>(q) * k + j;
+      if (bk[j] != ~0ull) {
         out_d[o] = bd[j];
         out_labels[o] = labels[bk[j]];
         if (out_keys) out_keys[o] = row_offset + bk[j];
@@ -1094,9 +1146,22 @@ struct FlatPlan {
   int dim = 0, dpad = 0, kk = 0, n_qtiles = 0, n_chunks = 0, qpb = 0, group_rows = 1;
   int64_t chunk_rows = 0;
   size_t slots = 0;
+  int rescan_slices = 1;  // row slices of an uncertified query's rescan
   size_t qp = 0, qn2 = 0, eps = 0, qbad = 0, fail = 0, cand_d = 0, cand_r = 0, cand_n = 0,
-         thr = 0, tc = 0, flags = 0, total = 0;
+         thr = 0, tc = 0, flags = 0, rescan = 0, total = 0;
 };
+
+// Row slices of one uncertified query's rescan: enough for the rows to stream from many SMs, at
+// least 4096 rows each, the per-slice results of every query within kRescanScratchBytes, and at
+// most 4096 entries per query to merge.
+constexpr size_t kRescanScratchBytes = size_t{32} << 20;
+static int rescan_slices_for(size_t nrows, size_t nq, size_t k, int nsm) {
+  const size_t per_slice = nq * k * (sizeof(float) + sizeof(uint64_t));
+  size_t sl = std::min<size_t>(2 * static_cast<size_t>(nsm), ceil_div(nrows, 4096));
+  sl = std::min(sl, kRescanScratchBytes / std::max<size_t>(per_slice, 1));
+  sl = std::min(sl, 4096 / k);
+  return static_cast<int>(std::max<size_t>(sl, 1));
+}
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t{255}; }
 
@@ -1151,6 +1216,11 @@ static FlatPlan plan_search(const FlatState& s, size_t nq, size_t k, bool allow_
   P.thr = take(nq * sizeof(unsigned));
   if (P.tensor) P.tc = take(flat_tc_scratch_bytes(s, nq, k, P.kk));
   if (own_flags) P.flags = take(kSearchFlagWords * sizeof(int));
+  // The allocation-free entry point (own_flags) rescans each query in one block: no slice results.
+  P.rescan_slices = own_flags ? 1 : rescan_slices_for(nrows, nq, k, nsm);
+  if (P.rescan_slices > 1)
+    P.rescan = take(nq * static_cast<size_t>(P.rescan_slices) * k *
+                    (sizeof(float) + sizeof(uint64_t)));
   P.total = off;
   return P;
 }
@@ -1266,14 +1336,31 @@ static void run_search(const FlatState& s, const FlatPlan& P, unsigned char* bas
   }
 
   const int cap = static_cast<int>(next_pow2(k + 256));
-  const size_t rsmem = cap * (sizeof(float) + sizeof(uint64_t));
+  const int slices = P.rescan_slices;
+  float* sl_d = slices > 1 ? reinterpret_cast<float*>(base + P.rescan) : nullptr;
+  uint64_t* sl_r = slices > 1 ? reinterpret_cast<uint64_t*>(
+                                    sl_d + nq * static_cast<size_t>(slices) * k)
+                              : nullptr;
+  const size_t rsmem = dpad * sizeof(float) + cap * (sizeof(float) + sizeof(uint64_t));
   QV_CUDA(cudaFuncSetAttribute(flat_rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)rsmem));
-  flat_rescan_kernel<<<static_cast<unsigned>(std::min<size_t>(nq, 2 * nsm)), 256, rsmem, st>>>(
+  flat_rescan_kernel<<<static_cast<unsigned>(std::min<size_t>(nq * slices, 2 * nsm)), 256, rsmem,
+                       st>>>(
       qp, dpad, s.x.get<float>(), dim, static_cast<int64_t>(s.n), s.labels.get<uint64_t>(),
-      d_bitmap, s.row_offset, l2, kind, static_cast<int>(k), cap, fail_count, fail_q, fail_dk, d_labels,
-      d_dists, d_keys);
+      d_bitmap, s.row_offset, l2, kind, static_cast<int>(k), cap, slices, fail_count, fail_q,
+      fail_dk, sl_d, sl_r, d_labels, d_dists, d_keys);
   check_launch("flat_rescan_kernel");
+  if (slices > 1) {
+    const int pool = static_cast<int>(next_pow2(static_cast<size_t>(slices) * k));
+    const size_t msmem = pool * (sizeof(float) + sizeof(uint64_t));
+    QV_CUDA(cudaFuncSetAttribute(flat_rescan_merge_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)msmem));
+    flat_rescan_merge_kernel<<<static_cast<unsigned>(std::min<size_t>(nq, 2 * nsm)), 256, msmem,
+                               st>>>(fail_count, fail_q, slices, static_cast<int>(k), pool, sl_d,
+                                     sl_r, s.labels.get<uint64_t>(), s.row_offset, d_labels,
+                                     d_dists, d_keys);
+    check_launch("flat_rescan_merge_kernel");
+  }
 }
 
 void flat_search(const FlatState& s, const float* d_queries, size_t nq, size_t k,

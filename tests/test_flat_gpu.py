@@ -130,6 +130,31 @@ def test_uncertified_queries_take_the_exact_rescan(gpu, oracle, monkeypatch):
     assert_topk_parity(l, d, wl, wd, exact=True, what="rescan")
 
 
+@pytest.mark.parametrize("k,filtered", [(10, False), (10, True), (300, False)])
+def test_rescan_split_over_row_slices(gpu, oracle, monkeypatch, k, filtered):
+    """Uncertified queries over 60,000 rows: each is rescanned by several blocks over row slices
+    (per-slice k best, then a merge), with exact ties at the boundary, a label filter and a large
+    k (fewer slices); the results equal the oracle's."""
+    from quiver_b200.synthetic import skewed_ints
+    base = skewed_ints(60000, 16, 13)
+    base[:, 6:] = 0  # many equal distances
+    q = skewed_ints(40, 16, 14)
+    q[:, 6:] = 0
+    labels = np.arange(60000, dtype=np.uint64)
+    allowed = np.random.default_rng(15).choice(60000, 20000, replace=False).astype(np.uint64) \
+        if filtered else None
+    ix = gpu.FlatIndex(16)
+    ix.add(base)
+    monkeypatch.setenv("QV_FLAT_KK", str(k))
+    gpu._native.set_timing(True)
+    l, d = ix.search(q, k, filter=allowed)
+    stats = gpu.last_search_stats()
+    gpu._native.set_timing(False)
+    assert stats["rescanned_queries"] > 0
+    wl, wd = oracle.flat_search(base, labels, "l2", q, k, allowed=allowed)
+    assert_topk_parity(l, d, wl, wd, exact=True, what=f"sliced rescan k={k}")
+
+
 def test_save_load_roundtrip_and_reference_format(gpu, tmp_path, reference):
     x = np.random.default_rng(4).standard_normal((100, 16)).astype(np.float32)
     ix = gpu.FlatIndex(16, "cosine")
