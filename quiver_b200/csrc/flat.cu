@@ -909,7 +909,7 @@ __global__ void __launch_bounds__(256) flat_rescan_kernel(
   float* sq = reinterpret_cast<float*>(smem_raw);  // dpad floats (16-byte multiple)
   float* bd = sq + dpad;
   uint64_t* bk = reinterpret_cast<uint64_t*>(bd + cap);
-  __shared__ int s_cnt;
+  __shared__ int s_cnt, s_strict;
   __shared__ float s_thr;
   const int nfail = *fail_count;
   const int64_t pairs = static_cast<int64_t>(nfail) * slices;
@@ -922,15 +922,19 @@ __global__ void __launch_bounds__(256) flat_rescan_kernel(
     if (threadIdx.x == 0) {
       s_cnt = 0;
       s_thr = fail_dk[f];
+      s_strict = 0;
     }
     __syncthreads();
     const int64_t per_round = blockDim.x;
     for (int64_t rb = lo; rb < hi; rb += per_round) {
+      // Once a compaction has kept k rows, the k-th of them precedes every row still to come
+      // (rows are scanned in ascending order), so a row at exactly the threshold loses the tie.
       const float thr = s_thr;
+      const bool strict = s_strict != 0;
       const int64_t row = rb + threadIdx.x;
       if (row < hi && dev::bitmap_test(bitmap, static_cast<uint64_t>(row))) {
         const float e = dev::nan_to_inf(lane_exact_distance(sq, x + row * dim, dim, l2, kind));
-        if (e <= thr) {
+        if (e < thr || (e == thr && !strict)) {
           const int slot = atomicAdd(&s_cnt, 1);
           bd[slot] = e;
           bk[slot] = static_cast<uint64_t>(row);
@@ -945,7 +949,10 @@ __global__ void __launch_bounds__(256) flat_rescan_kernel(
         dev::block_bitonic_sort<false>(bd, bk, nullptr, cap);
         if (threadIdx.x == 0) {
           s_cnt = min(s_cnt, k);
-          if (s_cnt == k) s_thr = fminf(s_thr, bd[k - 1]);
+          if (s_cnt == k) {
+            s_thr = fminf(s_thr, bd[k - 1]);
+            s_strict = 1;
+          }
         }
       }
       __syncthreads();
