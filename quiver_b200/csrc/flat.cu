@@ -37,6 +37,7 @@ constexpr int kScreenRows = 32;   // rows per shared-memory tile of the SIMT scr
 constexpr int kScreenDChunk = 256;  // columns per shared-memory tile
 constexpr int kFinalizeThreads = 256;
 constexpr int kMaxCandidatesPerQuery = 1024;  // n_chunks * KK, merged in one block
+constexpr size_t kTcMinChunkRows = 2048;      // rows per tensor-core work unit, at least
 constexpr float kInf = __builtin_huge_valf();
 
 // ---- normalization and per-row statistics ---------------------------------------------------------
@@ -1127,8 +1128,9 @@ void flat_append(FlatState& s, const float* d_rows, const uint64_t* d_labels, si
 // fill the GPU, at most `max_chunks` (the finalize merges n_chunks * KK candidates per query in
 // one block), preferring counts that leave the last wave of a persistent grid nearly full.
 static int choose_chunks(size_t nrows, int n_qtiles, int max_chunks, int grid, int64_t align,
-                         int64_t* chunk_rows) {
-  const int limit = static_cast<int>(std::min<size_t>(max_chunks, ceil_div(nrows, align)));
+                         int64_t* chunk_rows, size_t min_chunk_rows = 0) {
+  const int limit = static_cast<int>(std::min<size_t>(
+      max_chunks, ceil_div(nrows, std::max<size_t>(static_cast<size_t>(align), min_chunk_rows))));
   int best = 1;
   double best_eff = -1.0;
   for (int c = 1; c <= limit; ++c) {
@@ -1190,8 +1192,10 @@ static FlatPlan plan_search(const FlatState& s, size_t nq, size_t k, bool allow_
     // Work units cover query groups of 2 x 128 (narrow screen), 4 x 128 (narrow screen in CTA
     // pairs) or one 128-query tile (wide).
     P.n_qtiles = static_cast<int>(ceil_div(nq, static_cast<size_t>(flat_tc_group_rows(s, k))));
+    // At least kTcMinChunkRows rows per unit: every unit has a fixed candidate cost (each query's
+    // list starts empty and takes most of its first groups), which small tables cannot amortize.
     P.n_chunks = choose_chunks(nrows, P.n_qtiles, std::max(1, kMaxCandidatesPerQuery / P.kk),
-                               flat_tc_workers(s, k), 128, &P.chunk_rows);
+                               flat_tc_workers(s, k), 128, &P.chunk_rows, kTcMinChunkRows);
     P.group_rows = kTcGroupRows;
   } else {
     P.kk = static_cast<int>(next_pow2(k + std::max<size_t>(8, k / 4)));
