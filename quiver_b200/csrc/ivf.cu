@@ -461,10 +461,91 @@ struct ScanArgs {
   uint64_t* out_keys;
 };
 
+// When the buffer holds more than 2 x keep entries (and at most 4 per thread), the keep-th
+// smallest distance t is found first by a radix select over the distances' ordered bits (-0
+// counted as +0, as the (distance, key) order treats them), and only the entries at or below t
+// (keep of them plus ties at t) are moved to the front and sorted: every entry left out has a
+// larger distance than all of them, so the keep best by (distance, key) are among them.
+constexpr int kSelectPerThread = 4;  // the select path serves up to this many entries per thread
+
+__device__ __forceinline__ uint32_t select_bits(float d) { return dev::ordered_bits(d + 0.0f); }
+
+// Returns the number of entries moved to the front of bd / bk / bp (at least keep).
+__device__ int select_front(float* bd, uint64_t* bk, uint64_t* bp, int n, int keep) {
+  __shared__ unsigned hist[256];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_need, s_moved;
+  uint32_t prefix = 0;
+  int need = keep;  // rank (1-based) of the target among the entries matching the prefix
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    const uint32_t above = pass == 0 ? 0u : ~0u << (shift + 8);
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const uint32_t u = select_bits(bd[i]);
+      if ((u & above) == prefix) atomicAdd(&hist[(u >> shift) & 255u], 1u);
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      const int lane = threadIdx.x;
+      unsigned h[8], sum = 0;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        h[b] = hist[lane * 8 + b];
+        sum += h[b];
+      }
+      unsigned incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      unsigned cum = incl - sum;
+#pragma unroll
+      for (int b = 0; b < 8; ++b) {
+        if (cum < static_cast<unsigned>(need) && static_cast<unsigned>(need) <= cum + h[b]) {
+          s_prefix = prefix | (static_cast<uint32_t>(lane * 8 + b) << shift);
+          s_need = need - static_cast<int>(cum);
+        }
+        cum += h[b];
+      }
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    need = s_need;
+  }
+  // prefix: the ordered bits of the keep-th smallest distance. Entries at or below it move to
+  // the front, one block-wide round of blockDim entries at a time: a round writes only below the
+  // count of entries selected so far, i.e. into positions already read (this round's included).
+  if (threadIdx.x == 0) s_moved = 0;
+  for (int base = 0; base < n; base += blockDim.x) {
+    const int i = base + threadIdx.x;
+    const bool in = i < n && select_bits(bd[i]) <= prefix;
+    const float d = in ? bd[i] : 0.0f;
+    const uint64_t k = in ? bk[i] : 0, p = in ? bp[i] : 0;
+    __syncthreads();  // every entry of this round has been read (and s_moved set)
+    if (in) {
+      const int slot = atomicAdd(&s_moved, 1);
+      bd[slot] = d;
+      bk[slot] = k;
+      bp[slot] = p;
+    }
+    __syncthreads();
+  }
+  return s_moved;
+}
+
 // Compacts the block buffer to its best `keep` (distance, key) entries; updates the threshold.
-// Sorts only the filled part, rounded up to a power of two (at least `keep`'s).
+// Sorts only the filled part (or the selected front), rounded up to a power of two (at least
+// `keep`'s).
 __device__ void scan_compact(float* bd, uint64_t* bk, uint64_t* bp, int cap, int keep, int* cnt,
                              float* thr) {
+  if (*cnt > 2 * keep && *cnt <= kSelectPerThread * static_cast<int>(blockDim.x)) {
+    const int moved = select_front(bd, bk, bp, *cnt, keep);
+    if (threadIdx.x == 0) *cnt = moved;
+    __syncthreads();
+  }
   int n2 = 1;
   while (n2 < *cnt || n2 < keep) n2 <<= 1;
   n2 = min(n2, cap);
