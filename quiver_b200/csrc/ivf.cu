@@ -640,9 +640,12 @@ template <int M>
 __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int ts = (M > 0 ? M : a.m) * kSubCentroids;
+  // One probed list with the L2 precomputed terms: the query term goes straight into that list's
+  // table (the same rounded sum pre + (-2 * ip)), so no separate query table is kept.
+  const bool fused = a.use_pre && !a.ip && a.nprobe == 1;
   float* table = reinterpret_cast<float*>(smem_raw);
   float* qtab = table + ts;                                // L2 precomputed only
-  float* qv = qtab + (a.use_pre ? ts : 0);                 // dim (residual scratch for L2)
+  float* qv = qtab + (a.use_pre && !fused ? ts : 0);       // dim (residual scratch for L2)
   float* bd = qv + ((a.dim + 3) & ~3);
   uint64_t* bk = reinterpret_cast<uint64_t*>(bd + a.cap);
   uint64_t* bp = bk + a.cap;
@@ -660,7 +663,8 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
   __syncthreads();
   // Query-side tables: ip_table (CentroidTable::dot over each sub-space, sequential in t).
   if (a.ip || a.use_pre) {
-    float* dst = a.ip ? table : qtab;
+    float* dst = (a.ip || fused) ? table : qtab;
+    const float* pre0 = fused ? a.pre + static_cast<size_t>(a.probes[q]) * ts : nullptr;
     if (a.dsub == 4) {
       // Sub-spaces of 4 (configs 2 and 3): one 16-byte load per entry, eight entries' loads in
       // flight per thread (the codebook is read from L2 by every query).
@@ -672,7 +676,9 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
         acc = __fadd_rn(acc, __fmul_rn(qs[1], c.y));
         acc = __fadd_rn(acc, __fmul_rn(qs[2], c.z));
         acc = __fadd_rn(acc, __fmul_rn(qs[3], c.w));
-        dst[e] = a.ip ? acc : __fmul_rn(acc, -2.0f);  // query_table = -2 * ip_table (:316-317)
+        // query_table = -2 * ip_table (:316-317); fused: its list's table entry pre + that
+        const float v = a.ip ? acc : __fmul_rn(acc, -2.0f);
+        dst[e] = fused ? __fadd_rn(__ldg(pre0 + e), v) : v;
       }
     } else {
       for (int e = tid; e < ts; e += blockDim.x) {
@@ -681,7 +687,8 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
         const float* qs = qv + j * a.dsub;
         float acc = 0.0f;
         for (int t = 0; t < a.dsub; ++t) acc = __fadd_rn(acc, __fmul_rn(qs[t], cbv[t]));
-        dst[e] = a.ip ? acc : __fmul_rn(acc, -2.0f);
+        const float v = a.ip ? acc : __fmul_rn(acc, -2.0f);
+        dst[e] = fused ? __fadd_rn(__ldg(pre0 + e), v) : v;
       }
     }
   }
@@ -701,7 +708,7 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
       for (int i = 0; i < M; ++i) pf[i] = __ldg(pre + tid + i * kScanThreads);
     }
   };
-  if (a.use_pre && !a.ip) prefetch(0);
+  if (a.use_pre && !a.ip && !fused) prefetch(0);
   for (int pi = 0; pi < a.nprobe; ++pi) {
     const uint32_t l = a.probes[q * a.nprobe + pi];
     const uint64_t off = a.offsets[l];
@@ -713,6 +720,8 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
     float base;
     if (a.ip) {
       base = -a.probe_d[q * a.nprobe + pi];
+    } else if (fused) {
+      base = a.probe_d[q];  // the table was built with the query term
     } else if (a.use_pre) {
       base = a.probe_d[q * a.nprobe + pi];
       __syncthreads();
@@ -1020,7 +1029,9 @@ void run_scan(const IvfState& s, const Prepared& p, size_t nq, size_t keep, size
   a.out_d = out_d;
   a.out_keys = out_keys;
   const size_t ts = s.m * kSubCentroids * sizeof(float);
-  const size_t smem = ts * (a.use_pre ? 2 : 1) + ((s.dim + 3) & ~size_t{3}) * sizeof(float) +
+  const bool fused = a.use_pre && p.nprobe == 1;  // no separate query table (see the kernel)
+  const size_t smem = ts * (a.use_pre && !fused ? 2 : 1) +
+                      ((s.dim + 3) & ~size_t{3}) * sizeof(float) +
                       a.cap * (sizeof(float) + 2 * sizeof(uint64_t));
   if (smem > 227 * 1024) {
     fail(QV_ERR_UNSUPPORTED,
