@@ -636,16 +636,22 @@ __device__ __forceinline__ void adc2(const float* table, const CodeWords<M>& c0,
 // 0.0f (ProductQuantizer::adc, src/product_quantizer.cc:188-217); dist = ip ? 1-(base+s) : base+s
 // (src/ivfpq_index.cc:346). Survivors of the running threshold and the position bitmap go to a
 // block buffer that is compacted to the best `keep` after every pass of 2 x kScanThreads codes.
-template <int M>
+// kRegQ (code width 32, L2 with precomputed terms, several probed lists): the query term is kept
+// in registers instead of shared memory (thread tid owns entries tid + i * kScanThreads, the same
+// entries it adds into each list's table). It costs registers (2 resident blocks per SM instead
+// of 4), which the single-list case, whose table needs no query term, does not pay.
+template <int M, bool kRegQ = false>
 __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
+  static_assert(!kRegQ || M > 0, "the register query term needs a compile-time code width");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int ts = (M > 0 ? M : a.m) * kSubCentroids;
   // One probed list with the L2 precomputed terms: the query term goes straight into that list's
   // table (the same rounded sum pre + (-2 * ip)), so no separate query table is kept.
   const bool fused = a.use_pre && !a.ip && a.nprobe == 1;
+  float qreg[kRegQ ? M : 1];
   float* table = reinterpret_cast<float*>(smem_raw);
-  float* qtab = table + ts;                                // L2 precomputed only
-  float* qv = qtab + (a.use_pre && !fused ? ts : 0);       // dim (residual scratch for L2)
+  float* qtab = table + ts;                                // L2 precomputed, in shared memory
+  float* qv = qtab + (a.use_pre && !fused && !kRegQ ? ts : 0);  // dim (residual scratch for L2)
   float* bd = qv + ((a.dim + 3) & ~3);
   uint64_t* bk = reinterpret_cast<uint64_t*>(bd + a.cap);
   uint64_t* bp = bk + a.cap;
@@ -666,10 +672,13 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
     float* dst = (a.ip || fused) ? table : qtab;
     const float* pre0 = fused ? a.pre + static_cast<size_t>(a.probes[q]) * ts : nullptr;
     if (a.dsub == 4) {
-      // Sub-spaces of 4 (configs 2 and 3): one 16-byte load per entry, eight entries' loads in
-      // flight per thread (the codebook is read from L2 by every query).
-#pragma unroll 8
-      for (int e = tid; e < ts; e += kScanThreads) {
+      // Sub-spaces of 4 (configs 2 and 3): one 16-byte load per entry, the loop unrolled so that
+      // many entries' loads are in flight per thread (the codebook is read from L2 by every
+      // query).
+#pragma unroll
+      for (int i = 0; i < (M > 0 ? M : ts / kScanThreads + 1); ++i) {
+        const int e = tid + i * kScanThreads;
+        if (M == 0 && e >= ts) break;
         const float4 c = __ldg(reinterpret_cast<const float4*>(a.cb) + e);
         const float* qs = qv + (e / kSubCentroids) * 4;
         float acc = __fadd_rn(0.0f, __fmul_rn(qs[0], c.x));
@@ -678,16 +687,31 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
         acc = __fadd_rn(acc, __fmul_rn(qs[3], c.w));
         // query_table = -2 * ip_table (:316-317); fused: its list's table entry pre + that
         const float v = a.ip ? acc : __fmul_rn(acc, -2.0f);
+        if constexpr (kRegQ) {
+          if (!a.ip && !fused) {
+            qreg[i] = v;
+            continue;
+          }
+        }
         dst[e] = fused ? __fadd_rn(__ldg(pre0 + e), v) : v;
       }
     } else {
-      for (int e = tid; e < ts; e += blockDim.x) {
+#pragma unroll
+      for (int i = 0; i < (M > 0 ? M : ts / kScanThreads + 1); ++i) {
+        const int e = tid + i * kScanThreads;
+        if (M == 0 && e >= ts) break;
         const int j = e / kSubCentroids;
         const float* cbv = a.cb + static_cast<size_t>(e) * a.dsub;
         const float* qs = qv + j * a.dsub;
         float acc = 0.0f;
         for (int t = 0; t < a.dsub; ++t) acc = __fadd_rn(acc, __fmul_rn(qs[t], cbv[t]));
         const float v = a.ip ? acc : __fmul_rn(acc, -2.0f);
+        if constexpr (kRegQ) {
+          if (!a.ip && !fused) {
+            qreg[i] = v;
+            continue;
+          }
+        }
         dst[e] = fused ? __fadd_rn(__ldg(pre0 + e), v) : v;
       }
     }
@@ -729,7 +753,10 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
 #pragma unroll
         for (int i = 0; i < M; ++i) {
           const int e = tid + i * kScanThreads;
-          table[e] = __fadd_rn(pf[i], qtab[e]);
+          if constexpr (kRegQ)
+            table[e] = __fadd_rn(pf[i], qreg[i]);
+          else
+            table[e] = __fadd_rn(pf[i], qtab[e]);
         }
       } else {
         const float* pre = a.pre + static_cast<size_t>(l) * ts;
@@ -1030,7 +1057,9 @@ void run_scan(const IvfState& s, const Prepared& p, size_t nq, size_t keep, size
   a.out_keys = out_keys;
   const size_t ts = s.m * kSubCentroids * sizeof(float);
   const bool fused = a.use_pre && p.nprobe == 1;  // no separate query table (see the kernel)
-  const size_t smem = ts * (a.use_pre && !fused ? 2 : 1) +
+  // Several probed lists with the precomputed terms and code width 32: the query term in registers.
+  const bool reg_q = s.m == 32 && a.use_pre && !fused;
+  const size_t smem = ts * (a.use_pre && !fused && !reg_q ? 2 : 1) +
                       ((s.dim + 3) & ~size_t{3}) * sizeof(float) +
                       a.cap * (sizeof(float) + 2 * sizeof(uint64_t));
   if (smem > 227 * 1024) {
@@ -1046,7 +1075,7 @@ void run_scan(const IvfState& s, const Prepared& p, size_t nq, size_t keep, size
     case 10: kernel = ivf_scan_kernel<10>; break;
     case 16: kernel = ivf_scan_kernel<16>; break;
     case 25: kernel = ivf_scan_kernel<25>; break;
-    case 32: kernel = ivf_scan_kernel<32>; break;
+    case 32: kernel = reg_q ? ivf_scan_kernel<32, true> : ivf_scan_kernel<32>; break;
     case 48: kernel = ivf_scan_kernel<48>; break;
     case 64: kernel = ivf_scan_kernel<64>; break;
     default: break;
