@@ -641,7 +641,8 @@ __device__ __forceinline__ void adc2(const float* table, const CodeWords<M>& c0,
 // entries it adds into each list's table). It costs registers (2 resident blocks per SM instead
 // of 4), which the single-list case, whose table needs no query term, does not pay.
 template <int M, bool kRegQ = false>
-__global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
+__global__ void __launch_bounds__(kScanThreads, kRegQ ? 3 : (M <= 32 ? 4 : 2))
+    ivf_scan_kernel(ScanArgs a) {
   static_assert(!kRegQ || M > 0, "the register query term needs a compile-time code width");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int ts = (M > 0 ? M : a.m) * kSubCentroids;
@@ -721,8 +722,9 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
   float thr = kInf;
   // With the L2 precomputed terms and a compile-time code width, each thread keeps its M
   // entries of the next probed list's precomputed slice in registers: they are loaded while the
-  // current list is scanned and only added to the query's table after it.
-  constexpr bool kPrefetch = M > 0;
+  // current list is scanned and only added to the query's table after it. (kRegQ instead holds
+  // the query term there and loads each slice when it builds the table: 3 blocks per SM.)
+  constexpr bool kPrefetch = M > 0 && !kRegQ;
   float pf[kPrefetch ? M : 1];
   auto prefetch = [&](int pi) {
     if constexpr (kPrefetch) {
@@ -753,10 +755,14 @@ __global__ void __launch_bounds__(kScanThreads) ivf_scan_kernel(ScanArgs a) {
 #pragma unroll
         for (int i = 0; i < M; ++i) {
           const int e = tid + i * kScanThreads;
-          if constexpr (kRegQ)
-            table[e] = __fadd_rn(pf[i], qreg[i]);
-          else
-            table[e] = __fadd_rn(pf[i], qtab[e]);
+          table[e] = __fadd_rn(pf[i], qtab[e]);
+        }
+      } else if constexpr (kRegQ) {
+        const float* pre = a.pre + static_cast<size_t>(l) * ts;
+#pragma unroll
+        for (int i = 0; i < M; ++i) {
+          const int e = tid + i * kScanThreads;
+          table[e] = __fadd_rn(__ldg(pre + e), qreg[i]);
         }
       } else {
         const float* pre = a.pre + static_cast<size_t>(l) * ts;
