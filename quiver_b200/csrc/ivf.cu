@@ -24,6 +24,7 @@ namespace {
 constexpr float kInf = __builtin_huge_valf();
 constexpr size_t kMaxPrecomputedBytes = size_t{256} << 20;  // src/ivfpq_index.cc:74
 constexpr int kScanThreads = 256;
+constexpr int kSeqLists = 256;  // probes up to which inner-product scans run as one sequence
 
 // ---- trained state -------------------------------------------------------------------------------
 
@@ -456,6 +457,9 @@ struct ScanArgs {
   bool refine;
   // outputs (final mode): labels/dists nq x k. candidate mode: dists/keys/labels nq x keep
   bool candidate_mode;
+  // Inner-product metrics with at most kSeqLists probes: the probed lists are scanned as one
+  // sequence (per-list data in dynamic shared memory after the survivor buffer).
+  bool seq;
   uint64_t* out_labels;
   float* out_d;
   uint64_t* out_keys;
@@ -656,6 +660,13 @@ __global__ void __launch_bounds__(kScanThreads, kRegQ ? 3 : (M <= 32 ? 4 : 2))
   float* bd = qv + ((a.dim + 3) & ~3);
   uint64_t* bk = reinterpret_cast<uint64_t*>(bd + a.cap);
   uint64_t* bp = bk + a.cap;
+  // seq: per probed list its first index in the sequence (nprobe + 1 entries), first code
+  // position, list id, global base and coarse term.
+  int64_t* s_start = reinterpret_cast<int64_t*>(bp + a.cap);
+  uint64_t* s_off = reinterpret_cast<uint64_t*>(s_start + a.nprobe + 1);
+  uint32_t* s_list = reinterpret_cast<uint32_t*>(s_off + a.nprobe);
+  uint32_t* s_gb = s_list + a.nprobe;
+  float* s_base = reinterpret_cast<float*>(s_gb + a.nprobe);
   __shared__ int s_cnt;
   __shared__ float s_thr;
 
@@ -735,7 +746,67 @@ __global__ void __launch_bounds__(kScanThreads, kRegQ ? 3 : (M <= 32 ? 4 : 2))
     }
   };
   if (a.use_pre && !a.ip && !fused) prefetch(0);
-  for (int pi = 0; pi < a.nprobe; ++pi) {
+  if (a.seq) {
+    // Inner product: one table serves every list (only the coarse term differs), so the lists'
+    // codes form one sequence and a pass of 2 x kScanThreads codes may span list boundaries
+    // instead of ending with each list. Each code's arithmetic, key and position are the ones
+    // the per-list loop below gives it.
+    for (int pi = tid; pi < a.nprobe; pi += blockDim.x) {
+      const uint32_t l = a.probes[q * a.nprobe + pi];
+      s_list[pi] = l;
+      s_off[pi] = a.offsets[l];
+      s_gb[pi] = a.global_base[l];
+      s_base[pi] = -a.probe_d[q * a.nprobe + pi];
+    }
+    __syncthreads();
+    if (tid == 0) {
+      int64_t acc = 0;
+      for (int pi = 0; pi < a.nprobe; ++pi) {
+        s_start[pi] = acc;
+        acc += static_cast<int64_t>(a.offsets[s_list[pi] + 1] - s_off[pi]);
+      }
+      s_start[a.nprobe] = acc;
+    }
+    __syncthreads();
+    const int64_t total = s_start[a.nprobe];
+    int cur[2] = {0, 0};  // the list holding this thread's next code of each half
+    for (int64_t r0 = 0; r0 < total; r0 += 2 * kScanThreads) {
+      int64_t g[2];
+      bool v[2];
+      uint64_t pos[2];
+      CodeWords<M> c[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        g[h] = r0 + h * kScanThreads + tid;
+        v[h] = g[h] < total;
+        while (v[h] && s_start[cur[h] + 1] <= g[h]) ++cur[h];
+        pos[h] = v[h] ? s_off[cur[h]] + static_cast<uint64_t>(g[h] - s_start[cur[h]]) : 0;
+        c[h].load(a.codes, pos[h], a.m);
+      }
+      float sum[2];
+      adc2<M>(table, c[0], c[1], a.m, sum[0], sum[1]);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int pi = cur[h];
+        float dist = __fsub_rn(1.0f, __fadd_rn(s_base[pi], sum[h]));
+        dist = dev::nan_to_inf(dist);
+        if (v[h] && dist <= thr && dev::bitmap_test(a.bitmap, pos[h])) {
+          const uint64_t i = pos[h] - s_off[pi];
+          const int slot = atomicAdd(&s_cnt, 1);
+          bd[slot] = dist;
+          bk[slot] = (static_cast<uint64_t>(s_list[pi]) << 32) | (s_gb[pi] + i);
+          bp[slot] = pos[h];
+        }
+      }
+      __syncthreads();
+      const int filled = s_cnt;
+      __syncthreads();
+      if (filled > a.cap - 2 * kScanThreads || (thr == kInf && filled >= 8 * a.keep))
+        scan_compact(bd, bk, bp, a.cap, a.keep, &s_cnt, &s_thr);
+      thr = s_thr;
+    }
+  }
+  for (int pi = 0; pi < (a.seq ? 0 : a.nprobe); ++pi) {
     const uint32_t l = a.probes[q * a.nprobe + pi];
     const uint64_t off = a.offsets[l];
     const int64_t len = static_cast<int64_t>(a.offsets[l + 1] - off);
@@ -1058,6 +1129,7 @@ void run_scan(const IvfState& s, const Prepared& p, size_t nq, size_t keep, size
   a.cap = static_cast<int>(std::max<size_t>(1024, next_pow2(keep + 2 * kScanThreads)));
   a.refine = refine;
   a.candidate_mode = candidate_mode;
+  a.seq = a.ip && p.nprobe <= kSeqLists;
   a.out_labels = out_labels;
   a.out_d = out_d;
   a.out_keys = out_keys;
@@ -1065,9 +1137,12 @@ void run_scan(const IvfState& s, const Prepared& p, size_t nq, size_t keep, size
   const bool fused = a.use_pre && p.nprobe == 1;  // no separate query table (see the kernel)
   // Several probed lists with the precomputed terms and code width 32: the query term in registers.
   const bool reg_q = s.m == 32 && a.use_pre && !fused;
+  const size_t seq_bytes =
+      a.seq ? (p.nprobe + 1) * sizeof(int64_t) + p.nprobe * (sizeof(uint64_t) + 3 * sizeof(uint32_t))
+            : 0;
   const size_t smem = ts * (a.use_pre && !fused && !reg_q ? 2 : 1) +
                       ((s.dim + 3) & ~size_t{3}) * sizeof(float) +
-                      a.cap * (sizeof(float) + 2 * sizeof(uint64_t));
+                      a.cap * (sizeof(float) + 2 * sizeof(uint64_t)) + seq_bytes;
   if (smem > 227 * 1024) {
     fail(QV_ERR_UNSUPPORTED,
          "IVF-PQ search: m=" + std::to_string(s.m) + " with keep=" + std::to_string(keep) +
